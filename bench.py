@@ -1,0 +1,401 @@
+#!/usr/bin/env python
+"""Benchmark of the quantized decode matvec path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl neon|reference]
+
+Workload (the Q4_0 x fp32 matvec configuration the metric is quoted on): W
+4096x4096 Q4_0 (blocks of 32 along K: fp16 d = |N(0,1)|*0.02 and 16 bytes of
+nibbles uniform 0..15), x fp32 N(0,1), batch 1, seeded. The GPU keeps a
+rotation of 48 distinct weight tensors (455 MB, 3.6x the 126 MB L2) so every
+call streams its weights from HBM. One step = 1024 matvec calls, each on the
+next tensor of the rotation. Metric: algorithmic bytes (weights + scales + x +
+y) per second, whole job.
+
+  value     device-resident: the step's 1024 launches replayed from a CUDA
+            graph, timed with CUDA events on the launch stream.
+  e2e       through the public host-buffer API (neon_cuda.proj_all_positions:
+            pinned host x in, host y out, blocking per call, like the
+            reference's fwd::proj_all_positions).
+  roofline  the Q4_0 decode kernel against the measured HBM copy bandwidth.
+  cpu_baseline
+            the reference's own CPU path (oracle/_ref, rawllm_forward.hpp
+            compiled with its flags) on this host's cores, bounded sample.
+
+With --gpus N under torchrun every rank runs its own rotation (weak scaling,
+no data-path collective); value = all ranks' bytes / max-over-ranks time.
+--impl reference times the reference's CPU path alone (rank 0 only).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "neon-runtime-beta-variation_b200")
+sys.path.insert(0, PKG)
+
+import numpy as np  # noqa: E402
+
+import synth as S  # noqa: E402
+
+METRIC = "Q4_0 matvec HBM GB/s vs peak"
+UNIT = "GB/s"
+ROWS = COLS = 4096
+ROTATION = 48
+CALLS_PER_STEP = 1024
+FALLBACK_HBM_GBS = 6650.0
+KERNEL = "q4_0_seq1_kernel"
+PROFILE_SUMMARY = os.path.join(ROOT, "profiles", "q4_0_seq1_kernel_4096x4096.txt")
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=400)
+    p.add_argument("--warmup", type=int, default=10)
+    p.add_argument("--impl", choices=["neon", "reference"], default="neon")
+    p.add_argument("--e2e-steps", type=int, default=3)
+    p.add_argument("--cpu-seconds", type=float, default=12.0)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def workload_config():
+    return {
+        "workload": "Q4_0 x fp32 matvec, W 4096x4096, batch 1 (fp16 d=|N(0,1)|*0.02, nibbles U(0..15), "
+                    "x N(0,1), seeded)",
+        "rows": ROWS, "cols": COLS, "batch": 1,
+        "rotation_tensors": ROTATION, "calls_per_step": CALLS_PER_STEP,
+        "l2": f"inputs larger than L2: {ROTATION} distinct weight tensors "
+              f"({ROTATION * S.row_bytes(S.GGML_Q4_0, COLS) * ROWS / 1e6:.0f} MB) rotated, L2 126 MB",
+        "bytes_per_call": S.algorithmic_bytes(S.GGML_Q4_0, ROWS, COLS),
+    }
+
+
+def measured_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def profile_traffic():
+    """DRAM bytes per launch of the kernel from the committed ncu summary."""
+    try:
+        with open(PROFILE_SUMMARY) as f:
+            for line in f:
+                if line.startswith("dram_bytes_per_launch:"):
+                    return int(float(line.split(":", 1)[1].split()[0]))
+    except OSError:
+        pass
+    return None
+
+
+# ---------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ---------------------------------------------------------------------------
+
+class ClockSampler:
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_ids):
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.proc = None
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "50",
+                 "-i", ",".join(str(g) for g in gpu_ids)],
+                stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        self.f.flush()
+
+    def summary(self, t0, t1):
+        rows = []
+        try:
+            with open(self.f.name) as f:
+                for line in f:
+                    parts = [p.strip() for p in line.split(",")]
+                    if len(parts) < 9:
+                        continue
+                    try:
+                        ts = time.mktime(time.strptime(parts[0].split(".")[0], "%Y/%m/%d %H:%M:%S"))
+                        ts += float("0." + parts[0].split(".")[1]) if "." in parts[0] else 0.0
+                        rows.append((ts, int(parts[2]), int(parts[3]), parts[5:9]))
+                    except ValueError:
+                        continue
+        finally:
+            os.unlink(self.f.name)
+        inside = [r for r in rows if t0 - 0.05 <= r[0] <= t1 + 0.05]
+        note = "samples inside the timed region"
+        if not inside and rows:
+            inside = sorted(rows, key=lambda r: min(abs(r[0] - t0), abs(r[0] - t1)))[:4]
+            note = "timed region shorter than the 50 ms sampling period; nearest samples"
+        if not inside:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in inside for i, v in enumerate(r[3]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[1] for r in inside), "sm_max_mhz": max(r[2] for r in inside),
+                "reasons": reasons, "samples": len(inside), "note": note}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the reference's own path on this host
+# ---------------------------------------------------------------------------
+
+def cpu_reference_gbs(host_weights, x, seconds, max_calls=None):
+    """GB/s of the reference's proj_all_positions over the rotation, on a
+    util::ThreadPool of all host cores, for about `seconds` of CPU work."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+
+    if O.ref_available():
+        pool = O.RefPool(os.cpu_count() or 1)
+        kind, cores = "reference", pool.n
+
+        def call(W, Y):
+            pool.proj_all_positions(S.GGML_Q4_0, W, ROWS, COLS, x, Y)
+    else:
+        pool, kind, cores = None, "port", 1
+
+        def call(W, Y):
+            Y[:] = O.proj_all_positions(S.GGML_Q4_0, W, ROWS, COLS, x)
+    Y = np.zeros((1, ROWS), np.float32)
+    call(host_weights[0], Y)  # warm
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds and (max_calls is None or n < max_calls):
+        call(host_weights[n % len(host_weights)], Y)
+        n += 1
+    dt = time.perf_counter() - t0
+    if pool is not None:
+        pool.close()
+    gbs = n * S.algorithmic_bytes(S.GGML_Q4_0, ROWS, COLS) / dt / 1e9
+    return {"value": round(gbs, 3), "unit": UNIT, "cores": cores, "kind": kind,
+            "sample": f"{n} calls of proj_all_positions on Q4_0 4096x4096 over a rotation of "
+                      f"{len(host_weights)} tensors in {dt:.1f} s"}
+
+
+def host_rotation(rank, n):
+    return [S.q4_0_weights(ROWS, COLS, seed=100000 * rank + i) for i in range(n)]
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    cpu_n = 16
+    weights = host_rotation(0, cpu_n)
+    x = S.activations(1, COLS, seed=7)
+    K, W = max(1, args.steps), max(0, args.warmup)
+    budget = 120.0
+    per_step_calls = cpu_n
+    res = cpu_reference_gbs(weights, x, seconds=0.5)  # warm-up + calibration
+    est_call_s = S.algorithmic_bytes(S.GGML_Q4_0, ROWS, COLS) / (res["value"] * 1e9)
+    per_step_calls = max(1, min(cpu_n, int(budget / max(1, K + W) / est_call_s)))
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    pool = O.RefPool(os.cpu_count() or 1) if O.ref_available() else None
+    Y = np.zeros((1, ROWS), np.float32)
+
+    def step():
+        for j in range(per_step_calls):
+            if pool is not None:
+                pool.proj_all_positions(S.GGML_Q4_0, weights[j], ROWS, COLS, x, Y)
+            else:
+                Y[:] = O.proj_all_positions(S.GGML_Q4_0, weights[j], ROWS, COLS, x)
+    for _ in range(W):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(K):
+        step()
+    dt = time.perf_counter() - t0
+    value = K * per_step_calls * S.algorithmic_bytes(S.GGML_Q4_0, ROWS, COLS) / dt / 1e9
+    cores = pool.n if pool is not None else 1
+    kind = "reference" if pool is not None else "port"
+    if pool is not None:
+        pool.close()
+    cfg = workload_config()
+    cfg["calls_per_step"] = per_step_calls
+    cfg["rotation_tensors"] = cpu_n
+    cfg["l2"] = (f"host: {cpu_n} distinct weight tensors "
+                 f"({cpu_n * S.row_bytes(S.GGML_Q4_0, COLS) * ROWS / 1e6:.0f} MB) rotated")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": 0,
+        "steps": K, "warmup": W, "ms_per_step": round(dt / K * 1e3, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8/fp32", "data": "synthetic", "config": cfg,
+        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": cores, "kind": kind,
+                         "sample": f"{K} steps x {per_step_calls} calls of the reference's "
+                                   f"fwd::proj_all_positions (util::ThreadPool of {cores})"},
+        "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+
+def run_neon(args):
+    import torch
+    import torch.distributed as dist
+
+    import neon_cuda as N
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus and world > 1:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    N.init(local)
+    dev = torch.device("cuda", local)
+
+    host_w = host_rotation(rank, ROTATION)
+    tensors = [N.DeviceTensor(w, S.GGML_Q4_0, ROWS, COLS) for w in host_w]
+    x_host = S.activations(1, COLS, seed=7)
+    dx = torch.from_numpy(x_host).to(dev)
+    ys = torch.zeros((ROTATION, ROWS), device=dev)
+    stream = torch.cuda.Stream(device=dev)
+
+    def launch_step(s):
+        for j in range(CALLS_PER_STEP):
+            t = tensors[j % ROTATION]
+            t.matvec(dx, ys[j % ROTATION], stream=s)
+
+    with torch.cuda.stream(stream):
+        tensors[0].matvec(dx, ys[0], stream=stream)
+    stream.synchronize()
+
+    # capture one step (1024 launches) in a CUDA graph
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        launch_step(stream)
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    K, W = args.steps, max(3, args.warmup)
+    with torch.cuda.stream(stream):
+        for _ in range(W):
+            graph.replay()
+    torch.cuda.synchronize()
+
+    sampler = ClockSampler([local]) if rank == 0 else None
+    time.sleep(0.2 if sampler else 0)
+    launches_before = N.launch_count()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    t_wall0 = time.time()
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        for _ in range(K):
+            graph.replay()
+        end.record(stream)
+    torch.cuda.synchronize()
+    t_wall1 = time.time()
+    barrier()
+    ms = start.elapsed_time(end)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    if sampler:
+        sampler.stop()
+    assert N.launch_count() == launches_before, "graph replay should not go through the launch API"
+    gpu_launches = K * CALLS_PER_STEP
+    bytes_call = S.algorithmic_bytes(S.GGML_Q4_0, ROWS, COLS)
+    total_bytes = world * K * CALLS_PER_STEP * bytes_call
+    value = total_bytes / (ms / 1e3) / 1e9
+    per_launch_s = ms / 1e3 / (K * CALLS_PER_STEP)
+    achieved = bytes_call / per_launch_s / 1e9
+
+    # end to end through the public host-buffer API
+    x_pin = torch.from_numpy(x_host.copy()).pin_memory()
+    y_pin = torch.zeros(ROWS, dtype=torch.float32).pin_memory()
+    x_np, y_np = x_pin.numpy(), y_pin.numpy()
+    infos = [N.TensorInfo(f"rot{i}", [COLS, ROWS], S.GGML_Q4_0, host_w[i]) for i in range(ROTATION)]
+    for i in range(ROTATION):  # upload happens once, at "load" time, outside the timed region
+        N.proj_all_positions(infos[i], x_np, COLS, y_np, ROWS, 1)
+    e2e_steps = max(1, min(args.e2e_steps, K))
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        for j in range(CALLS_PER_STEP):
+            N.proj_all_positions(infos[j % ROTATION], x_np, COLS, y_np, ROWS, 1)
+    e2e_s = time.perf_counter() - t0
+    if world > 1:
+        t = torch.tensor([e2e_s], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e_value = world * e2e_steps * CALLS_PER_STEP * bytes_call / e2e_s / 1e9
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_reference_gbs(host_w, x_host, args.cpu_seconds)
+
+    if rank == 0:
+        peak, peak_kind = measured_peak()
+        traffic = profile_traffic()
+        clocks = sampler.summary(t_wall0, t_wall1) if sampler else {}
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": K,
+            "warmup": W, "ms_per_step": round(ms / K, 5), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8/fp32 (q4_0 x q8_0 dp4a, fp32 scales)", "data": "synthetic",
+            "config": {**workload_config(), "parallelism": f"dp{world} (independent rotations)",
+                       "launch": "CUDA graph of 1024 PDL launches per step"},
+            "e2e": {"value": round(e2e_value, 2), "unit": UNIT,
+                    "h2d_bytes_per_step": CALLS_PER_STEP * COLS * 4,
+                    "d2h_bytes_per_step": CALLS_PER_STEP * ROWS * 4,
+                    "api": "neon_cuda.proj_all_positions (host buffers, blocking per call)",
+                    "steps": e2e_steps},
+            "roofline": {"bound": "hbm", "kernel": KERNEL, "achieved": round(achieved, 1),
+                         "peak": peak, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
+                         if peak_kind == "measured" else "fallback 6.65 TB/s",
+                         "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "traffic": traffic, "algorithmic_bytes_per_launch": bytes_call},
+            "cpu_baseline": cpu,
+            "gpu_launches": gpu_launches,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    del graph
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_neon(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,550 @@
+// neon_cuda.cu -- C ABI of the sm_100a quantized matvec backend (see
+// include/neon_cuda.h for the contract of every entry point).
+#include "neon_cuda.h"
+#include "neon_kernels.cuh"
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+using namespace neon;
+
+struct neon_tensor {
+    int device;
+    int type;
+    size_t rows, cols, nb;
+    uint8_t* base;  // single allocation: payload plane, then scale plane
+    uint8_t* qs;
+    uint16_t* d;
+    size_t bytes;
+};
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+// Rows per warp tile and 32-block chunks per lane of the decode kernels.
+constexpr int kQ4R = 2, kQ4U = 4;
+constexpr int kQ8R = 2, kQ8U = 2;
+constexpr int kMpR = 2, kMpT = 4;
+// Largest input dim a one-position launch stages in shared memory.
+constexpr int kMaxSmem = 200 * 1024;
+
+thread_local std::string g_err;
+std::atomic<uint64_t> g_launches{0};
+std::atomic<int> g_pdl{1};
+
+struct DeviceState {
+    bool ready = false;
+    int sms = 0;
+    int occ_q4 = 0, occ_q8 = 0;  // resident CTAs per SM of the decode kernels
+    std::mutex mu;
+    // scratch of multi-position Q4_0 calls (activation quants)
+    int8_t* xq = nullptr;
+    float* xd = nullptr;
+    int* xs = nullptr;
+    size_t scratch_cols = 0;  // capacity in seq*cols elements
+    // staging of the host-buffer calls
+    cudaStream_t stream = nullptr;
+    float* dx = nullptr;
+    float* dy = nullptr;
+    size_t dx_cap = 0, dy_cap = 0;
+};
+DeviceState g_dev[kMaxDevices];
+std::mutex g_init_mu;
+
+int set_err(int code, const std::string& msg) {
+    g_err = msg;
+    return code;
+}
+
+int cuda_err(cudaError_t e, const char* what) {
+    return set_err(NEON_ERR_CUDA, std::string("CUDA error in ") + what + ": " + cudaGetErrorString(e));
+}
+
+#define NEON_CUDA_TRY(call)                                      \
+    do {                                                         \
+        cudaError_t _e = (call);                                 \
+        if (_e != cudaSuccess) return cuda_err(_e, #call);       \
+    } while (0)
+
+size_t payload_bytes(int type) { return type == NEON_GGML_Q4_0 ? 16 : 32; }
+size_t gguf_block_bytes(int type) { return type == NEON_GGML_Q4_0 ? 18 : 34; }
+bool supported_type(int type) { return type == NEON_GGML_Q4_0 || type == NEON_GGML_Q8_0; }
+
+// Runs `fn` with `device` current, restoring the caller's device afterwards.
+struct DeviceGuard {
+    int prev = -1;
+    bool ok = true;
+    explicit DeviceGuard(int device) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != device) ok = cudaSetDevice(device) == cudaSuccess;
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+template <typename Kern>
+int ensure_smem(Kern k, int bytes) {
+    if (bytes > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+        if (e != cudaSuccess) return cuda_err(e, "cudaFuncSetAttribute");
+    }
+    return NEON_OK;
+}
+
+int init_device(int device) {
+    if (device < 0 || device >= kMaxDevices) return set_err(NEON_ERR_INVALID, "device index out of range");
+    DeviceState& st = g_dev[device];
+    std::lock_guard<std::mutex> lk(g_init_mu);
+    if (st.ready) return NEON_OK;
+    int n = 0;
+    NEON_CUDA_TRY(cudaGetDeviceCount(&n));
+    if (device >= n) return set_err(NEON_ERR_INVALID, "device " + std::to_string(device) + " not present");
+    DeviceGuard g(device);
+    if (!g.ok) return set_err(NEON_ERR_CUDA, "cudaSetDevice failed");
+    cudaDeviceProp p;
+    NEON_CUDA_TRY(cudaGetDeviceProperties(&p, device));
+    if (p.major < 10)
+        return set_err(NEON_ERR_UNSUPPORTED, std::string("device ") + p.name +
+                                                 " is not sm_100-class; this library is built for sm_100a only");
+    st.sms = p.multiProcessorCount;
+    NEON_CUDA_TRY(cudaStreamCreateWithFlags(&st.stream, cudaStreamNonBlocking));
+    // Occupancy at a typical input dim (4096) sets the decode grid size.
+    int rc = ensure_smem(q4_0_seq1_kernel<kQ4R, kQ4U>, kMaxSmem);
+    if (rc) return rc;
+    rc = ensure_smem(q8_0_seq1_kernel<kQ8R, kQ8U>, kMaxSmem);
+    if (rc) return rc;
+    NEON_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&st.occ_q4, q4_0_seq1_kernel<kQ4R, kQ4U>,
+                                                                kThreads, q4_seq1_smem_bytes(128)));
+    NEON_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&st.occ_q8, q8_0_seq1_kernel<kQ8R, kQ8U>,
+                                                                kThreads, q8_seq1_smem_bytes(128)));
+    st.occ_q4 = std::max(1, st.occ_q4);
+    st.occ_q8 = std::max(1, st.occ_q8);
+    st.ready = true;
+    return NEON_OK;
+}
+
+int current_device(int* dev) {
+    cudaError_t e = cudaGetDevice(dev);
+    if (e != cudaSuccess) return cuda_err(e, "cudaGetDevice");
+    return init_device(*dev);
+}
+
+template <typename... KArgs, typename... Args>
+int launch(void (*kern)(KArgs...), dim3 grid, size_t smem, cudaStream_t st, Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    if (g_pdl.load(std::memory_order_relaxed)) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+    if (e != cudaSuccess) return cuda_err(e, "cudaLaunchKernelEx");
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return NEON_OK;
+}
+
+int grow(void** p, size_t* cap, size_t need) {
+    if (*cap >= need) return NEON_OK;
+    if (*p) cudaFree(*p);
+    *p = nullptr;
+    *cap = 0;
+    cudaError_t e = cudaMalloc(p, need);
+    if (e != cudaSuccess) {
+        *p = nullptr;
+        return set_err(NEON_ERR_NOMEM, std::string("cudaMalloc of library scratch failed: ") + cudaGetErrorString(e));
+    }
+    *cap = need;
+    return NEON_OK;
+}
+
+// Device scratch for seq*cols Q8_0 activations (quants, scales, sums).
+int ensure_act_scratch(DeviceState& st, size_t n) {
+    if (st.scratch_cols >= n) return NEON_OK;
+    if (st.xq) cudaFree(st.xq);
+    if (st.xd) cudaFree(st.xd);
+    if (st.xs) cudaFree(st.xs);
+    st.xq = nullptr; st.xd = nullptr; st.xs = nullptr; st.scratch_cols = 0;
+    size_t nblk = n / 32 + 1;
+    if (cudaMalloc(&st.xq, n) != cudaSuccess || cudaMalloc(&st.xd, nblk * 4) != cudaSuccess ||
+        cudaMalloc(&st.xs, nblk * 4) != cudaSuccess)
+        return set_err(NEON_ERR_NOMEM, "cudaMalloc of activation scratch failed");
+    st.scratch_cols = n;
+    return NEON_OK;
+}
+
+int validate_tensor(neon_tensor_t W) {
+    if (!W) return set_err(NEON_ERR_INVALID, "null tensor handle");
+    if (!supported_type(W->type)) return set_err(NEON_ERR_UNSUPPORTED, "tensor type not supported");
+    return NEON_OK;
+}
+
+// One group of targets that share type and input dim -> one launch.
+struct Group {
+    int type;
+    size_t cols;
+    std::vector<const neon_proj_target_t*> t;
+};
+
+int launch_group(const Group& g, const float* dX, size_t x_stride, size_t seq, cudaStream_t st,
+                 DeviceState& ds) {
+    const int nb = (int)(g.cols / 32);
+    const bool q4 = g.type == NEON_GGML_Q4_0;
+    const int R = seq == 1 ? (q4 ? kQ4R : kQ8R) : kMpR;
+    size_t start = 0;
+    while (start < g.t.size()) {
+        MatvecArgs a;
+        std::memset(&a, 0, sizeof(a));
+        a.x = dX;
+        a.x_stride = (long long)x_stride;
+        a.nb = nb;
+        a.seq = (int)seq;
+        int tiles = 0;
+        size_t n = std::min(g.t.size() - start, (size_t)kMaxSpans);
+        for (size_t i = 0; i < n; ++i) {
+            const neon_proj_target_t* tg = g.t[start + i];
+            Span& s = a.span[i];
+            s.qs = tg->W->qs;
+            s.d = tg->W->d;
+            s.y = tg->Y;
+            s.y_stride = (long long)tg->y_stride;
+            s.rows = (int)tg->W->rows;
+            s.tile0 = tiles;
+            tiles += (int)((tg->W->rows + R - 1) / R);
+        }
+        a.n_spans = (int)n;
+        a.n_tiles = tiles;
+        int rc;
+        if (seq == 1) {
+            const int smem = q4 ? q4_seq1_smem_bytes(nb) : q8_seq1_smem_bytes(nb);
+            if (smem > kMaxSmem)
+                return set_err(NEON_ERR_UNSUPPORTED, "input dim " + std::to_string(g.cols) +
+                                                         " exceeds the one-position kernel's shared-memory limit");
+            int ctas = (tiles + kWarps - 1) / kWarps;
+            ctas = std::min(ctas, ds.sms * (q4 ? ds.occ_q4 : ds.occ_q8));
+            if (q4)
+                rc = launch(q4_0_seq1_kernel<kQ4R, kQ4U>, dim3(ctas), smem, st, a);
+            else
+                rc = launch(q8_0_seq1_kernel<kQ8R, kQ8U>, dim3(ctas), smem, st, a);
+        } else {
+            if (q4) {
+                a.xq = ds.xq;
+                a.xd = ds.xd;
+                a.xs = ds.xs;
+            }
+            int ctas = (tiles + kWarps - 1) / kWarps;
+            ctas = std::min(ctas, ds.sms * 4);
+            dim3 grid(ctas, (unsigned)((seq + kMpT - 1) / kMpT));
+            if (q4)
+                rc = launch(matvec_multipos_kernel<NEON_GGML_Q4_0, kMpR, kMpT>, grid, 0, st, a);
+            else
+                rc = launch(matvec_multipos_kernel<NEON_GGML_Q8_0, kMpR, kMpT>, grid, 0, st, a);
+        }
+        if (rc) return rc;
+        start += n;
+    }
+    return NEON_OK;
+}
+
+// Shared body of neon_cuda_matvec[_multi] on device buffers.
+int matvec_targets(const neon_proj_target_t* targets, size_t n_targets, const float* dX,
+                   size_t x_stride, size_t seq, void* stream) {
+    if (n_targets == 0 || seq == 0) return NEON_OK;
+    if (!targets || !dX) return set_err(NEON_ERR_INVALID, "null targets or X");
+    int device = targets[0].W ? targets[0].W->device : -1;
+    std::vector<Group> groups;
+    size_t q4_cols = 0;
+    for (size_t i = 0; i < n_targets; ++i) {
+        const neon_proj_target_t& tg = targets[i];
+        int rc = validate_tensor(tg.W);
+        if (rc) return rc;
+        if (!tg.Y) return set_err(NEON_ERR_INVALID, "null output pointer");
+        if (tg.W->device != device)
+            return set_err(NEON_ERR_INVALID, "targets of one call live on different devices");
+        if (seq > 1 && tg.y_stride < tg.W->rows)
+            return set_err(NEON_ERR_INVALID, "y_stride smaller than the tensor's rows");
+        if (tg.W->type == NEON_GGML_Q4_0) {
+            if (q4_cols != 0 && q4_cols != tg.W->cols)
+                return set_err(NEON_ERR_INVALID,
+                               "forward(): proj_all_positions_multi() got Q4_0 targets with mismatched input dims (" +
+                                   std::to_string(q4_cols) + " vs " + std::to_string(tg.W->cols) +
+                                   ") in one call -- the shared Q8_0 activation buffer assumes all fused Q4_0 "
+                                   "targets share `cols`");
+            q4_cols = tg.W->cols;
+        }
+        Group* g = nullptr;
+        for (auto& gg : groups)
+            if (gg.type == tg.W->type && gg.cols == tg.W->cols) g = &gg;
+        if (!g) {
+            groups.push_back(Group{tg.W->type, tg.W->cols, {}});
+            g = &groups.back();
+        }
+        g->t.push_back(&tg);
+    }
+    DeviceGuard guard(device);
+    if (!guard.ok) return set_err(NEON_ERR_CUDA, "cudaSetDevice failed");
+    int rc = init_device(device);
+    if (rc) return rc;
+    DeviceState& ds = g_dev[device];
+    cudaStream_t st = (cudaStream_t)stream;
+    if (seq > 1 && q4_cols) {
+        // Quantise X once for every Q4_0 target (quantize_rows_q8_0 on the
+        // calling thread in the reference, rawllm_forward.hpp:544-552).
+        rc = ensure_act_scratch(ds, seq * q4_cols);
+        if (rc) return rc;
+        const int nb = (int)(q4_cols / 32);
+        long long blocks = (long long)nb * (long long)seq;
+        int ctas = (int)std::min<long long>((blocks + kWarps - 1) / kWarps, (long long)ds.sms * 8);
+        rc = launch(quantize_q8_0_kernel, dim3(ctas), 0, st, dX, (long long)x_stride, nb, (int)seq, ds.xq,
+                    ds.xd, ds.xs);
+        if (rc) return rc;
+    }
+    for (const Group& g : groups) {
+        rc = launch_group(g, dX, x_stride, seq, st, ds);
+        if (rc) return rc;
+    }
+    return NEON_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* neon_cuda_last_error(void) { return g_err.c_str(); }
+
+const char* neon_cuda_version(void) { return "0.1.0"; }
+
+int neon_cuda_device_count(int* count) {
+    if (!count) return set_err(NEON_ERR_INVALID, "null count");
+    cudaError_t e = cudaGetDeviceCount(count);
+    if (e == cudaErrorNoDevice || e == cudaErrorInsufficientDriver) {
+        *count = 0;
+        cudaGetLastError();
+        return NEON_OK;
+    }
+    if (e != cudaSuccess) return cuda_err(e, "cudaGetDeviceCount");
+    return NEON_OK;
+}
+
+int neon_cuda_init(int device) {
+    int rc = init_device(device);
+    if (rc) return rc;
+    NEON_CUDA_TRY(cudaSetDevice(device));
+    return NEON_OK;
+}
+
+int neon_cuda_set_pdl(int enabled) {
+    g_pdl.store(enabled ? 1 : 0);
+    return NEON_OK;
+}
+
+uint64_t neon_cuda_launch_count(void) { return g_launches.load(); }
+
+int neon_cuda_upload(const uint8_t* host_bytes, int ggml_type, size_t rows, size_t cols, int shard_mode,
+                     int shard_index, int shard_count, neon_tensor_t* out) {
+    if (!out) return set_err(NEON_ERR_INVALID, "null output handle");
+    *out = nullptr;
+    if (!host_bytes) return set_err(NEON_ERR_INVALID, "null weight bytes");
+    if (!supported_type(ggml_type))
+        return set_err(NEON_ERR_UNSUPPORTED, "quant type " + std::to_string(ggml_type) +
+                                                 " is not supported by the CUDA backend (Q4_0 and Q8_0 are)");
+    if (rows == 0 || cols == 0) return set_err(NEON_ERR_INVALID, "empty tensor");
+    if (cols % 32 != 0)
+        return set_err(NEON_ERR_INVALID, "forward(): input dim (" + std::to_string(cols) +
+                                             ") isn't a multiple of its quant block size (32) -- can't dequantize safely.");
+    if (rows > (size_t)INT32_MAX / 2 || cols / 32 > (size_t)INT32_MAX / 64)
+        return set_err(NEON_ERR_INVALID, "tensor too large");
+    size_t nb = cols / 32;
+    size_t r0 = 0, r1 = rows, b0 = 0, b1 = nb;
+    if (shard_mode != NEON_SHARD_NONE) {
+        if (shard_count <= 0 || shard_index < 0 || shard_index >= shard_count)
+            return set_err(NEON_ERR_INVALID, "bad shard index/count");
+        if (shard_mode == NEON_SHARD_ROWS) {
+            r0 = rows * (size_t)shard_index / (size_t)shard_count;
+            r1 = rows * (size_t)(shard_index + 1) / (size_t)shard_count;
+        } else if (shard_mode == NEON_SHARD_COLS) {
+            b0 = nb * (size_t)shard_index / (size_t)shard_count;
+            b1 = nb * (size_t)(shard_index + 1) / (size_t)shard_count;
+        } else {
+            return set_err(NEON_ERR_INVALID, "unknown shard mode");
+        }
+        if (r1 <= r0 || b1 <= b0) return set_err(NEON_ERR_INVALID, "empty shard");
+    }
+    int device = 0;
+    int rc = current_device(&device);
+    if (rc) return rc;
+    const size_t P = payload_bytes(ggml_type);
+    const size_t src_row = nb * gguf_block_bytes(ggml_type);
+    const size_t lrows = r1 - r0, lnb = b1 - b0;
+    const size_t qs_bytes = lrows * lnb * P;
+    const size_t d_off = (qs_bytes + 255) / 256 * 256;
+    const size_t total = d_off + lrows * lnb * 2;
+
+    neon_tensor* t = new neon_tensor();
+    t->device = device;
+    t->type = ggml_type;
+    t->rows = lrows;
+    t->cols = lnb * 32;
+    t->nb = lnb;
+    t->bytes = total;
+    cudaError_t e = cudaMalloc(&t->base, total);
+    if (e != cudaSuccess) {
+        delete t;
+        return set_err(NEON_ERR_NOMEM, std::string("cudaMalloc of weights failed: ") + cudaGetErrorString(e));
+    }
+    t->qs = t->base;
+    t->d = reinterpret_cast<uint16_t*>(t->base + d_off);
+
+    // Stage the GGUF rows in chunks of <= 256 MiB and repack them on the device.
+    const size_t chunk_rows = std::max<size_t>(1, (256u << 20) / src_row);
+    uint8_t* tmp = nullptr;
+    size_t tmp_bytes = std::min(lrows, chunk_rows) * src_row;
+    e = cudaMalloc(&tmp, tmp_bytes);
+    if (e != cudaSuccess) {
+        cudaFree(t->base);
+        delete t;
+        return set_err(NEON_ERR_NOMEM, "cudaMalloc of the upload staging buffer failed");
+    }
+    cudaStream_t st = g_dev[device].stream;
+    for (size_t c = 0; c < lrows; c += chunk_rows) {
+        size_t nr = std::min(chunk_rows, lrows - c);
+        e = cudaMemcpyAsync(tmp, host_bytes + (r0 + c) * src_row, nr * src_row, cudaMemcpyHostToDevice, st);
+        if (e != cudaSuccess) break;
+        long long n = (long long)nr * (long long)lnb;
+        int grid = (int)std::min<long long>((n + 255) / 256, 65535LL * 8);
+        repack_kernel<<<grid, 256, 0, st>>>(tmp, (long long)src_row, (int)nr, (int)b0, (int)lnb, (int)P,
+                                            t->qs + c * lnb * P, t->d + c * lnb);
+        g_launches.fetch_add(1, std::memory_order_relaxed);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) break;
+        e = cudaStreamSynchronize(st);  // tmp is reused by the next chunk
+        if (e != cudaSuccess) break;
+    }
+    cudaFree(tmp);
+    if (e != cudaSuccess) {
+        cudaFree(t->base);
+        delete t;
+        return cuda_err(e, "weight upload");
+    }
+    *out = t;
+    return NEON_OK;
+}
+
+int neon_cuda_tensor_info(neon_tensor_t W, size_t* rows, size_t* cols, int* ggml_type, size_t* device_bytes) {
+    if (!W) return set_err(NEON_ERR_INVALID, "null tensor handle");
+    if (rows) *rows = W->rows;
+    if (cols) *cols = W->cols;
+    if (ggml_type) *ggml_type = W->type;
+    if (device_bytes) *device_bytes = W->bytes;
+    return NEON_OK;
+}
+
+int neon_cuda_free(neon_tensor_t W) {
+    if (!W) return NEON_OK;
+    DeviceGuard g(W->device);
+    cudaError_t e = cudaFree(W->base);
+    delete W;
+    if (e != cudaSuccess) return cuda_err(e, "cudaFree");
+    return NEON_OK;
+}
+
+int neon_cuda_quantize_q8_0(const float* dX, size_t x_stride, size_t cols, size_t seq, float* d_out,
+                            int8_t* q_out, void* stream) {
+    if (seq == 0 || cols == 0) return NEON_OK;
+    if (!dX || !d_out || !q_out) return set_err(NEON_ERR_INVALID, "null pointer");
+    if (cols % 32 != 0) return set_err(NEON_ERR_INVALID, "cols is not a multiple of 32");
+    int device = 0;
+    int rc = current_device(&device);
+    if (rc) return rc;
+    const int nb = (int)(cols / 32);
+    long long blocks = (long long)nb * (long long)seq;
+    int ctas = (int)std::min<long long>((blocks + kWarps - 1) / kWarps, (long long)g_dev[device].sms * 8);
+    return launch(quantize_q8_0_kernel, dim3(ctas), 0, (cudaStream_t)stream, dX, (long long)x_stride, nb,
+                  (int)seq, q_out, d_out, (int*)nullptr);
+}
+
+int neon_cuda_matvec(neon_tensor_t W, const float* dX, size_t x_stride, float* dY, size_t y_stride, size_t seq,
+                     void* stream) {
+    neon_proj_target_t t{W, dY, y_stride};
+    return matvec_targets(&t, 1, dX, x_stride, seq, stream);
+}
+
+int neon_cuda_matvec_multi(const neon_proj_target_t* targets, size_t n_targets, const float* dX, size_t x_stride,
+                           size_t seq, void* stream) {
+    return matvec_targets(targets, n_targets, dX, x_stride, seq, stream);
+}
+
+int neon_cuda_proj_all_positions_multi(const neon_proj_target_t* targets, size_t n_targets, const float* hX,
+                                       size_t x_stride, size_t seq) {
+    if (n_targets == 0 || seq == 0) return NEON_OK;
+    if (!targets || !hX) return set_err(NEON_ERR_INVALID, "null targets or X");
+    int rc = validate_tensor(targets[0].W);
+    if (rc) return rc;
+    const int device = targets[0].W->device;
+    rc = init_device(device);
+    if (rc) return rc;
+    DeviceState& ds = g_dev[device];
+    std::lock_guard<std::mutex> lk(ds.mu);
+    DeviceGuard guard(device);
+    size_t x_elems = (seq - 1) * x_stride + targets[0].W->cols;
+    for (size_t i = 0; i < n_targets; ++i)
+        if (targets[i].W) x_elems = std::max(x_elems, (seq - 1) * x_stride + targets[i].W->cols);
+    std::vector<size_t> y_off(n_targets), y_len(n_targets);
+    size_t y_total = 0;
+    for (size_t i = 0; i < n_targets; ++i) {
+        rc = validate_tensor(targets[i].W);
+        if (rc) return rc;
+        size_t ys = seq > 1 ? targets[i].y_stride : targets[i].W->rows;
+        y_len[i] = (seq - 1) * ys + targets[i].W->rows;
+        y_off[i] = y_total;
+        y_total += (y_len[i] + 63) / 64 * 64;
+    }
+    rc = grow((void**)&ds.dx, &ds.dx_cap, x_elems * 4);
+    if (rc) return rc;
+    rc = grow((void**)&ds.dy, &ds.dy_cap, y_total * 4);
+    if (rc) return rc;
+    cudaStream_t st = ds.stream;
+    NEON_CUDA_TRY(cudaMemcpyAsync(ds.dx, hX, x_elems * 4, cudaMemcpyHostToDevice, st));
+    std::vector<neon_proj_target_t> dt(targets, targets + n_targets);
+    for (size_t i = 0; i < n_targets; ++i) {
+        dt[i].Y = ds.dy + y_off[i];
+        dt[i].y_stride = seq > 1 ? targets[i].y_stride : targets[i].W->rows;
+        if (seq > 1 && targets[i].y_stride > targets[i].W->rows) {
+            // Positions between rows and y_stride keep the caller's values.
+            NEON_CUDA_TRY(cudaMemcpyAsync(dt[i].Y, targets[i].Y, y_len[i] * 4, cudaMemcpyHostToDevice, st));
+        }
+    }
+    rc = matvec_targets(dt.data(), n_targets, ds.dx, x_stride, seq, st);
+    if (rc) return rc;
+    for (size_t i = 0; i < n_targets; ++i)
+        NEON_CUDA_TRY(cudaMemcpyAsync(targets[i].Y, dt[i].Y, y_len[i] * 4, cudaMemcpyDeviceToHost, st));
+    NEON_CUDA_TRY(cudaStreamSynchronize(st));
+    return NEON_OK;
+}
+
+int neon_cuda_proj_all_positions(neon_tensor_t W, const float* hX, size_t x_stride, float* hY, size_t y_stride,
+                                 size_t seq) {
+    neon_proj_target_t t{W, hY, y_stride};
+    return neon_cuda_proj_all_positions_multi(&t, 1, hX, x_stride, seq);
+}
+
+int neon_cuda_sync(void* stream) {
+    NEON_CUDA_TRY(cudaStreamSynchronize((cudaStream_t)stream));
+    return NEON_OK;
+}
+
+}  // extern "C"

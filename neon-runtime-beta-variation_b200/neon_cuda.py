@@ -1,0 +1,292 @@
+"""Python binding of libneon_cuda.so (include/neon_cuda.h) with the NEON
+runtime's operator surface for the quantized matvec path.
+
+The reference runs every projection of its decode loop through
+``fwd::proj_all_positions(W, X, x_stride, Y, y_stride, seq, pool)`` and
+``fwd::proj_all_positions_multi(targets, X, x_stride, seq, pool)``
+(rawllm_forward.hpp:522-726) over ``loader::TensorInfo`` handles
+(rawllm_loader.hpp:34-41). This module keeps those names, argument meanings and
+error behaviour:
+
+* :class:`TensorInfo` -- name, GGUF shape ``[cols, rows]``, GGML type and the raw
+  tensor bytes (what ``data_ptr`` points at).
+* :func:`proj_all_positions` / :func:`proj_all_positions_multi` -- host numpy
+  buffers in and out, blocking, ``RuntimeError`` (the reference's
+  ``std::runtime_error``) with the reference's message on a bad argument.
+  Weights are uploaded to HBM on first use and stay there (a side table keyed
+  by the TensorInfo object), the load-time hook of rawllm_loader.hpp:84-177.
+* :class:`DeviceTensor` with :meth:`DeviceTensor.matvec` and :func:`matvec_multi`
+  -- the device-pointer entry points for callers that keep activations on the
+  GPU (torch tensors or raw pointers), asynchronous on a CUDA stream.
+
+There is no CPU fallback: if the CUDA library cannot be loaded, every call
+raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import threading
+import weakref
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libneon_cuda.so")
+
+NEON_OK = 0
+GGML_F32 = 0
+GGML_F16 = 1
+GGML_Q4_0 = 2
+GGML_Q8_0 = 8
+SHARD_NONE = 0
+SHARD_ROWS = 1
+SHARD_COLS = 2
+
+# Public C entry points, in the order include/neon_cuda.h declares them.
+C_ENTRY_POINTS = (
+    "neon_cuda_last_error",
+    "neon_cuda_version",
+    "neon_cuda_device_count",
+    "neon_cuda_init",
+    "neon_cuda_upload",
+    "neon_cuda_tensor_info",
+    "neon_cuda_free",
+    "neon_cuda_quantize_q8_0",
+    "neon_cuda_matvec",
+    "neon_cuda_matvec_multi",
+    "neon_cuda_proj_all_positions",
+    "neon_cuda_proj_all_positions_multi",
+    "neon_cuda_sync",
+    "neon_cuda_launch_count",
+    "neon_cuda_set_pdl",
+)
+
+_sz = C.c_size_t
+_vp = C.c_void_p
+
+
+class _Target(C.Structure):
+    _fields_ = [("W", _vp), ("Y", _vp), ("y_stride", _sz)]
+
+
+class NeonError(RuntimeError):
+    """A failed library call; the message is the library's (or the reference's)."""
+
+
+_lib = None
+_lock = threading.Lock()
+
+
+def load(path: str | None = None) -> C.CDLL:
+    """Load libneon_cuda.so (building it first if it is missing)."""
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        p = path or LIB_PATH
+        if not os.path.exists(p):
+            import importlib.util
+
+            spec = importlib.util.spec_from_file_location("_neon_build", os.path.join(HERE, "build.py"))
+            mod = importlib.util.module_from_spec(spec)
+            spec.loader.exec_module(mod)
+            mod.build()
+        L = C.CDLL(p)
+        L.neon_cuda_last_error.restype = C.c_char_p
+        L.neon_cuda_version.restype = C.c_char_p
+        L.neon_cuda_device_count.argtypes = [C.POINTER(C.c_int)]
+        L.neon_cuda_init.argtypes = [C.c_int]
+        L.neon_cuda_upload.argtypes = [_vp, C.c_int, _sz, _sz, C.c_int, C.c_int, C.c_int, C.POINTER(_vp)]
+        L.neon_cuda_tensor_info.argtypes = [_vp, C.POINTER(_sz), C.POINTER(_sz), C.POINTER(C.c_int),
+                                            C.POINTER(_sz)]
+        L.neon_cuda_free.argtypes = [_vp]
+        L.neon_cuda_quantize_q8_0.argtypes = [_vp, _sz, _sz, _sz, _vp, _vp, _vp]
+        L.neon_cuda_matvec.argtypes = [_vp, _vp, _sz, _vp, _sz, _sz, _vp]
+        L.neon_cuda_matvec_multi.argtypes = [C.POINTER(_Target), _sz, _vp, _sz, _sz, _vp]
+        L.neon_cuda_proj_all_positions.argtypes = [_vp, _vp, _sz, _vp, _sz, _sz]
+        L.neon_cuda_proj_all_positions_multi.argtypes = [C.POINTER(_Target), _sz, _vp, _sz, _sz]
+        L.neon_cuda_sync.argtypes = [_vp]
+        L.neon_cuda_launch_count.restype = C.c_uint64
+        L.neon_cuda_set_pdl.argtypes = [C.c_int]
+        _lib = L
+        return L
+
+
+def _check(rc: int) -> None:
+    if rc != NEON_OK:
+        raise NeonError(load().neon_cuda_last_error().decode(errors="replace"))
+
+
+def device_count() -> int:
+    n = C.c_int(0)
+    _check(load().neon_cuda_device_count(C.byref(n)))
+    return n.value
+
+
+def init(device: int = 0) -> None:
+    _check(load().neon_cuda_init(int(device)))
+
+
+def launch_count() -> int:
+    return int(load().neon_cuda_launch_count())
+
+
+def set_pdl(enabled: bool) -> None:
+    _check(load().neon_cuda_set_pdl(1 if enabled else 0))
+
+
+def sync(stream: int = 0) -> None:
+    _check(load().neon_cuda_sync(_vp(stream)))
+
+
+def _ptr(a) -> int:
+    """Address of a numpy array, a torch tensor or an int."""
+    if a is None:
+        return 0
+    if isinstance(a, int):
+        return a
+    if isinstance(a, np.ndarray):
+        return a.ctypes.data
+    if hasattr(a, "data_ptr"):
+        return int(a.data_ptr())
+    raise TypeError(f"cannot take the address of {type(a).__name__}")
+
+
+def _stream(stream) -> int:
+    if stream is None:
+        return 0
+    if isinstance(stream, int):
+        return stream
+    return int(getattr(stream, "cuda_stream", stream))
+
+
+# ---------------------------------------------------------------------------
+# device tensors
+# ---------------------------------------------------------------------------
+
+class DeviceTensor:
+    """A weight tensor resident in HBM (an uploaded GGUF tensor or shard)."""
+
+    def __init__(self, raw: np.ndarray, ggml_type: int, rows: int, cols: int,
+                 shard_mode: int = SHARD_NONE, shard_index: int = 0, shard_count: int = 1):
+        L = load()
+        raw = np.ascontiguousarray(raw)
+        h = _vp()
+        _check(L.neon_cuda_upload(raw.ctypes.data, int(ggml_type), int(rows), int(cols), int(shard_mode),
+                                  int(shard_index), int(shard_count), C.byref(h)))
+        self.handle = h.value
+        r, c, t, b = _sz(), _sz(), C.c_int(), _sz()
+        _check(L.neon_cuda_tensor_info(self.handle, C.byref(r), C.byref(c), C.byref(t), C.byref(b)))
+        self.rows, self.cols, self.type, self.device_bytes = r.value, c.value, t.value, b.value
+        self._fin = weakref.finalize(self, L.neon_cuda_free, self.handle)
+
+    def free(self) -> None:
+        self._fin()
+
+    def matvec(self, X, Y, seq: int = 1, x_stride: int | None = None, y_stride: int | None = None,
+               stream=None) -> None:
+        """Y[t*y_stride + r] = W_r . X_t on device buffers (torch tensors or pointers)."""
+        x_stride = self.cols if x_stride is None else x_stride
+        y_stride = self.rows if y_stride is None else y_stride
+        _check(load().neon_cuda_matvec(self.handle, _ptr(X), x_stride, _ptr(Y), y_stride, seq,
+                                       _vp(_stream(stream))))
+
+
+def matvec_multi(targets, X, seq: int = 1, x_stride: int | None = None, stream=None) -> None:
+    """targets: list of (DeviceTensor, Y device buffer, y_stride or None)."""
+    n = len(targets)
+    arr = (_Target * n)()
+    for i, (w, y, ys) in enumerate(targets):
+        arr[i].W = w.handle
+        arr[i].Y = _ptr(y)
+        arr[i].y_stride = w.rows if ys is None else ys
+    x_stride = targets[0][0].cols if x_stride is None else x_stride
+    _check(load().neon_cuda_matvec_multi(arr, n, _ptr(X), x_stride, seq, _vp(_stream(stream))))
+
+
+def quantize_q8_0(X, cols: int, seq: int, d_out, q_out, x_stride: int | None = None, stream=None) -> None:
+    """Device Q8_0 activation quantisation (bit-exact with quantize_rows_q8_0)."""
+    x_stride = cols if x_stride is None else x_stride
+    _check(load().neon_cuda_quantize_q8_0(_ptr(X), x_stride, cols, seq, _ptr(d_out), _ptr(q_out),
+                                          _vp(_stream(stream))))
+
+
+# ---------------------------------------------------------------------------
+# the reference's operator surface
+# ---------------------------------------------------------------------------
+
+class TensorInfo:
+    """Mirror of loader::TensorInfo (rawllm_loader.hpp:34-41): name, GGUF shape
+    ``[cols, rows]`` (contiguous dim first), GGML type and the tensor's raw
+    bytes (what ``data_ptr`` addresses)."""
+
+    def __init__(self, name: str, shape, ggml_type: int, data: np.ndarray):
+        self.name = name
+        self.shape = list(shape)
+        self.type = int(ggml_type)
+        self.data = np.ascontiguousarray(data).reshape(-1).view(np.uint8)
+        self.nbytes = self.data.nbytes
+
+
+class ProjTarget:
+    """Mirror of fwd::ProjTarget (rawllm_forward.hpp:626-630)."""
+
+    def __init__(self, W: TensorInfo, Y: np.ndarray, y_stride: int):
+        self.W, self.Y, self.y_stride = W, Y, y_stride
+
+
+_BLOCK = {GGML_Q4_0: 32, GGML_Q8_0: 32}
+_uploaded: "weakref.WeakKeyDictionary[TensorInfo, DeviceTensor]" = weakref.WeakKeyDictionary()
+
+
+def _check_shape(W: TensorInfo):
+    """The reference's argument checks (rawllm_forward.hpp:527-534)."""
+    if len(W.shape) < 2:
+        raise RuntimeError("forward(): expected a 2D weight tensor: " + W.name)
+    cols, rows = int(W.shape[0]), int(W.shape[1])
+    bs = _BLOCK.get(W.type, 1)
+    if cols % bs != 0:
+        raise RuntimeError(f"forward(): {W.name} input dim ({cols}) isn't a multiple of its quant block "
+                           f"size ({bs}) — can't dequantize safely.")
+    return cols, rows
+
+
+def upload(W: TensorInfo) -> DeviceTensor:
+    """The one-time HBM upload of a tensor (cached per TensorInfo)."""
+    dt = _uploaded.get(W)
+    if dt is None:
+        cols, rows = _check_shape(W)
+        dt = DeviceTensor(W.data, W.type, rows, cols)
+        _uploaded[W] = dt
+    return dt
+
+
+def proj_all_positions(W: TensorInfo, X: np.ndarray, x_stride: int, Y: np.ndarray, y_stride: int,
+                       seq: int, pool=None) -> None:
+    """Y[t*y_stride + r] = W_r . X_t (host buffers, blocking). ``pool`` is
+    accepted for signature parity with the reference and ignored: the GPU grid
+    replaces the CPU thread pool."""
+    _check_shape(W)
+    dt = upload(W)
+    X = np.ascontiguousarray(X, dtype=np.float32)
+    if Y.dtype != np.float32 or not Y.flags.c_contiguous:
+        raise RuntimeError("Y must be a C-contiguous float32 array")
+    _check(load().neon_cuda_proj_all_positions(dt.handle, X.ctypes.data, x_stride, Y.ctypes.data, y_stride,
+                                               seq))
+
+
+def proj_all_positions_multi(targets, X: np.ndarray, x_stride: int, seq: int, pool=None) -> None:
+    """Several ProjTargets that share X (host buffers, blocking)."""
+    n = len(targets)
+    for t in targets:
+        _check_shape(t.W)
+    arr = (_Target * n)()
+    for i, t in enumerate(targets):
+        if t.Y.dtype != np.float32 or not t.Y.flags.c_contiguous:
+            raise RuntimeError("Y must be a C-contiguous float32 array")
+        arr[i].W = upload(t.W).handle
+        arr[i].Y = t.Y.ctypes.data
+        arr[i].y_stride = t.y_stride
+    X = np.ascontiguousarray(X, dtype=np.float32)
+    _check(load().neon_cuda_proj_all_positions_multi(arr, n, X.ctypes.data, x_stride, seq))

@@ -1,0 +1,42 @@
+"""Test configuration: import paths, the `gpu` marker and shared helpers.
+
+`-m "not gpu"` runs on any CPU host (oracle against the golden vectors, oracle
+against the reference's own compiled path, the C ABI's exports and host-side
+checks). `-m gpu` runs the parity tests of the CUDA kernels on a B200.
+"""
+import os
+import sys
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+PKG = os.path.join(ROOT, "neon-runtime-beta-variation_b200")
+GOLDEN = os.path.join(ROOT, "tests", "golden")
+for p in (os.path.join(ROOT, "oracle"), PKG, ROOT):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA GPU (sm_100a, B200)")
+
+
+def load_golden(name):
+    return np.load(os.path.join(GOLDEN, name))
+
+
+# fp32 parity bar of the matvec outputs: per output element (one matrix row),
+# |y - y_ref| <= 1e-3 * max(|y_ref|, 0.01 * rms(y_ref)). The floor keeps rows
+# whose exact value is ~0 from turning fp32 summation-order noise into an
+# unbounded relative error.
+MATVEC_RTOL = 1e-3
+
+
+def max_rel_err(y, ref):
+    y = np.asarray(y, np.float64).reshape(-1)
+    ref = np.asarray(ref, np.float64).reshape(-1)
+    if ref.size == 0:
+        return 0.0
+    floor = 0.01 * np.sqrt(np.mean(ref * ref)) + 1e-30
+    return float(np.max(np.abs(y - ref) / np.maximum(np.abs(ref), floor)))

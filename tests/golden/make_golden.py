@@ -1,0 +1,133 @@
+"""Generate the golden vectors in tests/golden/ from the reference itself.
+
+    make -C oracle ref && python tests/golden/make_golden.py
+
+Every expected output here is produced by the reference's own CPU path --
+rawllm_forward.hpp compiled with the reference's flags into
+oracle/_ref/libneon_ref.so (oracle/Makefile) -- on seeded synthetic inputs.
+The reference ships no golden vectors or known-answer tests of its own for
+this path, so these fixtures are what pins both the C restatement in
+oracle/neon_oracle.c and the CUDA kernels.
+
+Outputs (numpy .npz, a few hundred KB in all):
+  quantize_q8_0.npz  X -> (d, q) of quantize_rows_q8_0, incl. edge cases
+  block_isum.npz     4096 random Q4_0 blocks x Q8_0 blocks -> isum
+  matvec.npz         Q4_0 / Q8_0 proj_all_positions cases (W bytes, X, Y)
+  multi.npz          a proj_all_positions_multi case shaped like Q/K/V
+"""
+from __future__ import annotations
+
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+sys.path.insert(0, os.path.join(ROOT, "neon-runtime-beta-variation_b200"))
+
+import oracle as O  # noqa: E402
+import synth as S  # noqa: E402
+
+# (type, rows, cols, seq): small shapes, ragged row counts, the smallest
+# input dim (32), several positions, and one full 4096-wide row set.
+MATVEC_CASES = [
+    (S.GGML_Q4_0, 64, 256, 1),
+    (S.GGML_Q4_0, 37, 4096, 1),
+    (S.GGML_Q4_0, 5, 32, 1),
+    (S.GGML_Q4_0, 24, 1024, 3),
+    (S.GGML_Q4_0, 130, 96, 2),
+    (S.GGML_Q8_0, 64, 256, 1),
+    (S.GGML_Q8_0, 19, 4096, 1),
+    (S.GGML_Q8_0, 3, 32, 1),
+    (S.GGML_Q8_0, 24, 1024, 3),
+    (S.GGML_Q8_0, 70, 160, 2),
+]
+
+
+def quantize_inputs() -> np.ndarray:
+    rng = np.random.default_rng(101)
+    blocks = []
+    blocks.append(rng.standard_normal(32).astype(np.float32))               # ordinary
+    blocks.append(np.zeros(32, np.float32))                                  # amax = 0 -> d = 0
+    blocks.append((rng.standard_normal(32) * 1e-39).astype(np.float32))      # denormal inputs
+    blocks.append((rng.standard_normal(32) * 1e-43).astype(np.float32))      # 1/d overflows
+    blocks.append((rng.standard_normal(32) * 3e37).astype(np.float32))       # near FLT_MAX
+    b = rng.standard_normal(32).astype(np.float32); b[3] = np.inf; blocks.append(b)
+    b = rng.standard_normal(32).astype(np.float32); b[7] = np.nan; blocks.append(b)
+    b = rng.standard_normal(32).astype(np.float32); b[:] = np.nan; blocks.append(b)
+    b = np.zeros(32, np.float32); b[0] = -127.0; b[1:] = np.arange(-15.5, 15.5, 1.0, dtype=np.float32)
+    blocks.append(b)                                                         # exact halfway cases
+    b = np.full(32, 2.5, np.float32); b[0] = 127.0; b[1] = -2.5; blocks.append(b)
+    b = rng.integers(-127, 128, 32).astype(np.float32) * np.float32(0.37); blocks.append(b)
+    blocks.append(np.full(32, -0.0, np.float32))
+    x = np.concatenate(blocks)
+    # plus 3 rows x 4096 of N(0,1) for the seq > 1 layout
+    more = rng.standard_normal((3, 4096)).astype(np.float32)
+    return x, more
+
+
+def main() -> None:
+    R = O.ref()
+    if R is None:
+        raise SystemExit("oracle/_ref/libneon_ref.so is missing: run `make -C oracle ref` first")
+    pool = O.RefPool(4)
+
+    # --- quantize_rows_q8_0
+    x_edge, x_rows = quantize_inputs()
+    X1 = x_edge.reshape(1, -1)
+    d1 = np.empty((1, X1.shape[1] // 32), np.float32)
+    q1 = np.empty(X1.shape, np.int8)
+    R.ref_quantize_rows_q8_0(X1.reshape(-1), X1.shape[1], X1.shape[1], 1, d1.reshape(-1), q1.reshape(-1))
+    d3 = np.empty((3, 128), np.float32)
+    q3 = np.empty((3, 4096), np.int8)
+    R.ref_quantize_rows_q8_0(x_rows.reshape(-1), 4096, 4096, 3, d3.reshape(-1), q3.reshape(-1))
+    np.savez_compressed(os.path.join(HERE, "quantize_q8_0.npz"), x_edge=X1, d_edge=d1, q_edge=q1,
+                        x_rows=x_rows, d_rows=d3, q_rows=q3)
+
+    # --- block isum (exact integer dot of 4096 random block pairs)
+    rng = np.random.default_rng(202)
+    qs = rng.integers(0, 256, (4096, 16), dtype=np.uint8)
+    xq = rng.integers(-127, 128, (4096, 32), dtype=np.int8)
+    xq[0] = 127; xq[1] = -127; qs[0] = 0xFF; qs[1] = 0x00
+    isum = np.array([R.ref_block_isum(qs[i], xq[i]) for i in range(len(qs))], np.int32)
+    np.savez_compressed(os.path.join(HERE, "block_isum.npz"), qs=qs, xq=xq, isum=isum)
+
+    # --- proj_all_positions cases
+    out = {}
+    for i, (typ, rows, cols, seq) in enumerate(MATVEC_CASES):
+        W = S.weights(typ, rows, cols, seed=1000 + i)
+        X = S.activations(seq, cols, seed=2000 + i)
+        Y = np.zeros((seq, rows), np.float32)
+        pool.proj_all_positions(typ, W, rows, cols, X, Y)
+        out[f"c{i}_meta"] = np.array([typ, rows, cols, seq], np.int64)
+        out[f"c{i}_W"] = W
+        out[f"c{i}_X"] = X
+        out[f"c{i}_Y"] = Y
+    out["n"] = np.array(len(MATVEC_CASES))
+    np.savez_compressed(os.path.join(HERE, "matvec.npz"), **out)
+
+    # --- proj_all_positions_multi: Q/K/V-shaped (q_dim 128, kv_dim 64), mixed types
+    cols, seq = 256, 2
+    specs = [(S.GGML_Q4_0, 128), (S.GGML_Q4_0, 64), (S.GGML_Q8_0, 64)]
+    X = S.activations(seq, cols, seed=3000)
+    targets, out = [], {}
+    for j, (typ, rows) in enumerate(specs):
+        W = S.weights(typ, rows, cols, seed=3100 + j)
+        Y = np.zeros((seq, rows), np.float32)
+        targets.append((typ, W, rows, cols, Y))
+        out[f"t{j}_meta"] = np.array([typ, rows, cols], np.int64)
+        out[f"t{j}_W"] = W
+    pool.proj_all_positions_multi(targets, X)
+    for j, t in enumerate(targets):
+        out[f"t{j}_Y"] = t[4]
+    out["X"] = X
+    out["n"] = np.array(len(specs))
+    np.savez_compressed(os.path.join(HERE, "multi.npz"), **out)
+    pool.close()
+    print("golden vectors written to", HERE)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,70 @@
+"""The C ABI library on a host without a GPU: it loads, exports every entry
+point include/neon_cuda.h declares, and the reference-mirroring argument checks
+of the Python surface raise the reference's errors before touching a device."""
+import ctypes
+import os
+import re
+import subprocess
+
+import numpy as np
+import pytest
+
+import neon_cuda as N
+from conftest import ROOT
+
+
+def header_functions():
+    text = open(os.path.join(ROOT, "include", "neon_cuda.h")).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(neon_cuda_\w+)\s*\(", text)))
+
+
+def test_library_builds_and_loads():
+    L = N.load()
+    assert L.neon_cuda_version().decode().count(".") == 2
+
+
+def test_exports_every_declared_symbol():
+    L = N.load()
+    declared = header_functions()
+    assert declared, "no declarations parsed"
+    for name in declared:
+        assert hasattr(L, name), f"{name} declared in include/neon_cuda.h but not exported"
+    assert sorted(N.C_ENTRY_POINTS) == declared
+    out = subprocess.run(["nm", "-D", "--defined-only", N.LIB_PATH], capture_output=True, text=True).stdout
+    exported = sorted(set(re.findall(r" T (neon_cuda_\w+)", out)))
+    assert exported == declared, "exported C symbols differ from the header"
+
+
+def test_no_gpu_host_calls_fail_cleanly():
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("host has a GPU")
+    L = N.load()
+    n = ctypes.c_int(-1)
+    assert L.neon_cuda_device_count(ctypes.byref(n)) == 0 and n.value == 0
+    h = ctypes.c_void_p()
+    raw = np.zeros(18, np.uint8)
+    rc = L.neon_cuda_upload(raw.ctypes.data, 2, 1, 32, 0, 0, 1, ctypes.byref(h))
+    assert rc != 0 and L.neon_cuda_last_error()
+
+
+def test_upload_argument_checks_precede_device_use():
+    L = N.load()
+    h = ctypes.c_void_p()
+    raw = np.zeros(64, np.uint8)
+    assert L.neon_cuda_upload(raw.ctypes.data, 2, 1, 31, 0, 0, 1, ctypes.byref(h)) == -1
+    assert b"multiple of its quant block size" in L.neon_cuda_last_error()
+    assert L.neon_cuda_upload(raw.ctypes.data, 12, 1, 256, 0, 0, 1, ctypes.byref(h)) == -2
+    assert L.neon_cuda_upload(None, 2, 1, 32, 0, 0, 1, ctypes.byref(h)) == -1
+    assert L.neon_cuda_upload(raw.ctypes.data, 2, 4, 32, 1, 3, 2, ctypes.byref(h)) == -1
+    assert L.neon_cuda_matvec(None, None, 0, None, 0, 1, None) == -1
+
+
+def test_reference_error_messages():
+    W = N.TensorInfo("blk.0.attn_q.weight", [4096], N.GGML_Q4_0, np.zeros(18, np.uint8))
+    with pytest.raises(RuntimeError, match="expected a 2D weight tensor: blk.0.attn_q.weight"):
+        N.proj_all_positions(W, np.zeros(4096, np.float32), 4096, np.zeros(1, np.float32), 1, 1)
+    W = N.TensorInfo("blk.0.ffn_up.weight", [100, 2], N.GGML_Q4_0, np.zeros(36, np.uint8))
+    with pytest.raises(RuntimeError, match=r"input dim \(100\) isn't a multiple of its quant block size \(32\)"):
+        N.proj_all_positions(W, np.zeros(100, np.float32), 100, np.zeros(2, np.float32), 2, 1)
