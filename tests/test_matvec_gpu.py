@@ -199,7 +199,7 @@ def test_row_and_col_shards(typ, n):
     W = S.weights(typ, rows, cols, seed=31)
     X = S.activations(1, cols, seed=32)
     full = O.proj_all_positions(typ, W, rows, cols, X)
-    dx = torch.from_numpy(X).cuda()
+    dx = torch.from_numpy(X[0]).cuda()
     parts = []
     for i in range(n):
         # output-dim split: rows [i*rows/n, (i+1)*rows/n)
