@@ -139,6 +139,19 @@ NEON_API int neon_cuda_sync(void* stream);
 /* Number of kernels this library has launched in this process (all devices). */
 NEON_API uint64_t neon_cuda_launch_count(void);
 
+/* Allocation-free Q4_0 matvec, for callers that cannot let a library allocate
+ * device memory (a server that has reserved all of HBM for its own pools, a
+ * framework allocator that holds the free memory, a loop that cannot take
+ * cudaMalloc's device-wide synchronisation). Same arguments and results as
+ * neon_cuda_matvec on a Q4_0 tensor, but the Q8_0 activations live in a fixed
+ * 1.25 MiB array compiled into the library (held by every GPU that loads it)
+ * instead of allocated scratch: seq*cols may not exceed 1,048,576. The first
+ * call on a device looks up that array's address; make it before any stream
+ * capture. Calls share the array, so calls that overlap on the GPU race.
+ * This entry point has no counterpart in the reference. */
+NEON_API int neon_cuda_matvec_q4_0_noalloc(neon_tensor_t W, const float* dX, size_t x_stride, float* dY,
+                                           size_t y_stride, size_t seq, void* stream);
+
 /* Launch option: programmatic dependent launch (PDL) lets a matvec fetch its
  * weights while the previous kernel on the stream finishes; on by default. */
 NEON_API int neon_cuda_set_pdl(int enabled);

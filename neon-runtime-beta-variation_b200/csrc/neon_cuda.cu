@@ -548,3 +548,106 @@ int neon_cuda_sync(void* stream) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of the multi-position Q4_0 matvec.
+//
+// neon_cuda_matvec quantises X into library scratch that it cudaMalloc's on
+// first use. Some callers cannot let a library allocate device memory: an
+// inference server that reserves all of HBM for its own weight and KV-cache
+// pools at start-up (a lazy cudaMalloc then fails, or breaks its budget), a
+// process whose framework caching allocator already holds the free memory, or
+// a latency-critical loop that cannot take cudaMalloc's implicit device-wide
+// synchronisation. neon_cuda_matvec_q4_0_noalloc runs the same two kernels
+// (quantize_q8_0_kernel, then matvec_multipos_kernel) with their scratch in
+// the fixed array below instead: it calls no cudaMalloc, cudaFree or other
+// allocating routine.
+//
+// The array is part of the library's device image, so every GPU that loads
+// the library holds its 1.25 MiB until the process exits. Its device address
+// is looked up once per device, on the first call made with that device's
+// tensor (cudaGetSymbolAddress with the device current); make that first call
+// before any stream capture. All calls share the one array: two calls whose
+// kernels overlap on the GPU (different streams, or different host threads)
+// race on it, so callers must order them. The quantiser writes every byte the
+// matvec then reads, so nothing has to be cleared between calls, and the
+// array keeps the last call's contents.
+// ---------------------------------------------------------------------------
+
+namespace {
+constexpr size_t kNoAllocMaxElems = size_t(1) << 20;           // seq * cols limit
+constexpr size_t kNoAllocQBytes = kNoAllocMaxElems;              // int8 quants
+constexpr size_t kNoAllocDBytes = kNoAllocMaxElems / 32 * 4;     // fp32 block scales
+constexpr size_t kNoAllocSBytes = kNoAllocMaxElems / 32 * 4;     // int32 block sums
+constexpr size_t kNoAllocBytes = kNoAllocQBytes + kNoAllocDBytes + kNoAllocSBytes;
+}  // namespace
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
+
+namespace {
+std::mutex g_noalloc_mu;
+unsigned char* g_noalloc_base[kMaxDevices] = {};
+
+// Device address of g_noalloc_scratch on `device` (which must be current).
+int noalloc_scratch(int device, unsigned char** base) {
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_base[device]) {
+        void* p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) return cuda_err(e, "cudaGetSymbolAddress");
+        g_noalloc_base[device] = static_cast<unsigned char*>(p);
+    }
+    *base = g_noalloc_base[device];
+    return NEON_OK;
+}
+}  // namespace
+
+extern "C" int neon_cuda_matvec_q4_0_noalloc(neon_tensor_t W, const float* dX, size_t x_stride, float* dY,
+                                             size_t y_stride, size_t seq, void* stream) {
+    if (!W) return set_err(NEON_ERR_INVALID, "null tensor handle");
+    if (W->type != NEON_GGML_Q4_0)
+        return set_err(NEON_ERR_UNSUPPORTED, "neon_cuda_matvec_q4_0_noalloc runs Q4_0 tensors only");
+    if (seq == 0) return NEON_OK;
+    if (!dX || !dY) return set_err(NEON_ERR_INVALID, "null X or Y");
+    if (seq > 1 && y_stride < W->rows) return set_err(NEON_ERR_INVALID, "y_stride smaller than the tensor's rows");
+    if (seq > kNoAllocMaxElems / W->cols)
+        return set_err(NEON_ERR_INVALID, "seq*cols = " + std::to_string(seq) + "*" + std::to_string(W->cols) +
+                                             " exceeds the allocation-free limit of " +
+                                             std::to_string(kNoAllocMaxElems) + " activation elements");
+    DeviceGuard guard(W->device);
+    if (!guard.ok) return set_err(NEON_ERR_CUDA, "cudaSetDevice failed");
+    unsigned char* base = nullptr;
+    int rc = noalloc_scratch(W->device, &base);
+    if (rc) return rc;
+    int sms = 0;
+    NEON_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, W->device));
+    int8_t* xq = reinterpret_cast<int8_t*>(base);
+    float* xd = reinterpret_cast<float*>(base + kNoAllocQBytes);
+    int* xs = reinterpret_cast<int*>(base + kNoAllocQBytes + kNoAllocDBytes);
+    cudaStream_t st = (cudaStream_t)stream;
+    const int nb = (int)W->nb;
+    const long long blocks = (long long)nb * (long long)seq;
+    int qctas = (int)std::min<long long>((blocks + kWarps - 1) / kWarps, (long long)sms * 8);
+    rc = launch(quantize_q8_0_kernel, dim3(qctas), 0, st, dX, (long long)x_stride, nb, (int)seq, xq, xd, xs);
+    if (rc) return rc;
+    MatvecArgs a;
+    std::memset(&a, 0, sizeof(a));
+    a.span[0].qs = W->qs;
+    a.span[0].d = W->d;
+    a.span[0].y = dY;
+    a.span[0].y_stride = (long long)(seq > 1 ? y_stride : W->rows);
+    a.span[0].rows = (int)W->rows;
+    a.span[0].tile0 = 0;
+    a.n_spans = 1;
+    a.n_tiles = (int)((W->rows + kMpR - 1) / kMpR);
+    a.nb = nb;
+    a.seq = (int)seq;
+    a.x = dX;
+    a.x_stride = (long long)x_stride;
+    a.xq = xq;
+    a.xd = xd;
+    a.xs = xs;
+    int ctas = std::min((a.n_tiles + kWarps - 1) / kWarps, sms * 4);
+    dim3 grid(ctas, (unsigned)((seq + kMpT - 1) / kMpT));
+    return launch(matvec_multipos_kernel<NEON_GGML_Q4_0, kMpR, kMpT>, grid, 0, st, a);
+}

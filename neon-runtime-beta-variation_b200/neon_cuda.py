@@ -59,6 +59,7 @@ C_ENTRY_POINTS = (
     "neon_cuda_proj_all_positions_multi",
     "neon_cuda_sync",
     "neon_cuda_launch_count",
+    "neon_cuda_matvec_q4_0_noalloc",
     "neon_cuda_set_pdl",
 )
 
@@ -109,6 +110,7 @@ def load(path: str | None = None) -> C.CDLL:
         L.neon_cuda_sync.argtypes = [_vp]
         L.neon_cuda_launch_count.restype = C.c_uint64
         L.neon_cuda_set_pdl.argtypes = [C.c_int]
+        L.neon_cuda_matvec_q4_0_noalloc.argtypes = [_vp, _vp, _sz, _vp, _sz, _sz, _vp]
         _lib = L
         return L
 
