@@ -44,14 +44,37 @@ import numpy as np  # noqa: E402
 
 import synth as S  # noqa: E402
 
-METRIC = "Q4_0 matvec HBM GB/s vs peak"
 UNIT = "GB/s"
-ROWS = COLS = 4096
-ROTATION = 48
 CALLS_PER_STEP = 1024
+ROTATION_BYTES = 3 * 126e6  # weights rotated per step: 3x the L2
 FALLBACK_HBM_GBS = 6650.0
-KERNEL = "q4_0_seq1_kernel"
-PROFILE_SUMMARY = os.path.join(ROOT, "profiles", "q4_0_seq1_kernel_4096x4096.txt")
+KERNEL = "matvec_stream_kernel"
+
+# name -> (ggml type, rows, cols); the first is the headline workload.
+WORKLOADS = {
+    "q4_0_4096x4096": (S.GGML_Q4_0, 4096, 4096),
+    "q8_0_4096x4096": (S.GGML_Q8_0, 4096, 4096),
+    "q8_0_14336x4096": (S.GGML_Q8_0, 14336, 4096),
+    "q8_0_4096x14336": (S.GGML_Q8_0, 4096, 14336),
+    "q4_0_28672x8192": (S.GGML_Q4_0, 28672, 8192),
+    "q4_0_8192x28672": (S.GGML_Q4_0, 8192, 28672),
+}
+TYPE, ROWS, COLS = WORKLOADS["q4_0_4096x4096"]
+ROTATION = 48
+METRIC = "Q4_0 matvec HBM GB/s vs peak"
+TYPE_NAME = "Q4_0"
+
+
+def select_workload(name):
+    global TYPE, ROWS, COLS, ROTATION, METRIC, TYPE_NAME
+    TYPE, ROWS, COLS = WORKLOADS[name]
+    TYPE_NAME = "Q4_0" if TYPE == S.GGML_Q4_0 else "Q8_0"
+    METRIC = f"{TYPE_NAME} matvec HBM GB/s vs peak"
+    ROTATION = max(2, int(-(-ROTATION_BYTES // (ROWS * S.row_bytes(TYPE, COLS)))))
+
+
+def profile_summary_path():
+    return os.path.join(ROOT, "profiles", f"matvec_stream_{TYPE_NAME.lower()}_{ROWS}x{COLS}.txt")
 
 
 def parse_args():
@@ -63,18 +86,22 @@ def parse_args():
     p.add_argument("--e2e-steps", type=int, default=3)
     p.add_argument("--cpu-seconds", type=float, default=12.0)
     p.add_argument("--no-cpu-baseline", action="store_true")
-    return p.parse_args()
+    p.add_argument("--workload", choices=sorted(WORKLOADS), default="q4_0_4096x4096")
+    args = p.parse_args()
+    select_workload(args.workload)
+    return args
 
 
 def workload_config():
+    dist = ("fp16 d=|N(0,1)|*0.02, nibbles U(0..15)" if TYPE == S.GGML_Q4_0
+            else "fp16 d=|N(0,1)|*0.01, int8 U(-127..127)")
     return {
-        "workload": "Q4_0 x fp32 matvec, W 4096x4096, batch 1 (fp16 d=|N(0,1)|*0.02, nibbles U(0..15), "
-                    "x N(0,1), seeded)",
+        "workload": f"{TYPE_NAME} x fp32 matvec, W {ROWS}x{COLS}, batch 1 ({dist}, x N(0,1), seeded)",
         "rows": ROWS, "cols": COLS, "batch": 1,
         "rotation_tensors": ROTATION, "calls_per_step": CALLS_PER_STEP,
         "l2": f"inputs larger than L2: {ROTATION} distinct weight tensors "
-              f"({ROTATION * S.row_bytes(S.GGML_Q4_0, COLS) * ROWS / 1e6:.0f} MB) rotated, L2 126 MB",
-        "bytes_per_call": S.algorithmic_bytes(S.GGML_Q4_0, ROWS, COLS),
+              f"({ROTATION * S.row_bytes(TYPE, COLS) * ROWS / 1e6:.0f} MB) rotated, L2 126 MB",
+        "bytes_per_call": S.algorithmic_bytes(TYPE, ROWS, COLS),
     }
 
 
@@ -90,7 +117,7 @@ def measured_peak():
 def profile_traffic():
     """DRAM bytes per launch of the kernel from the committed ncu summary."""
     try:
-        with open(PROFILE_SUMMARY) as f:
+        with open(profile_summary_path()) as f:
             for line in f:
                 if line.startswith("dram_bytes_per_launch:"):
                     return int(float(line.split(":", 1)[1].split()[0]))
@@ -172,12 +199,12 @@ def cpu_reference_gbs(host_weights, x, seconds, max_calls=None):
         kind, cores = "reference", pool.n
 
         def call(W, Y):
-            pool.proj_all_positions(S.GGML_Q4_0, W, ROWS, COLS, x, Y)
+            pool.proj_all_positions(TYPE, W, ROWS, COLS, x, Y)
     else:
         pool, kind, cores = None, "port", 1
 
         def call(W, Y):
-            Y[:] = O.proj_all_positions(S.GGML_Q4_0, W, ROWS, COLS, x)
+            Y[:] = O.proj_all_positions(TYPE, W, ROWS, COLS, x)
     Y = np.zeros((1, ROWS), np.float32)
     call(host_weights[0], Y)  # warm
     n, t0 = 0, time.perf_counter()
@@ -187,28 +214,28 @@ def cpu_reference_gbs(host_weights, x, seconds, max_calls=None):
     dt = time.perf_counter() - t0
     if pool is not None:
         pool.close()
-    gbs = n * S.algorithmic_bytes(S.GGML_Q4_0, ROWS, COLS) / dt / 1e9
+    gbs = n * S.algorithmic_bytes(TYPE, ROWS, COLS) / dt / 1e9
     return {"value": round(gbs, 3), "unit": UNIT, "cores": cores, "kind": kind,
-            "sample": f"{n} calls of proj_all_positions on Q4_0 4096x4096 over a rotation of "
+            "sample": f"{n} calls of proj_all_positions on {TYPE_NAME} {ROWS}x{COLS} over a rotation of "
                       f"{len(host_weights)} tensors in {dt:.1f} s"}
 
 
 def host_rotation(rank, n):
-    return [S.q4_0_weights(ROWS, COLS, seed=100000 * rank + i) for i in range(n)]
+    return [S.weights(TYPE, ROWS, COLS, seed=100000 * rank + i) for i in range(n)]
 
 
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    cpu_n = 16
+    cpu_n = min(16, ROTATION)
     weights = host_rotation(0, cpu_n)
     x = S.activations(1, COLS, seed=7)
     K, W = max(1, args.steps), max(0, args.warmup)
     budget = 120.0
     per_step_calls = cpu_n
     res = cpu_reference_gbs(weights, x, seconds=0.5)  # warm-up + calibration
-    est_call_s = S.algorithmic_bytes(S.GGML_Q4_0, ROWS, COLS) / (res["value"] * 1e9)
+    est_call_s = S.algorithmic_bytes(TYPE, ROWS, COLS) / (res["value"] * 1e9)
     per_step_calls = max(1, min(cpu_n, int(budget / max(1, K + W) / est_call_s)))
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
@@ -218,16 +245,16 @@ def run_reference(args):
     def step():
         for j in range(per_step_calls):
             if pool is not None:
-                pool.proj_all_positions(S.GGML_Q4_0, weights[j], ROWS, COLS, x, Y)
+                pool.proj_all_positions(TYPE, weights[j], ROWS, COLS, x, Y)
             else:
-                Y[:] = O.proj_all_positions(S.GGML_Q4_0, weights[j], ROWS, COLS, x)
+                Y[:] = O.proj_all_positions(TYPE, weights[j], ROWS, COLS, x)
     for _ in range(W):
         step()
     t0 = time.perf_counter()
     for _ in range(K):
         step()
     dt = time.perf_counter() - t0
-    value = K * per_step_calls * S.algorithmic_bytes(S.GGML_Q4_0, ROWS, COLS) / dt / 1e9
+    value = K * per_step_calls * S.algorithmic_bytes(TYPE, ROWS, COLS) / dt / 1e9
     cores = pool.n if pool is not None else 1
     kind = "reference" if pool is not None else "port"
     if pool is not None:
@@ -236,7 +263,7 @@ def run_reference(args):
     cfg["calls_per_step"] = per_step_calls
     cfg["rotation_tensors"] = cpu_n
     cfg["l2"] = (f"host: {cpu_n} distinct weight tensors "
-                 f"({cpu_n * S.row_bytes(S.GGML_Q4_0, COLS) * ROWS / 1e6:.0f} MB) rotated")
+                 f"({cpu_n * S.row_bytes(TYPE, COLS) * ROWS / 1e6:.0f} MB) rotated")
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": 0,
         "steps": K, "warmup": W, "ms_per_step": round(dt / K * 1e3, 4), "higher_is_better": True,
@@ -273,9 +300,10 @@ def run_neon(args):
     dev = torch.device("cuda", local)
 
     host_w = host_rotation(rank, ROTATION)
-    tensors = [N.DeviceTensor(w, S.GGML_Q4_0, ROWS, COLS) for w in host_w]
+    tensors = [N.DeviceTensor(w, TYPE, ROWS, COLS) for w in host_w]
     x_host = S.activations(1, COLS, seed=7)
     dx = torch.from_numpy(x_host).to(dev)
+    assert x_host.shape == (1, COLS)
     ys = torch.zeros((ROTATION, ROWS), device=dev)
     stream = torch.cuda.Stream(device=dev)
 
@@ -328,7 +356,7 @@ def run_neon(args):
         sampler.stop()
     assert N.launch_count() == launches_before, "graph replay should not go through the launch API"
     gpu_launches = K * CALLS_PER_STEP
-    bytes_call = S.algorithmic_bytes(S.GGML_Q4_0, ROWS, COLS)
+    bytes_call = S.algorithmic_bytes(TYPE, ROWS, COLS)
     total_bytes = world * K * CALLS_PER_STEP * bytes_call
     value = total_bytes / (ms / 1e3) / 1e9
     per_launch_s = ms / 1e3 / (K * CALLS_PER_STEP)
@@ -338,7 +366,7 @@ def run_neon(args):
     x_pin = torch.from_numpy(x_host.copy()).pin_memory()
     y_pin = torch.zeros(ROWS, dtype=torch.float32).pin_memory()
     x_np, y_np = x_pin.numpy(), y_pin.numpy()
-    infos = [N.TensorInfo(f"rot{i}", [COLS, ROWS], S.GGML_Q4_0, host_w[i]) for i in range(ROTATION)]
+    infos = [N.TensorInfo(f"rot{i}", [COLS, ROWS], TYPE, host_w[i]) for i in range(ROTATION)]
     for i in range(ROTATION):  # upload happens once, at "load" time, outside the timed region
         N.proj_all_positions(infos[i], x_np, COLS, y_np, ROWS, 1)
     e2e_steps = max(1, min(args.e2e_steps, K))
@@ -365,7 +393,10 @@ def run_neon(args):
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": K,
             "warmup": W, "ms_per_step": round(ms / K, 5), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "int8/fp32 (q4_0 x q8_0 dp4a, fp32 scales)", "data": "synthetic",
+            "vs_baseline": None,
+            "dtype": ("int8/fp32 (q4_0 x q8_0 dp4a, fp32 scales)" if TYPE == S.GGML_Q4_0
+                      else "fp32 (q8_0 int8 weights x fp32 x, fp32 accumulate)"),
+            "data": "synthetic",
             "config": {**workload_config(), "parallelism": f"dp{world} (independent rotations)",
                        "launch": "CUDA graph of 1024 PDL launches per step"},
             "e2e": {"value": round(e2e_value, 2), "unit": UNIT,

@@ -28,12 +28,14 @@ struct neon_tensor {
 namespace {
 
 constexpr int kMaxDevices = 64;
-// Rows per warp tile and 32-block chunks per lane of the decode kernels.
-constexpr int kQ4R = 2, kQ4U = 4;
-constexpr int kQ8R = 2, kQ8U = 2;
+// Rows per warp tile and positions per CTA of the multi-position kernel.
 constexpr int kMpR = 2, kMpT = 4;
-// Largest input dim a one-position launch stages in shared memory.
-constexpr int kMaxSmem = 200 * 1024;
+// Shared memory a streaming launch may use, and the target bytes of one ring
+// stage (weights of one item).
+constexpr int kMaxSmem = 220 * 1024;
+constexpr int kStageTarget = 40 * 1024;
+// Resident streaming CTAs per SM the grid is sized for.
+constexpr int kStreamCtasPerSm = 4;
 
 thread_local std::string g_err;
 std::atomic<uint64_t> g_launches{0};
@@ -42,7 +44,7 @@ std::atomic<int> g_pdl{1};
 struct DeviceState {
     bool ready = false;
     int sms = 0;
-    int occ_q4 = 0, occ_q8 = 0;  // resident CTAs per SM of the decode kernels
+    unsigned int* err = nullptr;  // device error word (g_neon_device_err on this device)
     std::mutex mu;
     // scratch of multi-position Q4_0 calls (activation quants)
     int8_t* xq = nullptr;
@@ -57,6 +59,12 @@ struct DeviceState {
 };
 DeviceState g_dev[kMaxDevices];
 std::mutex g_init_mu;
+}  // namespace
+
+// Device-side error word: bit 0 = a bounded wait in a kernel timed out.
+static __device__ unsigned int g_neon_device_err;
+
+namespace {
 
 int set_err(int code, const std::string& msg) {
     g_err = msg;
@@ -91,6 +99,9 @@ struct DeviceGuard {
     }
 };
 
+using StreamKernel = void (*)(StreamArgs);
+StreamKernel stream_kernel(int type, int rc);
+
 template <typename Kern>
 int ensure_smem(Kern k, int bytes) {
     if (bytes > 48 * 1024) {
@@ -117,17 +128,13 @@ int init_device(int device) {
                                                  " is not sm_100-class; this library is built for sm_100a only");
     st.sms = p.multiProcessorCount;
     NEON_CUDA_TRY(cudaStreamCreateWithFlags(&st.stream, cudaStreamNonBlocking));
-    // Occupancy at a typical input dim (4096) sets the decode grid size.
-    int rc = ensure_smem(q4_0_seq1_kernel<kQ4R, kQ4U>, kMaxSmem);
+    int rc = NEON_OK;
+    for (int t : {NEON_GGML_Q4_0, NEON_GGML_Q8_0})
+        for (int r : {2, 4, 8, 16, 32}) rc = rc ? rc : ensure_smem(stream_kernel(t, r), kMaxSmem);
     if (rc) return rc;
-    rc = ensure_smem(q8_0_seq1_kernel<kQ8R, kQ8U>, kMaxSmem);
-    if (rc) return rc;
-    NEON_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&st.occ_q4, q4_0_seq1_kernel<kQ4R, kQ4U>,
-                                                                kThreads, q4_seq1_smem_bytes(128)));
-    NEON_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&st.occ_q8, q8_0_seq1_kernel<kQ8R, kQ8U>,
-                                                                kThreads, q8_seq1_smem_bytes(128)));
-    st.occ_q4 = std::max(1, st.occ_q4);
-    st.occ_q8 = std::max(1, st.occ_q8);
+    void* err = nullptr;
+    NEON_CUDA_TRY(cudaGetSymbolAddress(&err, g_neon_device_err));
+    st.err = static_cast<unsigned int*>(err);
     st.ready = true;
     return NEON_OK;
 }
@@ -139,10 +146,10 @@ int current_device(int* dev) {
 }
 
 template <typename... KArgs, typename... Args>
-int launch(void (*kern)(KArgs...), dim3 grid, size_t smem, cudaStream_t st, Args&&... args) {
+int launch_n(void (*kern)(KArgs...), dim3 grid, int threads, size_t smem, cudaStream_t st, Args&&... args) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3(threads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -155,6 +162,158 @@ int launch(void (*kern)(KArgs...), dim3 grid, size_t smem, cudaStream_t st, Args
     cudaError_t e = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
     if (e != cudaSuccess) return cuda_err(e, "cudaLaunchKernelEx");
     g_launches.fetch_add(1, std::memory_order_relaxed);
+    return NEON_OK;
+}
+
+template <typename... KArgs, typename... Args>
+int launch(void (*kern)(KArgs...), dim3 grid, size_t smem, cudaStream_t st, Args&&... args) {
+    return launch_n(kern, grid, kThreads, smem, st, std::forward<Args>(args)...);
+}
+
+// Tile plan of a streaming (one-position) launch.
+struct StreamPlan {
+    int rc, kc, nch, stages, stage_bytes, smem;
+};
+
+// Rows per tile: the largest of 32, 16, 8, 4, 2 whose tile fits one stage and
+// still gives every SM a tile; rows that do not fit a stage even 2 at a time
+// are cut into chunks.
+StreamPlan plan_stream(int type, int nb, size_t total_rows, int sms) {
+    const int P = type == NEON_GGML_Q4_0 ? 16 : 32;
+    const long long row_bytes = (long long)nb * (P + 2);
+    StreamPlan p{};
+    if (row_bytes * 2 <= kStageTarget) {
+        p.kc = nb;
+        p.nch = 1;
+        p.rc = 32;
+        while (p.rc > 2 && ((long long)p.rc * row_bytes > kStageTarget ||
+                            (long long)((total_rows + p.rc - 1) / p.rc) < sms))
+            p.rc /= 2;
+    } else {
+        p.rc = 2;
+        int nch = (int)((row_bytes * 2 + kStageTarget - 1) / kStageTarget);
+        p.kc = ((nb + nch - 1) / nch + 7) & ~7;
+        p.nch = (nb + p.kc - 1) / p.kc;
+    }
+    p.stage_bytes = stream_stage_bytes(type, p.rc, p.kc);
+    p.stages = kMaxStages;
+    p.smem = stream_smem_bytes(type, nb, p.stages, p.stage_bytes);
+    while (p.stages > 1 && p.smem > kMaxSmem) {
+        --p.stages;
+        p.smem = stream_smem_bytes(type, nb, p.stages, p.stage_bytes);
+    }
+    return p;
+}
+
+// The streaming kernel instantiation for (type, rows per tile).
+StreamKernel stream_kernel(int type, int rc) {
+    if (type == NEON_GGML_Q4_0) {
+        switch (rc) {
+            case 2: return matvec_stream_kernel<NEON_GGML_Q4_0, 2, 1>;
+            case 4: return matvec_stream_kernel<NEON_GGML_Q4_0, 4, 1>;
+            case 8: return matvec_stream_kernel<NEON_GGML_Q4_0, 8, 1>;
+            case 16: return matvec_stream_kernel<NEON_GGML_Q4_0, 16, 1>;
+            default: return matvec_stream_kernel<NEON_GGML_Q4_0, 32, 1>;
+        }
+    }
+    switch (rc) {
+        case 2: return matvec_stream_kernel<NEON_GGML_Q8_0, 2, 2>;
+        case 4: return matvec_stream_kernel<NEON_GGML_Q8_0, 4, 2>;
+        case 8: return matvec_stream_kernel<NEON_GGML_Q8_0, 8, 2>;
+        case 16: return matvec_stream_kernel<NEON_GGML_Q8_0, 16, 2>;
+        default: return matvec_stream_kernel<NEON_GGML_Q8_0, 32, 2>;
+    }
+}
+
+// Resident CTAs per SM of a streaming kernel instantiation at `smem` bytes.
+int stream_occupancy(int type, int rc, int smem) {
+    static std::mutex mu;
+    static std::vector<std::pair<long long, int>> cache;
+    const long long key = ((long long)type << 40) | ((long long)rc << 32) | (unsigned)smem;
+    std::lock_guard<std::mutex> lk(mu);
+    for (auto& kv : cache)
+        if (kv.first == key) return kv.second;
+    int occ = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, stream_kernel(type, rc), kStreamThreads, smem) !=
+        cudaSuccess)
+        occ = 1;
+    occ = std::max(1, occ);
+    cache.emplace_back(key, occ);
+    return occ;
+}
+
+int launch_stream(const std::vector<const neon_proj_target_t*>& t, int type, int nb, const float* dX,
+                  cudaStream_t st, DeviceState& ds) {
+    size_t total_rows = 0;
+    for (auto* tg : t) total_rows += tg->W->rows;
+    const StreamPlan p = plan_stream(type, nb, total_rows, ds.sms);
+    if (p.smem > kMaxSmem)
+        return set_err(NEON_ERR_UNSUPPORTED, "input dim " + std::to_string((size_t)nb * 32) +
+                                                 " is too large for the one-position kernel's shared memory");
+    const int rc_rows = p.rc;
+    size_t start = 0;
+    while (start < t.size()) {
+        StreamArgs a;
+        std::memset(&a, 0, sizeof(a));
+        size_t n = std::min(t.size() - start, (size_t)kMaxSpans);
+        int tiles = 0;
+        for (size_t i = 0; i < n; ++i) {
+            const neon_proj_target_t* tg = t[start + i];
+            Span& s = a.span[i];
+            s.qs = tg->W->qs;
+            s.d = tg->W->d;
+            s.y = tg->Y;
+            s.y_stride = (long long)tg->y_stride;
+            s.rows = (int)tg->W->rows;
+            s.tile0 = tiles;
+            tiles += (int)((tg->W->rows + rc_rows - 1) / rc_rows);
+        }
+        a.x = dX;
+        a.err = ds.err;
+        a.n_spans = (int)n;
+        a.n_tiles = tiles;
+        a.nb = nb;
+        a.kc = p.kc;
+        a.nch = p.nch;
+        a.stage_bytes = p.stage_bytes;
+        a.x_vec = (reinterpret_cast<uintptr_t>(dX) % 16) == 0;
+        // Pick the ring depth that keeps the most weight bytes in flight per
+        // SM (resident CTAs x stages x stage bytes), then size the grid to what
+        // is resident: a CTA that starts late repays the X staging.
+        int best_stages = 1, best_occ = 1;
+        long long best_bytes = -1;
+        for (int st_n = 1; st_n <= p.stages; ++st_n) {
+            const int sm_bytes = stream_smem_bytes(type, nb, st_n, p.stage_bytes);
+            const int occ = std::min(stream_occupancy(type, p.rc, sm_bytes), kStreamCtasPerSm);
+            const long long inflight = (long long)occ * st_n * p.stage_bytes;
+            if (inflight >= best_bytes) {
+                best_bytes = inflight;
+                best_stages = st_n;
+                best_occ = occ;
+            }
+        }
+        const int grid = std::min(tiles, ds.sms * best_occ);
+        const int per_cta_items = ((tiles + grid - 1) / grid) * p.nch;
+        a.stages = std::max(1, std::min(best_stages, per_cta_items));
+        const int smem = stream_smem_bytes(type, nb, a.stages, p.stage_bytes);
+        int rc = launch_n(stream_kernel(type, p.rc), dim3(grid), kStreamThreads, smem, st, a);
+        if (rc) return rc;
+        start += n;
+    }
+    return NEON_OK;
+}
+
+// Reads (and clears) the device error word after the stream has drained.
+int check_device_err(int device) {
+    if (device < 0 || device >= kMaxDevices || !g_dev[device].ready) return NEON_OK;
+    unsigned int v = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(&v, g_neon_device_err, sizeof(v));
+    if (e != cudaSuccess) return cuda_err(e, "cudaMemcpyFromSymbol");
+    if (v) {
+        const unsigned int zero = 0;
+        cudaMemcpyToSymbol(g_neon_device_err, &zero, sizeof(zero));
+        return set_err(NEON_ERR_CUDA, "a device-side wait timed out (shared-memory copy never completed)");
+    }
     return NEON_OK;
 }
 
@@ -204,7 +363,7 @@ int launch_group(const Group& g, const float* dX, size_t x_stride, size_t seq, c
                  DeviceState& ds) {
     const int nb = (int)(g.cols / 32);
     const bool q4 = g.type == NEON_GGML_Q4_0;
-    const int R = seq == 1 ? (q4 ? kQ4R : kQ8R) : kMpR;
+    if (seq == 1) return launch_stream(g.t, g.type, nb, dX, st, ds);
     size_t start = 0;
     while (start < g.t.size()) {
         MatvecArgs a;
@@ -224,36 +383,20 @@ int launch_group(const Group& g, const float* dX, size_t x_stride, size_t seq, c
             s.y_stride = (long long)tg->y_stride;
             s.rows = (int)tg->W->rows;
             s.tile0 = tiles;
-            tiles += (int)((tg->W->rows + R - 1) / R);
+            tiles += (int)((tg->W->rows + kMpR - 1) / kMpR);
         }
         a.n_spans = (int)n;
         a.n_tiles = tiles;
-        int rc;
-        if (seq == 1) {
-            const int smem = q4 ? q4_seq1_smem_bytes(nb) : q8_seq1_smem_bytes(nb);
-            if (smem > kMaxSmem)
-                return set_err(NEON_ERR_UNSUPPORTED, "input dim " + std::to_string(g.cols) +
-                                                         " exceeds the one-position kernel's shared-memory limit");
-            int ctas = (tiles + kWarps - 1) / kWarps;
-            ctas = std::min(ctas, ds.sms * (q4 ? ds.occ_q4 : ds.occ_q8));
-            if (q4)
-                rc = launch(q4_0_seq1_kernel<kQ4R, kQ4U>, dim3(ctas), smem, st, a);
-            else
-                rc = launch(q8_0_seq1_kernel<kQ8R, kQ8U>, dim3(ctas), smem, st, a);
-        } else {
-            if (q4) {
-                a.xq = ds.xq;
-                a.xd = ds.xd;
-                a.xs = ds.xs;
-            }
-            int ctas = (tiles + kWarps - 1) / kWarps;
-            ctas = std::min(ctas, ds.sms * 4);
-            dim3 grid(ctas, (unsigned)((seq + kMpT - 1) / kMpT));
-            if (q4)
-                rc = launch(matvec_multipos_kernel<NEON_GGML_Q4_0, kMpR, kMpT>, grid, 0, st, a);
-            else
-                rc = launch(matvec_multipos_kernel<NEON_GGML_Q8_0, kMpR, kMpT>, grid, 0, st, a);
+        if (q4) {
+            a.xq = ds.xq;
+            a.xd = ds.xd;
+            a.xs = ds.xs;
         }
+        int ctas = (tiles + kWarps - 1) / kWarps;
+        ctas = std::min(ctas, ds.sms * 4);
+        dim3 grid(ctas, (unsigned)((seq + kMpT - 1) / kMpT));
+        int rc = q4 ? launch(matvec_multipos_kernel<NEON_GGML_Q4_0, kMpR, kMpT>, grid, 0, st, a)
+                    : launch(matvec_multipos_kernel<NEON_GGML_Q8_0, kMpR, kMpT>, grid, 0, st, a);
         if (rc) return rc;
         start += n;
     }
@@ -392,7 +535,7 @@ int neon_cuda_upload(const uint8_t* host_bytes, int ggml_type, size_t rows, size
     const size_t lrows = r1 - r0, lnb = b1 - b0;
     const size_t qs_bytes = lrows * lnb * P;
     const size_t d_off = (qs_bytes + 255) / 256 * 256;
-    const size_t total = d_off + lrows * lnb * 2;
+    const size_t total = d_off + lrows * lnb * 2 + 16;  // tail: aligned scale windows
 
     neon_tensor* t = new neon_tensor();
     t->device = device;
@@ -533,7 +676,7 @@ int neon_cuda_proj_all_positions_multi(const neon_proj_target_t* targets, size_t
     for (size_t i = 0; i < n_targets; ++i)
         NEON_CUDA_TRY(cudaMemcpyAsync(targets[i].Y, dt[i].Y, y_len[i] * 4, cudaMemcpyDeviceToHost, st));
     NEON_CUDA_TRY(cudaStreamSynchronize(st));
-    return NEON_OK;
+    return check_device_err(device);
 }
 
 int neon_cuda_proj_all_positions(neon_tensor_t W, const float* hX, size_t x_stride, float* hY, size_t y_stride,
@@ -544,7 +687,9 @@ int neon_cuda_proj_all_positions(neon_tensor_t W, const float* hX, size_t x_stri
 
 int neon_cuda_sync(void* stream) {
     NEON_CUDA_TRY(cudaStreamSynchronize((cudaStream_t)stream));
-    return NEON_OK;
+    int device = 0;
+    NEON_CUDA_TRY(cudaGetDevice(&device));
+    return check_device_err(device);
 }
 
 }  // extern "C"

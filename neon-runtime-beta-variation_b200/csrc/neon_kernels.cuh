@@ -27,6 +27,12 @@ namespace neon {
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
 constexpr int kMaxSpans = 8;
+// Q8_0 activation record in shared memory: 32 quants, fp32 d, int32 sum, pad
+// (a 48-byte pitch keeps a warp's 128-bit reads conflict-free).
+constexpr int kQ4Rec = 48;
+// fp32 X block pitch in shared memory, in floats (144 bytes: conflict-free
+// 128-bit reads when lane l reads block l).
+constexpr int kQ8Pitch = 36;
 
 // One projection target of a launch: rows [0, rows) of one uploaded tensor.
 struct Span {
@@ -223,6 +229,12 @@ __device__ __forceinline__ int q4_block_isum(const uint4 w, const uint4 x0, cons
     return acc - 8 * qsum;
 }
 
+// Exact int -> float for |v| < 2^22 without the conversion pipe: the bits of
+// 1.5*2^23 + v read as a float are 12582912 + v exactly.
+__device__ __forceinline__ float small_int_to_f32(int v) {
+    return __int_as_float(0x4B400000 + v) - 12582912.0f;
+}
+
 // Sum over one Q8_0 block of q[j] * x[j] in fp32 (w0, w1 = 32 int8).
 __device__ __forceinline__ float q8_block_dot(const uint4 w0, const uint4 w1, const float4* xv) {
     const uint32_t ws[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
@@ -253,206 +265,439 @@ __device__ __forceinline__ void store_tile(const float (&acc)[R], float* y, int 
 }
 
 // ---------------------------------------------------------------------------
-// Q4_0 weights, one position: X quantised to Q8_0 inside every CTA.
+// One position (decode): the streaming kernel.
+//
+// A CTA of kStreamWarps warps owns row tiles of RC rows
+// (tiles t = blockIdx.x, blockIdx.x + gridDim.x, ...). A tile's input dim is
+// cut into nch chunks of kc blocks; one (tile, chunk) pair is an "item". Warp 0
+// copies items into a ring of shared-memory stages with cp.async.bulk, one
+// mbarrier per stage counting the bytes. When the whole row fits one chunk,
+// a tile's RC rows are contiguous in both planes and an item is two copies
+// (payload, scales); otherwise each row is two copies. The first items are
+// issued before the PDL wait: weights are never written by earlier kernels,
+// so a launch streams its weights while the previous kernel is finishing.
+//
+// After the PDL wait the CTA stages X once: Q4_0 quantises it to Q8_0 records
+// (bit-exact with quantize_rows_q8_0), 1, 2 or 4 threads per 32-block so that
+// one L2 round trip brings all of X in; Q8_0 keeps fp32. Only then does the
+// CTA let the next launch on the stream start (a trigger before this point
+// lets several launches' CTAs pile up on the SMs).
+//
+// Dot products: see the work mapping above matvec_stream_kernel. Q8_0 tiles
+// give each thread two rows so that one read of a block of X serves both.
+//
+// Stage layout: payload RC x kc_max x P bytes (row r at r*kc_max*P), then the
+// scales: the 16-byte-aligned window around the wanted scales (the scale plane
+// carries 16 bytes of tail padding so a window never leaves the allocation),
+// one window per tile (contiguous case) or per row at a pitch of SPH halfs.
 // ---------------------------------------------------------------------------
+constexpr int kStreamWarps = 8;
+constexpr int kStreamThreads = kStreamWarps * 32;
+constexpr int kMaxStages = 3;
 
-// Shared memory: nb records of 48 bytes (32 quants, fp32 d, int32 sum, pad) --
-// the 48-byte pitch keeps a warp's 128-bit reads conflict-free -- followed by a
-// staging area of kThreads x 33 floats for X (33-float pitch: one thread reads
-// one block without bank conflicts).
-constexpr int kQ4Rec = 48;
-__host__ __device__ constexpr int q4_seq1_smem_bytes(int nb) {
-    return nb * kQ4Rec + kThreads * 33 * 4;
+struct StreamArgs {
+    Span span[kMaxSpans];
+    const float* x;         // fp32 activations of the one position
+    unsigned int* err;      // device error word: bit 0 = a bounded wait timed out
+    int n_spans;
+    int n_tiles;
+    int nb;                 // blocks per row
+    int kc;                 // blocks per chunk (the last chunk may be shorter)
+    int nch;                // chunks per row
+    int stages;             // ring depth
+    int stage_bytes;        // bytes per stage
+    int x_vec;              // x is 16-byte aligned: 128-bit loads
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
-template <int R, int U>
-__global__ void __launch_bounds__(kThreads) q4_0_seq1_kernel(const __grid_constant__ MatvecArgs a) {
-    extern __shared__ __align__(16) unsigned char smem[];
-    unsigned char* rec = smem;
-    float* stage = reinterpret_cast<float*>(smem + a.nb * kQ4Rec);
-    const int lane = threadIdx.x & 31;
-    const int nb = a.nb;
-    const int tile_step = gridDim.x * kWarps;
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
 
-    pdl_launch_dependents();
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
 
-    // 1. Fetch the first chunk of this warp's first tile. Weights are never
-    //    written by earlier kernels, so this may run before the PDL wait.
-    int tile = blockIdx.x * kWarps + (threadIdx.x >> 5);
-    uint4 wq[R][U];
-    uint16_t wd[R][U];
-    int si = 0, row0 = 0;
-    auto load_chunk = [&](int c) {
-        const Span& sp = a.span[si];
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const int b = c + u * 32 + lane;
-#pragma unroll
-            for (int r = 0; r < R; ++r) {
-                const int row = row0 + r;
-                if (b < nb && row < sp.rows) {
-                    const long long i = (long long)row * nb + b;
-                    wq[r][u] = ld_weights_u4(sp.qs + i * 16);
-                    wd[r][u] = ld_weights_u16(sp.d + i);
-                } else {
-                    wq[r][u] = make_uint4(0, 0, 0, 0);
-                    wd[r][u] = 0;
-                }
-            }
-        }
-    };
-    if (tile < a.n_tiles) {
-        si = find_span(a, tile);
-        row0 = (tile - a.span[si].tile0) * R;
-        load_chunk(0);
-    }
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
 
-    // 2. Quantise X (written by the previous kernel) into shared memory,
-    //    kThreads blocks at a time, one block per thread.
-    pdl_wait();
-    const float* x = a.x;
-    for (int c0 = 0; c0 < nb; c0 += kThreads) {
-        const int nblk = min(kThreads, nb - c0);
-        for (int i = threadIdx.x; i < nblk * 32; i += kThreads)
-            stage[(i >> 5) * 33 + (i & 31)] = x[(long long)c0 * 32 + i];
-        __syncthreads();
-        if ((int)threadIdx.x < nblk) {
-            uint32_t q[8];
-            float d;
-            int s;
-            quantize_block_thread(stage + threadIdx.x * 33, q, d, s);
-            uint4* r4 = reinterpret_cast<uint4*>(rec + (c0 + threadIdx.x) * kQ4Rec);
-            r4[0] = make_uint4(q[0], q[1], q[2], q[3]);
-            r4[1] = make_uint4(q[4], q[5], q[6], q[7]);
-            r4[2] = make_uint4(__float_as_uint(d), (uint32_t)s, 0u, 0u);
-        }
-        __syncthreads();
-    }
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
 
-    // 3. Row tiles.
-    while (tile < a.n_tiles) {
-        const Span& sp = a.span[si];
-        float acc[R];
-#pragma unroll
-        for (int r = 0; r < R; ++r) acc[r] = 0.f;
-        for (int c = 0;;) {
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-                const int b = c + u * 32 + lane;
-                if (b < nb) {
-                    const uint4* r4 = reinterpret_cast<const uint4*>(rec + b * kQ4Rec);
-                    const uint4 x0 = r4[0], x1 = r4[1], xm = r4[2];
-                    const float xd = __uint_as_float(xm.x);
-                    const int xs = (int)xm.y;
-#pragma unroll
-                    for (int r = 0; r < R; ++r) {
-                        const int isum = q4_block_isum(wq[r][u], x0, x1, xs);
-                        acc[r] = fmaf(fp16_bits_to_f32(wd[r][u]) * xd, (float)isum, acc[r]);
-                    }
-                }
-            }
-            c += 32 * U;
-            if (c >= nb) break;
-            load_chunk(c);
-        }
-        store_tile<R>(acc, sp.y, row0, sp.rows, lane);
-        tile += tile_step;
-        if (tile < a.n_tiles) {
-            si = find_span(a, tile);
-            row0 = (tile - a.span[si].tile0) * R;
-            load_chunk(0);
+// Bulk copy global -> this CTA's shared memory; completion is counted in
+// bytes on `bar`. dst, src and bytes must be multiples of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Wait for phase `parity` of `bar`; give up after ~2 s, record the timeout in
+// *err and return false (the caller leaves the kernel, CTA-uniformly).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int* err) {
+    const uint32_t addr = smem_u32(bar);
+    uint32_t done = 0;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+        : "=r"(done)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    if (done) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (;;) {
+        asm volatile(
+            "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+            : "=r"(done)
+            : "r"(addr), "r"(parity)
+            : "memory");
+        if (done) return true;
+        if (globaltimer_ns() - t0 > 2000000000ull) {
+            if (err) atomicOr(err, 1u);
+            return false;
         }
     }
 }
 
-// ---------------------------------------------------------------------------
-// Q8_0 weights, one position: fp32 X staged in shared memory.
-// ---------------------------------------------------------------------------
+template <class Args>
+__device__ __forceinline__ int find_span_of(const Args& a, int tile) {
+    int s = 0;
+#pragma unroll
+    for (int i = 1; i < kMaxSpans; ++i)
+        if (i < a.n_spans && a.span[i].tile0 <= tile) s = i;
+    return s;
+}
 
-// X block b at smem float offset b*36 (a 144-byte pitch keeps the warp's
-// 128-bit reads conflict-free).
-constexpr int kQ8Pitch = 36;
-__host__ __device__ constexpr int q8_seq1_smem_bytes(int nb) { return nb * kQ8Pitch * 4; }
+__host__ __device__ constexpr int stream_scale_pitch(int kc) { return ((kc + 7) & ~7) + 8; }
+__host__ __device__ constexpr int stream_x_bytes(int type, int nb) {
+    return ((type == 2 ? nb * kQ4Rec : nb * kQ8Pitch * 4) + 127) & ~127;
+}
 
-template <int R, int U>
-__global__ void __launch_bounds__(kThreads) q8_0_seq1_kernel(const __grid_constant__ MatvecArgs a) {
-    extern __shared__ __align__(16) unsigned char smem[];
-    float* xs = reinterpret_cast<float*>(smem);
+// Quantise X (nb blocks) into the CTA's Q8_0 records, TPB threads per block.
+// Whole warps iterate together (the shuffles need every lane); the TPB
+// threads of one block are always all active or all idle.
+template <int TPB>
+__device__ __forceinline__ void stage_x_q8(const float* __restrict__ x, int nb, bool x_vec, unsigned char* rec) {
+    constexpr int EPT = 32 / TPB;
     const int lane = threadIdx.x & 31;
-    const int nb = a.nb;
-    const int tile_step = gridDim.x * kWarps;
-
-    pdl_launch_dependents();
-
-    int tile = blockIdx.x * kWarps + (threadIdx.x >> 5);
-    uint4 wq[R][U][2];
-    uint16_t wd[R][U];
-    int si = 0, row0 = 0;
-    auto load_chunk = [&](int c) {
-        const Span& sp = a.span[si];
+    const int n = nb * TPB;
+    for (int i0 = threadIdx.x - lane; i0 < n; i0 += kStreamThreads) {
+        const int i = i0 + lane;
+        const bool act = i < n;
+        const int b = act ? i / TPB : 0, part = i % TPB;
+        const float* xb = x + (long long)b * 32 + part * EPT;
+        float xv[EPT];
+        if (act && x_vec) {
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const int b = c + u * 32 + lane;
-#pragma unroll
-            for (int r = 0; r < R; ++r) {
-                const int row = row0 + r;
-                if (b < nb && row < sp.rows) {
-                    const long long i = (long long)row * nb + b;
-                    wq[r][u][0] = ld_weights_u4(sp.qs + i * 32);
-                    wq[r][u][1] = ld_weights_u4(sp.qs + i * 32 + 16);
-                    wd[r][u] = ld_weights_u16(sp.d + i);
-                } else {
-                    wq[r][u][0] = make_uint4(0, 0, 0, 0);
-                    wq[r][u][1] = make_uint4(0, 0, 0, 0);
-                    wd[r][u] = 0;
-                }
+            for (int k = 0; k < EPT / 4; ++k) {
+                const float4 v = __ldg(reinterpret_cast<const float4*>(xb) + k);
+                xv[4 * k] = v.x; xv[4 * k + 1] = v.y; xv[4 * k + 2] = v.z; xv[4 * k + 3] = v.w;
             }
+        } else if (act) {
+#pragma unroll
+            for (int j = 0; j < EPT; ++j) xv[j] = __ldg(xb + j);
+        } else {
+#pragma unroll
+            for (int j = 0; j < EPT; ++j) xv[j] = 0.f;
         }
-    };
-    if (tile < a.n_tiles) {
-        si = find_span(a, tile);
-        row0 = (tile - a.span[si].tile0) * R;
-        load_chunk(0);
+        float amax = 0.f;
+#pragma unroll
+        for (int j = 0; j < EPT; ++j) amax = fmaxf(amax, fabsf(xv[j]));
+#pragma unroll
+        for (int o = 1; o < TPB; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        const float d = __fdiv_rn(amax, 127.0f);
+        const float id = d > 0.f ? __fdiv_rn(1.0f, d) : 0.f;
+        uint32_t q[EPT / 4];
+        int s = 0;
+#pragma unroll
+        for (int k = 0; k < EPT / 4; ++k) {
+            uint32_t w = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int v = q8_round_clamp(__fmul_rn(xv[4 * k + j], id));
+                s += v;
+                w |= (uint32_t)(v & 0xFF) << (8 * j);
+            }
+            q[k] = w;
+        }
+#pragma unroll
+        for (int o = 1; o < TPB; o <<= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        if (act) {
+            uint32_t* r32 = reinterpret_cast<uint32_t*>(rec + b * kQ4Rec) + part * (EPT / 4);
+#pragma unroll
+            for (int k = 0; k < EPT / 4; ++k) r32[k] = q[k];
+            if (part == 0)
+                *reinterpret_cast<uint2*>(rec + b * kQ4Rec + 32) = make_uint2(__float_as_uint(d), (uint32_t)s);
+        }
     }
+}
 
-    pdl_wait();
-    const float* x = a.x;
-    for (int i = threadIdx.x; i < nb * 32; i += kThreads) xs[(i >> 5) * kQ8Pitch + (i & 31)] = x[i];
+// Packed fp32x2 arithmetic of sm_100 (one instruction, two lanes of fp32).
+__device__ __forceinline__ unsigned long long f32x2_fma(unsigned long long a, unsigned long long b,
+                                                        unsigned long long c) {
+    unsigned long long d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ unsigned long long f32x2_add(unsigned long long a, unsigned long long b) {
+    unsigned long long d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+// Bytes 0,1 (sel 0) or 2,3 (sel 1) of (w ^ 0x80808080) as the floats
+// 8388608 + 128 + q, packed in one 64-bit register.
+template <int HALF>
+__device__ __forceinline__ unsigned long long i8x2_magic(uint32_t u) {
+    unsigned long long v;
+    if (HALF == 0)
+        asm("{ .reg .b32 lo, hi; prmt.b32 lo, %1, 0x4B000000, 0x7650; prmt.b32 hi, %1, 0x4B000000, 0x7651; "
+            "mov.b64 %0, {lo, hi}; }"
+            : "=l"(v) : "r"(u));
+    else
+        asm("{ .reg .b32 lo, hi; prmt.b32 lo, %1, 0x4B000000, 0x7652; prmt.b32 hi, %1, 0x4B000000, 0x7653; "
+            "mov.b64 %0, {lo, hi}; }"
+            : "=l"(v) : "r"(u));
+    return v;
+}
+
+// Sum over one Q8_0 block of q[j]*x[j] in fp32 with packed arithmetic:
+// two interleaved partial sums (even and odd elements), added at the end.
+// xv: the block's 32 floats as 16 packed pairs.
+__device__ __forceinline__ float q8_block_dot_x2(const uint4 w0, const uint4 w1, const unsigned long long* xv) {
+    const uint32_t ws[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+    const unsigned long long neg_magic = 0xCB000080CB000080ull;  // {-8388736.f, -8388736.f}
+    unsigned long long acc = 0ull;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const uint32_t u = ws[k] ^ 0x80808080u;
+        acc = f32x2_fma(f32x2_add(i8x2_magic<0>(u), neg_magic), xv[2 * k], acc);
+        acc = f32x2_fma(f32x2_add(i8x2_magic<1>(u), neg_magic), xv[2 * k + 1], acc);
+    }
+    return __uint_as_float((uint32_t)acc) + __uint_as_float((uint32_t)(acc >> 32));
+}
+
+// Work mapping: a tile has RC rows; every thread owns R consecutive rows and a
+// slice of the blocks of a chunk. G = RC/R row groups share the CTA's threads,
+// TPG = kStreamThreads/G per group: WPG = TPG/32 whole warps per group when
+// TPG >= 32 (a row split over several warps: K-split, finished through shared
+// memory), else 32/TPG groups per warp (finished by a shuffle tree).
+template <int TYPE, int RC, int R>
+__global__ void __launch_bounds__(kStreamThreads) matvec_stream_kernel(const __grid_constant__ StreamArgs a) {
+    constexpr int P = TYPE == 2 ? 16 : 32;
+    constexpr int G = RC / R;
+    constexpr int TPG = kStreamThreads / G;
+    constexpr int WPG = TPG >= 32 ? TPG / 32 : 1;
+    constexpr int LPG = TPG >= 32 ? 32 : TPG;
+    static_assert(RC % R == 0 && kStreamThreads % G == 0, "bad tile shape");
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ float red[RC * WPG];
+    const int nb = a.nb, KC = a.kc, nch = a.nch, S = a.stages;
+    const int SPH = stream_scale_pitch(KC);
+    unsigned char* xsm = smem;
+    unsigned char* ring = smem + stream_x_bytes(TYPE, nb);
+    uint64_t* full = reinterpret_cast<uint64_t*>(ring + S * a.stage_bytes);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = TPG >= 32 ? warp / WPG : warp * (32 / TPG) + lane / TPG;
+    const int slice = TPG >= 32 ? (warp % WPG) * 32 + lane : lane % TPG;
+
+    const int my_tiles = (int)blockIdx.x < a.n_tiles ? (a.n_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    const int n_items = my_tiles * nch;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) mbar_init(&full[s], 1);
+        fence_mbar_init();
+    }
     __syncthreads();
 
-    while (tile < a.n_tiles) {
-        const Span& sp = a.span[si];
-        float acc[R];
-#pragma unroll
-        for (int r = 0; r < R; ++r) acc[r] = 0.f;
-        for (int c = 0;;) {
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-                const int b = c + u * 32 + lane;
-                if (b < nb) {
-                    const float4* xv = reinterpret_cast<const float4*>(xs + b * kQ8Pitch);
-                    float4 xr[8];
-#pragma unroll
-                    for (int k = 0; k < 8; ++k) xr[k] = xv[k];
-#pragma unroll
-                    for (int r = 0; r < R; ++r) {
-                        const float s = q8_block_dot(wq[r][u][0], wq[r][u][1], xr);
-                        acc[r] = fmaf(fp16_bits_to_f32(wd[r][u]), s, acc[r]);
-                    }
-                }
+    // Warp 0: copy item `item` of this CTA into its stage.
+    auto issue = [&](int item) {
+        const int stage = item % S;
+        const int tile = (int)blockIdx.x + (item / nch) * (int)gridDim.x;
+        const int chunk = item % nch;
+        const Span& sp = a.span[find_span_of(a, tile)];
+        const int row0 = (tile - sp.tile0) * RC;
+        const int k0 = chunk * KC;
+        const int kc = min(KC, nb - k0);
+        const int nrows = min(RC, sp.rows - row0);
+        unsigned char* pay = ring + stage * a.stage_bytes;
+        uint16_t* sc = reinterpret_cast<uint16_t*>(pay + RC * KC * P);
+        if (nch == 1) {
+            const long long e = (long long)row0 * nb;
+            const int off = (int)(e & 7);
+            const uint32_t pbytes = (uint32_t)(nrows * nb * P);
+            const uint32_t sbytes = 2u * (uint32_t)((off + nrows * nb + 7) & ~7);
+            if (lane == 0) {
+                mbar_arrive_expect_tx(&full[stage], pbytes + sbytes);
+                bulk_g2s(pay, sp.qs + e * P, pbytes, &full[stage]);
+                bulk_g2s(sc, sp.d + (e - off), sbytes, &full[stage]);
             }
-            c += 32 * U;
-            if (c >= nb) break;
-            load_chunk(c);
+            return;
         }
-        store_tile<R>(acc, sp.y, row0, sp.rows, lane);
-        tile += tile_step;
-        if (tile < a.n_tiles) {
-            si = find_span(a, tile);
-            row0 = (tile - a.span[si].tile0) * R;
-            load_chunk(0);
+        uint32_t bytes = 0;
+        for (int r = lane; r < nrows; r += 32) {
+            const long long e = (long long)(row0 + r) * nb + k0;
+            const int off = (int)(e & 7);
+            bytes += (uint32_t)(kc * P) + 2u * (uint32_t)((off + kc + 7) & ~7);
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) bytes += __shfl_xor_sync(0xffffffffu, bytes, o);
+        if (lane == 0) mbar_arrive_expect_tx(&full[stage], bytes);
+        __syncwarp();
+        for (int r = lane; r < nrows; r += 32) {
+            const long long e = (long long)(row0 + r) * nb + k0;
+            const int off = (int)(e & 7);
+            bulk_g2s(pay + r * KC * P, sp.qs + e * P, (uint32_t)(kc * P), &full[stage]);
+            bulk_g2s(sc + r * SPH, sp.d + (e - off), 2u * (uint32_t)((off + kc + 7) & ~7), &full[stage]);
+        }
+    };
+
+    if (warp == 0) {
+        const int first = min(S, n_items);
+        for (int i = 0; i < first; ++i) issue(i);
+    }
+    pdl_wait();
+
+    // Stage X once per CTA, then let the next launch start.
+    if (TYPE == 2) {
+        const int tpb = kStreamThreads / nb;
+        if (tpb >= 4) stage_x_q8<4>(a.x, nb, a.x_vec, xsm);
+        else if (tpb >= 2) stage_x_q8<2>(a.x, nb, a.x_vec, xsm);
+        else stage_x_q8<1>(a.x, nb, a.x_vec, xsm);
+    } else {
+        float* xs = reinterpret_cast<float*>(xsm);
+        if (a.x_vec) {
+            for (int i = threadIdx.x; i < nb * 8; i += kStreamThreads)
+                *reinterpret_cast<float4*>(xs + (i >> 3) * kQ8Pitch + (i & 7) * 4) =
+                    __ldg(reinterpret_cast<const float4*>(a.x) + i);
+        } else {
+            for (int i = threadIdx.x; i < nb * 32; i += kStreamThreads)
+                xs[(i >> 5) * kQ8Pitch + (i & 31)] = __ldg(a.x + i);
         }
     }
+    __syncthreads();
+    pdl_launch_dependents();
+
+    float acc[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) acc[r] = 0.f;
+    for (int item = 0; item < n_items; ++item) {
+        const int stage = item % S;
+        const uint32_t parity = (uint32_t)((item / S) & 1);
+        const int tile = (int)blockIdx.x + (item / nch) * (int)gridDim.x;
+        const int chunk = item % nch;
+        const Span& sp = a.span[find_span_of(a, tile)];
+        const int row0 = (tile - sp.tile0) * RC;
+        const int k0 = chunk * KC;
+        const int kc = min(KC, nb - k0);
+        const bool ok = mbar_wait(&full[stage], parity, a.err);
+        if (__syncthreads_or(!ok)) return;
+
+        const unsigned char* pay = ring + stage * a.stage_bytes;
+        const uint16_t* sc = reinterpret_cast<const uint16_t*>(pay + RC * KC * P);
+        int sbase[R];
+        const unsigned char* prow[R];
+#pragma unroll
+        for (int rr = 0; rr < R; ++rr) {
+            const int r = g * R + rr;
+            sbase[rr] = nch == 1 ? (int)(((long long)row0 * nb) & 7) + r * nb
+                                 : r * SPH + (int)(((long long)(row0 + r) * nb + k0) & 7);
+            prow[rr] = pay + r * KC * P;
+        }
+        float part[R];
+#pragma unroll
+        for (int rr = 0; rr < R; ++rr) part[rr] = 0.f;
+#pragma unroll 2
+        for (int bi = slice; bi < kc; bi += TPG) {
+            if (TYPE == 2) {
+                const uint4* r4 = reinterpret_cast<const uint4*>(xsm + (k0 + bi) * kQ4Rec);
+                const uint4 x0 = r4[0], x1 = r4[1];
+                const uint2 xm = *reinterpret_cast<const uint2*>(r4 + 2);
+                const float xd = __uint_as_float(xm.x);
+#pragma unroll
+                for (int rr = 0; rr < R; ++rr) {
+                    const float wd = fp16_bits_to_f32(sc[sbase[rr] + bi]);
+                    const uint4 w = *reinterpret_cast<const uint4*>(prow[rr] + bi * P);
+                    part[rr] = fmaf(wd * xd, small_int_to_f32(q4_block_isum(w, x0, x1, (int)xm.y)), part[rr]);
+                }
+            } else {
+                const ulonglong2* xv2 = reinterpret_cast<const ulonglong2*>(
+                    reinterpret_cast<const float*>(xsm) + (k0 + bi) * kQ8Pitch);
+                unsigned long long xv[16];
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    const ulonglong2 t = xv2[k];
+                    xv[2 * k] = t.x;
+                    xv[2 * k + 1] = t.y;
+                }
+#pragma unroll
+                for (int rr = 0; rr < R; ++rr) {
+                    const float wd = fp16_bits_to_f32(sc[sbase[rr] + bi]);
+                    const uint4* w4 = reinterpret_cast<const uint4*>(prow[rr] + bi * P);
+                    part[rr] = fmaf(wd, q8_block_dot_x2(w4[0], w4[1], xv), part[rr]);
+                }
+            }
+        }
+#pragma unroll
+        for (int rr = 0; rr < R; ++rr) acc[rr] += part[rr];
+        if (chunk == nch - 1) {
+#pragma unroll
+            for (int rr = 0; rr < R; ++rr)
+#pragma unroll
+                for (int o = LPG / 2; o; o >>= 1) acc[rr] += __shfl_xor_sync(0xffffffffu, acc[rr], o);
+            if (WPG == 1) {
+                if (slice == 0) {
+#pragma unroll
+                    for (int rr = 0; rr < R; ++rr) {
+                        const int row = row0 + g * R + rr;
+                        if (row < sp.rows) sp.y[row] = acc[rr];
+                    }
+                }
+            } else {
+                if (lane == 0) {
+#pragma unroll
+                    for (int rr = 0; rr < R; ++rr) red[(g * R + rr) * WPG + (warp % WPG)] = acc[rr];
+                }
+                __syncthreads();
+                if ((int)threadIdx.x < RC) {
+                    float v = 0.f;
+#pragma unroll
+                    for (int w = 0; w < WPG; ++w) v += red[threadIdx.x * WPG + w];
+                    const int row = row0 + threadIdx.x;
+                    if (row < sp.rows) sp.y[row] = v;
+                }
+            }
+#pragma unroll
+            for (int rr = 0; rr < R; ++rr) acc[rr] = 0.f;
+        }
+        __syncthreads();  // every warp is done with this stage (and with red[])
+        if (warp == 0 && item + S < n_items) {
+            fence_proxy_async_smem();
+            issue(item + S);
+        }
+    }
+}
+
+// Shared-memory bytes of a streaming launch.
+__host__ __device__ constexpr int stream_smem_bytes(int type, int nb, int stages, int stage_bytes) {
+    return stream_x_bytes(type, nb) + stages * stage_bytes + kMaxStages * 8;
+}
+
+// Bytes of one ring stage for RC rows x kc blocks.
+__host__ __device__ constexpr int stream_stage_bytes(int type, int rc, int kc) {
+    return ((rc * kc * (type == 2 ? 16 : 32) + rc * stream_scale_pitch(kc) * 2 + 16) + 127) & ~127;
 }
 
 // ---------------------------------------------------------------------------

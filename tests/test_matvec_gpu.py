@@ -150,7 +150,8 @@ def test_prefill_128_sampled_rows(typ, rows, cols):
 
 @pytest.mark.parametrize("typ", [S.GGML_Q4_0, S.GGML_Q8_0])
 @pytest.mark.parametrize("rows,cols,seq", [(1, 32, 1), (3, 64, 1), (33, 96, 1), (129, 8192, 1),
-                                           (5, 32, 7), (67, 2048, 5), (2, 12288, 1)])
+                                           (5, 32, 7), (67, 2048, 5), (2, 12288, 1), (301, 800, 1),
+                                           (77, 1152, 1), (1000, 3072, 1), (19, 28672, 1)])
 def test_ragged(typ, rows, cols, seq):
     W = S.weights(typ, rows, cols, seed=rows * 7 + cols)
     X = S.activations(seq, cols, seed=seq + 3)
