@@ -73,3 +73,80 @@ def algorithmic_bytes(ggml_type: int, rows: int, cols: int, seq: int = 1) -> int
     """Bytes a matvec must move at minimum: the quantized weight payload and
     scales once, plus fp32 X read and fp32 Y written for every position."""
     return rows * row_bytes(ggml_type, cols) + seq * (cols + rows) * 4
+
+
+# ---------------------------------------------------------------------------
+# Whole decoder models (NANITY_ARCHITECTURE_SPEC.md tensor list, GGUF ne shapes)
+# ---------------------------------------------------------------------------
+
+# Tensor roles, numbered as include/neon_cuda.h's NEON_ROLE_* values.
+ROLE_TOKEN_EMBD, ROLE_OUTPUT_NORM, ROLE_OUTPUT = 0, 1, 2
+ROLE_ATTN_NORM, ROLE_ATTN_Q, ROLE_ATTN_K, ROLE_ATTN_V, ROLE_ATTN_OUT = 3, 4, 5, 6, 7
+ROLE_FFN_NORM, ROLE_FFN_GATE, ROLE_FFN_UP, ROLE_FFN_DOWN = 8, 9, 10, 11
+
+
+class ModelConfig:
+    """Hyperparameters of a NANITY decoder (engine::Config, rawllm_common.hpp:113-145)."""
+
+    FIELDS = ("n_vocab", "n_embd", "n_layer", "n_head", "n_kv_head", "head_dim", "n_ff", "ctx_len",
+              "rope_base", "rope_scale", "rope_dim_count", "norm_eps")
+
+    def __init__(self, n_vocab, n_embd, n_layer, n_head, n_kv_head, head_dim, n_ff, ctx_len=4096,
+                 rope_base=10000.0, rope_scale=1.0, rope_dim_count=0, norm_eps=1e-5, name=""):
+        self.n_vocab, self.n_embd, self.n_layer = n_vocab, n_embd, n_layer
+        self.n_head, self.n_kv_head, self.head_dim, self.n_ff = n_head, n_kv_head, head_dim, n_ff
+        self.ctx_len, self.rope_base, self.rope_scale = ctx_len, rope_base, rope_scale
+        self.rope_dim_count, self.norm_eps, self.name = rope_dim_count, norm_eps, name
+
+    @property
+    def q_dim(self):
+        return self.n_head * self.head_dim
+
+    @property
+    def kv_dim(self):
+        return self.n_kv_head * self.head_dim
+
+    def with_(self, **kw):
+        d = {f: getattr(self, f) for f in self.FIELDS}
+        d["name"] = self.name
+        d.update(kw)
+        return ModelConfig(**d)
+
+
+# The decoder shapes of the benchmark configurations.
+QWEN3_0_6B = ModelConfig(151936, 1024, 28, 16, 8, 128, 3072, ctx_len=512, rope_base=1e6, norm_eps=1e-6,
+                         name="Qwen3-0.6B-shaped")
+PHI4_MINI = ModelConfig(200064, 3072, 32, 24, 8, 128, 8192, ctx_len=1152, rope_base=1e4, norm_eps=1e-5,
+                        name="Phi-4-mini-shaped")
+LLAMA3_70B = ModelConfig(128256, 8192, 80, 64, 8, 128, 28672, ctx_len=2432, rope_base=5e5, norm_eps=1e-5,
+                         name="Llama-3-70B-shaped")
+
+
+def model_tensors(cfg: ModelConfig, seed: int, wtype: int = GGML_Q4_0, embd_type: int = GGML_Q8_0,
+                  tied: bool = True):
+    """Seeded random-init tensors of a decoder, in GGUF layout:
+    yields (role, layer, raw bytes uint8, ggml type, ne0, ne1); ne1 = 0 for 1-D.
+    Projections are `wtype` with the benchmark's block distributions, the
+    embedding (also the lm_head when tied) is `embd_type`, norm weights fp32 1."""
+    def sub(role, layer):
+        return seed * 1000003 + role * 10007 + layer + 1
+
+    ones = np.ones(cfg.n_embd, np.float32).view(np.uint8)
+    yield ROLE_TOKEN_EMBD, -1, weights(embd_type, cfg.n_vocab, cfg.n_embd, sub(0, 0)), embd_type, cfg.n_embd, cfg.n_vocab
+    yield ROLE_OUTPUT_NORM, -1, ones, GGML_F32, cfg.n_embd, 0
+    if not tied:
+        yield ROLE_OUTPUT, -1, weights(wtype, cfg.n_vocab, cfg.n_embd, sub(2, 0)), wtype, cfg.n_embd, cfg.n_vocab
+    shapes = {ROLE_ATTN_Q: (cfg.q_dim, cfg.n_embd), ROLE_ATTN_K: (cfg.kv_dim, cfg.n_embd),
+              ROLE_ATTN_V: (cfg.kv_dim, cfg.n_embd), ROLE_ATTN_OUT: (cfg.n_embd, cfg.q_dim),
+              ROLE_FFN_GATE: (cfg.n_ff, cfg.n_embd), ROLE_FFN_UP: (cfg.n_ff, cfg.n_embd),
+              ROLE_FFN_DOWN: (cfg.n_embd, cfg.n_ff)}
+    for li in range(cfg.n_layer):
+        yield ROLE_ATTN_NORM, li, ones, GGML_F32, cfg.n_embd, 0
+        yield ROLE_FFN_NORM, li, ones, GGML_F32, cfg.n_embd, 0
+        for role, (rows, cols) in shapes.items():
+            yield role, li, weights(wtype, rows, cols, sub(role, li)), wtype, cols, rows
+
+
+def prompt_tokens(n: int, n_vocab: int, seed: int) -> np.ndarray:
+    """Seeded random prompt token ids."""
+    return np.random.default_rng(seed).integers(0, n_vocab, size=n, dtype=np.int32)

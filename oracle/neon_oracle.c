@@ -21,11 +21,14 @@
  *     acc[l]) over i = l (mod 8), then (acc[l] + acc[l+4]) for l < 4 and two
  *     horizontal adds, i.e. ((s0 + s1) + (s2 + s3)); restated with scalars.
  * Build with -ffp-contract=off so the compiler adds no contraction of its own.
+ * The row loops run under OpenMP when built with -fopenmp: rows are
+ * independent, so the results do not depend on the thread count.
  */
 #include <math.h>
 #include <stdint.h>
 #include <stddef.h>
 #include <string.h>
+#include <stdlib.h>
 
 #define ORACLE_GGML_Q4_0 2
 #define ORACLE_GGML_Q8_0 8
@@ -186,16 +189,266 @@ int oracle_proj_all_positions(int type, const uint8_t* W, size_t rows, size_t co
     size_t nb = cols / 32;
     if (type == ORACLE_GGML_Q4_0) {
         oracle_quantize_rows_q8_0(X, x_stride, cols, seq, scratch_d, scratch_q);
+#pragma omp parallel for schedule(static)
         for (size_t r = 0; r < rows; ++r)
             for (size_t t = 0; t < seq; ++t)
                 Y[t * y_stride + r] = oracle_dot_q4_0_q8_0(W + r * row_bytes, scratch_d + t * nb,
                                                            scratch_q + t * cols, cols);
         return 0;
     }
-    for (size_t r = 0; r < rows; ++r) {
-        oracle_dequant_q8_0(W + r * row_bytes, cols, rowbuf);
-        for (size_t t = 0; t < seq; ++t)
-            Y[t * y_stride + r] = oracle_dot_f32(rowbuf, X + t * x_stride, cols);
+    (void)rowbuf;
+#pragma omp parallel
+    {
+        float* rb = (float*)malloc(sizeof(float) * cols);
+#pragma omp for schedule(static)
+        for (size_t r = 0; r < rows; ++r) {
+            oracle_dequant_q8_0(W + r * row_bytes, cols, rb);
+            for (size_t t = 0; t < seq; ++t)
+                Y[t * y_stride + r] = oracle_dot_f32(rb, X + t * x_stride, cols);
+        }
+        free(rb);
     }
     return 0;
+}
+
+/* ======================================================================== */
+/* Decode step: restatement of fwd::transformer_forward                      */
+/* (rawllm_forward.hpp:987-1236) and the pieces it calls.                    */
+/* ======================================================================== */
+#include <stdlib.h>
+
+/* Schraudolph exp approximation with the reference's constants; g++ contracts
+ * kA * x + kB into one FMA. Restates engine::fast_expf, rawllm_common.hpp:88-100. */
+float oracle_fast_expf(float x) {
+    if (x < -88.f || x > 88.f) return expf(x);
+    const float kA = 12102203.9f;
+    const float kB = 1064872507.f;
+    int32_t i = (int32_t)fmaf(kA, x, kB);
+    float f;
+    memcpy(&f, &i, 4);
+    return f;
+}
+
+/* x / (1 + fast_expf(-x)). Restates fwd::silu, rawllm_forward.hpp:740. */
+float oracle_silu(float x) { return x / (1.0f + oracle_fast_expf(-x)); }
+
+/* RMSNorm with a double accumulator (contracted into FMAs by g++).
+ * Restates fwd::rms_norm, rawllm_forward.hpp:730-735. */
+void oracle_rms_norm(const float* x, const float* w, float* out, size_t n, float eps) {
+    double ss = 0.0;
+    for (size_t i = 0; i < n; ++i) ss = fma((double)x[i], (double)x[i], ss);
+    float scale = 1.0f / sqrtf((float)(ss / (double)n) + eps);
+    for (size_t i = 0; i < n; ++i) out[i] = x[i] * scale * w[i];
+}
+
+/* freqs[i] = base^(-2i/head_dim). Restates fwd::rope_make_freqs, :755-761. */
+void oracle_rope_freqs(size_t head_dim, float base, float* out) {
+    for (size_t i = 0; i < head_dim / 2; ++i) out[i] = powf(base, -2.0f * (float)i / (float)head_dim);
+}
+
+/* Adjacent-pair rotation of every head at position pos.
+ * Restates fwd::rope_apply, rawllm_forward.hpp:767-782, with g++'s
+ * contraction of x0*c - x1*s and x0*s + x1*c. */
+void oracle_rope_apply(float* vec, size_t n_heads, size_t head_dim, size_t rope_half, size_t pos,
+                       float rope_scale, const float* freqs) {
+    float fpos = (float)pos / rope_scale;
+    for (size_t h = 0; h < n_heads; ++h) {
+        float* v = vec + h * head_dim;
+        for (size_t i = 0; i < rope_half; ++i) {
+            float theta = fpos * freqs[i];
+            float c = cosf(theta), s = sinf(theta);
+            float x0 = v[2 * i], x1 = v[2 * i + 1];
+            v[2 * i] = fmaf(x0, c, -(x1 * s));
+            v[2 * i + 1] = fmaf(x0, s, x1 * c);
+        }
+    }
+}
+
+/* out[i] += w * v[i] as one FMA per element (AVX2+FMA build).
+ * Restates fwd::axpy_f32, rawllm_forward.hpp:485-503. */
+void oracle_axpy_f32(float* out, float w, const float* v, size_t n) {
+    for (size_t i = 0; i < n; ++i) out[i] = fmaf(w, v[i], out[i]);
+}
+
+enum { R_TOKEN_EMBD = 0, R_OUTPUT_NORM, R_OUTPUT, R_ATTN_NORM, R_ATTN_Q, R_ATTN_K, R_ATTN_V, R_ATTN_OUT,
+       R_FFN_NORM, R_FFN_GATE, R_FFN_UP, R_FFN_DOWN };
+#define ORACLE_LAYER_ROLES 9 /* R_ATTN_NORM .. R_FFN_DOWN */
+
+typedef struct {
+    uint32_t n_vocab, n_embd, n_layer, n_head, n_kv_head, head_dim, n_ff, ctx_len;
+    float rope_base, rope_scale;
+    uint32_t rope_dim_count;
+    float norm_eps;
+} oracle_config_t;
+
+typedef struct {
+    uint8_t* data; /* owned copy, NULL if absent */
+    int type;
+    size_t ne0, ne1;
+} oracle_tensor_t;
+
+typedef struct {
+    oracle_config_t cfg;
+    oracle_tensor_t global[3];  /* token_embd, output_norm, output */
+    oracle_tensor_t* layers;    /* n_layer * 9 */
+    float *K, *V;               /* [layer][ctx_len][kv_dim] */
+    size_t length;
+} oracle_model_t;
+
+void* oracle_model_new(const oracle_config_t* cfg) {
+    oracle_model_t* m = (oracle_model_t*)calloc(1, sizeof(oracle_model_t));
+    m->cfg = *cfg;
+    m->layers = (oracle_tensor_t*)calloc((size_t)cfg->n_layer * ORACLE_LAYER_ROLES, sizeof(oracle_tensor_t));
+    size_t kv = (size_t)cfg->n_layer * cfg->ctx_len * cfg->n_kv_head * cfg->head_dim;
+    m->K = (float*)calloc(kv, sizeof(float));
+    m->V = (float*)calloc(kv, sizeof(float));
+    return m;
+}
+
+void oracle_model_free(void* p) {
+    oracle_model_t* m = (oracle_model_t*)p;
+    for (int i = 0; i < 3; ++i) free(m->global[i].data);
+    for (size_t i = 0; i < (size_t)m->cfg.n_layer * ORACLE_LAYER_ROLES; ++i) free(m->layers[i].data);
+    free(m->layers);
+    free(m->K);
+    free(m->V);
+    free(m);
+}
+
+int oracle_model_set(void* p, int role, int layer, const uint8_t* bytes, size_t nbytes, int type, size_t ne0,
+                     size_t ne1) {
+    oracle_model_t* m = (oracle_model_t*)p;
+    oracle_tensor_t* t;
+    if (role <= R_OUTPUT) {
+        t = &m->global[role];
+    } else {
+        if (layer < 0 || (uint32_t)layer >= m->cfg.n_layer || role > R_FFN_DOWN) return -1;
+        t = &m->layers[(size_t)layer * ORACLE_LAYER_ROLES + (role - R_ATTN_NORM)];
+    }
+    free(t->data);
+    t->data = (uint8_t*)malloc(nbytes ? nbytes : 1);
+    memcpy(t->data, bytes, nbytes);
+    t->type = type;
+    t->ne0 = ne0;
+    t->ne1 = ne1;
+    return 0;
+}
+
+size_t oracle_model_length(void* p) { return ((oracle_model_t*)p)->length; }
+void oracle_model_set_length(void* p, size_t n) { ((oracle_model_t*)p)->length = n; }
+
+static const oracle_tensor_t* L_(const oracle_model_t* m, uint32_t li, int role) {
+    return &m->layers[(size_t)li * ORACLE_LAYER_ROLES + (role - R_ATTN_NORM)];
+}
+
+/* Y (seq x y_stride) = proj of X (seq x x_stride) through a 2-D tensor. */
+static int proj(const oracle_tensor_t* W, const float* X, size_t x_stride, float* Y, size_t y_stride, size_t seq) {
+    size_t cols = W->ne0, rows = W->ne1;
+    float* sd = (float*)malloc(sizeof(float) * (seq * cols / 32 + 1));
+    int8_t* sq = (int8_t*)malloc(seq * cols + 1);
+    float* rb = (float*)malloc(sizeof(float) * (cols + 1));
+    int rc = oracle_proj_all_positions(W->type, W->data, rows, cols, X, x_stride, Y, y_stride, seq, sd, sq, rb);
+    free(sd);
+    free(sq);
+    free(rb);
+    return rc;
+}
+
+/* fwd::transformer_forward (rawllm_forward.hpp:987-1236): appends `n` new
+ * tokens to the KV cache and writes the logits of the last one. */
+int oracle_model_forward(void* p, const int32_t* tokens, size_t seq, float* out_logits) {
+    oracle_model_t* m = (oracle_model_t*)p;
+    const oracle_config_t* c = &m->cfg;
+    const size_t n_embd = c->n_embd, n_head = c->n_head, n_kv = c->n_kv_head, hd = c->head_dim, n_ff = c->n_ff;
+    const size_t kv_dim = n_kv * hd, q_dim = n_head * hd, base = m->length;
+    if (seq == 0 || base + seq > c->ctx_len) return -1;
+    const size_t rope_half = c->rope_dim_count ? c->rope_dim_count / 2 : hd / 2;
+    float* freqs = (float*)malloc(sizeof(float) * (hd / 2 + 1));
+    oracle_rope_freqs(hd, c->rope_base, freqs);
+
+    float* h = (float*)malloc(sizeof(float) * seq * n_embd);
+    const oracle_tensor_t* te = &m->global[R_TOKEN_EMBD];
+    size_t te_row = oracle_row_bytes(te->type, n_embd);
+    for (size_t t = 0; t < seq; ++t) {
+        if (tokens[t] < 0 || (size_t)tokens[t] >= te->ne1) return -2;
+        const uint8_t* row = te->data + (size_t)tokens[t] * te_row;
+        if (te->type == ORACLE_GGML_Q8_0) oracle_dequant_q8_0(row, n_embd, h + t * n_embd);
+        else oracle_dequant_q4_0(row, n_embd, h + t * n_embd);
+    }
+    float* normed = (float*)malloc(sizeof(float) * seq * n_embd);
+    float* q = (float*)malloc(sizeof(float) * seq * q_dim);
+    float* k = (float*)malloc(sizeof(float) * seq * kv_dim);
+    float* v = (float*)malloc(sizeof(float) * seq * kv_dim);
+    float* att = (float*)malloc(sizeof(float) * seq * q_dim);
+    float* pout = (float*)malloc(sizeof(float) * seq * n_embd);
+    float* g = (float*)malloc(sizeof(float) * seq * n_ff);
+    float* u = (float*)malloc(sizeof(float) * seq * n_ff);
+    float* scores = (float*)malloc(sizeof(float) * (base + seq));
+    const size_t group = n_head / n_kv;
+    const float scale = 1.0f / sqrtf((float)hd);
+
+    for (uint32_t li = 0; li < c->n_layer; ++li) {
+        const float* wn = (const float*)L_(m, li, R_ATTN_NORM)->data;
+        for (size_t t = 0; t < seq; ++t) oracle_rms_norm(h + t * n_embd, wn, normed + t * n_embd, n_embd, c->norm_eps);
+        proj(L_(m, li, R_ATTN_Q), normed, n_embd, q, q_dim, seq);
+        proj(L_(m, li, R_ATTN_K), normed, n_embd, k, kv_dim, seq);
+        proj(L_(m, li, R_ATTN_V), normed, n_embd, v, kv_dim, seq);
+        for (size_t t = 0; t < seq; ++t) {
+            oracle_rope_apply(q + t * q_dim, n_head, hd, rope_half, base + t, c->rope_scale, freqs);
+            oracle_rope_apply(k + t * kv_dim, n_kv, hd, rope_half, base + t, c->rope_scale, freqs);
+        }
+        float* Kl = m->K + (size_t)li * c->ctx_len * kv_dim;
+        float* Vl = m->V + (size_t)li * c->ctx_len * kv_dim;
+        for (size_t t = 0; t < seq; ++t) {
+            memcpy(Kl + (base + t) * kv_dim, k + t * kv_dim, kv_dim * sizeof(float));
+            memcpy(Vl + (base + t) * kv_dim, v + t * kv_dim, kv_dim * sizeof(float));
+        }
+        /* causal GQA attention, rawllm_forward.hpp:1115-1151 */
+        for (size_t t = 0; t < seq; ++t) {
+            for (size_t hh = 0; hh < n_head; ++hh) {
+                size_t kvh = hh / group, klen = base + t + 1;
+                const float* qv = q + t * q_dim + hh * hd;
+                float maxs = -INFINITY;
+                for (size_t s = 0; s < klen; ++s) {
+                    float dot = oracle_dot_f32(qv, Kl + s * kv_dim + kvh * hd, hd) * scale;
+                    scores[s] = dot;
+                    if (dot > maxs) maxs = dot;
+                }
+                float sum = 0.f;
+                for (size_t s = 0; s < klen; ++s) {
+                    scores[s] = oracle_fast_expf(scores[s] - maxs);
+                    sum += scores[s];
+                }
+                float inv = 1.0f / sum;
+                float* o = att + t * q_dim + hh * hd;
+                for (size_t i = 0; i < hd; ++i) o[i] = 0.f;
+                for (size_t s = 0; s < klen; ++s) oracle_axpy_f32(o, scores[s] * inv, Vl + s * kv_dim + kvh * hd, hd);
+            }
+        }
+        proj(L_(m, li, R_ATTN_OUT), att, q_dim, pout, n_embd, seq);
+        for (size_t i = 0; i < seq * n_embd; ++i) h[i] += pout[i];
+        const float* wf = (const float*)L_(m, li, R_FFN_NORM)->data;
+        for (size_t t = 0; t < seq; ++t) oracle_rms_norm(h + t * n_embd, wf, normed + t * n_embd, n_embd, c->norm_eps);
+        proj(L_(m, li, R_FFN_GATE), normed, n_embd, g, n_ff, seq);
+        proj(L_(m, li, R_FFN_UP), normed, n_embd, u, n_ff, seq);
+        for (size_t i = 0; i < seq * n_ff; ++i) g[i] = oracle_silu(g[i]) * u[i];
+        proj(L_(m, li, R_FFN_DOWN), g, n_ff, pout, n_embd, seq);
+        for (size_t i = 0; i < seq * n_embd; ++i) h[i] += pout[i];
+    }
+    m->length = base + seq;
+    float* fin = (float*)malloc(sizeof(float) * n_embd);
+    oracle_rms_norm(h + (seq - 1) * n_embd, (const float*)m->global[R_OUTPUT_NORM].data, fin, n_embd, c->norm_eps);
+    const oracle_tensor_t* ow = m->global[R_OUTPUT].data ? &m->global[R_OUTPUT] : te;
+    proj(ow, fin, n_embd, out_logits, c->n_vocab, 1);
+    free(fin); free(freqs); free(h); free(normed); free(q); free(k); free(v); free(att); free(pout); free(g);
+    free(u); free(scores);
+    return 0;
+}
+
+/* K/V rows of one layer for positions [0, n). */
+void oracle_model_kv(void* p, int layer, size_t n, float* k, float* v) {
+    oracle_model_t* m = (oracle_model_t*)p;
+    size_t kvd = (size_t)m->cfg.n_kv_head * m->cfg.head_dim;
+    memcpy(k, m->K + (size_t)layer * m->cfg.ctx_len * kvd, n * kvd * sizeof(float));
+    memcpy(v, m->V + (size_t)layer * m->cfg.ctx_len * kvd, n * kvd * sizeof(float));
 }

@@ -194,3 +194,119 @@ class RefPool:
                                                  X.reshape(-1), x_stride, seq)
         if rc != 0:
             raise RuntimeError(self.L.ref_last_error().decode())
+
+
+# ----------------------------------------------------------------------------
+# Decode step: the restatement (C) and the reference's transformer_forward
+# ----------------------------------------------------------------------------
+
+class _Config(C.Structure):
+    _fields_ = [(f, C.c_uint32) for f in ("n_vocab", "n_embd", "n_layer", "n_head", "n_kv_head", "head_dim",
+                                          "n_ff", "ctx_len")] + [
+        ("rope_base", C.c_float), ("rope_scale", C.c_float), ("rope_dim_count", C.c_uint32),
+        ("norm_eps", C.c_float)]
+
+
+def _config(cfg):
+    return _Config(*[getattr(cfg, f) for f in ("n_vocab", "n_embd", "n_layer", "n_head", "n_kv_head",
+                                               "head_dim", "n_ff", "ctx_len")],
+                   cfg.rope_base, cfg.rope_scale, cfg.rope_dim_count, cfg.norm_eps)
+
+
+class Model:
+    """A decoder held by the oracle restatement (kind="port") or by the
+    reference's own transformer_forward (kind="reference").
+
+    forward(tokens) appends the tokens to the KV cache and returns the logits
+    of the last one, as fwd::transformer_forward does."""
+
+    def __init__(self, cfg, tensors, kind="port", threads=None):
+        self.cfg, self.kind = cfg, kind
+        if kind == "port":
+            L = lib()
+            L.oracle_model_new.restype = C.c_void_p
+            L.oracle_model_new.argtypes = [C.POINTER(_Config)]
+            L.oracle_model_free.argtypes = [C.c_void_p]
+            L.oracle_model_set.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p, _sz, C.c_int, _sz, _sz]
+            L.oracle_model_forward.argtypes = [C.c_void_p, C.c_void_p, _sz, _f32p]
+            L.oracle_model_length.argtypes = [C.c_void_p]
+            L.oracle_model_length.restype = _sz
+            L.oracle_model_set_length.argtypes = [C.c_void_p, _sz]
+            L.oracle_model_kv.argtypes = [C.c_void_p, C.c_int, _sz, _f32p, _f32p]
+            self.L, self.pool = L, None
+            self._new, self._free, self._set = L.oracle_model_new, L.oracle_model_free, L.oracle_model_set
+            self._len, self._setlen, self._kv = L.oracle_model_length, L.oracle_model_set_length, L.oracle_model_kv
+            self._fwd = lambda h, t, n, out: L.oracle_model_forward(h, t, n, out)
+        elif kind == "reference":
+            L = ref()
+            if L is None:
+                raise RuntimeError("reference CPU path not built (oracle/_ref missing)")
+            L.ref_model_new.restype = C.c_void_p
+            L.ref_model_new.argtypes = [C.POINTER(_Config)]
+            L.ref_model_free.argtypes = [C.c_void_p]
+            L.ref_model_set.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p, _sz, C.c_int, _sz, _sz]
+            L.ref_model_forward.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, _sz, _f32p]
+            L.ref_model_length.argtypes = [C.c_void_p]
+            L.ref_model_length.restype = _sz
+            L.ref_model_set_length.argtypes = [C.c_void_p, _sz]
+            L.ref_model_kv.argtypes = [C.c_void_p, C.c_int, _sz, _f32p, _f32p]
+            self.L = L
+            self.pool = RefPool(threads or os.cpu_count() or 1)
+            self._new, self._free, self._set = L.ref_model_new, L.ref_model_free, L.ref_model_set
+            self._len, self._setlen, self._kv = L.ref_model_length, L.ref_model_set_length, L.ref_model_kv
+            self._fwd = lambda h, t, n, out: L.ref_model_forward(h, self.pool.h, t, n, out)
+        else:
+            raise ValueError(kind)
+        self._cfg = _config(cfg)
+        self.h = self._new(C.byref(self._cfg))
+        for role, layer, raw, typ, ne0, ne1 in tensors:
+            raw = np.ascontiguousarray(raw)
+            if self._set(self.h, role, layer, raw.ctypes.data, raw.nbytes, typ, ne0, ne1) != 0:
+                raise RuntimeError(f"bad tensor role {role} layer {layer}")
+
+    def forward(self, tokens):
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        out = np.zeros(self.cfg.n_vocab, np.float32)
+        rc = self._fwd(self.h, t.ctypes.data, t.size, out)
+        if rc != 0:
+            raise RuntimeError("forward failed" + (": " + self.L.ref_last_error().decode() if self.kind == "reference" else ""))
+        return out
+
+    @property
+    def length(self):
+        return int(self._len(self.h))
+
+    def set_length(self, n):
+        self._setlen(self.h, n)
+
+    def kv(self, layer, n):
+        k = np.zeros((n, self.cfg.kv_dim), np.float32)
+        v = np.zeros((n, self.cfg.kv_dim), np.float32)
+        self._kv(self.h, layer, n, k.reshape(-1), v.reshape(-1))
+        return k, v
+
+    def generate_greedy(self, prompt, n_new):
+        """run_generation's loop (NEON-3.cpp:744-758) with greedy sampling
+        (first maximum, NEON-3.cpp:471-474). Returns tokens and per-step logits."""
+        logits = self.forward(prompt)
+        toks, all_logits = [], [logits]
+        nxt = int(np.argmax(logits))
+        for _ in range(n_new):
+            toks.append(nxt)
+            logits = self.forward(np.array([nxt], np.int32))
+            all_logits.append(logits)
+            nxt = int(np.argmax(logits))
+        return np.array(toks, np.int32), np.stack(all_logits)
+
+    def close(self):
+        if self.h:
+            self._free(self.h)
+            self.h = None
+        if self.pool is not None:
+            self.pool.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -134,3 +134,130 @@ int ref_proj_all_positions_multi(void* pool, size_t n_targets, const uint8_t* co
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Decode step: the reference's own transformer_forward (rawllm_forward.hpp:
+// 987-1236) on a model held in memory. Tensor roles and their numbering match
+// include/neon_cuda.h's NEON_ROLE_* values.
+// ---------------------------------------------------------------------------
+namespace {
+
+enum Role { TOKEN_EMBD = 0, OUTPUT_NORM = 1, OUTPUT = 2, ATTN_NORM = 3, ATTN_Q = 4, ATTN_K = 5, ATTN_V = 6,
+            ATTN_OUT = 7, FFN_NORM = 8, FFN_GATE = 9, FFN_UP = 10, FFN_DOWN = 11 };
+
+struct RefModel {
+    engine::Config cfg;
+    std::vector<std::vector<uint8_t>> blobs;           // owned tensor bytes
+    std::vector<std::unique_ptr<loader::TensorInfo>> tensors;
+    fwd::ModelWeights mw;
+    fwd::KVCache cache;
+};
+
+}  // namespace
+
+extern "C" {
+
+typedef struct {
+    uint32_t n_vocab, n_embd, n_layer, n_head, n_kv_head, head_dim, n_ff, ctx_len;
+    float rope_base, rope_scale;
+    uint32_t rope_dim_count;
+    float norm_eps;
+} ref_config_t;
+
+void* ref_model_new(const ref_config_t* c) {
+    auto* m = new RefModel();
+    m->cfg.n_vocab = c->n_vocab;
+    m->cfg.n_embd = c->n_embd;
+    m->cfg.n_layer = c->n_layer;
+    m->cfg.n_head = c->n_head;
+    m->cfg.n_kv_head = c->n_kv_head;
+    m->cfg.head_dim = c->head_dim;
+    m->cfg.n_ff = c->n_ff;
+    m->cfg.ctx_len = c->ctx_len;
+    m->cfg.kv_window = c->ctx_len;
+    m->cfg.rope_base = c->rope_base;
+    m->cfg.rope_scale = c->rope_scale;
+    m->cfg.rope_dim_count = c->rope_dim_count;
+    m->cfg.norm_eps = c->norm_eps;
+    m->cfg.use_swiglu = true;
+    m->mw.layers.resize(c->n_layer);
+    m->cache = fwd::KVCache(c->n_layer, (size_t)c->n_kv_head * c->head_dim, c->ctx_len);
+    return m;
+}
+
+void ref_model_free(void* p) { delete static_cast<RefModel*>(p); }
+
+// Copies `nbytes` of tensor data; shape is GGUF ne (ne1 == 0 for a 1-D tensor).
+int ref_model_set(void* p, int role, int layer, const uint8_t* bytes, size_t nbytes, int type, size_t ne0,
+                  size_t ne1) {
+    auto* m = static_cast<RefModel*>(p);
+    m->blobs.emplace_back(bytes, bytes + nbytes);
+    auto t = std::make_unique<loader::TensorInfo>();
+    t->name = "role" + std::to_string(role) + "." + std::to_string(layer);
+    t->shape = ne1 ? std::vector<uint64_t>{ne0, ne1} : std::vector<uint64_t>{ne0};
+    t->type = static_cast<loader::GGMLType>(type);
+    t->nbytes = nbytes;
+    t->data_ptr = m->blobs.back().data();
+    const loader::TensorInfo* tp = t.get();
+    m->tensors.push_back(std::move(t));
+    if (role <= OUTPUT) {
+        if (role == TOKEN_EMBD) m->mw.token_embd = tp;
+        if (role == OUTPUT_NORM) m->mw.output_norm = tp;
+        if (role == OUTPUT) m->mw.output = tp;
+        return 0;
+    }
+    if (layer < 0 || (size_t)layer >= m->mw.layers.size()) return -1;
+    auto& L = m->mw.layers[layer];
+    switch (role) {
+        case ATTN_NORM: L.attn_norm = tp; break;
+        case ATTN_Q: L.attn_q = tp; break;
+        case ATTN_K: L.attn_k = tp; break;
+        case ATTN_V: L.attn_v = tp; break;
+        case ATTN_OUT: L.attn_out = tp; break;
+        case FFN_NORM: L.ffn_norm = tp; break;
+        case FFN_GATE: L.ffn_gate = tp; break;
+        case FFN_UP: L.ffn_up = tp; break;
+        case FFN_DOWN: L.ffn_down = tp; break;
+        default: return -1;
+    }
+    return 0;
+}
+
+// fwd::transformer_forward on `n` new tokens; logits of the last one.
+int ref_model_forward(void* p, void* pool, const int32_t* tokens, size_t n, float* logits) {
+    auto* m = static_cast<RefModel*>(p);
+    try {
+        std::vector<int32_t> t(tokens, tokens + n);
+        fwd::transformer_forward(m->cfg, m->mw, t, m->cache, logits, *static_cast<util::ThreadPool*>(pool));
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+size_t ref_model_length(void* p) { return static_cast<RefModel*>(p)->cache.length; }
+void ref_model_set_length(void* p, size_t len) { static_cast<RefModel*>(p)->cache.length = len; }
+
+// K/V cache rows of one layer (kv_dim floats each) for positions [0, n).
+void ref_model_kv(void* p, int layer, size_t n, float* k, float* v) {
+    auto* m = static_cast<RefModel*>(p);
+    const size_t kvd = m->cache.kv_dim;
+    std::memcpy(k, m->cache.k_row(layer, 0), n * kvd * sizeof(float));
+    std::memcpy(v, m->cache.v_row(layer, 0), n * kvd * sizeof(float));
+}
+
+// Building blocks, exposed for pinning the C restatement.
+float ref_fast_expf(float x) { return engine::fast_expf(x); }
+float ref_silu(float x) { return fwd::silu(x); }
+void ref_rms_norm(const float* x, const float* w, float* out, size_t n, float eps) { fwd::rms_norm(x, w, out, n, eps); }
+void ref_rope_freqs(size_t head_dim, float base, float* out) {
+    auto f = fwd::rope_make_freqs(head_dim, base);
+    std::memcpy(out, f.data(), f.size() * sizeof(float));
+}
+void ref_rope_apply(float* vec, size_t n_heads, size_t head_dim, size_t rope_half, size_t pos, float rope_scale,
+                    const float* freqs) {
+    fwd::rope_apply(vec, n_heads, head_dim, rope_half, pos, rope_scale, freqs);
+}
+void ref_axpy_f32(float* out, float w, const float* v, size_t n) { fwd::axpy_f32(out, w, v, n); }
+
+}  // extern "C"

@@ -1,6 +1,6 @@
 """Generate the golden vectors in tests/golden/ from the reference itself.
 
-    make -C oracle ref && python tests/golden/make_golden.py
+    make -C oracle ref && python tests/golden/make_golden.py && python tests/golden/make_golden.py --decode
 
 Every expected output here is produced by the reference's own CPU path --
 rawllm_forward.hpp compiled with the reference's flags into
@@ -14,6 +14,7 @@ Outputs (numpy .npz, a few hundred KB in all):
   block_isum.npz     4096 random Q4_0 blocks x Q8_0 blocks -> isum
   matvec.npz         Q4_0 / Q8_0 proj_all_positions cases (W bytes, X, Y)
   multi.npz          a proj_all_positions_multi case shaped like Q/K/V
+  decode_tiny.npz    greedy generation of transformer_forward on a small model
 """
 from __future__ import annotations
 
@@ -129,5 +130,31 @@ def main() -> None:
     print("golden vectors written to", HERE)
 
 
-if __name__ == "__main__":
+if __name__ == "__main__" and "--decode" not in sys.argv:
     main()
+
+
+def decode_golden() -> None:
+    """decode_tiny.npz: greedy generation of the reference's transformer_forward
+    on a small seeded model (the prompt, 16 tokens, the logits of every step and
+    a checksum of the regenerated weights)."""
+    import hashlib
+
+    cfg = TINY_CFG
+    tensors = list(S.model_tensors(cfg, seed=TINY_SEED))
+    h = hashlib.sha256()
+    for role, layer, raw, typ, ne0, ne1 in tensors:
+        h.update(np.ascontiguousarray(raw).tobytes())
+    m = O.Model(cfg, tensors, "reference", threads=4)
+    prompt = S.prompt_tokens(8, cfg.n_vocab, TINY_SEED + 1)
+    toks, logits = m.generate_greedy(prompt, 16)
+    m.close()
+    np.savez_compressed(os.path.join(HERE, "decode_tiny.npz"), prompt=prompt, tokens=toks, logits=logits,
+                        weights_sha256=np.frombuffer(h.digest(), np.uint8))
+
+
+TINY_CFG = S.ModelConfig(1000, 256, 2, 4, 2, 64, 512, ctx_len=64, rope_base=1e4, name="tiny")
+TINY_SEED = 3
+
+if __name__ == "__main__" and "--decode" in sys.argv:
+    decode_golden()

@@ -1,0 +1,102 @@
+"""The decode-step restatement of the oracle (oracle/neon_oracle.c: fast_expf,
+silu, rms_norm, RoPE, GQA attention and transformer_forward) against the
+golden generation of the reference's own transformer_forward, and against
+the reference build itself. Bit-exact."""
+import ctypes as C
+import hashlib
+
+import numpy as np
+import pytest
+
+import oracle as O
+import synth as S
+from conftest import load_golden
+
+TINY = S.ModelConfig(1000, 256, 2, 4, 2, 64, 512, ctx_len=64, rope_base=1e4, name="tiny")
+f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
+
+
+def bits(a):
+    return np.ascontiguousarray(a, np.float32).view(np.uint32)
+
+
+def test_tiny_model_generation_matches_golden():
+    g = load_golden("decode_tiny.npz")
+    tensors = list(S.model_tensors(TINY, seed=3))
+    h = hashlib.sha256()
+    for t in tensors:
+        h.update(np.ascontiguousarray(t[2]).tobytes())
+    assert np.array_equal(np.frombuffer(h.digest(), np.uint8), g["weights_sha256"]), "weights regenerated differently"
+    m = O.Model(TINY, tensors, "port")
+    toks, logits = m.generate_greedy(g["prompt"], 16)
+    assert np.array_equal(toks, g["tokens"])
+    assert np.array_equal(bits(logits), bits(g["logits"]))
+    assert m.length == len(g["prompt"]) + 16
+
+
+def test_length_rewind_recomputes_identically():
+    """Rewinding cache.length (run_generation's prefix reuse, NEON-3.cpp:690-703)
+    and re-feeding the same tokens gives the same logits."""
+    g = load_golden("decode_tiny.npz")
+    m = O.Model(TINY, list(S.model_tensors(TINY, seed=3)), "port")
+    a = m.forward(g["prompt"])
+    b = m.forward(np.array([5, 7, 9], np.int32))
+    m.set_length(len(g["prompt"]))
+    c = m.forward(np.array([5, 7, 9], np.int32))
+    assert np.array_equal(bits(b), bits(c)) and not np.array_equal(bits(a), bits(b))
+
+
+ref_only = pytest.mark.skipif(not O.ref_available(), reason="oracle/_ref not built")
+
+
+@ref_only
+def test_pieces_match_reference():
+    L, R = O.lib(), O.ref()
+    for name in ("fast_expf", "silu"):
+        fo, fr = getattr(L, "oracle_" + name), getattr(R, "ref_" + name)
+        fo.argtypes = fr.argtypes = [C.c_float]
+        fo.restype = fr.restype = C.c_float
+        xs = np.concatenate([np.linspace(-100, 100, 4001, dtype=np.float32),
+                             np.random.default_rng(0).standard_normal(4000).astype(np.float32) * 10])
+        assert all(np.float32(fo(x)).view(np.uint32) == np.float32(fr(x)).view(np.uint32) for x in xs), name
+    L.oracle_rms_norm.argtypes = R.ref_rms_norm.argtypes = [f32p, f32p, f32p, C.c_size_t, C.c_float]
+    rng = np.random.default_rng(1)
+    for n in (1024, 3072, 8192):
+        x = (rng.standard_normal(n) * 3).astype(np.float32)
+        w = rng.standard_normal(n).astype(np.float32)
+        a, b = np.zeros(n, np.float32), np.zeros(n, np.float32)
+        L.oracle_rms_norm(x, w, a, n, 1e-5)
+        R.ref_rms_norm(x, w, b, n, 1e-5)
+        assert np.array_equal(bits(a), bits(b))
+    L.oracle_rope_freqs.argtypes = R.ref_rope_freqs.argtypes = [C.c_size_t, C.c_float, f32p]
+    L.oracle_rope_apply.argtypes = R.ref_rope_apply.argtypes = [f32p, C.c_size_t, C.c_size_t, C.c_size_t,
+                                                               C.c_size_t, C.c_float, f32p]
+    for base in (1e4, 5e5, 1e6):
+        fa, fb = np.zeros(64, np.float32), np.zeros(64, np.float32)
+        L.oracle_rope_freqs(128, base, fa)
+        R.ref_rope_freqs(128, base, fb)
+        assert np.array_equal(bits(fa), bits(fb))
+        for pos in (0, 1, 17, 511, 2047):
+            v = rng.standard_normal(8 * 128).astype(np.float32)
+            va, vb = v.copy(), v.copy()
+            L.oracle_rope_apply(va, 8, 128, 64, pos, 1.0, fb)
+            R.ref_rope_apply(vb, 8, 128, 64, pos, 1.0, fb)
+            assert np.array_equal(bits(va), bits(vb))
+
+
+@ref_only
+@pytest.mark.parametrize("cfg,prompt,steps", [
+    (TINY.with_(n_kv_head=4), 5, 6),                                             # MHA (group 1)
+    (TINY.with_(n_vocab=777, n_embd=384, n_ff=1024, n_head=6, n_kv_head=2), 9, 5),  # group 3, odd vocab
+    (S.QWEN3_0_6B.with_(n_layer=2, n_vocab=4096, ctx_len=96), 24, 8),            # Qwen-shaped layers
+])
+def test_model_forward_matches_reference(cfg, prompt, steps):
+    tensors = list(S.model_tensors(cfg, seed=11))
+    mo, mr = O.Model(cfg, tensors, "port"), O.Model(cfg, tensors, "reference", threads=4)
+    p = S.prompt_tokens(prompt, cfg.n_vocab, 12)
+    ta, la = mo.generate_greedy(p, steps)
+    tb, lb = mr.generate_greedy(p, steps)
+    assert np.array_equal(ta, tb) and np.array_equal(bits(la), bits(lb))
+    k1, v1 = mo.kv(1, prompt + steps)
+    k2, v2 = mr.kv(1, prompt + steps)
+    assert np.array_equal(bits(k1), bits(k2)) and np.array_equal(bits(v1), bits(v2))
