@@ -152,6 +152,76 @@ NEON_API uint64_t neon_cuda_launch_count(void);
 NEON_API int neon_cuda_matvec_q4_0_noalloc(neon_tensor_t W, const float* dX, size_t x_stride, float* dY,
                                            size_t y_stride, size_t seq, void* stream);
 
+/* ------------------------------------------------------------------------ */
+/* Decode step on the device                                                */
+/* ------------------------------------------------------------------------ */
+
+/* Tensor roles of a NANITY decoder (NANITY_ARCHITECTURE_SPEC.md section 4;
+ * fwd::ModelWeights / LayerWeights, rawllm_forward.hpp:823-834). */
+#define NEON_ROLE_TOKEN_EMBD 0 /* token_embd.weight  [n_embd, n_vocab] */
+#define NEON_ROLE_OUTPUT_NORM 1 /* output_norm.weight [n_embd] F32 */
+#define NEON_ROLE_OUTPUT 2     /* output.weight      [n_embd, n_vocab], optional (tied) */
+#define NEON_ROLE_ATTN_NORM 3  /* blk.i.attn_norm.weight [n_embd] F32 */
+#define NEON_ROLE_ATTN_Q 4     /* blk.i.attn_q.weight    [n_embd, q_dim] */
+#define NEON_ROLE_ATTN_K 5     /* blk.i.attn_k.weight    [n_embd, kv_dim] */
+#define NEON_ROLE_ATTN_V 6     /* blk.i.attn_v.weight    [n_embd, kv_dim] */
+#define NEON_ROLE_ATTN_OUT 7   /* blk.i.attn_output.weight [q_dim, n_embd] */
+#define NEON_ROLE_FFN_NORM 8   /* blk.i.ffn_norm.weight  [n_embd] F32 */
+#define NEON_ROLE_FFN_GATE 9   /* blk.i.ffn_gate.weight  [n_embd, n_ff] */
+#define NEON_ROLE_FFN_UP 10    /* blk.i.ffn_up.weight    [n_embd, n_ff] */
+#define NEON_ROLE_FFN_DOWN 11  /* blk.i.ffn_down.weight  [n_ff, n_embd] */
+
+/* Hyperparameters, the fields of engine::Config (rawllm_common.hpp:113-145)
+ * the forward pass reads. ctx_len is the KV-cache capacity in positions. */
+typedef struct {
+    uint32_t n_vocab, n_embd, n_layer, n_head, n_kv_head, head_dim, n_ff, ctx_len;
+    float rope_base, rope_scale;
+    uint32_t rope_dim_count; /* 0: rotate all of head_dim */
+    float norm_eps;
+} neon_model_config_t;
+
+typedef struct neon_model* neon_model_t;
+
+/* A decoder on the current device: its KV cache (fp32, like fwd::KVCache,
+ * rawllm_forward.hpp:905-927), activations and RoPE table. Tensors are added
+ * with neon_cuda_model_set_tensor. Replaces get_engine_state's ModelWeights
+ * + KVCache (NEON-3.cpp:535-564). */
+NEON_API int neon_cuda_model_create(const neon_model_config_t* cfg, neon_model_t* out);
+
+/* Upload one tensor (GGUF bytes; ne1 = 0 for a 1-D norm weight). Projection
+ * and embedding tensors are Q4_0 or Q8_0, norm weights F32. */
+NEON_API int neon_cuda_model_set_tensor(neon_model_t m, int role, int layer, const uint8_t* host_bytes,
+                                        size_t nbytes, int ggml_type, size_t ne0, size_t ne1);
+
+/* fwd::transformer_forward (rawllm_forward.hpp:987-1236): process `n` new
+ * tokens at positions length .. length+n-1, append their K/V to the cache,
+ * advance length, and write the n_vocab logits of the last token to
+ * logits_host (may be NULL). Blocks until done. */
+NEON_API int neon_cuda_model_forward(neon_model_t m, const int32_t* tokens, size_t n, float* logits_host);
+
+/* run_generation's loop (NEON-3.cpp:676-759) with greedy sampling (the first
+ * maximum, NEON-3.cpp:471-474), device-resident: the prompt is processed,
+ * then every decode step runs from one CUDA graph with the sampled token fed
+ * back on the device. Writes up to max_new tokens (stopping before eos_id,
+ * as the reference does; eos_id < 0: never) and their count. */
+NEON_API int neon_cuda_model_generate(neon_model_t m, const int32_t* prompt, size_t n_prompt, size_t max_new,
+                                      int32_t eos_id, int32_t* out_tokens, size_t* n_out);
+
+/* KV-cache length (KVCache::length), and rewinding it (run_generation's
+ * prefix reuse, NEON-3.cpp:690-703). */
+NEON_API int neon_cuda_model_length(neon_model_t m, size_t* length);
+NEON_API int neon_cuda_model_set_length(neon_model_t m, size_t length);
+
+/* Copy the K and V rows of `layer` for positions [0, n) to the host
+ * (n x n_kv_head*head_dim floats each). */
+NEON_API int neon_cuda_model_read_kv(neon_model_t m, int layer, size_t n, float* k_host, float* v_host);
+
+/* Time of the last neon_cuda_model_generate's decode steps, device-measured
+ * (CUDA events around the replayed graphs), in milliseconds. */
+NEON_API int neon_cuda_model_decode_ms(neon_model_t m, float* ms);
+
+NEON_API int neon_cuda_model_free(neon_model_t m);
+
 /* Launch option: programmatic dependent launch (PDL) lets a matvec fetch its
  * weights while the previous kernel on the stream finishes; on by default. */
 NEON_API int neon_cuda_set_pdl(int enabled);

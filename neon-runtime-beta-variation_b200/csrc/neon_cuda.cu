@@ -1,6 +1,7 @@
 // neon_cuda.cu -- C ABI of the sm_100a quantized matvec backend (see
 // include/neon_cuda.h for the contract of every entry point).
 #include "neon_cuda.h"
+#include "neon_internal.h"
 #include "neon_kernels.cuh"
 
 #include <cuda_runtime.h>
@@ -14,16 +15,6 @@
 #include <vector>
 
 using namespace neon;
-
-struct neon_tensor {
-    int device;
-    int type;
-    size_t rows, cols, nb;
-    uint8_t* base;  // single allocation: payload plane, then scale plane
-    uint8_t* qs;
-    uint16_t* d;
-    size_t bytes;
-};
 
 namespace {
 
@@ -243,7 +234,7 @@ int stream_occupancy(int type, int rc, int smem) {
 }
 
 int launch_stream(const std::vector<const neon_proj_target_t*>& t, int type, int nb, const float* dX,
-                  cudaStream_t st, DeviceState& ds) {
+                  cudaStream_t st, DeviceState& ds, int accumulate) {
     size_t total_rows = 0;
     for (auto* tg : t) total_rows += tg->W->rows;
     const StreamPlan p = plan_stream(type, nb, total_rows, ds.sms);
@@ -277,6 +268,7 @@ int launch_stream(const std::vector<const neon_proj_target_t*>& t, int type, int
         a.nch = p.nch;
         a.stage_bytes = p.stage_bytes;
         a.x_vec = (reinterpret_cast<uintptr_t>(dX) % 16) == 0;
+        a.accumulate = accumulate;
         // Pick the ring depth that keeps the most weight bytes in flight per
         // SM (resident CTAs x stages x stage bytes), then size the grid to what
         // is resident: a CTA that starts late repays the X staging.
@@ -360,10 +352,10 @@ struct Group {
 };
 
 int launch_group(const Group& g, const float* dX, size_t x_stride, size_t seq, cudaStream_t st,
-                 DeviceState& ds) {
+                 DeviceState& ds, int accumulate) {
     const int nb = (int)(g.cols / 32);
     const bool q4 = g.type == NEON_GGML_Q4_0;
-    if (seq == 1) return launch_stream(g.t, g.type, nb, dX, st, ds);
+    if (seq == 1) return launch_stream(g.t, g.type, nb, dX, st, ds, accumulate);
     size_t start = 0;
     while (start < g.t.size()) {
         MatvecArgs a;
@@ -387,6 +379,7 @@ int launch_group(const Group& g, const float* dX, size_t x_stride, size_t seq, c
         }
         a.n_spans = (int)n;
         a.n_tiles = tiles;
+        a.accumulate = accumulate;
         if (q4) {
             a.xq = ds.xq;
             a.xd = ds.xd;
@@ -405,7 +398,7 @@ int launch_group(const Group& g, const float* dX, size_t x_stride, size_t seq, c
 
 // Shared body of neon_cuda_matvec[_multi] on device buffers.
 int matvec_targets(const neon_proj_target_t* targets, size_t n_targets, const float* dX,
-                   size_t x_stride, size_t seq, void* stream) {
+                   size_t x_stride, size_t seq, void* stream, int accumulate = 0) {
     if (n_targets == 0 || seq == 0) return NEON_OK;
     if (!targets || !dX) return set_err(NEON_ERR_INVALID, "null targets or X");
     int device = targets[0].W ? targets[0].W->device : -1;
@@ -457,13 +450,34 @@ int matvec_targets(const neon_proj_target_t* targets, size_t n_targets, const fl
         if (rc) return rc;
     }
     for (const Group& g : groups) {
-        rc = launch_group(g, dX, x_stride, seq, st, ds);
+        rc = launch_group(g, dX, x_stride, seq, st, ds, accumulate);
         if (rc) return rc;
     }
     return NEON_OK;
 }
 
 }  // namespace
+
+// Library-internal (not exported): the matvec launcher with the accumulate
+// epilogue, and the error helpers, for the decode engine (neon_decode.cu).
+namespace neon_internal {
+int matvec(const neon_proj_target_t* targets, size_t n, const float* dX, size_t x_stride, size_t seq,
+           cudaStream_t st, int accumulate) {
+    return matvec_targets(targets, n, dX, x_stride, seq, (void*)st, accumulate);
+}
+int error(int code, const std::string& msg) { return set_err(code, msg); }
+int cuda_error(cudaError_t e, const char* what) { return cuda_err(e, what); }
+int launched(int n) {
+    g_launches.fetch_add((uint64_t)n, std::memory_order_relaxed);
+    return NEON_OK;
+}
+bool pdl_enabled() { return g_pdl.load(std::memory_order_relaxed) != 0; }
+int device_sms(int device) {
+    int rc = init_device(device);
+    return rc ? -1 : g_dev[device].sms;
+}
+int check_device_error(int device) { return check_device_err(device); }
+}  // namespace neon_internal
 
 extern "C" {
 

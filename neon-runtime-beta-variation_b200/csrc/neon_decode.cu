@@ -1,0 +1,732 @@
+// neon_decode.cu -- the decode step of a NANITY decoder on one device.
+//
+// Reference: fwd::transformer_forward (rawllm_forward.hpp:987-1236) and the
+// greedy loop of run_generation (NEON-3.cpp:676-759). Per layer:
+//   xn = rms_norm(h, attn_norm)                     rmsnorm_kernel
+//   q, k, v = proj_multi(xn)                        streaming matvec (one launch)
+//   rope(q, k); K/V cache[pos] = k, v               rope_kv_kernel
+//   att = causal GQA attention(q, cache)            attention_kernel
+//   h += proj(att, attn_output)                     matvec, accumulate epilogue
+//   xn = rms_norm(h, ffn_norm)                      rmsnorm_kernel
+//   g, u = proj_multi(xn); act = silu(g) * u        matvec + silu_mul_kernel
+//   h += proj(act, ffn_down)                        matvec, accumulate epilogue
+// then logits = proj(rms_norm(h_last, output_norm), output ?? token_embd) and,
+// in generation, the first maximum (argmax_kernel), fed back on the device.
+//
+// Element-wise arithmetic mirrors the reference's optimised build: RoPE with
+// the reference's cos/sin values (host libm, uploaded as a table) and g++'s
+// FMA contraction, fast_expf's Schraudolph constants, silu as x/(1+e), the
+// RMSNorm scale in fp32 from a double sum of squares. Reductions (dot
+// products, softmax sums, the double sum) run as parallel trees, so sums
+// differ from the reference's sequential order by fp32 rounding only.
+#include "neon_cuda.h"
+#include "neon_internal.h"
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <string>
+#include <vector>
+
+using neon_internal::cuda_error;
+using neon_internal::error;
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kMaxChunk = 256;      // positions per forward chunk (prefill)
+constexpr int kMaxCtx = 16384;      // attention scores live in shared memory
+
+#define DEC_TRY(call)                                              \
+    do {                                                           \
+        cudaError_t _e = (call);                                   \
+        if (_e != cudaSuccess) return cuda_error(_e, #call);       \
+    } while (0)
+
+// ---------------------------------------------------------------------------
+// device helpers
+// ---------------------------------------------------------------------------
+
+// engine::fast_expf (rawllm_common.hpp:88-100): 2^(x/ln2) through the float
+// bit pattern; kA*x + kB is one FMA in the reference build, truncated to int.
+__device__ __forceinline__ float fast_expf_dev(float x) {
+    if (x < -88.f || x > 88.f) return expf(x);
+    return __int_as_float(__float2int_rz(__fmaf_rn(12102203.9f, x, 1064872507.f)));
+}
+
+__device__ __forceinline__ float warp_sum_f(float v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float warp_max_f(float v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Block-wide reductions for kThreads threads (scratch: 32 entries).
+__device__ float block_sum_f(float v, float* scratch) {
+    v = warp_sum_f(v);
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    __syncthreads();
+    if (l == 0) scratch[w] = v;
+    __syncthreads();
+    float r = l < (int)(blockDim.x >> 5) ? scratch[l] : 0.f;
+    r = warp_sum_f(r);
+    return r;
+}
+
+__device__ float block_max_f(float v, float* scratch) {
+    v = warp_max_f(v);
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    __syncthreads();
+    if (l == 0) scratch[w] = v;
+    __syncthreads();
+    float r = l < (int)(blockDim.x >> 5) ? scratch[l] : -INFINITY;
+    r = warp_max_f(r);
+    return r;
+}
+
+__device__ double block_sum_d(double v, double* scratch) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    __syncthreads();
+    if (l == 0) scratch[w] = v;
+    __syncthreads();
+    double r = l < (int)(blockDim.x >> 5) ? scratch[l] : 0.0;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
+    return r;
+}
+
+// ---------------------------------------------------------------------------
+// kernels
+// ---------------------------------------------------------------------------
+
+// h[t] = dequantised row tokens[t] of the embedding (dequant_q8_0 /
+// dequant_q4_0, rawllm_forward.hpp:143-162; transformer_forward :1023-1033).
+// One thread per 32-block. An out-of-range id sets bit 1 of *err and reads row 0.
+__global__ void embed_kernel(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dpl, int type, int nb,
+                             const int* __restrict__ tokens, int n_vocab, float* __restrict__ h,
+                             unsigned* err) {
+    const int t = blockIdx.y;
+    int tok = tokens[t];
+    if (tok < 0 || tok >= n_vocab) {
+        if (threadIdx.x == 0) atomicOr(err, 2u);
+        tok = 0;
+    }
+    float* out = h + (long long)t * nb * 32;
+    for (int b = blockIdx.x * blockDim.x + threadIdx.x; b < nb; b += gridDim.x * blockDim.x) {
+        const long long i = (long long)tok * nb + b;
+        const float d = __half2float(__ushort_as_half(dpl[i]));
+        if (type == NEON_GGML_Q8_0) {
+            const int8_t* q = reinterpret_cast<const int8_t*>(qs + i * 32);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) out[b * 32 + j] = __fmul_rn(d, (float)q[j]);
+        } else {
+            const uint8_t* q = qs + i * 16;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                out[b * 32 + j] = __fmul_rn(d, __fsub_rn((float)(q[j] & 0xF), 8.f));
+                out[b * 32 + j + 16] = __fmul_rn(d, __fsub_rn((float)(q[j] >> 4), 8.f));
+            }
+        }
+    }
+}
+
+// out = x * (1/sqrt(mean(x^2) + eps)) * w per row; one CTA per row
+// (fwd::rms_norm, rawllm_forward.hpp:730-735).
+__global__ void __launch_bounds__(kThreads) rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                                           float* __restrict__ out, int n, float eps) {
+    __shared__ double dscratch[32];
+    const float* xr = x + (long long)blockIdx.x * n;
+    float* o = out + (long long)blockIdx.x * n;
+    double ss = 0.0;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) ss = fma((double)xr[i], (double)xr[i], ss);
+    ss = block_sum_d(ss, dscratch);
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)(ss / (double)n), eps)));
+    for (int i = threadIdx.x; i < n; i += blockDim.x) o[i] = __fmul_rn(__fmul_rn(xr[i], scale), w[i]);
+}
+
+// RoPE on q and k of position pos = *d_pos + blockIdx.x (fwd::rope_apply,
+// rawllm_forward.hpp:767-782, with the reference's cos/sin from `cs`), then
+// K/V cache rows at pos (transformer_forward :1104-1107).
+__global__ void rope_kv_kernel(float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
+                               const float2* __restrict__ cs, const int* __restrict__ d_pos, int n_head, int n_kv,
+                               int hd, int rope_half, int q_dim, int kv_dim, float* __restrict__ Kc,
+                               float* __restrict__ Vc) {
+    const int t = blockIdx.x;
+    const int pos = *d_pos + t;
+    const int half = hd / 2;
+    const float2* csp = cs + (long long)pos * rope_half;
+    float* qt = q + (long long)t * q_dim;
+    for (int idx = threadIdx.x; idx < n_head * half; idx += blockDim.x) {
+        const int h = idx / half, i = idx % half;
+        if (i < rope_half) {
+            const float2 c = csp[i];
+            float* p = qt + h * hd + 2 * i;
+            const float x0 = p[0], x1 = p[1];
+            p[0] = __fmaf_rn(x0, c.x, -__fmul_rn(x1, c.y));
+            p[1] = __fmaf_rn(x0, c.y, __fmul_rn(x1, c.x));
+        }
+    }
+    const float* kt = k + (long long)t * kv_dim;
+    float* kc = Kc + (long long)pos * kv_dim;
+    for (int idx = threadIdx.x; idx < n_kv * half; idx += blockDim.x) {
+        const int h = idx / half, i = idx % half;
+        const float x0 = kt[h * hd + 2 * i], x1 = kt[h * hd + 2 * i + 1];
+        if (i < rope_half) {
+            const float2 c = csp[i];
+            kc[h * hd + 2 * i] = __fmaf_rn(x0, c.x, -__fmul_rn(x1, c.y));
+            kc[h * hd + 2 * i + 1] = __fmaf_rn(x0, c.y, __fmul_rn(x1, c.x));
+        } else {
+            kc[h * hd + 2 * i] = x0;
+            kc[h * hd + 2 * i + 1] = x1;
+        }
+    }
+    const float* vt = v + (long long)t * kv_dim;
+    float* vc = Vc + (long long)pos * kv_dim;
+    for (int j = threadIdx.x; j < kv_dim; j += blockDim.x) vc[j] = vt[j];
+}
+
+// Causal GQA attention of query head blockIdx.x at position *d_pos +
+// blockIdx.y over cache positions [0, pos] (transformer_forward :1115-1151):
+// scores = (q . k_s) * scale, p_s = fast_expf(score - max), out = sum_s
+// (p_s / sum p) v_s. Scores live in shared memory (L floats).
+__global__ void __launch_bounds__(kThreads) attention_kernel(const float* __restrict__ q, const float* __restrict__ Kc,
+                                                             const float* __restrict__ Vc, float* __restrict__ out,
+                                                             const int* __restrict__ d_pos, int q_dim, int kv_dim,
+                                                             int hd, int group, float scale) {
+    extern __shared__ float sc[];
+    __shared__ float scratch[32];
+    __shared__ float part[kThreads];
+    const int h = blockIdx.x, t = blockIdx.y;
+    const int L = *d_pos + t + 1;
+    const int kvh = h / group;
+    const float* qv = q + (long long)t * q_dim + (long long)h * hd;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    // scores: warp per position, lanes split head_dim
+    float qr[8];
+    const int per = hd / 32;  // head_dim is a multiple of 32, at most 256
+#pragma unroll
+    for (int j = 0; j < 8; ++j) qr[j] = j < per ? qv[lane + 32 * j] : 0.f;
+    for (int s = warp; s < L; s += nw) {
+        const float* kr = Kc + (long long)s * kv_dim + (long long)kvh * hd;
+        float acc = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            if (j < per) acc = __fmaf_rn(qr[j], kr[lane + 32 * j], acc);
+        acc = warp_sum_f(acc);
+        if (lane == 0) sc[s] = __fmul_rn(acc, scale);
+    }
+    __syncthreads();
+    float m = -INFINITY;
+    for (int s = threadIdx.x; s < L; s += blockDim.x) m = fmaxf(m, sc[s]);
+    m = block_max_f(m, scratch);
+    float sum = 0.f;
+    for (int s = threadIdx.x; s < L; s += blockDim.x) {
+        const float p = fast_expf_dev(__fsub_rn(sc[s], m));
+        sc[s] = p;
+        sum += p;
+    }
+    sum = block_sum_f(sum, scratch);
+    const float inv = __fdiv_rn(1.0f, sum);
+    // out[d] = sum_s (p_s * inv) * v_s[d]; the CTA's threads split (d, s mod parts)
+    const int parts = blockDim.x / hd;
+    const int d = threadIdx.x % hd, pidx = threadIdx.x / hd;
+    float acc = 0.f;
+    if (pidx < parts) {
+        const float* vb = Vc + (long long)kvh * hd + d;
+        for (int s = pidx; s < L; s += parts) acc = __fmaf_rn(__fmul_rn(sc[s], inv), vb[(long long)s * kv_dim], acc);
+    }
+    part[threadIdx.x] = acc;
+    __syncthreads();
+    if (threadIdx.x < hd) {
+        float r = 0.f;
+        for (int p = 0; p < parts; ++p) r += part[p * hd + threadIdx.x];
+        out[(long long)t * q_dim + (long long)h * hd + threadIdx.x] = r;
+    }
+}
+
+// act = silu(g) * u with silu(x) = x / (1 + fast_expf(-x)) (rawllm_forward.hpp:740, :1186).
+__global__ void silu_mul_kernel(float* __restrict__ g, const float* __restrict__ u, long long n) {
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        const float x = g[i];
+        g[i] = __fmul_rn(__fdiv_rn(x, __fadd_rn(1.0f, fast_expf_dev(-x))), u[i]);
+    }
+}
+
+// Greedy sampling: the first maximum of the logits (std::max_element,
+// NEON-3.cpp:471-474). Writes the token to *d_tok and to out[*d_step], then
+// advances *d_step and, when `advance`, the position *d_pos.
+__global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ logits, int n, int* d_tok,
+                                                      int* out, int* d_step, int* d_pos, int advance) {
+    __shared__ float bv[32];
+    __shared__ int bi[32];
+    float best = -INFINITY;
+    int idx = 0x7fffffff;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const float v = logits[i];
+        if (v > best) { best = v; idx = i; }
+    }
+    // reduce: larger value wins, ties go to the lower index
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+        if (ov > best || (ov == best && oi < idx)) { best = ov; idx = oi; }
+    }
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    if (l == 0) { bv[w] = best; bi[w] = idx; }
+    __syncthreads();
+    if (w == 0) {
+        best = l < (int)(blockDim.x >> 5) ? bv[l] : -INFINITY;
+        idx = l < (int)(blockDim.x >> 5) ? bi[l] : 0x7fffffff;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+            if (ov > best || (ov == best && oi < idx)) { best = ov; idx = oi; }
+        }
+        if (l == 0) {
+            if (idx == 0x7fffffff) idx = 0;  // all NaN: std::max_element keeps element 0
+            *d_tok = idx;
+            out[*d_step] = idx;
+            *d_step += 1;
+            if (advance) *d_pos += 1;
+        }
+    }
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// the model
+// ---------------------------------------------------------------------------
+
+struct neon_model {
+    neon_model_config_t cfg{};
+    int device = 0;
+    size_t q_dim = 0, kv_dim = 0, rope_half = 0;
+    neon_tensor_t embd = nullptr, output = nullptr;
+    float* output_norm = nullptr;
+    struct Layer {
+        float *attn_norm = nullptr, *ffn_norm = nullptr;
+        neon_tensor_t w[7] = {};  // q, k, v, out, gate, up, down
+    };
+    std::vector<Layer> layers;
+    float *K = nullptr, *V = nullptr;   // [layer][ctx][kv_dim]
+    float2* rope_cs = nullptr;          // [ctx][rope_half]
+    float *h = nullptr, *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr;
+    float *g = nullptr, *u = nullptr, *logits = nullptr;
+    int *d_tokens = nullptr, *d_tok = nullptr, *d_pos = nullptr, *d_step = nullptr, *d_out = nullptr;
+    unsigned* d_err = nullptr;
+    size_t out_cap = 0;
+    size_t length = 0;
+    cudaStream_t stream = nullptr;
+    cudaGraphExec_t step_graph = nullptr;
+    cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    float decode_ms = 0.f;
+    std::vector<void*> allocs;
+};
+
+namespace {
+
+int dev_alloc(neon_model* m, void** p, size_t bytes) {
+    cudaError_t e = cudaMalloc(p, bytes ? bytes : 16);
+    if (e != cudaSuccess) return error(NEON_ERR_NOMEM, std::string("cudaMalloc in the decode engine: ") + cudaGetErrorString(e));
+    m->allocs.push_back(*p);
+    return NEON_OK;
+}
+
+struct ModelDevice {  // makes the model's device current for a scope
+    int prev = -1;
+    explicit ModelDevice(int d) {
+        cudaGetDevice(&prev);
+        if (prev != d) cudaSetDevice(d);
+    }
+    ~ModelDevice() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+int check_launch(const char* what) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_error(e, what);
+    return neon_internal::launched(1);
+}
+
+int rmsnorm(neon_model* m, const float* x, const float* w, float* out, int rows) {
+    rmsnorm_kernel<<<rows, kThreads, 0, m->stream>>>(x, w, out, (int)m->cfg.n_embd, m->cfg.norm_eps);
+    return check_launch("rmsnorm_kernel");
+}
+
+int proj(neon_model* m, std::initializer_list<neon_proj_target_t> t, const float* x, size_t x_stride, size_t seq,
+         int accumulate) {
+    std::vector<neon_proj_target_t> v(t);
+    return neon_internal::matvec(v.data(), v.size(), x, x_stride, seq, m->stream, accumulate);
+}
+
+// All layers for `seq` positions starting at *d_pos, tokens in `toks` (device).
+int run_layers(neon_model* m, const int* toks, int seq) {
+    const auto& c = m->cfg;
+    const neon_tensor_t E = m->embd;
+    const int nb = (int)(c.n_embd / 32);
+    embed_kernel<<<dim3((nb + 127) / 128, seq), 128, 0, m->stream>>>(E->qs, E->d, E->type, nb, toks, (int)c.n_vocab,
+                                                                     m->h, m->d_err);
+    int rc = check_launch("embed_kernel");
+    const size_t n_embd = c.n_embd, q_dim = m->q_dim, kv_dim = m->kv_dim, n_ff = c.n_ff;
+    const float scale = 1.0f / std::sqrt((float)c.head_dim);
+    const int group = (int)(c.n_head / c.n_kv_head);
+    const size_t attn_smem = sizeof(float) * c.ctx_len;
+    for (uint32_t li = 0; li < c.n_layer && !rc; ++li) {
+        auto& L = m->layers[li];
+        float* Kl = m->K + (size_t)li * c.ctx_len * kv_dim;
+        float* Vl = m->V + (size_t)li * c.ctx_len * kv_dim;
+        rc = rmsnorm(m, m->h, L.attn_norm, m->xn, seq);
+        if (!rc) rc = proj(m, {{L.w[0], m->q, q_dim}, {L.w[1], m->k, kv_dim}, {L.w[2], m->v, kv_dim}}, m->xn, n_embd, seq, 0);
+        if (!rc) {
+            rope_kv_kernel<<<seq, kThreads, 0, m->stream>>>(m->q, m->k, m->v, m->rope_cs, m->d_pos, (int)c.n_head,
+                                                            (int)c.n_kv_head, (int)c.head_dim, (int)m->rope_half,
+                                                            (int)q_dim, (int)kv_dim, Kl, Vl);
+            rc = check_launch("rope_kv_kernel");
+        }
+        if (!rc) {
+            attention_kernel<<<dim3(c.n_head, seq), kThreads, attn_smem, m->stream>>>(
+                m->q, Kl, Vl, m->att, m->d_pos, (int)q_dim, (int)kv_dim, (int)c.head_dim, group, scale);
+            rc = check_launch("attention_kernel");
+        }
+        if (!rc) rc = proj(m, {{L.w[3], m->h, n_embd}}, m->att, q_dim, seq, 1);
+        if (!rc) rc = rmsnorm(m, m->h, L.ffn_norm, m->xn, seq);
+        if (!rc) rc = proj(m, {{L.w[4], m->g, n_ff}, {L.w[5], m->u, n_ff}}, m->xn, n_embd, seq, 0);
+        if (!rc) {
+            const long long n = (long long)seq * n_ff;
+            silu_mul_kernel<<<(int)std::min<long long>((n + 255) / 256, 4096), 256, 0, m->stream>>>(m->g, m->u, n);
+            rc = check_launch("silu_mul_kernel");
+        }
+        if (!rc) rc = proj(m, {{L.w[6], m->h, n_embd}}, m->g, n_ff, seq, 1);
+    }
+    return rc;
+}
+
+// logits of row `row` of h
+int run_head(neon_model* m, int row) {
+    int rc = rmsnorm(m, m->h + (size_t)row * m->cfg.n_embd, m->output_norm, m->xn, 1);
+    if (rc) return rc;
+    neon_tensor_t W = m->output ? m->output : m->embd;
+    return proj(m, {{W, m->logits, (size_t)m->cfg.n_vocab}}, m->xn, m->cfg.n_embd, 1, 0);
+}
+
+int check_ready(neon_model* m) {
+    if (!m->embd || !m->output_norm) return error(NEON_ERR_INVALID, "forward(): token_embd.weight / output_norm.weight not set");
+    for (uint32_t i = 0; i < m->cfg.n_layer; ++i) {
+        auto& L = m->layers[i];
+        if (!L.attn_norm || !L.ffn_norm)
+            return error(NEON_ERR_INVALID, "forward(): layer " + std::to_string(i) + " is missing a norm weight");
+        for (auto* w : L.w)
+            if (!w) return error(NEON_ERR_INVALID, "forward(): layer " + std::to_string(i) + " is missing a projection");
+    }
+    return NEON_OK;
+}
+
+int sync_and_check(neon_model* m) {
+    DEC_TRY(cudaStreamSynchronize(m->stream));
+    unsigned e = 0;
+    DEC_TRY(cudaMemcpy(&e, m->d_err, sizeof(e), cudaMemcpyDeviceToHost));
+    if (e & 2u) {
+        DEC_TRY(cudaMemset(m->d_err, 0, sizeof(unsigned)));
+        return error(NEON_ERR_INVALID, "forward(): token id out of vocab range");
+    }
+    return neon_internal::check_device_error(m->device);
+}
+
+// Tokens [0, n) of `tokens_dev` at positions length..; logits of the last.
+int forward_device(neon_model* m, const int32_t* tokens_host, size_t n) {
+    for (size_t off = 0; off < n; off += kMaxChunk) {
+        const int seq = (int)std::min<size_t>(kMaxChunk, n - off);
+        const int pos = (int)(m->length + off);
+        DEC_TRY(cudaMemcpyAsync(m->d_tokens, tokens_host + off, seq * sizeof(int32_t), cudaMemcpyHostToDevice, m->stream));
+        DEC_TRY(cudaMemcpyAsync(m->d_pos, &pos, sizeof(int), cudaMemcpyHostToDevice, m->stream));
+        int rc = run_layers(m, m->d_tokens, seq);
+        if (rc) return rc;
+        if (off + seq == n) {
+            rc = run_head(m, seq - 1);
+            if (rc) return rc;
+        }
+        DEC_TRY(cudaStreamSynchronize(m->stream));  // pos / tokens are reused by the next chunk
+    }
+    return NEON_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int neon_cuda_model_create(const neon_model_config_t* cfg, neon_model_t* out) {
+    if (!cfg || !out) return error(NEON_ERR_INVALID, "null argument");
+    *out = nullptr;
+    const auto& c = *cfg;
+    if (c.n_embd == 0 || c.n_layer == 0 || c.n_head == 0 || c.n_kv_head == 0 || c.head_dim == 0 || c.n_ff == 0 ||
+        c.n_vocab == 0 || c.ctx_len == 0)
+        return error(NEON_ERR_INVALID, "NANITY: one or more required hyperparameters is zero.");
+    if (c.n_head % c.n_kv_head != 0)
+        return error(NEON_ERR_INVALID, "NANITY: attention.head_count must be an exact multiple of attention.head_count_kv");
+    if (c.head_dim % 32 != 0 || c.head_dim > 256 || c.n_embd % 32 != 0 || c.n_ff % 32 != 0)
+        return error(NEON_ERR_UNSUPPORTED, "head_dim must be a multiple of 32 up to 256; n_embd and n_ff multiples of 32");
+    if (c.ctx_len > (uint32_t)kMaxCtx) return error(NEON_ERR_UNSUPPORTED, "ctx_len above 16384");
+    if (c.rope_dim_count > c.head_dim) return error(NEON_ERR_INVALID, "rope dimension count above head_dim");
+    auto* m = new neon_model();
+    m->cfg = c;
+    cudaGetDevice(&m->device);
+    m->q_dim = (size_t)c.n_head * c.head_dim;
+    m->kv_dim = (size_t)c.n_kv_head * c.head_dim;
+    m->rope_half = c.rope_dim_count ? c.rope_dim_count / 2 : c.head_dim / 2;
+    m->layers.resize(c.n_layer);
+    int rc = NEON_OK;
+    const size_t S = kMaxChunk;
+    auto A = [&](void** p, size_t bytes) {
+        if (!rc) rc = dev_alloc(m, p, bytes);
+    };
+    const size_t kv_bytes = sizeof(float) * (size_t)c.n_layer * c.ctx_len * m->kv_dim;
+    A((void**)&m->K, kv_bytes);
+    A((void**)&m->V, kv_bytes);
+    A((void**)&m->rope_cs, sizeof(float2) * (size_t)c.ctx_len * std::max<size_t>(1, m->rope_half));
+    A((void**)&m->h, sizeof(float) * S * c.n_embd);
+    A((void**)&m->xn, sizeof(float) * S * c.n_embd);
+    A((void**)&m->q, sizeof(float) * S * m->q_dim);
+    A((void**)&m->k, sizeof(float) * S * m->kv_dim);
+    A((void**)&m->v, sizeof(float) * S * m->kv_dim);
+    A((void**)&m->att, sizeof(float) * S * m->q_dim);
+    A((void**)&m->g, sizeof(float) * S * c.n_ff);
+    A((void**)&m->u, sizeof(float) * S * c.n_ff);
+    A((void**)&m->logits, sizeof(float) * c.n_vocab);
+    A((void**)&m->d_tokens, sizeof(int) * S);
+    A((void**)&m->d_tok, sizeof(int));
+    A((void**)&m->d_pos, sizeof(int));
+    A((void**)&m->d_step, sizeof(int));
+    A((void**)&m->d_err, sizeof(unsigned));
+    if (!rc) rc = cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) == cudaSuccess ? NEON_OK : error(NEON_ERR_CUDA, "cudaStreamCreate");
+    if (!rc) rc = (cudaEventCreate(&m->ev0) == cudaSuccess && cudaEventCreate(&m->ev1) == cudaSuccess) ? NEON_OK : error(NEON_ERR_CUDA, "cudaEventCreate");
+    if (!rc) {
+        // RoPE cos/sin of every position with the host libm, as rope_apply computes
+        // them (rawllm_forward.hpp:755-782): theta = ((float)pos / scale) * freq.
+        std::vector<float> freqs(c.head_dim / 2);
+        for (size_t i = 0; i < c.head_dim / 2; ++i) freqs[i] = std::pow(c.rope_base, -2.0f * (float)i / (float)c.head_dim);
+        std::vector<float2> tab((size_t)c.ctx_len * std::max<size_t>(1, m->rope_half));
+        for (size_t p = 0; p < c.ctx_len; ++p) {
+            const float fpos = (float)p / c.rope_scale;
+            for (size_t i = 0; i < m->rope_half; ++i) {
+                const float theta = fpos * freqs[i];
+                tab[p * m->rope_half + i] = make_float2(std::cos(theta), std::sin(theta));
+            }
+        }
+        if (cudaMemcpy(m->rope_cs, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice) != cudaSuccess ||
+            cudaMemset(m->d_err, 0, sizeof(unsigned)) != cudaSuccess || cudaMemset(m->K, 0, kv_bytes) != cudaSuccess ||
+            cudaMemset(m->V, 0, kv_bytes) != cudaSuccess)
+            rc = error(NEON_ERR_CUDA, "model initialisation copies failed");
+    }
+    if (!rc && c.ctx_len * sizeof(float) > 48 * 1024) {
+        if (cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(c.ctx_len * sizeof(float))) != cudaSuccess)
+            rc = error(NEON_ERR_CUDA, "cudaFuncSetAttribute(attention_kernel)");
+    }
+    if (rc) {
+        neon_cuda_model_free(m);
+        return rc;
+    }
+    *out = m;
+    return NEON_OK;
+}
+
+int neon_cuda_model_set_tensor(neon_model_t m, int role, int layer, const uint8_t* host_bytes, size_t nbytes,
+                               int ggml_type, size_t ne0, size_t ne1) {
+    if (!m || !host_bytes) return error(NEON_ERR_INVALID, "null argument");
+    ModelDevice md(m->device);
+    const auto& c = m->cfg;
+    if (role == NEON_ROLE_OUTPUT_NORM || role == NEON_ROLE_ATTN_NORM || role == NEON_ROLE_FFN_NORM) {
+        if (ggml_type != NEON_GGML_F32 || ne0 != c.n_embd || ne1 > 1 || nbytes != ne0 * 4)
+            return error(NEON_ERR_INVALID, "NANITY: norm weight must be F32 [n_embd]");
+        float* p = nullptr;
+        int rc = dev_alloc(m, (void**)&p, nbytes);
+        if (rc) return rc;
+        DEC_TRY(cudaMemcpy(p, host_bytes, nbytes, cudaMemcpyHostToDevice));
+        if (role == NEON_ROLE_OUTPUT_NORM) m->output_norm = p;
+        else {
+            if (layer < 0 || (uint32_t)layer >= c.n_layer) return error(NEON_ERR_INVALID, "layer index out of range");
+            (role == NEON_ROLE_ATTN_NORM ? m->layers[layer].attn_norm : m->layers[layer].ffn_norm) = p;
+        }
+        return NEON_OK;
+    }
+    // projections: expected GGUF ne = [cols, rows]
+    size_t want0 = 0, want1 = 0;
+    switch (role) {
+        case NEON_ROLE_TOKEN_EMBD: case NEON_ROLE_OUTPUT: want0 = c.n_embd; want1 = c.n_vocab; break;
+        case NEON_ROLE_ATTN_Q: want0 = c.n_embd; want1 = m->q_dim; break;
+        case NEON_ROLE_ATTN_K: case NEON_ROLE_ATTN_V: want0 = c.n_embd; want1 = m->kv_dim; break;
+        case NEON_ROLE_ATTN_OUT: want0 = m->q_dim; want1 = c.n_embd; break;
+        case NEON_ROLE_FFN_GATE: case NEON_ROLE_FFN_UP: want0 = c.n_embd; want1 = c.n_ff; break;
+        case NEON_ROLE_FFN_DOWN: want0 = c.n_ff; want1 = c.n_embd; break;
+        default: return error(NEON_ERR_INVALID, "unknown tensor role " + std::to_string(role));
+    }
+    if (ne0 != want0 || ne1 != want1)
+        return error(NEON_ERR_INVALID, "NANITY: tensor of role " + std::to_string(role) + " has shape [" + std::to_string(ne0) +
+                                           ", " + std::to_string(ne1) + "], expected [" + std::to_string(want0) + ", " +
+                                           std::to_string(want1) + "].");
+    neon_tensor_t t = nullptr;
+    int rc = neon_cuda_upload(host_bytes, ggml_type, ne1, ne0, NEON_SHARD_NONE, 0, 1, &t);
+    if (rc) return rc;
+    neon_tensor_t* slot = nullptr;
+    if (role == NEON_ROLE_TOKEN_EMBD) slot = &m->embd;
+    else if (role == NEON_ROLE_OUTPUT) slot = &m->output;
+    else {
+        if (layer < 0 || (uint32_t)layer >= c.n_layer) {
+            neon_cuda_free(t);
+            return error(NEON_ERR_INVALID, "layer index out of range");
+        }
+        // projection slots: q, k, v, out (roles 4-7), gate, up, down (roles 9-11)
+        const int idx = role <= NEON_ROLE_ATTN_OUT ? role - NEON_ROLE_ATTN_Q : role - NEON_ROLE_FFN_GATE + 4;
+        slot = &m->layers[layer].w[idx];
+    }
+    if (*slot) neon_cuda_free(*slot);
+    *slot = t;
+    return NEON_OK;
+}
+
+int neon_cuda_model_forward(neon_model_t m, const int32_t* tokens, size_t n, float* logits_host) {
+    if (!m || (!tokens && n)) return error(NEON_ERR_INVALID, "null argument");
+    if (n == 0) return error(NEON_ERR_INVALID, "forward(): empty token batch");
+    if (m->length + n > m->cfg.ctx_len)
+        return error(NEON_ERR_INVALID, "forward(): KV cache exhausted (ctx_len=" + std::to_string(m->cfg.ctx_len) + " exceeded)");
+    for (size_t i = 0; i < n; ++i)
+        if (tokens[i] < 0 || (uint32_t)tokens[i] >= m->cfg.n_vocab)
+            return error(NEON_ERR_INVALID, "forward(): token id " + std::to_string(tokens[i]) + " out of vocab range");
+    int rc = check_ready(m);
+    if (rc) return rc;
+    ModelDevice md(m->device);
+    rc = forward_device(m, tokens, n);
+    if (!rc) rc = sync_and_check(m);
+    if (rc) return rc;
+    m->length += n;
+    if (logits_host) DEC_TRY(cudaMemcpy(logits_host, m->logits, sizeof(float) * m->cfg.n_vocab, cudaMemcpyDeviceToHost));
+    return NEON_OK;
+}
+
+int neon_cuda_model_generate(neon_model_t m, const int32_t* prompt, size_t n_prompt, size_t max_new, int32_t eos_id,
+                             int32_t* out_tokens, size_t* n_out) {
+    if (!m || !prompt || !out_tokens || !n_out) return error(NEON_ERR_INVALID, "null argument");
+    *n_out = 0;
+    if (n_prompt == 0) return error(NEON_ERR_INVALID, "forward(): empty token batch");
+    if (m->length + n_prompt + max_new > m->cfg.ctx_len)
+        return error(NEON_ERR_INVALID, "forward(): KV cache exhausted (ctx_len=" + std::to_string(m->cfg.ctx_len) + " exceeded)");
+    int rc = neon_cuda_model_forward(m, prompt, n_prompt, nullptr);
+    if (rc) return rc;
+    ModelDevice md(m->device);
+    if (m->out_cap < max_new + 1) {
+        if (m->d_out) cudaFree(m->d_out);
+        m->d_out = nullptr;
+        DEC_TRY(cudaMalloc(&m->d_out, sizeof(int) * (max_new + 1)));
+        m->out_cap = max_new + 1;
+    }
+    const int zero = 0, pos = (int)m->length;
+    DEC_TRY(cudaMemcpyAsync(m->d_step, &zero, sizeof(int), cudaMemcpyHostToDevice, m->stream));
+    DEC_TRY(cudaMemcpyAsync(m->d_pos, &pos, sizeof(int), cudaMemcpyHostToDevice, m->stream));
+    // first token: from the prompt's logits
+    argmax_kernel<<<1, 1024, 0, m->stream>>>(m->logits, (int)m->cfg.n_vocab, m->d_tok, m->d_out, m->d_step, m->d_pos, 0);
+    rc = check_launch("argmax_kernel");
+    if (rc) return rc;
+    if (max_new > 0) {
+        // one decode step as a CUDA graph: embed(d_tok) .. logits .. argmax -> d_tok, pos += 1
+        if (m->step_graph) {
+            cudaGraphExecDestroy(m->step_graph);
+            m->step_graph = nullptr;
+        }
+        cudaGraph_t g = nullptr;
+        DEC_TRY(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
+        rc = run_layers(m, m->d_tok, 1);
+        if (!rc) rc = run_head(m, 0);
+        if (!rc) {
+            argmax_kernel<<<1, 1024, 0, m->stream>>>(m->logits, (int)m->cfg.n_vocab, m->d_tok, m->d_out, m->d_step, m->d_pos, 1);
+            rc = check_launch("argmax_kernel");
+        }
+        cudaError_t ce = cudaStreamEndCapture(m->stream, &g);
+        if (rc) {
+            if (g) cudaGraphDestroy(g);
+            return rc;
+        }
+        if (ce != cudaSuccess) return cuda_error(ce, "cudaStreamEndCapture");
+        ce = cudaGraphInstantiate(&m->step_graph, g, 0);
+        cudaGraphDestroy(g);
+        if (ce != cudaSuccess) return cuda_error(ce, "cudaGraphInstantiate");
+        DEC_TRY(cudaEventRecord(m->ev0, m->stream));
+        for (size_t s = 0; s < max_new; ++s) DEC_TRY(cudaGraphLaunch(m->step_graph, m->stream));
+        DEC_TRY(cudaEventRecord(m->ev1, m->stream));
+    }
+    rc = sync_and_check(m);
+    if (rc) return rc;
+    if (max_new > 0) cudaEventElapsedTime(&m->decode_ms, m->ev0, m->ev1);
+    std::vector<int32_t> toks(max_new + 1);
+    DEC_TRY(cudaMemcpy(toks.data(), m->d_out, sizeof(int) * (max_new + 1), cudaMemcpyDeviceToHost));
+    size_t n = 0;
+    while (n < max_new && toks[n] != eos_id) {
+        out_tokens[n] = toks[n];
+        ++n;
+    }
+    *n_out = n;
+    m->length += n;  // one forward per emitted token, as run_generation does
+    return NEON_OK;
+}
+
+int neon_cuda_model_length(neon_model_t m, size_t* length) {
+    if (!m || !length) return error(NEON_ERR_INVALID, "null argument");
+    *length = m->length;
+    return NEON_OK;
+}
+
+int neon_cuda_model_set_length(neon_model_t m, size_t length) {
+    if (!m) return error(NEON_ERR_INVALID, "null model");
+    if (length > m->cfg.ctx_len) return error(NEON_ERR_INVALID, "length above the KV-cache capacity");
+    m->length = length;
+    return NEON_OK;
+}
+
+int neon_cuda_model_read_kv(neon_model_t m, int layer, size_t n, float* k_host, float* v_host) {
+    if (!m || !k_host || !v_host) return error(NEON_ERR_INVALID, "null argument");
+    if (layer < 0 || (uint32_t)layer >= m->cfg.n_layer || n > m->cfg.ctx_len) return error(NEON_ERR_INVALID, "layer or n out of range");
+    ModelDevice md(m->device);
+    const size_t off = (size_t)layer * m->cfg.ctx_len * m->kv_dim;
+    DEC_TRY(cudaMemcpy(k_host, m->K + off, sizeof(float) * n * m->kv_dim, cudaMemcpyDeviceToHost));
+    DEC_TRY(cudaMemcpy(v_host, m->V + off, sizeof(float) * n * m->kv_dim, cudaMemcpyDeviceToHost));
+    return NEON_OK;
+}
+
+int neon_cuda_model_decode_ms(neon_model_t m, float* ms) {
+    if (!m || !ms) return error(NEON_ERR_INVALID, "null argument");
+    *ms = m->decode_ms;
+    return NEON_OK;
+}
+
+int neon_cuda_model_free(neon_model_t m) {
+    if (!m) return NEON_OK;
+    ModelDevice md(m->device);
+    if (m->stream) cudaStreamSynchronize(m->stream);
+    if (m->step_graph) cudaGraphExecDestroy(m->step_graph);
+    neon_cuda_free(m->embd);
+    neon_cuda_free(m->output);
+    for (auto& L : m->layers)
+        for (auto* w : L.w) neon_cuda_free(w);
+    for (void* p : m->allocs) cudaFree(p);
+    if (m->d_out) cudaFree(m->d_out);
+    if (m->ev0) cudaEventDestroy(m->ev0);
+    if (m->ev1) cudaEventDestroy(m->ev1);
+    if (m->stream) cudaStreamDestroy(m->stream);
+    delete m;
+    return NEON_OK;
+}
+
+}  // extern "C"

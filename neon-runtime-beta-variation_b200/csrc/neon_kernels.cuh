@@ -55,6 +55,7 @@ struct MatvecArgs {
     int n_tiles;
     int nb;
     int seq;
+    int accumulate;      // 1: y += result (the residual add of the decode loop)
 };
 
 // ---------------------------------------------------------------------------
@@ -307,6 +308,7 @@ struct StreamArgs {
     int stages;             // ring depth
     int stage_bytes;        // bytes per stage
     int x_vec;              // x is 16-byte aligned: 128-bit loads
+    int accumulate;         // 1: y += result (the residual add of the decode loop)
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -662,7 +664,7 @@ __global__ void __launch_bounds__(kStreamThreads) matvec_stream_kernel(const __g
 #pragma unroll
                     for (int rr = 0; rr < R; ++rr) {
                         const int row = row0 + g * R + rr;
-                        if (row < sp.rows) sp.y[row] = acc[rr];
+                        if (row < sp.rows) sp.y[row] = a.accumulate ? sp.y[row] + acc[rr] : acc[rr];
                     }
                 }
             } else {
@@ -676,7 +678,7 @@ __global__ void __launch_bounds__(kStreamThreads) matvec_stream_kernel(const __g
 #pragma unroll
                     for (int w = 0; w < WPG; ++w) v += red[threadIdx.x * WPG + w];
                     const int row = row0 + threadIdx.x;
-                    if (row < sp.rows) sp.y[row] = v;
+                    if (row < sp.rows) sp.y[row] = a.accumulate ? sp.y[row] + v : v;
                 }
             }
 #pragma unroll
@@ -770,7 +772,10 @@ __global__ void __launch_bounds__(kThreads) matvec_multipos_kernel(const __grid_
                 const float v = warp_sum(acc[r][t]);
                 if (lane == r) mine = v;
             }
-            if (lane < R && row0 + lane < sp.rows) sp.y[(long long)tt * sp.y_stride + row0 + lane] = mine;
+            if (lane < R && row0 + lane < sp.rows) {
+                float* yp = sp.y + (long long)tt * sp.y_stride + row0 + lane;
+                *yp = a.accumulate ? *yp + mine : mine;
+            }
         }
     }
 }

@@ -60,6 +60,15 @@ C_ENTRY_POINTS = (
     "neon_cuda_sync",
     "neon_cuda_launch_count",
     "neon_cuda_matvec_q4_0_noalloc",
+    "neon_cuda_model_create",
+    "neon_cuda_model_set_tensor",
+    "neon_cuda_model_forward",
+    "neon_cuda_model_generate",
+    "neon_cuda_model_length",
+    "neon_cuda_model_set_length",
+    "neon_cuda_model_read_kv",
+    "neon_cuda_model_decode_ms",
+    "neon_cuda_model_free",
     "neon_cuda_set_pdl",
 )
 
@@ -69,6 +78,13 @@ _vp = C.c_void_p
 
 class _Target(C.Structure):
     _fields_ = [("W", _vp), ("Y", _vp), ("y_stride", _sz)]
+
+
+class _ModelConfig(C.Structure):
+    _fields_ = [(f, C.c_uint32) for f in ("n_vocab", "n_embd", "n_layer", "n_head", "n_kv_head", "head_dim",
+                                          "n_ff", "ctx_len")] + [
+        ("rope_base", C.c_float), ("rope_scale", C.c_float), ("rope_dim_count", C.c_uint32),
+        ("norm_eps", C.c_float)]
 
 
 class NeonError(RuntimeError):
@@ -111,6 +127,15 @@ def load(path: str | None = None) -> C.CDLL:
         L.neon_cuda_launch_count.restype = C.c_uint64
         L.neon_cuda_set_pdl.argtypes = [C.c_int]
         L.neon_cuda_matvec_q4_0_noalloc.argtypes = [_vp, _vp, _sz, _vp, _sz, _sz, _vp]
+        L.neon_cuda_model_create.argtypes = [C.POINTER(_ModelConfig), C.POINTER(_vp)]
+        L.neon_cuda_model_set_tensor.argtypes = [_vp, C.c_int, C.c_int, _vp, _sz, C.c_int, _sz, _sz]
+        L.neon_cuda_model_forward.argtypes = [_vp, _vp, _sz, _vp]
+        L.neon_cuda_model_generate.argtypes = [_vp, _vp, _sz, _sz, C.c_int32, _vp, C.POINTER(_sz)]
+        L.neon_cuda_model_length.argtypes = [_vp, C.POINTER(_sz)]
+        L.neon_cuda_model_set_length.argtypes = [_vp, _sz]
+        L.neon_cuda_model_read_kv.argtypes = [_vp, C.c_int, _sz, _vp, _vp]
+        L.neon_cuda_model_decode_ms.argtypes = [_vp, C.POINTER(C.c_float)]
+        L.neon_cuda_model_free.argtypes = [_vp]
         _lib = L
         return L
 
@@ -292,3 +317,75 @@ def proj_all_positions_multi(targets, X: np.ndarray, x_stride: int, seq: int, po
         arr[i].y_stride = t.y_stride
     X = np.ascontiguousarray(X, dtype=np.float32)
     _check(load().neon_cuda_proj_all_positions_multi(arr, n, X.ctypes.data, x_stride, seq))
+
+
+# ---------------------------------------------------------------------------
+# the decode step (transformer_forward / run_generation on the device)
+# ---------------------------------------------------------------------------
+
+class Model:
+    """A NANITY decoder on the current device (neon_cuda_model_*).
+
+    ``cfg`` has the fields of engine::Config the forward pass reads (n_vocab,
+    n_embd, n_layer, n_head, n_kv_head, head_dim, n_ff, ctx_len, rope_base,
+    rope_scale, rope_dim_count, norm_eps); ``tensors`` yields (role, layer,
+    GGUF bytes, ggml type, ne0, ne1)."""
+
+    def __init__(self, cfg, tensors=()):
+        L = load()
+        self.cfg = cfg
+        c = _ModelConfig(*[getattr(cfg, f) for f in ("n_vocab", "n_embd", "n_layer", "n_head", "n_kv_head",
+                                                     "head_dim", "n_ff", "ctx_len")],
+                         cfg.rope_base, cfg.rope_scale, cfg.rope_dim_count, cfg.norm_eps)
+        h = _vp()
+        _check(L.neon_cuda_model_create(C.byref(c), C.byref(h)))
+        self.handle = h.value
+        self._fin = weakref.finalize(self, L.neon_cuda_model_free, self.handle)
+        for t in tensors:
+            self.set_tensor(*t)
+
+    def set_tensor(self, role, layer, raw, ggml_type, ne0, ne1):
+        raw = np.ascontiguousarray(raw)
+        _check(load().neon_cuda_model_set_tensor(self.handle, int(role), int(layer), raw.ctypes.data, raw.nbytes,
+                                                 int(ggml_type), int(ne0), int(ne1)))
+
+    def forward(self, tokens) -> np.ndarray:
+        """fwd::transformer_forward: append tokens, return the last logits."""
+        t = np.ascontiguousarray(tokens, dtype=np.int32).reshape(-1)
+        out = np.zeros(self.cfg.n_vocab, np.float32)
+        _check(load().neon_cuda_model_forward(self.handle, t.ctypes.data, t.size, out.ctypes.data))
+        return out
+
+    def generate(self, prompt, max_new: int, eos_id: int = -1) -> np.ndarray:
+        """Greedy run_generation on the device; returns the emitted tokens."""
+        p = np.ascontiguousarray(prompt, dtype=np.int32).reshape(-1)
+        out = np.zeros(max(1, max_new), np.int32)
+        n = _sz()
+        _check(load().neon_cuda_model_generate(self.handle, p.ctypes.data, p.size, max_new, int(eos_id),
+                                               out.ctypes.data, C.byref(n)))
+        return out[:n.value].copy()
+
+    @property
+    def length(self) -> int:
+        n = _sz()
+        _check(load().neon_cuda_model_length(self.handle, C.byref(n)))
+        return n.value
+
+    def set_length(self, n: int) -> None:
+        _check(load().neon_cuda_model_set_length(self.handle, n))
+
+    def read_kv(self, layer: int, n: int):
+        kv = self.cfg.n_kv_head * self.cfg.head_dim
+        k = np.zeros((n, kv), np.float32)
+        v = np.zeros((n, kv), np.float32)
+        _check(load().neon_cuda_model_read_kv(self.handle, layer, n, k.ctypes.data, v.ctypes.data))
+        return k, v
+
+    @property
+    def decode_ms(self) -> float:
+        ms = C.c_float()
+        _check(load().neon_cuda_model_decode_ms(self.handle, C.byref(ms)))
+        return ms.value
+
+    def free(self) -> None:
+        self._fin()

@@ -114,10 +114,16 @@ int32_t oracle_block_isum(const uint8_t* qs, const int8_t* xq) {
 /* One GGUF Q4_0 row (18-byte blocks: fp16 d, 16 nibble bytes) against one Q8_0
  * activation row. Restates dot_q4_0_q8_0, rawllm_forward.hpp:419-434, with the
  * FMA contraction of the optimised reference build. */
+/* Test switch: when nonzero, dot_q4_0_q8_0 sums its blocks in reverse order.
+ * A legitimate fp32 reordering, used only by tests/test_oracle_decode.py to
+ * measure how far a mere summation-order change moves whole-model logits. */
+int oracle_reverse_block_order = 0;
+
 float oracle_dot_q4_0_q8_0(const uint8_t* w, const float* x_d, const int8_t* x_q, size_t cols) {
     size_t nb = cols / 32;
     float total = 0.f;
-    for (size_t b = 0; b < nb; ++b) {
+    for (size_t bb = 0; bb < nb; ++bb) {
+        size_t b = oracle_reverse_block_order ? nb - 1 - bb : bb;
         const uint8_t* blk = w + b * 18;
         float wd = rd_fp16(blk);
         int32_t isum = oracle_block_isum(blk + 2, x_q + b * 32);

@@ -40,3 +40,19 @@ def max_rel_err(y, ref):
         return 0.0
     floor = 0.01 * np.sqrt(np.mean(ref * ref)) + 1e-30
     return float(np.max(np.abs(y - ref) / np.maximum(np.abs(ref), floor)))
+
+
+# Whole-model bar. A decode step quantises activations to Q8_0 (rounding x*id to
+# int8), which is discontinuous: an fp32 summation-order change of ~1e-7 flips an
+# int8 wherever x*id sits within ~1e-7 of a .5 tie, moving that projection by
+# ~1e-3 and the logits of that position by up to ~1 in max_rel_err. The oracle
+# shows this with the reference's own arithmetic (tests/test_oracle_decode.py,
+# reversed block order). Full-model parity is therefore identical greedy tokens
+# plus logits within MODEL_L2_RTOL in relative L2 norm at every step.
+MODEL_L2_RTOL = 5e-2
+
+
+def rel_l2(y, ref):
+    y = np.asarray(y, np.float64).reshape(-1)
+    ref = np.asarray(ref, np.float64).reshape(-1)
+    return float(np.linalg.norm(y - ref) / max(np.linalg.norm(ref), 1e-30))

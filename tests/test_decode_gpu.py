@@ -1,0 +1,107 @@
+"""The device decode step (neon_cuda_model_*) against the reference's
+transformer_forward: the golden generation of a small model, the oracle
+restatement, and -- at full depth on the Qwen3-0.6B-shaped decoder -- the
+reference's own build. The bar: identical greedy tokens; logits within
+MODEL_L2_RTOL in relative L2 at every step (conftest.py explains why a
+multi-layer Q8_0-quantised forward is not held to the per-element matvec bar);
+the small model's first steps and K/V cache also within the per-element bar."""
+import numpy as np
+import pytest
+
+import neon_cuda as N
+import oracle as O
+import synth as S
+from conftest import MATVEC_RTOL, MODEL_L2_RTOL, load_golden, max_rel_err, rel_l2
+
+pytestmark = pytest.mark.gpu
+torch = pytest.importorskip("torch")
+
+TINY = S.ModelConfig(1000, 256, 2, 4, 2, 64, 512, ctx_len=64, rope_base=1e4, name="tiny")
+
+
+@pytest.fixture(scope="module", autouse=True)
+def device():
+    assert torch.cuda.is_available()
+    N.init(0)
+
+
+def test_tiny_golden_generation():
+    g = load_golden("decode_tiny.npz")
+    m = N.Model(TINY, S.model_tensors(TINY, seed=3))
+    toks = m.generate(g["prompt"], 16)
+    assert np.array_equal(toks, g["tokens"])
+    assert m.length == len(g["prompt"]) + 16
+
+
+def test_tiny_forward_logits_and_kv():
+    g = load_golden("decode_tiny.npz")
+    m = N.Model(TINY, S.model_tensors(TINY, seed=3))
+    logits = m.forward(g["prompt"])
+    assert max_rel_err(logits, g["logits"][0]) <= MATVEC_RTOL
+    for i, t in enumerate(g["tokens"][:6]):
+        logits = m.forward([t])
+        assert max_rel_err(logits, g["logits"][i + 1]) <= MATVEC_RTOL, f"step {i}"
+    o = O.Model(TINY, list(S.model_tensors(TINY, seed=3)), "port")
+    o.forward(g["prompt"])
+    for t in g["tokens"][:6]:
+        o.forward([t])
+    n = len(g["prompt"]) + 6
+    for layer in range(TINY.n_layer):
+        k1, v1 = m.read_kv(layer, n)
+        k2, v2 = o.kv(layer, n)
+        assert max_rel_err(k1, k2) <= MATVEC_RTOL and max_rel_err(v1, v2) <= MATVEC_RTOL
+
+
+def test_rewind_and_eos():
+    g = load_golden("decode_tiny.npz")
+    m = N.Model(TINY, S.model_tensors(TINY, seed=3))
+    m.forward(g["prompt"])
+    m.set_length(3)  # keep the first 3 prompt positions, re-feed the rest
+    logits = m.forward(g["prompt"][3:])
+    assert max_rel_err(logits, g["logits"][0]) <= MATVEC_RTOL
+    # stopping before the eos token, as run_generation does
+    m2 = N.Model(TINY, S.model_tensors(TINY, seed=3))
+    eos = int(g["tokens"][5])
+    toks = m2.generate(g["prompt"], 16, eos_id=eos)
+    first = list(g["tokens"]).index(eos)
+    assert np.array_equal(toks, g["tokens"][:first]) and m2.length == len(g["prompt"]) + first
+
+
+def test_errors_match_reference_messages():
+    m = N.Model(TINY, S.model_tensors(TINY, seed=3))
+    with pytest.raises(RuntimeError, match="out of vocab range"):
+        m.forward([TINY.n_vocab])
+    with pytest.raises(RuntimeError, match="KV cache exhausted"):
+        m.forward(np.zeros(TINY.ctx_len + 1, np.int32))
+    with pytest.raises(RuntimeError, match="empty token batch"):
+        m.forward([])
+    with pytest.raises(RuntimeError, match="has shape"):
+        m.set_tensor(S.ROLE_ATTN_Q, 0, S.q4_0_weights(32, 256, 1), S.GGML_Q4_0, 256, 32)
+
+
+@pytest.mark.parametrize("cfg,n_prompt,steps", [
+    (TINY.with_(n_vocab=777, n_embd=384, n_ff=1024, n_head=6, n_kv_head=2, ctx_len=300), 200, 24),
+    (S.QWEN3_0_6B.with_(ctx_len=128 + 64 + 1), 128, 64),
+])
+def test_greedy_matches_reference(cfg, n_prompt, steps):
+    """Identical greedy tokens to the reference's own transformer_forward."""
+    if not O.ref_available():
+        pytest.skip("oracle/_ref not built")
+    tensors = list(S.model_tensors(cfg, seed=21))
+    prompt = S.prompt_tokens(n_prompt, cfg.n_vocab, 22)
+    ref = O.Model(cfg, tensors, "reference")
+    ref_toks, ref_logits = ref.generate_greedy(prompt, steps)
+    ref.close()
+    m = N.Model(cfg, tensors)
+    toks = m.generate(prompt, steps)
+    # the smallest top-2 logit margin of the reference run, for the record
+    top2 = np.sort(ref_logits, axis=1)[:, -2:]
+    margin = float(np.min(top2[:, 1] - top2[:, 0]))
+    assert np.array_equal(toks, ref_toks), f"greedy tokens differ (min top-2 margin {margin:.3g})"
+    # logits step by step on the same token stream
+    m2 = N.Model(cfg, tensors)
+    errs = [rel_l2(m2.forward(prompt), ref_logits[0])]
+    for i, t in enumerate(ref_toks[:8]):
+        errs.append(rel_l2(m2.forward([t]), ref_logits[i + 1]))
+    print(f"{cfg.name}: min top-2 margin {margin:.3g}, logits rel-L2 max {max(errs):.2e}")
+    assert max(errs) <= MODEL_L2_RTOL

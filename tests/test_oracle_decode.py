@@ -100,3 +100,28 @@ def test_model_forward_matches_reference(cfg, prompt, steps):
     k1, v1 = mo.kv(1, prompt + steps)
     k2, v2 = mr.kv(1, prompt + steps)
     assert np.array_equal(bits(k1), bits(k2)) and np.array_equal(bits(v1), bits(v2))
+
+
+def test_summation_order_sensitivity_of_the_reference_algorithm():
+    """Reversing the order of the Q4_0 block sums (a pure fp32 reordering of
+    the reference's own arithmetic) moves some positions' logits far beyond the
+    single-matvec 1e-3 bar, but stays within the whole-model bar and keeps the
+    greedy tokens. This is why full-model parity is checked on tokens and on
+    relative L2 (MODEL_L2_RTOL), not per element."""
+    from conftest import MODEL_L2_RTOL, max_rel_err, rel_l2
+    cfg = S.ModelConfig(777, 384, 1, 6, 2, 64, 1024, ctx_len=300, rope_base=1e4)
+    tensors = list(S.model_tensors(cfg, seed=21))
+    prompt = S.prompt_tokens(60, cfg.n_vocab, 22)
+    flag = C.c_int.in_dll(O.lib(), "oracle_reverse_block_order")
+    a = O.Model(cfg, tensors, "port")
+    la = [a.forward(prompt[t:t + 1]) for t in range(60)]
+    flag.value = 1
+    try:
+        b = O.Model(cfg, tensors, "port")
+        lb = [b.forward(prompt[t:t + 1]) for t in range(60)]
+    finally:
+        flag.value = 0
+    worst = max(max_rel_err(y, r) for y, r in zip(lb, la))
+    assert worst > 1e-2, "expected at least one quantisation flip among 60 positions"
+    assert max(rel_l2(y, r) for y, r in zip(lb, la)) <= MODEL_L2_RTOL
+    assert all(int(np.argmax(y)) == int(np.argmax(r)) for y, r in zip(lb, la))
