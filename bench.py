@@ -65,8 +65,19 @@ METRIC = "Q4_0 matvec HBM GB/s vs peak"
 TYPE_NAME = "Q4_0"
 
 
+# decode workloads: name -> (model config, prompt tokens, generated tokens)
+DECODE_WORKLOADS = {
+    "decode_qwen3": (S.QWEN3_0_6B, 128, 256),
+    "decode_phi4": (S.PHI4_MINI, 512, 512),
+    "decode_llama70b": (S.LLAMA3_70B, 2048, 256),
+}
+DECODE_METRIC = "batch-1 decode tokens/s"
+
+
 def select_workload(name):
     global TYPE, ROWS, COLS, ROTATION, METRIC, TYPE_NAME
+    if name in DECODE_WORKLOADS:
+        return
     TYPE, ROWS, COLS = WORKLOADS[name]
     TYPE_NAME = "Q4_0" if TYPE == S.GGML_Q4_0 else "Q8_0"
     METRIC = f"{TYPE_NAME} matvec HBM GB/s vs peak"
@@ -86,7 +97,10 @@ def parse_args():
     p.add_argument("--e2e-steps", type=int, default=3)
     p.add_argument("--cpu-seconds", type=float, default=12.0)
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--workload", choices=sorted(WORKLOADS), default="q4_0_4096x4096")
+    p.add_argument("--workload", choices=sorted(WORKLOADS) + sorted(DECODE_WORKLOADS), default="q4_0_4096x4096")
+    p.add_argument("--prompt", type=int, default=None, help="decode workloads: prompt tokens (default: the config's)")
+    p.add_argument("--new-tokens", type=int, default=None, help="decode workloads: generated tokens")
+    p.add_argument("--no-decode", action="store_true", help="matvec workloads: skip the decode sub-measurement")
     args = p.parse_args()
     select_workload(args.workload)
     return args
@@ -224,9 +238,110 @@ def host_rotation(rank, n):
     return [S.weights(TYPE, ROWS, COLS, seed=100000 * rank + i) for i in range(n)]
 
 
+def decode_config(name, prompt=None, new_tokens=None):
+    cfg, n_prompt, n_new = DECODE_WORKLOADS[name]
+    n_prompt = n_prompt if prompt is None else prompt
+    n_new = n_new if new_tokens is None else new_tokens
+    return cfg.with_(ctx_len=n_prompt + n_new + 1), n_prompt, n_new
+
+
+def decode_desc(cfg, n_prompt, n_new):
+    return (f"{cfg.name} decoder ({cfg.n_layer} layers, hidden {cfg.n_embd}, {cfg.n_head}/{cfg.n_kv_head} heads, "
+            f"head_dim {cfg.head_dim}, ffn {cfg.n_ff}, vocab {cfg.n_vocab}), random-init Q4_0 projections, "
+            f"Q8_0 tied embedding/lm_head, fp32 norms; greedy decode of {n_new} tokens after a {n_prompt}-token "
+            f"seeded-random prompt")
+
+
+def measure_decode_gpu(name, prompt=None, new_tokens=None):
+    """Device-timed greedy decode through neon_cuda.Model.generate (CUDA graph
+    per token); returns (result dict, model config, prompt tokens)."""
+    import neon_cuda as N
+
+    cfg, n_prompt, n_new = decode_config(name, prompt, new_tokens)
+    t0 = time.perf_counter()
+    m = N.Model(cfg, S.model_tensors(cfg, seed=5))
+    load_s = time.perf_counter() - t0
+    prompt_toks = S.prompt_tokens(n_prompt, cfg.n_vocab, 6)
+    t0 = time.perf_counter()
+    toks = m.generate(prompt_toks, n_new)
+    wall = time.perf_counter() - t0
+    ms = m.decode_ms
+    m.free()
+    return {"workload": decode_desc(cfg, n_prompt, n_new), "tokens_per_s": round(n_new * 1e3 / ms, 2),
+            "ms_per_token": round(ms / n_new, 4), "generated": int(len(toks)),
+            "timing": "CUDA events around the replayed per-token graphs",
+            "e2e_tokens_per_s": round(n_new / wall, 2),
+            "e2e": "neon_cuda.Model.generate wall clock incl. prompt prefill and token read-back",
+            "load_s": round(load_s, 2)}, cfg, prompt_toks
+
+
+def measure_decode_cpu(cfg, prompt_toks, steps, threads=None):
+    """The reference's own transformer_forward (oracle/_ref) on the host:
+    prompt prefill, then `steps` greedy decode steps; tokens/s of the decode."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+
+    kind = "reference" if O.ref_available() else "port"
+    m = O.Model(cfg, S.model_tensors(cfg, seed=5), kind, threads=threads)
+    logits = m.forward(prompt_toks)
+    nxt = int(np.argmax(logits))
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        logits = m.forward(np.array([nxt], np.int32))
+        nxt = int(np.argmax(logits))
+    dt = time.perf_counter() - t0
+    cores = m.pool.n if m.pool is not None else 1
+    m.close()
+    return {"tokens_per_s": round(steps / dt, 3), "kind": kind, "cores": cores,
+            "sample": f"{steps} greedy decode steps of the reference's transformer_forward after the "
+                      f"{len(prompt_toks)}-token prompt"}
+
+
+def run_decode(args):
+    """--workload decode_*: one line, metric batch-1 decode tokens/s."""
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world > 1:
+        raise SystemExit("decode workloads run on one GPU in this build")
+    torch.cuda.set_device(0)
+    import neon_cuda as N
+
+    N.init(0)
+    sampler = ClockSampler([0])
+    time.sleep(0.2)
+    t0 = time.time()
+    res, cfg, prompt_toks = measure_decode_gpu(args.workload, args.prompt, args.new_tokens)
+    t1 = time.time()
+    sampler.stop()
+    cpu = None if args.no_cpu_baseline else measure_decode_cpu(cfg, prompt_toks, steps=8)
+    line = {"metric": DECODE_METRIC, "value": res["tokens_per_s"], "unit": "tokens/s", "n_gpus": 1,
+            "steps": res["generated"], "warmup": 0, "ms_per_step": res["ms_per_token"], "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "int8/fp32 (q4_0 x q8_0 dp4a, fp32 scales)",
+            "data": "synthetic", "config": {"workload": res["workload"], "parallelism": "tp1"},
+            "e2e": {"value": res["e2e_tokens_per_s"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 4, "api": res["e2e"]},
+            "cpu_baseline": cpu, "clocks": sampler.summary(t0, t1)}
+    print(json.dumps(line), flush=True)
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
+        return
+    if args.workload in DECODE_WORKLOADS:
+        cfg, n_prompt, n_new = decode_config(args.workload, args.prompt, args.new_tokens)
+        prompt_toks = S.prompt_tokens(n_prompt, cfg.n_vocab, 6)
+        steps = max(1, min(args.steps, 16))
+        cpu = measure_decode_cpu(cfg, prompt_toks, steps)
+        line = {"impl": "reference", "metric": DECODE_METRIC, "value": cpu["tokens_per_s"], "unit": "tokens/s",
+                "n_gpus": 0, "steps": steps, "warmup": 0, "ms_per_step": round(1e3 / cpu["tokens_per_s"], 3),
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8/fp32",
+                "data": "synthetic", "config": {"workload": decode_desc(cfg, n_prompt, n_new), "parallelism": "cpu"},
+                "cpu_baseline": {**cpu, "value": cpu["tokens_per_s"], "unit": "tokens/s"},
+                "e2e": {"value": cpu["tokens_per_s"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
         return
     cpu_n = min(16, ROTATION)
     weights = host_rotation(0, cpu_n)
@@ -385,6 +500,18 @@ def run_neon(args):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_reference_gbs(host_w, x_host, args.cpu_seconds)
+    decode = None
+    if rank == 0 and world == 1 and not args.no_decode:
+        del tensors
+        torch.cuda.empty_cache()
+        decode, dcfg, dprompt = measure_decode_gpu("decode_qwen3")
+        if not args.no_cpu_baseline:
+            dcpu = measure_decode_cpu(dcfg, dprompt, steps=8)
+            decode["cpu_reference_tokens_per_s"] = dcpu["tokens_per_s"]
+            decode["cpu_reference_cores"] = dcpu["cores"]
+            decode["cpu_reference_kind"] = dcpu["kind"]
+        decode["parity"] = ("greedy tokens identical to the reference's transformer_forward over 64 steps "
+                            "(tests/test_decode_gpu.py)")
 
     if rank == 0:
         peak, peak_kind = measured_peak()
@@ -410,6 +537,7 @@ def run_neon(args):
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "traffic": traffic, "algorithmic_bytes_per_launch": bytes_call},
             "cpu_baseline": cpu,
+            "decode": decode,
             "gpu_launches": gpu_launches,
             "clocks": clocks,
         }
@@ -424,6 +552,8 @@ def main():
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload in DECODE_WORKLOADS:
+        run_decode(args)
     else:
         run_neon(args)
 

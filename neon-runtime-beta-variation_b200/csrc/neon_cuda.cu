@@ -234,7 +234,8 @@ int stream_occupancy(int type, int rc, int smem) {
 }
 
 int launch_stream(const std::vector<const neon_proj_target_t*>& t, int type, int nb, const float* dX,
-                  cudaStream_t st, DeviceState& ds, int accumulate) {
+                  cudaStream_t st, DeviceState& ds, int accumulate, const neon_proj_target_t* base,
+                  const neon_internal::MatvecExt* ext) {
     size_t total_rows = 0;
     for (auto* tg : t) total_rows += tg->W->rows;
     const StreamPlan p = plan_stream(type, nb, total_rows, ds.sms);
@@ -258,9 +259,22 @@ int launch_stream(const std::vector<const neon_proj_target_t*>& t, int type, int
             s.rows = (int)tg->W->rows;
             s.tile0 = tiles;
             tiles += (int)((tg->W->rows + rc_rows - 1) / rc_rows);
+            if (ext && ext->epi) {
+                const size_t k = (size_t)(tg - base);
+                s.epi = ext->epi[k];
+                s.pos_stride = ext->pos_stride ? ext->pos_stride[k] : 0;
+            }
         }
         a.x = dX;
         a.err = ds.err;
+        if (ext) {
+            a.norm_w = ext->norm_w;
+            a.norm_eps = ext->norm_eps;
+            a.d_pos = ext->d_pos;
+            a.rope_cs = ext->rope_cs;
+            a.rope_half = ext->rope_half;
+            a.head_dim = ext->head_dim;
+        }
         a.n_spans = (int)n;
         a.n_tiles = tiles;
         a.nb = nb;
@@ -352,10 +366,12 @@ struct Group {
 };
 
 int launch_group(const Group& g, const float* dX, size_t x_stride, size_t seq, cudaStream_t st,
-                 DeviceState& ds, int accumulate) {
+                 DeviceState& ds, int accumulate, const neon_proj_target_t* base,
+                 const neon_internal::MatvecExt* ext) {
     const int nb = (int)(g.cols / 32);
     const bool q4 = g.type == NEON_GGML_Q4_0;
-    if (seq == 1) return launch_stream(g.t, g.type, nb, dX, st, ds, accumulate);
+    if (seq == 1) return launch_stream(g.t, g.type, nb, dX, st, ds, accumulate, base, ext);
+    if (ext) return set_err(NEON_ERR_UNSUPPORTED, "fused norm / epilogues need one position");
     size_t start = 0;
     while (start < g.t.size()) {
         MatvecArgs a;
@@ -398,7 +414,8 @@ int launch_group(const Group& g, const float* dX, size_t x_stride, size_t seq, c
 
 // Shared body of neon_cuda_matvec[_multi] on device buffers.
 int matvec_targets(const neon_proj_target_t* targets, size_t n_targets, const float* dX,
-                   size_t x_stride, size_t seq, void* stream, int accumulate = 0) {
+                   size_t x_stride, size_t seq, void* stream, int accumulate = 0,
+                   const neon_internal::MatvecExt* ext = nullptr) {
     if (n_targets == 0 || seq == 0) return NEON_OK;
     if (!targets || !dX) return set_err(NEON_ERR_INVALID, "null targets or X");
     int device = targets[0].W ? targets[0].W->device : -1;
@@ -449,8 +466,9 @@ int matvec_targets(const neon_proj_target_t* targets, size_t n_targets, const fl
                     ds.xd, ds.xs);
         if (rc) return rc;
     }
+    if (ext && groups.size() > 1) return set_err(NEON_ERR_UNSUPPORTED, "fused epilogues need one launch group");
     for (const Group& g : groups) {
-        rc = launch_group(g, dX, x_stride, seq, st, ds, accumulate);
+        rc = launch_group(g, dX, x_stride, seq, st, ds, accumulate, targets, ext);
         if (rc) return rc;
     }
     return NEON_OK;
@@ -462,8 +480,8 @@ int matvec_targets(const neon_proj_target_t* targets, size_t n_targets, const fl
 // epilogue, and the error helpers, for the decode engine (neon_decode.cu).
 namespace neon_internal {
 int matvec(const neon_proj_target_t* targets, size_t n, const float* dX, size_t x_stride, size_t seq,
-           cudaStream_t st, int accumulate) {
-    return matvec_targets(targets, n, dX, x_stride, seq, (void*)st, accumulate);
+           cudaStream_t st, int accumulate, const MatvecExt* ext) {
+    return matvec_targets(targets, n, dX, x_stride, seq, (void*)st, accumulate, ext);
 }
 int error(int code, const std::string& msg) { return set_err(code, msg); }
 int cuda_error(cudaError_t e, const char* what) { return cuda_err(e, what); }

@@ -1,17 +1,22 @@
 // neon_decode.cu -- the decode step of a NANITY decoder on one device.
 //
 // Reference: fwd::transformer_forward (rawllm_forward.hpp:987-1236) and the
-// greedy loop of run_generation (NEON-3.cpp:676-759). Per layer:
-//   xn = rms_norm(h, attn_norm)                     rmsnorm_kernel
-//   q, k, v = proj_multi(xn)                        streaming matvec (one launch)
-//   rope(q, k); K/V cache[pos] = k, v               rope_kv_kernel
-//   att = causal GQA attention(q, cache)            attention_kernel
-//   h += proj(att, attn_output)                     matvec, accumulate epilogue
-//   xn = rms_norm(h, ffn_norm)                      rmsnorm_kernel
-//   g, u = proj_multi(xn); act = silu(g) * u        matvec + silu_mul_kernel
-//   h += proj(act, ffn_down)                        matvec, accumulate epilogue
-// then logits = proj(rms_norm(h_last, output_norm), output ?? token_embd) and,
-// in generation, the first maximum (argmax_kernel), fed back on the device.
+// greedy loop of run_generation (NEON-3.cpp:676-759). One decode position is
+// five launches per layer:
+//   q, k, v = proj_multi(rms_norm(h, attn_norm))   streaming matvec; the norm is
+//        RoPE'd q -> q, RoPE'd k / v -> cache[pos]   folded into its X staging,
+//                                                  RoPE and the cache writes
+//                                                  into its epilogue
+//   att = causal GQA attention(q, cache)           attention_kernel
+//   h += proj(att, attn_output)                    matvec, accumulate epilogue
+//   act = silu(g) * u, (g, u) = proj(rms_norm(h, ffn_norm))
+//                                                  one matvec over the gate/up
+//                                                  rows interleaved at upload
+//   h += proj(act, ffn_down)                       matvec, accumulate epilogue
+// then logits = proj(rms_norm(h, output_norm), output ?? token_embd) and, in
+// generation, the first maximum (argmax_kernel), fed back on the device. A
+// prompt (several positions) runs the same steps unfused: rmsnorm_kernel,
+// multi-position matvecs, rope_kv_kernel, swiglu_pairs_kernel.
 //
 // Element-wise arithmetic mirrors the reference's optimised build: RoPE with
 // the reference's cos/sin values (host libm, uploaded as a table) and g++'s
@@ -21,6 +26,11 @@
 // differ from the reference's sequential order by fp32 rounding only.
 #include "neon_cuda.h"
 #include "neon_internal.h"
+
+namespace neon {
+// epilogue kinds of the one-position matvec kernel (see neon_kernels.cuh)
+enum : int { kEpiStore = 0, kEpiRope = 1, kEpiAtPos = 2, kEpiSwiglu = 3 };
+}  // namespace neon
 
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -254,28 +264,179 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const float* __rest
     }
 }
 
-// act = silu(g) * u with silu(x) = x / (1 + fast_expf(-x)) (rawllm_forward.hpp:740, :1186).
-__global__ void silu_mul_kernel(float* __restrict__ g, const float* __restrict__ u, long long n) {
-    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
-        const float x = g[i];
-        g[i] = __fmul_rn(__fdiv_rn(x, __fadd_rn(1.0f, fast_expf_dev(-x))), u[i]);
+// ---------------------------------------------------------------------------
+// Decode attention (one position, L = *d_pos + 1 cache rows), split over
+// positions: CTA (kvh, split) takes cache rows [split*chunk, ...) for the
+// `group` query heads of KV head kvh, so each K/V row is read once for the
+// whole group. The softmax keeps the reference's form p_s = fast_expf(score_s
+// - max over ALL positions) (transformer_forward :1123-1137), so the scores go
+// through global scratch: attn_scores_kernel writes them and a per-split
+// maximum; attn_values_kernel takes the global maximum, forms p_s, the split's
+// sum of p_s and of p_s * v_s, and the last CTA of each KV head combines the
+// splits in split order: out = (sum_splits p v) / (sum_splits p).
+// ---------------------------------------------------------------------------
+constexpr int kAttnMaxGroup = 8;
+
+__global__ void __launch_bounds__(kThreads) attn_scores_kernel(const float* __restrict__ q, const float* __restrict__ Kc,
+                                                               const int* __restrict__ d_pos, int kv_dim, int hd, int group,
+                                                               float scale, int nsplit, int ctx, float* __restrict__ scores,
+                                                               float* __restrict__ pmax) {
+    __shared__ float qs[kAttnMaxGroup * 256];
+    __shared__ float wmax[kAttnMaxGroup][kThreads / 32];
+    const int kvh = blockIdx.x, split = blockIdx.y;
+    const int L = *d_pos + 1;
+    const int chunk = (L + nsplit - 1) / nsplit;
+    const int s0 = split * chunk, s1 = min(L, s0 + chunk);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    const int per = hd / 32;
+    for (int i = threadIdx.x; i < group * hd; i += blockDim.x) qs[i] = q[(long long)kvh * group * hd + i];
+    __syncthreads();
+    float mx[kAttnMaxGroup];
+#pragma unroll
+    for (int gq = 0; gq < kAttnMaxGroup; ++gq) mx[gq] = -INFINITY;
+    for (int s = s0 + warp; s < s1; s += nw) {
+        const float* kr = Kc + (long long)s * kv_dim + (long long)kvh * hd;
+        float kv[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) kv[j] = j < per ? __ldg(kr + lane + 32 * j) : 0.f;
+#pragma unroll
+        for (int gq = 0; gq < kAttnMaxGroup; ++gq) {
+            if (gq >= group) break;
+            float acc = 0.f;
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                if (j < per) acc = __fmaf_rn(qs[gq * hd + lane + 32 * j], kv[j], acc);
+            acc = warp_sum_f(acc);
+            const float sc = __fmul_rn(acc, scale);
+            if (lane == 0) scores[((long long)kvh * group + gq) * ctx + s] = sc;
+            mx[gq] = fmaxf(mx[gq], sc);
+        }
+    }
+#pragma unroll
+    for (int gq = 0; gq < kAttnMaxGroup; ++gq)
+        if (gq < group && lane == 0) wmax[gq][warp] = mx[gq];
+    __syncthreads();
+    if ((int)threadIdx.x < group) {
+        float m = -INFINITY;
+        for (int w = 0; w < nw; ++w) m = fmaxf(m, wmax[threadIdx.x][w]);
+        pmax[((long long)kvh * group + threadIdx.x) * nsplit + split] = m;
     }
 }
 
+__global__ void __launch_bounds__(kThreads) attn_values_kernel(const float* __restrict__ Vc, const int* __restrict__ d_pos,
+                                                               int kv_dim, int hd, int group, int nsplit, int ctx,
+                                                               const float* __restrict__ scores, const float* __restrict__ pmax,
+                                                               float* __restrict__ psum, float* __restrict__ pout,
+                                                               unsigned int* __restrict__ counters, float* __restrict__ out) {
+    __shared__ float gmax[kAttnMaxGroup];
+    __shared__ float red[kThreads];
+    __shared__ bool last;
+    const int kvh = blockIdx.x, split = blockIdx.y;
+    const int L = *d_pos + 1;
+    const int chunk = (L + nsplit - 1) / nsplit;
+    const int s0 = split * chunk, s1 = min(L, s0 + chunk);
+    if ((int)threadIdx.x < group) {
+        const float* pm = pmax + ((long long)kvh * group + threadIdx.x) * nsplit;
+        float m = -INFINITY;
+        for (int k = 0; k < nsplit; ++k) m = fmaxf(m, pm[k]);
+        gmax[threadIdx.x] = m;
+    }
+    __syncthreads();
+    // threads split (dim, position parity): parts = blockDim / hd
+    const int parts = blockDim.x / hd;
+    const int d = threadIdx.x % hd, pidx = threadIdx.x / hd;
+    float acc[kAttnMaxGroup], sump[kAttnMaxGroup];
+#pragma unroll
+    for (int gq = 0; gq < kAttnMaxGroup; ++gq) { acc[gq] = 0.f; sump[gq] = 0.f; }
+    if (pidx < parts) {
+        const float* vb = Vc + (long long)kvh * hd + d;
+#pragma unroll 4
+        for (int s = s0 + pidx; s < s1; s += parts) {
+            const float v = __ldg(vb + (long long)s * kv_dim);
+#pragma unroll
+            for (int gq = 0; gq < kAttnMaxGroup; ++gq) {
+                if (gq >= group) break;
+                const float p = fast_expf_dev(__fsub_rn(scores[((long long)kvh * group + gq) * ctx + s], gmax[gq]));
+                acc[gq] = __fmaf_rn(p, v, acc[gq]);
+                sump[gq] += p;
+            }
+        }
+    }
+    // combine the position parts of this CTA
+    for (int gq = 0; gq < group; ++gq) {
+        red[threadIdx.x] = acc[gq];
+        __syncthreads();
+        if ((int)threadIdx.x < hd) {
+            float r = 0.f;
+            for (int k = 0; k < parts; ++k) r += red[k * hd + threadIdx.x];
+            pout[(((long long)kvh * group + gq) * nsplit + split) * hd + threadIdx.x] = r;
+        }
+        __syncthreads();
+        // the split's sum of p: threads with d == 0 hold disjoint positions
+        red[threadIdx.x] = (d == 0 && pidx < parts) ? sump[gq] : 0.f;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            float r = 0.f;
+            for (int k = 0; k < parts; ++k) r += red[k * hd];
+            psum[((long long)kvh * group + gq) * nsplit + split] = r;
+        }
+        __syncthreads();
+    }
+    // the last split CTA of this KV head combines the splits in order: every
+    // writer fences its partials before thread 0 counts this CTA in
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) last = atomicAdd(&counters[kvh], 1u) == (unsigned)(nsplit - 1);
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    for (int gq = 0; gq < group; ++gq) {
+        const long long hb = ((long long)kvh * group + gq) * nsplit;
+        float tot = 0.f;
+        for (int k = 0; k < nsplit; ++k) tot += __ldcg(psum + hb + k);
+        const float inv = __fdiv_rn(1.0f, tot);
+        for (int dd = threadIdx.x; dd < hd; dd += blockDim.x) {
+            float r = 0.f;
+            for (int k = 0; k < nsplit; ++k) r += __ldcg(pout + (hb + k) * hd + dd);
+            out[((long long)kvh * group + gq) * hd + dd] = __fmul_rn(r, inv);
+        }
+    }
+    if (threadIdx.x == 0) counters[kvh] = 0u;
+}
+
+// act[t][i] = silu(y[t][2i]) * y[t][2i+1] over the interleaved gate/up rows,
+// silu(x) = x / (1 + fast_expf(-x)) (rawllm_forward.hpp:740, :1186).
+__global__ void swiglu_pairs_kernel(const float* __restrict__ y, float* __restrict__ act, long long n) {
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        const float x = y[2 * i];
+        act[i] = __fmul_rn(__fdiv_rn(x, __fadd_rn(1.0f, fast_expf_dev(-x))), y[2 * i + 1]);
+    }
+}
+
+// Orderable 32-bit image of a float: larger float, larger unsigned.
+__device__ __forceinline__ unsigned int float_order(float v) {
+    const unsigned int u = __float_as_uint(v);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
 // Greedy sampling: the first maximum of the logits (std::max_element,
-// NEON-3.cpp:471-474). Writes the token to *d_tok and to out[*d_step], then
-// advances *d_step and, when `advance`, the position *d_pos.
-__global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ logits, int n, int* d_tok,
-                                                      int* out, int* d_step, int* d_pos, int advance) {
-    __shared__ float bv[32];
-    __shared__ int bi[32];
+// NEON-3.cpp:471-474) over the whole grid. Each CTA folds its best (value,
+// index) into *key as (order(value) << 32) | ~index with atomicMax -- the
+// larger value wins, among equal values the lower index; the last CTA to
+// finish writes the token to *d_tok and out[*d_step], advances *d_step (and
+// *d_pos when `advance`), and clears *key and *counter for the next launch.
+__global__ void __launch_bounds__(256) argmax_kernel(const float* __restrict__ logits, int n,
+                                                     unsigned long long* key, unsigned int* counter, int* d_tok,
+                                                     int* out, int* d_step, int* d_pos, int advance) {
+    __shared__ float bv[8];
+    __shared__ int bi[8];
+    __shared__ bool last;
     float best = -INFINITY;
     int idx = 0x7fffffff;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
         const float v = logits[i];
         if (v > best) { best = v; idx = i; }
     }
-    // reduce: larger value wins, ties go to the lower index
 #pragma unroll
     for (int o = 16; o; o >>= 1) {
         const float ov = __shfl_xor_sync(0xffffffffu, best, o);
@@ -285,22 +446,24 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ 
     const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
     if (l == 0) { bv[w] = best; bi[w] = idx; }
     __syncthreads();
-    if (w == 0) {
-        best = l < (int)(blockDim.x >> 5) ? bv[l] : -INFINITY;
-        idx = l < (int)(blockDim.x >> 5) ? bi[l] : 0x7fffffff;
-#pragma unroll
-        for (int o = 16; o; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
-            if (ov > best || (ov == best && oi < idx)) { best = ov; idx = oi; }
-        }
-        if (l == 0) {
-            if (idx == 0x7fffffff) idx = 0;  // all NaN: std::max_element keeps element 0
-            *d_tok = idx;
-            out[*d_step] = idx;
-            *d_step += 1;
-            if (advance) *d_pos += 1;
-        }
+    if (threadIdx.x == 0) {
+        for (int k = 1; k < (int)(blockDim.x >> 5); ++k)
+            if (bv[k] > best || (bv[k] == best && bi[k] < idx)) { best = bv[k]; idx = bi[k]; }
+        if (idx != 0x7fffffff)
+            atomicMax(key, ((unsigned long long)float_order(best) << 32) | (unsigned long long)(0xFFFFFFFFu - (unsigned)idx));
+        __threadfence();
+        last = atomicAdd(counter, 1u) == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (last && threadIdx.x == 0) {
+        const unsigned long long k = atomicAdd(key, 0ull);
+        const int tok = k ? (int)(0xFFFFFFFFu - (unsigned)(k & 0xFFFFFFFFull)) : 0;  // all NaN: element 0
+        *d_tok = tok;
+        out[*d_step] = tok;
+        *d_step += 1;
+        if (advance) *d_pos += 1;
+        *key = 0ull;
+        *counter = 0u;
     }
 }
 
@@ -318,15 +481,23 @@ struct neon_model {
     float* output_norm = nullptr;
     struct Layer {
         float *attn_norm = nullptr, *ffn_norm = nullptr;
-        neon_tensor_t w[7] = {};  // q, k, v, out, gate, up, down
+        neon_tensor_t w[5] = {};  // q, k, v, out, down
+        neon_tensor_t gateup = nullptr;  // gate and up rows interleaved (2*n_ff rows)
+        std::vector<uint8_t> gate_bytes, up_bytes;  // held until both halves are set
+        int gate_type = -1, up_type = -1;
     };
     std::vector<Layer> layers;
     float *K = nullptr, *V = nullptr;   // [layer][ctx][kv_dim]
     float2* rope_cs = nullptr;          // [ctx][rope_half]
     float *h = nullptr, *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr;
-    float *g = nullptr, *u = nullptr, *logits = nullptr;
+    float *gu = nullptr, *act = nullptr, *logits = nullptr;
     int *d_tokens = nullptr, *d_tok = nullptr, *d_pos = nullptr, *d_step = nullptr, *d_out = nullptr;
     unsigned* d_err = nullptr;
+    unsigned long long* am_key = nullptr;  // argmax scratch
+    unsigned int* am_count = nullptr;
+    int att_split = 1;                     // decode attention: position splits per KV head
+    float *att_scores = nullptr, *att_pmax = nullptr, *att_psum = nullptr, *att_pout = nullptr;
+    unsigned int* att_count = nullptr;
     size_t out_cap = 0;
     size_t length = 0;
     cudaStream_t stream = nullptr;
@@ -405,23 +576,95 @@ int run_layers(neon_model* m, const int* toks, int seq) {
         }
         if (!rc) rc = proj(m, {{L.w[3], m->h, n_embd}}, m->att, q_dim, seq, 1);
         if (!rc) rc = rmsnorm(m, m->h, L.ffn_norm, m->xn, seq);
-        if (!rc) rc = proj(m, {{L.w[4], m->g, n_ff}, {L.w[5], m->u, n_ff}}, m->xn, n_embd, seq, 0);
+        if (!rc) rc = proj(m, {{L.gateup, m->gu, 2 * n_ff}}, m->xn, n_embd, seq, 0);
         if (!rc) {
             const long long n = (long long)seq * n_ff;
-            silu_mul_kernel<<<(int)std::min<long long>((n + 255) / 256, 4096), 256, 0, m->stream>>>(m->g, m->u, n);
-            rc = check_launch("silu_mul_kernel");
+            swiglu_pairs_kernel<<<(int)std::min<long long>((n + 255) / 256, 4096), 256, 0, m->stream>>>(m->gu, m->act, n);
+            rc = check_launch("swiglu_pairs_kernel");
         }
-        if (!rc) rc = proj(m, {{L.w[6], m->h, n_embd}}, m->g, n_ff, seq, 1);
+        if (!rc) rc = proj(m, {{L.w[4], m->h, n_embd}}, m->act, n_ff, seq, 1);
     }
     return rc;
 }
 
-// logits of row `row` of h
+// logits of row `row` of h: rms_norm(output_norm) folded into the lm_head matvec
 int run_head(neon_model* m, int row) {
-    int rc = rmsnorm(m, m->h + (size_t)row * m->cfg.n_embd, m->output_norm, m->xn, 1);
-    if (rc) return rc;
     neon_tensor_t W = m->output ? m->output : m->embd;
-    return proj(m, {{W, m->logits, (size_t)m->cfg.n_vocab}}, m->xn, m->cfg.n_embd, 1, 0);
+    neon_proj_target_t t{W, m->logits, (size_t)m->cfg.n_vocab};
+    neon_internal::MatvecExt ext;
+    ext.norm_w = m->output_norm;
+    ext.norm_eps = m->cfg.norm_eps;
+    return neon_internal::matvec(&t, 1, m->h + (size_t)row * m->cfg.n_embd, m->cfg.n_embd, 1, m->stream, 0, &ext);
+}
+
+// One decode position (token in *d_tok, position *d_pos): the fused step.
+int run_step(neon_model* m) {
+    const auto& c = m->cfg;
+    const neon_tensor_t E = m->embd;
+    const int nb = (int)(c.n_embd / 32);
+    embed_kernel<<<dim3((nb + 127) / 128, 1), 128, 0, m->stream>>>(E->qs, E->d, E->type, nb, m->d_tok, (int)c.n_vocab,
+                                                                   m->h, m->d_err);
+    int rc = check_launch("embed_kernel");
+    const size_t n_embd = c.n_embd, q_dim = m->q_dim, kv_dim = m->kv_dim, n_ff = c.n_ff;
+    const float scale = 1.0f / std::sqrt((float)c.head_dim);
+    const int group = (int)(c.n_head / c.n_kv_head);
+    for (uint32_t li = 0; li < c.n_layer && !rc; ++li) {
+        auto& L = m->layers[li];
+        float* Kl = m->K + (size_t)li * c.ctx_len * kv_dim;
+        float* Vl = m->V + (size_t)li * c.ctx_len * kv_dim;
+        {
+            // q, k, v = W x with x = rms_norm(h); RoPE on q and k; k and v into the cache
+            const neon_proj_target_t t[3] = {{L.w[0], m->q, q_dim}, {L.w[1], Kl, kv_dim}, {L.w[2], Vl, kv_dim}};
+            const int epi[3] = {neon::kEpiRope, neon::kEpiRope, neon::kEpiAtPos};
+            const long long stride[3] = {0, (long long)kv_dim, (long long)kv_dim};
+            neon_internal::MatvecExt ext;
+            ext.norm_w = L.attn_norm;
+            ext.norm_eps = c.norm_eps;
+            ext.d_pos = m->d_pos;
+            ext.rope_cs = m->rope_cs;
+            ext.rope_half = (int)m->rope_half;
+            ext.head_dim = (int)c.head_dim;
+            ext.epi = epi;
+            ext.pos_stride = stride;
+            rc = neon_internal::matvec(t, 3, m->h, n_embd, 1, m->stream, 0, &ext);
+        }
+        if (!rc) {
+            const dim3 grid(c.n_kv_head, m->att_split);
+            attn_scores_kernel<<<grid, kThreads, 0, m->stream>>>(m->q, Kl, m->d_pos, (int)kv_dim, (int)c.head_dim, group,
+                                                                 scale, m->att_split, (int)c.ctx_len, m->att_scores,
+                                                                 m->att_pmax);
+            rc = check_launch("attn_scores_kernel");
+            if (!rc) {
+                attn_values_kernel<<<grid, kThreads, 0, m->stream>>>(Vl, m->d_pos, (int)kv_dim, (int)c.head_dim, group,
+                                                                     m->att_split, (int)c.ctx_len, m->att_scores,
+                                                                     m->att_pmax, m->att_psum, m->att_pout,
+                                                                     m->att_count, m->att);
+                rc = check_launch("attn_values_kernel");
+            }
+        }
+        if (!rc) rc = proj(m, {{L.w[3], m->h, n_embd}}, m->att, q_dim, 1, 1);
+        if (!rc) {
+            // act = silu(gate) * up, (gate, up) = W x with x = rms_norm(h)
+            const neon_proj_target_t t{L.gateup, m->act, n_ff};
+            const int epi = neon::kEpiSwiglu;
+            const long long stride = 0;
+            neon_internal::MatvecExt ext;
+            ext.norm_w = L.ffn_norm;
+            ext.norm_eps = c.norm_eps;
+            ext.epi = &epi;
+            ext.pos_stride = &stride;
+            rc = neon_internal::matvec(&t, 1, m->h, n_embd, 1, m->stream, 0, &ext);
+        }
+        if (!rc) rc = proj(m, {{L.w[4], m->h, n_embd}}, m->act, n_ff, 1, 1);
+    }
+    return rc;
+}
+
+int launch_argmax(neon_model* m, int advance) {
+    const int grid = std::max(1, std::min<int>(148, (int)((m->cfg.n_vocab + 1023) / 1024)));
+    argmax_kernel<<<grid, 256, 0, m->stream>>>(m->logits, (int)m->cfg.n_vocab, m->am_key, m->am_count, m->d_tok,
+                                               m->d_out, m->d_step, m->d_pos, advance);
+    return check_launch("argmax_kernel");
 }
 
 int check_ready(neon_model* m) {
@@ -432,6 +675,8 @@ int check_ready(neon_model* m) {
             return error(NEON_ERR_INVALID, "forward(): layer " + std::to_string(i) + " is missing a norm weight");
         for (auto* w : L.w)
             if (!w) return error(NEON_ERR_INVALID, "forward(): layer " + std::to_string(i) + " is missing a projection");
+        if (!L.gateup)
+            return error(NEON_ERR_INVALID, "forward(): layer " + std::to_string(i) + " is missing ffn_gate or ffn_up");
     }
     return NEON_OK;
 }
@@ -454,7 +699,13 @@ int forward_device(neon_model* m, const int32_t* tokens_host, size_t n) {
         const int pos = (int)(m->length + off);
         DEC_TRY(cudaMemcpyAsync(m->d_tokens, tokens_host + off, seq * sizeof(int32_t), cudaMemcpyHostToDevice, m->stream));
         DEC_TRY(cudaMemcpyAsync(m->d_pos, &pos, sizeof(int), cudaMemcpyHostToDevice, m->stream));
-        int rc = run_layers(m, m->d_tokens, seq);
+        int rc;
+        if (seq == 1) {
+            DEC_TRY(cudaMemcpyAsync(m->d_tok, tokens_host + off, sizeof(int32_t), cudaMemcpyHostToDevice, m->stream));
+            rc = run_step(m);
+        } else {
+            rc = run_layers(m, m->d_tokens, seq);
+        }
         if (rc) return rc;
         if (off + seq == n) {
             rc = run_head(m, seq - 1);
@@ -481,6 +732,7 @@ int neon_cuda_model_create(const neon_model_config_t* cfg, neon_model_t* out) {
     if (c.head_dim % 32 != 0 || c.head_dim > 256 || c.n_embd % 32 != 0 || c.n_ff % 32 != 0)
         return error(NEON_ERR_UNSUPPORTED, "head_dim must be a multiple of 32 up to 256; n_embd and n_ff multiples of 32");
     if (c.ctx_len > (uint32_t)kMaxCtx) return error(NEON_ERR_UNSUPPORTED, "ctx_len above 16384");
+    if (c.n_head / c.n_kv_head > 8) return error(NEON_ERR_UNSUPPORTED, "more than 8 query heads per KV head");
     if (c.rope_dim_count > c.head_dim) return error(NEON_ERR_INVALID, "rope dimension count above head_dim");
     auto* m = new neon_model();
     m->cfg = c;
@@ -504,8 +756,21 @@ int neon_cuda_model_create(const neon_model_config_t* cfg, neon_model_t* out) {
     A((void**)&m->k, sizeof(float) * S * m->kv_dim);
     A((void**)&m->v, sizeof(float) * S * m->kv_dim);
     A((void**)&m->att, sizeof(float) * S * m->q_dim);
-    A((void**)&m->g, sizeof(float) * S * c.n_ff);
-    A((void**)&m->u, sizeof(float) * S * c.n_ff);
+    A((void**)&m->gu, sizeof(float) * S * 2 * c.n_ff);
+    A((void**)&m->act, sizeof(float) * S * c.n_ff);
+    A((void**)&m->am_key, sizeof(unsigned long long));
+    A((void**)&m->am_count, sizeof(unsigned int));
+    // decode attention: splits so that (KV heads x splits) fills about two CTAs per SM
+    {
+        int sms = neon_internal::device_sms(m->device);
+        if (sms <= 0) sms = 148;
+        m->att_split = (int)std::max<long long>(1, std::min<long long>((c.ctx_len + 31) / 32, (2LL * sms) / c.n_kv_head));
+    }
+    A((void**)&m->att_scores, sizeof(float) * (size_t)c.n_head * c.ctx_len);
+    A((void**)&m->att_pmax, sizeof(float) * (size_t)c.n_head * m->att_split);
+    A((void**)&m->att_psum, sizeof(float) * (size_t)c.n_head * m->att_split);
+    A((void**)&m->att_pout, sizeof(float) * (size_t)c.n_head * m->att_split * c.head_dim);
+    A((void**)&m->att_count, sizeof(unsigned int) * c.n_kv_head);
     A((void**)&m->logits, sizeof(float) * c.n_vocab);
     A((void**)&m->d_tokens, sizeof(int) * S);
     A((void**)&m->d_tok, sizeof(int));
@@ -529,6 +794,9 @@ int neon_cuda_model_create(const neon_model_config_t* cfg, neon_model_t* out) {
         }
         if (cudaMemcpy(m->rope_cs, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice) != cudaSuccess ||
             cudaMemset(m->d_err, 0, sizeof(unsigned)) != cudaSuccess || cudaMemset(m->K, 0, kv_bytes) != cudaSuccess ||
+            cudaMemset(m->am_key, 0, sizeof(unsigned long long)) != cudaSuccess ||
+            cudaMemset(m->am_count, 0, sizeof(unsigned int)) != cudaSuccess ||
+            cudaMemset(m->att_count, 0, sizeof(unsigned int) * c.n_kv_head) != cudaSuccess ||
             cudaMemset(m->V, 0, kv_bytes) != cudaSuccess)
             rc = error(NEON_ERR_CUDA, "model initialisation copies failed");
     }
@@ -578,6 +846,35 @@ int neon_cuda_model_set_tensor(neon_model_t m, int role, int layer, const uint8_
         return error(NEON_ERR_INVALID, "NANITY: tensor of role " + std::to_string(role) + " has shape [" + std::to_string(ne0) +
                                            ", " + std::to_string(ne1) + "], expected [" + std::to_string(want0) + ", " +
                                            std::to_string(want1) + "].");
+    if (role != NEON_ROLE_TOKEN_EMBD && role != NEON_ROLE_OUTPUT && (layer < 0 || (uint32_t)layer >= c.n_layer))
+        return error(NEON_ERR_INVALID, "layer index out of range");
+    if (role == NEON_ROLE_FFN_GATE || role == NEON_ROLE_FFN_UP) {
+        // held until both halves are present, then uploaded as one tensor whose
+        // row 2i is gate row i and row 2i+1 up row i (same bytes, same math)
+        auto& L = m->layers[layer];
+        const size_t row_b = ggml_type == NEON_GGML_Q4_0 ? ne0 / 32 * 18 : ggml_type == NEON_GGML_Q8_0 ? ne0 / 32 * 34 : 0;
+        if (row_b == 0) return error(NEON_ERR_UNSUPPORTED, "ffn_gate / ffn_up must be Q4_0 or Q8_0");
+        if (nbytes < row_b * ne1) return error(NEON_ERR_INVALID, "tensor bytes shorter than its shape");
+        (role == NEON_ROLE_FFN_GATE ? L.gate_bytes : L.up_bytes).assign(host_bytes, host_bytes + row_b * ne1);
+        (role == NEON_ROLE_FFN_GATE ? L.gate_type : L.up_type) = ggml_type;
+        if (L.gate_bytes.empty() || L.up_bytes.empty()) return NEON_OK;
+        if (L.gate_type != L.up_type) return error(NEON_ERR_UNSUPPORTED, "ffn_gate and ffn_up must share a quant type");
+        std::vector<uint8_t> inter(2 * row_b * ne1);
+        for (size_t r = 0; r < ne1; ++r) {
+            std::memcpy(inter.data() + (2 * r) * row_b, L.gate_bytes.data() + r * row_b, row_b);
+            std::memcpy(inter.data() + (2 * r + 1) * row_b, L.up_bytes.data() + r * row_b, row_b);
+        }
+        neon_tensor_t t = nullptr;
+        int rc = neon_cuda_upload(inter.data(), ggml_type, 2 * ne1, ne0, NEON_SHARD_NONE, 0, 1, &t);
+        if (rc) return rc;
+        if (L.gateup) neon_cuda_free(L.gateup);
+        L.gateup = t;
+        L.gate_bytes.clear();
+        L.gate_bytes.shrink_to_fit();
+        L.up_bytes.clear();
+        L.up_bytes.shrink_to_fit();
+        return NEON_OK;
+    }
     neon_tensor_t t = nullptr;
     int rc = neon_cuda_upload(host_bytes, ggml_type, ne1, ne0, NEON_SHARD_NONE, 0, 1, &t);
     if (rc) return rc;
@@ -585,12 +882,8 @@ int neon_cuda_model_set_tensor(neon_model_t m, int role, int layer, const uint8_
     if (role == NEON_ROLE_TOKEN_EMBD) slot = &m->embd;
     else if (role == NEON_ROLE_OUTPUT) slot = &m->output;
     else {
-        if (layer < 0 || (uint32_t)layer >= c.n_layer) {
-            neon_cuda_free(t);
-            return error(NEON_ERR_INVALID, "layer index out of range");
-        }
-        // projection slots: q, k, v, out (roles 4-7), gate, up, down (roles 9-11)
-        const int idx = role <= NEON_ROLE_ATTN_OUT ? role - NEON_ROLE_ATTN_Q : role - NEON_ROLE_FFN_GATE + 4;
+        // projection slots: q, k, v, out (roles 4-7), down (role 11)
+        const int idx = role <= NEON_ROLE_ATTN_OUT ? role - NEON_ROLE_ATTN_Q : 4;
         slot = &m->layers[layer].w[idx];
     }
     if (*slot) neon_cuda_free(*slot);
@@ -637,8 +930,7 @@ int neon_cuda_model_generate(neon_model_t m, const int32_t* prompt, size_t n_pro
     DEC_TRY(cudaMemcpyAsync(m->d_step, &zero, sizeof(int), cudaMemcpyHostToDevice, m->stream));
     DEC_TRY(cudaMemcpyAsync(m->d_pos, &pos, sizeof(int), cudaMemcpyHostToDevice, m->stream));
     // first token: from the prompt's logits
-    argmax_kernel<<<1, 1024, 0, m->stream>>>(m->logits, (int)m->cfg.n_vocab, m->d_tok, m->d_out, m->d_step, m->d_pos, 0);
-    rc = check_launch("argmax_kernel");
+    rc = launch_argmax(m, 0);
     if (rc) return rc;
     if (max_new > 0) {
         // one decode step as a CUDA graph: embed(d_tok) .. logits .. argmax -> d_tok, pos += 1
@@ -648,12 +940,9 @@ int neon_cuda_model_generate(neon_model_t m, const int32_t* prompt, size_t n_pro
         }
         cudaGraph_t g = nullptr;
         DEC_TRY(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
-        rc = run_layers(m, m->d_tok, 1);
+        rc = run_step(m);
         if (!rc) rc = run_head(m, 0);
-        if (!rc) {
-            argmax_kernel<<<1, 1024, 0, m->stream>>>(m->logits, (int)m->cfg.n_vocab, m->d_tok, m->d_out, m->d_step, m->d_pos, 1);
-            rc = check_launch("argmax_kernel");
-        }
+        if (!rc) rc = launch_argmax(m, 1);
         cudaError_t ce = cudaStreamEndCapture(m->stream, &g);
         if (rc) {
             if (g) cudaGraphDestroy(g);
@@ -718,8 +1007,10 @@ int neon_cuda_model_free(neon_model_t m) {
     if (m->step_graph) cudaGraphExecDestroy(m->step_graph);
     neon_cuda_free(m->embd);
     neon_cuda_free(m->output);
-    for (auto& L : m->layers)
+    for (auto& L : m->layers) {
         for (auto* w : L.w) neon_cuda_free(w);
+        neon_cuda_free(L.gateup);
+    }
     for (void* p : m->allocs) cudaFree(p);
     if (m->d_out) cudaFree(m->d_out);
     if (m->ev0) cudaEventDestroy(m->ev0);

@@ -23,9 +23,25 @@ struct neon_tensor {
 };
 
 namespace neon_internal {
+
+// Decode-step options of a one-position matvec launch (seq == 1 only):
+// RMSNorm of X folded into the X staging, and per-target epilogues (the
+// kEpi* values of neon_kernels.cuh: plain store, RoPE pairs stored at the
+// position's cache row, store at the position's cache row, SwiGLU pairs).
+struct MatvecExt {
+    const float* norm_w = nullptr;
+    float norm_eps = 0.f;
+    const int* d_pos = nullptr;
+    const float2* rope_cs = nullptr;
+    int rope_half = 0;
+    int head_dim = 0;
+    const int* epi = nullptr;               // per target; null: plain store
+    const long long* pos_stride = nullptr;  // per target
+};
+
 // neon_cuda_matvec_multi on `st`, with y += result when `accumulate`.
 int matvec(const neon_proj_target_t* targets, size_t n, const float* dX, size_t x_stride, size_t seq,
-           cudaStream_t st, int accumulate);
+           cudaStream_t st, int accumulate, const MatvecExt* ext = nullptr);
 int error(int code, const std::string& msg);
 int cuda_error(cudaError_t e, const char* what);
 int launched(int n);  // count kernels launched outside the matvec path

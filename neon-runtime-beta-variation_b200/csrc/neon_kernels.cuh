@@ -35,13 +35,24 @@ constexpr int kQ4Rec = 48;
 constexpr int kQ8Pitch = 36;
 
 // One projection target of a launch: rows [0, rows) of one uploaded tensor.
+// Epilogues of the one-position kernel (decode step). Pair epilogues take
+// rows (2i, 2i+1), which always share a tile (tiles start at even rows).
+enum : int {
+    kEpiStore = 0,   // y[r] = v (or += with accumulate)
+    kEpiRope = 1,    // RoPE on pairs (fwd::rope_apply), then store at y + pos*pos_stride
+    kEpiAtPos = 2,   // store at y + pos*pos_stride (the V cache row of the position)
+    kEpiSwiglu = 3,  // rows interleave gate/up: y[i] = silu(v_2i) * v_2i+1
+};
+
 struct Span {
     const uint8_t* qs;   // payload plane
     const uint16_t* d;   // fp16 scale plane
     float* y;            // output, element (t, r) at y[t*y_stride + r]
     long long y_stride;
+    long long pos_stride;  // kEpiRope / kEpiAtPos: y advances this far per position
     int rows;
     int tile0;           // index of this span's first row tile in the launch
+    int epi;             // kEpi*
 };
 
 struct MatvecArgs {
@@ -309,6 +320,12 @@ struct StreamArgs {
     int stage_bytes;        // bytes per stage
     int x_vec;              // x is 16-byte aligned: 128-bit loads
     int accumulate;         // 1: y += result (the residual add of the decode loop)
+    const float* norm_w;    // non-null: X is replaced by rms_norm(X, norm_w, norm_eps) first
+    float norm_eps;
+    const int* d_pos;       // position of the token (RoPE / cache epilogues)
+    const float2* rope_cs;  // [position][rope_half] (cos, sin)
+    int rope_half;
+    int head_dim;
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -388,11 +405,35 @@ __host__ __device__ constexpr int stream_x_bytes(int type, int nb) {
     return ((type == 2 ? nb * kQ4Rec : nb * kQ8Pitch * 4) + 127) & ~127;
 }
 
+// rms_norm's scale 1/sqrt(mean(x^2) + eps) of n floats (fwd::rms_norm,
+// rawllm_forward.hpp:730-735): a double sum of squares over the whole CTA,
+// so every CTA of the launch derives the same scale.
+__device__ float cta_rms_scale(const float* __restrict__ x, int n, float eps, double* scratch) {
+    double ss = 0.0;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const double v = (double)__ldg(x + i);
+        ss = fma(v, v, ss);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    if (l == 0) scratch[w] = ss;
+    __syncthreads();
+    double r = l < (int)(blockDim.x >> 5) ? scratch[l] : 0.0;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
+    __syncthreads();  // scratch may be reused right after
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)(r / (double)n), eps)));
+}
+
 // Quantise X (nb blocks) into the CTA's Q8_0 records, TPB threads per block.
 // Whole warps iterate together (the shuffles need every lane); the TPB
 // threads of one block are always all active or all idle.
+// With norm_w, each element is first replaced by (x * scale) * w, rms_norm's
+// output (the reference multiplies in that order).
 template <int TPB>
-__device__ __forceinline__ void stage_x_q8(const float* __restrict__ x, int nb, bool x_vec, unsigned char* rec) {
+__device__ __forceinline__ void stage_x_q8(const float* __restrict__ x, int nb, bool x_vec, unsigned char* rec,
+                                           const float* __restrict__ norm_w = nullptr, float scale = 1.f) {
     constexpr int EPT = 32 / TPB;
     const int lane = threadIdx.x & 31;
     const int n = nb * TPB;
@@ -414,6 +455,11 @@ __device__ __forceinline__ void stage_x_q8(const float* __restrict__ x, int nb, 
         } else {
 #pragma unroll
             for (int j = 0; j < EPT; ++j) xv[j] = 0.f;
+        }
+        if (norm_w && act) {
+            const float* wb = norm_w + (long long)b * 32 + part * EPT;
+#pragma unroll
+            for (int j = 0; j < EPT; ++j) xv[j] = __fmul_rn(__fmul_rn(xv[j], scale), __ldg(wb + j));
         }
         float amax = 0.f;
 #pragma unroll
@@ -491,6 +537,57 @@ __device__ __forceinline__ float q8_block_dot_x2(const uint4 w0, const uint4 w1,
     return __uint_as_float((uint32_t)acc) + __uint_as_float((uint32_t)(acc >> 32));
 }
 
+__device__ __forceinline__ float silu_dev(float x) {
+    // x / (1 + fast_expf(-x)) with engine::fast_expf (rawllm_common.hpp:88-100):
+    // Schraudolph's exp, kA*x + kB as one FMA truncated to int.
+    const float e = (-x < -88.f || -x > 88.f)
+                        ? expf(-x)
+                        : __int_as_float(__float2int_rz(__fmaf_rn(12102203.9f, -x, 1064872507.f)));
+    return __fdiv_rn(x, __fadd_rn(1.0f, e));
+}
+
+// Writes the RC row results of a tile (rowv[], shared memory) through the
+// span's epilogue; threads t < RC own row row0 + t.
+__device__ __forceinline__ void stream_epilogue(const StreamArgs& a, const Span& sp, int row0, int RC,
+                                                const float* rowv) {
+    const int t = threadIdx.x;
+    if (t >= RC) return;
+    const int row = row0 + t;
+    if (row >= sp.rows) return;
+    const float v = rowv[t];
+    switch (sp.epi) {
+        case kEpiStore:
+            sp.y[row] = a.accumulate ? sp.y[row] + v : v;
+            break;
+        case kEpiAtPos:
+            sp.y[(long long)(*a.d_pos) * sp.pos_stride + row] = v;
+            break;
+        case kEpiRope: {
+            // rotate (v_2i, v_2i+1) of a head by the position's angle
+            // (fwd::rope_apply, rawllm_forward.hpp:767-782, with g++'s FMA
+            // contraction); pairs at or beyond rope_half are stored unrotated
+            const int pos = *a.d_pos;
+            float* dst = sp.y + (long long)pos * sp.pos_stride;
+            if (t & 1) break;
+            const float x0 = v, x1 = rowv[t + 1];
+            const int i = (row % a.head_dim) / 2;
+            if (i < a.rope_half) {
+                const float2 c = a.rope_cs[(long long)pos * a.rope_half + i];
+                dst[row] = __fmaf_rn(x0, c.x, -__fmul_rn(x1, c.y));
+                dst[row + 1] = __fmaf_rn(x0, c.y, __fmul_rn(x1, c.x));
+            } else {
+                dst[row] = x0;
+                dst[row + 1] = x1;
+            }
+            break;
+        }
+        case kEpiSwiglu:
+            // silu(gate) * up (rawllm_forward.hpp:1186)
+            if (!(t & 1)) sp.y[row / 2] = __fmul_rn(silu_dev(v), rowv[t + 1]);
+            break;
+    }
+}
+
 // Work mapping: a tile has RC rows; every thread owns R consecutive rows and a
 // slice of the blocks of a chunk. G = RC/R row groups share the CTA's threads,
 // TPG = kStreamThreads/G per group: WPG = TPG/32 whole warps per group when
@@ -506,6 +603,7 @@ __global__ void __launch_bounds__(kStreamThreads) matvec_stream_kernel(const __g
     static_assert(RC % R == 0 && kStreamThreads % G == 0, "bad tile shape");
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ float red[RC * WPG];
+    __shared__ float rowv[RC];
     const int nb = a.nb, KC = a.kc, nch = a.nch, S = a.stages;
     const int SPH = stream_scale_pitch(KC);
     unsigned char* xsm = smem;
@@ -572,21 +670,21 @@ __global__ void __launch_bounds__(kStreamThreads) matvec_stream_kernel(const __g
     }
     pdl_wait();
 
-    // Stage X once per CTA, then let the next launch start.
+    // Stage X once per CTA (normalised first when asked), then let the next
+    // launch start.
+    __shared__ double dscratch[32];
+    const float nscale = a.norm_w ? cta_rms_scale(a.x, nb * 32, a.norm_eps, dscratch) : 1.f;
     if (TYPE == 2) {
         const int tpb = kStreamThreads / nb;
-        if (tpb >= 4) stage_x_q8<4>(a.x, nb, a.x_vec, xsm);
-        else if (tpb >= 2) stage_x_q8<2>(a.x, nb, a.x_vec, xsm);
-        else stage_x_q8<1>(a.x, nb, a.x_vec, xsm);
+        if (tpb >= 4) stage_x_q8<4>(a.x, nb, a.x_vec, xsm, a.norm_w, nscale);
+        else if (tpb >= 2) stage_x_q8<2>(a.x, nb, a.x_vec, xsm, a.norm_w, nscale);
+        else stage_x_q8<1>(a.x, nb, a.x_vec, xsm, a.norm_w, nscale);
     } else {
         float* xs = reinterpret_cast<float*>(xsm);
-        if (a.x_vec) {
-            for (int i = threadIdx.x; i < nb * 8; i += kStreamThreads)
-                *reinterpret_cast<float4*>(xs + (i >> 3) * kQ8Pitch + (i & 7) * 4) =
-                    __ldg(reinterpret_cast<const float4*>(a.x) + i);
-        } else {
-            for (int i = threadIdx.x; i < nb * 32; i += kStreamThreads)
-                xs[(i >> 5) * kQ8Pitch + (i & 31)] = __ldg(a.x + i);
+        for (int i = threadIdx.x; i < nb * 32; i += kStreamThreads) {
+            float v = __ldg(a.x + i);
+            if (a.norm_w) v = __fmul_rn(__fmul_rn(v, nscale), __ldg(a.norm_w + i));
+            xs[(i >> 5) * kQ8Pitch + (i & 31)] = v;
         }
     }
     __syncthreads();
@@ -659,28 +757,25 @@ __global__ void __launch_bounds__(kStreamThreads) matvec_stream_kernel(const __g
             for (int rr = 0; rr < R; ++rr)
 #pragma unroll
                 for (int o = LPG / 2; o; o >>= 1) acc[rr] += __shfl_xor_sync(0xffffffffu, acc[rr], o);
+            // row results -> rowv[] in shared memory
             if (WPG == 1) {
                 if (slice == 0) {
 #pragma unroll
-                    for (int rr = 0; rr < R; ++rr) {
-                        const int row = row0 + g * R + rr;
-                        if (row < sp.rows) sp.y[row] = a.accumulate ? sp.y[row] + acc[rr] : acc[rr];
-                    }
+                    for (int rr = 0; rr < R; ++rr) rowv[g * R + rr] = acc[rr];
                 }
-            } else {
-                if (lane == 0) {
+            } else if (lane == 0) {
 #pragma unroll
-                    for (int rr = 0; rr < R; ++rr) red[(g * R + rr) * WPG + (warp % WPG)] = acc[rr];
-                }
-                __syncthreads();
-                if ((int)threadIdx.x < RC) {
-                    float v = 0.f;
-#pragma unroll
-                    for (int w = 0; w < WPG; ++w) v += red[threadIdx.x * WPG + w];
-                    const int row = row0 + threadIdx.x;
-                    if (row < sp.rows) sp.y[row] = a.accumulate ? sp.y[row] + v : v;
-                }
+                for (int rr = 0; rr < R; ++rr) red[(g * R + rr) * WPG + (warp % WPG)] = acc[rr];
             }
+            __syncthreads();
+            if (WPG > 1 && (int)threadIdx.x < RC) {
+                float v = 0.f;
+#pragma unroll
+                for (int w = 0; w < WPG; ++w) v += red[threadIdx.x * WPG + w];
+                rowv[threadIdx.x] = v;
+            }
+            if (WPG > 1) __syncthreads();
+            stream_epilogue(a, sp, row0, RC, rowv);
 #pragma unroll
             for (int rr = 0; rr < R; ++rr) acc[rr] = 0.f;
         }
