@@ -222,6 +222,53 @@ NEON_API int neon_cuda_model_decode_ms(neon_model_t m, float* ms);
 
 NEON_API int neon_cuda_model_free(neon_model_t m);
 
+/* ---- Tensor parallelism: one rank (process) per GPU ------------------------
+ * The reference declares an fp32 all-reduce across devices
+ * (rocm::MultiGpuCtx::all_reduce_sum, rawllm_rocm.hpp:531-562) but runs
+ * transformer_forward on one device. Here a decoder can be split over up to 8
+ * ranks: attention by KV head, the FFN by 32-row groups, the lm_head by
+ * vocabulary rows (neon_cuda_tp_shard), with attn_output and ffn_down summed
+ * across ranks by the communicator's one-shot all-reduce over peer memory.
+ *
+ * Setup on every rank, with the rank's device current:
+ *   neon_cuda_comm_create(rank, world, floats, &c)  floats >= neon_cuda_model_comm_floats()
+ *   neon_cuda_comm_ipc_handle(c, buf, &bytes)       exchange the handles between
+ *                                                   the ranks (any transport)
+ *   neon_cuda_comm_connect(c, all_handles, bytes)   handles of ranks 0..world-1, back to back
+ *   neon_cuda_model_create_tp(&cfg, c, &m)          then set_tensor with WHOLE tensors:
+ *                                                   each rank keeps its shard
+ * Every rank must then make the same calls in the same order (forward,
+ * generate, set_length): each collective waits for all ranks, at most the
+ * communicator's timeout (default 4 s), after which it reports an error and
+ * the communicator must be recreated. Never run two ranks on one GPU. */
+typedef struct neon_comm* neon_comm_t;
+
+NEON_API int neon_cuda_comm_create(int rank, int world, size_t max_floats, neon_comm_t* out);
+/* CUDA IPC handle of this rank's buffer; handle_out NULL: only the size. */
+NEON_API int neon_cuda_comm_ipc_handle(neon_comm_t c, void* handle_out, size_t* handle_bytes);
+NEON_API int neon_cuda_comm_connect(neon_comm_t c, const void* all_handles, size_t handle_bytes);
+/* Connect the n communicators of ranks 0..n-1 created in THIS process (one
+ * per device; peer access is enabled as needed). */
+NEON_API int neon_cuda_comm_connect_local(neon_comm_t* comms, int n);
+NEON_API int neon_cuda_comm_set_timeout(neon_comm_t c, double seconds);
+/* dOut[i] = (add ? dOut[i] : 0) + sum over ranks, in rank order, of dIn[i],
+ * for i < n, asynchronous on `stream`. */
+NEON_API int neon_cuda_comm_allreduce(neon_comm_t c, const float* dIn, float* dOut, size_t n, int add, void* stream);
+/* NEON_OK, or NEON_ERR_CUDA when a collective gave up waiting for a peer. */
+NEON_API int neon_cuda_comm_check(neon_comm_t c);
+NEON_API int neon_cuda_comm_free(neon_comm_t c);
+
+/* Receive-slot size (floats) a communicator needs for this model and world. */
+NEON_API int neon_cuda_model_comm_floats(const neon_model_config_t* cfg, int world, size_t* n);
+/* The part of a tensor of `role` that `rank` of `world` keeps: rows
+ * [range[0], range[1]) and columns [range[2], range[3]) of its GGUF shape
+ * [ne0 = columns, ne1 = rows]. Host-only; needs no GPU. */
+NEON_API int neon_cuda_tp_shard(const neon_model_config_t* cfg, int role, int rank, int world, size_t range[4]);
+/* A decoder over the ranks of `comm` (NULL: one device, as
+ * neon_cuda_model_create). neon_cuda_model_read_kv then returns this rank's
+ * KV heads only; logits and tokens are whole on every rank. */
+NEON_API int neon_cuda_model_create_tp(const neon_model_config_t* cfg, neon_comm_t comm, neon_model_t* out);
+
 /* Launch option: programmatic dependent launch (PDL) lets a matvec fetch its
  * weights while the previous kernel on the stream finishes; on by default. */
 NEON_API int neon_cuda_set_pdl(int enabled);

@@ -27,7 +27,7 @@ NVCC_FLAGS = [
     "--expt-relaxed-constexpr",
 ]
 
-SOURCES = ["neon_cuda.cu", "neon_decode.cu"]
+SOURCES = ["neon_cuda.cu", "neon_decode.cu", "neon_comm.cu"]
 
 
 def _nvcc() -> str:

@@ -421,13 +421,15 @@ __device__ __forceinline__ unsigned int float_order(float v) {
 
 // Greedy sampling: the first maximum of the logits (std::max_element,
 // NEON-3.cpp:471-474) over the whole grid. Each CTA folds its best (value,
-// index) into *key as (order(value) << 32) | ~index with atomicMax -- the
-// larger value wins, among equal values the lower index; the last CTA to
-// finish writes the token to *d_tok and out[*d_step], advances *d_step (and
-// *d_pos when `advance`), and clears *key and *counter for the next launch.
-__global__ void __launch_bounds__(256) argmax_kernel(const float* __restrict__ logits, int n,
+// index + index0) into *key as (order(value) << 32) | ~index with atomicMax --
+// the larger value wins, among equal values the lower index. With `finalize`,
+// the last CTA to finish writes the token to *d_tok and out[*d_step], advances
+// *d_step (and *d_pos when `advance`) and clears *key; without it (a
+// vocabulary shard of a tensor-parallel lm_head) *key is left for the ranks'
+// key exchange. The last CTA always clears *counter for the next launch.
+__global__ void __launch_bounds__(256) argmax_kernel(const float* __restrict__ logits, int n, int index0,
                                                      unsigned long long* key, unsigned int* counter, int* d_tok,
-                                                     int* out, int* d_step, int* d_pos, int advance) {
+                                                     int* out, int* d_step, int* d_pos, int advance, int finalize) {
     __shared__ float bv[8];
     __shared__ int bi[8];
     __shared__ bool last;
@@ -450,12 +452,14 @@ __global__ void __launch_bounds__(256) argmax_kernel(const float* __restrict__ l
         for (int k = 1; k < (int)(blockDim.x >> 5); ++k)
             if (bv[k] > best || (bv[k] == best && bi[k] < idx)) { best = bv[k]; idx = bi[k]; }
         if (idx != 0x7fffffff)
-            atomicMax(key, ((unsigned long long)float_order(best) << 32) | (unsigned long long)(0xFFFFFFFFu - (unsigned)idx));
+            atomicMax(key, ((unsigned long long)float_order(best) << 32) |
+                               (unsigned long long)(0xFFFFFFFFu - (unsigned)(idx + index0)));
         __threadfence();
         last = atomicAdd(counter, 1u) == gridDim.x - 1;
     }
     __syncthreads();
-    if (last && threadIdx.x == 0) {
+    if (last && threadIdx.x == 0 && !finalize) *counter = 0u;
+    if (last && threadIdx.x == 0 && finalize) {
         const unsigned long long k = atomicAdd(key, 0ull);
         const int tok = k ? (int)(0xFFFFFFFFu - (unsigned)(k & 0xFFFFFFFFull)) : 0;  // all NaN: element 0
         *d_tok = tok;
@@ -476,7 +480,18 @@ __global__ void __launch_bounds__(256) argmax_kernel(const float* __restrict__ l
 struct neon_model {
     neon_model_config_t cfg{};
     int device = 0;
+    // q_dim / kv_dim / n_ff_l are this rank's shares (the whole model on one device)
     size_t q_dim = 0, kv_dim = 0, rope_half = 0;
+    // tensor parallelism over `world` ranks: this rank keeps query heads
+    // [rank*n_head_l, ..), KV heads [rank*n_kv_l, ..), FFN rows [ff0, ff0+n_ff_l)
+    // and vocabulary rows [vocab0, vocab0+vocab_l)
+    neon_comm_impl* comm = nullptr;  // null: one device
+    int rank = 0, world = 1;
+    size_t n_head_l = 0, n_kv_l = 0, ff0 = 0, n_ff_l = 0, vocab0 = 0, vocab_l = 0;
+    neon_tensor_t head = nullptr;    // lm_head shard (tensor parallel only)
+    bool head_from_output = false;   // `head` was cut from output.weight, not the tied embedding
+    float* part = nullptr;           // partial sums of the column-split projections
+    float* logits_full = nullptr;    // all-gathered logits (tensor parallel only)
     neon_tensor_t embd = nullptr, output = nullptr;
     float* output_norm = nullptr;
     struct Layer {
@@ -534,6 +549,40 @@ int check_launch(const char* what) {
     return neon_internal::launched(1);
 }
 
+// Tensor-parallel shard of a GGUF tensor [ne0 = cols, ne1 = rows] kept by
+// `rank` of `world`: rows [r[0], r[1]) and columns [r[2], r[3]). Attention is
+// split by KV head (with its query heads), the FFN by 32-row groups of n_ff,
+// the lm_head by vocabulary rows; attn_output and ffn_down are split along
+// their input (the matching columns), so each rank's result is a partial sum
+// of the residual update. Norms and token_embd stay whole on every rank.
+int tp_shard(const neon_model_config_t& c, int role, int rank, int world, size_t r[4]) {
+    if (world < 1 || rank < 0 || rank >= world) return error(NEON_ERR_INVALID, "bad rank / world");
+    const size_t q_dim = (size_t)c.n_head * c.head_dim, kv_dim = (size_t)c.n_kv_head * c.head_dim;
+    const size_t nbff = c.n_ff / 32, W = (size_t)world, i = (size_t)rank;
+    const size_t ff0 = 32 * (nbff * i / W), ff1 = 32 * (nbff * (i + 1) / W);
+    size_t rows = 0, cols = 0;
+    switch (role) {
+        case NEON_ROLE_OUTPUT_NORM: case NEON_ROLE_ATTN_NORM: case NEON_ROLE_FFN_NORM: rows = 1; cols = c.n_embd; break;
+        case NEON_ROLE_TOKEN_EMBD: case NEON_ROLE_OUTPUT: rows = c.n_vocab; cols = c.n_embd; break;
+        case NEON_ROLE_ATTN_Q: rows = q_dim; cols = c.n_embd; break;
+        case NEON_ROLE_ATTN_K: case NEON_ROLE_ATTN_V: rows = kv_dim; cols = c.n_embd; break;
+        case NEON_ROLE_ATTN_OUT: rows = c.n_embd; cols = q_dim; break;
+        case NEON_ROLE_FFN_GATE: case NEON_ROLE_FFN_UP: rows = c.n_ff; cols = c.n_embd; break;
+        case NEON_ROLE_FFN_DOWN: rows = c.n_embd; cols = c.n_ff; break;
+        default: return error(NEON_ERR_INVALID, "unknown tensor role " + std::to_string(role));
+    }
+    r[0] = 0; r[1] = rows; r[2] = 0; r[3] = cols;
+    switch (role) {
+        case NEON_ROLE_OUTPUT: case NEON_ROLE_ATTN_Q: case NEON_ROLE_ATTN_K: case NEON_ROLE_ATTN_V:
+            r[0] = rows * i / W; r[1] = rows * (i + 1) / W; break;  // head-aligned: n_kv_head % world == 0
+        case NEON_ROLE_ATTN_OUT: r[2] = cols * i / W; r[3] = cols * (i + 1) / W; break;
+        case NEON_ROLE_FFN_GATE: case NEON_ROLE_FFN_UP: r[0] = ff0; r[1] = ff1; break;
+        case NEON_ROLE_FFN_DOWN: r[2] = ff0; r[3] = ff1; break;
+        default: break;
+    }
+    return NEON_OK;
+}
+
 int rmsnorm(neon_model* m, const float* x, const float* w, float* out, int rows) {
     rmsnorm_kernel<<<rows, kThreads, 0, m->stream>>>(x, w, out, (int)m->cfg.n_embd, m->cfg.norm_eps);
     return check_launch("rmsnorm_kernel");
@@ -545,6 +594,17 @@ int proj(neon_model* m, std::initializer_list<neon_proj_target_t> t, const float
     return neon_internal::matvec(v.data(), v.size(), x, x_stride, seq, m->stream, accumulate);
 }
 
+// h += W x for `seq` positions (attn_output, ffn_down). Tensor parallel: W is
+// this rank's column shard, its partial sum goes through the all-reduce, and
+// h += sum over ranks in rank order (identical on every rank).
+int residual_proj(neon_model* m, neon_tensor_t W, const float* x, size_t x_stride, size_t seq) {
+    const size_t n_embd = m->cfg.n_embd;
+    if (m->world == 1) return proj(m, {{W, m->h, n_embd}}, x, x_stride, seq, 1);
+    int rc = proj(m, {{W, m->part, n_embd}}, x, x_stride, seq, 0);
+    if (!rc) rc = neon_internal::comm_allreduce(m->comm, m->part, m->h, (long long)(seq * n_embd), 1, m->stream);
+    return rc;
+}
+
 // All layers for `seq` positions starting at *d_pos, tokens in `toks` (device).
 int run_layers(neon_model* m, const int* toks, int seq) {
     const auto& c = m->cfg;
@@ -553,7 +613,7 @@ int run_layers(neon_model* m, const int* toks, int seq) {
     embed_kernel<<<dim3((nb + 127) / 128, seq), 128, 0, m->stream>>>(E->qs, E->d, E->type, nb, toks, (int)c.n_vocab,
                                                                      m->h, m->d_err);
     int rc = check_launch("embed_kernel");
-    const size_t n_embd = c.n_embd, q_dim = m->q_dim, kv_dim = m->kv_dim, n_ff = c.n_ff;
+    const size_t n_embd = c.n_embd, q_dim = m->q_dim, kv_dim = m->kv_dim, n_ff = m->n_ff_l;
     const float scale = 1.0f / std::sqrt((float)c.head_dim);
     const int group = (int)(c.n_head / c.n_kv_head);
     const size_t attn_smem = sizeof(float) * c.ctx_len;
@@ -564,17 +624,17 @@ int run_layers(neon_model* m, const int* toks, int seq) {
         rc = rmsnorm(m, m->h, L.attn_norm, m->xn, seq);
         if (!rc) rc = proj(m, {{L.w[0], m->q, q_dim}, {L.w[1], m->k, kv_dim}, {L.w[2], m->v, kv_dim}}, m->xn, n_embd, seq, 0);
         if (!rc) {
-            rope_kv_kernel<<<seq, kThreads, 0, m->stream>>>(m->q, m->k, m->v, m->rope_cs, m->d_pos, (int)c.n_head,
-                                                            (int)c.n_kv_head, (int)c.head_dim, (int)m->rope_half,
+            rope_kv_kernel<<<seq, kThreads, 0, m->stream>>>(m->q, m->k, m->v, m->rope_cs, m->d_pos, (int)m->n_head_l,
+                                                            (int)m->n_kv_l, (int)c.head_dim, (int)m->rope_half,
                                                             (int)q_dim, (int)kv_dim, Kl, Vl);
             rc = check_launch("rope_kv_kernel");
         }
         if (!rc) {
-            attention_kernel<<<dim3(c.n_head, seq), kThreads, attn_smem, m->stream>>>(
+            attention_kernel<<<dim3((unsigned)m->n_head_l, seq), kThreads, attn_smem, m->stream>>>(
                 m->q, Kl, Vl, m->att, m->d_pos, (int)q_dim, (int)kv_dim, (int)c.head_dim, group, scale);
             rc = check_launch("attention_kernel");
         }
-        if (!rc) rc = proj(m, {{L.w[3], m->h, n_embd}}, m->att, q_dim, seq, 1);
+        if (!rc) rc = residual_proj(m, L.w[3], m->att, q_dim, seq);
         if (!rc) rc = rmsnorm(m, m->h, L.ffn_norm, m->xn, seq);
         if (!rc) rc = proj(m, {{L.gateup, m->gu, 2 * n_ff}}, m->xn, n_embd, seq, 0);
         if (!rc) {
@@ -582,15 +642,15 @@ int run_layers(neon_model* m, const int* toks, int seq) {
             swiglu_pairs_kernel<<<(int)std::min<long long>((n + 255) / 256, 4096), 256, 0, m->stream>>>(m->gu, m->act, n);
             rc = check_launch("swiglu_pairs_kernel");
         }
-        if (!rc) rc = proj(m, {{L.w[4], m->h, n_embd}}, m->act, n_ff, seq, 1);
+        if (!rc) rc = residual_proj(m, L.w[4], m->act, n_ff, seq);
     }
     return rc;
 }
 
 // logits of row `row` of h: rms_norm(output_norm) folded into the lm_head matvec
 int run_head(neon_model* m, int row) {
-    neon_tensor_t W = m->output ? m->output : m->embd;
-    neon_proj_target_t t{W, m->logits, (size_t)m->cfg.n_vocab};
+    neon_tensor_t W = m->world > 1 ? m->head : m->output ? m->output : m->embd;
+    neon_proj_target_t t{W, m->logits, m->vocab_l};
     neon_internal::MatvecExt ext;
     ext.norm_w = m->output_norm;
     ext.norm_eps = m->cfg.norm_eps;
@@ -605,7 +665,7 @@ int run_step(neon_model* m) {
     embed_kernel<<<dim3((nb + 127) / 128, 1), 128, 0, m->stream>>>(E->qs, E->d, E->type, nb, m->d_tok, (int)c.n_vocab,
                                                                    m->h, m->d_err);
     int rc = check_launch("embed_kernel");
-    const size_t n_embd = c.n_embd, q_dim = m->q_dim, kv_dim = m->kv_dim, n_ff = c.n_ff;
+    const size_t n_embd = c.n_embd, q_dim = m->q_dim, kv_dim = m->kv_dim, n_ff = m->n_ff_l;
     const float scale = 1.0f / std::sqrt((float)c.head_dim);
     const int group = (int)(c.n_head / c.n_kv_head);
     for (uint32_t li = 0; li < c.n_layer && !rc; ++li) {
@@ -629,7 +689,7 @@ int run_step(neon_model* m) {
             rc = neon_internal::matvec(t, 3, m->h, n_embd, 1, m->stream, 0, &ext);
         }
         if (!rc) {
-            const dim3 grid(c.n_kv_head, m->att_split);
+            const dim3 grid((unsigned)m->n_kv_l, m->att_split);
             attn_scores_kernel<<<grid, kThreads, 0, m->stream>>>(m->q, Kl, m->d_pos, (int)kv_dim, (int)c.head_dim, group,
                                                                  scale, m->att_split, (int)c.ctx_len, m->att_scores,
                                                                  m->att_pmax);
@@ -642,7 +702,7 @@ int run_step(neon_model* m) {
                 rc = check_launch("attn_values_kernel");
             }
         }
-        if (!rc) rc = proj(m, {{L.w[3], m->h, n_embd}}, m->att, q_dim, 1, 1);
+        if (!rc) rc = residual_proj(m, L.w[3], m->att, q_dim, 1);
         if (!rc) {
             // act = silu(gate) * up, (gate, up) = W x with x = rms_norm(h)
             const neon_proj_target_t t{L.gateup, m->act, n_ff};
@@ -655,20 +715,24 @@ int run_step(neon_model* m) {
             ext.pos_stride = &stride;
             rc = neon_internal::matvec(&t, 1, m->h, n_embd, 1, m->stream, 0, &ext);
         }
-        if (!rc) rc = proj(m, {{L.w[4], m->h, n_embd}}, m->act, n_ff, 1, 1);
+        if (!rc) rc = residual_proj(m, L.w[4], m->act, n_ff, 1);
     }
     return rc;
 }
 
 int launch_argmax(neon_model* m, int advance) {
-    const int grid = std::max(1, std::min<int>(148, (int)((m->cfg.n_vocab + 1023) / 1024)));
-    argmax_kernel<<<grid, 256, 0, m->stream>>>(m->logits, (int)m->cfg.n_vocab, m->am_key, m->am_count, m->d_tok,
-                                               m->d_out, m->d_step, m->d_pos, advance);
-    return check_launch("argmax_kernel");
+    const int grid = std::max(1, std::min<int>(148, (int)((m->vocab_l + 1023) / 1024)));
+    argmax_kernel<<<grid, 256, 0, m->stream>>>(m->logits, (int)m->vocab_l, (int)m->vocab0, m->am_key, m->am_count,
+                                               m->d_tok, m->d_out, m->d_step, m->d_pos, advance, m->world == 1);
+    int rc = check_launch("argmax_kernel");
+    if (!rc && m->world > 1)
+        rc = neon_internal::comm_argmax(m->comm, m->am_key, m->d_tok, m->d_out, m->d_step, m->d_pos, advance, m->stream);
+    return rc;
 }
 
 int check_ready(neon_model* m) {
     if (!m->embd || !m->output_norm) return error(NEON_ERR_INVALID, "forward(): token_embd.weight / output_norm.weight not set");
+    if (m->world > 1 && !m->head) return error(NEON_ERR_INVALID, "forward(): lm_head shard not set");
     for (uint32_t i = 0; i < m->cfg.n_layer; ++i) {
         auto& L = m->layers[i];
         if (!L.attn_norm || !L.ffn_norm)
@@ -688,6 +752,10 @@ int sync_and_check(neon_model* m) {
     if (e & 2u) {
         DEC_TRY(cudaMemset(m->d_err, 0, sizeof(unsigned)));
         return error(NEON_ERR_INVALID, "forward(): token id out of vocab range");
+    }
+    if (m->world > 1) {
+        const int rc = neon_cuda_comm_check(static_cast<neon_comm*>(m->comm));
+        if (rc) return rc;
     }
     return neon_internal::check_device_error(m->device);
 }
@@ -709,6 +777,8 @@ int forward_device(neon_model* m, const int32_t* tokens_host, size_t n) {
         if (rc) return rc;
         if (off + seq == n) {
             rc = run_head(m, seq - 1);
+            if (!rc && m->world > 1)
+                rc = neon_internal::comm_allgather(m->comm, m->logits, m->logits_full, (long long)m->cfg.n_vocab, m->stream);
             if (rc) return rc;
         }
         DEC_TRY(cudaStreamSynchronize(m->stream));  // pos / tokens are reused by the next chunk
@@ -720,7 +790,22 @@ int forward_device(neon_model* m, const int32_t* tokens_host, size_t n) {
 
 extern "C" {
 
+int neon_cuda_model_comm_floats(const neon_model_config_t* cfg, int world, size_t* n) {
+    if (!cfg || !n || world < 1) return error(NEON_ERR_INVALID, "bad argument");
+    *n = std::max<size_t>((size_t)kMaxChunk * cfg->n_embd, ((size_t)cfg->n_vocab + world - 1) / world);
+    return NEON_OK;
+}
+
+int neon_cuda_tp_shard(const neon_model_config_t* cfg, int role, int rank, int world, size_t range[4]) {
+    if (!cfg || !range) return error(NEON_ERR_INVALID, "null argument");
+    return tp_shard(*cfg, role, rank, world, range);
+}
+
 int neon_cuda_model_create(const neon_model_config_t* cfg, neon_model_t* out) {
+    return neon_cuda_model_create_tp(cfg, nullptr, out);
+}
+
+int neon_cuda_model_create_tp(const neon_model_config_t* cfg, neon_comm_t comm, neon_model_t* out) {
     if (!cfg || !out) return error(NEON_ERR_INVALID, "null argument");
     *out = nullptr;
     const auto& c = *cfg;
@@ -734,11 +819,42 @@ int neon_cuda_model_create(const neon_model_config_t* cfg, neon_model_t* out) {
     if (c.ctx_len > (uint32_t)kMaxCtx) return error(NEON_ERR_UNSUPPORTED, "ctx_len above 16384");
     if (c.n_head / c.n_kv_head > 8) return error(NEON_ERR_UNSUPPORTED, "more than 8 query heads per KV head");
     if (c.rope_dim_count > c.head_dim) return error(NEON_ERR_INVALID, "rope dimension count above head_dim");
+    const int world = comm ? comm->peers.world : 1, rank = comm ? comm->peers.rank : 0;
+    if (comm) {
+        if (!comm->connected) return error(NEON_ERR_INVALID, "communicator not connected");
+        int dev = -1;
+        cudaGetDevice(&dev);
+        if (dev != comm->device) return error(NEON_ERR_INVALID, "the communicator lives on another device");
+        if (c.n_kv_head % (uint32_t)world != 0)
+            return error(NEON_ERR_UNSUPPORTED, "tensor parallelism needs n_kv_head divisible by the number of ranks");
+        if (c.n_ff / 32 < (uint32_t)world || c.n_vocab < (uint32_t)world)
+            return error(NEON_ERR_UNSUPPORTED, "n_ff / 32 and n_vocab must be at least the number of ranks");
+        size_t need = 0;
+        neon_cuda_model_comm_floats(cfg, world, &need);
+        if ((size_t)comm->peers.max_floats < need)
+            return error(NEON_ERR_INVALID, "communicator buffer below neon_cuda_model_comm_floats() = " + std::to_string(need));
+    }
     auto* m = new neon_model();
     m->cfg = c;
     cudaGetDevice(&m->device);
-    m->q_dim = (size_t)c.n_head * c.head_dim;
-    m->kv_dim = (size_t)c.n_kv_head * c.head_dim;
+    m->comm = world > 1 ? comm : nullptr;
+    m->world = world;
+    m->rank = rank;
+    {
+        size_t r[4];
+        tp_shard(c, NEON_ROLE_ATTN_Q, rank, world, r);
+        m->q_dim = r[1] - r[0];
+        tp_shard(c, NEON_ROLE_ATTN_K, rank, world, r);
+        m->kv_dim = r[1] - r[0];
+        tp_shard(c, NEON_ROLE_FFN_GATE, rank, world, r);
+        m->ff0 = r[0];
+        m->n_ff_l = r[1] - r[0];
+        tp_shard(c, NEON_ROLE_OUTPUT, rank, world, r);
+        m->vocab0 = r[0];
+        m->vocab_l = r[1] - r[0];
+    }
+    m->n_head_l = c.n_head / world;
+    m->n_kv_l = c.n_kv_head / world;
     m->rope_half = c.rope_dim_count ? c.rope_dim_count / 2 : c.head_dim / 2;
     m->layers.resize(c.n_layer);
     int rc = NEON_OK;
@@ -756,22 +872,26 @@ int neon_cuda_model_create(const neon_model_config_t* cfg, neon_model_t* out) {
     A((void**)&m->k, sizeof(float) * S * m->kv_dim);
     A((void**)&m->v, sizeof(float) * S * m->kv_dim);
     A((void**)&m->att, sizeof(float) * S * m->q_dim);
-    A((void**)&m->gu, sizeof(float) * S * 2 * c.n_ff);
-    A((void**)&m->act, sizeof(float) * S * c.n_ff);
+    A((void**)&m->gu, sizeof(float) * S * 2 * m->n_ff_l);
+    A((void**)&m->act, sizeof(float) * S * m->n_ff_l);
+    if (world > 1) {
+        A((void**)&m->part, sizeof(float) * S * c.n_embd);
+        A((void**)&m->logits_full, sizeof(float) * c.n_vocab);
+    }
     A((void**)&m->am_key, sizeof(unsigned long long));
     A((void**)&m->am_count, sizeof(unsigned int));
     // decode attention: splits so that (KV heads x splits) fills about two CTAs per SM
     {
         int sms = neon_internal::device_sms(m->device);
         if (sms <= 0) sms = 148;
-        m->att_split = (int)std::max<long long>(1, std::min<long long>((c.ctx_len + 31) / 32, (2LL * sms) / c.n_kv_head));
+        m->att_split = (int)std::max<long long>(1, std::min<long long>((c.ctx_len + 31) / 32, (2LL * sms) / (long long)m->n_kv_l));
     }
-    A((void**)&m->att_scores, sizeof(float) * (size_t)c.n_head * c.ctx_len);
-    A((void**)&m->att_pmax, sizeof(float) * (size_t)c.n_head * m->att_split);
-    A((void**)&m->att_psum, sizeof(float) * (size_t)c.n_head * m->att_split);
-    A((void**)&m->att_pout, sizeof(float) * (size_t)c.n_head * m->att_split * c.head_dim);
-    A((void**)&m->att_count, sizeof(unsigned int) * c.n_kv_head);
-    A((void**)&m->logits, sizeof(float) * c.n_vocab);
+    A((void**)&m->att_scores, sizeof(float) * m->n_head_l * c.ctx_len);
+    A((void**)&m->att_pmax, sizeof(float) * m->n_head_l * m->att_split);
+    A((void**)&m->att_psum, sizeof(float) * m->n_head_l * m->att_split);
+    A((void**)&m->att_pout, sizeof(float) * m->n_head_l * m->att_split * c.head_dim);
+    A((void**)&m->att_count, sizeof(unsigned int) * m->n_kv_l);
+    A((void**)&m->logits, sizeof(float) * m->vocab_l);
     A((void**)&m->d_tokens, sizeof(int) * S);
     A((void**)&m->d_tok, sizeof(int));
     A((void**)&m->d_pos, sizeof(int));
@@ -796,7 +916,7 @@ int neon_cuda_model_create(const neon_model_config_t* cfg, neon_model_t* out) {
             cudaMemset(m->d_err, 0, sizeof(unsigned)) != cudaSuccess || cudaMemset(m->K, 0, kv_bytes) != cudaSuccess ||
             cudaMemset(m->am_key, 0, sizeof(unsigned long long)) != cudaSuccess ||
             cudaMemset(m->am_count, 0, sizeof(unsigned int)) != cudaSuccess ||
-            cudaMemset(m->att_count, 0, sizeof(unsigned int) * c.n_kv_head) != cudaSuccess ||
+            cudaMemset(m->att_count, 0, sizeof(unsigned int) * m->n_kv_l) != cudaSuccess ||
             cudaMemset(m->V, 0, kv_bytes) != cudaSuccess)
             rc = error(NEON_ERR_CUDA, "model initialisation copies failed");
     }
@@ -831,16 +951,17 @@ int neon_cuda_model_set_tensor(neon_model_t m, int role, int layer, const uint8_
         }
         return NEON_OK;
     }
-    // projections: expected GGUF ne = [cols, rows]
+    // projections: expected GGUF ne = [cols, rows] of the whole tensor; a
+    // tensor-parallel rank keeps its shard (tp_shard)
+    size_t sh[4];
+    int rc0 = tp_shard(c, role, m->rank, m->world, sh);
+    if (rc0) return rc0;
     size_t want0 = 0, want1 = 0;
-    switch (role) {
-        case NEON_ROLE_TOKEN_EMBD: case NEON_ROLE_OUTPUT: want0 = c.n_embd; want1 = c.n_vocab; break;
-        case NEON_ROLE_ATTN_Q: want0 = c.n_embd; want1 = m->q_dim; break;
-        case NEON_ROLE_ATTN_K: case NEON_ROLE_ATTN_V: want0 = c.n_embd; want1 = m->kv_dim; break;
-        case NEON_ROLE_ATTN_OUT: want0 = m->q_dim; want1 = c.n_embd; break;
-        case NEON_ROLE_FFN_GATE: case NEON_ROLE_FFN_UP: want0 = c.n_embd; want1 = c.n_ff; break;
-        case NEON_ROLE_FFN_DOWN: want0 = c.n_ff; want1 = c.n_embd; break;
-        default: return error(NEON_ERR_INVALID, "unknown tensor role " + std::to_string(role));
+    {
+        size_t whole[4];
+        tp_shard(c, role, 0, 1, whole);
+        want0 = whole[3];
+        want1 = whole[1];
     }
     if (ne0 != want0 || ne1 != want1)
         return error(NEON_ERR_INVALID, "NANITY: tensor of role " + std::to_string(role) + " has shape [" + std::to_string(ne0) +
@@ -851,21 +972,24 @@ int neon_cuda_model_set_tensor(neon_model_t m, int role, int layer, const uint8_
     if (role == NEON_ROLE_FFN_GATE || role == NEON_ROLE_FFN_UP) {
         // held until both halves are present, then uploaded as one tensor whose
         // row 2i is gate row i and row 2i+1 up row i (same bytes, same math)
+        // (a tensor-parallel rank keeps rows [ff0, ff0 + n_ff_l) of both)
         auto& L = m->layers[layer];
         const size_t row_b = ggml_type == NEON_GGML_Q4_0 ? ne0 / 32 * 18 : ggml_type == NEON_GGML_Q8_0 ? ne0 / 32 * 34 : 0;
         if (row_b == 0) return error(NEON_ERR_UNSUPPORTED, "ffn_gate / ffn_up must be Q4_0 or Q8_0");
         if (nbytes < row_b * ne1) return error(NEON_ERR_INVALID, "tensor bytes shorter than its shape");
-        (role == NEON_ROLE_FFN_GATE ? L.gate_bytes : L.up_bytes).assign(host_bytes, host_bytes + row_b * ne1);
+        const size_t r0 = sh[0], nr = sh[1] - sh[0];
+        (role == NEON_ROLE_FFN_GATE ? L.gate_bytes : L.up_bytes)
+            .assign(host_bytes + r0 * row_b, host_bytes + (r0 + nr) * row_b);
         (role == NEON_ROLE_FFN_GATE ? L.gate_type : L.up_type) = ggml_type;
         if (L.gate_bytes.empty() || L.up_bytes.empty()) return NEON_OK;
         if (L.gate_type != L.up_type) return error(NEON_ERR_UNSUPPORTED, "ffn_gate and ffn_up must share a quant type");
-        std::vector<uint8_t> inter(2 * row_b * ne1);
-        for (size_t r = 0; r < ne1; ++r) {
+        std::vector<uint8_t> inter(2 * row_b * nr);
+        for (size_t r = 0; r < nr; ++r) {
             std::memcpy(inter.data() + (2 * r) * row_b, L.gate_bytes.data() + r * row_b, row_b);
             std::memcpy(inter.data() + (2 * r + 1) * row_b, L.up_bytes.data() + r * row_b, row_b);
         }
         neon_tensor_t t = nullptr;
-        int rc = neon_cuda_upload(inter.data(), ggml_type, 2 * ne1, ne0, NEON_SHARD_NONE, 0, 1, &t);
+        int rc = neon_cuda_upload(inter.data(), ggml_type, 2 * nr, ne0, NEON_SHARD_NONE, 0, 1, &t);
         if (rc) return rc;
         if (L.gateup) neon_cuda_free(L.gateup);
         L.gateup = t;
@@ -875,8 +999,25 @@ int neon_cuda_model_set_tensor(neon_model_t m, int role, int layer, const uint8_
         L.up_bytes.shrink_to_fit();
         return NEON_OK;
     }
+    int mode = NEON_SHARD_NONE;
+    if (m->world > 1) {
+        if (sh[0] != 0 || sh[1] != ne1) mode = NEON_SHARD_ROWS;
+        else if (sh[2] != 0 || sh[3] != ne0) mode = NEON_SHARD_COLS;
+    }
+    if (m->world > 1 && (role == NEON_ROLE_OUTPUT || (role == NEON_ROLE_TOKEN_EMBD && !m->head_from_output))) {
+        // the lm_head's vocabulary shard (of output.weight, or of the tied embedding)
+        neon_tensor_t hs = nullptr;
+        int rc = neon_cuda_upload(host_bytes, ggml_type, ne1, ne0, NEON_SHARD_ROWS, m->rank, m->world, &hs);
+        if (rc) return rc;
+        if (m->head) neon_cuda_free(m->head);
+        m->head = hs;
+        if (role == NEON_ROLE_OUTPUT) {
+            m->head_from_output = true;
+            return NEON_OK;
+        }
+    }
     neon_tensor_t t = nullptr;
-    int rc = neon_cuda_upload(host_bytes, ggml_type, ne1, ne0, NEON_SHARD_NONE, 0, 1, &t);
+    int rc = neon_cuda_upload(host_bytes, ggml_type, ne1, ne0, mode, m->rank, m->world, &t);
     if (rc) return rc;
     neon_tensor_t* slot = nullptr;
     if (role == NEON_ROLE_TOKEN_EMBD) slot = &m->embd;
@@ -906,7 +1047,9 @@ int neon_cuda_model_forward(neon_model_t m, const int32_t* tokens, size_t n, flo
     if (!rc) rc = sync_and_check(m);
     if (rc) return rc;
     m->length += n;
-    if (logits_host) DEC_TRY(cudaMemcpy(logits_host, m->logits, sizeof(float) * m->cfg.n_vocab, cudaMemcpyDeviceToHost));
+    if (logits_host)
+        DEC_TRY(cudaMemcpy(logits_host, m->world > 1 ? m->logits_full : m->logits, sizeof(float) * m->cfg.n_vocab,
+                           cudaMemcpyDeviceToHost));
     return NEON_OK;
 }
 
@@ -1007,6 +1150,7 @@ int neon_cuda_model_free(neon_model_t m) {
     if (m->step_graph) cudaGraphExecDestroy(m->step_graph);
     neon_cuda_free(m->embd);
     neon_cuda_free(m->output);
+    neon_cuda_free(m->head);
     for (auto& L : m->layers) {
         for (auto* w : L.w) neon_cuda_free(w);
         neon_cuda_free(L.gateup);

@@ -22,7 +22,60 @@ struct neon_tensor {
     size_t bytes;
 };
 
+// Tensor-parallel communicator: one per rank (process, device). Every rank
+// owns a buffer in its own HBM, exported with CUDA IPC and opened by all
+// peers; collectives push data into the peers' buffers with plain P2P stores
+// and publish an epoch flag, then wait (bounded) for every peer's flag.
+constexpr int kCommMaxRanks = 8;
+constexpr int kCommSlices = 32;  // CTAs of the all-reduce kernel (one flag each)
+
+struct CommPeers {  // passed to kernels by value
+    unsigned char* base[kCommMaxRanks];  // each rank's buffer, mapped here (own: base[rank])
+    int rank, world;
+    long long max_floats;                // capacity of one receive slot, in floats
+};
+
+// Buffer layout (bytes from base): two parity halves of `world` receive slots
+// of max_floats floats, then flags[src][slice], then argmax keys
+// [parity][src] (8 bytes each) and their flags [src].
+__host__ __device__ inline long long comm_recv_off(const CommPeers& c, int parity, int src) {
+    return ((long long)parity * c.world + src) * c.max_floats * 4;
+}
+__host__ __device__ inline long long comm_flags_off(const CommPeers& c) { return 2LL * c.world * c.max_floats * 4; }
+__host__ __device__ inline long long comm_keys_off(const CommPeers& c) {
+    return comm_flags_off(c) + (long long)kCommMaxRanks * kCommSlices * 4;
+}
+__host__ __device__ inline long long comm_kflags_off(const CommPeers& c) {
+    return comm_keys_off(c) + 2LL * kCommMaxRanks * 8;
+}
+__host__ __device__ inline long long comm_bytes(const CommPeers& c) {
+    return comm_kflags_off(c) + (long long)kCommMaxRanks * 4 + 256;
+}
+
+struct neon_comm_impl {
+    int device = 0;
+    CommPeers peers{};
+    unsigned char* local = nullptr;        // this rank's buffer
+    unsigned int* epochs = nullptr;        // device: per-slice call count (+1: key exchanges)
+    unsigned int* err = nullptr;           // device error word: bit 0 = a peer wait timed out
+    unsigned long long timeout_ns = 4000000000ull;  // bound of every wait on a peer
+    bool connected = false;
+    bool opened_ipc = false;               // peers' buffers were opened with CUDA IPC
+    std::string ipc_handle;                // cudaIpcMemHandle_t bytes
+};
+struct neon_comm : neon_comm_impl {};  // the public handle type (neon_comm_t)
+
 namespace neon_internal {
+
+// out[i] (+)= sum over ranks, in rank order, of in[i] for i < n, on stream `st`.
+int comm_allreduce(neon_comm_impl* c, const float* in, float* out, long long n, int add, cudaStream_t st);
+// out[n*r/world .. n*(r+1)/world) = rank r's `in` (its shard of the n rows), for every r.
+int comm_allgather(neon_comm_impl* c, const float* in, float* out, long long n, cudaStream_t st);
+// Greedy-sampling exchange: every rank's argmax key (*key, the packed
+// (value, index) of argmax_kernel) is compared; the winner's index becomes
+// *d_tok and out[*d_step]; *d_step += 1, *d_pos += advance, *key = 0.
+int comm_argmax(neon_comm_impl* c, unsigned long long* key, int* d_tok, int* out, int* d_step, int* d_pos,
+                int advance, cudaStream_t st);
 
 // Decode-step options of a one-position matvec launch (seq == 1 only):
 // RMSNorm of X folded into the X staging, and per-target epilogues (the

@@ -69,6 +69,17 @@ C_ENTRY_POINTS = (
     "neon_cuda_model_read_kv",
     "neon_cuda_model_decode_ms",
     "neon_cuda_model_free",
+    "neon_cuda_comm_create",
+    "neon_cuda_comm_ipc_handle",
+    "neon_cuda_comm_connect",
+    "neon_cuda_comm_connect_local",
+    "neon_cuda_comm_set_timeout",
+    "neon_cuda_comm_allreduce",
+    "neon_cuda_comm_check",
+    "neon_cuda_comm_free",
+    "neon_cuda_model_comm_floats",
+    "neon_cuda_tp_shard",
+    "neon_cuda_model_create_tp",
     "neon_cuda_set_pdl",
 )
 
@@ -136,6 +147,17 @@ def load(path: str | None = None) -> C.CDLL:
         L.neon_cuda_model_read_kv.argtypes = [_vp, C.c_int, _sz, _vp, _vp]
         L.neon_cuda_model_decode_ms.argtypes = [_vp, C.POINTER(C.c_float)]
         L.neon_cuda_model_free.argtypes = [_vp]
+        L.neon_cuda_comm_create.argtypes = [C.c_int, C.c_int, _sz, C.POINTER(_vp)]
+        L.neon_cuda_comm_ipc_handle.argtypes = [_vp, _vp, C.POINTER(_sz)]
+        L.neon_cuda_comm_connect.argtypes = [_vp, _vp, _sz]
+        L.neon_cuda_comm_connect_local.argtypes = [C.POINTER(_vp), C.c_int]
+        L.neon_cuda_comm_set_timeout.argtypes = [_vp, C.c_double]
+        L.neon_cuda_comm_allreduce.argtypes = [_vp, _vp, _vp, _sz, C.c_int, _vp]
+        L.neon_cuda_comm_check.argtypes = [_vp]
+        L.neon_cuda_comm_free.argtypes = [_vp]
+        L.neon_cuda_model_comm_floats.argtypes = [C.POINTER(_ModelConfig), C.c_int, C.POINTER(_sz)]
+        L.neon_cuda_tp_shard.argtypes = [C.POINTER(_ModelConfig), C.c_int, C.c_int, C.c_int, C.POINTER(_sz)]
+        L.neon_cuda_model_create_tp.argtypes = [C.POINTER(_ModelConfig), _vp, C.POINTER(_vp)]
         _lib = L
         return L
 
@@ -323,22 +345,106 @@ def proj_all_positions_multi(targets, X: np.ndarray, x_stride: int, seq: int, po
 # the decode step (transformer_forward / run_generation on the device)
 # ---------------------------------------------------------------------------
 
+def _config(cfg) -> _ModelConfig:
+    return _ModelConfig(*[getattr(cfg, f) for f in ("n_vocab", "n_embd", "n_layer", "n_head", "n_kv_head",
+                                                    "head_dim", "n_ff", "ctx_len")],
+                        cfg.rope_base, cfg.rope_scale, cfg.rope_dim_count, cfg.norm_eps)
+
+
+def tp_shard(cfg, role: int, rank: int, world: int):
+    """(row0, row1, col0, col1): the part of a GGUF tensor of ``role`` that
+    tensor-parallel ``rank`` of ``world`` keeps (host-only, no GPU needed)."""
+    r = (_sz * 4)()
+    _check(load().neon_cuda_tp_shard(C.byref(_config(cfg)), int(role), int(rank), int(world), r))
+    return tuple(int(v) for v in r)
+
+
+def model_comm_floats(cfg, world: int) -> int:
+    """Receive-slot size (floats) a communicator needs for this model."""
+    n = _sz()
+    _check(load().neon_cuda_model_comm_floats(C.byref(_config(cfg)), int(world), C.byref(n)))
+    return n.value
+
+
+class Comm:
+    """Tensor-parallel communicator of one rank (neon_cuda_comm_*): a buffer
+    in this GPU's HBM that every peer maps; collectives are one kernel each
+    over peer memory. Create it with the rank's device current."""
+
+    def __init__(self, rank: int, world: int, max_floats: int):
+        L = load()
+        h = _vp()
+        _check(L.neon_cuda_comm_create(int(rank), int(world), int(max_floats), C.byref(h)))
+        self.handle = h.value
+        self.rank, self.world = int(rank), int(world)
+        self._fin = weakref.finalize(self, L.neon_cuda_comm_free, self.handle)
+
+    def ipc_handle(self) -> bytes:
+        n = _sz(0)
+        _check(load().neon_cuda_comm_ipc_handle(self.handle, None, C.byref(n)))
+        buf = C.create_string_buffer(n.value)
+        _check(load().neon_cuda_comm_ipc_handle(self.handle, buf, C.byref(n)))
+        return buf.raw
+
+    def connect(self, handles) -> None:
+        """Open the peers' buffers from the IPC handles of ranks 0..world-1."""
+        handles = list(handles)
+        if len(handles) != self.world or len({len(h) for h in handles}) != 1:
+            raise NeonError("connect() needs one IPC handle per rank, all of one size")
+        blob = b"".join(handles)
+        _check(load().neon_cuda_comm_connect(self.handle, blob, len(handles[0])))
+
+    @classmethod
+    def from_process_group(cls, max_floats: int, group=None) -> "Comm":
+        """Create and connect over an initialised torch.distributed group (any
+        backend; it only carries the IPC handles)."""
+        import torch.distributed as dist
+
+        c = cls(dist.get_rank(group), dist.get_world_size(group), max_floats)
+        handles = [None] * c.world
+        dist.all_gather_object(handles, c.ipc_handle(), group=group)
+        c.connect(handles)
+        return c
+
+    @staticmethod
+    def connect_local(comms) -> None:
+        """Connect the communicators of ranks 0..n-1 created in this process."""
+        arr = (_vp * len(comms))(*[c.handle for c in comms])
+        _check(load().neon_cuda_comm_connect_local(arr, len(comms)))
+
+    def set_timeout(self, seconds: float) -> None:
+        _check(load().neon_cuda_comm_set_timeout(self.handle, float(seconds)))
+
+    def allreduce(self, x, out, n: int | None = None, add: bool = False, stream=None) -> None:
+        """out (+)= sum over ranks of x (device buffers, e.g. torch tensors)."""
+        if n is None:
+            n = x.numel()
+        _check(load().neon_cuda_comm_allreduce(self.handle, _ptr(x), _ptr(out), int(n), 1 if add else 0,
+                                               _stream(stream)))
+
+    def check(self) -> None:
+        _check(load().neon_cuda_comm_check(self.handle))
+
+    def free(self) -> None:
+        self._fin()
+
+
 class Model:
     """A NANITY decoder on the current device (neon_cuda_model_*).
 
     ``cfg`` has the fields of engine::Config the forward pass reads (n_vocab,
     n_embd, n_layer, n_head, n_kv_head, head_dim, n_ff, ctx_len, rope_base,
     rope_scale, rope_dim_count, norm_eps); ``tensors`` yields (role, layer,
-    GGUF bytes, ggml type, ne0, ne1)."""
+    GGUF bytes, ggml type, ne0, ne1). With a connected :class:`Comm`, the
+    model is this rank's tensor-parallel share; every rank passes the WHOLE
+    tensors and makes the same calls in the same order."""
 
-    def __init__(self, cfg, tensors=()):
+    def __init__(self, cfg, tensors=(), comm: Comm | None = None):
         L = load()
         self.cfg = cfg
-        c = _ModelConfig(*[getattr(cfg, f) for f in ("n_vocab", "n_embd", "n_layer", "n_head", "n_kv_head",
-                                                     "head_dim", "n_ff", "ctx_len")],
-                         cfg.rope_base, cfg.rope_scale, cfg.rope_dim_count, cfg.norm_eps)
+        self.comm = comm
         h = _vp()
-        _check(L.neon_cuda_model_create(C.byref(c), C.byref(h)))
+        _check(L.neon_cuda_model_create_tp(C.byref(_config(cfg)), comm.handle if comm else None, C.byref(h)))
         self.handle = h.value
         self._fin = weakref.finalize(self, L.neon_cuda_model_free, self.handle)
         for t in tensors:
@@ -375,7 +481,9 @@ class Model:
         _check(load().neon_cuda_model_set_length(self.handle, n))
 
     def read_kv(self, layer: int, n: int):
-        kv = self.cfg.n_kv_head * self.cfg.head_dim
+        """K and V cache rows [0, n) of `layer` (this rank's KV heads)."""
+        world = self.comm.world if self.comm else 1
+        kv = self.cfg.n_kv_head // world * self.cfg.head_dim
         k = np.zeros((n, kv), np.float32)
         v = np.zeros((n, kv), np.float32)
         _check(load().neon_cuda_model_read_kv(self.handle, layer, n, k.ctypes.data, v.ctypes.data))

@@ -1,0 +1,82 @@
+"""Tensor-parallel decode on two GPUs (one process per GPU, launched with
+torch.distributed.run): the peer-memory all-reduce bit-exact against host
+sums, and the split decoder against the reference's greedy tokens -- the small
+model's golden generation and, for the Qwen3-0.6B-shaped decoder, the same
+tokens as one GPU and as the reference's own transformer_forward. Skipped on
+a host with fewer than two GPUs."""
+import os
+import signal
+import socket
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+
+import oracle as O
+import synth as S
+from conftest import MODEL_L2_RTOL, load_golden, rel_l2
+
+pytestmark = pytest.mark.gpu
+torch = pytest.importorskip("torch")
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+QWEN_PROMPT, QWEN_STEPS = 128, 32
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.fixture(scope="module")
+def tp2(tmp_path_factory):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    out = tmp_path_factory.mktemp("tp2") / "rank0.npz"
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes", "1", "--nproc-per-node", "2",
+           "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
+           os.path.join(HERE, "tp_gpu_worker.py"), "--out", str(out),
+           "--qwen-prompt", str(QWEN_PROMPT), "--qwen-steps", str(QWEN_STEPS)]
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", OMP_NUM_THREADS="4")
+    p = subprocess.Popen(cmd, env=env, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, start_new_session=True)
+    try:
+        log, _ = p.communicate(timeout=900)
+    except subprocess.TimeoutExpired:
+        os.killpg(p.pid, signal.SIGTERM)
+        log, _ = p.communicate()
+        pytest.fail("tensor-parallel worker timed out:\n" + log.decode(errors="replace")[-4000:])
+    text = log.decode(errors="replace")
+    assert p.returncode == 0, text[-4000:]
+    print(text[-2000:])
+    return dict(np.load(out))
+
+
+def test_allreduce_bit_exact(tp2):
+    for k, v in tp2.items():
+        if k.startswith("allreduce_"):
+            assert float(v) == 0.0, k
+
+
+def test_tiny_golden_tokens_and_logits(tp2):
+    g = load_golden("decode_tiny.npz")
+    assert np.array_equal(tp2["tiny_tokens"], g["tokens"])
+    for i, lg in enumerate(tp2["tiny_logits"]):
+        assert rel_l2(lg, g["logits"][i]) <= MODEL_L2_RTOL, f"step {i}"
+        assert int(np.argmax(lg)) == int(np.argmax(g["logits"][i]))
+    # each rank holds its own KV heads
+    assert tuple(tp2["tiny_k0_shape"]) == (len(g["prompt"]), 2 // 2 * 64)
+
+
+def test_qwen_split_matches_one_gpu_and_reference(tp2):
+    assert np.array_equal(tp2["qwen_tokens"], tp2["qwen_tokens_1gpu"])
+    print(f"decode {QWEN_STEPS} tokens: 2 GPUs {float(tp2['qwen_tp_ms']):.2f} ms, "
+          f"1 GPU {float(tp2['qwen_1gpu_ms']):.2f} ms")
+    if not O.ref_available():
+        pytest.skip("oracle/_ref not built")
+    cfg = S.QWEN3_0_6B.with_(ctx_len=QWEN_PROMPT + QWEN_STEPS + 1)
+    ref = O.Model(cfg, list(S.model_tensors(cfg, seed=21)), "reference")
+    toks, _ = ref.generate_greedy(S.prompt_tokens(QWEN_PROMPT, cfg.n_vocab, 22), QWEN_STEPS)
+    ref.close()
+    assert np.array_equal(tp2["qwen_tokens"], toks)
