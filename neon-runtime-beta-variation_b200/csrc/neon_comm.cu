@@ -36,11 +36,17 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstring>
 #include <string>
 
 using neon_internal::cuda_error;
 using neon_internal::error;
+
+namespace {
+constexpr int kEpochWords = kCommSlices + 3;  // slices, key exchange, fused calls, fused counter
+std::atomic<int> g_fused{1};
+}  // namespace
 
 namespace {
 
@@ -189,9 +195,21 @@ __global__ void __launch_bounds__(256) comm_reduce_kernel(CommPeers c, const flo
     if (threadIdx.x == 0) epochs[slice] = epoch;
 }
 
-// One warp: lane p pushes this rank's argmax key to rank p and lane src waits
-// for rank src's key; the largest key wins (argmax_kernel's packing: the
-// larger value, among equal values the lower global index).
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64c(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_relaxed_sys_u64c(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// One warp, LL words: lane p stores this rank's argmax key -- its high and
+// low halves as two words tagged with the exchange number -- into slot
+// [parity][rank] of rank p, and lane src polls (bounded) slot [parity][src]
+// of this rank. The largest key wins (argmax_kernel's packing: the larger
+// value, among equal values the lower global index).
 __global__ void comm_argmax_kernel(CommPeers c, unsigned long long* key, int* d_tok, int* out, int* d_step, int* d_pos,
                                    int advance, unsigned int* __restrict__ epochs, unsigned int* __restrict__ err,
                                    unsigned long long timeout) {
@@ -202,20 +220,33 @@ __global__ void comm_argmax_kernel(CommPeers c, unsigned long long* key, int* d_
     const unsigned int epoch = epochs[kCommSlices] + 1u;
     const int parity = (int)(epoch & 1u);
     const unsigned long long mine = __ldcg(key);
+    const long long keys = comm_ll_off(c) + ll_keys_off(c.world);
     if (lane < c.world) {
         unsigned long long* dst =
-            reinterpret_cast<unsigned long long*>(c.base[lane] + comm_keys_off(c)) + parity * kCommMaxRanks + c.rank;
-        *reinterpret_cast<volatile unsigned long long*>(dst) = mine;
-        __threadfence_system();
-        st_release_sys(reinterpret_cast<unsigned int*>(c.base[lane] + comm_kflags_off(c)) + c.rank, epoch);
+            reinterpret_cast<unsigned long long*>(c.base[lane] + keys) + 2 * (parity * kCommMaxRanks + c.rank);
+        st_relaxed_sys_u64c(dst, ((unsigned long long)epoch << 32) | (mine >> 32));
+        st_relaxed_sys_u64c(dst + 1, ((unsigned long long)epoch << 32) | (mine & 0xFFFFFFFFull));
     }
     bool ok = true;
     unsigned long long k = 0ull;
     if (lane < c.world) {
-        ok = wait_flag(reinterpret_cast<const unsigned int*>(c.base[c.rank] + comm_kflags_off(c)) + lane, epoch, timeout);
-        if (ok)
-            k = *reinterpret_cast<volatile const unsigned long long*>(
-                reinterpret_cast<const unsigned long long*>(c.base[c.rank] + comm_keys_off(c)) + parity * kCommMaxRanks + lane);
+        const unsigned long long* src =
+            reinterpret_cast<const unsigned long long*>(c.base[c.rank] + keys) + 2 * (parity * kCommMaxRanks + lane);
+        unsigned long long hi = ld_relaxed_sys_u64c(src), lo = ld_relaxed_sys_u64c(src + 1);
+        if ((unsigned int)(hi >> 32) != epoch || (unsigned int)(lo >> 32) != epoch) {
+            const unsigned long long t0 = gtimer();
+            for (;;) {
+                hi = ld_relaxed_sys_u64c(src);
+                lo = ld_relaxed_sys_u64c(src + 1);
+                if ((unsigned int)(hi >> 32) == epoch && (unsigned int)(lo >> 32) == epoch) break;
+                if (gtimer() - t0 > timeout) {
+                    ok = false;
+                    break;
+                }
+                __nanosleep(32);
+            }
+        }
+        k = (hi << 32) | (lo & 0xFFFFFFFFull);
     }
     if (__any_sync(0xffffffffu, !ok)) {
         if (lane == 0) atomicOr(err, 1u);
@@ -278,6 +309,20 @@ int comm_allgather(neon_comm_impl* c, const float* in, float* out, long long n, 
                        c->timeout_ns);
 }
 
+PeerSet comm_peer_set(neon_comm_impl* c) {
+    PeerSet p{};
+    for (int r = 0; r < c->peers.world; ++r) p.base[r] = c->peers.base[r] + comm_ll_off(c->peers);
+    p.calls = c->epochs + kCommSlices + 1;
+    p.counter = c->epochs + kCommSlices + 2;
+    p.err = c->err;
+    p.timeout_ns = c->timeout_ns;
+    p.rank = c->peers.rank;
+    p.world = c->peers.world;
+    return p;
+}
+
+bool fused_collectives() { return g_fused.load(std::memory_order_relaxed) != 0; }
+
 int comm_argmax(neon_comm_impl* c, unsigned long long* key, int* d_tok, int* out, int* d_step, int* d_pos, int advance,
                 cudaStream_t st) {
     if (!c || !c->connected) return error(NEON_ERR_INVALID, "communicator not connected");
@@ -303,8 +348,8 @@ int neon_cuda_comm_create(int rank, int world, size_t max_floats, neon_comm_t* o
     const long long bytes = comm_bytes(c->peers);
     cudaError_t e = cudaMalloc(&c->local, (size_t)bytes);
     if (e == cudaSuccess) e = cudaMemset(c->local, 0, (size_t)bytes);
-    if (e == cudaSuccess) e = cudaMalloc(&c->epochs, sizeof(unsigned int) * (kCommSlices + 1));
-    if (e == cudaSuccess) e = cudaMemset(c->epochs, 0, sizeof(unsigned int) * (kCommSlices + 1));
+    if (e == cudaSuccess) e = cudaMalloc(&c->epochs, sizeof(unsigned int) * kEpochWords);
+    if (e == cudaSuccess) e = cudaMemset(c->epochs, 0, sizeof(unsigned int) * kEpochWords);
     if (e == cudaSuccess) e = cudaMalloc(&c->err, sizeof(unsigned int));
     if (e == cudaSuccess) e = cudaMemset(c->err, 0, sizeof(unsigned int));
     cudaIpcMemHandle_t h;
@@ -390,6 +435,11 @@ int neon_cuda_comm_connect_local(neon_comm_t* comms, int n) {
 int neon_cuda_comm_set_timeout(neon_comm_t c, double seconds) {
     if (!c || !(seconds > 0.0) || seconds > 3600.0) return error(NEON_ERR_INVALID, "timeout must be in (0, 3600] s");
     c->timeout_ns = (unsigned long long)(seconds * 1e9);
+    return NEON_OK;
+}
+
+int neon_cuda_set_fused_collectives(int enabled) {
+    g_fused.store(enabled ? 1 : 0);
     return NEON_OK;
 }
 

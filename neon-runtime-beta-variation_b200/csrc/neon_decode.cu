@@ -491,6 +491,7 @@ struct neon_model {
     neon_tensor_t head = nullptr;    // lm_head shard (tensor parallel only)
     bool head_from_output = false;   // `head` was cut from output.weight, not the tied embedding
     float* part = nullptr;           // partial sums of the column-split projections
+    float* h2 = nullptr;             // second residual buffer of the fused collectives
     float* logits_full = nullptr;    // all-gathered logits (tensor parallel only)
     neon_tensor_t embd = nullptr, output = nullptr;
     float* output_norm = nullptr;
@@ -647,18 +648,36 @@ int run_layers(neon_model* m, const int* toks, int seq) {
     return rc;
 }
 
-// logits of row `row` of h: rms_norm(output_norm) folded into the lm_head matvec
-int run_head(neon_model* m, int row) {
+// Options of a norm-folded matvec that consumes a pending fused all-reduce:
+// X = x + the ranks' partial sums, the sum written to `out`.
+void consume_pending(neon_model* m, neon_internal::MatvecExt& ext, float* out) {
+    ext.peer_mode = 2;
+    ext.peer = neon_internal::comm_peer_set(m->comm);
+    ext.red_out = out;
+}
+
+// logits of residual row x: rms_norm(output_norm) folded into the lm_head
+// matvec; with `pending`, x still lacks the last fused all-reduce.
+int run_head(neon_model* m, const float* x, bool pending = false) {
     neon_tensor_t W = m->world > 1 ? m->head : m->output ? m->output : m->embd;
     neon_proj_target_t t{W, m->logits, m->vocab_l};
     neon_internal::MatvecExt ext;
     ext.norm_w = m->output_norm;
     ext.norm_eps = m->cfg.norm_eps;
-    return neon_internal::matvec(&t, 1, m->h + (size_t)row * m->cfg.n_embd, m->cfg.n_embd, 1, m->stream, 0, &ext);
+    if (pending) consume_pending(m, ext, x == m->h ? m->h2 : m->h);
+    return neon_internal::matvec(&t, 1, x, m->cfg.n_embd, 1, m->stream, 0, &ext);
 }
 
 // One decode position (token in *d_tok, position *d_pos): the fused step.
-int run_step(neon_model* m) {
+// Returns the residual row the lm_head reads in *x_out and, in *pending,
+// whether it still lacks the last fused all-reduce.
+//
+// Tensor parallel with fused collectives: attn_output and ffn_down store their
+// partial rows straight into every rank's slot (no launch of their own), and
+// the next norm-folded matvec (q/k/v, gate/up, lm_head) sums the slots into
+// its X, writing the new residual to the other residual buffer (hc / hn
+// alternate: the launch that sums must not overwrite the X its CTAs read).
+int run_step(neon_model* m, const float** x_out, bool* pending_out) {
     const auto& c = m->cfg;
     const neon_tensor_t E = m->embd;
     const int nb = (int)(c.n_embd / 32);
@@ -668,6 +687,36 @@ int run_step(neon_model* m) {
     const size_t n_embd = c.n_embd, q_dim = m->q_dim, kv_dim = m->kv_dim, n_ff = m->n_ff_l;
     const float scale = 1.0f / std::sqrt((float)c.head_dim);
     const int group = (int)(c.n_head / c.n_kv_head);
+    const bool fused = m->world > 1 && neon_internal::fused_collectives();
+    float* hc = m->h;
+    float* hn = m->h2;
+    bool pending = false;
+    // a norm-folded launch on hc that takes in the pending all-reduce
+    auto take_pending = [&](neon_internal::MatvecExt& ext) {
+        if (!pending) return;
+        consume_pending(m, ext, hn);
+    };
+    auto swap_after = [&]() {
+        if (!pending) return;
+        std::swap(hc, hn);
+        pending = false;
+    };
+    // h += W x: fused producer, or matvec + all-reduce, or one device's accumulate
+    auto residual = [&](neon_tensor_t W, const float* x, size_t x_stride) {
+        if (!fused) {
+            if (m->world == 1) return proj(m, {{W, hc, n_embd}}, x, x_stride, 1, 1);
+            int r = proj(m, {{W, m->part, n_embd}}, x, x_stride, 1, 0);
+            if (!r) r = neon_internal::comm_allreduce(m->comm, m->part, hc, (long long)n_embd, 1, m->stream);
+            return r;
+        }
+        const neon_proj_target_t t{W, m->part, n_embd};
+        neon_internal::MatvecExt ext;
+        ext.peer_mode = 1;
+        ext.peer = neon_internal::comm_peer_set(m->comm);
+        const int r = neon_internal::matvec(&t, 1, x, x_stride, 1, m->stream, 0, &ext);
+        pending = true;
+        return r;
+    };
     for (uint32_t li = 0; li < c.n_layer && !rc; ++li) {
         auto& L = m->layers[li];
         float* Kl = m->K + (size_t)li * c.ctx_len * kv_dim;
@@ -686,7 +735,9 @@ int run_step(neon_model* m) {
             ext.head_dim = (int)c.head_dim;
             ext.epi = epi;
             ext.pos_stride = stride;
-            rc = neon_internal::matvec(t, 3, m->h, n_embd, 1, m->stream, 0, &ext);
+            take_pending(ext);
+            rc = neon_internal::matvec(t, 3, hc, n_embd, 1, m->stream, 0, &ext);
+            swap_after();
         }
         if (!rc) {
             const dim3 grid((unsigned)m->n_kv_l, m->att_split);
@@ -702,7 +753,7 @@ int run_step(neon_model* m) {
                 rc = check_launch("attn_values_kernel");
             }
         }
-        if (!rc) rc = residual_proj(m, L.w[3], m->att, q_dim, 1);
+        if (!rc) rc = residual(L.w[3], m->att, q_dim);
         if (!rc) {
             // act = silu(gate) * up, (gate, up) = W x with x = rms_norm(h)
             const neon_proj_target_t t{L.gateup, m->act, n_ff};
@@ -713,10 +764,14 @@ int run_step(neon_model* m) {
             ext.norm_eps = c.norm_eps;
             ext.epi = &epi;
             ext.pos_stride = &stride;
-            rc = neon_internal::matvec(&t, 1, m->h, n_embd, 1, m->stream, 0, &ext);
+            take_pending(ext);
+            rc = neon_internal::matvec(&t, 1, hc, n_embd, 1, m->stream, 0, &ext);
+            swap_after();
         }
-        if (!rc) rc = residual_proj(m, L.w[4], m->act, n_ff, 1);
+        if (!rc) rc = residual(L.w[4], m->act, n_ff);
     }
+    *x_out = hc;
+    *pending_out = pending;
     return rc;
 }
 
@@ -768,15 +823,17 @@ int forward_device(neon_model* m, const int32_t* tokens_host, size_t n) {
         DEC_TRY(cudaMemcpyAsync(m->d_tokens, tokens_host + off, seq * sizeof(int32_t), cudaMemcpyHostToDevice, m->stream));
         DEC_TRY(cudaMemcpyAsync(m->d_pos, &pos, sizeof(int), cudaMemcpyHostToDevice, m->stream));
         int rc;
+        const float* hx = m->h + (size_t)(seq - 1) * m->cfg.n_embd;
+        bool pending = false;
         if (seq == 1) {
             DEC_TRY(cudaMemcpyAsync(m->d_tok, tokens_host + off, sizeof(int32_t), cudaMemcpyHostToDevice, m->stream));
-            rc = run_step(m);
+            rc = run_step(m, &hx, &pending);
         } else {
             rc = run_layers(m, m->d_tokens, seq);
         }
         if (rc) return rc;
         if (off + seq == n) {
-            rc = run_head(m, seq - 1);
+            rc = run_head(m, hx, pending);
             if (!rc && m->world > 1)
                 rc = neon_internal::comm_allgather(m->comm, m->logits, m->logits_full, (long long)m->cfg.n_vocab, m->stream);
             if (rc) return rc;
@@ -874,6 +931,7 @@ int neon_cuda_model_create_tp(const neon_model_config_t* cfg, neon_comm_t comm, 
     A((void**)&m->att, sizeof(float) * S * m->q_dim);
     A((void**)&m->gu, sizeof(float) * S * 2 * m->n_ff_l);
     A((void**)&m->act, sizeof(float) * S * m->n_ff_l);
+    A((void**)&m->h2, sizeof(float) * c.n_embd);
     if (world > 1) {
         A((void**)&m->part, sizeof(float) * S * c.n_embd);
         A((void**)&m->logits_full, sizeof(float) * c.n_vocab);
@@ -1083,8 +1141,10 @@ int neon_cuda_model_generate(neon_model_t m, const int32_t* prompt, size_t n_pro
         }
         cudaGraph_t g = nullptr;
         DEC_TRY(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
-        rc = run_step(m);
-        if (!rc) rc = run_head(m, 0);
+        const float* hx = nullptr;
+        bool pending = false;
+        rc = run_step(m, &hx, &pending);
+        if (!rc) rc = run_head(m, hx, pending);
         if (!rc) rc = launch_argmax(m, 1);
         cudaError_t ce = cudaStreamEndCapture(m->stream, &g);
         if (rc) {

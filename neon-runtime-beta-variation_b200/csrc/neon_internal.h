@@ -24,39 +24,73 @@ struct neon_tensor {
 
 // Tensor-parallel communicator: one per rank (process, device). Every rank
 // owns a buffer in its own HBM, exported with CUDA IPC and opened by all
-// peers; collectives push data into the peers' buffers with plain P2P stores
-// and publish an epoch flag, then wait (bounded) for every peer's flag.
+// peers; collectives push data into the peers' buffers with plain P2P stores.
+// Two protocols share the buffer:
+//  - bulk (comm kernel, any size): data, then a system-scope fence and a
+//    released epoch flag per slice; readers acquire the flag, then the data;
+//  - low latency ("LL", decode-sized vectors): every 8-byte word carries a
+//    value and the call number that wrote it, so no fence or flag is needed --
+//    a reader polls a word until the number is the one it expects (one 8-byte
+//    store is single-copy atomic, so value and number arrive together).
 constexpr int kCommMaxRanks = 8;
-constexpr int kCommSlices = 32;  // CTAs of the all-reduce kernel (one flag each)
+constexpr int kCommSlices = 32;         // CTAs of the bulk all-reduce kernel (one flag each)
+constexpr int kCommFusedFloats = 65536; // LL slot: one position's vector (n_embd), at most
 
 struct CommPeers {  // passed to kernels by value
     unsigned char* base[kCommMaxRanks];  // each rank's buffer, mapped here (own: base[rank])
     int rank, world;
-    long long max_floats;                // capacity of one receive slot, in floats
+    long long max_floats;                // capacity of one bulk receive slot, in floats
 };
 
-// Buffer layout (bytes from base): two parity halves of `world` receive slots
-// of max_floats floats, then flags[src][slice], then argmax keys
-// [parity][src] (8 bytes each) and their flags [src].
+// Buffer layout (bytes from base):
+//   bulk slots  [parity][src][max_floats] f32
+//   bulk flags  [src][slice] u32
+//   LL slots    [parity][src][kCommFusedFloats] u64   (comm_ll_off)
+//   LL keys     [parity][src][2] u64                  (argmax exchange)
 __host__ __device__ inline long long comm_recv_off(const CommPeers& c, int parity, int src) {
     return ((long long)parity * c.world + src) * c.max_floats * 4;
 }
 __host__ __device__ inline long long comm_flags_off(const CommPeers& c) { return 2LL * c.world * c.max_floats * 4; }
-__host__ __device__ inline long long comm_keys_off(const CommPeers& c) {
-    return comm_flags_off(c) + (long long)kCommMaxRanks * kCommSlices * 4;
+__host__ __device__ inline long long comm_ll_off(const CommPeers& c) {
+    return (comm_flags_off(c) + (long long)kCommMaxRanks * kCommSlices * 4 + 255) & ~255LL;
 }
-__host__ __device__ inline long long comm_kflags_off(const CommPeers& c) {
-    return comm_keys_off(c) + 2LL * kCommMaxRanks * 8;
+// offsets inside the LL region
+__host__ __device__ inline long long ll_slot_off(int world, int parity, int src) {
+    return ((long long)parity * world + src) * kCommFusedFloats * 8;
 }
+__host__ __device__ inline long long ll_keys_off(int world) { return 2LL * world * kCommFusedFloats * 8; }
 __host__ __device__ inline long long comm_bytes(const CommPeers& c) {
-    return comm_kflags_off(c) + (long long)kCommMaxRanks * 4 + 256;
+    return comm_ll_off(c) + ll_keys_off(c.world) + 2LL * kCommMaxRanks * 2 * 8 + 256;
 }
+
+// An LL word: the value's bits, and the call number in the high half.
+__host__ __device__ inline unsigned long long ll_pack(float v, unsigned int call) {
+    union { float f; unsigned int u; } b;
+    b.f = v;
+    return ((unsigned long long)call << 32) | b.u;
+}
+
+// What a matvec launch needs to take part in a fused (LL) collective: the
+// producing launch (attn_output / ffn_down of one position) stores each row
+// as an LL word into slot [parity][rank] of every rank; the consuming launch
+// (the next norm-folded matvec) polls the words of all ranks' slots while it
+// stages X = residual + (slot_0 + slot_1 + ...), the bulk kernel's sum, bit
+// for bit, and its last CTA advances the call count.
+struct PeerSet {
+    unsigned char* base[kCommMaxRanks];  // every rank's LL region (this process's mappings)
+    unsigned int* calls;                 // this rank's count of completed LL collectives (device)
+    unsigned int* counter;               // last-CTA election of a consuming launch (device)
+    unsigned int* err;                   // the communicator's error word
+    unsigned long long timeout_ns;
+    int rank, world;
+};
 
 struct neon_comm_impl {
     int device = 0;
     CommPeers peers{};
     unsigned char* local = nullptr;        // this rank's buffer
-    unsigned int* epochs = nullptr;        // device: per-slice call count (+1: key exchanges)
+    unsigned int* epochs = nullptr;        // device: per-slice call counts, then the key-exchange count,
+                                           // the fused collectives' count and their last-CTA counter
     unsigned int* err = nullptr;           // device error word: bit 0 = a peer wait timed out
     unsigned long long timeout_ns = 4000000000ull;  // bound of every wait on a peer
     bool connected = false;
@@ -76,6 +110,9 @@ int comm_allgather(neon_comm_impl* c, const float* in, float* out, long long n, 
 // *d_tok and out[*d_step]; *d_step += 1, *d_pos += advance, *key = 0.
 int comm_argmax(neon_comm_impl* c, unsigned long long* key, int* d_tok, int* out, int* d_step, int* d_pos,
                 int advance, cudaStream_t st);
+// The fused-collective view of a connected communicator.
+PeerSet comm_peer_set(neon_comm_impl* c);
+bool fused_collectives();
 
 // Decode-step options of a one-position matvec launch (seq == 1 only):
 // RMSNorm of X folded into the X staging, and per-target epilogues (the
@@ -90,6 +127,12 @@ struct MatvecExt {
     int head_dim = 0;
     const int* epi = nullptr;               // per target; null: plain store
     const long long* pos_stride = nullptr;  // per target
+    // fused collective: 1 = produce (one target; its rows go to every rank's
+    // slot), 2 = consume (X += the ranks' slots; needs norm_w; CTA 0 writes
+    // the summed X, the new residual, to red_out)
+    int peer_mode = 0;
+    PeerSet peer{};
+    float* red_out = nullptr;
 };
 
 // neon_cuda_matvec_multi on `st`, with y += result when `accumulate`.

@@ -22,6 +22,8 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include "neon_internal.h"
+
 namespace neon {
 
 constexpr int kWarps = 8;
@@ -42,6 +44,7 @@ enum : int {
     kEpiRope = 1,    // RoPE on pairs (fwd::rope_apply), then store at y + pos*pos_stride
     kEpiAtPos = 2,   // store at y + pos*pos_stride (the V cache row of the position)
     kEpiSwiglu = 3,  // rows interleave gate/up: y[i] = silu(v_2i) * v_2i+1
+    kEpiPeer = 4,    // fused collective: row r into slot [parity][rank] of every rank
 };
 
 struct Span {
@@ -326,6 +329,9 @@ struct StreamArgs {
     const float2* rope_cs;  // [position][rope_half] (cos, sin)
     int rope_half;
     int head_dim;
+    int peer_mode;          // fused collective: 1 produce, 2 consume (neon_internal::MatvecExt)
+    float* red_out;         // consume: CTA 0 writes the summed X here
+    PeerSet peer;
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -367,6 +373,72 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 
 // Wait for phase `parity` of `bar`; give up after ~2 s, record the timeout in
 // *err and return false (the caller leaves the kernel, CTA-uniformly).
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// The consuming side of an LL collective inside a launch: rank r's partial
+// of element i is LL word slots[r * kCommFusedFloats + i] once it carries
+// `call`. Every poll is bounded by the communicator's timeout; the first wait
+// that runs out sets bit 0 of the error word and *skip, after which (as when
+// the communicator was already in error) nothing waits and the launch runs
+// on with whatever the words hold.
+struct LLView {
+    const unsigned long long* slots;  // rank 0's slot of this call's parity; null: nothing pending
+    unsigned int call;
+    int world;
+    unsigned int* err;
+    unsigned long long timeout_ns;
+    volatile int* skip;               // shared memory
+};
+
+__device__ __forceinline__ float ll_wait(const unsigned long long* p, unsigned int call, unsigned int* err,
+                                      unsigned long long timeout_ns, volatile int* skip) {
+    const uint64_t t0 = globaltimer_ns();
+    unsigned long long w;
+    for (;;) {
+        w = ld_relaxed_sys_u64(p);
+        if ((unsigned int)(w >> 32) == call || *skip) break;
+        if (globaltimer_ns() - t0 > timeout_ns) {
+            atomicOr(err, 1u);
+            *skip = 1;
+            break;
+        }
+        __nanosleep(32);
+    }
+    return __uint_as_float((unsigned int)w);
+}
+
+__device__ __forceinline__ float ll_value(const unsigned long long* p, const LLView& v) {
+    const unsigned long long w = ld_relaxed_sys_u64(p);
+    if ((unsigned int)(w >> 32) == v.call) return __uint_as_float((unsigned int)w);
+    return ll_wait(p, v.call, v.err, v.timeout_ns, v.skip);
+}
+
+// slot_0[i] + slot_1[i] + ... in rank order (the bulk kernel's sum), waiting
+// for every word to carry the call
+__device__ __forceinline__ float ll_sum_wait(const LLView& v, long long i) {
+    float s = ll_value(v.slots + i, v);
+    for (int r = 1; r < v.world; ++r) s += ll_value(v.slots + (long long)r * kCommFusedFloats + i, v);
+    return s;
+}
+
+// The same sum once this CTA has seen every word carry the call (after
+// ll_sum_wait over all i and a barrier): the words cannot change again before
+// the call after next, so plain reads suffice.
+__device__ __forceinline__ float ll_sum(const LLView& v, long long i) {
+    float s = __uint_as_float((unsigned int)ld_relaxed_sys_u64(v.slots + i));
+    for (int r = 1; r < v.world; ++r)
+        s += __uint_as_float((unsigned int)ld_relaxed_sys_u64(v.slots + (long long)r * kCommFusedFloats + i));
+    return s;
+}
+
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int* err) {
     const uint32_t addr = smem_u32(bar);
     uint32_t done = 0;
@@ -408,10 +480,21 @@ __host__ __device__ constexpr int stream_x_bytes(int type, int nb) {
 // rms_norm's scale 1/sqrt(mean(x^2) + eps) of n floats (fwd::rms_norm,
 // rawllm_forward.hpp:730-735): a double sum of squares over the whole CTA,
 // so every CTA of the launch derives the same scale.
-__device__ float cta_rms_scale(const float* __restrict__ x, int n, float eps, double* scratch) {
+// X element i, with a pending fused all-reduce folded in when `ll` has
+// slots: x[i] + ((slot_0[i] + slot_1[i]) + ...), the bulk kernel's order.
+__device__ __forceinline__ float x_plus_slots(const float* __restrict__ x, int i, const LLView& ll) {
+    const float v = __ldg(x + i);
+    if (!ll.slots) return v;
+    return v + ll_sum(ll, i);
+}
+
+__device__ __forceinline__ float cta_rms_scale(const float* __restrict__ x, int n, float eps, double* scratch,
+                                               const LLView& ll, float* out = nullptr) {
     double ss = 0.0;
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        const double v = (double)__ldg(x + i);
+        const float xv = ll.slots ? __ldg(x + i) + ll_sum_wait(ll, i) : __ldg(x + i);
+        if (out) out[i] = xv;
+        const double v = (double)xv;
         ss = fma(v, v, ss);
     }
 #pragma unroll
@@ -433,7 +516,7 @@ __device__ float cta_rms_scale(const float* __restrict__ x, int n, float eps, do
 // output (the reference multiplies in that order).
 template <int TPB>
 __device__ __forceinline__ void stage_x_q8(const float* __restrict__ x, int nb, bool x_vec, unsigned char* rec,
-                                           const float* __restrict__ norm_w = nullptr, float scale = 1.f) {
+                                           const float* __restrict__ norm_w, float scale, const LLView& ll) {
     constexpr int EPT = 32 / TPB;
     const int lane = threadIdx.x & 31;
     const int n = nb * TPB;
@@ -446,12 +529,19 @@ __device__ __forceinline__ void stage_x_q8(const float* __restrict__ x, int nb, 
         if (act && x_vec) {
 #pragma unroll
             for (int k = 0; k < EPT / 4; ++k) {
-                const float4 v = __ldg(reinterpret_cast<const float4*>(xb) + k);
+                float4 v = __ldg(reinterpret_cast<const float4*>(xb) + k);
+                if (ll.slots) {
+                    const long long e = (long long)b * 32 + part * EPT + 4 * k;
+                    v.x = v.x + ll_sum(ll, e);
+                    v.y = v.y + ll_sum(ll, e + 1);
+                    v.z = v.z + ll_sum(ll, e + 2);
+                    v.w = v.w + ll_sum(ll, e + 3);
+                }
                 xv[4 * k] = v.x; xv[4 * k + 1] = v.y; xv[4 * k + 2] = v.z; xv[4 * k + 3] = v.w;
             }
         } else if (act) {
 #pragma unroll
-            for (int j = 0; j < EPT; ++j) xv[j] = __ldg(xb + j);
+            for (int j = 0; j < EPT; ++j) xv[j] = x_plus_slots(x, b * 32 + part * EPT + j, ll);
         } else {
 #pragma unroll
             for (int j = 0; j < EPT; ++j) xv[j] = 0.f;
@@ -549,7 +639,7 @@ __device__ __forceinline__ float silu_dev(float x) {
 // Writes the RC row results of a tile (rowv[], shared memory) through the
 // span's epilogue; threads t < RC own row row0 + t.
 __device__ __forceinline__ void stream_epilogue(const StreamArgs& a, const Span& sp, int row0, int RC,
-                                                const float* rowv) {
+                                                const float* rowv, unsigned int peer_call) {
     const int t = threadIdx.x;
     if (t >= RC) return;
     const int row = row0 + t;
@@ -585,6 +675,14 @@ __device__ __forceinline__ void stream_epilogue(const StreamArgs& a, const Span&
             // silu(gate) * up (rawllm_forward.hpp:1186)
             if (!(t & 1)) sp.y[row / 2] = __fmul_rn(silu_dev(v), rowv[t + 1]);
             break;
+        case kEpiPeer: {
+            // this rank's partial row sum, as an LL word, into its slot on every rank (NVLink stores)
+            const long long off = ll_slot_off(a.peer.world, (int)(peer_call & 1u), a.peer.rank) / 8 + row;
+            const unsigned long long w = ll_pack(v, peer_call);
+            for (int p = 0; p < a.peer.world; ++p)
+                st_relaxed_sys_u64(reinterpret_cast<unsigned long long*>(a.peer.base[p]) + off, w);
+            break;
+        }
     }
 }
 
@@ -670,19 +768,42 @@ __global__ void __launch_bounds__(kStreamThreads) matvec_stream_kernel(const __g
     }
     pdl_wait();
 
+    // Fused (LL) collective: this launch's call number -- the next one after
+    // the last completed -- and, for a consumer, the view of the ranks' slots.
+    unsigned int peer_call = 0;
+    __shared__ int ll_skip;
+    LLView ll;
+    ll.slots = nullptr;
+    if (a.peer_mode) {
+        peer_call = *reinterpret_cast<volatile const unsigned int*>(a.peer.calls) + 1u;
+        if (a.peer_mode == 2) {
+            if (threadIdx.x == 0) ll_skip = *reinterpret_cast<volatile const unsigned int*>(a.peer.err) != 0u;
+            __syncthreads();
+            ll.slots = reinterpret_cast<const unsigned long long*>(
+                a.peer.base[a.peer.rank] + ll_slot_off(a.peer.world, (int)(peer_call & 1u), 0));
+            ll.call = peer_call;
+            ll.world = a.peer.world;
+            ll.err = a.peer.err;
+            ll.timeout_ns = a.peer.timeout_ns;
+            ll.skip = &ll_skip;
+        }
+    }
+
     // Stage X once per CTA (normalised first when asked), then let the next
     // launch start.
     __shared__ double dscratch[32];
-    const float nscale = a.norm_w ? cta_rms_scale(a.x, nb * 32, a.norm_eps, dscratch) : 1.f;
+    const float nscale = a.norm_w ? cta_rms_scale(a.x, nb * 32, a.norm_eps, dscratch, ll,
+                                                  blockIdx.x == 0 ? a.red_out : nullptr)
+                                  : 1.f;
     if (TYPE == 2) {
         const int tpb = kStreamThreads / nb;
-        if (tpb >= 4) stage_x_q8<4>(a.x, nb, a.x_vec, xsm, a.norm_w, nscale);
-        else if (tpb >= 2) stage_x_q8<2>(a.x, nb, a.x_vec, xsm, a.norm_w, nscale);
-        else stage_x_q8<1>(a.x, nb, a.x_vec, xsm, a.norm_w, nscale);
+        if (tpb >= 4) stage_x_q8<4>(a.x, nb, a.x_vec, xsm, a.norm_w, nscale, ll);
+        else if (tpb >= 2) stage_x_q8<2>(a.x, nb, a.x_vec, xsm, a.norm_w, nscale, ll);
+        else stage_x_q8<1>(a.x, nb, a.x_vec, xsm, a.norm_w, nscale, ll);
     } else {
         float* xs = reinterpret_cast<float*>(xsm);
         for (int i = threadIdx.x; i < nb * 32; i += kStreamThreads) {
-            float v = __ldg(a.x + i);
+            float v = x_plus_slots(a.x, i, ll);
             if (a.norm_w) v = __fmul_rn(__fmul_rn(v, nscale), __ldg(a.norm_w + i));
             xs[(i >> 5) * kQ8Pitch + (i & 31)] = v;
         }
@@ -775,7 +896,7 @@ __global__ void __launch_bounds__(kStreamThreads) matvec_stream_kernel(const __g
                 rowv[threadIdx.x] = v;
             }
             if (WPG > 1) __syncthreads();
-            stream_epilogue(a, sp, row0, RC, rowv);
+            stream_epilogue(a, sp, row0, RC, rowv, peer_call);
 #pragma unroll
             for (int rr = 0; rr < R; ++rr) acc[rr] = 0.f;
         }
@@ -783,6 +904,15 @@ __global__ void __launch_bounds__(kStreamThreads) matvec_stream_kernel(const __g
         if (warp == 0 && item + S < n_items) {
             fence_proxy_async_smem();
             issue(item + S);
+        }
+    }
+    if (a.peer_mode == 2) {
+        // The last CTA to finish records the call as completed: every CTA read
+        // the count before it counted itself in here.
+        __syncthreads();
+        if (threadIdx.x == 0 && atomicAdd(a.peer.counter, 1u) == gridDim.x - 1) {
+            *a.peer.counter = 0u;
+            *a.peer.calls = peer_call;
         }
     }
 }

@@ -80,6 +80,7 @@ C_ENTRY_POINTS = (
     "neon_cuda_model_comm_floats",
     "neon_cuda_tp_shard",
     "neon_cuda_model_create_tp",
+    "neon_cuda_set_fused_collectives",
     "neon_cuda_set_pdl",
 )
 
@@ -158,6 +159,7 @@ def load(path: str | None = None) -> C.CDLL:
         L.neon_cuda_model_comm_floats.argtypes = [C.POINTER(_ModelConfig), C.c_int, C.POINTER(_sz)]
         L.neon_cuda_tp_shard.argtypes = [C.POINTER(_ModelConfig), C.c_int, C.c_int, C.c_int, C.POINTER(_sz)]
         L.neon_cuda_model_create_tp.argtypes = [C.POINTER(_ModelConfig), _vp, C.POINTER(_vp)]
+        L.neon_cuda_set_fused_collectives.argtypes = [C.c_int]
         _lib = L
         return L
 
@@ -183,6 +185,11 @@ def launch_count() -> int:
 
 def set_pdl(enabled: bool) -> None:
     _check(load().neon_cuda_set_pdl(1 if enabled else 0))
+
+
+def set_fused_collectives(enabled: bool) -> None:
+    """Sharded decode: fold the all-reduces into the matvecs (default) or not."""
+    _check(load().neon_cuda_set_fused_collectives(1 if enabled else 0))
 
 
 def sync(stream: int = 0) -> None:

@@ -65,14 +65,17 @@ def test_tiny_golden_tokens_and_logits(tp2):
     for i, lg in enumerate(tp2["tiny_logits"]):
         assert rel_l2(lg, g["logits"][i]) <= MODEL_L2_RTOL, f"step {i}"
         assert int(np.argmax(lg)) == int(np.argmax(g["logits"][i]))
+    # the fused collectives give the same bits as separate all-reduce launches
+    assert np.array_equal(tp2["tiny_logits"], tp2["tiny_logits_unfused"])
     # each rank holds its own KV heads
     assert tuple(tp2["tiny_k0_shape"]) == (len(g["prompt"]), 2 // 2 * 64)
 
 
 def test_qwen_split_matches_one_gpu_and_reference(tp2):
     assert np.array_equal(tp2["qwen_tokens"], tp2["qwen_tokens_1gpu"])
-    print(f"decode {QWEN_STEPS} tokens: 2 GPUs {float(tp2['qwen_tp_ms']):.2f} ms, "
-          f"1 GPU {float(tp2['qwen_1gpu_ms']):.2f} ms")
+    assert np.array_equal(tp2["qwen_tokens"], tp2["qwen_tokens_unfused"])
+    print(f"decode {QWEN_STEPS} tokens: 2 GPUs fused {float(tp2['qwen_tp_ms']):.2f} ms, "
+          f"unfused {float(tp2['qwen_tp_unfused_ms']):.2f} ms, 1 GPU {float(tp2['qwen_1gpu_ms']):.2f} ms")
     if not O.ref_available():
         pytest.skip("oracle/_ref not built")
     cfg = S.QWEN3_0_6B.with_(ctx_len=QWEN_PROMPT + QWEN_STEPS + 1)

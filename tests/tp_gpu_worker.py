@@ -81,12 +81,15 @@ def main():
         m = NC.Model(TINY, S.model_tensors(TINY, seed=3), comm)
         dist.barrier()
         res["tiny_tokens"] = m.generate(g["prompt"], 16)
-        m.set_length(0)
-        dist.barrier()
-        logits = [m.forward(g["prompt"])]
-        for t in g["tokens"][:8]:
-            logits.append(m.forward([t]))
-        res["tiny_logits"] = np.stack(logits)
+        for fused in (True, False):
+            NC.set_fused_collectives(fused)
+            m.set_length(0)
+            dist.barrier()
+            logits = [m.forward(g["prompt"])]
+            for t in g["tokens"][:8]:
+                logits.append(m.forward([t]))
+            res["tiny_logits" if fused else "tiny_logits_unfused"] = np.stack(logits)
+        NC.set_fused_collectives(True)
         k, v = m.read_kv(0, len(g["prompt"]))
         res["tiny_k0_shape"] = np.array(k.shape)
         m.free()
@@ -95,9 +98,15 @@ def main():
         tensors = list(S.model_tensors(qwen, seed=21))
         prompt = S.prompt_tokens(a.qwen_prompt, qwen.n_vocab, 22)
         m = NC.Model(qwen, tensors, comm)
-        dist.barrier()
-        res["qwen_tokens"] = m.generate(prompt, a.qwen_steps)
-        res["qwen_tp_ms"] = np.array(m.decode_ms)
+        for fused in (False, True):
+            NC.set_fused_collectives(fused)
+            m.set_length(0)
+            dist.barrier()
+            toks = m.generate(prompt, a.qwen_steps)
+            if fused:
+                res["qwen_tokens"], res["qwen_tp_ms"] = toks, np.array(m.decode_ms)
+            else:
+                res["qwen_tokens_unfused"], res["qwen_tp_unfused_ms"] = toks, np.array(m.decode_ms)
         m.free()
         comm.check()
         dist.barrier()
