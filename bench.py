@@ -100,9 +100,15 @@ def parse_args():
     p.add_argument("--workload", choices=sorted(WORKLOADS) + sorted(DECODE_WORKLOADS), default="q4_0_4096x4096")
     p.add_argument("--prompt", type=int, default=None, help="decode workloads: prompt tokens (default: the config's)")
     p.add_argument("--new-tokens", type=int, default=None, help="decode workloads: generated tokens")
+    p.add_argument("--no-fused-collectives", action="store_true",
+                   help="decode workloads at N>1: one all-reduce launch per column-split projection")
+    p.add_argument("--layers", type=int, default=None,
+                   help="decode workloads: fewer layers (kernel shapes unchanged; for profiling)")
     p.add_argument("--no-decode", action="store_true", help="matvec workloads: skip the decode sub-measurement")
     args = p.parse_args()
     select_workload(args.workload)
+    global LAYERS
+    LAYERS = args.layers
     return args
 
 
@@ -238,11 +244,17 @@ def host_rotation(rank, n):
     return [S.weights(TYPE, ROWS, COLS, seed=100000 * rank + i) for i in range(n)]
 
 
+LAYERS = None  # --layers
+
+
 def decode_config(name, prompt=None, new_tokens=None):
     cfg, n_prompt, n_new = DECODE_WORKLOADS[name]
     n_prompt = n_prompt if prompt is None else prompt
     n_new = n_new if new_tokens is None else new_tokens
-    return cfg.with_(ctx_len=n_prompt + n_new + 1), n_prompt, n_new
+    cfg = cfg.with_(ctx_len=n_prompt + n_new + 1)
+    if LAYERS:
+        cfg = cfg.with_(n_layer=LAYERS)
+    return cfg, n_prompt, n_new
 
 
 def decode_desc(cfg, n_prompt, n_new):
@@ -252,24 +264,42 @@ def decode_desc(cfg, n_prompt, n_new):
             f"seeded-random prompt")
 
 
-def measure_decode_gpu(name, prompt=None, new_tokens=None):
+def is_big(cfg):
+    return cfg.n_embd * cfg.n_ff * cfg.n_layer > 4e9
+
+
+def model_bytes(cfg):
+    """GGUF bytes of the synthetic decoder: Q4_0 projections, Q8_0 embedding."""
+    per_layer = (2 * cfg.q_dim * cfg.n_embd + 2 * cfg.kv_dim * cfg.n_embd + 3 * cfg.n_ff * cfg.n_embd) * 18 // 32
+    return cfg.n_layer * per_layer + cfg.n_vocab * cfg.n_embd * 34 // 32
+
+
+def measure_decode_gpu(name, prompt=None, new_tokens=None, comm=None, barrier=None, max_over_ranks=None):
     """Device-timed greedy decode through neon_cuda.Model.generate (CUDA graph
-    per token); returns (result dict, model config, prompt tokens)."""
+    per token), on one GPU or split over the ranks of `comm` (tensor
+    parallel); returns (result dict, model config, prompt tokens)."""
     import neon_cuda as N
 
+    barrier = barrier or (lambda: None)
+    max_over_ranks = max_over_ranks or (lambda v: v)
     cfg, n_prompt, n_new = decode_config(name, prompt, new_tokens)
+    big = is_big(cfg)
     t0 = time.perf_counter()
-    m = N.Model(cfg, S.model_tensors(cfg, seed=5))
+    m = N.Model(cfg, S.model_tensors(cfg, seed=5, pooled=big), comm)
     load_s = time.perf_counter() - t0
     prompt_toks = S.prompt_tokens(n_prompt, cfg.n_vocab, 6)
+    barrier()
     t0 = time.perf_counter()
     toks = m.generate(prompt_toks, n_new)
-    wall = time.perf_counter() - t0
-    ms = m.decode_ms
+    wall = max_over_ranks(time.perf_counter() - t0)
+    ms = max_over_ranks(m.decode_ms)
     m.free()
-    return {"workload": decode_desc(cfg, n_prompt, n_new), "tokens_per_s": round(n_new * 1e3 / ms, 2),
+    world = comm.world if comm is not None else 1
+    return {"workload": decode_desc(cfg, n_prompt, n_new) + (" (weights cut from a seeded block pool)" if big else ""),
+            "n_gpus": world, "parallelism": f"tp{world}",
+            "tokens_per_s": round(n_new * 1e3 / ms, 2),
             "ms_per_token": round(ms / n_new, 4), "generated": int(len(toks)),
-            "timing": "CUDA events around the replayed per-token graphs",
+            "timing": "CUDA events around the replayed per-token graphs, max over ranks",
             "e2e_tokens_per_s": round(n_new / wall, 2),
             "e2e": "neon_cuda.Model.generate wall clock incl. prompt prefill and token read-back",
             "load_s": round(load_s, 2)}, cfg, prompt_toks
@@ -282,7 +312,7 @@ def measure_decode_cpu(cfg, prompt_toks, steps, threads=None):
     import oracle as O
 
     kind = "reference" if O.ref_available() else "port"
-    m = O.Model(cfg, S.model_tensors(cfg, seed=5), kind, threads=threads)
+    m = O.Model(cfg, S.model_tensors(cfg, seed=5, pooled=is_big(cfg)), kind, threads=threads)
     logits = m.forward(prompt_toks)
     nxt = int(np.argmax(logits))
     t0 = time.perf_counter()
@@ -298,31 +328,76 @@ def measure_decode_cpu(cfg, prompt_toks, steps, threads=None):
 
 
 def run_decode(args):
-    """--workload decode_*: one line, metric batch-1 decode tokens/s."""
+    """--workload decode_*: one line, metric batch-1 decode tokens/s; under
+    torchrun the decoder is split over the N ranks (tensor parallel)."""
     import torch
+    import torch.distributed as dist
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
-    if world > 1:
-        raise SystemExit("decode workloads run on one GPU in this build")
-    torch.cuda.set_device(0)
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
     import neon_cuda as N
 
-    N.init(0)
-    sampler = ClockSampler([0])
+    N.init(local)
+    N.set_fused_collectives(not args.no_fused_collectives)
+    comm = None
+    barrier, max_over_ranks = (lambda: None), (lambda v: v)
+    if world > 1:
+        import datetime
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
+        cfg0, _, _ = decode_config(args.workload, args.prompt, args.new_tokens)
+        comm = N.Comm.from_process_group(N.model_comm_floats(cfg0, world))
+        comm.set_timeout(30.0)
+        barrier = dist.barrier
+
+        def max_over_ranks(v):
+            t = torch.tensor([float(v)], dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            return float(t.item())
+    sampler = ClockSampler([local]) if rank == 0 else None
     time.sleep(0.2)
     t0 = time.time()
-    res, cfg, prompt_toks = measure_decode_gpu(args.workload, args.prompt, args.new_tokens)
+    res, cfg, prompt_toks = measure_decode_gpu(args.workload, args.prompt, args.new_tokens, comm, barrier,
+                                               max_over_ranks)
     t1 = time.time()
-    sampler.stop()
-    cpu = None if args.no_cpu_baseline else measure_decode_cpu(cfg, prompt_toks, steps=8)
-    line = {"metric": DECODE_METRIC, "value": res["tokens_per_s"], "unit": "tokens/s", "n_gpus": 1,
-            "steps": res["generated"], "warmup": 0, "ms_per_step": res["ms_per_token"], "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "int8/fp32 (q4_0 x q8_0 dp4a, fp32 scales)",
-            "data": "synthetic", "config": {"workload": res["workload"], "parallelism": "tp1"},
-            "e2e": {"value": res["e2e_tokens_per_s"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
-                    "d2h_bytes_per_step": 4, "api": res["e2e"]},
-            "cpu_baseline": cpu, "clocks": sampler.summary(t0, t1)}
-    print(json.dumps(line), flush=True)
+    if sampler:
+        sampler.stop()
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = measure_decode_cpu_bounded(cfg, prompt_toks)
+    if rank == 0:
+        line = {"metric": DECODE_METRIC, "value": res["tokens_per_s"], "unit": "tokens/s", "n_gpus": world,
+                "steps": res["generated"], "warmup": 0, "ms_per_step": res["ms_per_token"], "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "int8/fp32 (q4_0 x q8_0 dp4a, fp32 scales)",
+                "data": "synthetic", "config": {"workload": res["workload"], "parallelism": res["parallelism"]},
+                "e2e": {"value": res["e2e_tokens_per_s"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 4, "api": res["e2e"]},
+                "load_s": res["load_s"], "cpu_baseline": cpu, "clocks": sampler.summary(t0, t1)}
+        print(json.dumps(line), flush=True)
+    if comm is not None:
+        barrier()
+        comm.free()
+        dist.destroy_process_group()
+
+
+def measure_decode_cpu_bounded(cfg, prompt_toks):
+    """The reference's CPU decode on a bounded sample: the full prompt when the
+    model is small, else a 16-token prompt and 2 steps (stated in `sample`);
+    skipped when the host has too little memory for the model."""
+    big = is_big(cfg)
+    need = model_bytes(cfg)
+    try:
+        import psutil
+        avail = psutil.virtual_memory().available
+    except Exception:
+        avail = 0
+    if big and avail < need * 1.5:
+        return {"skipped": f"host memory {avail / 1e9:.0f} GB too small for the reference CPU model "
+                           f"({need / 1e9:.0f} GB)"}
+    if big:
+        return measure_decode_cpu(cfg.with_(ctx_len=32), prompt_toks[:16], steps=2)
+    return measure_decode_cpu(cfg, prompt_toks, steps=8)
 
 
 def run_reference(args):

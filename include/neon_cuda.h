@@ -269,10 +269,11 @@ NEON_API int neon_cuda_tp_shard(const neon_model_config_t* cfg, int role, int ra
  * KV heads only; logits and tokens are whole on every rank. */
 NEON_API int neon_cuda_model_create_tp(const neon_model_config_t* cfg, neon_comm_t comm, neon_model_t* out);
 /* Launch option of the sharded decode step: fused collectives (default on)
- * -- attn_output / ffn_down store their partial rows straight into every
- * rank's buffer and the next norm-folded matvec sums them while staging its
- * input -- or, off, one all-reduce launch after each of those projections.
- * Both give bit-identical results. Set it before the first generate. */
+ * -- attn_output / ffn_down store their partial rows, each word tagged with
+ * the call number, straight into every rank's buffer, and a small reduce
+ * launch adds them into the residual -- or, off, the projection writes
+ * locally and a fenced one-shot all-reduce follows. Both give bit-identical
+ * results. Set it before the first generate. */
 NEON_API int neon_cuda_set_fused_collectives(int enabled);
 
 /* Launch option: programmatic dependent launch (PDL) lets a matvec fetch its

@@ -268,6 +268,60 @@ __global__ void comm_argmax_kernel(CommPeers c, unsigned long long* key, int* d_
     }
 }
 
+// Bounded poll of one LL word until it carries `call`.
+__device__ __noinline__ unsigned long long ll_wait_word(const unsigned long long* a, unsigned int call, unsigned int* err,
+                                                        unsigned long long timeout, volatile int* skip) {
+    const unsigned long long t0 = gtimer();
+    for (;;) {
+        const unsigned long long w = ld_relaxed_sys_u64c(a);
+        if ((unsigned int)(w >> 32) == call || *skip) return w;
+        if (gtimer() - t0 > timeout) {
+            atomicOr(err, 1u);
+            *skip = 1;
+            return w;
+        }
+        __nanosleep(32);
+    }
+}
+
+// Second half of a fused all-reduce (the producing matvec stored this rank's
+// partial rows as LL words in every rank's slot): h[i] += slot_0[i] +
+// slot_1[i] + ... in rank order, one thread per element; all of a thread's
+// loads are issued before any wait. The last CTA records the call as
+// completed (every CTA read the count before it counted itself in).
+__global__ void __launch_bounds__(256) comm_ll_reduce_kernel(PeerSet p, float* __restrict__ h, int n) {
+    __shared__ int s_skip;
+    pdl_wait_c();
+    pdl_trigger_c();
+    if (threadIdx.x == 0) s_skip = *reinterpret_cast<volatile unsigned int*>(p.err) != 0u;
+    __syncthreads();
+    const unsigned int call = *reinterpret_cast<volatile const unsigned int*>(p.calls) + 1u;
+    const unsigned long long* slots =
+        reinterpret_cast<const unsigned long long*>(p.base[p.rank] + ll_slot_off(p.world, (int)(call & 1u), 0));
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        unsigned long long w[kCommMaxRanks];
+#pragma unroll
+        for (int r = 0; r < kCommMaxRanks; ++r)
+            if (r < p.world) w[r] = ld_relaxed_sys_u64c(slots + (long long)r * kCommFusedFloats + i);
+        float s = 0.f;
+#pragma unroll
+        for (int r = 0; r < kCommMaxRanks; ++r) {
+            if (r < p.world) {
+                if ((unsigned int)(w[r] >> 32) != call)
+                    w[r] = ll_wait_word(slots + (long long)r * kCommFusedFloats + i, call, p.err, p.timeout_ns, &s_skip);
+                const float v = __uint_as_float((unsigned int)w[r]);
+                s = r ? s + v : v;
+            }
+        }
+        h[i] = h[i] + s;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && atomicAdd(p.counter, 1u) == gridDim.x - 1) {
+        *p.counter = 0u;
+        *p.calls = call;
+    }
+}
+
 template <typename... KArgs, typename... Args>
 int launch_comm(void (*kern)(KArgs...), int grid, int threads, cudaStream_t st, Args... args) {
     cudaLaunchConfig_t cfg = {};
@@ -322,6 +376,13 @@ PeerSet comm_peer_set(neon_comm_impl* c) {
 }
 
 bool fused_collectives() { return g_fused.load(std::memory_order_relaxed) != 0; }
+
+int comm_ll_reduce(neon_comm_impl* c, float* h, long long n, cudaStream_t st) {
+    if (!c || !c->connected) return error(NEON_ERR_INVALID, "communicator not connected");
+    if (n <= 0 || n > kCommFusedFloats) return error(NEON_ERR_INVALID, "fused all-reduce: bad length");
+    const int grid = (int)std::min<long long>((n + 255) / 256, 148);
+    return launch_comm(comm_ll_reduce_kernel, grid, 256, st, comm_peer_set(c), h, (int)n);
+}
 
 int comm_argmax(neon_comm_impl* c, unsigned long long* key, int* d_tok, int* out, int* d_step, int* d_pos, int advance,
                 cudaStream_t st) {

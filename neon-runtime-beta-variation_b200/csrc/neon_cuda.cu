@@ -276,7 +276,6 @@ int launch_stream(const std::vector<const neon_proj_target_t*>& t, int type, int
             a.rope_half = ext->rope_half;
             a.head_dim = ext->head_dim;
             a.peer_mode = ext->peer_mode;
-            a.red_out = ext->red_out;
             if (ext->peer_mode) a.peer = ext->peer;
         }
         a.n_spans = (int)n;
@@ -471,13 +470,13 @@ int matvec_targets(const neon_proj_target_t* targets, size_t n_targets, const fl
         if (rc) return rc;
     }
     if (ext && groups.size() > 1) return set_err(NEON_ERR_UNSUPPORTED, "fused epilogues need one launch group");
+    if (ext && ext->rope_cs && (ext->rope_half < 0 || ext->rope_half > kMaxRopeHalf))
+        return set_err(NEON_ERR_UNSUPPORTED, "RoPE epilogue: rope dimension above 256");
     if (ext && ext->peer_mode) {
-        if (seq != 1 || (ext->peer_mode == 1 && n_targets != 1) ||
-            (ext->peer_mode == 2 && (!ext->norm_w || !ext->red_out)) || ext->peer.world < 1 ||
+        if (seq != 1 || ext->peer_mode != 1 || n_targets != 1 || ext->peer.world < 1 ||
             ext->peer.world > kCommMaxRanks)
             return set_err(NEON_ERR_INVALID, "fused collective: bad launch options");
-        if ((ext->peer_mode == 1 && targets[0].W->rows > (size_t)kCommFusedFloats) ||
-            (ext->peer_mode == 2 && groups[0].cols > (size_t)kCommFusedFloats))
+        if (targets[0].W->rows > (size_t)kCommFusedFloats)
             return set_err(NEON_ERR_UNSUPPORTED, "fused collective: vector longer than its slot");
     }
     for (const Group& g : groups) {

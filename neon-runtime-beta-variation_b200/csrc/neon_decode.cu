@@ -67,6 +67,11 @@ __device__ __forceinline__ float fast_expf_dev(float x) {
     return __int_as_float(__float2int_rz(__fmaf_rn(12102203.9f, x, 1064872507.f)));
 }
 
+// Programmatic dependent launch (see neon_kernels.cuh): wait for the previous
+// kernel's results, and let the next kernel start its prologue.
+__device__ __forceinline__ void pdl_wait_d() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger_d() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ float warp_sum_f(float v) {
 #pragma unroll
     for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -125,6 +130,8 @@ __device__ double block_sum_d(double v, double* scratch) {
 __global__ void embed_kernel(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dpl, int type, int nb,
                              const int* __restrict__ tokens, int n_vocab, float* __restrict__ h,
                              unsigned* err) {
+    pdl_wait_d();
+    pdl_trigger_d();
     const int t = blockIdx.y;
     int tok = tokens[t];
     if (tok < 0 || tok >= n_vocab) {
@@ -283,6 +290,8 @@ __global__ void __launch_bounds__(kThreads) attn_scores_kernel(const float* __re
                                                                float* __restrict__ pmax) {
     __shared__ float qs[kAttnMaxGroup * 256];
     __shared__ float wmax[kAttnMaxGroup][kThreads / 32];
+    pdl_wait_d();
+    pdl_trigger_d();
     const int kvh = blockIdx.x, split = blockIdx.y;
     const int L = *d_pos + 1;
     const int chunk = (L + nsplit - 1) / nsplit;
@@ -328,13 +337,17 @@ __global__ void __launch_bounds__(kThreads) attn_values_kernel(const float* __re
                                                                const float* __restrict__ scores, const float* __restrict__ pmax,
                                                                float* __restrict__ psum, float* __restrict__ pout,
                                                                unsigned int* __restrict__ counters, float* __restrict__ out) {
+    extern __shared__ float psm[];  // [group][chunk] softmax numerators of this split
     __shared__ float gmax[kAttnMaxGroup];
-    __shared__ float red[kThreads];
+    __shared__ float red[kAttnMaxGroup * kThreads];
     __shared__ bool last;
+    pdl_wait_d();
+    pdl_trigger_d();
     const int kvh = blockIdx.x, split = blockIdx.y;
     const int L = *d_pos + 1;
     const int chunk = (L + nsplit - 1) / nsplit;
-    const int s0 = split * chunk, s1 = min(L, s0 + chunk);
+    const int s0 = min(L, split * chunk), s1 = min(L, s0 + chunk);
+    const int len = s1 - s0;
     if ((int)threadIdx.x < group) {
         const float* pm = pmax + ((long long)kvh * group + threadIdx.x) * nsplit;
         float m = -INFINITY;
@@ -342,64 +355,63 @@ __global__ void __launch_bounds__(kThreads) attn_values_kernel(const float* __re
         gmax[threadIdx.x] = m;
     }
     __syncthreads();
-    // threads split (dim, position parity): parts = blockDim / hd
+    // p_s = fast_expf(score_s - max over all positions), once per (head, s)
+    for (int idx = threadIdx.x; idx < group * len; idx += blockDim.x) {
+        const int gq = idx / len, j = idx - gq * len;
+        psm[gq * chunk + j] =
+            fast_expf_dev(__fsub_rn(__ldg(scores + ((long long)kvh * group + gq) * ctx + s0 + j), gmax[gq]));
+    }
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (warp < group) {  // the split's sum of p for head `warp`
+        float sp = 0.f;
+        for (int j = lane; j < len; j += 32) sp += psm[warp * chunk + j];
+        sp = warp_sum_f(sp);
+        if (lane == 0) psum[((long long)kvh * group + warp) * nsplit + split] = sp;
+    }
+    // sum_s p_s v_s[d]: threads split (d, position parity); parts = blockDim / hd
     const int parts = blockDim.x / hd;
     const int d = threadIdx.x % hd, pidx = threadIdx.x / hd;
-    float acc[kAttnMaxGroup], sump[kAttnMaxGroup];
+    float acc[kAttnMaxGroup];
 #pragma unroll
-    for (int gq = 0; gq < kAttnMaxGroup; ++gq) { acc[gq] = 0.f; sump[gq] = 0.f; }
+    for (int gq = 0; gq < kAttnMaxGroup; ++gq) acc[gq] = 0.f;
     if (pidx < parts) {
         const float* vb = Vc + (long long)kvh * hd + d;
 #pragma unroll 4
-        for (int s = s0 + pidx; s < s1; s += parts) {
-            const float v = __ldg(vb + (long long)s * kv_dim);
+        for (int j = pidx; j < len; j += parts) {
+            const float v = __ldg(vb + (long long)(s0 + j) * kv_dim);
 #pragma unroll
-            for (int gq = 0; gq < kAttnMaxGroup; ++gq) {
-                if (gq >= group) break;
-                const float p = fast_expf_dev(__fsub_rn(scores[((long long)kvh * group + gq) * ctx + s], gmax[gq]));
-                acc[gq] = __fmaf_rn(p, v, acc[gq]);
-                sump[gq] += p;
-            }
+            for (int gq = 0; gq < kAttnMaxGroup; ++gq)
+                if (gq < group) acc[gq] = __fmaf_rn(psm[gq * chunk + j], v, acc[gq]);
         }
     }
-    // combine the position parts of this CTA
-    for (int gq = 0; gq < group; ++gq) {
-        red[threadIdx.x] = acc[gq];
-        __syncthreads();
-        if ((int)threadIdx.x < hd) {
-            float r = 0.f;
-            for (int k = 0; k < parts; ++k) r += red[k * hd + threadIdx.x];
-            pout[(((long long)kvh * group + gq) * nsplit + split) * hd + threadIdx.x] = r;
-        }
-        __syncthreads();
-        // the split's sum of p: threads with d == 0 hold disjoint positions
-        red[threadIdx.x] = (d == 0 && pidx < parts) ? sump[gq] : 0.f;
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            float r = 0.f;
-            for (int k = 0; k < parts; ++k) r += red[k * hd];
-            psum[((long long)kvh * group + gq) * nsplit + split] = r;
-        }
-        __syncthreads();
+#pragma unroll
+    for (int gq = 0; gq < kAttnMaxGroup; ++gq)
+        if (gq < group) red[gq * kThreads + threadIdx.x] = acc[gq];
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < group * hd; idx += blockDim.x) {
+        const int gq = idx / hd, dd = idx - gq * hd;
+        float r = 0.f;
+        for (int k = 0; k < parts; ++k) r += red[gq * kThreads + k * hd + dd];
+        pout[(((long long)kvh * group + gq) * nsplit + split) * hd + dd] = r;
     }
-    // the last split CTA of this KV head combines the splits in order: every
-    // writer fences its partials before thread 0 counts this CTA in
+    // the last split CTA of this KV head combines the splits in split order:
+    // every writer fences its partials before thread 0 counts this CTA in
     __threadfence();
     __syncthreads();
     if (threadIdx.x == 0) last = atomicAdd(&counters[kvh], 1u) == (unsigned)(nsplit - 1);
     __syncthreads();
     if (!last) return;
     __threadfence();
-    for (int gq = 0; gq < group; ++gq) {
+    for (int idx = threadIdx.x; idx < group * hd; idx += blockDim.x) {
+        const int gq = idx / hd, dd = idx - gq * hd;
         const long long hb = ((long long)kvh * group + gq) * nsplit;
-        float tot = 0.f;
-        for (int k = 0; k < nsplit; ++k) tot += __ldcg(psum + hb + k);
-        const float inv = __fdiv_rn(1.0f, tot);
-        for (int dd = threadIdx.x; dd < hd; dd += blockDim.x) {
-            float r = 0.f;
-            for (int k = 0; k < nsplit; ++k) r += __ldcg(pout + (hb + k) * hd + dd);
-            out[((long long)kvh * group + gq) * hd + dd] = __fmul_rn(r, inv);
+        float tot = 0.f, r = 0.f;
+        for (int k = 0; k < nsplit; ++k) {
+            tot += __ldcg(psum + hb + k);
+            r += __ldcg(pout + (hb + k) * hd + dd);
         }
+        out[((long long)kvh * group + gq) * hd + dd] = __fmul_rn(r, __fdiv_rn(1.0f, tot));
     }
     if (threadIdx.x == 0) counters[kvh] = 0u;
 }
@@ -433,6 +445,8 @@ __global__ void __launch_bounds__(256) argmax_kernel(const float* __restrict__ l
     __shared__ float bv[8];
     __shared__ int bi[8];
     __shared__ bool last;
+    pdl_wait_d();
+    pdl_trigger_d();
     float best = -INFINITY;
     int idx = 0x7fffffff;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
@@ -491,7 +505,6 @@ struct neon_model {
     neon_tensor_t head = nullptr;    // lm_head shard (tensor parallel only)
     bool head_from_output = false;   // `head` was cut from output.weight, not the tied embedding
     float* part = nullptr;           // partial sums of the column-split projections
-    float* h2 = nullptr;             // second residual buffer of the fused collectives
     float* logits_full = nullptr;    // all-gathered logits (tensor parallel only)
     neon_tensor_t embd = nullptr, output = nullptr;
     float* output_norm = nullptr;
@@ -584,6 +597,34 @@ int tp_shard(const neon_model_config_t& c, int role, int rank, int world, size_t
     return NEON_OK;
 }
 
+// Launch with programmatic dependent launch when enabled (the kernel waits for
+// its predecessor with griddepcontrol.wait before reading its results).
+template <typename... KArgs, typename... Args>
+int launch_k(const char* what, void (*kern)(KArgs...), dim3 grid, int threads, size_t smem, cudaStream_t st,
+             Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(threads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    if (neon_internal::pdl_enabled()) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+    if (e != cudaSuccess) return cuda_error(e, what);
+    return neon_internal::launched(1);
+}
+
+// Dynamic shared memory of attn_values_kernel: the p of one split.
+size_t attn_values_smem(const neon_model* m) {
+    const size_t group = m->cfg.n_head / m->cfg.n_kv_head;
+    return sizeof(float) * group * (((size_t)m->cfg.ctx_len + m->att_split - 1) / m->att_split);
+}
+
 int rmsnorm(neon_model* m, const float* x, const float* w, float* out, int rows) {
     rmsnorm_kernel<<<rows, kThreads, 0, m->stream>>>(x, w, out, (int)m->cfg.n_embd, m->cfg.norm_eps);
     return check_launch("rmsnorm_kernel");
@@ -648,60 +689,33 @@ int run_layers(neon_model* m, const int* toks, int seq) {
     return rc;
 }
 
-// Options of a norm-folded matvec that consumes a pending fused all-reduce:
-// X = x + the ranks' partial sums, the sum written to `out`.
-void consume_pending(neon_model* m, neon_internal::MatvecExt& ext, float* out) {
-    ext.peer_mode = 2;
-    ext.peer = neon_internal::comm_peer_set(m->comm);
-    ext.red_out = out;
-}
-
-// logits of residual row x: rms_norm(output_norm) folded into the lm_head
-// matvec; with `pending`, x still lacks the last fused all-reduce.
-int run_head(neon_model* m, const float* x, bool pending = false) {
+// logits of residual row x: rms_norm(output_norm) folded into the lm_head matvec
+int run_head(neon_model* m, const float* x) {
     neon_tensor_t W = m->world > 1 ? m->head : m->output ? m->output : m->embd;
     neon_proj_target_t t{W, m->logits, m->vocab_l};
     neon_internal::MatvecExt ext;
     ext.norm_w = m->output_norm;
     ext.norm_eps = m->cfg.norm_eps;
-    if (pending) consume_pending(m, ext, x == m->h ? m->h2 : m->h);
     return neon_internal::matvec(&t, 1, x, m->cfg.n_embd, 1, m->stream, 0, &ext);
 }
 
 // One decode position (token in *d_tok, position *d_pos): the fused step.
-// Returns the residual row the lm_head reads in *x_out and, in *pending,
-// whether it still lacks the last fused all-reduce.
 //
 // Tensor parallel with fused collectives: attn_output and ffn_down store their
-// partial rows straight into every rank's slot (no launch of their own), and
-// the next norm-folded matvec (q/k/v, gate/up, lm_head) sums the slots into
-// its X, writing the new residual to the other residual buffer (hc / hn
-// alternate: the launch that sums must not overwrite the X its CTAs read).
-int run_step(neon_model* m, const float** x_out, bool* pending_out) {
+// partial rows as LL words straight into every rank's slot, and a small
+// reduce launch adds the ranks' rows into the residual.
+int run_step(neon_model* m) {
     const auto& c = m->cfg;
     const neon_tensor_t E = m->embd;
     const int nb = (int)(c.n_embd / 32);
-    embed_kernel<<<dim3((nb + 127) / 128, 1), 128, 0, m->stream>>>(E->qs, E->d, E->type, nb, m->d_tok, (int)c.n_vocab,
-                                                                   m->h, m->d_err);
-    int rc = check_launch("embed_kernel");
+    int rc = launch_k("embed_kernel", embed_kernel, dim3((nb + 127) / 128, 1), 128, 0, m->stream, E->qs, E->d, E->type,
+                      nb, m->d_tok, (int)c.n_vocab, m->h, m->d_err);
     const size_t n_embd = c.n_embd, q_dim = m->q_dim, kv_dim = m->kv_dim, n_ff = m->n_ff_l;
     const float scale = 1.0f / std::sqrt((float)c.head_dim);
     const int group = (int)(c.n_head / c.n_kv_head);
     const bool fused = m->world > 1 && neon_internal::fused_collectives();
     float* hc = m->h;
-    float* hn = m->h2;
-    bool pending = false;
-    // a norm-folded launch on hc that takes in the pending all-reduce
-    auto take_pending = [&](neon_internal::MatvecExt& ext) {
-        if (!pending) return;
-        consume_pending(m, ext, hn);
-    };
-    auto swap_after = [&]() {
-        if (!pending) return;
-        std::swap(hc, hn);
-        pending = false;
-    };
-    // h += W x: fused producer, or matvec + all-reduce, or one device's accumulate
+    // h += W x: fused producer + LL reduce, or matvec + all-reduce, or one device's accumulate
     auto residual = [&](neon_tensor_t W, const float* x, size_t x_stride) {
         if (!fused) {
             if (m->world == 1) return proj(m, {{W, hc, n_embd}}, x, x_stride, 1, 1);
@@ -713,8 +727,8 @@ int run_step(neon_model* m, const float** x_out, bool* pending_out) {
         neon_internal::MatvecExt ext;
         ext.peer_mode = 1;
         ext.peer = neon_internal::comm_peer_set(m->comm);
-        const int r = neon_internal::matvec(&t, 1, x, x_stride, 1, m->stream, 0, &ext);
-        pending = true;
+        int r = neon_internal::matvec(&t, 1, x, x_stride, 1, m->stream, 0, &ext);
+        if (!r) r = neon_internal::comm_ll_reduce(m->comm, hc, (long long)n_embd, m->stream);
         return r;
     };
     for (uint32_t li = 0; li < c.n_layer && !rc; ++li) {
@@ -735,23 +749,17 @@ int run_step(neon_model* m, const float** x_out, bool* pending_out) {
             ext.head_dim = (int)c.head_dim;
             ext.epi = epi;
             ext.pos_stride = stride;
-            take_pending(ext);
             rc = neon_internal::matvec(t, 3, hc, n_embd, 1, m->stream, 0, &ext);
-            swap_after();
         }
         if (!rc) {
             const dim3 grid((unsigned)m->n_kv_l, m->att_split);
-            attn_scores_kernel<<<grid, kThreads, 0, m->stream>>>(m->q, Kl, m->d_pos, (int)kv_dim, (int)c.head_dim, group,
-                                                                 scale, m->att_split, (int)c.ctx_len, m->att_scores,
-                                                                 m->att_pmax);
-            rc = check_launch("attn_scores_kernel");
-            if (!rc) {
-                attn_values_kernel<<<grid, kThreads, 0, m->stream>>>(Vl, m->d_pos, (int)kv_dim, (int)c.head_dim, group,
-                                                                     m->att_split, (int)c.ctx_len, m->att_scores,
-                                                                     m->att_pmax, m->att_psum, m->att_pout,
-                                                                     m->att_count, m->att);
-                rc = check_launch("attn_values_kernel");
-            }
+            rc = launch_k("attn_scores_kernel", attn_scores_kernel, grid, kThreads, 0, m->stream, m->q, Kl, m->d_pos,
+                          (int)kv_dim, (int)c.head_dim, group, scale, m->att_split, (int)c.ctx_len, m->att_scores,
+                          m->att_pmax);
+            if (!rc)
+                rc = launch_k("attn_values_kernel", attn_values_kernel, grid, kThreads, attn_values_smem(m), m->stream,
+                              Vl, m->d_pos, (int)kv_dim, (int)c.head_dim, group, m->att_split, (int)c.ctx_len,
+                              m->att_scores, m->att_pmax, m->att_psum, m->att_pout, m->att_count, m->att);
         }
         if (!rc) rc = residual(L.w[3], m->att, q_dim);
         if (!rc) {
@@ -764,22 +772,18 @@ int run_step(neon_model* m, const float** x_out, bool* pending_out) {
             ext.norm_eps = c.norm_eps;
             ext.epi = &epi;
             ext.pos_stride = &stride;
-            take_pending(ext);
             rc = neon_internal::matvec(&t, 1, hc, n_embd, 1, m->stream, 0, &ext);
-            swap_after();
         }
         if (!rc) rc = residual(L.w[4], m->act, n_ff);
     }
-    *x_out = hc;
-    *pending_out = pending;
     return rc;
 }
 
 int launch_argmax(neon_model* m, int advance) {
     const int grid = std::max(1, std::min<int>(148, (int)((m->vocab_l + 1023) / 1024)));
-    argmax_kernel<<<grid, 256, 0, m->stream>>>(m->logits, (int)m->vocab_l, (int)m->vocab0, m->am_key, m->am_count,
-                                               m->d_tok, m->d_out, m->d_step, m->d_pos, advance, m->world == 1);
-    int rc = check_launch("argmax_kernel");
+    int rc = launch_k("argmax_kernel", argmax_kernel, dim3(grid), 256, 0, m->stream, m->logits, (int)m->vocab_l,
+                      (int)m->vocab0, m->am_key, m->am_count, m->d_tok, m->d_out, m->d_step, m->d_pos, advance,
+                      (int)(m->world == 1));
     if (!rc && m->world > 1)
         rc = neon_internal::comm_argmax(m->comm, m->am_key, m->d_tok, m->d_out, m->d_step, m->d_pos, advance, m->stream);
     return rc;
@@ -823,17 +827,15 @@ int forward_device(neon_model* m, const int32_t* tokens_host, size_t n) {
         DEC_TRY(cudaMemcpyAsync(m->d_tokens, tokens_host + off, seq * sizeof(int32_t), cudaMemcpyHostToDevice, m->stream));
         DEC_TRY(cudaMemcpyAsync(m->d_pos, &pos, sizeof(int), cudaMemcpyHostToDevice, m->stream));
         int rc;
-        const float* hx = m->h + (size_t)(seq - 1) * m->cfg.n_embd;
-        bool pending = false;
         if (seq == 1) {
             DEC_TRY(cudaMemcpyAsync(m->d_tok, tokens_host + off, sizeof(int32_t), cudaMemcpyHostToDevice, m->stream));
-            rc = run_step(m, &hx, &pending);
+            rc = run_step(m);
         } else {
             rc = run_layers(m, m->d_tokens, seq);
         }
         if (rc) return rc;
         if (off + seq == n) {
-            rc = run_head(m, hx, pending);
+            rc = run_head(m, m->h + (size_t)(seq - 1) * m->cfg.n_embd);
             if (!rc && m->world > 1)
                 rc = neon_internal::comm_allgather(m->comm, m->logits, m->logits_full, (long long)m->cfg.n_vocab, m->stream);
             if (rc) return rc;
@@ -931,7 +933,6 @@ int neon_cuda_model_create_tp(const neon_model_config_t* cfg, neon_comm_t comm, 
     A((void**)&m->att, sizeof(float) * S * m->q_dim);
     A((void**)&m->gu, sizeof(float) * S * 2 * m->n_ff_l);
     A((void**)&m->act, sizeof(float) * S * m->n_ff_l);
-    A((void**)&m->h2, sizeof(float) * c.n_embd);
     if (world > 1) {
         A((void**)&m->part, sizeof(float) * S * c.n_embd);
         A((void**)&m->logits_full, sizeof(float) * c.n_vocab);
@@ -943,6 +944,8 @@ int neon_cuda_model_create_tp(const neon_model_config_t* cfg, neon_comm_t comm, 
         int sms = neon_internal::device_sms(m->device);
         if (sms <= 0) sms = 148;
         m->att_split = (int)std::max<long long>(1, std::min<long long>((c.ctx_len + 31) / 32, (2LL * sms) / (long long)m->n_kv_l));
+        // the p of a split must fit attn_values_kernel's shared memory
+        while (attn_values_smem(m) > 160 * 1024) ++m->att_split;
     }
     A((void**)&m->att_scores, sizeof(float) * m->n_head_l * c.ctx_len);
     A((void**)&m->att_pmax, sizeof(float) * m->n_head_l * m->att_split);
@@ -977,6 +980,11 @@ int neon_cuda_model_create_tp(const neon_model_config_t* cfg, neon_comm_t comm, 
             cudaMemset(m->att_count, 0, sizeof(unsigned int) * m->n_kv_l) != cudaSuccess ||
             cudaMemset(m->V, 0, kv_bytes) != cudaSuccess)
             rc = error(NEON_ERR_CUDA, "model initialisation copies failed");
+    }
+    if (!rc && attn_values_smem(m) > 48 * 1024) {
+        if (cudaFuncSetAttribute(attn_values_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn_values_smem(m)) !=
+            cudaSuccess)
+            rc = error(NEON_ERR_CUDA, "cudaFuncSetAttribute(attn_values_kernel)");
     }
     if (!rc && c.ctx_len * sizeof(float) > 48 * 1024) {
         if (cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(c.ctx_len * sizeof(float))) != cudaSuccess)
@@ -1141,10 +1149,8 @@ int neon_cuda_model_generate(neon_model_t m, const int32_t* prompt, size_t n_pro
         }
         cudaGraph_t g = nullptr;
         DEC_TRY(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
-        const float* hx = nullptr;
-        bool pending = false;
-        rc = run_step(m, &hx, &pending);
-        if (!rc) rc = run_head(m, hx, pending);
+        rc = run_step(m);
+        if (!rc) rc = run_head(m, m->h);
         if (!rc) rc = launch_argmax(m, 1);
         cudaError_t ce = cudaStreamEndCapture(m->stream, &g);
         if (rc) {

@@ -70,16 +70,16 @@ __host__ __device__ inline unsigned long long ll_pack(float v, unsigned int call
     return ((unsigned long long)call << 32) | b.u;
 }
 
-// What a matvec launch needs to take part in a fused (LL) collective: the
-// producing launch (attn_output / ffn_down of one position) stores each row
-// as an LL word into slot [parity][rank] of every rank; the consuming launch
-// (the next norm-folded matvec) polls the words of all ranks' slots while it
-// stages X = residual + (slot_0 + slot_1 + ...), the bulk kernel's sum, bit
-// for bit, and its last CTA advances the call count.
+// What a matvec launch needs to produce a fused (LL) all-reduce: the
+// column-split projection (attn_output / ffn_down of one position) stores
+// each row as an LL word into slot [parity][rank] of every rank; the
+// communicator's LL reduce kernel then polls the words of all ranks' slots
+// and adds slot_0 + slot_1 + ... (the bulk kernel's order, bit for bit) into
+// the residual, and records the call as completed.
 struct PeerSet {
     unsigned char* base[kCommMaxRanks];  // every rank's LL region (this process's mappings)
     unsigned int* calls;                 // this rank's count of completed LL collectives (device)
-    unsigned int* counter;               // last-CTA election of a consuming launch (device)
+    unsigned int* counter;               // last-CTA election of the reduce kernel (device)
     unsigned int* err;                   // the communicator's error word
     unsigned long long timeout_ns;
     int rank, world;
@@ -112,6 +112,9 @@ int comm_argmax(neon_comm_impl* c, unsigned long long* key, int* d_tok, int* out
                 int advance, cudaStream_t st);
 // The fused-collective view of a connected communicator.
 PeerSet comm_peer_set(neon_comm_impl* c);
+// Completes a fused all-reduce a producing matvec started: h[i] += slot_0[i]
+// + slot_1[i] + ... for i < n, waiting (bounded) for every rank's words.
+int comm_ll_reduce(neon_comm_impl* c, float* h, long long n, cudaStream_t st);
 bool fused_collectives();
 
 // Decode-step options of a one-position matvec launch (seq == 1 only):
@@ -127,12 +130,10 @@ struct MatvecExt {
     int head_dim = 0;
     const int* epi = nullptr;               // per target; null: plain store
     const long long* pos_stride = nullptr;  // per target
-    // fused collective: 1 = produce (one target; its rows go to every rank's
-    // slot), 2 = consume (X += the ranks' slots; needs norm_w; CTA 0 writes
-    // the summed X, the new residual, to red_out)
+    // 1: produce a fused collective (one target, one position): the rows go
+    // as LL words to every rank's slot instead of to Y
     int peer_mode = 0;
     PeerSet peer{};
-    float* red_out = nullptr;
 };
 
 // neon_cuda_matvec_multi on `st`, with y += result when `accumulate`.

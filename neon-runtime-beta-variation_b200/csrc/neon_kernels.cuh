@@ -308,6 +308,7 @@ __device__ __forceinline__ void store_tile(const float (&acc)[R], float* y, int 
 // ---------------------------------------------------------------------------
 constexpr int kStreamWarps = 8;
 constexpr int kStreamThreads = kStreamWarps * 32;
+constexpr int kMaxRopeHalf = 128;  // head_dim <= 256
 constexpr int kMaxStages = 3;
 
 struct StreamArgs {
@@ -329,8 +330,7 @@ struct StreamArgs {
     const float2* rope_cs;  // [position][rope_half] (cos, sin)
     int rope_half;
     int head_dim;
-    int peer_mode;          // fused collective: 1 produce, 2 consume (neon_internal::MatvecExt)
-    float* red_out;         // consume: CTA 0 writes the summed X here
+    int peer_mode;          // 1: fused collective producer (neon_internal::MatvecExt)
     PeerSet peer;
 };
 
@@ -373,70 +373,8 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 
 // Wait for phase `parity` of `bar`; give up after ~2 s, record the timeout in
 // *err and return false (the caller leaves the kernel, CTA-uniformly).
-__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
-    unsigned long long v;
-    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-    return v;
-}
-
 __device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
     asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-
-// The consuming side of an LL collective inside a launch: rank r's partial
-// of element i is LL word slots[r * kCommFusedFloats + i] once it carries
-// `call`. Every poll is bounded by the communicator's timeout; the first wait
-// that runs out sets bit 0 of the error word and *skip, after which (as when
-// the communicator was already in error) nothing waits and the launch runs
-// on with whatever the words hold.
-struct LLView {
-    const unsigned long long* slots;  // rank 0's slot of this call's parity; null: nothing pending
-    unsigned int call;
-    int world;
-    unsigned int* err;
-    unsigned long long timeout_ns;
-    volatile int* skip;               // shared memory
-};
-
-__device__ __forceinline__ float ll_wait(const unsigned long long* p, unsigned int call, unsigned int* err,
-                                      unsigned long long timeout_ns, volatile int* skip) {
-    const uint64_t t0 = globaltimer_ns();
-    unsigned long long w;
-    for (;;) {
-        w = ld_relaxed_sys_u64(p);
-        if ((unsigned int)(w >> 32) == call || *skip) break;
-        if (globaltimer_ns() - t0 > timeout_ns) {
-            atomicOr(err, 1u);
-            *skip = 1;
-            break;
-        }
-        __nanosleep(32);
-    }
-    return __uint_as_float((unsigned int)w);
-}
-
-__device__ __forceinline__ float ll_value(const unsigned long long* p, const LLView& v) {
-    const unsigned long long w = ld_relaxed_sys_u64(p);
-    if ((unsigned int)(w >> 32) == v.call) return __uint_as_float((unsigned int)w);
-    return ll_wait(p, v.call, v.err, v.timeout_ns, v.skip);
-}
-
-// slot_0[i] + slot_1[i] + ... in rank order (the bulk kernel's sum), waiting
-// for every word to carry the call
-__device__ __forceinline__ float ll_sum_wait(const LLView& v, long long i) {
-    float s = ll_value(v.slots + i, v);
-    for (int r = 1; r < v.world; ++r) s += ll_value(v.slots + (long long)r * kCommFusedFloats + i, v);
-    return s;
-}
-
-// The same sum once this CTA has seen every word carry the call (after
-// ll_sum_wait over all i and a barrier): the words cannot change again before
-// the call after next, so plain reads suffice.
-__device__ __forceinline__ float ll_sum(const LLView& v, long long i) {
-    float s = __uint_as_float((unsigned int)ld_relaxed_sys_u64(v.slots + i));
-    for (int r = 1; r < v.world; ++r)
-        s += __uint_as_float((unsigned int)ld_relaxed_sys_u64(v.slots + (long long)r * kCommFusedFloats + i));
-    return s;
 }
 
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int* err) {
@@ -480,21 +418,10 @@ __host__ __device__ constexpr int stream_x_bytes(int type, int nb) {
 // rms_norm's scale 1/sqrt(mean(x^2) + eps) of n floats (fwd::rms_norm,
 // rawllm_forward.hpp:730-735): a double sum of squares over the whole CTA,
 // so every CTA of the launch derives the same scale.
-// X element i, with a pending fused all-reduce folded in when `ll` has
-// slots: x[i] + ((slot_0[i] + slot_1[i]) + ...), the bulk kernel's order.
-__device__ __forceinline__ float x_plus_slots(const float* __restrict__ x, int i, const LLView& ll) {
-    const float v = __ldg(x + i);
-    if (!ll.slots) return v;
-    return v + ll_sum(ll, i);
-}
-
-__device__ __forceinline__ float cta_rms_scale(const float* __restrict__ x, int n, float eps, double* scratch,
-                                               const LLView& ll, float* out = nullptr) {
+__device__ __forceinline__ float cta_rms_scale(const float* __restrict__ x, int n, float eps, double* scratch) {
     double ss = 0.0;
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        const float xv = ll.slots ? __ldg(x + i) + ll_sum_wait(ll, i) : __ldg(x + i);
-        if (out) out[i] = xv;
-        const double v = (double)xv;
+        const double v = (double)__ldg(x + i);
         ss = fma(v, v, ss);
     }
 #pragma unroll
@@ -514,9 +441,73 @@ __device__ __forceinline__ float cta_rms_scale(const float* __restrict__ x, int 
 // threads of one block are always all active or all idle.
 // With norm_w, each element is first replaced by (x * scale) * w, rms_norm's
 // output (the reference multiplies in that order).
+// Q8_0 record of the EPT elements xv[] a thread holds of block b (TPB
+// threads per block, `part` this thread's share): amax over the TPB lanes,
+// d = amax/127, q = clamp(lround(x / d)), and the block's sum of q.
+template <int TPB>
+__device__ __forceinline__ void quantize_store_q8(float (&xv)[32 / TPB], bool act, int b, int part,
+                                                  unsigned char* rec) {
+    constexpr int EPT = 32 / TPB;
+    float amax = 0.f;
+#pragma unroll
+    for (int j = 0; j < EPT; ++j) amax = fmaxf(amax, fabsf(xv[j]));
+#pragma unroll
+    for (int o = 1; o < TPB; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float d = __fdiv_rn(amax, 127.0f);
+    const float id = d > 0.f ? __fdiv_rn(1.0f, d) : 0.f;
+    uint32_t q[EPT / 4];
+    int s = 0;
+#pragma unroll
+    for (int k = 0; k < EPT / 4; ++k) {
+        uint32_t w = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int v = q8_round_clamp(__fmul_rn(xv[4 * k + j], id));
+            s += v;
+            w |= (uint32_t)(v & 0xFF) << (8 * j);
+        }
+        q[k] = w;
+    }
+#pragma unroll
+    for (int o = 1; o < TPB; o <<= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (act) {
+        uint32_t* r32 = reinterpret_cast<uint32_t*>(rec + b * kQ4Rec) + part * (EPT / 4);
+#pragma unroll
+        for (int k = 0; k < EPT / 4; ++k) r32[k] = q[k];
+        if (part == 0)
+            *reinterpret_cast<uint2*>(rec + b * kQ4Rec + 32) = make_uint2(__float_as_uint(d), (uint32_t)s);
+    }
+}
+
+// The EPT elements of X thread `part` of block b holds.
+template <int TPB>
+__device__ __forceinline__ void load_x_part(const float* __restrict__ x, bool x_vec, bool act, int b, int part,
+                                            float (&xv)[32 / TPB]) {
+    constexpr int EPT = 32 / TPB;
+    const long long e0 = (long long)b * 32 + part * EPT;
+    if (act && x_vec) {
+#pragma unroll
+        for (int k = 0; k < EPT / 4; ++k) {
+            const float4 v = __ldg(reinterpret_cast<const float4*>(x + e0) + k);
+            xv[4 * k] = v.x; xv[4 * k + 1] = v.y; xv[4 * k + 2] = v.z; xv[4 * k + 3] = v.w;
+        }
+    } else if (act) {
+#pragma unroll
+        for (int j = 0; j < EPT; ++j) xv[j] = __ldg(x + e0 + j);
+    } else {
+#pragma unroll
+        for (int j = 0; j < EPT; ++j) xv[j] = 0.f;
+    }
+}
+
+// Quantise X (nb blocks) into the CTA's Q8_0 records, TPB threads per block.
+// Whole warps iterate together (the shuffles need every lane); the TPB
+// threads of one block are always all active or all idle.
+// With norm_w, each element is first replaced by (x * scale) * w, rms_norm's
+// output (the reference multiplies in that order).
 template <int TPB>
 __device__ __forceinline__ void stage_x_q8(const float* __restrict__ x, int nb, bool x_vec, unsigned char* rec,
-                                           const float* __restrict__ norm_w, float scale, const LLView& ll) {
+                                           const float* __restrict__ norm_w, float scale) {
     constexpr int EPT = 32 / TPB;
     const int lane = threadIdx.x & 31;
     const int n = nb * TPB;
@@ -524,63 +515,48 @@ __device__ __forceinline__ void stage_x_q8(const float* __restrict__ x, int nb, 
         const int i = i0 + lane;
         const bool act = i < n;
         const int b = act ? i / TPB : 0, part = i % TPB;
-        const float* xb = x + (long long)b * 32 + part * EPT;
         float xv[EPT];
-        if (act && x_vec) {
-#pragma unroll
-            for (int k = 0; k < EPT / 4; ++k) {
-                float4 v = __ldg(reinterpret_cast<const float4*>(xb) + k);
-                if (ll.slots) {
-                    const long long e = (long long)b * 32 + part * EPT + 4 * k;
-                    v.x = v.x + ll_sum(ll, e);
-                    v.y = v.y + ll_sum(ll, e + 1);
-                    v.z = v.z + ll_sum(ll, e + 2);
-                    v.w = v.w + ll_sum(ll, e + 3);
-                }
-                xv[4 * k] = v.x; xv[4 * k + 1] = v.y; xv[4 * k + 2] = v.z; xv[4 * k + 3] = v.w;
-            }
-        } else if (act) {
-#pragma unroll
-            for (int j = 0; j < EPT; ++j) xv[j] = x_plus_slots(x, b * 32 + part * EPT + j, ll);
-        } else {
-#pragma unroll
-            for (int j = 0; j < EPT; ++j) xv[j] = 0.f;
-        }
+        load_x_part<TPB>(x, x_vec, act, b, part, xv);
         if (norm_w && act) {
             const float* wb = norm_w + (long long)b * 32 + part * EPT;
 #pragma unroll
             for (int j = 0; j < EPT; ++j) xv[j] = __fmul_rn(__fmul_rn(xv[j], scale), __ldg(wb + j));
         }
-        float amax = 0.f;
-#pragma unroll
-        for (int j = 0; j < EPT; ++j) amax = fmaxf(amax, fabsf(xv[j]));
-#pragma unroll
-        for (int o = 1; o < TPB; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-        const float d = __fdiv_rn(amax, 127.0f);
-        const float id = d > 0.f ? __fdiv_rn(1.0f, d) : 0.f;
-        uint32_t q[EPT / 4];
-        int s = 0;
-#pragma unroll
-        for (int k = 0; k < EPT / 4; ++k) {
-            uint32_t w = 0;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int v = q8_round_clamp(__fmul_rn(xv[4 * k + j], id));
-                s += v;
-                w |= (uint32_t)(v & 0xFF) << (8 * j);
-            }
-            q[k] = w;
-        }
-#pragma unroll
-        for (int o = 1; o < TPB; o <<= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-        if (act) {
-            uint32_t* r32 = reinterpret_cast<uint32_t*>(rec + b * kQ4Rec) + part * (EPT / 4);
-#pragma unroll
-            for (int k = 0; k < EPT / 4; ++k) r32[k] = q[k];
-            if (part == 0)
-                *reinterpret_cast<uint2*>(rec + b * kQ4Rec + 32) = make_uint2(__float_as_uint(d), (uint32_t)s);
-        }
+        quantize_store_q8<TPB>(xv, act, b, part, rec);
     }
+}
+
+// rms_norm folded into the Q8_0 staging in one pass, when the CTA's threads
+// cover X once (nb * TPB <= kStreamThreads): every thread loads its elements,
+// the CTA reduces the double sum of squares, and the same registers are
+// scaled, multiplied by the norm weight and quantised.
+template <int TPB>
+__device__ __forceinline__ void stage_x_q8_norm(const float* __restrict__ x, int nb, bool x_vec, unsigned char* rec,
+                                                const float* __restrict__ norm_w, float eps, double* scratch) {
+    constexpr int EPT = 32 / TPB;
+    const int i = threadIdx.x;
+    const bool act = i < nb * TPB;
+    const int b = act ? i / TPB : 0, part = i % TPB;
+    const long long e0 = (long long)b * 32 + part * EPT;
+    float xv[EPT];
+    load_x_part<TPB>(x, x_vec, act, b, part, xv);
+    double ss = 0.0;
+#pragma unroll
+    for (int j = 0; j < EPT; ++j) ss = fma((double)xv[j], (double)xv[j], ss);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    if (l == 0) scratch[w] = ss;
+    __syncthreads();
+    double r = l < kStreamWarps ? scratch[l] : 0.0;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)(r / (double)(nb * 32)), eps)));
+    if (act) {
+#pragma unroll
+        for (int j = 0; j < EPT; ++j) xv[j] = __fmul_rn(__fmul_rn(xv[j], scale), __ldg(norm_w + e0 + j));
+    }
+    quantize_store_q8<TPB>(xv, act, b, part, rec);
 }
 
 // Packed fp32x2 arithmetic of sm_100 (one instruction, two lanes of fp32).
@@ -637,9 +613,12 @@ __device__ __forceinline__ float silu_dev(float x) {
 }
 
 // Writes the RC row results of a tile (rowv[], shared memory) through the
-// span's epilogue; threads t < RC own row row0 + t.
+// span's epilogue; threads t < RC own row row0 + t. `pos` is the token's
+// position, `rcs` its RoPE (cos, sin) row staged in shared memory, `yold` the
+// row's previous output (read ahead of the dot products when accumulating).
 __device__ __forceinline__ void stream_epilogue(const StreamArgs& a, const Span& sp, int row0, int RC,
-                                                const float* rowv, unsigned int peer_call) {
+                                                const float* rowv, unsigned int peer_call, int pos,
+                                                const float2* rcs, float yold) {
     const int t = threadIdx.x;
     if (t >= RC) return;
     const int row = row0 + t;
@@ -647,22 +626,21 @@ __device__ __forceinline__ void stream_epilogue(const StreamArgs& a, const Span&
     const float v = rowv[t];
     switch (sp.epi) {
         case kEpiStore:
-            sp.y[row] = a.accumulate ? sp.y[row] + v : v;
+            sp.y[row] = a.accumulate ? yold + v : v;
             break;
         case kEpiAtPos:
-            sp.y[(long long)(*a.d_pos) * sp.pos_stride + row] = v;
+            sp.y[(long long)pos * sp.pos_stride + row] = v;
             break;
         case kEpiRope: {
             // rotate (v_2i, v_2i+1) of a head by the position's angle
             // (fwd::rope_apply, rawllm_forward.hpp:767-782, with g++'s FMA
             // contraction); pairs at or beyond rope_half are stored unrotated
-            const int pos = *a.d_pos;
             float* dst = sp.y + (long long)pos * sp.pos_stride;
             if (t & 1) break;
             const float x0 = v, x1 = rowv[t + 1];
             const int i = (row % a.head_dim) / 2;
             if (i < a.rope_half) {
-                const float2 c = a.rope_cs[(long long)pos * a.rope_half + i];
+                const float2 c = rcs[i];
                 dst[row] = __fmaf_rn(x0, c.x, -__fmul_rn(x1, c.y));
                 dst[row + 1] = __fmaf_rn(x0, c.y, __fmul_rn(x1, c.x));
             } else {
@@ -768,42 +746,35 @@ __global__ void __launch_bounds__(kStreamThreads) matvec_stream_kernel(const __g
     }
     pdl_wait();
 
-    // Fused (LL) collective: this launch's call number -- the next one after
-    // the last completed -- and, for a consumer, the view of the ranks' slots.
-    unsigned int peer_call = 0;
-    __shared__ int ll_skip;
-    LLView ll;
-    ll.slots = nullptr;
-    if (a.peer_mode) {
-        peer_call = *reinterpret_cast<volatile const unsigned int*>(a.peer.calls) + 1u;
-        if (a.peer_mode == 2) {
-            if (threadIdx.x == 0) ll_skip = *reinterpret_cast<volatile const unsigned int*>(a.peer.err) != 0u;
-            __syncthreads();
-            ll.slots = reinterpret_cast<const unsigned long long*>(
-                a.peer.base[a.peer.rank] + ll_slot_off(a.peer.world, (int)(peer_call & 1u), 0));
-            ll.call = peer_call;
-            ll.world = a.peer.world;
-            ll.err = a.peer.err;
-            ll.timeout_ns = a.peer.timeout_ns;
-            ll.skip = &ll_skip;
-        }
-    }
+    // Fused (LL) collective, producing side: this launch's call number, the
+    // one after the last completed.
+    const unsigned int peer_call =
+        a.peer_mode ? *reinterpret_cast<volatile const unsigned int*>(a.peer.calls) + 1u : 0u;
+
+    // the token's position and its RoPE row, read once per launch
+    __shared__ float2 rcs[kMaxRopeHalf];
+    const int pos = a.d_pos ? *a.d_pos : 0;
+    if (a.rope_cs)
+        for (int i = threadIdx.x; i < a.rope_half; i += kStreamThreads) rcs[i] = a.rope_cs[(long long)pos * a.rope_half + i];
 
     // Stage X once per CTA (normalised first when asked), then let the next
     // launch start.
     __shared__ double dscratch[32];
-    const float nscale = a.norm_w ? cta_rms_scale(a.x, nb * 32, a.norm_eps, dscratch, ll,
-                                                  blockIdx.x == 0 ? a.red_out : nullptr)
-                                  : 1.f;
-    if (TYPE == 2) {
-        const int tpb = kStreamThreads / nb;
-        if (tpb >= 4) stage_x_q8<4>(a.x, nb, a.x_vec, xsm, a.norm_w, nscale, ll);
-        else if (tpb >= 2) stage_x_q8<2>(a.x, nb, a.x_vec, xsm, a.norm_w, nscale, ll);
-        else stage_x_q8<1>(a.x, nb, a.x_vec, xsm, a.norm_w, nscale, ll);
+    const int tpb = TYPE == 2 ? kStreamThreads / nb : 0;
+    if (TYPE == 2 && a.norm_w && tpb >= 1) {
+        if (tpb >= 4) stage_x_q8_norm<4>(a.x, nb, a.x_vec, xsm, a.norm_w, a.norm_eps, dscratch);
+        else if (tpb >= 2) stage_x_q8_norm<2>(a.x, nb, a.x_vec, xsm, a.norm_w, a.norm_eps, dscratch);
+        else stage_x_q8_norm<1>(a.x, nb, a.x_vec, xsm, a.norm_w, a.norm_eps, dscratch);
+    } else if (TYPE == 2) {
+        const float nscale = a.norm_w ? cta_rms_scale(a.x, nb * 32, a.norm_eps, dscratch) : 1.f;
+        if (tpb >= 4) stage_x_q8<4>(a.x, nb, a.x_vec, xsm, a.norm_w, nscale);
+        else if (tpb >= 2) stage_x_q8<2>(a.x, nb, a.x_vec, xsm, a.norm_w, nscale);
+        else stage_x_q8<1>(a.x, nb, a.x_vec, xsm, a.norm_w, nscale);
     } else {
+        const float nscale = a.norm_w ? cta_rms_scale(a.x, nb * 32, a.norm_eps, dscratch) : 1.f;
         float* xs = reinterpret_cast<float*>(xsm);
         for (int i = threadIdx.x; i < nb * 32; i += kStreamThreads) {
-            float v = x_plus_slots(a.x, i, ll);
+            float v = __ldg(a.x + i);
             if (a.norm_w) v = __fmul_rn(__fmul_rn(v, nscale), __ldg(a.norm_w + i));
             xs[(i >> 5) * kQ8Pitch + (i & 31)] = v;
         }
@@ -825,6 +796,11 @@ __global__ void __launch_bounds__(kStreamThreads) matvec_stream_kernel(const __g
         const int kc = min(KC, nb - k0);
         const bool ok = mbar_wait(&full[stage], parity, a.err);
         if (__syncthreads_or(!ok)) return;
+        // the accumulate epilogue's y[row], fetched while the dot products run
+        float yold = 0.f;
+        if (a.accumulate && chunk == nch - 1 && sp.epi == kEpiStore && (int)threadIdx.x < RC &&
+            row0 + (int)threadIdx.x < sp.rows)
+            yold = sp.y[row0 + threadIdx.x];
 
         const unsigned char* pay = ring + stage * a.stage_bytes;
         const uint16_t* sc = reinterpret_cast<const uint16_t*>(pay + RC * KC * P);
@@ -873,6 +849,13 @@ __global__ void __launch_bounds__(kStreamThreads) matvec_stream_kernel(const __g
         }
 #pragma unroll
         for (int rr = 0; rr < R; ++rr) acc[rr] += part[rr];
+        // every warp is done with this stage: refill it before the row
+        // reduction and the epilogue, so their latency overlaps the copy
+        __syncthreads();
+        if (warp == 0 && item + S < n_items) {
+            fence_proxy_async_smem();
+            issue(item + S);
+        }
         if (chunk == nch - 1) {
 #pragma unroll
             for (int rr = 0; rr < R; ++rr)
@@ -896,23 +879,9 @@ __global__ void __launch_bounds__(kStreamThreads) matvec_stream_kernel(const __g
                 rowv[threadIdx.x] = v;
             }
             if (WPG > 1) __syncthreads();
-            stream_epilogue(a, sp, row0, RC, rowv, peer_call);
+            stream_epilogue(a, sp, row0, RC, rowv, peer_call, pos, rcs, yold);
 #pragma unroll
             for (int rr = 0; rr < R; ++rr) acc[rr] = 0.f;
-        }
-        __syncthreads();  // every warp is done with this stage (and with red[])
-        if (warp == 0 && item + S < n_items) {
-            fence_proxy_async_smem();
-            issue(item + S);
-        }
-    }
-    if (a.peer_mode == 2) {
-        // The last CTA to finish records the call as completed: every CTA read
-        // the count before it counted itself in here.
-        __syncthreads();
-        if (threadIdx.x == 0 && atomicAdd(a.peer.counter, 1u) == gridDim.x - 1) {
-            *a.peer.counter = 0u;
-            *a.peer.calls = peer_call;
         }
     }
 }

@@ -55,6 +55,38 @@ def q8_0_weights(rows: int, cols: int, seed: int, scale: float = 0.01) -> np.nda
     return out.reshape(rows, nb * 34)
 
 
+_POOL_BLOCKS = 1 << 23  # 8M blocks: 144 MB of Q4_0, 272 MB of Q8_0
+_pools = {}
+
+
+def pooled_weights(ggml_type: int, rows: int, cols: int, seed: int) -> np.ndarray:
+    """rows x cols GGUF bytes cut from a seeded pool of 8M random blocks (same
+    per-block distributions as q4_0_weights / q8_0_weights) at a seeded
+    offset: a read-only view when the tensor fits in the pool, else a copy
+    that repeats the pool. For benchmark models of tens of GB, where drawing
+    every block would take minutes; tensors are not independent of one another."""
+    if ggml_type not in _pools:
+        gen = q4_0_weights if ggml_type == GGML_Q4_0 else q8_0_weights
+        pool = gen(_POOL_BLOCKS // 256, 256 * BLOCK, seed=987654321).reshape(-1)
+        pool.flags.writeable = False
+        _pools[ggml_type] = pool
+    pool = _pools[ggml_type]
+    bb = BLOCK_BYTES[ggml_type]
+    n = rows * (cols // BLOCK)
+    rng = np.random.default_rng(seed)
+    if n <= _POOL_BLOCKS:
+        off = int(rng.integers(0, _POOL_BLOCKS - n + 1)) * bb
+        return pool[off:off + n * bb].reshape(rows, (cols // BLOCK) * bb)
+    out = np.empty(n * bb, np.uint8)
+    pos, src = 0, int(rng.integers(0, _POOL_BLOCKS)) * bb
+    while pos < out.size:
+        k = min(out.size - pos, pool.size - src)
+        out[pos:pos + k] = pool[src:src + k]
+        pos += k
+        src = 0
+    return out.reshape(rows, (cols // BLOCK) * bb)
+
+
 def weights(ggml_type: int, rows: int, cols: int, seed: int) -> np.ndarray:
     if ggml_type == GGML_Q4_0:
         return q4_0_weights(rows, cols, seed)
@@ -123,19 +155,21 @@ LLAMA3_70B = ModelConfig(128256, 8192, 80, 64, 8, 128, 28672, ctx_len=2432, rope
 
 
 def model_tensors(cfg: ModelConfig, seed: int, wtype: int = GGML_Q4_0, embd_type: int = GGML_Q8_0,
-                  tied: bool = True):
+                  tied: bool = True, pooled: bool = False):
     """Seeded random-init tensors of a decoder, in GGUF layout:
     yields (role, layer, raw bytes uint8, ggml type, ne0, ne1); ne1 = 0 for 1-D.
     Projections are `wtype` with the benchmark's block distributions, the
-    embedding (also the lm_head when tied) is `embd_type`, norm weights fp32 1."""
+    embedding (also the lm_head when tied) is `embd_type`, norm weights fp32 1.
+    `pooled`: tensors cut from one random block pool (pooled_weights)."""
+    weights_fn = pooled_weights if pooled else weights
     def sub(role, layer):
         return seed * 1000003 + role * 10007 + layer + 1
 
     ones = np.ones(cfg.n_embd, np.float32).view(np.uint8)
-    yield ROLE_TOKEN_EMBD, -1, weights(embd_type, cfg.n_vocab, cfg.n_embd, sub(0, 0)), embd_type, cfg.n_embd, cfg.n_vocab
+    yield ROLE_TOKEN_EMBD, -1, weights_fn(embd_type, cfg.n_vocab, cfg.n_embd, sub(0, 0)), embd_type, cfg.n_embd, cfg.n_vocab
     yield ROLE_OUTPUT_NORM, -1, ones, GGML_F32, cfg.n_embd, 0
     if not tied:
-        yield ROLE_OUTPUT, -1, weights(wtype, cfg.n_vocab, cfg.n_embd, sub(2, 0)), wtype, cfg.n_embd, cfg.n_vocab
+        yield ROLE_OUTPUT, -1, weights_fn(wtype, cfg.n_vocab, cfg.n_embd, sub(2, 0)), wtype, cfg.n_embd, cfg.n_vocab
     shapes = {ROLE_ATTN_Q: (cfg.q_dim, cfg.n_embd), ROLE_ATTN_K: (cfg.kv_dim, cfg.n_embd),
               ROLE_ATTN_V: (cfg.kv_dim, cfg.n_embd), ROLE_ATTN_OUT: (cfg.n_embd, cfg.q_dim),
               ROLE_FFN_GATE: (cfg.n_ff, cfg.n_embd), ROLE_FFN_UP: (cfg.n_ff, cfg.n_embd),
@@ -144,7 +178,7 @@ def model_tensors(cfg: ModelConfig, seed: int, wtype: int = GGML_Q4_0, embd_type
         yield ROLE_ATTN_NORM, li, ones, GGML_F32, cfg.n_embd, 0
         yield ROLE_FFN_NORM, li, ones, GGML_F32, cfg.n_embd, 0
         for role, (rows, cols) in shapes.items():
-            yield role, li, weights(wtype, rows, cols, sub(role, li)), wtype, cols, rows
+            yield role, li, weights_fn(wtype, rows, cols, sub(role, li)), wtype, cols, rows
 
 
 def prompt_tokens(n: int, n_vocab: int, seed: int) -> np.ndarray:
