@@ -104,7 +104,9 @@ def parse_args():
                    help="decode workloads at N>1: one all-reduce launch per column-split projection")
     p.add_argument("--layers", type=int, default=None,
                    help="decode workloads: fewer layers (kernel shapes unchanged; for profiling)")
-    p.add_argument("--no-decode", action="store_true", help="matvec workloads: skip the decode sub-measurement")
+    p.add_argument("--no-decode", action="store_true", help="matvec workloads: skip the decode sub-measurements")
+    p.add_argument("--no-large-decode", action="store_true",
+                   help="matvec workloads: skip the Llama-3-70B-shaped split decode sub-measurement")
     args = p.parse_args()
     select_workload(args.workload)
     global LAYERS
@@ -305,6 +307,20 @@ def measure_decode_gpu(name, prompt=None, new_tokens=None, comm=None, barrier=No
             "load_s": round(load_s, 2)}, cfg, prompt_toks
 
 
+def decode_roofline(d, cfg, world):
+    """Effective HBM rate of a decode step: the bytes one rank streams per
+    token (its share of the weights, plus K and V of the average context)
+    over the device time per token, against the measured copy bandwidth."""
+    peak, kind = measured_peak()
+    kv = 2 * cfg.n_layer * cfg.kv_dim * 4 / world
+    ctx_avg = cfg.ctx_len - 1 - (d["generated"] / 2 if d.get("generated") else 0)
+    per_token = model_bytes(cfg) / world + kv * ctx_avg
+    gbs = per_token / (d["ms_per_token"] * 1e-3) / 1e9
+    d["hbm"] = {"bytes_per_token_per_gpu": int(per_token), "achieved_gbs_per_gpu": round(gbs, 1),
+                "peak_gbs": peak, "peak_source": kind, "frac": round(gbs / peak, 4)}
+    return d
+
+
 def measure_decode_cpu(cfg, prompt_toks, steps, threads=None):
     """The reference's own transformer_forward (oracle/_ref) on the host:
     prompt prefill, then `steps` greedy decode steps; tokens/s of the decode."""
@@ -373,7 +389,8 @@ def run_decode(args):
                 "data": "synthetic", "config": {"workload": res["workload"], "parallelism": res["parallelism"]},
                 "e2e": {"value": res["e2e_tokens_per_s"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 4, "api": res["e2e"]},
-                "load_s": res["load_s"], "cpu_baseline": cpu, "clocks": sampler.summary(t0, t1)}
+                "load_s": res["load_s"], "roofline": decode_roofline(dict(res), cfg, world)["hbm"],
+                "cpu_baseline": cpu, "clocks": sampler.summary(t0, t1)}
         print(json.dumps(line), flush=True)
     if comm is not None:
         barrier()
@@ -576,17 +593,44 @@ def run_neon(args):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_reference_gbs(host_w, x_host, args.cpu_seconds)
     decode = None
-    if rank == 0 and world == 1 and not args.no_decode:
-        del tensors
+    if not args.no_decode:
+        # batch-1 decode tokens/s: the Qwen3-0.6B-shaped decoder on one GPU,
+        # and the Llama-3-70B-shaped decoder split over all N ranks
+        del tensors, graph
+        graph = None
+        torch.cuda.synchronize()
         torch.cuda.empty_cache()
-        decode, dcfg, dprompt = measure_decode_gpu("decode_qwen3")
-        if not args.no_cpu_baseline:
-            dcpu = measure_decode_cpu(dcfg, dprompt, steps=8)
-            decode["cpu_reference_tokens_per_s"] = dcpu["tokens_per_s"]
-            decode["cpu_reference_cores"] = dcpu["cores"]
-            decode["cpu_reference_kind"] = dcpu["kind"]
-        decode["parity"] = ("greedy tokens identical to the reference's transformer_forward over 64 steps "
-                            "(tests/test_decode_gpu.py)")
+        decode = []
+        if world == 1:
+            d, dcfg, dprompt = measure_decode_gpu("decode_qwen3")
+            if not args.no_cpu_baseline:
+                dcpu = measure_decode_cpu(dcfg, dprompt, steps=8)
+                d["cpu_reference_tokens_per_s"] = dcpu["tokens_per_s"]
+                d["cpu_reference_cores"] = dcpu["cores"]
+                d["cpu_reference_kind"] = dcpu["kind"]
+            d["parity"] = ("greedy tokens identical to the reference's transformer_forward over 64 steps "
+                           "(tests/test_decode_gpu.py)")
+            decode.append(decode_roofline(d, dcfg, 1))
+        if not args.no_large_decode:
+            comm = None
+            if world > 1:
+                cfg0, _, _ = decode_config("decode_llama70b")
+                comm = N.Comm.from_process_group(N.model_comm_floats(cfg0, world))
+                comm.set_timeout(30.0)
+
+            def max_over(v):
+                if world == 1:
+                    return v
+                t = torch.tensor([float(v)], device=dev, dtype=torch.float64)
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                return float(t.item())
+            d, dcfg, _ = measure_decode_gpu("decode_llama70b", comm=comm, barrier=barrier, max_over_ranks=max_over)
+            d["parity"] = ("split decode: greedy tokens identical to one GPU and to the reference on the "
+                           "Qwen3-shaped decoder at 2 GPUs (tests/test_tp_gpu.py)")
+            decode.append(decode_roofline(d, dcfg, world))
+            if comm is not None:
+                barrier()
+                comm.free()
 
     if rank == 0:
         peak, peak_kind = measured_peak()
@@ -617,7 +661,8 @@ def run_neon(args):
             "clocks": clocks,
         }
         print(json.dumps(line), flush=True)
-    del graph
+    if args.no_decode:
+        del graph
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -172,12 +172,16 @@ NEON_API int neon_cuda_matvec_q4_0_noalloc(neon_tensor_t W, const float* dX, siz
 #define NEON_ROLE_FFN_DOWN 11  /* blk.i.ffn_down.weight  [n_ff, n_embd] */
 
 /* Hyperparameters, the fields of engine::Config (rawllm_common.hpp:113-145)
- * the forward pass reads. ctx_len is the KV-cache capacity in positions. */
+ * the forward pass reads. ctx_len is the KV-cache capacity in positions.
+ * plain_ffn = !use_swiglu: 0 (the NANITY default) is SwiGLU,
+ * act = silu(ffn_gate x) * ffn_up x; 1 is the plain SiLU-FFN variant,
+ * act = silu(ffn_up x), with no ffn_gate tensor (rawllm_forward.hpp:1167-1190). */
 typedef struct {
     uint32_t n_vocab, n_embd, n_layer, n_head, n_kv_head, head_dim, n_ff, ctx_len;
     float rope_base, rope_scale;
     uint32_t rope_dim_count; /* 0: rotate all of head_dim */
     float norm_eps;
+    uint32_t plain_ffn;
 } neon_model_config_t;
 
 typedef struct neon_model* neon_model_t;

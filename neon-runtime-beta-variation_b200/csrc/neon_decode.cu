@@ -29,7 +29,7 @@
 
 namespace neon {
 // epilogue kinds of the one-position matvec kernel (see neon_kernels.cuh)
-enum : int { kEpiStore = 0, kEpiRope = 1, kEpiAtPos = 2, kEpiSwiglu = 3 };
+enum : int { kEpiStore = 0, kEpiRope = 1, kEpiAtPos = 2, kEpiSwiglu = 3, kEpiSilu = 5 };
 }  // namespace neon
 
 #include <cuda_fp16.h>
@@ -425,6 +425,14 @@ __global__ void swiglu_pairs_kernel(const float* __restrict__ y, float* __restri
     }
 }
 
+// act[i] = silu(y[i]): the plain SiLU-FFN variant (rawllm_forward.hpp:1189).
+__global__ void silu_kernel(const float* __restrict__ y, float* __restrict__ act, long long n) {
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        const float x = y[i];
+        act[i] = __fdiv_rn(x, __fadd_rn(1.0f, fast_expf_dev(-x)));
+    }
+}
+
 // Orderable 32-bit image of a float: larger float, larger unsigned.
 __device__ __forceinline__ unsigned int float_order(float v) {
     const unsigned int u = __float_as_uint(v);
@@ -511,7 +519,7 @@ struct neon_model {
     struct Layer {
         float *attn_norm = nullptr, *ffn_norm = nullptr;
         neon_tensor_t w[5] = {};  // q, k, v, out, down
-        neon_tensor_t gateup = nullptr;  // gate and up rows interleaved (2*n_ff rows)
+        neon_tensor_t gateup = nullptr;  // gate and up rows interleaved (2*n_ff rows); up alone for a plain FFN
         std::vector<uint8_t> gate_bytes, up_bytes;  // held until both halves are set
         int gate_type = -1, up_type = -1;
     };
@@ -678,11 +686,18 @@ int run_layers(neon_model* m, const int* toks, int seq) {
         }
         if (!rc) rc = residual_proj(m, L.w[3], m->att, q_dim, seq);
         if (!rc) rc = rmsnorm(m, m->h, L.ffn_norm, m->xn, seq);
-        if (!rc) rc = proj(m, {{L.gateup, m->gu, 2 * n_ff}}, m->xn, n_embd, seq, 0);
+        const size_t gu_rows = m->cfg.plain_ffn ? n_ff : 2 * n_ff;
+        if (!rc) rc = proj(m, {{L.gateup, m->gu, gu_rows}}, m->xn, n_embd, seq, 0);
         if (!rc) {
             const long long n = (long long)seq * n_ff;
-            swiglu_pairs_kernel<<<(int)std::min<long long>((n + 255) / 256, 4096), 256, 0, m->stream>>>(m->gu, m->act, n);
-            rc = check_launch("swiglu_pairs_kernel");
+            const int grid = (int)std::min<long long>((n + 255) / 256, 4096);
+            if (m->cfg.plain_ffn) {
+                silu_kernel<<<grid, 256, 0, m->stream>>>(m->gu, m->act, n);
+                rc = check_launch("silu_kernel");
+            } else {
+                swiglu_pairs_kernel<<<grid, 256, 0, m->stream>>>(m->gu, m->act, n);
+                rc = check_launch("swiglu_pairs_kernel");
+            }
         }
         if (!rc) rc = residual_proj(m, L.w[4], m->act, n_ff, seq);
     }
@@ -763,9 +778,9 @@ int run_step(neon_model* m) {
         }
         if (!rc) rc = residual(L.w[3], m->att, q_dim);
         if (!rc) {
-            // act = silu(gate) * up, (gate, up) = W x with x = rms_norm(h)
+            // act = silu(gate) * up, (gate, up) = W x with x = rms_norm(h); or silu(up)
             const neon_proj_target_t t{L.gateup, m->act, n_ff};
-            const int epi = neon::kEpiSwiglu;
+            const int epi = m->cfg.plain_ffn ? neon::kEpiSilu : neon::kEpiSwiglu;
             const long long stride = 0;
             neon_internal::MatvecExt ext;
             ext.norm_w = L.ffn_norm;
@@ -1035,6 +1050,21 @@ int neon_cuda_model_set_tensor(neon_model_t m, int role, int layer, const uint8_
                                            std::to_string(want1) + "].");
     if (role != NEON_ROLE_TOKEN_EMBD && role != NEON_ROLE_OUTPUT && (layer < 0 || (uint32_t)layer >= c.n_layer))
         return error(NEON_ERR_INVALID, "layer index out of range");
+    if (role == NEON_ROLE_FFN_GATE && c.plain_ffn)
+        return error(NEON_ERR_INVALID, "ffn_gate given to a plain SiLU-FFN model (plain_ffn = 1)");
+    if (role == NEON_ROLE_FFN_UP && c.plain_ffn) {
+        // plain SiLU-FFN: the up rows alone (this rank's [ff0, ff0 + n_ff_l))
+        const size_t row_b = ggml_type == NEON_GGML_Q4_0 ? ne0 / 32 * 18 : ggml_type == NEON_GGML_Q8_0 ? ne0 / 32 * 34 : 0;
+        if (row_b == 0) return error(NEON_ERR_UNSUPPORTED, "ffn_up must be Q4_0 or Q8_0");
+        if (nbytes < row_b * ne1) return error(NEON_ERR_INVALID, "tensor bytes shorter than its shape");
+        neon_tensor_t t = nullptr;
+        int rc = neon_cuda_upload(host_bytes + sh[0] * row_b, ggml_type, sh[1] - sh[0], ne0, NEON_SHARD_NONE, 0, 1, &t);
+        if (rc) return rc;
+        auto& L = m->layers[layer];
+        if (L.gateup) neon_cuda_free(L.gateup);
+        L.gateup = t;
+        return NEON_OK;
+    }
     if (role == NEON_ROLE_FFN_GATE || role == NEON_ROLE_FFN_UP) {
         // held until both halves are present, then uploaded as one tensor whose
         // row 2i is gate row i and row 2i+1 up row i (same bytes, same math)

@@ -45,6 +45,7 @@ enum : int {
     kEpiAtPos = 2,   // store at y + pos*pos_stride (the V cache row of the position)
     kEpiSwiglu = 3,  // rows interleave gate/up: y[i] = silu(v_2i) * v_2i+1
     kEpiPeer = 4,    // fused collective: row r into slot [parity][rank] of every rank
+    kEpiSilu = 5,    // y[r] = silu(v): the plain SiLU-FFN variant's activation
 };
 
 struct Span {
@@ -652,6 +653,10 @@ __device__ __forceinline__ void stream_epilogue(const StreamArgs& a, const Span&
         case kEpiSwiglu:
             // silu(gate) * up (rawllm_forward.hpp:1186)
             if (!(t & 1)) sp.y[row / 2] = __fmul_rn(silu_dev(v), rowv[t + 1]);
+            break;
+        case kEpiSilu:
+            // silu(up), the FFN without a gate (rawllm_forward.hpp:1189)
+            sp.y[row] = silu_dev(v);
             break;
         case kEpiPeer: {
             // this rank's partial row sum, as an LL word, into its slot on every rank (NVLink stores)

@@ -132,4 +132,123 @@ void proj_all_positions_multi(const std::vector<ProjTargetT>& targets, const flo
     check(neon_cuda_proj_all_positions_multi(t.data(), t.size(), X, x_stride, seq));
 }
 
+// ---------------------------------------------------------------------------
+// The decode step on the device (neon_cuda_model_*): replaces get_engine_state's
+// ModelWeights + KVCache and the transformer_forward calls of run_generation
+// (NEON-3.cpp:535-564, 676-759).
+// ---------------------------------------------------------------------------
+
+// engine::Config (rawllm_common.hpp:113-145) -> the C config. The KV cache
+// holds cfg.kv_window positions when it is set, as get_engine_state sizes it
+// (NEON-3.cpp:560), else cfg.ctx_len.
+template <class ConfigT>
+neon_model_config_t model_config(const ConfigT& c) {
+    neon_model_config_t m{};
+    m.n_vocab = c.n_vocab;
+    m.n_embd = c.n_embd;
+    m.n_layer = c.n_layer;
+    m.n_head = c.n_head;
+    m.n_kv_head = c.n_kv_head;
+    m.head_dim = c.head_dim;
+    m.n_ff = c.n_ff;
+    m.ctx_len = c.kv_window ? c.kv_window : c.ctx_len;
+    m.rope_base = c.rope_base;
+    m.rope_scale = c.rope_scale;
+    m.rope_dim_count = c.rope_dim_count;
+    m.norm_eps = c.norm_eps;
+    m.plain_ffn = c.use_swiglu ? 0u : 1u;
+    return m;
+}
+
+// GGUF tensor name -> (NEON_ROLE_*, layer), for the names ModelWeights::build
+// looks up (rawllm_forward.hpp:847-866); false for any other tensor.
+inline bool tensor_role(const std::string& name, int* role, int* layer) {
+    static const struct { const char* name; int role; } globals[] = {
+        {"token_embd.weight", NEON_ROLE_TOKEN_EMBD}, {"output_norm.weight", NEON_ROLE_OUTPUT_NORM},
+        {"output.weight", NEON_ROLE_OUTPUT}};
+    static const struct { const char* suffix; int role; } per_layer[] = {
+        {"attn_norm.weight", NEON_ROLE_ATTN_NORM}, {"attn_q.weight", NEON_ROLE_ATTN_Q},
+        {"attn_k.weight", NEON_ROLE_ATTN_K},       {"attn_v.weight", NEON_ROLE_ATTN_V},
+        {"attn_output.weight", NEON_ROLE_ATTN_OUT}, {"ffn_norm.weight", NEON_ROLE_FFN_NORM},
+        {"ffn_gate.weight", NEON_ROLE_FFN_GATE},   {"ffn_up.weight", NEON_ROLE_FFN_UP},
+        {"ffn_down.weight", NEON_ROLE_FFN_DOWN}};
+    for (const auto& g : globals)
+        if (name == g.name) {
+            *role = g.role;
+            *layer = -1;
+            return true;
+        }
+    if (name.compare(0, 4, "blk.") != 0) return false;
+    const size_t dot = name.find('.', 4);
+    if (dot == std::string::npos || dot == 4) return false;
+    int li = 0;
+    for (size_t i = 4; i < dot; ++i) {
+        if (name[i] < '0' || name[i] > '9') return false;
+        li = li * 10 + (name[i] - '0');
+    }
+    const std::string rest = name.substr(dot + 1);
+    for (const auto& p : per_layer)
+        if (rest == p.suffix) {
+            *role = p.role;
+            *layer = li;
+            return true;
+        }
+    return false;
+}
+
+// A decoder on the current device, or this rank's share of one split over the
+// ranks of `comm` (every rank passes the whole loader; each keeps its shard).
+class Decoder {
+public:
+    template <class ConfigT, class LoaderT>
+    Decoder(const ConfigT& cfg, const LoaderT& loader, neon_comm_t comm = nullptr) {
+        const neon_model_config_t c = model_config(cfg);
+        check(neon_cuda_model_create_tp(&c, comm, &m_));
+        try {
+            for (const auto& t : loader.tensors) {
+                int role = 0, layer = -1;
+                if (!tensor_role(t.name, &role, &layer)) continue;
+                if (role == NEON_ROLE_FFN_GATE && c.plain_ffn) continue;
+                const size_t ne0 = (size_t)t.shape[0], ne1 = t.shape.size() > 1 ? (size_t)t.shape[1] : 0;
+                check(neon_cuda_model_set_tensor(m_, role, layer, t.data_ptr, t.nbytes, static_cast<int>(t.type), ne0,
+                                                 ne1));
+            }
+        } catch (...) {
+            neon_cuda_model_free(m_);
+            throw;
+        }
+    }
+    ~Decoder() { neon_cuda_model_free(m_); }
+    Decoder(const Decoder&) = delete;
+    Decoder& operator=(const Decoder&) = delete;
+
+    // fwd::transformer_forward: append `tokens` at positions length.., return
+    // the logits of the last one.
+    std::vector<float> forward(const std::vector<int32_t>& tokens, size_t n_vocab) {
+        std::vector<float> logits(n_vocab);
+        check(neon_cuda_model_forward(m_, tokens.data(), tokens.size(), logits.data()));
+        return logits;
+    }
+    // run_generation's greedy loop: the prompt, then up to max_new tokens,
+    // stopping before eos_id.
+    std::vector<int32_t> generate(const std::vector<int32_t>& prompt, size_t max_new, int32_t eos_id) {
+        std::vector<int32_t> out(max_new ? max_new : 1);
+        size_t n = 0;
+        check(neon_cuda_model_generate(m_, prompt.data(), prompt.size(), max_new, eos_id, out.data(), &n));
+        out.resize(n);
+        return out;
+    }
+    size_t length() const {
+        size_t n = 0;
+        check(neon_cuda_model_length(m_, &n));
+        return n;
+    }
+    // KVCache::length rewind (run_generation's prefix reuse, NEON-3.cpp:690-703)
+    void set_length(size_t n) { check(neon_cuda_model_set_length(m_, n)); }
+    neon_model_t handle() const { return m_; }
+
+private:
+    neon_model_t m_ = nullptr;
+};
+
 }  // namespace neon_cuda

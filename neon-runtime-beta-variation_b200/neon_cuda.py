@@ -96,7 +96,7 @@ class _ModelConfig(C.Structure):
     _fields_ = [(f, C.c_uint32) for f in ("n_vocab", "n_embd", "n_layer", "n_head", "n_kv_head", "head_dim",
                                           "n_ff", "ctx_len")] + [
         ("rope_base", C.c_float), ("rope_scale", C.c_float), ("rope_dim_count", C.c_uint32),
-        ("norm_eps", C.c_float)]
+        ("norm_eps", C.c_float), ("plain_ffn", C.c_uint32)]
 
 
 class NeonError(RuntimeError):
@@ -355,7 +355,8 @@ def proj_all_positions_multi(targets, X: np.ndarray, x_stride: int, seq: int, po
 def _config(cfg) -> _ModelConfig:
     return _ModelConfig(*[getattr(cfg, f) for f in ("n_vocab", "n_embd", "n_layer", "n_head", "n_kv_head",
                                                     "head_dim", "n_ff", "ctx_len")],
-                        cfg.rope_base, cfg.rope_scale, cfg.rope_dim_count, cfg.norm_eps)
+                        cfg.rope_base, cfg.rope_scale, cfg.rope_dim_count, cfg.norm_eps,
+                        1 if getattr(cfg, "plain_ffn", False) else 0)
 
 
 def tp_shard(cfg, role: int, rank: int, world: int):

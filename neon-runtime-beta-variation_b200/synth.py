@@ -121,14 +121,16 @@ class ModelConfig:
     """Hyperparameters of a NANITY decoder (engine::Config, rawllm_common.hpp:113-145)."""
 
     FIELDS = ("n_vocab", "n_embd", "n_layer", "n_head", "n_kv_head", "head_dim", "n_ff", "ctx_len",
-              "rope_base", "rope_scale", "rope_dim_count", "norm_eps")
+              "rope_base", "rope_scale", "rope_dim_count", "norm_eps", "plain_ffn")
 
     def __init__(self, n_vocab, n_embd, n_layer, n_head, n_kv_head, head_dim, n_ff, ctx_len=4096,
-                 rope_base=10000.0, rope_scale=1.0, rope_dim_count=0, norm_eps=1e-5, name=""):
+                 rope_base=10000.0, rope_scale=1.0, rope_dim_count=0, norm_eps=1e-5, name="", plain_ffn=False):
         self.n_vocab, self.n_embd, self.n_layer = n_vocab, n_embd, n_layer
         self.n_head, self.n_kv_head, self.head_dim, self.n_ff = n_head, n_kv_head, head_dim, n_ff
         self.ctx_len, self.rope_base, self.rope_scale = ctx_len, rope_base, rope_scale
         self.rope_dim_count, self.norm_eps, self.name = rope_dim_count, norm_eps, name
+        # engine::Config::use_swiglu == false: act = silu(ffn_up x), no ffn_gate
+        self.plain_ffn = plain_ffn
 
     @property
     def q_dim(self):
@@ -174,6 +176,8 @@ def model_tensors(cfg: ModelConfig, seed: int, wtype: int = GGML_Q4_0, embd_type
               ROLE_ATTN_V: (cfg.kv_dim, cfg.n_embd), ROLE_ATTN_OUT: (cfg.n_embd, cfg.q_dim),
               ROLE_FFN_GATE: (cfg.n_ff, cfg.n_embd), ROLE_FFN_UP: (cfg.n_ff, cfg.n_embd),
               ROLE_FFN_DOWN: (cfg.n_embd, cfg.n_ff)}
+    if cfg.plain_ffn:
+        del shapes[ROLE_FFN_GATE]
     for li in range(cfg.n_layer):
         yield ROLE_ATTN_NORM, li, ones, GGML_F32, cfg.n_embd, 0
         yield ROLE_FFN_NORM, li, ones, GGML_F32, cfg.n_embd, 0

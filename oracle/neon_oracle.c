@@ -285,6 +285,7 @@ typedef struct {
     float rope_base, rope_scale;
     uint32_t rope_dim_count;
     float norm_eps;
+    uint32_t plain_ffn; /* 1: act = silu(up), no gate (engine::Config::use_swiglu == false) */
 } oracle_config_t;
 
 typedef struct {
@@ -435,9 +436,14 @@ int oracle_model_forward(void* p, const int32_t* tokens, size_t seq, float* out_
         for (size_t i = 0; i < seq * n_embd; ++i) h[i] += pout[i];
         const float* wf = (const float*)L_(m, li, R_FFN_NORM)->data;
         for (size_t t = 0; t < seq; ++t) oracle_rms_norm(h + t * n_embd, wf, normed + t * n_embd, n_embd, c->norm_eps);
-        proj(L_(m, li, R_FFN_GATE), normed, n_embd, g, n_ff, seq);
+        /* SwiGLU or the plain SiLU-FFN variant (rawllm_forward.hpp:1167-1190) */
         proj(L_(m, li, R_FFN_UP), normed, n_embd, u, n_ff, seq);
-        for (size_t i = 0; i < seq * n_ff; ++i) g[i] = oracle_silu(g[i]) * u[i];
+        if (c->plain_ffn) {
+            for (size_t i = 0; i < seq * n_ff; ++i) g[i] = oracle_silu(u[i]);
+        } else {
+            proj(L_(m, li, R_FFN_GATE), normed, n_embd, g, n_ff, seq);
+            for (size_t i = 0; i < seq * n_ff; ++i) g[i] = oracle_silu(g[i]) * u[i];
+        }
         proj(L_(m, li, R_FFN_DOWN), g, n_ff, pout, n_embd, seq);
         for (size_t i = 0; i < seq * n_embd; ++i) h[i] += pout[i];
     }

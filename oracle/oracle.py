@@ -204,13 +204,14 @@ class _Config(C.Structure):
     _fields_ = [(f, C.c_uint32) for f in ("n_vocab", "n_embd", "n_layer", "n_head", "n_kv_head", "head_dim",
                                           "n_ff", "ctx_len")] + [
         ("rope_base", C.c_float), ("rope_scale", C.c_float), ("rope_dim_count", C.c_uint32),
-        ("norm_eps", C.c_float)]
+        ("norm_eps", C.c_float), ("plain_ffn", C.c_uint32)]
 
 
 def _config(cfg):
     return _Config(*[getattr(cfg, f) for f in ("n_vocab", "n_embd", "n_layer", "n_head", "n_kv_head",
                                                "head_dim", "n_ff", "ctx_len")],
-                   cfg.rope_base, cfg.rope_scale, cfg.rope_dim_count, cfg.norm_eps)
+                   cfg.rope_base, cfg.rope_scale, cfg.rope_dim_count, cfg.norm_eps,
+                   1 if getattr(cfg, "plain_ffn", False) else 0)
 
 
 class Model:

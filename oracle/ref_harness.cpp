@@ -162,6 +162,7 @@ typedef struct {
     float rope_base, rope_scale;
     uint32_t rope_dim_count;
     float norm_eps;
+    uint32_t plain_ffn;
 } ref_config_t;
 
 void* ref_model_new(const ref_config_t* c) {
@@ -179,7 +180,7 @@ void* ref_model_new(const ref_config_t* c) {
     m->cfg.rope_scale = c->rope_scale;
     m->cfg.rope_dim_count = c->rope_dim_count;
     m->cfg.norm_eps = c->norm_eps;
-    m->cfg.use_swiglu = true;
+    m->cfg.use_swiglu = c->plain_ffn == 0;
     m->mw.layers.resize(c->n_layer);
     m->cache = fwd::KVCache(c->n_layer, (size_t)c->n_kv_head * c->head_dim, c->ctx_len);
     return m;

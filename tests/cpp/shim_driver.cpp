@@ -6,6 +6,12 @@
 //   shim_driver single <type> <rows> <cols> <seq> W.bin X.bin Y.out
 //   shim_driver multi  <cols> <seq> X.bin Y.out <type> <rows> W.bin [<type> <rows> W.bin ...]
 //   shim_driver badshape       (expects the reference's error message)
+//   shim_driver roles <name>...  (GGUF tensor name -> "role layer", or "none")
+//   shim_driver decode <dir> <n_new>
+//       builds neon_cuda::Decoder from <dir>/config.txt (engine::Config fields),
+//       <dir>/manifest.txt ("name type ne0 ne1 file" per tensor) and
+//       <dir>/prompt.bin (int32); writes tokens.bin (greedy generation) and
+//       logits.bin (forward of the prompt after a rewind to 0)
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -37,6 +43,21 @@ struct ProjTarget {  // fwd::ProjTarget (rawllm_forward.hpp:626-630)
 };
 }  // namespace fwd
 
+namespace engine {
+struct Config {  // the fields of engine::Config the decoder reads (rawllm_common.hpp:113-145)
+    uint32_t n_vocab = 0, n_embd = 0, n_layer = 0, n_head = 0, n_kv_head = 0, head_dim = 0, n_ff = 0;
+    uint32_t ctx_len = 4096, kv_window = 0;
+    float rope_base = 10000.f, rope_scale = 1.f;
+    uint32_t rope_dim_count = 0;
+    float norm_eps = 1e-5f;
+    bool use_swiglu = true;
+};
+}  // namespace engine
+
+struct Loader {  // a loader's public tensor list (GGUFLoader::tensors)
+    std::vector<loader::TensorInfo> tensors;
+};
+
 struct DummyPool {
     int size() const { return 1; }
 };
@@ -67,6 +88,57 @@ int main(int argc, char** argv) {
                 return 0;
             }
             return 1;
+        }
+        if (mode == "roles") {
+            for (int i = 2; i < argc; ++i) {
+                int role = 0, layer = 0;
+                if (neon_cuda::tensor_role(argv[i], &role, &layer)) std::cout << role << " " << layer << "\n";
+                else std::cout << "none\n";
+            }
+            return 0;
+        }
+        if (mode == "decode" && argc == 4) {
+            const std::string dir = argv[2];
+            const size_t n_new = std::strtoull(argv[3], nullptr, 10);
+            engine::Config cfg;
+            {
+                std::ifstream f(dir + "/config.txt");
+                int swiglu = 1;
+                f >> cfg.n_vocab >> cfg.n_embd >> cfg.n_layer >> cfg.n_head >> cfg.n_kv_head >> cfg.head_dim >> cfg.n_ff >>
+                    cfg.ctx_len >> cfg.kv_window >> cfg.rope_base >> cfg.rope_scale >> cfg.rope_dim_count >> cfg.norm_eps >>
+                    swiglu;
+                cfg.use_swiglu = swiglu != 0;
+            }
+            Loader g;
+            std::vector<std::vector<uint8_t>> blobs;
+            {
+                std::ifstream f(dir + "/manifest.txt");
+                std::string name, file;
+                int type;
+                uint64_t ne0, ne1;
+                while (f >> name >> type >> ne0 >> ne1 >> file) {
+                    blobs.push_back(read_file((dir + "/" + file).c_str()));
+                    loader::TensorInfo t{name, ne1 ? std::vector<uint64_t>{ne0, ne1} : std::vector<uint64_t>{ne0},
+                                         static_cast<loader::GGMLType>(type), 0, blobs.back().size(), nullptr};
+                    g.tensors.push_back(t);
+                }
+                for (size_t i = 0; i < g.tensors.size(); ++i) g.tensors[i].data_ptr = blobs[i].data();
+            }
+            auto pb = read_file((dir + "/prompt.bin").c_str());
+            std::vector<int32_t> prompt(pb.size() / 4);
+            std::memcpy(prompt.data(), pb.data(), pb.size());
+            neon_cuda::check(neon_cuda_init(0));
+            neon_cuda::Decoder d(cfg, g);
+            auto toks = d.generate(prompt, n_new, -1);
+            {
+                std::ofstream f(dir + "/tokens.bin", std::ios::binary);
+                f.write(reinterpret_cast<const char*>(toks.data()), toks.size() * 4);
+            }
+            if (d.length() != prompt.size() + toks.size()) return 5;
+            d.set_length(0);
+            auto logits = d.forward(prompt, cfg.n_vocab);
+            write_file((dir + "/logits.bin").c_str(), logits.data(), logits.size());
+            return 0;
         }
         if (mode == "single" && argc == 9) {
             int type = std::atoi(argv[2]);

@@ -89,6 +89,7 @@ def test_pieces_match_reference():
     (TINY.with_(n_kv_head=4), 5, 6),                                             # MHA (group 1)
     (TINY.with_(n_vocab=777, n_embd=384, n_ff=1024, n_head=6, n_kv_head=2), 9, 5),  # group 3, odd vocab
     (S.QWEN3_0_6B.with_(n_layer=2, n_vocab=4096, ctx_len=96), 24, 8),            # Qwen-shaped layers
+    (TINY.with_(plain_ffn=True), 6, 6),                                          # SiLU-FFN, no gate
 ])
 def test_model_forward_matches_reference(cfg, prompt, steps):
     tensors = list(S.model_tensors(cfg, seed=11))

@@ -29,6 +29,27 @@ def test_shim_compiles_and_links(driver):
     assert os.access(driver, os.X_OK)
 
 
+NAMES = {S.ROLE_TOKEN_EMBD: "token_embd.weight", S.ROLE_OUTPUT_NORM: "output_norm.weight",
+         S.ROLE_OUTPUT: "output.weight", S.ROLE_ATTN_NORM: "attn_norm.weight", S.ROLE_ATTN_Q: "attn_q.weight",
+         S.ROLE_ATTN_K: "attn_k.weight", S.ROLE_ATTN_V: "attn_v.weight", S.ROLE_ATTN_OUT: "attn_output.weight",
+         S.ROLE_FFN_NORM: "ffn_norm.weight", S.ROLE_FFN_GATE: "ffn_gate.weight", S.ROLE_FFN_UP: "ffn_up.weight",
+         S.ROLE_FFN_DOWN: "ffn_down.weight"}
+
+
+def gguf_name(role, layer):
+    """The tensor names ModelWeights::build looks up (rawllm_forward.hpp:847-866)."""
+    return NAMES[role] if layer < 0 else f"blk.{layer}.{NAMES[role]}"
+
+
+def test_shim_tensor_names_map_to_roles(driver):
+    names = [gguf_name(r, -1 if r < S.ROLE_ATTN_NORM else 17) for r in NAMES]
+    names += ["blk.x.attn_q.weight", "blk.3.attn_q.bias", "rope_freqs.weight", "blk..ffn_up.weight"]
+    out = subprocess.run([driver, "roles", *names], capture_output=True, text=True, check=True).stdout.split("\n")
+    for i, r in enumerate(NAMES):
+        assert out[i] == f"{r} {-1 if r < S.ROLE_ATTN_NORM else 17}"
+    assert out[len(NAMES):len(NAMES) + 4] == ["none"] * 4
+
+
 def test_shim_reference_error_before_device_use(driver):
     out = subprocess.run([driver, "badshape"], capture_output=True, text=True)
     assert out.returncode == 0, out.stderr
@@ -69,3 +90,34 @@ def test_shim_multi_matches_oracle(driver, tmp_path):
         ref = O.proj_all_positions(typ, W, rows, cols, X)
         assert max_rel_err(Y[off:off + rows * seq], ref) <= MATVEC_RTOL
         off += rows * seq
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("plain", [False, True])
+def test_shim_decoder_from_loader_matches_reference(driver, tmp_path, plain):
+    """neon_cuda::Decoder built from a loader's GGUF-named tensors and an
+    engine::Config gives the reference's greedy tokens."""
+    from conftest import MODEL_L2_RTOL, rel_l2
+
+    cfg = S.ModelConfig(1000, 256, 2, 4, 2, 64, 512, ctx_len=64, rope_base=1e4, plain_ffn=plain)
+    tensors = list(S.model_tensors(cfg, seed=7))
+    lines = []
+    for i, (role, layer, raw, typ, ne0, ne1) in enumerate(tensors):
+        np.ascontiguousarray(raw).tofile(tmp_path / f"t{i}.bin")
+        lines.append(f"{gguf_name(role, layer)} {typ} {ne0} {ne1} t{i}.bin")
+    (tmp_path / "manifest.txt").write_text("\n".join(lines) + "\n")
+    (tmp_path / "config.txt").write_text(
+        f"{cfg.n_vocab} {cfg.n_embd} {cfg.n_layer} {cfg.n_head} {cfg.n_kv_head} {cfg.head_dim} {cfg.n_ff} "
+        f"{cfg.ctx_len} 0 {cfg.rope_base} {cfg.rope_scale} {cfg.rope_dim_count} {cfg.norm_eps} {0 if plain else 1}\n")
+    prompt = S.prompt_tokens(8, cfg.n_vocab, 8)
+    prompt.astype(np.int32).tofile(tmp_path / "prompt.bin")
+    out = subprocess.run([driver, "decode", str(tmp_path), "16"], capture_output=True, text=True)
+    assert out.returncode == 0, out.stderr
+    toks = np.fromfile(tmp_path / "tokens.bin", np.int32)
+    logits = np.fromfile(tmp_path / "logits.bin", np.float32)
+    kind = "reference" if O.ref_available() else "port"
+    ref = O.Model(cfg, tensors, kind)
+    ref_toks, ref_logits = ref.generate_greedy(prompt, 16)
+    ref.close()
+    assert np.array_equal(toks, ref_toks)
+    assert rel_l2(logits, ref_logits[0]) <= MODEL_L2_RTOL
