@@ -283,6 +283,7 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const float* __rest
 // splits in split order: out = (sum_splits p v) / (sum_splits p).
 // ---------------------------------------------------------------------------
 constexpr int kAttnMaxGroup = 8;
+constexpr int kAttnRows = 4;  // cache rows a warp loads at once in attn_scores_kernel
 
 __global__ void __launch_bounds__(kThreads) attn_scores_kernel(const float* __restrict__ q, const float* __restrict__ Kc,
                                                                const int* __restrict__ d_pos, int kv_dim, int hd, int group,
@@ -303,22 +304,31 @@ __global__ void __launch_bounds__(kThreads) attn_scores_kernel(const float* __re
     float mx[kAttnMaxGroup];
 #pragma unroll
     for (int gq = 0; gq < kAttnMaxGroup; ++gq) mx[gq] = -INFINITY;
-    for (int s = s0 + warp; s < s1; s += nw) {
-        const float* kr = Kc + (long long)s * kv_dim + (long long)kvh * hd;
-        float kv[8];
+    // a warp takes kAttnRows positions at a time, all their K loads in flight together
+    for (int sb = s0 + warp * kAttnRows; sb < s1; sb += nw * kAttnRows) {
+        float kv[kAttnRows][8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) kv[j] = j < per ? __ldg(kr + lane + 32 * j) : 0.f;
+        for (int u = 0; u < kAttnRows; ++u) {
+            const float* kr = Kc + (long long)min(sb + u, s1 - 1) * kv_dim + (long long)kvh * hd;
 #pragma unroll
-        for (int gq = 0; gq < kAttnMaxGroup; ++gq) {
-            if (gq >= group) break;
-            float acc = 0.f;
+            for (int j = 0; j < 8; ++j) kv[u][j] = j < per ? __ldg(kr + lane + 32 * j) : 0.f;
+        }
 #pragma unroll
-            for (int j = 0; j < 8; ++j)
-                if (j < per) acc = __fmaf_rn(qs[gq * hd + lane + 32 * j], kv[j], acc);
-            acc = warp_sum_f(acc);
-            const float sc = __fmul_rn(acc, scale);
-            if (lane == 0) scores[((long long)kvh * group + gq) * ctx + s] = sc;
-            mx[gq] = fmaxf(mx[gq], sc);
+        for (int u = 0; u < kAttnRows; ++u) {
+            const int s = sb + u;
+            if (s >= s1) break;
+#pragma unroll
+            for (int gq = 0; gq < kAttnMaxGroup; ++gq) {
+                if (gq >= group) break;
+                float acc = 0.f;
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    if (j < per) acc = __fmaf_rn(qs[gq * hd + lane + 32 * j], kv[u][j], acc);
+                acc = warp_sum_f(acc);
+                const float sc = __fmul_rn(acc, scale);
+                if (lane == 0) scores[((long long)kvh * group + gq) * ctx + s] = sc;
+                mx[gq] = fmaxf(mx[gq], sc);
+            }
         }
     }
 #pragma unroll
@@ -348,11 +358,13 @@ __global__ void __launch_bounds__(kThreads) attn_values_kernel(const float* __re
     const int chunk = (L + nsplit - 1) / nsplit;
     const int s0 = min(L, split * chunk), s1 = min(L, s0 + chunk);
     const int len = s1 - s0;
-    if ((int)threadIdx.x < group) {
-        const float* pm = pmax + ((long long)kvh * group + threadIdx.x) * nsplit;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (warp < group) {  // the max over all splits of head `warp`: lanes over the splits
+        const float* pm = pmax + ((long long)kvh * group + warp) * nsplit;
         float m = -INFINITY;
-        for (int k = 0; k < nsplit; ++k) m = fmaxf(m, pm[k]);
-        gmax[threadIdx.x] = m;
+        for (int k = lane; k < nsplit; k += 32) m = fmaxf(m, __ldg(pm + k));
+        m = warp_max_f(m);
+        if (lane == 0) gmax[warp] = m;
     }
     __syncthreads();
     // p_s = fast_expf(score_s - max over all positions), once per (head, s)
@@ -362,7 +374,6 @@ __global__ void __launch_bounds__(kThreads) attn_values_kernel(const float* __re
             fast_expf_dev(__fsub_rn(__ldg(scores + ((long long)kvh * group + gq) * ctx + s0 + j), gmax[gq]));
     }
     __syncthreads();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (warp < group) {  // the split's sum of p for head `warp`
         float sp = 0.f;
         for (int j = lane; j < len; j += 32) sp += psm[warp * chunk + j];
@@ -377,7 +388,7 @@ __global__ void __launch_bounds__(kThreads) attn_values_kernel(const float* __re
     for (int gq = 0; gq < kAttnMaxGroup; ++gq) acc[gq] = 0.f;
     if (pidx < parts) {
         const float* vb = Vc + (long long)kvh * hd + d;
-#pragma unroll 4
+#pragma unroll 8
         for (int j = pidx; j < len; j += parts) {
             const float v = __ldg(vb + (long long)(s0 + j) * kv_dim);
 #pragma unroll
@@ -403,15 +414,33 @@ __global__ void __launch_bounds__(kThreads) attn_values_kernel(const float* __re
     __syncthreads();
     if (!last) return;
     __threadfence();
-    for (int idx = threadIdx.x; idx < group * hd; idx += blockDim.x) {
-        const int gq = idx / hd, dd = idx - gq * hd;
-        const long long hb = ((long long)kvh * group + gq) * nsplit;
-        float tot = 0.f, r = 0.f;
+    // 1/sum p per head: warp gq, lanes over the splits (a fixed tree)
+    if (warp < group) {
+        const long long hb = ((long long)kvh * group + warp) * nsplit;
+        float tot = 0.f;
+        for (int k = lane; k < nsplit; k += 32) tot += __ldcg(psum + hb + k);
+        tot = warp_sum_f(tot);
+        if (lane == 0) gmax[warp] = __fdiv_rn(1.0f, tot);
+    }
+    __syncthreads();
+    // out = (sum over splits of p.v) / sum p: warp gq, lane l takes dims l, l+32, ..
+    // (head_dim <= 256: at most 8), all of a split's loads in flight together
+    if (warp < group) {
+        const float* po = pout + ((long long)kvh * group + warp) * nsplit * hd;
+        float r[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) r[u] = 0.f;
+#pragma unroll 8
         for (int k = 0; k < nsplit; ++k) {
-            tot += __ldcg(psum + hb + k);
-            r += __ldcg(pout + (hb + k) * hd + dd);
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                if (lane + 32 * u < hd) r[u] += __ldcg(po + (long long)k * hd + lane + 32 * u);
         }
-        out[((long long)kvh * group + gq) * hd + dd] = __fmul_rn(r, __fdiv_rn(1.0f, tot));
+        const float inv = gmax[warp];
+        float* o = out + ((long long)kvh * group + warp) * hd;
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+            if (lane + 32 * u < hd) o[lane + 32 * u] = __fmul_rn(r[u], inv);
     }
     if (threadIdx.x == 0) counters[kvh] = 0u;
 }
@@ -958,7 +987,7 @@ int neon_cuda_model_create_tp(const neon_model_config_t* cfg, neon_comm_t comm, 
     {
         int sms = neon_internal::device_sms(m->device);
         if (sms <= 0) sms = 148;
-        m->att_split = (int)std::max<long long>(1, std::min<long long>((c.ctx_len + 31) / 32, (2LL * sms) / (long long)m->n_kv_l));
+        m->att_split = (int)std::max<long long>(1, std::min<long long>((c.ctx_len + 15) / 16, (3LL * sms) / (long long)m->n_kv_l));
         // the p of a split must fit attn_values_kernel's shared memory
         while (attn_values_smem(m) > 160 * 1024) ++m->att_split;
     }
