@@ -32,6 +32,7 @@ namespace neon {
 enum : int { kEpiStore = 0, kEpiRope = 1, kEpiAtPos = 2, kEpiSwiglu = 3, kEpiSilu = 5 };
 }  // namespace neon
 
+#include <cooperative_groups.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -271,178 +272,160 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const float* __rest
     }
 }
 
-// ---------------------------------------------------------------------------
-// Decode attention (one position, L = *d_pos + 1 cache rows), split over
-// positions: CTA (kvh, split) takes cache rows [split*chunk, ...) for the
-// `group` query heads of KV head kvh, so each K/V row is read once for the
-// whole group. The softmax keeps the reference's form p_s = fast_expf(score_s
-// - max over ALL positions) (transformer_forward :1123-1137), so the scores go
-// through global scratch: attn_scores_kernel writes them and a per-split
-// maximum; attn_values_kernel takes the global maximum, forms p_s, the split's
-// sum of p_s and of p_s * v_s, and the last CTA of each KV head combines the
-// splits in split order: out = (sum_splits p v) / (sum_splits p).
-// ---------------------------------------------------------------------------
-constexpr int kAttnMaxGroup = 8;
-constexpr int kAttnRows = 4;  // cache rows a warp loads at once in attn_scores_kernel
+constexpr int kAttnMaxGroup = 8;  // query heads per KV head in the decode attention
 
-__global__ void __launch_bounds__(kThreads) attn_scores_kernel(const float* __restrict__ q, const float* __restrict__ Kc,
-                                                               const int* __restrict__ d_pos, int kv_dim, int hd, int group,
-                                                               float scale, int nsplit, int ctx, float* __restrict__ scores,
-                                                               float* __restrict__ pmax) {
-    __shared__ float qs[kAttnMaxGroup * 256];
-    __shared__ float wmax[kAttnMaxGroup][kThreads / 32];
-    pdl_wait_d();
-    pdl_trigger_d();
-    const int kvh = blockIdx.x, split = blockIdx.y;
-    const int L = *d_pos + 1;
-    const int chunk = (L + nsplit - 1) / nsplit;
-    const int s0 = split * chunk, s1 = min(L, s0 + chunk);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-    const int per = hd / 32;
-    for (int i = threadIdx.x; i < group * hd; i += blockDim.x) qs[i] = q[(long long)kvh * group * hd + i];
-    __syncthreads();
-    float mx[kAttnMaxGroup];
-#pragma unroll
-    for (int gq = 0; gq < kAttnMaxGroup; ++gq) mx[gq] = -INFINITY;
-    // a warp takes kAttnRows positions at a time, all their K loads in flight together
-    for (int sb = s0 + warp * kAttnRows; sb < s1; sb += nw * kAttnRows) {
-        float kv[kAttnRows][8];
-#pragma unroll
-        for (int u = 0; u < kAttnRows; ++u) {
-            const float* kr = Kc + (long long)min(sb + u, s1 - 1) * kv_dim + (long long)kvh * hd;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) kv[u][j] = j < per ? __ldg(kr + lane + 32 * j) : 0.f;
-        }
-#pragma unroll
-        for (int u = 0; u < kAttnRows; ++u) {
-            const int s = sb + u;
-            if (s >= s1) break;
-#pragma unroll
-            for (int gq = 0; gq < kAttnMaxGroup; ++gq) {
-                if (gq >= group) break;
-                float acc = 0.f;
-#pragma unroll
-                for (int j = 0; j < 8; ++j)
-                    if (j < per) acc = __fmaf_rn(qs[gq * hd + lane + 32 * j], kv[u][j], acc);
-                acc = warp_sum_f(acc);
-                const float sc = __fmul_rn(acc, scale);
-                if (lane == 0) scores[((long long)kvh * group + gq) * ctx + s] = sc;
-                mx[gq] = fmaxf(mx[gq], sc);
-            }
-        }
-    }
-#pragma unroll
-    for (int gq = 0; gq < kAttnMaxGroup; ++gq)
-        if (gq < group && lane == 0) wmax[gq][warp] = mx[gq];
-    __syncthreads();
-    if ((int)threadIdx.x < group) {
-        float m = -INFINITY;
-        for (int w = 0; w < nw; ++w) m = fmaxf(m, wmax[threadIdx.x][w]);
-        pmax[((long long)kvh * group + threadIdx.x) * nsplit + split] = m;
-    }
+// ---------------------------------------------------------------------------
+// Decode attention in one launch: a thread-block cluster of cs CTAs (8, or 16
+// for long contexts) per KV head. CTA r of the cluster takes positions [r*chunk, (r+1)*chunk) of
+// the L = *d_pos + 1 cache rows and scores them for the head's query group
+// into shared memory; the CTAs exchange their maxima through distributed
+// shared memory, so every CTA forms p_s = fast_expf(score_s - max over ALL
+// positions) exactly as transformer_forward does (:1123-1137); each CTA sums
+// p and p * v over its positions, and CTA 0 of the cluster adds the partials
+// in rank order: out = (sum p v) / (sum p). Cluster barriers replace the
+// global round trips of a split kernel pair.
+// ---------------------------------------------------------------------------
+constexpr int kAttnMaxCluster = 16;
+
+struct AttnSmem {  // offsets (floats) into the dynamic shared memory
+    int q, sc, red, co, csum, cmax, total;
+};
+__host__ __device__ inline AttnSmem attn_smem_layout(int group, int hd, int chunk_max, int cs) {
+    auto up4 = [](int v) { return (v + 3) & ~3; };  // float4-aligned regions
+    AttnSmem l;
+    l.q = 0;
+    l.sc = up4(l.q + group * hd);
+    l.red = up4(l.sc + group * chunk_max);
+    l.co = up4(l.red + (kThreads / (hd / 4)) * group * hd);
+    l.csum = up4(l.co + cs * group * hd);
+    l.cmax = up4(l.csum + cs * kAttnMaxGroup);
+    l.total = up4(l.cmax + cs * kAttnMaxGroup);
+    return l;
 }
 
-__global__ void __launch_bounds__(kThreads) attn_values_kernel(const float* __restrict__ Vc, const int* __restrict__ d_pos,
-                                                               int kv_dim, int hd, int group, int nsplit, int ctx,
-                                                               const float* __restrict__ scores, const float* __restrict__ pmax,
-                                                               float* __restrict__ psum, float* __restrict__ pout,
-                                                               unsigned int* __restrict__ counters, float* __restrict__ out) {
-    extern __shared__ float psm[];  // [group][chunk] softmax numerators of this split
-    __shared__ float gmax[kAttnMaxGroup];
-    __shared__ float red[kAttnMaxGroup * kThreads];
-    __shared__ bool last;
+__global__ void __launch_bounds__(kThreads) attn_decode_kernel(const float* __restrict__ q, const float* __restrict__ Kc,
+                                                               const float* __restrict__ Vc, const int* __restrict__ d_pos,
+                                                               int kv_dim, int hd, int group, float scale, int chunk_max,
+                                                               float* __restrict__ out) {
+    namespace cg = cooperative_groups;
+    extern __shared__ __align__(16) float sm[];
+    cg::cluster_group cl = cg::this_cluster();
+    const int rank = (int)cl.block_rank(), cs = (int)cl.num_blocks();
+    const int kvh = blockIdx.x / cs;
+    const AttnSmem lay = attn_smem_layout(group, hd, chunk_max, cs);
+    float* qs = sm + lay.q;
+    float* sc = sm + lay.sc;     // [group][chunk_max]
+    float* red = sm + lay.red;   // [parts][group][hd]
+    float* co = sm + lay.co;     // [cluster][group][hd]   (read in CTA 0)
+    float* csum = sm + lay.csum; // [cluster][kAttnMaxGroup] (read in CTA 0)
+    float* cmax = sm + lay.cmax; // [cluster][kAttnMaxGroup]
+    __shared__ float gm[kAttnMaxGroup];
     pdl_wait_d();
     pdl_trigger_d();
-    const int kvh = blockIdx.x, split = blockIdx.y;
     const int L = *d_pos + 1;
-    const int chunk = (L + nsplit - 1) / nsplit;
-    const int s0 = min(L, split * chunk), s1 = min(L, s0 + chunk);
-    const int len = s1 - s0;
+    const int chunk = (L + cs - 1) / cs;
+    const int s0 = min(L, rank * chunk), len = min(L, s0 + chunk) - s0;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (warp < group) {  // the max over all splits of head `warp`: lanes over the splits
-        const float* pm = pmax + ((long long)kvh * group + warp) * nsplit;
-        float m = -INFINITY;
-        for (int k = lane; k < nsplit; k += 32) m = fmaxf(m, __ldg(pm + k));
-        m = warp_max_f(m);
-        if (lane == 0) gmax[warp] = m;
+    const int nd4 = hd / 4;
+    for (int i = threadIdx.x; i < group * hd; i += blockDim.x) qs[i] = q[(long long)kvh * group * hd + i];
+    __syncthreads();
+    // scores: a thread per position, its whole K row in flight
+    for (int j = threadIdx.x; j < len; j += blockDim.x) {
+        const float4* kr = reinterpret_cast<const float4*>(Kc + (long long)(s0 + j) * kv_dim + (long long)kvh * hd);
+        float acc[kAttnMaxGroup];
+#pragma unroll
+        for (int gq = 0; gq < kAttnMaxGroup; ++gq) acc[gq] = 0.f;
+#pragma unroll 8
+        for (int c = 0; c < nd4; ++c) {
+            const float4 k4 = __ldg(kr + c);
+#pragma unroll
+            for (int gq = 0; gq < kAttnMaxGroup; ++gq) {
+                if (gq < group) {
+                    const float4 q4 = reinterpret_cast<const float4*>(qs + gq * hd)[c];
+                    acc[gq] = __fmaf_rn(q4.x, k4.x, acc[gq]);
+                    acc[gq] = __fmaf_rn(q4.y, k4.y, acc[gq]);
+                    acc[gq] = __fmaf_rn(q4.z, k4.z, acc[gq]);
+                    acc[gq] = __fmaf_rn(q4.w, k4.w, acc[gq]);
+                }
+            }
+        }
+#pragma unroll
+        for (int gq = 0; gq < kAttnMaxGroup; ++gq)
+            if (gq < group) sc[gq * chunk_max + j] = __fmul_rn(acc[gq], scale);
     }
     __syncthreads();
-    // p_s = fast_expf(score_s - max over all positions), once per (head, s)
+    // this CTA's max per query head (warp gq), published to every CTA of the cluster
+    if (warp < group) {
+        float m = -INFINITY;
+        for (int j = lane; j < len; j += 32) m = fmaxf(m, sc[warp * chunk_max + j]);
+        m = warp_max_f(m);
+        if (lane < cs) *cl.map_shared_rank(&cmax[rank * kAttnMaxGroup + warp], lane) = m;
+    }
+    cl.sync();
+    if ((int)threadIdx.x < group) {
+        float m = -INFINITY;
+        for (int r = 0; r < cs; ++r) m = fmaxf(m, cmax[r * kAttnMaxGroup + threadIdx.x]);
+        gm[threadIdx.x] = m;
+    }
+    __syncthreads();
+    // p = fast_expf(score - max), in place; the CTA's sum of p per head to CTA 0
     for (int idx = threadIdx.x; idx < group * len; idx += blockDim.x) {
         const int gq = idx / len, j = idx - gq * len;
-        psm[gq * chunk + j] =
-            fast_expf_dev(__fsub_rn(__ldg(scores + ((long long)kvh * group + gq) * ctx + s0 + j), gmax[gq]));
+        sc[gq * chunk_max + j] = fast_expf_dev(__fsub_rn(sc[gq * chunk_max + j], gm[gq]));
     }
     __syncthreads();
-    if (warp < group) {  // the split's sum of p for head `warp`
+    if (warp < group) {
         float sp = 0.f;
-        for (int j = lane; j < len; j += 32) sp += psm[warp * chunk + j];
+        for (int j = lane; j < len; j += 32) sp += sc[warp * chunk_max + j];
         sp = warp_sum_f(sp);
-        if (lane == 0) psum[((long long)kvh * group + warp) * nsplit + split] = sp;
+        if (lane == 0) *cl.map_shared_rank(&csum[rank * kAttnMaxGroup + warp], 0) = sp;
     }
-    // sum_s p_s v_s[d]: threads split (d, position parity); parts = blockDim / hd
-    const int parts = blockDim.x / hd;
-    const int d = threadIdx.x % hd, pidx = threadIdx.x / hd;
-    float acc[kAttnMaxGroup];
+    // sum over positions of p * v: thread (column of 4 dims, part), parts = threads / (hd/4)
+    const int parts = blockDim.x / nd4;
+    const int c4 = threadIdx.x % nd4, part = threadIdx.x / nd4;
+    float4 acc[kAttnMaxGroup];
 #pragma unroll
-    for (int gq = 0; gq < kAttnMaxGroup; ++gq) acc[gq] = 0.f;
-    if (pidx < parts) {
-        const float* vb = Vc + (long long)kvh * hd + d;
-#pragma unroll 8
-        for (int j = pidx; j < len; j += parts) {
-            const float v = __ldg(vb + (long long)(s0 + j) * kv_dim);
+    for (int gq = 0; gq < kAttnMaxGroup; ++gq) acc[gq] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (part < parts) {
+        const float4* vb = reinterpret_cast<const float4*>(Vc + (long long)kvh * hd) + c4;
+#pragma unroll 4
+        for (int j = part; j < len; j += parts) {
+            const float4 v4 = __ldg(vb + (long long)(s0 + j) * (kv_dim / 4));
 #pragma unroll
-            for (int gq = 0; gq < kAttnMaxGroup; ++gq)
-                if (gq < group) acc[gq] = __fmaf_rn(psm[gq * chunk + j], v, acc[gq]);
+            for (int gq = 0; gq < kAttnMaxGroup; ++gq) {
+                if (gq < group) {
+                    const float p = sc[gq * chunk_max + j];
+                    acc[gq].x = __fmaf_rn(p, v4.x, acc[gq].x);
+                    acc[gq].y = __fmaf_rn(p, v4.y, acc[gq].y);
+                    acc[gq].z = __fmaf_rn(p, v4.z, acc[gq].z);
+                    acc[gq].w = __fmaf_rn(p, v4.w, acc[gq].w);
+                }
+            }
         }
-    }
 #pragma unroll
-    for (int gq = 0; gq < kAttnMaxGroup; ++gq)
-        if (gq < group) red[gq * kThreads + threadIdx.x] = acc[gq];
+        for (int gq = 0; gq < kAttnMaxGroup; ++gq)
+            if (gq < group) reinterpret_cast<float4*>(red + ((long long)part * group + gq) * hd)[c4] = acc[gq];
+    }
     __syncthreads();
+    // the CTA's partial of every (head, dim) to CTA 0's slot [rank]
+    float* co0 = cl.map_shared_rank(co, 0);
     for (int idx = threadIdx.x; idx < group * hd; idx += blockDim.x) {
-        const int gq = idx / hd, dd = idx - gq * hd;
         float r = 0.f;
-        for (int k = 0; k < parts; ++k) r += red[gq * kThreads + k * hd + dd];
-        pout[(((long long)kvh * group + gq) * nsplit + split) * hd + dd] = r;
+        for (int k = 0; k < parts; ++k) r += red[(long long)k * group * hd + idx];
+        co0[rank * group * hd + idx] = r;
     }
-    // the last split CTA of this KV head combines the splits in split order:
-    // every writer fences its partials before thread 0 counts this CTA in
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) last = atomicAdd(&counters[kvh], 1u) == (unsigned)(nsplit - 1);
-    __syncthreads();
-    if (!last) return;
-    __threadfence();
-    // 1/sum p per head: warp gq, lanes over the splits (a fixed tree)
-    if (warp < group) {
-        const long long hb = ((long long)kvh * group + warp) * nsplit;
-        float tot = 0.f;
-        for (int k = lane; k < nsplit; k += 32) tot += __ldcg(psum + hb + k);
-        tot = warp_sum_f(tot);
-        if (lane == 0) gmax[warp] = __fdiv_rn(1.0f, tot);
-    }
-    __syncthreads();
-    // out = (sum over splits of p.v) / sum p: warp gq, lane l takes dims l, l+32, ..
-    // (head_dim <= 256: at most 8), all of a split's loads in flight together
-    if (warp < group) {
-        const float* po = pout + ((long long)kvh * group + warp) * nsplit * hd;
-        float r[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) r[u] = 0.f;
-#pragma unroll 8
-        for (int k = 0; k < nsplit; ++k) {
-#pragma unroll
-            for (int u = 0; u < 8; ++u)
-                if (lane + 32 * u < hd) r[u] += __ldcg(po + (long long)k * hd + lane + 32 * u);
+    cl.sync();
+    if (rank == 0) {
+        for (int idx = threadIdx.x; idx < group * hd; idx += blockDim.x) {
+            const int gq = idx / hd;
+            float num = 0.f, den = 0.f;
+            for (int r = 0; r < cs; ++r) {
+                num += co[r * group * hd + idx];
+                den += csum[r * kAttnMaxGroup + gq];
+            }
+            out[(long long)kvh * group * hd + idx] = __fmul_rn(num, __fdiv_rn(1.0f, den));
         }
-        const float inv = gmax[warp];
-        float* o = out + ((long long)kvh * group + warp) * hd;
-#pragma unroll
-        for (int u = 0; u < 8; ++u)
-            if (lane + 32 * u < hd) o[lane + 32 * u] = __fmul_rn(r[u], inv);
     }
-    if (threadIdx.x == 0) counters[kvh] = 0u;
 }
 
 // act[t][i] = silu(y[t][2i]) * y[t][2i+1] over the interleaved gate/up rows,
@@ -542,6 +525,7 @@ struct neon_model {
     neon_tensor_t head = nullptr;    // lm_head shard (tensor parallel only)
     bool head_from_output = false;   // `head` was cut from output.weight, not the tied embedding
     float* part = nullptr;           // partial sums of the column-split projections
+    int att_cs = 8;                  // CTAs per KV head in the decode attention (a cluster)
     float* logits_full = nullptr;    // all-gathered logits (tensor parallel only)
     neon_tensor_t embd = nullptr, output = nullptr;
     float* output_norm = nullptr;
@@ -561,9 +545,6 @@ struct neon_model {
     unsigned* d_err = nullptr;
     unsigned long long* am_key = nullptr;  // argmax scratch
     unsigned int* am_count = nullptr;
-    int att_split = 1;                     // decode attention: position splits per KV head
-    float *att_scores = nullptr, *att_pmax = nullptr, *att_psum = nullptr, *att_pout = nullptr;
-    unsigned int* att_count = nullptr;
     size_t out_cap = 0;
     size_t length = 0;
     cudaStream_t stream = nullptr;
@@ -656,10 +637,41 @@ int launch_k(const char* what, void (*kern)(KArgs...), dim3 grid, int threads, s
     return neon_internal::launched(1);
 }
 
-// Dynamic shared memory of attn_values_kernel: the p of one split.
-size_t attn_values_smem(const neon_model* m) {
-    const size_t group = m->cfg.n_head / m->cfg.n_kv_head;
-    return sizeof(float) * group * (((size_t)m->cfg.ctx_len + m->att_split - 1) / m->att_split);
+// Dynamic shared memory of attn_decode_kernel.
+int attn_chunk_max(const neon_model* m) { return (int)((m->cfg.ctx_len + m->att_cs - 1) / m->att_cs); }
+size_t attn_decode_smem(const neon_model* m) {
+    const int group = (int)(m->cfg.n_head / m->cfg.n_kv_head);
+    return sizeof(float) * (size_t)attn_smem_layout(group, (int)m->cfg.head_dim, attn_chunk_max(m), m->att_cs).total;
+}
+
+// attn_decode_kernel: one cluster of att_cs CTAs per KV head, PDL when enabled.
+int launch_attn_decode(neon_model* m, const float* Kl, const float* Vl) {
+    const auto& c = m->cfg;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(m->n_kv_l * m->att_cs));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = attn_decode_smem(m);
+    cfg.stream = m->stream;
+    cudaLaunchAttribute attr[2];
+    int n = 0;
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = (unsigned)m->att_cs;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+    if (neon_internal::pdl_enabled()) {
+        attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[n].val.programmaticStreamSerializationAllowed = 1;
+        ++n;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = n;
+    const float scale = 1.0f / std::sqrt((float)c.head_dim);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, attn_decode_kernel, (const float*)m->q, Kl, Vl, (const int*)m->d_pos,
+                                       (int)m->kv_dim, (int)c.head_dim, (int)(c.n_head / c.n_kv_head), scale,
+                                       attn_chunk_max(m), m->att);
+    if (e != cudaSuccess) return cuda_error(e, "attn_decode_kernel");
+    return neon_internal::launched(1);
 }
 
 int rmsnorm(neon_model* m, const float* x, const float* w, float* out, int rows) {
@@ -755,8 +767,6 @@ int run_step(neon_model* m) {
     int rc = launch_k("embed_kernel", embed_kernel, dim3((nb + 127) / 128, 1), 128, 0, m->stream, E->qs, E->d, E->type,
                       nb, m->d_tok, (int)c.n_vocab, m->h, m->d_err);
     const size_t n_embd = c.n_embd, q_dim = m->q_dim, kv_dim = m->kv_dim, n_ff = m->n_ff_l;
-    const float scale = 1.0f / std::sqrt((float)c.head_dim);
-    const int group = (int)(c.n_head / c.n_kv_head);
     const bool fused = m->world > 1 && neon_internal::fused_collectives();
     float* hc = m->h;
     // h += W x: fused producer + LL reduce, or matvec + all-reduce, or one device's accumulate
@@ -795,16 +805,7 @@ int run_step(neon_model* m) {
             ext.pos_stride = stride;
             rc = neon_internal::matvec(t, 3, hc, n_embd, 1, m->stream, 0, &ext);
         }
-        if (!rc) {
-            const dim3 grid((unsigned)m->n_kv_l, m->att_split);
-            rc = launch_k("attn_scores_kernel", attn_scores_kernel, grid, kThreads, 0, m->stream, m->q, Kl, m->d_pos,
-                          (int)kv_dim, (int)c.head_dim, group, scale, m->att_split, (int)c.ctx_len, m->att_scores,
-                          m->att_pmax);
-            if (!rc)
-                rc = launch_k("attn_values_kernel", attn_values_kernel, grid, kThreads, attn_values_smem(m), m->stream,
-                              Vl, m->d_pos, (int)kv_dim, (int)c.head_dim, group, m->att_split, (int)c.ctx_len,
-                              m->att_scores, m->att_pmax, m->att_psum, m->att_pout, m->att_count, m->att);
-        }
+        if (!rc) rc = launch_attn_decode(m, Kl, Vl);
         if (!rc) rc = residual(L.w[3], m->att, q_dim);
         if (!rc) {
             // act = silu(gate) * up, (gate, up) = W x with x = rms_norm(h); or silu(up)
@@ -983,19 +984,6 @@ int neon_cuda_model_create_tp(const neon_model_config_t* cfg, neon_comm_t comm, 
     }
     A((void**)&m->am_key, sizeof(unsigned long long));
     A((void**)&m->am_count, sizeof(unsigned int));
-    // decode attention: splits so that (KV heads x splits) fills about two CTAs per SM
-    {
-        int sms = neon_internal::device_sms(m->device);
-        if (sms <= 0) sms = 148;
-        m->att_split = (int)std::max<long long>(1, std::min<long long>((c.ctx_len + 15) / 16, (3LL * sms) / (long long)m->n_kv_l));
-        // the p of a split must fit attn_values_kernel's shared memory
-        while (attn_values_smem(m) > 160 * 1024) ++m->att_split;
-    }
-    A((void**)&m->att_scores, sizeof(float) * m->n_head_l * c.ctx_len);
-    A((void**)&m->att_pmax, sizeof(float) * m->n_head_l * m->att_split);
-    A((void**)&m->att_psum, sizeof(float) * m->n_head_l * m->att_split);
-    A((void**)&m->att_pout, sizeof(float) * m->n_head_l * m->att_split * c.head_dim);
-    A((void**)&m->att_count, sizeof(unsigned int) * m->n_kv_l);
     A((void**)&m->logits, sizeof(float) * m->vocab_l);
     A((void**)&m->d_tokens, sizeof(int) * S);
     A((void**)&m->d_tok, sizeof(int));
@@ -1021,14 +1009,40 @@ int neon_cuda_model_create_tp(const neon_model_config_t* cfg, neon_comm_t comm, 
             cudaMemset(m->d_err, 0, sizeof(unsigned)) != cudaSuccess || cudaMemset(m->K, 0, kv_bytes) != cudaSuccess ||
             cudaMemset(m->am_key, 0, sizeof(unsigned long long)) != cudaSuccess ||
             cudaMemset(m->am_count, 0, sizeof(unsigned int)) != cudaSuccess ||
-            cudaMemset(m->att_count, 0, sizeof(unsigned int) * m->n_kv_l) != cudaSuccess ||
             cudaMemset(m->V, 0, kv_bytes) != cudaSuccess)
             rc = error(NEON_ERR_CUDA, "model initialisation copies failed");
     }
-    if (!rc && attn_values_smem(m) > 48 * 1024) {
-        if (cudaFuncSetAttribute(attn_values_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn_values_smem(m)) !=
-            cudaSuccess)
-            rc = error(NEON_ERR_CUDA, "cudaFuncSetAttribute(attn_values_kernel)");
+    if (!rc) {
+        // long contexts: 16 CTAs per KV head when the device schedules clusters that large
+        if (c.ctx_len > 1024 &&
+            cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess) {
+            m->att_cs = kAttnMaxCluster;
+            cudaLaunchConfig_t q = {};
+            q.gridDim = dim3((unsigned)(m->n_kv_l * m->att_cs));
+            q.blockDim = dim3(kThreads);
+            q.dynamicSmemBytes = attn_decode_smem(m);
+            cudaLaunchAttribute qa[1];
+            qa[0].id = cudaLaunchAttributeClusterDimension;
+            qa[0].val.clusterDim.x = (unsigned)m->att_cs;
+            qa[0].val.clusterDim.y = 1;
+            qa[0].val.clusterDim.z = 1;
+            q.attrs = qa;
+            q.numAttrs = 1;
+            int clusters = 0;
+            if (q.dynamicSmemBytes > 48 * 1024)
+                cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)q.dynamicSmemBytes);
+            if (cudaOccupancyMaxActiveClusters(&clusters, attn_decode_kernel, &q) != cudaSuccess || clusters < 1) {
+                cudaGetLastError();
+                m->att_cs = 8;
+            }
+        }
+    }
+    if (!rc && attn_decode_smem(m) > 48 * 1024) {
+        if (attn_decode_smem(m) > 220 * 1024)
+            rc = error(NEON_ERR_UNSUPPORTED, "decode attention: ctx_len too large for one cluster per KV head");
+        else if (cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)attn_decode_smem(m)) != cudaSuccess)
+            rc = error(NEON_ERR_CUDA, "cudaFuncSetAttribute(attn_decode_kernel)");
     }
     if (!rc && c.ctx_len * sizeof(float) > 48 * 1024) {
         if (cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(c.ctx_len * sizeof(float))) != cudaSuccess)

@@ -82,6 +82,7 @@ def test_errors_match_reference_messages():
 @pytest.mark.parametrize("cfg,n_prompt,steps", [
     (TINY.with_(n_vocab=777, n_embd=384, n_ff=1024, n_head=6, n_kv_head=2, ctx_len=300), 200, 24),
     (TINY.with_(plain_ffn=True, n_ff=768, ctx_len=120), 40, 24),                 # SiLU-FFN without a gate
+    (TINY.with_(n_head=8, n_kv_head=1, ctx_len=1100), 1060, 16),                 # long context: 16-CTA clusters, group 8
     (S.QWEN3_0_6B.with_(ctx_len=128 + 64 + 1), 128, 64),
 ])
 def test_greedy_matches_reference(cfg, n_prompt, steps):
