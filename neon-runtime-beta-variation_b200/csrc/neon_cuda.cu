@@ -198,13 +198,16 @@ StreamPlan plan_stream(int type, int nb, size_t total_rows, int sms) {
 
 // The streaming kernel instantiation for (type, rows per tile).
 StreamKernel stream_kernel(int type, int rc) {
+    // R rows per thread: each shared-memory read of an X block serves R rows
+    // (shared-memory bandwidth, not HBM, limits R = 1 on large matrices);
+    // 4 for tall tiles, 2 for the 8-row tiles of long rows (measured best)
     if (type == NEON_GGML_Q4_0) {
         switch (rc) {
-            case 2: return matvec_stream_kernel<NEON_GGML_Q4_0, 2, 1>;
-            case 4: return matvec_stream_kernel<NEON_GGML_Q4_0, 4, 1>;
-            case 8: return matvec_stream_kernel<NEON_GGML_Q4_0, 8, 1>;
-            case 16: return matvec_stream_kernel<NEON_GGML_Q4_0, 16, 1>;
-            default: return matvec_stream_kernel<NEON_GGML_Q4_0, 32, 1>;
+            case 2: return matvec_stream_kernel<NEON_GGML_Q4_0, 2, 2>;
+            case 4: return matvec_stream_kernel<NEON_GGML_Q4_0, 4, 2>;
+            case 8: return matvec_stream_kernel<NEON_GGML_Q4_0, 8, 2>;
+            case 16: return matvec_stream_kernel<NEON_GGML_Q4_0, 16, 4>;
+            default: return matvec_stream_kernel<NEON_GGML_Q4_0, 32, 4>;
         }
     }
     switch (rc) {
@@ -225,7 +228,7 @@ int stream_occupancy(int type, int rc, int smem) {
     for (auto& kv : cache)
         if (kv.first == key) return kv.second;
     int occ = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, stream_kernel(type, rc), kStreamThreads, smem) !=
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, stream_kernel(type, rc), kStreamBlock, smem) !=
         cudaSuccess)
         occ = 1;
     occ = std::max(1, occ);
@@ -305,7 +308,7 @@ int launch_stream(const std::vector<const neon_proj_target_t*>& t, int type, int
         const int per_cta_items = ((tiles + grid - 1) / grid) * p.nch;
         a.stages = std::max(1, std::min(best_stages, per_cta_items));
         const int smem = stream_smem_bytes(type, nb, a.stages, p.stage_bytes);
-        int rc = launch_n(stream_kernel(type, p.rc), dim3(grid), kStreamThreads, smem, st, a);
+        int rc = launch_n(stream_kernel(type, p.rc), dim3(grid), kStreamBlock, smem, st, a);
         if (rc) return rc;
         start += n;
     }

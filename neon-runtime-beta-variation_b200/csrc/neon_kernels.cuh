@@ -307,8 +307,9 @@ __device__ __forceinline__ void store_tile(const float (&acc)[R], float* y, int 
 // carries 16 bytes of tail padding so a window never leaves the allocation),
 // one window per tile (contiguous case) or per row at a pitch of SPH halfs.
 // ---------------------------------------------------------------------------
-constexpr int kStreamWarps = 8;
+constexpr int kStreamWarps = 8;                      // compute warps
 constexpr int kStreamThreads = kStreamWarps * 32;
+constexpr int kStreamBlock = kStreamThreads + 32;    // + the copy warp
 constexpr int kMaxRopeHalf = 128;  // head_dim <= 256
 constexpr int kMaxStages = 3;
 
@@ -378,6 +379,22 @@ __device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsign
     asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Barrier of the streaming kernel's compute warps only (named barrier 1,
+// kStreamThreads threads): its copy warp never waits on it.
+__device__ __forceinline__ void compute_sync() { asm volatile("bar.sync 1, %0;" ::"n"(256) : "memory"); }
+__device__ __forceinline__ bool compute_sync_or(bool v) {
+    uint32_t r;
+    asm volatile("{ .reg .pred p, q; setp.ne.u32 p, %1, 0; bar.red.or.pred q, 1, %2, p; selp.u32 %0, 1, 0, q; }"
+                 : "=r"(r)
+                 : "r"((uint32_t)v), "n"(256)
+                 : "memory");
+    return r != 0;
+}
+
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int* err) {
     const uint32_t addr = smem_u32(bar);
     uint32_t done = 0;
@@ -421,7 +438,7 @@ __host__ __device__ constexpr int stream_x_bytes(int type, int nb) {
 // so every CTA of the launch derives the same scale.
 __device__ __forceinline__ float cta_rms_scale(const float* __restrict__ x, int n, float eps, double* scratch) {
     double ss = 0.0;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    for (int i = threadIdx.x; i < n; i += kStreamThreads) {
         const double v = (double)__ldg(x + i);
         ss = fma(v, v, ss);
     }
@@ -429,11 +446,11 @@ __device__ __forceinline__ float cta_rms_scale(const float* __restrict__ x, int 
     for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
     const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
     if (l == 0) scratch[w] = ss;
-    __syncthreads();
-    double r = l < (int)(blockDim.x >> 5) ? scratch[l] : 0.0;
+    compute_sync();
+    double r = l < kStreamWarps ? scratch[l] : 0.0;
 #pragma unroll
     for (int o = 16; o; o >>= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
-    __syncthreads();  // scratch may be reused right after
+    compute_sync();  // scratch may be reused right after
     return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)(r / (double)n), eps)));
 }
 
@@ -548,7 +565,7 @@ __device__ __forceinline__ void stage_x_q8_norm(const float* __restrict__ x, int
     for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
     const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
     if (l == 0) scratch[w] = ss;
-    __syncthreads();
+    compute_sync();
     double r = l < kStreamWarps ? scratch[l] : 0.0;
 #pragma unroll
     for (int o = 16; o; o >>= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
@@ -675,7 +692,7 @@ __device__ __forceinline__ void stream_epilogue(const StreamArgs& a, const Span&
 // TPG >= 32 (a row split over several warps: K-split, finished through shared
 // memory), else 32/TPG groups per warp (finished by a shuffle tree).
 template <int TYPE, int RC, int R>
-__global__ void __launch_bounds__(kStreamThreads) matvec_stream_kernel(const __grid_constant__ StreamArgs a) {
+__global__ void __launch_bounds__(kStreamBlock) matvec_stream_kernel(const __grid_constant__ StreamArgs a) {
     constexpr int P = TYPE == 2 ? 16 : 32;
     constexpr int G = RC / R;
     constexpr int TPG = kStreamThreads / G;
@@ -683,13 +700,14 @@ __global__ void __launch_bounds__(kStreamThreads) matvec_stream_kernel(const __g
     constexpr int LPG = TPG >= 32 ? 32 : TPG;
     static_assert(RC % R == 0 && kStreamThreads % G == 0, "bad tile shape");
     extern __shared__ __align__(128) unsigned char smem[];
-    __shared__ float red[RC * WPG];
-    __shared__ float rowv[RC];
+    __shared__ float red[2][RC * WPG];  // by tile parity: a tile's reduction never waits on the last epilogue
+    __shared__ float rowv[2][RC];
     const int nb = a.nb, KC = a.kc, nch = a.nch, S = a.stages;
     const int SPH = stream_scale_pitch(KC);
     unsigned char* xsm = smem;
     unsigned char* ring = smem + stream_x_bytes(TYPE, nb);
     uint64_t* full = reinterpret_cast<uint64_t*>(ring + S * a.stage_bytes);
+    uint64_t* empty = full + kMaxStages;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = TPG >= 32 ? warp / WPG : warp * (32 / TPG) + lane / TPG;
     const int slice = TPG >= 32 ? (warp % WPG) * 32 + lane : lane % TPG;
@@ -698,12 +716,15 @@ __global__ void __launch_bounds__(kStreamThreads) matvec_stream_kernel(const __g
     const int n_items = my_tiles * nch;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < S; ++s) mbar_init(&full[s], 1);
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kStreamWarps);
+        }
         fence_mbar_init();
     }
     __syncthreads();
 
-    // Warp 0: copy item `item` of this CTA into its stage.
+    // The copy warp: item `item` of this CTA into its stage.
     auto issue = [&](int item) {
         const int stage = item % S;
         const int tile = (int)blockIdx.x + (item / nch) * (int)gridDim.x;
@@ -745,9 +766,18 @@ __global__ void __launch_bounds__(kStreamThreads) matvec_stream_kernel(const __g
         }
     };
 
-    if (warp == 0) {
-        const int first = min(S, n_items);
-        for (int i = 0; i < first; ++i) issue(i);
+    if (warp == kStreamWarps) {
+        // Copy warp (never reads what earlier kernels wrote, so no PDL wait):
+        // a stage is refilled as soon as every compute warp has released it.
+        // The CTA lets the next launch start when its compute warps have
+        // staged X; this warp, which lives until its last copy, signals now.
+        pdl_launch_dependents();
+        for (int item = 0; item < n_items; ++item) {
+            const int stage = item % S;
+            if (item >= S && !mbar_wait(&empty[stage], (uint32_t)(((item / S) - 1) & 1), a.err)) break;
+            issue(item);
+        }
+        return;
     }
     pdl_wait();
 
@@ -784,7 +814,7 @@ __global__ void __launch_bounds__(kStreamThreads) matvec_stream_kernel(const __g
             xs[(i >> 5) * kQ8Pitch + (i & 31)] = v;
         }
     }
-    __syncthreads();
+    compute_sync();
     pdl_launch_dependents();
 
     float acc[R];
@@ -800,7 +830,8 @@ __global__ void __launch_bounds__(kStreamThreads) matvec_stream_kernel(const __g
         const int k0 = chunk * KC;
         const int kc = min(KC, nb - k0);
         const bool ok = mbar_wait(&full[stage], parity, a.err);
-        if (__syncthreads_or(!ok)) return;
+        if (compute_sync_or(!ok)) return;
+        const int tb = (item / nch) & 1;
         // the accumulate epilogue's y[row], fetched while the dot products run
         float yold = 0.f;
         if (a.accumulate && chunk == nch - 1 && sp.epi == kEpiStore && (int)threadIdx.x < RC &&
@@ -854,13 +885,10 @@ __global__ void __launch_bounds__(kStreamThreads) matvec_stream_kernel(const __g
         }
 #pragma unroll
         for (int rr = 0; rr < R; ++rr) acc[rr] += part[rr];
-        // every warp is done with this stage: refill it before the row
-        // reduction and the epilogue, so their latency overlaps the copy
-        __syncthreads();
-        if (warp == 0 && item + S < n_items) {
-            fence_proxy_async_smem();
-            issue(item + S);
-        }
+        // this warp is done with the stage: release it to the copy warp
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[stage]);
         if (chunk == nch - 1) {
 #pragma unroll
             for (int rr = 0; rr < R; ++rr)
@@ -870,21 +898,21 @@ __global__ void __launch_bounds__(kStreamThreads) matvec_stream_kernel(const __g
             if (WPG == 1) {
                 if (slice == 0) {
 #pragma unroll
-                    for (int rr = 0; rr < R; ++rr) rowv[g * R + rr] = acc[rr];
+                    for (int rr = 0; rr < R; ++rr) rowv[tb][g * R + rr] = acc[rr];
                 }
             } else if (lane == 0) {
 #pragma unroll
-                for (int rr = 0; rr < R; ++rr) red[(g * R + rr) * WPG + (warp % WPG)] = acc[rr];
+                for (int rr = 0; rr < R; ++rr) red[tb][(g * R + rr) * WPG + (warp % WPG)] = acc[rr];
             }
-            __syncthreads();
+            compute_sync();
             if (WPG > 1 && (int)threadIdx.x < RC) {
                 float v = 0.f;
 #pragma unroll
-                for (int w = 0; w < WPG; ++w) v += red[threadIdx.x * WPG + w];
-                rowv[threadIdx.x] = v;
+                for (int w = 0; w < WPG; ++w) v += red[tb][threadIdx.x * WPG + w];
+                rowv[tb][threadIdx.x] = v;
             }
-            if (WPG > 1) __syncthreads();
-            stream_epilogue(a, sp, row0, RC, rowv, peer_call, pos, rcs, yold);
+            if (WPG > 1) compute_sync();
+            stream_epilogue(a, sp, row0, RC, rowv[tb], peer_call, pos, rcs, yold);
 #pragma unroll
             for (int rr = 0; rr < R; ++rr) acc[rr] = 0.f;
         }
@@ -893,7 +921,7 @@ __global__ void __launch_bounds__(kStreamThreads) matvec_stream_kernel(const __g
 
 // Shared-memory bytes of a streaming launch.
 __host__ __device__ constexpr int stream_smem_bytes(int type, int nb, int stages, int stage_bytes) {
-    return stream_x_bytes(type, nb) + stages * stage_bytes + kMaxStages * 8;
+    return stream_x_bytes(type, nb) + stages * stage_bytes + 2 * kMaxStages * 8;  // + full and empty barriers
 }
 
 // Bytes of one ring stage for RC rows x kc blocks.
