@@ -276,37 +276,70 @@ constexpr int kAttnMaxGroup = 8;  // query heads per KV head in the decode atten
 
 // ---------------------------------------------------------------------------
 // Decode attention in one launch: a thread-block cluster of cs CTAs (8, or 16
-// for long contexts) per KV head. CTA r of the cluster takes positions [r*chunk, (r+1)*chunk) of
-// the L = *d_pos + 1 cache rows and scores them for the head's query group
-// into shared memory; the CTAs exchange their maxima through distributed
-// shared memory, so every CTA forms p_s = fast_expf(score_s - max over ALL
-// positions) exactly as transformer_forward does (:1123-1137); each CTA sums
-// p and p * v over its positions, and CTA 0 of the cluster adds the partials
-// in rank order: out = (sum p v) / (sum p). Cluster barriers replace the
-// global round trips of a split kernel pair.
+// for long contexts) per KV head. CTA r of the cluster takes positions
+// [r*chunk, (r+1)*chunk) of the L = *d_pos + 1 cache rows. Its K rows, then its
+// V rows, stream through a two-slot shared-memory ring (cp.async.bulk, one row
+// per copy, rows padded by 64 bytes so the four threads scoring a row read
+// conflict-free quarters) in sub-chunks of kAttnSub rows: the copy of the next
+// sub-chunk is in flight while the current one is used. Scores for the head's
+// query group go to shared memory; the CTAs exchange their maxima through
+// distributed shared memory, so every CTA forms p_s = fast_expf(score_s - max
+// over ALL positions) exactly as transformer_forward does (:1123-1137); each
+// CTA sums p and p * v over its positions, and CTA 0 adds the partials in rank
+// order: out = (sum p v) / (sum p).
 // ---------------------------------------------------------------------------
 constexpr int kAttnMaxCluster = 16;
+constexpr int kAttnSub = 64;  // cache rows per ring slot
+
+__device__ __forceinline__ uint32_t smem_addr_d(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ bool mbar_wait_d(uint64_t* bar, uint32_t parity, unsigned int* err) {
+    uint32_t done = 0;
+    unsigned long long t0 = 0;
+    for (int it = 0;; ++it) {
+        asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+                     : "=r"(done)
+                     : "r"(smem_addr_d(bar)), "r"(parity)
+                     : "memory");
+        if (done) return true;
+        unsigned long long t;
+        asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+        if (it == 0) t0 = t;
+        else if (t - t0 > 2000000000ull) {
+            atomicOr(err, 4u);
+            return false;
+        }
+    }
+}
 
 struct AttnSmem {  // offsets (floats) into the dynamic shared memory
-    int q, sc, red, co, csum, cmax, total;
+    int q, sc, ring, co, csum, cmax, bar, total;
 };
 __host__ __device__ inline AttnSmem attn_smem_layout(int group, int hd, int chunk_max, int cs) {
     auto up4 = [](int v) { return (v + 3) & ~3; };  // float4-aligned regions
+    auto mx = [](int a, int b) { return a > b ? a : b; };
+    const int pitch = hd + 16;
+    const int parts = kThreads / (hd / 4);
     AttnSmem l;
     l.q = 0;
     l.sc = up4(l.q + group * hd);
-    l.red = up4(l.sc + group * chunk_max);
-    l.co = up4(l.red + (kThreads / (hd / 4)) * group * hd);
-    l.csum = up4(l.co + cs * group * hd);
+    l.ring = up4(l.sc + group * chunk_max);
+    // once the V rows are used, the ring holds the per-part partial sums, and
+    // then (in CTA 0) the cluster's partials
+    const int ring = mx(2 * kAttnSub * pitch, mx(parts * group * hd, cs * group * hd));
+    l.co = l.ring;
+    l.csum = up4(l.ring + ring);
     l.cmax = up4(l.csum + cs * kAttnMaxGroup);
-    l.total = up4(l.cmax + cs * kAttnMaxGroup);
+    l.bar = up4(l.cmax + cs * kAttnMaxGroup);
+    l.total = l.bar + 4 * 2;  // two 8-byte mbarriers
     return l;
 }
 
 __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const float* __restrict__ q, const float* __restrict__ Kc,
                                                                const float* __restrict__ Vc, const int* __restrict__ d_pos,
                                                                int kv_dim, int hd, int group, float scale, int chunk_max,
-                                                               float* __restrict__ out) {
+                                                               float* __restrict__ out, unsigned int* err) {
     namespace cg = cooperative_groups;
     extern __shared__ __align__(16) float sm[];
     cg::cluster_group cl = cg::this_cluster();
@@ -315,45 +348,98 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const float* __re
     const AttnSmem lay = attn_smem_layout(group, hd, chunk_max, cs);
     float* qs = sm + lay.q;
     float* sc = sm + lay.sc;     // [group][chunk_max]
-    float* red = sm + lay.red;   // [parts][group][hd]
-    float* co = sm + lay.co;     // [cluster][group][hd]   (read in CTA 0)
+    float* ring = sm + lay.ring; // [2][kAttnSub][hd + 4]; later [parts][group][hd]
+    float* co = sm + lay.co;     // [cluster][group][hd]   (CTA 0; overlays the ring)
     float* csum = sm + lay.csum; // [cluster][kAttnMaxGroup] (read in CTA 0)
     float* cmax = sm + lay.cmax; // [cluster][kAttnMaxGroup]
+    uint64_t* full = reinterpret_cast<uint64_t*>(sm + lay.bar);
     __shared__ float gm[kAttnMaxGroup];
+    const int pitch = hd + 16;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < 2; ++i)
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr_d(&full[i])) : "memory");
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
     pdl_wait_d();
     pdl_trigger_d();
+    __syncthreads();
     const int L = *d_pos + 1;
     const int chunk = (L + cs - 1) / cs;
     const int s0 = min(L, rank * chunk), len = min(L, s0 + chunk) - s0;
+    const int n_sub = (len + kAttnSub - 1) / kAttnSub;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nd4 = hd / 4;
+    // item t < n_sub: K rows of sub-chunk t; n_sub <= t < 2 n_sub: V rows of sub-chunk t - n_sub
+    auto issue = [&](int t) {
+        const int slot = t & 1;
+        const bool is_v = t >= n_sub;
+        const int sub = is_v ? t - n_sub : t;
+        const int j0 = sub * kAttnSub, rows = min(kAttnSub, len - j0);
+        const float* base = (is_v ? Vc : Kc) + (long long)kvh * hd;
+        float* dst = ring + slot * kAttnSub * pitch;
+        if (lane == 0)
+            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr_d(&full[slot])),
+                         "r"((uint32_t)(rows * hd * 4))
+                         : "memory");
+        __syncwarp();
+        for (int r = lane; r < rows; r += 32)
+            asm volatile(
+                "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                    smem_addr_d(dst + r * pitch)),
+                "l"(base + (long long)(s0 + j0 + r) * kv_dim), "r"((uint32_t)(hd * 4)), "r"(smem_addr_d(&full[slot]))
+                : "memory");
+    };
+    const int n_items = 2 * n_sub;
+    if (warp == 0)
+        for (int t = 0; t < min(2, n_items); ++t) issue(t);
     for (int i = threadIdx.x; i < group * hd; i += blockDim.x) qs[i] = q[(long long)kvh * group * hd + i];
     __syncthreads();
-    // scores: a thread per position, its whole K row in flight
-    for (int j = threadIdx.x; j < len; j += blockDim.x) {
-        const float4* kr = reinterpret_cast<const float4*>(Kc + (long long)(s0 + j) * kv_dim + (long long)kvh * hd);
-        float acc[kAttnMaxGroup];
+    bool ok = true;
+    // pass 1: scores, a thread per cache row of the slot
+    for (int t = 0; t < n_sub; ++t) {
+        ok = ok && mbar_wait_d(&full[t & 1], (uint32_t)((t >> 1) & 1), err);
+        const float* rows_k = ring + (t & 1) * kAttnSub * pitch;
+        const int j0 = t * kAttnSub, rows = min(kAttnSub, len - j0);
+        {
+            // four threads per row (lanes 4r'..4r'+3 of a warp), thread q4i takes float4
+            // columns q4i, q4i+4, ..; the four partial dots meet by two shuffles
+            const int r = threadIdx.x >> 2, q4i = threadIdx.x & 3;
+            const float4* kr = reinterpret_cast<const float4*>(rows_k + r * pitch);
+            float acc[kAttnMaxGroup];
 #pragma unroll
-        for (int gq = 0; gq < kAttnMaxGroup; ++gq) acc[gq] = 0.f;
-#pragma unroll 8
-        for (int c = 0; c < nd4; ++c) {
-            const float4 k4 = __ldg(kr + c);
+            for (int gq = 0; gq < kAttnMaxGroup; ++gq) acc[gq] = 0.f;
+            if (r < rows) {
+                for (int c = q4i; c < nd4; c += 4) {
+                    const float4 k4 = kr[c];
 #pragma unroll
-            for (int gq = 0; gq < kAttnMaxGroup; ++gq) {
-                if (gq < group) {
-                    const float4 q4 = reinterpret_cast<const float4*>(qs + gq * hd)[c];
-                    acc[gq] = __fmaf_rn(q4.x, k4.x, acc[gq]);
-                    acc[gq] = __fmaf_rn(q4.y, k4.y, acc[gq]);
-                    acc[gq] = __fmaf_rn(q4.z, k4.z, acc[gq]);
-                    acc[gq] = __fmaf_rn(q4.w, k4.w, acc[gq]);
+                    for (int gq = 0; gq < kAttnMaxGroup; ++gq) {
+                        if (gq < group) {
+                            const float4 q4 = reinterpret_cast<const float4*>(qs + gq * hd)[c];
+                            acc[gq] = __fmaf_rn(q4.x, k4.x, acc[gq]);
+                            acc[gq] = __fmaf_rn(q4.y, k4.y, acc[gq]);
+                            acc[gq] = __fmaf_rn(q4.z, k4.z, acc[gq]);
+                            acc[gq] = __fmaf_rn(q4.w, k4.w, acc[gq]);
+                        }
+                    }
                 }
             }
-        }
 #pragma unroll
-        for (int gq = 0; gq < kAttnMaxGroup; ++gq)
-            if (gq < group) sc[gq * chunk_max + j] = __fmul_rn(acc[gq], scale);
+            for (int gq = 0; gq < kAttnMaxGroup; ++gq) {
+                acc[gq] += __shfl_xor_sync(0xffffffffu, acc[gq], 1);
+                acc[gq] += __shfl_xor_sync(0xffffffffu, acc[gq], 2);
+            }
+            if (r < rows && q4i == 0) {
+#pragma unroll
+                for (int gq = 0; gq < kAttnMaxGroup; ++gq)
+                    if (gq < group) sc[gq * chunk_max + j0 + r] = __fmul_rn(acc[gq], scale);
+            }
+        }
+        __syncthreads();  // the slot is free
+        if (warp == 0 && t + 2 < n_items) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            issue(t + 2);
+        }
     }
-    __syncthreads();
     // this CTA's max per query head (warp gq), published to every CTA of the cluster
     if (warp < group) {
         float m = -INFINITY;
@@ -380,39 +466,64 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const float* __re
         sp = warp_sum_f(sp);
         if (lane == 0) *cl.map_shared_rank(&csum[rank * kAttnMaxGroup + warp], 0) = sp;
     }
-    // sum over positions of p * v: thread (column of 4 dims, part), parts = threads / (hd/4)
+    // pass 2: sum over positions of p * v; thread (column of 4 dims, part)
     const int parts = blockDim.x / nd4;
     const int c4 = threadIdx.x % nd4, part = threadIdx.x / nd4;
     float4 acc[kAttnMaxGroup];
 #pragma unroll
     for (int gq = 0; gq < kAttnMaxGroup; ++gq) acc[gq] = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (part < parts) {
-        const float4* vb = reinterpret_cast<const float4*>(Vc + (long long)kvh * hd) + c4;
-#pragma unroll 4
-        for (int j = part; j < len; j += parts) {
-            const float4 v4 = __ldg(vb + (long long)(s0 + j) * (kv_dim / 4));
+    for (int t = n_sub; t < n_items; ++t) {
+        ok = ok && mbar_wait_d(&full[t & 1], (uint32_t)((t >> 1) & 1), err);
+        const float* rows_v = ring + (t & 1) * kAttnSub * pitch;
+        const int j0 = (t - n_sub) * kAttnSub, rows = min(kAttnSub, len - j0);
+        if (part < parts) {
+            for (int r = part; r < rows; r += parts) {
+                const float4 v4 = reinterpret_cast<const float4*>(rows_v + r * pitch)[c4];
 #pragma unroll
-            for (int gq = 0; gq < kAttnMaxGroup; ++gq) {
-                if (gq < group) {
-                    const float p = sc[gq * chunk_max + j];
-                    acc[gq].x = __fmaf_rn(p, v4.x, acc[gq].x);
-                    acc[gq].y = __fmaf_rn(p, v4.y, acc[gq].y);
-                    acc[gq].z = __fmaf_rn(p, v4.z, acc[gq].z);
-                    acc[gq].w = __fmaf_rn(p, v4.w, acc[gq].w);
+                for (int gq = 0; gq < kAttnMaxGroup; ++gq) {
+                    if (gq < group) {
+                        const float p = sc[gq * chunk_max + j0 + r];
+                        acc[gq].x = __fmaf_rn(p, v4.x, acc[gq].x);
+                        acc[gq].y = __fmaf_rn(p, v4.y, acc[gq].y);
+                        acc[gq].z = __fmaf_rn(p, v4.z, acc[gq].z);
+                        acc[gq].w = __fmaf_rn(p, v4.w, acc[gq].w);
+                    }
                 }
             }
         }
+        __syncthreads();
+        if (warp == 0 && t + 2 < n_items) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            issue(t + 2);
+        }
+    }
+    (void)ok;  // a timed-out copy sets bit 2 of the error word; the results are then not used
+    // per-part partials -> the ring (its copies are all consumed), then the CTA's partial to CTA 0
+    float* red = ring;
+    if (part < parts) {
 #pragma unroll
         for (int gq = 0; gq < kAttnMaxGroup; ++gq)
             if (gq < group) reinterpret_cast<float4*>(red + ((long long)part * group + gq) * hd)[c4] = acc[gq];
     }
     __syncthreads();
-    // the CTA's partial of every (head, dim) to CTA 0's slot [rank]
-    float* co0 = cl.map_shared_rank(co, 0);
-    for (int idx = threadIdx.x; idx < group * hd; idx += blockDim.x) {
+    // this CTA's partial of every (head, dim), held while the cluster finishes
+    // with its rings (CTA 0's ring then takes the partials)
+    constexpr int kMaxPer = kAttnMaxGroup * 256 / kThreads;
+    float mine[kMaxPer];
+#pragma unroll
+    for (int u = 0; u < kMaxPer; ++u) {
+        const int idx = threadIdx.x + u * kThreads;
         float r = 0.f;
-        for (int k = 0; k < parts; ++k) r += red[(long long)k * group * hd + idx];
-        co0[rank * group * hd + idx] = r;
+        if (idx < group * hd)
+            for (int k = 0; k < parts; ++k) r += red[(long long)k * group * hd + idx];
+        mine[u] = r;
+    }
+    cl.sync();
+    float* co0 = cl.map_shared_rank(co, 0);
+#pragma unroll
+    for (int u = 0; u < kMaxPer; ++u) {
+        const int idx = threadIdx.x + u * kThreads;
+        if (idx < group * hd) co0[rank * group * hd + idx] = mine[u];
     }
     cl.sync();
     if (rank == 0) {
@@ -669,7 +780,7 @@ int launch_attn_decode(neon_model* m, const float* Kl, const float* Vl) {
     const float scale = 1.0f / std::sqrt((float)c.head_dim);
     cudaError_t e = cudaLaunchKernelEx(&cfg, attn_decode_kernel, (const float*)m->q, Kl, Vl, (const int*)m->d_pos,
                                        (int)m->kv_dim, (int)c.head_dim, (int)(c.n_head / c.n_kv_head), scale,
-                                       attn_chunk_max(m), m->att);
+                                       attn_chunk_max(m), m->att, m->d_err);
     if (e != cudaSuccess) return cuda_error(e, "attn_decode_kernel");
     return neon_internal::launched(1);
 }
@@ -857,6 +968,10 @@ int sync_and_check(neon_model* m) {
         DEC_TRY(cudaMemset(m->d_err, 0, sizeof(unsigned)));
         return error(NEON_ERR_INVALID, "forward(): token id out of vocab range");
     }
+    if (e & 4u) {
+        DEC_TRY(cudaMemset(m->d_err, 0, sizeof(unsigned)));
+        return error(NEON_ERR_CUDA, "decode attention: a shared-memory copy of the KV cache never completed");
+    }
     if (m->world > 1) {
         const int rc = neon_cuda_comm_check(static_cast<neon_comm*>(m->comm));
         if (rc) return rc;
@@ -1031,7 +1146,8 @@ int neon_cuda_model_create_tp(const neon_model_config_t* cfg, neon_comm_t comm, 
             int clusters = 0;
             if (q.dynamicSmemBytes > 48 * 1024)
                 cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)q.dynamicSmemBytes);
-            if (cudaOccupancyMaxActiveClusters(&clusters, attn_decode_kernel, &q) != cudaSuccess || clusters < 1) {
+            if (attn_decode_smem(m) > 220 * 1024 ||
+                cudaOccupancyMaxActiveClusters(&clusters, attn_decode_kernel, &q) != cudaSuccess || clusters < 1) {
                 cudaGetLastError();
                 m->att_cs = 8;
             }
