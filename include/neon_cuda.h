@@ -216,6 +216,13 @@ NEON_API int neon_cuda_model_generate(neon_model_t m, const int32_t* prompt, siz
 NEON_API int neon_cuda_model_length(neon_model_t m, size_t* length);
 NEON_API int neon_cuda_model_set_length(neon_model_t m, size_t length);
 
+/* fwd::kv_cache_shift (rawllm_forward.hpp:949-969), run_generation's sliding
+ * window (ensure_cache_room, NEON-3.cpp:590-630): positions [keep,
+ * keep+discard) are forgotten, the K rows after them rotated by -discard
+ * positions and both K and V moved down; length shrinks by discard. A no-op
+ * when discard is 0 or the cache holds no more than keep+discard positions. */
+NEON_API int neon_cuda_model_kv_shift(neon_model_t m, size_t keep, size_t discard);
+
 /* Copy the K and V rows of `layer` for positions [0, n) to the host
  * (n x n_kv_head*head_dim floats each). */
 NEON_API int neon_cuda_model_read_kv(neon_model_t m, int layer, size_t n, float* k_host, float* v_host);

@@ -548,6 +548,31 @@ __global__ void swiglu_pairs_kernel(const float* __restrict__ y, float* __restri
     }
 }
 
+// fwd::kv_cache_shift's rotation (rawllm_forward.hpp:949-969): the tail K rows
+// of one layer, rotated by -discard positions (rope_rotate_by_delta, :794-809,
+// with the host's cos/sin of that one angle per pair), into `dst`.
+__global__ void kv_shift_rotate_kernel(const float* __restrict__ src, float* __restrict__ dst, const float2* __restrict__ cs,
+                                       long long tail, int kv_dim, int hd, int rope_half) {
+    const int half = hd / 2;
+    const long long n = tail * (kv_dim / 2);
+    for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < n; idx += (long long)gridDim.x * blockDim.x) {
+        const long long row = idx / (kv_dim / 2);
+        const int pr = (int)(idx - row * (kv_dim / 2));  // pair index within the row
+        const int i = pr % half;
+        const float* s = src + row * kv_dim + 2 * pr;
+        float* d = dst + row * kv_dim + 2 * pr;
+        const float x0 = s[0], x1 = s[1];
+        if (i < rope_half) {
+            const float2 c = cs[i];
+            d[0] = __fmaf_rn(x0, c.x, -__fmul_rn(x1, c.y));
+            d[1] = __fmaf_rn(x0, c.y, __fmul_rn(x1, c.x));
+        } else {
+            d[0] = x0;
+            d[1] = x1;
+        }
+    }
+}
+
 // act[i] = silu(y[i]): the plain SiLU-FFN variant (rawllm_forward.hpp:1189).
 __global__ void silu_kernel(const float* __restrict__ y, float* __restrict__ act, long long n) {
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
@@ -636,6 +661,8 @@ struct neon_model {
     neon_tensor_t head = nullptr;    // lm_head shard (tensor parallel only)
     bool head_from_output = false;   // `head` was cut from output.weight, not the tied embedding
     float* part = nullptr;           // partial sums of the column-split projections
+    float* shift_scratch = nullptr;  // ctx_len x kv_dim, for neon_cuda_model_kv_shift
+    float2* shift_cs = nullptr;      // rope_half (cos, sin) of the shift angle
     int att_cs = 8;                  // CTAs per KV head in the decode attention (a cluster)
     float* logits_full = nullptr;    // all-gathered logits (tensor parallel only)
     neon_tensor_t embd = nullptr, output = nullptr;
@@ -1379,6 +1406,47 @@ int neon_cuda_model_set_length(neon_model_t m, size_t length) {
     if (!m) return error(NEON_ERR_INVALID, "null model");
     if (length > m->cfg.ctx_len) return error(NEON_ERR_INVALID, "length above the KV-cache capacity");
     m->length = length;
+    return NEON_OK;
+}
+
+int neon_cuda_model_kv_shift(neon_model_t m, size_t keep, size_t discard) {
+    if (!m) return error(NEON_ERR_INVALID, "null model");
+    if (discard == 0 || m->length <= keep + discard) return NEON_OK;  // as kv_cache_shift: nothing to slide
+    ModelDevice md(m->device);
+    const auto& c = m->cfg;
+    const size_t kv_dim = m->kv_dim, tail = m->length - keep - discard;
+    if (!m->shift_scratch) {
+        int rc = dev_alloc(m, (void**)&m->shift_scratch, sizeof(float) * (size_t)c.ctx_len * kv_dim);
+        if (!rc) rc = dev_alloc(m, (void**)&m->shift_cs, sizeof(float2) * std::max<size_t>(1, m->rope_half));
+        if (rc) return rc;
+    }
+    // the one angle of the shift, per pair, with the host libm (rope_rotate_by_delta)
+    std::vector<float2> cs(std::max<size_t>(1, m->rope_half));
+    const float fdelta = -(float)discard / c.rope_scale;
+    for (size_t i = 0; i < m->rope_half; ++i) {
+        const float freq = std::pow(c.rope_base, -2.0f * (float)i / (float)c.head_dim);
+        const float theta = fdelta * freq;
+        cs[i] = make_float2(std::cos(theta), std::sin(theta));
+    }
+    DEC_TRY(cudaMemcpyAsync(m->shift_cs, cs.data(), cs.size() * sizeof(float2), cudaMemcpyHostToDevice, m->stream));
+    const size_t row_bytes = kv_dim * sizeof(float);
+    for (uint32_t li = 0; li < c.n_layer; ++li) {
+        float* K = m->K + (size_t)li * c.ctx_len * kv_dim;
+        float* V = m->V + (size_t)li * c.ctx_len * kv_dim;
+        const long long pairs = (long long)tail * (long long)(kv_dim / 2);
+        const int grid = (int)std::min<long long>((pairs + 255) / 256, 4096);
+        kv_shift_rotate_kernel<<<grid, 256, 0, m->stream>>>(K + (keep + discard) * kv_dim, m->shift_scratch, m->shift_cs,
+                                                             (long long)tail, (int)kv_dim, (int)c.head_dim,
+                                                             (int)m->rope_half);
+        int rc = check_launch("kv_shift_rotate_kernel");
+        if (rc) return rc;
+        DEC_TRY(cudaMemcpyAsync(K + keep * kv_dim, m->shift_scratch, tail * row_bytes, cudaMemcpyDeviceToDevice, m->stream));
+        DEC_TRY(cudaMemcpyAsync(m->shift_scratch, V + (keep + discard) * kv_dim, tail * row_bytes, cudaMemcpyDeviceToDevice,
+                                m->stream));
+        DEC_TRY(cudaMemcpyAsync(V + keep * kv_dim, m->shift_scratch, tail * row_bytes, cudaMemcpyDeviceToDevice, m->stream));
+    }
+    DEC_TRY(cudaStreamSynchronize(m->stream));
+    m->length = keep + tail;
     return NEON_OK;
 }
 

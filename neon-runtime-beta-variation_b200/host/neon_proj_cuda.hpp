@@ -245,6 +245,8 @@ public:
     }
     // KVCache::length rewind (run_generation's prefix reuse, NEON-3.cpp:690-703)
     void set_length(size_t n) { check(neon_cuda_model_set_length(m_, n)); }
+    // fwd::kv_cache_shift: ensure_cache_room's slide of the window (NEON-3.cpp:590-630)
+    void kv_shift(size_t keep, size_t discard) { check(neon_cuda_model_kv_shift(m_, keep, discard)); }
     neon_model_t handle() const { return m_; }
 
 private:

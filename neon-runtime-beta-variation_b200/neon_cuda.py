@@ -66,6 +66,7 @@ C_ENTRY_POINTS = (
     "neon_cuda_model_generate",
     "neon_cuda_model_length",
     "neon_cuda_model_set_length",
+    "neon_cuda_model_kv_shift",
     "neon_cuda_model_read_kv",
     "neon_cuda_model_decode_ms",
     "neon_cuda_model_free",
@@ -145,6 +146,7 @@ def load(path: str | None = None) -> C.CDLL:
         L.neon_cuda_model_generate.argtypes = [_vp, _vp, _sz, _sz, C.c_int32, _vp, C.POINTER(_sz)]
         L.neon_cuda_model_length.argtypes = [_vp, C.POINTER(_sz)]
         L.neon_cuda_model_set_length.argtypes = [_vp, _sz]
+        L.neon_cuda_model_kv_shift.argtypes = [_vp, _sz, _sz]
         L.neon_cuda_model_read_kv.argtypes = [_vp, C.c_int, _sz, _vp, _vp]
         L.neon_cuda_model_decode_ms.argtypes = [_vp, C.POINTER(C.c_float)]
         L.neon_cuda_model_free.argtypes = [_vp]
@@ -487,6 +489,10 @@ class Model:
 
     def set_length(self, n: int) -> None:
         _check(load().neon_cuda_model_set_length(self.handle, n))
+
+    def kv_shift(self, keep: int, discard: int) -> None:
+        """fwd::kv_cache_shift: forget positions [keep, keep+discard), slide the rest down."""
+        _check(load().neon_cuda_model_kv_shift(self.handle, int(keep), int(discard)))
 
     def read_kv(self, layer: int, n: int):
         """K and V cache rows [0, n) of `layer` (this rank's KV heads)."""

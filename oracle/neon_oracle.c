@@ -342,6 +342,43 @@ int oracle_model_set(void* p, int role, int layer, const uint8_t* bytes, size_t 
 }
 
 size_t oracle_model_length(void* p) { return ((oracle_model_t*)p)->length; }
+
+/* fwd::kv_cache_shift (rawllm_forward.hpp:949-969): K rows [keep+discard,
+ * length) are rotated by -discard positions (rope_rotate_by_delta, :794-809,
+ * cos/sin from libm, g++'s contraction as in rope_apply), then K and V rows
+ * move down by `discard`; length shrinks by `discard`. */
+void oracle_model_kv_shift(void* p, size_t keep, size_t discard) {
+    oracle_model_t* m = (oracle_model_t*)p;
+    const oracle_config_t* c = &m->cfg;
+    if (discard == 0 || m->length <= keep + discard) return;
+    const size_t hd = c->head_dim, n_kv = c->n_kv_head, kv_dim = n_kv * hd;
+    const size_t rope_half = c->rope_dim_count ? c->rope_dim_count / 2 : hd / 2;
+    const size_t tail = m->length - keep - discard;
+    float* freqs = (float*)malloc(sizeof(float) * (hd / 2 + 1));
+    oracle_rope_freqs(hd, c->rope_base, freqs);
+    const float fdelta = -(float)discard / c->rope_scale;
+    for (size_t li = 0; li < c->n_layer; ++li) {
+        float* K = m->K + li * c->ctx_len * kv_dim;
+        float* V = m->V + li * c->ctx_len * kv_dim;
+        for (size_t t = 0; t < tail; ++t) {
+            float* row = K + (keep + discard + t) * kv_dim;
+            for (size_t h = 0; h < n_kv; ++h) {
+                float* v = row + h * hd;
+                for (size_t i = 0; i < rope_half; ++i) {
+                    float theta = fdelta * freqs[i];
+                    float cs = cosf(theta), sn = sinf(theta);
+                    float x0 = v[2 * i], x1 = v[2 * i + 1];
+                    v[2 * i] = fmaf(x0, cs, -(x1 * sn));
+                    v[2 * i + 1] = fmaf(x0, sn, x1 * cs);
+                }
+            }
+        }
+        memmove(K + keep * kv_dim, K + (keep + discard) * kv_dim, tail * kv_dim * sizeof(float));
+        memmove(V + keep * kv_dim, V + (keep + discard) * kv_dim, tail * kv_dim * sizeof(float));
+    }
+    m->length = keep + tail;
+    free(freqs);
+}
 void oracle_model_set_length(void* p, size_t n) { ((oracle_model_t*)p)->length = n; }
 
 static const oracle_tensor_t* L_(const oracle_model_t* m, uint32_t li, int role) {

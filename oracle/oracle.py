@@ -234,6 +234,8 @@ class Model:
             L.oracle_model_length.restype = _sz
             L.oracle_model_set_length.argtypes = [C.c_void_p, _sz]
             L.oracle_model_kv.argtypes = [C.c_void_p, C.c_int, _sz, _f32p, _f32p]
+            L.oracle_model_kv_shift.argtypes = [C.c_void_p, _sz, _sz]
+            self._shift = L.oracle_model_kv_shift
             self.L, self.pool = L, None
             self._new, self._free, self._set = L.oracle_model_new, L.oracle_model_free, L.oracle_model_set
             self._len, self._setlen, self._kv = L.oracle_model_length, L.oracle_model_set_length, L.oracle_model_kv
@@ -251,6 +253,8 @@ class Model:
             L.ref_model_length.restype = _sz
             L.ref_model_set_length.argtypes = [C.c_void_p, _sz]
             L.ref_model_kv.argtypes = [C.c_void_p, C.c_int, _sz, _f32p, _f32p]
+            L.ref_model_kv_shift.argtypes = [C.c_void_p, _sz, _sz]
+            self._shift = L.ref_model_kv_shift
             self.L = L
             self.pool = RefPool(threads or os.cpu_count() or 1)
             self._new, self._free, self._set = L.ref_model_new, L.ref_model_free, L.ref_model_set
@@ -279,6 +283,10 @@ class Model:
 
     def set_length(self, n):
         self._setlen(self.h, n)
+
+    def kv_shift(self, keep, discard):
+        """fwd::kv_cache_shift: forget positions [keep, keep+discard)."""
+        self._shift(self.h, keep, discard)
 
     def kv(self, layer, n):
         k = np.zeros((n, self.cfg.kv_dim), np.float32)

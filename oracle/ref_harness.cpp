@@ -239,6 +239,16 @@ int ref_model_forward(void* p, void* pool, const int32_t* tokens, size_t n, floa
 size_t ref_model_length(void* p) { return static_cast<RefModel*>(p)->cache.length; }
 void ref_model_set_length(void* p, size_t len) { static_cast<RefModel*>(p)->cache.length = len; }
 
+// fwd::kv_cache_shift (rawllm_forward.hpp:949-969) on the model's cache, with
+// the freqs ensure_cache_room builds (NEON-3.cpp:618-624).
+void ref_model_kv_shift(void* p, size_t keep, size_t discard) {
+    auto* m = static_cast<RefModel*>(p);
+    const auto& c = m->cfg;
+    const std::vector<float> freqs = fwd::rope_make_freqs(c.head_dim, c.rope_base);
+    const size_t rope_half = c.rope_dim_count ? c.rope_dim_count / 2 : c.head_dim / 2;
+    fwd::kv_cache_shift(m->cache, keep, discard, c.n_kv_head, c.head_dim, rope_half, c.rope_scale, freqs.data());
+}
+
 // K/V cache rows of one layer (kv_dim floats each) for positions [0, n).
 void ref_model_kv(void* p, int layer, size_t n, float* k, float* v) {
     auto* m = static_cast<RefModel*>(p);

@@ -107,3 +107,35 @@ def test_greedy_matches_reference(cfg, n_prompt, steps):
         errs.append(rel_l2(m2.forward([t]), ref_logits[i + 1]))
     print(f"{cfg.name}: min top-2 margin {margin:.3g}, logits rel-L2 max {max(errs):.2e}")
     assert max(errs) <= MODEL_L2_RTOL
+
+
+def test_kv_cache_shift_matches_reference():
+    """neon_cuda_model_kv_shift (fwd::kv_cache_shift): V rows move bit for bit,
+    the kept K rows stay, the slid K rows equal the reference's (same rotation
+    on K that already differs by fp32 summation order: the per-element bar), and
+    generation continues with the reference's greedy tokens."""
+    cfg = TINY.with_(rope_dim_count=48, ctx_len=80)
+    tensors = list(S.model_tensors(cfg, seed=7))
+    prompt = S.prompt_tokens(40, cfg.n_vocab, 8)
+    kind = "reference" if O.ref_available() else "port"
+    ref = O.Model(cfg, tensors, kind)
+    ref.forward(prompt)
+    ref.kv_shift(4, 13)
+    m = N.Model(cfg, tensors)
+    m.forward(prompt)
+    pre = [m.read_kv(layer, 40) for layer in range(cfg.n_layer)]
+    m.kv_shift(4, 0)  # no-op
+    m.kv_shift(4, 13)
+    assert m.length == ref.length == 27
+    for layer in range(cfg.n_layer):
+        k0, v0 = pre[layer]
+        k1, v1 = m.read_kv(layer, m.length)
+        k2, _ = ref.kv(layer, ref.length)
+        assert np.array_equal(v1[:4], v0[:4]) and np.array_equal(v1[4:], v0[17:]), f"layer {layer} V"
+        assert np.array_equal(k1[:4], k0[:4]), f"layer {layer} kept K"
+        assert max_rel_err(k1, k2) <= MATVEC_RTOL, f"layer {layer} slid K"
+    nxt = np.array([5], np.int32)
+    ref_toks, _ = ref.generate_greedy(nxt, 12)
+    ref.close()
+    toks = m.generate(nxt, 12)
+    assert np.array_equal(toks, ref_toks)

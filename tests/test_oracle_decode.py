@@ -126,3 +126,27 @@ def test_summation_order_sensitivity_of_the_reference_algorithm():
     assert worst > 1e-2, "expected at least one quantisation flip among 60 positions"
     assert max(rel_l2(y, r) for y, r in zip(lb, la)) <= MODEL_L2_RTOL
     assert all(int(np.argmax(y)) == int(np.argmax(r)) for y, r in zip(lb, la))
+
+
+@ref_only
+def test_kv_cache_shift_matches_reference():
+    """fwd::kv_cache_shift (rawllm_forward.hpp:949-969) restated in the oracle:
+    rotated K, moved V, and the next forward, bit for bit."""
+    cfg = TINY.with_(rope_dim_count=48)  # rotation on part of the head too
+    tensors = list(S.model_tensors(cfg, seed=7))
+    a, b = O.Model(cfg, tensors, "port"), O.Model(cfg, tensors, "reference", threads=2)
+    p = S.prompt_tokens(40, cfg.n_vocab, 8)
+    a.forward(p)
+    b.forward(p)
+    a.kv_shift(4, 0)  # no-ops, as the reference's
+    a.kv_shift(30, 20)
+    assert a.length == 40
+    a.kv_shift(4, 13)
+    b.kv_shift(4, 13)
+    assert a.length == b.length == 27
+    for layer in range(cfg.n_layer):
+        k1, v1 = a.kv(layer, a.length)
+        k2, v2 = b.kv(layer, b.length)
+        assert np.array_equal(bits(k1), bits(k2)) and np.array_equal(bits(v1), bits(v2))
+    la, lb = a.forward(np.array([5], np.int32)), b.forward(np.array([5], np.int32))
+    assert np.array_equal(bits(la), bits(lb))
