@@ -58,7 +58,15 @@ WORKLOADS = {
     "q8_0_4096x14336": (S.GGML_Q8_0, 4096, 14336),
     "q4_0_28672x8192": (S.GGML_Q4_0, 28672, 8192),
     "q4_0_8192x28672": (S.GGML_Q4_0, 8192, 28672),
+    # the other weight types (dequantising kernel)
+    **{f"{S.TYPE_NAMES[t].lower()}_4096x4096": (t, 4096, 4096)
+       for t in (S.GGML_Q4_1, S.GGML_Q5_0, S.GGML_Q5_1, S.GGML_Q4_K, S.GGML_Q5_K, S.GGML_Q6_K,
+                 S.GGML_F16, S.GGML_BF16, S.GGML_F32)},
+    "q4_k_14336x4096": (S.GGML_Q4_K, 14336, 4096),
+    "q6_k_4096x14336": (S.GGML_Q6_K, 4096, 14336),
 }
+# --type-sweep: every weight type at the decode shape, plus two FFN shapes
+TYPE_SWEEP = ["q4_0_4096x4096", "q8_0_4096x4096"] + [k for k in WORKLOADS if not k.startswith(("q4_0", "q8_0"))]
 TYPE, ROWS, COLS = WORKLOADS["q4_0_4096x4096"]
 ROTATION = 48
 METRIC = "Q4_0 matvec HBM GB/s vs peak"
@@ -75,17 +83,37 @@ DECODE_METRIC = "batch-1 decode tokens/s"
 
 
 def select_workload(name):
-    global TYPE, ROWS, COLS, ROTATION, METRIC, TYPE_NAME
+    global TYPE, ROWS, COLS, ROTATION, METRIC, TYPE_NAME, KERNEL
     if name in DECODE_WORKLOADS:
         return
     TYPE, ROWS, COLS = WORKLOADS[name]
-    TYPE_NAME = "Q4_0" if TYPE == S.GGML_Q4_0 else "Q8_0"
+    TYPE_NAME = S.TYPE_NAMES[TYPE]
+    KERNEL = "matvec_stream_kernel" if TYPE in (S.GGML_Q4_0, S.GGML_Q8_0) else "matvec_dq_kernel"
     METRIC = f"{TYPE_NAME} matvec HBM GB/s vs peak"
     ROTATION = max(2, int(-(-ROTATION_BYTES // (ROWS * S.row_bytes(TYPE, COLS)))))
 
 
 def profile_summary_path():
-    return os.path.join(ROOT, "profiles", f"matvec_stream_{TYPE_NAME.lower()}_{ROWS}x{COLS}.txt")
+    kind = "stream" if KERNEL == "matvec_stream_kernel" else "dq"
+    return os.path.join(ROOT, "profiles", f"matvec_{kind}_{TYPE_NAME.lower()}_{ROWS}x{COLS}.txt")
+
+
+def weight_distribution(t):
+    if t == S.GGML_Q4_0:
+        return "fp16 d=|N(0,1)|*0.02, nibbles U(0..15)"
+    if t == S.GGML_Q8_0:
+        return "fp16 d=|N(0,1)|*0.01, int8 U(-127..127)"
+    if t in (S.GGML_F32, S.GGML_F16, S.GGML_BF16):
+        return "values N(0,1)*0.02"
+    return "fp16 scales |N(0,1)|*s, quant bytes U(0..255)"
+
+
+def compute_dtype(t):
+    if t == S.GGML_Q4_0:
+        return "int8/fp32 (q4_0 x q8_0 dp4a, fp32 scales)"
+    if t == S.GGML_Q8_0:
+        return "fp32 (q8_0 int8 weights x fp32 x, fp32 accumulate)"
+    return f"fp32 ({S.TYPE_NAMES[t].lower()} weights decoded exactly x fp32 x, fp32 accumulate)"
 
 
 def parse_args():
@@ -105,6 +133,8 @@ def parse_args():
     p.add_argument("--layers", type=int, default=None,
                    help="decode workloads: fewer layers (kernel shapes unchanged; for profiling)")
     p.add_argument("--no-decode", action="store_true", help="matvec workloads: skip the decode sub-measurements")
+    p.add_argument("--type-sweep", action="store_true",
+                   help="time the matvec of every weight type (one JSON line each) instead of the headline")
     p.add_argument("--no-large-decode", action="store_true",
                    help="matvec workloads: skip the Llama-3-70B-shaped split decode sub-measurement")
     args = p.parse_args()
@@ -115,8 +145,7 @@ def parse_args():
 
 
 def workload_config():
-    dist = ("fp16 d=|N(0,1)|*0.02, nibbles U(0..15)" if TYPE == S.GGML_Q4_0
-            else "fp16 d=|N(0,1)|*0.01, int8 U(-127..127)")
+    dist = weight_distribution(TYPE)
     return {
         "workload": f"{TYPE_NAME} x fp32 matvec, W {ROWS}x{COLS}, batch 1 ({dist}, x N(0,1), seeded)",
         "rows": ROWS, "cols": COLS, "batch": 1,
@@ -640,8 +669,7 @@ def run_neon(args):
             "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": K,
             "warmup": W, "ms_per_step": round(ms / K, 5), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None,
-            "dtype": ("int8/fp32 (q4_0 x q8_0 dp4a, fp32 scales)" if TYPE == S.GGML_Q4_0
-                      else "fp32 (q8_0 int8 weights x fp32 x, fp32 accumulate)"),
+            "dtype": compute_dtype(TYPE),
             "data": "synthetic",
             "config": {**workload_config(), "parallelism": f"dp{world} (independent rotations)",
                        "launch": "CUDA graph of 1024 PDL launches per step"},
@@ -668,9 +696,61 @@ def run_neon(args):
         dist.destroy_process_group()
 
 
+def run_type_sweep(args):
+    """One JSON line per weight type: device GB/s of a CUDA graph of 1024
+    one-position launches over a rotation of tensors larger than L2, timed
+    with CUDA events (the headline's method), and the fraction of the HBM peak."""
+    import torch
+
+    import neon_cuda as N
+
+    torch.cuda.set_device(0)
+    N.init(0)
+    dev = torch.device("cuda", 0)
+    peak, peak_kind = measured_peak()
+    stream = torch.cuda.Stream(device=dev)
+    K, W = args.steps, max(3, args.warmup)
+    for name in TYPE_SWEEP:
+        select_workload(name)
+        tensors = [N.DeviceTensor(w, TYPE, ROWS, COLS) for w in host_rotation(0, ROTATION)]
+        dx = torch.from_numpy(S.activations(1, COLS, seed=7)).to(dev)
+        ys = torch.zeros((ROTATION, ROWS), device=dev)
+        with torch.cuda.stream(stream):
+            tensors[0].matvec(dx, ys[0], stream=stream)
+        stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for j in range(CALLS_PER_STEP):
+                tensors[j % ROTATION].matvec(dx, ys[j % ROTATION], stream=stream)
+        with torch.cuda.stream(stream):
+            for _ in range(W):
+                graph.replay()
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            for _ in range(K):
+                graph.replay()
+            end.record(stream)
+        torch.cuda.synchronize()
+        ms = start.elapsed_time(end)
+        bytes_call = S.algorithmic_bytes(TYPE, ROWS, COLS)
+        gbs = K * CALLS_PER_STEP * bytes_call / (ms / 1e3) / 1e9
+        print(json.dumps({"workload": name, "type": TYPE_NAME, "kernel": KERNEL, "rows": ROWS, "cols": COLS,
+                          "value": round(gbs, 1), "unit": UNIT, "frac": round(gbs / peak, 4),
+                          "peak": peak, "peak_source": peak_kind, "us_per_call": round(ms * 1e3 / (K * CALLS_PER_STEP), 3),
+                          "bytes_per_call": bytes_call, "rotation_tensors": ROTATION, "steps": K, "warmup": W}),
+              flush=True)
+        del graph, tensors
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+
+
 def main():
     args = parse_args()
-    if args.impl == "reference":
+    if args.type_sweep and args.impl != "reference":
+        run_type_sweep(args)
+    elif args.impl == "reference":
         run_reference(args)
     elif args.workload in DECODE_WORKLOADS:
         run_decode(args)

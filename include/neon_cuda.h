@@ -48,17 +48,28 @@ extern "C" {
 #define NEON_ERR_CUDA (-3)        /* a CUDA runtime call failed */
 #define NEON_ERR_NOMEM (-4)       /* device allocation failed */
 
-/* GGML tensor types, values of loader::GGMLType (rawllm_loader.hpp:23-32).
- * This backend runs Q4_0 and Q8_0; other values return NEON_ERR_UNSUPPORTED. */
+/* GGML tensor types, values of loader::GGMLType (rawllm_loader.hpp:23-32):
+ * the eleven that fwd::dequantize_row decodes (rawllm_forward.hpp:301-321).
+ * Q4_0 and Q8_0 run the streaming integer / fp32 kernels; the others run the
+ * dequantising kernel. Q8_1, Q2_K, Q3_K and IQ4_NL, which the reference does
+ * not dequantise either, return NEON_ERR_UNSUPPORTED. */
 #define NEON_GGML_F32 0
 #define NEON_GGML_F16 1
 #define NEON_GGML_Q4_0 2
+#define NEON_GGML_Q4_1 3
+#define NEON_GGML_Q5_0 6
+#define NEON_GGML_Q5_1 7
 #define NEON_GGML_Q8_0 8
+#define NEON_GGML_Q4_K 12
+#define NEON_GGML_Q5_K 13
+#define NEON_GGML_Q6_K 14
+#define NEON_GGML_BF16 30
 
 /* Shard modes of neon_cuda_upload for tensor parallelism. */
 #define NEON_SHARD_NONE 0 /* whole tensor */
 #define NEON_SHARD_ROWS 1 /* rows [i*rows/n, (i+1)*rows/n): output-dim split */
-#define NEON_SHARD_COLS 2 /* 32-blocks [i*nb/n, (i+1)*nb/n) of every row: input-dim split */
+#define NEON_SHARD_COLS 2 /* blocks [i*nb/n, (i+1)*nb/n) of every row: input-dim split (32-value
+                             blocks; 256-value super-blocks for Q4_K/Q5_K/Q6_K) */
 
 /* Opaque handle of a device-resident weight tensor. */
 typedef struct neon_tensor* neon_tensor_t;
@@ -88,7 +99,11 @@ NEON_API int neon_cuda_init(int device);
 
 /* Copy one GGUF tensor (rows x cols, `rows` rows of bytes_for_type(type, cols)
  * bytes, the layout TensorInfo::data_ptr points at, rawllm_loader.hpp:170-176)
- * into HBM on the current device, repacked into the coalesced device layout.
+ * into HBM on the current device, repacked into the coalesced device layout
+ * (Q4_0 / Q8_0: payload and scale planes; other types: the GGUF rows at a
+ * 16-byte pitch). `cols` must be a multiple of the type's block size (32, or
+ * 256 for the K-quants; any cols for F32/F16/BF16), as proj_all_positions
+ * requires (rawllm_forward.hpp:528-533).
  * With a shard mode, only shard `shard_index` of `shard_count` is kept.
  * Replaces the per-call host->device weight copy of matvec_rocblas
  * (rawllm_rocm.hpp:346-367): here weights move once, at load time. */
@@ -112,7 +127,8 @@ NEON_API int neon_cuda_quantize_q8_0(const float* dX, size_t x_stride, size_t co
 /* Y[t*y_stride + r] = W_r . X_t for r < rows, t < seq, on device buffers.
  * The device counterpart of fwd::proj_all_positions (rawllm_forward.hpp:522-609):
  * Q4_0 weights use the fused Q4_0 x Q8_0 integer dot against X quantised to
- * Q8_0 (bit-exact activations); Q8_0 weights multiply fp32 X. */
+ * Q8_0 (bit-exact activations); every other type is decoded (bit-exact values,
+ * dequantize_row) and multiplied with fp32 X. */
 NEON_API int neon_cuda_matvec(neon_tensor_t W, const float* dX, size_t x_stride, float* dY,
                      size_t y_stride, size_t seq, void* stream);
 

@@ -3,6 +3,7 @@
 #include "neon_cuda.h"
 #include "neon_internal.h"
 #include "neon_kernels.cuh"
+#include "neon_dequant.cuh"
 
 #include <cuda_runtime.h>
 
@@ -74,7 +75,34 @@ int cuda_err(cudaError_t e, const char* what) {
 
 size_t payload_bytes(int type) { return type == NEON_GGML_Q4_0 ? 16 : 32; }
 size_t gguf_block_bytes(int type) { return type == NEON_GGML_Q4_0 ? 18 : 34; }
-bool supported_type(int type) { return type == NEON_GGML_Q4_0 || type == NEON_GGML_Q8_0; }
+bool split_type(int type) { return type == NEON_GGML_Q4_0 || type == NEON_GGML_Q8_0; }
+// The types of the dequantising kernel (padded-row layout).
+bool dq_type(int type) {
+    int be, bb, cb;
+    dq_geometry(type, &be, &bb, &cb);
+    return be != 0;
+}
+bool supported_type(int type) { return split_type(type) || dq_type(type); }
+
+// Values per GGUF block (block_size_for, rawllm_forward.hpp:289-299) and
+// bytes per GGUF row (nbytes_for, rawllm_loader.hpp:367-386); 0 if unsupported.
+size_t block_elems_of(int type) {
+    if (split_type(type)) return 32;
+    if (type == NEON_GGML_F32 || type == NEON_GGML_F16 || type == NEON_GGML_BF16) return 1;
+    int be, bb, cb;
+    dq_geometry(type, &be, &bb, &cb);
+    return (size_t)be;
+}
+size_t row_bytes_of(int type, size_t cols) {
+    const size_t be = block_elems_of(type);
+    if (be == 0 || cols % be != 0) return 0;
+    if (split_type(type)) return cols / 32 * gguf_block_bytes(type);
+    if (type == NEON_GGML_F32) return cols * 4;
+    if (type == NEON_GGML_F16 || type == NEON_GGML_BF16) return cols * 2;
+    int e, bb, cb;
+    dq_geometry(type, &e, &bb, &cb);
+    return cols / be * (size_t)bb;
+}
 
 // Runs `fn` with `device` current, restoring the caller's device afterwards.
 struct DeviceGuard {
@@ -92,6 +120,10 @@ struct DeviceGuard {
 
 using StreamKernel = void (*)(StreamArgs);
 StreamKernel stream_kernel(int type, int rc);
+using DqKernel = void (*)(DqArgs);
+DqKernel dq_kernel(int type, int T);
+constexpr int kDqTypes[] = {NEON_GGML_F32, NEON_GGML_F16, NEON_GGML_BF16, NEON_GGML_Q4_1, NEON_GGML_Q5_0,
+                            NEON_GGML_Q5_1, NEON_GGML_Q4_K, NEON_GGML_Q5_K, NEON_GGML_Q6_K};
 
 template <typename Kern>
 int ensure_smem(Kern k, int bytes) {
@@ -122,6 +154,8 @@ int init_device(int device) {
     int rc = NEON_OK;
     for (int t : {NEON_GGML_Q4_0, NEON_GGML_Q8_0})
         for (int r : {2, 4, 8, 16, 32}) rc = rc ? rc : ensure_smem(stream_kernel(t, r), kMaxSmem);
+    for (int t : kDqTypes)
+        for (int T : {1, 2, 4}) rc = rc ? rc : ensure_smem(dq_kernel(t, T), kMaxSmem);
     if (rc) return rc;
     void* err = nullptr;
     NEON_CUDA_TRY(cudaGetSymbolAddress(&err, g_neon_device_err));
@@ -315,6 +349,114 @@ int launch_stream(const std::vector<const neon_proj_target_t*>& t, int type, int
     return NEON_OK;
 }
 
+// The dequantising kernel instantiation for (type, positions per CTA).
+DqKernel dq_kernel(int type, int T) {
+#define NEON_DQ_CASE(TY)                                               \
+    case TY:                                                           \
+        return T >= 4 ? matvec_dq_kernel<TY, 4>                        \
+                      : (T == 2 ? matvec_dq_kernel<TY, 2> : matvec_dq_kernel<TY, 1>);
+    switch (type) {
+        NEON_DQ_CASE(NEON_GGML_F32)
+        NEON_DQ_CASE(NEON_GGML_F16)
+        NEON_DQ_CASE(NEON_GGML_BF16)
+        NEON_DQ_CASE(NEON_GGML_Q4_1)
+        NEON_DQ_CASE(NEON_GGML_Q5_0)
+        NEON_DQ_CASE(NEON_GGML_Q5_1)
+        NEON_DQ_CASE(NEON_GGML_Q4_K)
+        NEON_DQ_CASE(NEON_GGML_Q5_K)
+        NEON_DQ_CASE(NEON_GGML_Q6_K)
+        default: return nullptr;
+    }
+#undef NEON_DQ_CASE
+}
+
+int dq_occupancy(int type, int T, int smem) {
+    static std::mutex mu;
+    static std::vector<std::pair<long long, int>> cache;
+    const long long key = ((long long)type << 40) | ((long long)T << 32) | (unsigned)smem;
+    std::lock_guard<std::mutex> lk(mu);
+    for (auto& kv : cache)
+        if (kv.first == key) return kv.second;
+    int occ = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, dq_kernel(type, T), kThreads, smem) != cudaSuccess)
+        occ = 1;
+    occ = std::max(1, occ);
+    cache.emplace_back(key, occ);
+    return occ;
+}
+
+// One launch group of a dequantising type: tiles of 8 rows, T positions per
+// CTA (grid.y over the positions), X of those positions in shared memory.
+int launch_dq(const std::vector<const neon_proj_target_t*>& t, int type, size_t cols, const float* dX,
+              size_t x_stride, size_t seq, cudaStream_t st, DeviceState& ds, int accumulate,
+              const neon_proj_target_t* base, const neon_internal::MatvecExt* ext) {
+    int be, bb, cb;
+    dq_geometry(type, &be, &bb, &cb);
+    const int nu = (int)((cols + 31) / 32);
+    const int nblk = nu / (be / 32);
+    const int chunk = cb * bb;
+    int T = 1;
+    if (seq >= 4 && dq_x_bytes(4, nu) + kWarps * chunk <= kMaxSmem) T = 4;
+    else if (seq >= 2 && dq_x_bytes(2, nu) + kWarps * chunk <= kMaxSmem) T = 2;
+    const int smem = dq_x_bytes(T, nu) + kWarps * chunk;
+    if (smem > kMaxSmem)
+        return set_err(NEON_ERR_UNSUPPORTED, "input dim " + std::to_string(cols) +
+                                                 " is too large for the dequantising kernel's shared memory");
+    if ((seq + T - 1) / T > 65535) return set_err(NEON_ERR_UNSUPPORTED, "too many positions in one call");
+    size_t start = 0;
+    while (start < t.size()) {
+        DqArgs a;
+        std::memset(&a, 0, sizeof(a));
+        size_t n = std::min(t.size() - start, (size_t)kMaxSpans);
+        int tiles = 0;
+        for (size_t i = 0; i < n; ++i) {
+            const neon_proj_target_t* tg = t[start + i];
+            Span& sp = a.s.span[i];
+            sp.qs = tg->W->qs;
+            sp.d = nullptr;
+            sp.y = tg->Y;
+            sp.y_stride = (long long)tg->y_stride;
+            sp.rows = (int)tg->W->rows;
+            sp.tile0 = tiles;
+            tiles += (int)((tg->W->rows + kWarps - 1) / kWarps);
+            if (ext && ext->epi) {
+                const size_t k = (size_t)(tg - base);
+                sp.epi = ext->epi[k];
+                sp.pos_stride = ext->pos_stride ? ext->pos_stride[k] : 0;
+            }
+            if (ext && ext->peer_mode == 1) sp.epi = kEpiPeer;
+        }
+        a.s.x = dX;
+        a.s.err = ds.err;
+        a.s.n_spans = (int)n;
+        a.s.n_tiles = tiles;
+        a.s.accumulate = accumulate;
+        if (ext) {
+            a.s.norm_w = ext->norm_w;
+            a.s.norm_eps = ext->norm_eps;
+            a.s.d_pos = ext->d_pos;
+            a.s.rope_cs = ext->rope_cs;
+            a.s.rope_half = ext->rope_half;
+            a.s.head_dim = ext->head_dim;
+            a.s.peer_mode = ext->peer_mode;
+            if (ext->peer_mode) a.s.peer = ext->peer;
+        }
+        a.pitch = (long long)t[start]->W->pitch;
+        a.x_stride = (long long)x_stride;
+        a.cols = (int)cols;
+        a.nu = nu;
+        a.nblk = nblk;
+        a.nch = (nblk + cb - 1) / cb;
+        a.seq = (int)seq;
+        const int occ = dq_occupancy(type, T, smem);
+        const int grid = std::min(tiles, ds.sms * occ);
+        int rc = launch_n(dq_kernel(type, T), dim3(grid, (unsigned)((seq + T - 1) / T)), kThreads, smem, st, a);
+        if (rc) return rc;
+        start += n;
+    }
+    return NEON_OK;
+}
+
 // Reads (and clears) the device error word after the stream has drained.
 int check_device_err(int device) {
     if (device < 0 || device >= kMaxDevices || !g_dev[device].ready) return NEON_OK;
@@ -374,6 +516,10 @@ struct Group {
 int launch_group(const Group& g, const float* dX, size_t x_stride, size_t seq, cudaStream_t st,
                  DeviceState& ds, int accumulate, const neon_proj_target_t* base,
                  const neon_internal::MatvecExt* ext) {
+    if (dq_type(g.type)) {
+        if (seq > 1 && ext) return set_err(NEON_ERR_UNSUPPORTED, "fused norm / epilogues need one position");
+        return launch_dq(g.t, g.type, g.cols, dX, x_stride, seq, st, ds, accumulate, base, ext);
+    }
     const int nb = (int)(g.cols / 32);
     const bool q4 = g.type == NEON_GGML_Q4_0;
     if (seq == 1) return launch_stream(g.t, g.type, nb, dX, st, ds, accumulate, base, ext);
@@ -499,6 +645,28 @@ int matvec(const neon_proj_target_t* targets, size_t n, const float* dX, size_t 
     return matvec_targets(targets, n, dX, x_stride, seq, (void*)st, accumulate, ext);
 }
 int error(int code, const std::string& msg) { return set_err(code, msg); }
+size_t gguf_row_bytes(int type, size_t cols) { return row_bytes_of(type, cols); }
+int embed_rows(const neon_tensor* E, const int* toks, int seq, int n_embd, int n_vocab, float* h, unsigned int* err,
+               cudaStream_t st) {
+    using EmbedKernel = void (*)(const unsigned char*, long long, int, const int*, int, float*, unsigned int*);
+    EmbedKernel k = nullptr;
+    switch (E->type) {
+        case NEON_GGML_F32: k = embed_dq_kernel<NEON_GGML_F32>; break;
+        case NEON_GGML_F16: k = embed_dq_kernel<NEON_GGML_F16>; break;
+        case NEON_GGML_BF16: k = embed_dq_kernel<NEON_GGML_BF16>; break;
+        case NEON_GGML_Q4_1: k = embed_dq_kernel<NEON_GGML_Q4_1>; break;
+        case NEON_GGML_Q5_0: k = embed_dq_kernel<NEON_GGML_Q5_0>; break;
+        case NEON_GGML_Q5_1: k = embed_dq_kernel<NEON_GGML_Q5_1>; break;
+        case NEON_GGML_Q4_K: k = embed_dq_kernel<NEON_GGML_Q4_K>; break;
+        case NEON_GGML_Q5_K: k = embed_dq_kernel<NEON_GGML_Q5_K>; break;
+        case NEON_GGML_Q6_K: k = embed_dq_kernel<NEON_GGML_Q6_K>; break;
+        default: return set_err(NEON_ERR_UNSUPPORTED, "embedding type not supported");
+    }
+    const int nu = (n_embd + 31) / 32;
+    return launch_n(k, dim3((nu + 127) / 128, seq), 128, 0, st, (const unsigned char*)E->qs, (long long)E->pitch,
+                    n_embd, toks, n_vocab, h, err);
+}
+size_t gguf_block_elems(int type) { return block_elems_of(type); }
 int cuda_error(cudaError_t e, const char* what) { return cuda_err(e, what); }
 int launched(int n) {
     g_launches.fetch_add((uint64_t)n, std::memory_order_relaxed);
@@ -544,6 +712,80 @@ int neon_cuda_set_pdl(int enabled) {
 
 uint64_t neon_cuda_launch_count(void) { return g_launches.load(); }
 
+}  // extern "C"
+
+namespace {
+// Upload of a dequantising type: the GGUF rows (or the kept shard of them)
+// copied unchanged into rows of a 16-byte pitch, the padding zeroed. One 2-D
+// copy straight from the caller's bytes; no repack kernel.
+int upload_rows(const uint8_t* host_bytes, int type, size_t rows, size_t cols, int shard_mode, int shard_index,
+                int shard_count, neon_tensor_t* out) {
+    int be, bb, cb;
+    dq_geometry(type, &be, &bb, &cb);
+    const size_t src_row = row_bytes_of(type, cols);
+    const size_t nu = (cols + 31) / 32;
+    const size_t nblk = nu / (size_t)(be / 32);
+    if (rows > (size_t)INT32_MAX / 2 || nu > (size_t)INT32_MAX / 64) return set_err(NEON_ERR_INVALID, "tensor too large");
+    size_t r0 = 0, r1 = rows, b0 = 0, b1 = nblk;
+    if (shard_mode != NEON_SHARD_NONE) {
+        if (shard_count <= 0 || shard_index < 0 || shard_index >= shard_count)
+            return set_err(NEON_ERR_INVALID, "bad shard index/count");
+        if (shard_mode == NEON_SHARD_ROWS) {
+            r0 = rows * (size_t)shard_index / (size_t)shard_count;
+            r1 = rows * (size_t)(shard_index + 1) / (size_t)shard_count;
+        } else if (shard_mode == NEON_SHARD_COLS) {
+            if (cols % (size_t)be != 0)
+                return set_err(NEON_ERR_UNSUPPORTED, "column split of a float tensor whose rows are not whole 32-value blocks");
+            b0 = nblk * (size_t)shard_index / (size_t)shard_count;
+            b1 = nblk * (size_t)(shard_index + 1) / (size_t)shard_count;
+        } else {
+            return set_err(NEON_ERR_INVALID, "unknown shard mode");
+        }
+        if (r1 <= r0 || b1 <= b0) return set_err(NEON_ERR_INVALID, "empty shard");
+    }
+    int device = 0;
+    int rc = current_device(&device);
+    if (rc) return rc;
+    const bool col_split = shard_mode == NEON_SHARD_COLS;
+    const size_t lrows = r1 - r0, lnb = b1 - b0;
+    const size_t lcols = col_split ? lnb * (size_t)be : cols;
+    const size_t pitch = (lnb * (size_t)bb + 15) & ~(size_t)15;
+    const size_t width = col_split ? lnb * (size_t)bb : src_row;
+    const size_t total = lrows * pitch;
+
+    neon_tensor* t = new neon_tensor();
+    t->device = device;
+    t->type = type;
+    t->rows = lrows;
+    t->cols = lcols;
+    t->nb = (lcols + 31) / 32;
+    t->bytes = total;
+    t->pitch = pitch;
+    cudaError_t e = cudaMalloc(&t->base, total);
+    if (e != cudaSuccess) {
+        delete t;
+        return set_err(NEON_ERR_NOMEM, std::string("cudaMalloc of weights failed: ") + cudaGetErrorString(e));
+    }
+    t->qs = t->base;
+    t->d = nullptr;
+    cudaStream_t st = g_dev[device].stream;
+    e = cudaMemsetAsync(t->base, 0, total, st);
+    if (e == cudaSuccess)
+        e = cudaMemcpy2DAsync(t->base, pitch, host_bytes + r0 * src_row + b0 * (size_t)bb, src_row, width, lrows,
+                              cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) {
+        cudaFree(t->base);
+        delete t;
+        return cuda_err(e, "weight upload");
+    }
+    *out = t;
+    return NEON_OK;
+}
+}  // namespace
+
+extern "C" {
+
 int neon_cuda_upload(const uint8_t* host_bytes, int ggml_type, size_t rows, size_t cols, int shard_mode,
                      int shard_index, int shard_count, neon_tensor_t* out) {
     if (!out) return set_err(NEON_ERR_INVALID, "null output handle");
@@ -553,9 +795,12 @@ int neon_cuda_upload(const uint8_t* host_bytes, int ggml_type, size_t rows, size
         return set_err(NEON_ERR_UNSUPPORTED, "quant type " + std::to_string(ggml_type) +
                                                  " is not supported by the CUDA backend (Q4_0 and Q8_0 are)");
     if (rows == 0 || cols == 0) return set_err(NEON_ERR_INVALID, "empty tensor");
-    if (cols % 32 != 0)
+    const size_t bs = block_elems_of(ggml_type);
+    if (cols % bs != 0)
         return set_err(NEON_ERR_INVALID, "forward(): input dim (" + std::to_string(cols) +
-                                             ") isn't a multiple of its quant block size (32) -- can't dequantize safely.");
+                                             ") isn't a multiple of its quant block size (" + std::to_string(bs) +
+                                             ") -- can't dequantize safely.");
+    if (dq_type(ggml_type)) return upload_rows(host_bytes, ggml_type, rows, cols, shard_mode, shard_index, shard_count, out);
     if (rows > (size_t)INT32_MAX / 2 || cols / 32 > (size_t)INT32_MAX / 64)
         return set_err(NEON_ERR_INVALID, "tensor too large");
     size_t nb = cols / 32;

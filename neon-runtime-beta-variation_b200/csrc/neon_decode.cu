@@ -775,6 +775,18 @@ int launch_k(const char* what, void (*kern)(KArgs...), dim3 grid, int threads, s
     return neon_internal::launched(1);
 }
 
+// h = the embedding rows of `seq` tokens (device ids): the split-layout
+// kernel for Q4_0 / Q8_0, the library's decoder for the other types.
+int launch_embed(neon_model* m, const int* toks, int seq) {
+    const auto& c = m->cfg;
+    const neon_tensor_t E = m->embd;
+    if (E->pitch)
+        return neon_internal::embed_rows(E, toks, seq, (int)c.n_embd, (int)c.n_vocab, m->h, m->d_err, m->stream);
+    const int nb = (int)(c.n_embd / 32);
+    return launch_k("embed_kernel", embed_kernel, dim3((nb + 127) / 128, seq), 128, 0, m->stream, E->qs, E->d, E->type,
+                    nb, toks, (int)c.n_vocab, m->h, m->d_err);
+}
+
 // Dynamic shared memory of attn_decode_kernel.
 int attn_chunk_max(const neon_model* m) { return (int)((m->cfg.ctx_len + m->att_cs - 1) / m->att_cs); }
 size_t attn_decode_smem(const neon_model* m) {
@@ -837,11 +849,7 @@ int residual_proj(neon_model* m, neon_tensor_t W, const float* x, size_t x_strid
 // All layers for `seq` positions starting at *d_pos, tokens in `toks` (device).
 int run_layers(neon_model* m, const int* toks, int seq) {
     const auto& c = m->cfg;
-    const neon_tensor_t E = m->embd;
-    const int nb = (int)(c.n_embd / 32);
-    embed_kernel<<<dim3((nb + 127) / 128, seq), 128, 0, m->stream>>>(E->qs, E->d, E->type, nb, toks, (int)c.n_vocab,
-                                                                     m->h, m->d_err);
-    int rc = check_launch("embed_kernel");
+    int rc = launch_embed(m, toks, seq);
     const size_t n_embd = c.n_embd, q_dim = m->q_dim, kv_dim = m->kv_dim, n_ff = m->n_ff_l;
     const float scale = 1.0f / std::sqrt((float)c.head_dim);
     const int group = (int)(c.n_head / c.n_kv_head);
@@ -900,10 +908,7 @@ int run_head(neon_model* m, const float* x) {
 // reduce launch adds the ranks' rows into the residual.
 int run_step(neon_model* m) {
     const auto& c = m->cfg;
-    const neon_tensor_t E = m->embd;
-    const int nb = (int)(c.n_embd / 32);
-    int rc = launch_k("embed_kernel", embed_kernel, dim3((nb + 127) / 128, 1), 128, 0, m->stream, E->qs, E->d, E->type,
-                      nb, m->d_tok, (int)c.n_vocab, m->h, m->d_err);
+    int rc = launch_embed(m, m->d_tok, 1);
     const size_t n_embd = c.n_embd, q_dim = m->q_dim, kv_dim = m->kv_dim, n_ff = m->n_ff_l;
     const bool fused = m->world > 1 && neon_internal::fused_collectives();
     float* hc = m->h;
@@ -1236,12 +1241,20 @@ int neon_cuda_model_set_tensor(neon_model_t m, int role, int layer, const uint8_
                                            std::to_string(want1) + "].");
     if (role != NEON_ROLE_TOKEN_EMBD && role != NEON_ROLE_OUTPUT && (layer < 0 || (uint32_t)layer >= c.n_layer))
         return error(NEON_ERR_INVALID, "layer index out of range");
+    {
+        const size_t rb = neon_internal::gguf_row_bytes(ggml_type, ne0);
+        if (rb == 0)
+            return error(NEON_ERR_UNSUPPORTED, "NANITY: tensor of role " + std::to_string(role) + ": quant type " +
+                                                   std::to_string(ggml_type) + " with input dim " + std::to_string(ne0) +
+                                                   " is not supported");
+        if (nbytes < rb * ne1) return error(NEON_ERR_INVALID, "tensor bytes shorter than its shape");
+    }
     if (role == NEON_ROLE_FFN_GATE && c.plain_ffn)
         return error(NEON_ERR_INVALID, "ffn_gate given to a plain SiLU-FFN model (plain_ffn = 1)");
     if (role == NEON_ROLE_FFN_UP && c.plain_ffn) {
         // plain SiLU-FFN: the up rows alone (this rank's [ff0, ff0 + n_ff_l))
-        const size_t row_b = ggml_type == NEON_GGML_Q4_0 ? ne0 / 32 * 18 : ggml_type == NEON_GGML_Q8_0 ? ne0 / 32 * 34 : 0;
-        if (row_b == 0) return error(NEON_ERR_UNSUPPORTED, "ffn_up must be Q4_0 or Q8_0");
+        const size_t row_b = neon_internal::gguf_row_bytes(ggml_type, ne0);
+        if (row_b == 0) return error(NEON_ERR_UNSUPPORTED, "ffn_up: unsupported quant type or input dim");
         if (nbytes < row_b * ne1) return error(NEON_ERR_INVALID, "tensor bytes shorter than its shape");
         neon_tensor_t t = nullptr;
         int rc = neon_cuda_upload(host_bytes + sh[0] * row_b, ggml_type, sh[1] - sh[0], ne0, NEON_SHARD_NONE, 0, 1, &t);
@@ -1256,8 +1269,8 @@ int neon_cuda_model_set_tensor(neon_model_t m, int role, int layer, const uint8_
         // row 2i is gate row i and row 2i+1 up row i (same bytes, same math)
         // (a tensor-parallel rank keeps rows [ff0, ff0 + n_ff_l) of both)
         auto& L = m->layers[layer];
-        const size_t row_b = ggml_type == NEON_GGML_Q4_0 ? ne0 / 32 * 18 : ggml_type == NEON_GGML_Q8_0 ? ne0 / 32 * 34 : 0;
-        if (row_b == 0) return error(NEON_ERR_UNSUPPORTED, "ffn_gate / ffn_up must be Q4_0 or Q8_0");
+        const size_t row_b = neon_internal::gguf_row_bytes(ggml_type, ne0);
+        if (row_b == 0) return error(NEON_ERR_UNSUPPORTED, "ffn_gate / ffn_up: unsupported quant type or input dim");
         if (nbytes < row_b * ne1) return error(NEON_ERR_INVALID, "tensor bytes shorter than its shape");
         const size_t r0 = sh[0], nr = sh[1] - sh[0];
         (role == NEON_ROLE_FFN_GATE ? L.gate_bytes : L.up_bytes)
@@ -1285,6 +1298,18 @@ int neon_cuda_model_set_tensor(neon_model_t m, int role, int layer, const uint8_
     if (m->world > 1) {
         if (sh[0] != 0 || sh[1] != ne1) mode = NEON_SHARD_ROWS;
         else if (sh[2] != 0 || sh[3] != ne0) mode = NEON_SHARD_COLS;
+    }
+    if (mode == NEON_SHARD_COLS) {
+        // the upload keeps blocks [nblk*r/W, nblk*(r+1)/W) of every row: that
+        // must be exactly this rank's column range (256-value K-quant blocks
+        // may not split where the 32-column plan does)
+        const size_t be = std::max<size_t>(32, neon_internal::gguf_block_elems(ggml_type));
+        const size_t nblk = ne0 / be;
+        const size_t b0 = nblk * (size_t)m->rank / (size_t)m->world, b1 = nblk * (size_t)(m->rank + 1) / (size_t)m->world;
+        if (ne0 % be != 0 || b0 * be != sh[2] || b1 * be != sh[3])
+            return error(NEON_ERR_UNSUPPORTED, "tensor-parallel column split of role " + std::to_string(role) +
+                                                   ": columns [" + std::to_string(sh[2]) + ", " + std::to_string(sh[3]) +
+                                                   ") do not fall on this type's " + std::to_string(be) + "-value blocks");
     }
     if (m->world > 1 && (role == NEON_ROLE_OUTPUT || (role == NEON_ROLE_TOKEN_EMBD && !m->head_from_output))) {
         // the lm_head's vocabulary shard (of output.weight, or of the tied embedding)

@@ -1,0 +1,438 @@
+// neon_dequant.cuh -- the matvec of the remaining GGUF weight types:
+// F32, F16, BF16, Q4_1, Q5_0, Q5_1 and the K-quant super-blocks Q4_K, Q5_K,
+// Q6_K (sm_100a, CUDA cores).
+//
+// Reference path: every weight type other than Q4_0 is dequantised a row at a
+// time (dequantize_row, rawllm_forward.hpp:301-321, with the block decoders of
+// :133-298) and dotted with fp32 X (dot_f32, :446-479), inside
+// proj_all_positions (:597-605) and proj_all_positions_multi (:632-726).
+// Here the weights are decoded straight from the block bytes in registers,
+// never written out as fp32 rows.
+//
+// Device layout (neon_cuda_upload): the GGUF rows unchanged, each row padded
+// to a 16-byte pitch so that every row -- and every chunk of CB blocks, whose
+// byte size is a multiple of 16 for every type -- starts on a 16-byte
+// boundary. The plain float types are cut into 32-value "blocks" and their
+// rows zero-padded to a whole number of them.
+//
+// Work decomposition: a CTA (8 warps) owns a tile of 8 consecutive rows, one
+// row per warp. A warp walks its row a chunk at a time: the chunk's bytes are
+// read with coalesced 128-bit loads (the next chunk's loads are in flight
+// while the current one is decoded), parked in the warp's shared-memory
+// buffer, and every lane then decodes whole 32-value sub-blocks from it (one
+// for the 32-value types, two for the K-quants: 8 super-blocks = 64
+// sub-blocks a chunk) and takes their dot products with X, which the CTA
+// staged once in shared memory (fp32, 36-float pitch per 32 values, so the
+// lanes' 128-bit reads of consecutive sub-blocks do not collide). A butterfly
+// shuffle finishes each row; the decode-step epilogues are the one-position
+// kernel's (stream_epilogue).
+//
+// Every decoded value equals the reference's bit for bit: each is one exact
+// product (at most 23 significant bits: fp16 scale x 6-bit sub-scale x 6-bit
+// quant) plus at most one rounded add, so fused or separate multiply-adds
+// give the same float. Only the order of the dot product's additions differs
+// from dot_f32's.
+#pragma once
+
+#include <string.h>
+
+#include "neon_kernels.cuh"
+
+namespace neon {
+
+// BE values and BB bytes per block; CB blocks per chunk (CB*BB is a multiple
+// of 16 for every type).
+template <int TYPE> struct DqType;
+template <> struct DqType<NEON_GGML_F32> { static constexpr int BE = 32, BB = 128, CB = 32; };
+template <> struct DqType<NEON_GGML_F16> { static constexpr int BE = 32, BB = 64, CB = 32; };
+template <> struct DqType<NEON_GGML_BF16> { static constexpr int BE = 32, BB = 64, CB = 32; };
+template <> struct DqType<NEON_GGML_Q4_1> { static constexpr int BE = 32, BB = 20, CB = 32; };
+template <> struct DqType<NEON_GGML_Q5_0> { static constexpr int BE = 32, BB = 22, CB = 32; };
+template <> struct DqType<NEON_GGML_Q5_1> { static constexpr int BE = 32, BB = 24, CB = 32; };
+template <> struct DqType<NEON_GGML_Q4_K> { static constexpr int BE = 256, BB = 144, CB = 8; };
+template <> struct DqType<NEON_GGML_Q5_K> { static constexpr int BE = 256, BB = 176, CB = 8; };
+template <> struct DqType<NEON_GGML_Q6_K> { static constexpr int BE = 256, BB = 210, CB = 8; };
+
+template <int TYPE> struct DqShape {
+    static constexpr int BE = DqType<TYPE>::BE, BB = DqType<TYPE>::BB, CB = DqType<TYPE>::CB;
+    static constexpr int SUBS = BE / 32;                 // 32-value sub-blocks per block
+    static constexpr int UNITS = CB * SUBS;              // sub-blocks per chunk: 32 or 64
+    static constexpr int UPL = UNITS / 32;               // per lane
+    static constexpr int CHUNK = CB * BB;                // bytes per chunk
+    static constexpr int WPL = (CHUNK / 16 + 31) / 32;   // 128-bit loads per lane per chunk
+    static_assert(CHUNK % 16 == 0, "chunks must stay 16-byte aligned");
+};
+
+// Host view of the block geometry of a type: values per block, bytes per
+// block, blocks per chunk (0 if the type is not one of this kernel's).
+__host__ __device__ inline void dq_geometry(int type, int* be, int* bb, int* cb) {
+    int e = 0, b = 0, c = 0;
+    switch (type) {
+        case NEON_GGML_F32: e = 32; b = 128; c = 32; break;
+        case NEON_GGML_F16: e = 32; b = 64; c = 32; break;
+        case NEON_GGML_BF16: e = 32; b = 64; c = 32; break;
+        case NEON_GGML_Q4_1: e = 32; b = 20; c = 32; break;
+        case NEON_GGML_Q5_0: e = 32; b = 22; c = 32; break;
+        case NEON_GGML_Q5_1: e = 32; b = 24; c = 32; break;
+        case NEON_GGML_Q4_K: e = 256; b = 144; c = 8; break;
+        case NEON_GGML_Q5_K: e = 256; b = 176; c = 8; break;
+        case NEON_GGML_Q6_K: e = 256; b = 210; c = 8; break;
+        default: break;
+    }
+    *be = e;
+    *bb = b;
+    *cb = c;
+}
+
+struct DqArgs {
+    StreamArgs s;         // spans (qs = the padded GGUF rows), X, epilogue and fused-collective options
+    long long pitch;      // bytes per device row (same for every span: one type, one input dim)
+    long long x_stride;   // floats between positions of X
+    int cols;             // values per row (X entries read; the float types may be ragged)
+    int nu;               // 32-value sub-blocks per row (cols rounded up)
+    int nblk;             // blocks per row
+    int nch;              // chunks per row
+    int seq;              // positions
+};
+
+// Shared memory of a launch: X for T positions, then one chunk buffer per warp.
+__host__ __device__ constexpr int dq_x_bytes(int T, int nu) { return ((T * nu * kQ8Pitch * 4) + 127) & ~127; }
+
+// The block decoders below are __host__ __device__: the host build of the
+// same source is what the CPU tests compare against the oracle.
+#ifdef __CUDA_ARCH__
+#define NEON_HD_MUL(a, b) __fmul_rn((a), (b))  // never contracted into an FMA
+#define NEON_HD_BITS_F32(u) __uint_as_float(u)
+#else
+#define NEON_HD_MUL(a, b) ((a) * (b))
+inline float neon_hd_bits_f32(uint32_t u) {
+    float f;
+    memcpy(&f, &u, 4);
+    return f;
+}
+#define NEON_HD_BITS_F32(u) neon_hd_bits_f32(u)
+#endif
+
+__host__ __device__ __forceinline__ uint32_t sh_u16(const unsigned char* p) { return *reinterpret_cast<const uint16_t*>(p); }
+__host__ __device__ __forceinline__ uint32_t sh_u32(const unsigned char* p) { return *reinterpret_cast<const uint32_t*>(p); }
+// binary16 -> binary32, exact (subnormals included)
+__host__ __device__ __forceinline__ float sh_half(const unsigned char* p) {
+    return __half2float(__ushort_as_half((unsigned short)sh_u16(p)));
+}
+
+// The (scale, min) pair of sub-block s of a Q4_K / Q5_K super-block from its
+// 12 packed bytes (get_scale_min_k4, rawllm_forward.hpp:224-233): sub-blocks
+// 0-3 use the low six bits of bytes s and s+4; 4-7 take a nibble of byte s+4
+// and two high bits from bytes s-4 (scale) and s (min).
+__host__ __device__ __forceinline__ void k4_scale_min(const unsigned char* sc, int s, int& scale, int& mn) {
+    if (s < 4) {
+        scale = sc[s] & 63;
+        mn = sc[s + 4] & 63;
+    } else {
+        scale = (sc[s + 4] & 0x0F) | ((sc[s - 4] >> 6) << 4);
+        mn = (sc[s + 4] >> 4) | ((sc[s] >> 6) << 4);
+    }
+}
+
+// The 32 values of sub-block s of the block at `blk` (shared or global memory,
+// aligned as a block of the padded-row layout is).
+// Formulas of rawllm_forward.hpp, regrouped by sub-block:
+//   F16 / BF16 / F32  :133-141
+//   Q4_1 :164-175  d*q + m             Q5_0 :177-191  d*(q - 16), q = nibble | qh bit << 4
+//   Q5_1 :193-208  d*q + m (q as Q5_0)
+//   Q4_K :235-253  (d*sc)*q - dmin*mn on nibble (s&1) of bytes 32*(s/2)..
+//   Q5_K :255-275  as Q4_K, q += 16 * bit s of qh[l]
+//   Q6_K :277-298  (d*sc)*(q - 32); sub-block s = 4h + k: low bytes 64h + 32(k&1)..,
+//                  high nibble when k >= 2, 2-bit pair k of qh[32h + l], scales 8h + 2k + l/16
+template <int TYPE>
+__host__ __device__ __forceinline__ void dq_sub(const unsigned char* blk, int s, float (&w)[32]) {
+    if constexpr (TYPE == NEON_GGML_F32) {
+        const float4* p = reinterpret_cast<const float4*>(blk);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const float4 v = p[k];
+            w[4 * k] = v.x;
+            w[4 * k + 1] = v.y;
+            w[4 * k + 2] = v.z;
+            w[4 * k + 3] = v.w;
+        }
+    } else if constexpr (TYPE == NEON_GGML_F16 || TYPE == NEON_GGML_BF16) {
+        const uint4* p = reinterpret_cast<const uint4*>(blk);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint4 v = p[k];
+            const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                if constexpr (TYPE == NEON_GGML_F16) {
+                    w[8 * k + 2 * i] = __half2float(__ushort_as_half((unsigned short)(u[i] & 0xFFFFu)));
+                    w[8 * k + 2 * i + 1] = __half2float(__ushort_as_half((unsigned short)(u[i] >> 16)));
+                } else {
+                    w[8 * k + 2 * i] = NEON_HD_BITS_F32(u[i] << 16);
+                    w[8 * k + 2 * i + 1] = NEON_HD_BITS_F32(u[i] & 0xFFFF0000u);
+                }
+            }
+        }
+    } else if constexpr (TYPE == NEON_GGML_Q4_1 || TYPE == NEON_GGML_Q5_1) {
+        // 4-byte aligned blocks (20 / 24 bytes)
+        constexpr bool five = TYPE == NEON_GGML_Q5_1;
+        const float d = sh_half(blk), m = sh_half(blk + 2);
+        const uint32_t qh = five ? sh_u32(blk + 4) : 0u;
+        const unsigned char* qs = blk + (five ? 8 : 4);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint32_t q4 = sh_u32(qs + 4 * k);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int j = 4 * k + i;
+                int lo = (q4 >> (8 * i)) & 0x0F, hi = (q4 >> (8 * i + 4)) & 0x0F;
+                if (five) {
+                    lo |= ((qh >> j) & 1u) << 4;
+                    hi |= ((qh >> (j + 16)) & 1u) << 4;
+                }
+                w[j] = fmaf(d, (float)lo, m);
+                w[j + 16] = fmaf(d, (float)hi, m);
+            }
+        }
+    } else if constexpr (TYPE == NEON_GGML_Q5_0) {
+        // 22-byte blocks: only 2-byte alignment
+        const float d = sh_half(blk);
+        const uint32_t qh = sh_u16(blk + 2) | (sh_u16(blk + 4) << 16);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const uint32_t q2 = sh_u16(blk + 6 + 2 * k);
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                const int j = 2 * k + i;
+                const int lo = ((q2 >> (8 * i)) & 0x0F) | (((qh >> j) & 1u) << 4);
+                const int hi = ((q2 >> (8 * i + 4)) & 0x0F) | (((qh >> (j + 16)) & 1u) << 4);
+                w[j] = NEON_HD_MUL(d, (float)(lo - 16));
+                w[j + 16] = NEON_HD_MUL(d, (float)(hi - 16));
+            }
+        }
+    } else if constexpr (TYPE == NEON_GGML_Q4_K || TYPE == NEON_GGML_Q5_K) {
+        // 16-byte aligned super-blocks (144 / 176 bytes)
+        constexpr bool five = TYPE == NEON_GGML_Q5_K;
+        const float d = sh_half(blk), dmin = sh_half(blk + 2);
+        int sc, mn;
+        k4_scale_min(blk + 4, s, sc, mn);
+        const float ds = NEON_HD_MUL(d, (float)sc), ms = NEON_HD_MUL(dmin, (float)mn);
+        const unsigned char* q = blk + (five ? 48 : 16) + 32 * (s >> 1);
+        const int shift = (s & 1) * 4;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const uint32_t q4 = sh_u32(q + 4 * k);
+            const uint32_t h4 = five ? sh_u32(blk + 16 + 4 * k) : 0u;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                int v = (q4 >> (8 * i + shift)) & 0x0F;
+                if (five) v |= ((h4 >> (8 * i + s)) & 1u) << 4;
+                w[4 * k + i] = fmaf(ds, (float)v, -ms);
+            }
+        }
+    } else if constexpr (TYPE == NEON_GGML_Q6_K) {
+        // 210-byte super-blocks: only 2-byte alignment
+        const int h = s >> 2, k = s & 3;
+        const unsigned char* ql = blk + 64 * h + 32 * (k & 1);
+        const unsigned char* qh = blk + 128 + 32 * h;
+        const signed char* scp = reinterpret_cast<const signed char*>(blk + 192 + 8 * h + 2 * k);
+        const float d = sh_half(blk + 208);
+        const float d0 = NEON_HD_MUL(d, (float)scp[0]), d1 = NEON_HD_MUL(d, (float)scp[1]);
+        const int lshift = (k >> 1) * 4, hshift = 2 * k;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const uint32_t l2 = sh_u16(ql + 2 * j), h2 = sh_u16(qh + 2 * j);
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                const int l = 2 * j + i;
+                const int q = (int)((((l2 >> (8 * i + lshift)) & 0x0F) | (((h2 >> (8 * i + hshift)) & 3u) << 4))) - 32;
+                w[l] = NEON_HD_MUL(l < 16 ? d0 : d1, (float)q);
+            }
+        }
+    }
+}
+
+// sum_j w[j] * x[j] for one 32-value sub-block (x: 32 floats, 16-byte aligned).
+__device__ __forceinline__ float dq_dot32(const float (&w)[32], const float* x) {
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+    float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; k += 2) {
+        const float4 a = x4[k], b = x4[k + 1];
+        s0 = fmaf(w[4 * k], a.x, s0);
+        s1 = fmaf(w[4 * k + 4], b.x, s1);
+        s0 = fmaf(w[4 * k + 1], a.y, s0);
+        s1 = fmaf(w[4 * k + 5], b.y, s1);
+        s0 = fmaf(w[4 * k + 2], a.z, s0);
+        s1 = fmaf(w[4 * k + 6], b.z, s1);
+        s0 = fmaf(w[4 * k + 3], a.w, s0);
+        s1 = fmaf(w[4 * k + 7], b.w, s1);
+    }
+    return s0 + s1;
+}
+
+// T positions per CTA (grid.y tiles the positions); one row per warp.
+template <int TYPE, int T>
+__global__ void __launch_bounds__(kThreads) matvec_dq_kernel(const __grid_constant__ DqArgs a) {
+    using D = DqShape<TYPE>;
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ float rowv[2][T][kWarps];   // by tile parity: a tile's results never wait on the last epilogue
+    __shared__ double dscratch[32];
+    __shared__ float2 rcs[kMaxRopeHalf];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nu = a.nu, nch = a.nch;
+    float* xs = reinterpret_cast<float*>(smem);
+    unsigned char* wbuf = smem + dq_x_bytes(T, nu) + warp * D::CHUNK;
+    const int p0 = (int)blockIdx.y * T;
+    const int npos = min(T, a.seq - p0);
+    const int my_tiles =
+        (int)blockIdx.x < a.s.n_tiles ? (a.s.n_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    const int n_items = my_tiles * nch;
+
+    // this warp's row of item `item`, its chunk, and the chunk's block count
+    auto locate = [&](int item, int& span, int& row0, int& chunk, int& nblk_c) {
+        const int tile = (int)blockIdx.x + (item / nch) * (int)gridDim.x;
+        span = find_span_of(a.s, tile);
+        row0 = (tile - a.s.span[span].tile0) * kWarps;
+        chunk = item % nch;
+        nblk_c = min(D::CB, a.nblk - chunk * D::CB);
+    };
+    uint4 pre[D::WPL];
+    auto load = [&](int item) {
+        int span, row0, chunk, nblk_c;
+        locate(item, span, row0, chunk, nblk_c);
+        const int row = row0 + warp;
+        if (row >= a.s.span[span].rows) return;
+        const unsigned char* src = a.s.span[span].qs + (long long)row * a.pitch + (long long)chunk * D::CHUNK;
+        const int words = (nblk_c * D::BB + 15) >> 4;
+#pragma unroll
+        for (int k = 0; k < D::WPL; ++k) {
+            const int wi = lane + 32 * k;
+            if (wi < words) pre[k] = ld_weights_u4(src + 16 * wi);
+        }
+    };
+    // weights are never written by an earlier kernel of the stream: their
+    // first loads go out before the dependency wait
+    if (n_items > 0) load(0);
+    pdl_wait();
+
+    const unsigned int peer_call =
+        a.s.peer_mode ? *reinterpret_cast<volatile const unsigned int*>(a.s.peer.calls) + 1u : 0u;
+    const int pos = a.s.d_pos ? *a.s.d_pos : 0;
+    if (a.s.rope_cs)
+        for (int i = threadIdx.x; i < a.s.rope_half; i += kThreads) rcs[i] = a.s.rope_cs[(long long)pos * a.s.rope_half + i];
+
+    // X of this CTA's positions (rms-normalised first when asked; one position then)
+    {
+        const float nscale = a.s.norm_w ? cta_rms_scale(a.s.x, a.cols, a.s.norm_eps, dscratch) : 1.f;
+        for (int t = 0; t < npos; ++t) {
+            const float* xp = a.s.x + (long long)(p0 + t) * a.x_stride;
+            float* xd = xs + (long long)t * nu * kQ8Pitch;
+            for (int i = threadIdx.x; i < nu * 32; i += kThreads) {
+                float v = 0.f;
+                if (i < a.cols) {
+                    v = __ldg(xp + i);
+                    if (a.s.norm_w) v = __fmul_rn(__fmul_rn(v, nscale), __ldg(a.s.norm_w + i));
+                }
+                xd[(i >> 5) * kQ8Pitch + (i & 31)] = v;
+            }
+        }
+    }
+    __syncthreads();
+    pdl_launch_dependents();
+
+    float acc[T];
+#pragma unroll
+    for (int t = 0; t < T; ++t) acc[t] = 0.f;
+    for (int item = 0; item < n_items; ++item) {
+        int span, row0, chunk, nblk_c;
+        locate(item, span, row0, chunk, nblk_c);
+        const Span& sp = a.s.span[span];
+        const bool valid = row0 + warp < sp.rows;
+        const int words = (nblk_c * D::BB + 15) >> 4;
+        // park the chunk in the warp's buffer, then start the next one's loads
+        __syncwarp();
+        if (valid) {
+#pragma unroll
+            for (int k = 0; k < D::WPL; ++k) {
+                const int wi = lane + 32 * k;
+                if (wi < words) reinterpret_cast<uint4*>(wbuf)[wi] = pre[k];
+            }
+        }
+        __syncwarp();
+        if (item + 1 < n_items) load(item + 1);
+        if (valid) {
+#pragma unroll
+            for (int j = 0; j < D::UPL; ++j) {
+                const int u = lane + 32 * j;
+                if (u < nblk_c * D::SUBS) {
+                    float w[32];
+                    dq_sub<TYPE>(wbuf + (u / D::SUBS) * D::BB, u % D::SUBS, w);
+                    const int unit = chunk * D::UNITS + u;
+#pragma unroll
+                    for (int t = 0; t < T; ++t)
+                        if (t < npos) acc[t] += dq_dot32(w, xs + ((long long)t * nu + unit) * kQ8Pitch);
+                }
+            }
+        }
+        if (chunk == nch - 1) {
+            const int tb = (item / nch) & 1;
+#pragma unroll
+            for (int t = 0; t < T; ++t) {
+#pragma unroll
+                for (int o = 16; o; o >>= 1) acc[t] += __shfl_xor_sync(0xffffffffu, acc[t], o);
+                if (lane == 0) rowv[tb][t][warp] = acc[t];
+                acc[t] = 0.f;
+            }
+            __syncthreads();
+            if constexpr (T == 1) {
+                // one position: the decode epilogues (plain store at position p0 otherwise)
+                Span spo = sp;
+                spo.y += (long long)p0 * sp.y_stride;
+                float yold = 0.f;
+                if (a.s.accumulate && spo.epi == kEpiStore && (int)threadIdx.x < kWarps &&
+                    row0 + (int)threadIdx.x < spo.rows)
+                    yold = spo.y[row0 + threadIdx.x];
+                stream_epilogue(a.s, spo, row0, kWarps, rowv[tb][0], peer_call, pos, rcs, yold);
+            } else {
+                const int t = threadIdx.x / kWarps, r = threadIdx.x % kWarps;
+                const int row = row0 + r;
+                if (t < npos && row < sp.rows) {
+                    float* y = sp.y + (long long)(p0 + t) * sp.y_stride + row;
+                    const float v = rowv[tb][t][r];
+                    *y = a.s.accumulate ? *y + v : v;
+                }
+            }
+        }
+    }
+}
+
+// h[t] = the values of embedding row tokens[t] (transformer_forward's
+// embedding lookup, rawllm_forward.hpp:1023-1033, through dequantize_row).
+// One thread per 32-value sub-block; an out-of-range id sets bit 1 of *err
+// and reads row 0 (the split-layout embed kernel's rule).
+template <int TYPE>
+__global__ void __launch_bounds__(128) embed_dq_kernel(const unsigned char* __restrict__ rows, long long pitch,
+                                                       int n_embd, const int* __restrict__ tokens, int n_vocab,
+                                                       float* __restrict__ h, unsigned int* err) {
+    using D = DqShape<TYPE>;
+    pdl_wait();
+    pdl_launch_dependents();
+    const int t = blockIdx.y;
+    int tok = tokens[t];
+    if (tok < 0 || tok >= n_vocab) {
+        if (threadIdx.x == 0) atomicOr(err, 2u);
+        tok = 0;
+    }
+    float* out = h + (long long)t * n_embd;
+    const int nu = (n_embd + 31) / 32;
+    for (int u = blockIdx.x * blockDim.x + threadIdx.x; u < nu; u += gridDim.x * blockDim.x) {
+        float w[32];
+        dq_sub<TYPE>(rows + (long long)tok * pitch + (u / D::SUBS) * D::BB, u % D::SUBS, w);
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+            if (u * 32 + j < n_embd) out[u * 32 + j] = w[j];
+    }
+}
+
+}  // namespace neon

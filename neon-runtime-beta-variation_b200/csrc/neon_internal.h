@@ -10,8 +10,10 @@
 
 #include "neon_cuda.h"
 
-// A device-resident weight tensor (or tensor-parallel shard) in the split
-// layout: payload plane rows x nb x P bytes, then fp16 scales rows x nb.
+// A device-resident weight tensor (or tensor-parallel shard). Q4_0 / Q8_0 use
+// the split layout: payload plane rows x nb x P bytes, then fp16 scales
+// rows x nb (pitch 0). The other types keep the GGUF rows, each padded to a
+// 16-byte pitch (d null; nb counts 32-value sub-blocks, cols rounded up).
 struct neon_tensor {
     int device;
     int type;
@@ -20,6 +22,7 @@ struct neon_tensor {
     uint8_t* qs;
     uint16_t* d;
     size_t bytes;
+    size_t pitch;   // bytes per row of the padded-row layout; 0 for the split layout
 };
 
 // Tensor-parallel communicator: one per rank (process, device). Every rank
@@ -140,6 +143,15 @@ struct MatvecExt {
 int matvec(const neon_proj_target_t* targets, size_t n, const float* dX, size_t x_stride, size_t seq,
            cudaStream_t st, int accumulate, const MatvecExt* ext = nullptr);
 int error(int code, const std::string& msg);
+// Bytes of one GGUF row of `type` with `cols` values (0: unsupported type, or
+// cols not a multiple of the type's block size). rawllm_loader.hpp:367-386.
+size_t gguf_row_bytes(int type, size_t cols);
+// Values per block of `type` (block_size_for, rawllm_forward.hpp:289-299); 0 if unsupported.
+size_t gguf_block_elems(int type);
+// h[t] = row toks[t] of a padded-row (non Q4_0/Q8_0) embedding, decoded; a
+// token id out of range sets bit 1 of *err. seq rows of n_embd floats.
+int embed_rows(const neon_tensor* E, const int* toks, int seq, int n_embd, int n_vocab, float* h, unsigned int* err,
+               cudaStream_t st);
 int cuda_error(cudaError_t e, const char* what);
 int launched(int n);  // count kernels launched outside the matvec path
 bool pdl_enabled();

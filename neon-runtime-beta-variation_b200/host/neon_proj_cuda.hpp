@@ -39,12 +39,27 @@ inline void check(int rc) {
 }
 
 // Bytes of one GGUF row, as loader::GGUFLoader::bytes_for_type
-// (rawllm_loader.hpp:367-386) gives them for the types this backend runs.
+// (rawllm_loader.hpp:367-386) gives them for the types this backend runs
+// (0 for any other type).
 inline size_t row_bytes(int ggml_type, size_t cols) {
-    if (ggml_type == NEON_GGML_Q4_0) return cols / 32 * 18;
-    if (ggml_type == NEON_GGML_Q8_0) return cols / 32 * 34;
-    return 0;
+    switch (ggml_type) {
+        case NEON_GGML_F32: return cols * 4;
+        case NEON_GGML_F16: case NEON_GGML_BF16: return cols * 2;
+        case NEON_GGML_Q4_0: return cols / 32 * 18;
+        case NEON_GGML_Q4_1: return cols / 32 * 20;
+        case NEON_GGML_Q5_0: return cols / 32 * 22;
+        case NEON_GGML_Q5_1: return cols / 32 * 24;
+        case NEON_GGML_Q8_0: return cols / 32 * 34;
+        case NEON_GGML_Q4_K: return cols / 256 * 144;
+        case NEON_GGML_Q5_K: return cols / 256 * 176;
+        case NEON_GGML_Q6_K: return cols / 256 * 210;
+        default: return 0;
+    }
 }
+
+// A 2-D weight type the backend multiplies (the eleven dequantize_row decodes,
+// rawllm_forward.hpp:301-321).
+inline bool runs_type(int ggml_type) { return row_bytes(ggml_type, 256) != 0; }
 
 // Side table TensorInfo address -> device tensor.
 class TensorTable {
@@ -98,14 +113,14 @@ inline TensorTable& tensors() {
     return t;
 }
 
-// Upload every 2-D Q4_0/Q8_0 tensor of a loader (GGUFLoader or NCTRLoader:
+// Upload every 2-D weight tensor of a loader (GGUFLoader or NCTRLoader:
 // anything with a `.tensors` vector of TensorInfo) once, at load time.
 template <class LoaderT>
 size_t upload_model(const LoaderT& loader) {
     size_t n = 0;
     for (const auto& t : loader.tensors) {
         const int ty = static_cast<int>(t.type);
-        if (t.shape.size() == 2 && (ty == NEON_GGML_Q4_0 || ty == NEON_GGML_Q8_0)) {
+        if (t.shape.size() == 2 && runs_type(ty)) {
             tensors().get(t);
             ++n;
         }

@@ -38,7 +38,14 @@ NEON_OK = 0
 GGML_F32 = 0
 GGML_F16 = 1
 GGML_Q4_0 = 2
+GGML_Q4_1 = 3
+GGML_Q5_0 = 6
+GGML_Q5_1 = 7
 GGML_Q8_0 = 8
+GGML_Q4_K = 12
+GGML_Q5_K = 13
+GGML_Q6_K = 14
+GGML_BF16 = 30
 SHARD_NONE = 0
 SHARD_ROWS = 1
 SHARD_COLS = 2
@@ -294,7 +301,9 @@ class ProjTarget:
         self.W, self.Y, self.y_stride = W, Y, y_stride
 
 
-_BLOCK = {GGML_Q4_0: 32, GGML_Q8_0: 32}
+# values per block (block_size_for, rawllm_forward.hpp:289-299); float types: 1
+_BLOCK = {GGML_Q4_0: 32, GGML_Q4_1: 32, GGML_Q5_0: 32, GGML_Q5_1: 32, GGML_Q8_0: 32,
+          GGML_Q4_K: 256, GGML_Q5_K: 256, GGML_Q6_K: 256}
 _uploaded: "weakref.WeakKeyDictionary[TensorInfo, DeviceTensor]" = weakref.WeakKeyDictionary()
 
 

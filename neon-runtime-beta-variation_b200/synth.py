@@ -9,6 +9,10 @@ the benchmark configurations state.
   32 nibbles uniform in 0..15 with value ``(q - 8) * d``.
 * Q8_0 block (34 bytes): ``d = fp16(|N(0,1)| * 0.01)`` then 32 int8 uniform
   in [-127, 127].
+* The other GGUF weight types (matvec parity tests only): fp16 scales drawn the
+  same way, every quant field uniform random bytes; Q4_1 / Q5_1 minimums put
+  the block's middle value near zero; Q6_K int8 sub-block scales uniform in
+  [-64, 64]; F32 / F16 / BF16 values ``N(0, 1) * 0.02``.
 * Activations: fp32 ``N(0, 1)``.
 """
 from __future__ import annotations
@@ -18,17 +22,35 @@ import numpy as np
 GGML_F32 = 0
 GGML_F16 = 1
 GGML_Q4_0 = 2
+GGML_Q4_1 = 3
+GGML_Q5_0 = 6
+GGML_Q5_1 = 7
 GGML_Q8_0 = 8
+GGML_Q4_K = 12
+GGML_Q5_K = 13
+GGML_Q6_K = 14
+GGML_BF16 = 30
 
 BLOCK = 32
-BLOCK_BYTES = {GGML_Q4_0: 18, GGML_Q8_0: 34}
+# bytes and values of one block of each weight type (rawllm_loader.hpp:367-386,
+# rawllm_forward.hpp:289-299)
+BLOCK_BYTES = {GGML_Q4_0: 18, GGML_Q8_0: 34, GGML_Q4_1: 20, GGML_Q5_0: 22, GGML_Q5_1: 24,
+               GGML_Q4_K: 144, GGML_Q5_K: 176, GGML_Q6_K: 210, GGML_F32: 4, GGML_F16: 2, GGML_BF16: 2}
+BLOCK_ELEMS = {GGML_Q4_0: 32, GGML_Q8_0: 32, GGML_Q4_1: 32, GGML_Q5_0: 32, GGML_Q5_1: 32,
+               GGML_Q4_K: 256, GGML_Q5_K: 256, GGML_Q6_K: 256, GGML_F32: 1, GGML_F16: 1, GGML_BF16: 1}
+ALL_TYPES = (GGML_F32, GGML_F16, GGML_BF16, GGML_Q4_0, GGML_Q4_1, GGML_Q5_0, GGML_Q5_1, GGML_Q8_0,
+             GGML_Q4_K, GGML_Q5_K, GGML_Q6_K)
+TYPE_NAMES = {GGML_F32: "F32", GGML_F16: "F16", GGML_BF16: "BF16", GGML_Q4_0: "Q4_0", GGML_Q4_1: "Q4_1",
+              GGML_Q5_0: "Q5_0", GGML_Q5_1: "Q5_1", GGML_Q8_0: "Q8_0", GGML_Q4_K: "Q4_K", GGML_Q5_K: "Q5_K",
+              GGML_Q6_K: "Q6_K"}
 
 
 def row_bytes(ggml_type: int, cols: int) -> int:
     """Bytes of one GGUF row (rawllm_loader.hpp:367-386)."""
-    if cols % BLOCK:
-        raise ValueError(f"cols={cols} is not a multiple of {BLOCK}")
-    return cols // BLOCK * BLOCK_BYTES[ggml_type]
+    be = BLOCK_ELEMS[ggml_type]
+    if cols % be:
+        raise ValueError(f"cols={cols} is not a multiple of {be}")
+    return cols // be * BLOCK_BYTES[ggml_type]
 
 
 def q4_0_weights(rows: int, cols: int, seed: int, scale: float = 0.02) -> np.ndarray:
@@ -87,11 +109,53 @@ def pooled_weights(ggml_type: int, rows: int, cols: int, seed: int) -> np.ndarra
     return out.reshape(rows, (cols // BLOCK) * bb)
 
 
+def _f16_bytes(a) -> np.ndarray:
+    return np.ascontiguousarray(a, np.float16).view(np.uint8)
+
+
+def other_weights(ggml_type: int, rows: int, cols: int, seed: int) -> np.ndarray:
+    """rows x cols tensor of one of the remaining GGUF types as raw bytes,
+    shape (rows, row_bytes) uint8 (distributions in the module docstring)."""
+    rng = np.random.default_rng(seed)
+    if ggml_type in (GGML_F32, GGML_F16, GGML_BF16):
+        v = rng.standard_normal((rows, cols), dtype=np.float32) * np.float32(0.02)
+        if ggml_type == GGML_F32:
+            return v.view(np.uint8).reshape(rows, cols * 4)
+        if ggml_type == GGML_F16:
+            return v.astype(np.float16).view(np.uint8).reshape(rows, cols * 2)
+        u = v.view(np.uint32)
+        bf = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)  # round to nearest even
+        return bf.view(np.uint8).reshape(rows, cols * 2)
+    be, bb = BLOCK_ELEMS[ggml_type], BLOCK_BYTES[ggml_type]
+    nb = cols // be
+    out = rng.integers(0, 256, size=(rows, nb, bb), dtype=np.uint8)
+    absn = lambda scale: np.abs(rng.standard_normal((rows, nb), dtype=np.float32)) * np.float32(scale)
+    if ggml_type in (GGML_Q4_1, GGML_Q5_1):
+        d = absn(0.02).astype(np.float16)
+        mid = 8 if ggml_type == GGML_Q4_1 else 16
+        m = (-mid * d.astype(np.float32)).astype(np.float16)
+        out[:, :, 0:2] = _f16_bytes(d).reshape(rows, nb, 2)
+        out[:, :, 2:4] = _f16_bytes(m).reshape(rows, nb, 2)
+    elif ggml_type == GGML_Q5_0:
+        out[:, :, 0:2] = _f16_bytes(absn(0.01)).reshape(rows, nb, 2)
+    elif ggml_type in (GGML_Q4_K, GGML_Q5_K):
+        out[:, :, 0:2] = _f16_bytes(absn(0.0005)).reshape(rows, nb, 2)
+        out[:, :, 2:4] = _f16_bytes(absn(0.004)).reshape(rows, nb, 2)
+    elif ggml_type == GGML_Q6_K:
+        out[:, :, 192:208] = rng.integers(-64, 65, size=(rows, nb, 16), dtype=np.int8).view(np.uint8)
+        out[:, :, 208:210] = _f16_bytes(absn(0.0005)).reshape(rows, nb, 2)
+    else:
+        raise ValueError(f"unsupported ggml type {ggml_type}")
+    return out.reshape(rows, nb * bb)
+
+
 def weights(ggml_type: int, rows: int, cols: int, seed: int) -> np.ndarray:
     if ggml_type == GGML_Q4_0:
         return q4_0_weights(rows, cols, seed)
     if ggml_type == GGML_Q8_0:
         return q8_0_weights(rows, cols, seed)
+    if ggml_type in BLOCK_BYTES:
+        return other_weights(ggml_type, rows, cols, seed)
     raise ValueError(f"unsupported ggml type {ggml_type}")
 
 

@@ -30,8 +30,17 @@
 #include <string.h>
 #include <stdlib.h>
 
+#define ORACLE_GGML_F32 0
+#define ORACLE_GGML_F16 1
 #define ORACLE_GGML_Q4_0 2
+#define ORACLE_GGML_Q4_1 3
+#define ORACLE_GGML_Q5_0 6
+#define ORACLE_GGML_Q5_1 7
 #define ORACLE_GGML_Q8_0 8
+#define ORACLE_GGML_Q4_K 12
+#define ORACLE_GGML_Q5_K 13
+#define ORACLE_GGML_Q6_K 14
+#define ORACLE_GGML_BF16 30
 
 /* Exact IEEE binary16 -> binary32, subnormals included.
  * Restates fp16_to_fp32, rawllm_forward.hpp:94-117. */
@@ -157,6 +166,138 @@ void oracle_dequant_q4_0(const uint8_t* p, size_t n, float* out) {
     }
 }
 
+size_t oracle_block_elems(int type);
+static size_t block_bytes(int type);
+
+/* bfloat16 -> fp32: the 16 bits become the high half. Restates bf16_to_fp32,
+ * rawllm_forward.hpp:119-123. */
+float oracle_bf16_to_fp32(uint16_t h) {
+    uint32_t bits = (uint32_t)h << 16;
+    float out;
+    memcpy(&out, &bits, 4);
+    return out;
+}
+
+/* The six-bit (scale, min) pair of sub-block s (0..7) of a Q4_K / Q5_K
+ * super-block, from its 12 packed bytes: sub-blocks 0-3 keep their pair in
+ * the low six bits of bytes s and s+4; sub-blocks 4-7 take four bits from
+ * byte s+4 and their top two bits from the spare high bits of bytes s-4 (scale)
+ * and s (min). Restates get_scale_min_k4, rawllm_forward.hpp:224-233. */
+static void k4_scale_min(const uint8_t* sc, int s, int* scale, int* min) {
+    if (s < 4) {
+        *scale = sc[s] & 63;
+        *min = sc[s + 4] & 63;
+    } else {
+        *scale = (sc[s + 4] & 0x0F) | ((sc[s - 4] >> 6) << 4);
+        *min = (sc[s + 4] >> 4) | ((sc[s] >> 6) << 4);
+    }
+}
+
+/* The 32 values of sub-block s of one block of `type` (s = 0 for the 32-value
+ * types; 0..7 for the 256-value K-quant super-blocks). Each restates the
+ * matching dequantiser of rawllm_forward.hpp, regrouped by sub-block:
+ *   Q4_1 :164-175  v = d*q + m,          q = nibble (low: j, high: j+16)
+ *   Q5_0 :177-191  v = d*(q - 16),       q = nibble | bit j (or j+16) of qh << 4
+ *   Q5_1 :193-208  v = d*q + m,          q as Q5_0
+ *   Q4_K :235-253  v = (d*sc)*q - dmin*mn, sub-block s: bytes 32*(s/2).., nibble s&1
+ *   Q5_K :255-275  as Q4_K with q += 16 * bit s of qh[l]
+ *   Q6_K :277-298  v = (d*sc)*(q - 32), q = nibble | 2-bit pair << 4; sub-block
+ *                  s = 4h + k takes low-nibble bytes 64h + 32(k&1).., the high
+ *                  nibble when k >= 2, pair k of qh[32h + l], scales 8h + l/16 + 2k
+ * Every product d*q here is exact in fp32 (at most 23 significant bits), so
+ * evaluating with or without fused multiply-adds gives the same values. */
+static void sub_block(int type, const uint8_t* blk, int s, float* out) {
+    switch (type) {
+        case ORACLE_GGML_Q4_1: {
+            const float d = rd_fp16(blk), m = rd_fp16(blk + 2);
+            for (int j = 0; j < 16; ++j) {
+                out[j] = d * (float)(blk[4 + j] & 0x0F) + m;
+                out[j + 16] = d * (float)(blk[4 + j] >> 4) + m;
+            }
+            return;
+        }
+        case ORACLE_GGML_Q5_0:
+        case ORACLE_GGML_Q5_1: {
+            const int has_m = type == ORACLE_GGML_Q5_1;
+            const float d = rd_fp16(blk), m = has_m ? rd_fp16(blk + 2) : 0.f;
+            uint32_t qh;
+            memcpy(&qh, blk + (has_m ? 4 : 2), 4);
+            const uint8_t* qs = blk + (has_m ? 8 : 6);
+            for (int j = 0; j < 16; ++j) {
+                int lo = (qs[j] & 0x0F) | (int)(((qh >> j) & 1u) << 4);
+                int hi = (qs[j] >> 4) | (int)(((qh >> (j + 16)) & 1u) << 4);
+                if (has_m) {
+                    out[j] = d * (float)lo + m;
+                    out[j + 16] = d * (float)hi + m;
+                } else {
+                    out[j] = d * (float)(lo - 16);
+                    out[j + 16] = d * (float)(hi - 16);
+                }
+            }
+            return;
+        }
+        case ORACLE_GGML_Q4_K:
+        case ORACLE_GGML_Q5_K: {
+            const int five = type == ORACLE_GGML_Q5_K;
+            const float d = rd_fp16(blk), dmin = rd_fp16(blk + 2);
+            int sc, mn;
+            k4_scale_min(blk + 4, s, &sc, &mn);
+            const float ds = d * (float)sc, ms = dmin * (float)mn;
+            const uint8_t* qh = blk + 16;
+            const uint8_t* q = blk + (five ? 48 : 16) + 32 * (s / 2);
+            for (int l = 0; l < 32; ++l) {
+                int v = (s & 1) ? (q[l] >> 4) : (q[l] & 0x0F);
+                if (five && ((qh[l] >> s) & 1)) v += 16;
+                out[l] = ds * (float)v - ms;
+            }
+            return;
+        }
+        case ORACLE_GGML_Q6_K: {
+            const int h = s / 4, k = s % 4;
+            const uint8_t* ql = blk + 64 * h + 32 * (k & 1);
+            const uint8_t* qh = blk + 128 + 32 * h;
+            const int8_t* sc = (const int8_t*)(blk + 192) + 8 * h + 2 * k;
+            const float d = rd_fp16(blk + 208);
+            for (int l = 0; l < 32; ++l) {
+                int lo = k >= 2 ? (ql[l] >> 4) : (ql[l] & 0x0F);
+                int q = (lo | (((qh[l] >> (2 * k)) & 3) << 4)) - 32;
+                out[l] = d * (float)sc[l / 16] * (float)q;
+            }
+            return;
+        }
+        default:
+            return;
+    }
+}
+
+/* n values of a row of `type` into out (n whole blocks of the type).
+ * Restates dequantize_row, rawllm_forward.hpp:301-321, and the dequantisers it
+ * dispatches to (:133-298). Returns -1 for a type the reference does not
+ * dequantise there. */
+int oracle_dequantize_row(int type, const uint8_t* p, size_t n, float* out) {
+    size_t be = oracle_block_elems(type), bb = block_bytes(type);
+    if (be == 0) return -1;
+    switch (type) {
+        case ORACLE_GGML_F32:
+            memcpy(out, p, n * 4);
+            return 0;
+        case ORACLE_GGML_F16:
+        case ORACLE_GGML_BF16:
+            for (size_t i = 0; i < n; ++i) {
+                uint16_t h;
+                memcpy(&h, p + 2 * i, 2);
+                out[i] = type == ORACLE_GGML_F16 ? oracle_fp16_to_fp32(h) : oracle_bf16_to_fp32(h);
+            }
+            return 0;
+        case ORACLE_GGML_Q8_0: oracle_dequant_q8_0(p, n, out); return 0;
+        case ORACLE_GGML_Q4_0: oracle_dequant_q4_0(p, n, out); return 0;
+        default:
+            for (size_t b = 0; b < n / be; ++b)
+                for (int s = 0; s < (int)(be / 32); ++s) sub_block(type, p + b * bb, s, out + b * be + 32 * s);
+            return 0;
+    }
+}
+
 /* fp32 dot product in the AVX2+FMA summation order.
  * Restates dot_f32, rawllm_forward.hpp:446-479 (the RAWLLM_AVX2 branch). */
 float oracle_dot_f32(const float* a, const float* b, size_t n) {
@@ -167,29 +308,72 @@ float oracle_dot_f32(const float* a, const float* b, size_t n) {
     float s0 = acc[0] + acc[4], s1 = acc[1] + acc[5];
     float s2 = acc[2] + acc[6], s3 = acc[3] + acc[7];
     float sum = (s0 + s1) + (s2 + s3);
-    for (; i < n; ++i) sum += a[i] * b[i];
+    /* the scalar tail (n not a multiple of 8: plain float rows only), as g++
+     * -O3 compiles `sum += a[i] * b[i]`: with four or more left, four products
+     * are formed as one vector multiply and added in order; the rest are
+     * contracted into FMAs */
+    if (n - i >= 4) {
+        for (int k = 0; k < 4; ++k, ++i) {
+            const float p = a[i] * b[i];
+            sum += p;
+        }
+    }
+    for (; i < n; ++i) sum = fmaf(a[i], b[i], sum);
     return sum;
 }
 
-/* Bytes per row of a GGUF tensor. Restates nbytes_for, rawllm_loader.hpp:367-386
- * (Q4_0 and Q8_0 rows only). Returns 0 for other types. */
-size_t oracle_row_bytes(int type, size_t cols) {
-    if (type == ORACLE_GGML_Q4_0) return cols / 32 * 18;
-    if (type == ORACLE_GGML_Q8_0) return cols / 32 * 34;
-    return 0;
+/* Elements per block of a weight type: 256 for the K-quants, 1 for the plain
+ * float types, 32 for the rest. Restates block_size_for,
+ * rawllm_forward.hpp:289-299. Returns 0 for a type the matvec path does not
+ * dequantise (rawllm_forward.hpp:301-321 throws for those). */
+size_t oracle_block_elems(int type) {
+    switch (type) {
+        case ORACLE_GGML_F32: case ORACLE_GGML_F16: case ORACLE_GGML_BF16: return 1;
+        case ORACLE_GGML_Q4_0: case ORACLE_GGML_Q4_1: case ORACLE_GGML_Q5_0:
+        case ORACLE_GGML_Q5_1: case ORACLE_GGML_Q8_0: return 32;
+        case ORACLE_GGML_Q4_K: case ORACLE_GGML_Q5_K: case ORACLE_GGML_Q6_K: return 256;
+        default: return 0;
+    }
 }
 
-/* Y[t*y_stride + r] = W_r . X_t for r < rows, t < seq, single-threaded.
+/* Bytes of one block of a weight type (the GGUF block structs' sizes).
+ * Restates nbytes_for, rawllm_loader.hpp:367-386. */
+static size_t block_bytes(int type) {
+    switch (type) {
+        case ORACLE_GGML_F32: return 4;
+        case ORACLE_GGML_F16: case ORACLE_GGML_BF16: return 2;
+        case ORACLE_GGML_Q4_0: return 18;   /* d, 16 nibble bytes */
+        case ORACLE_GGML_Q4_1: return 20;   /* d, m, 16 nibble bytes */
+        case ORACLE_GGML_Q5_0: return 22;   /* d, 4 high-bit bytes, 16 nibble bytes */
+        case ORACLE_GGML_Q5_1: return 24;   /* d, m, 4 high-bit bytes, 16 nibble bytes */
+        case ORACLE_GGML_Q8_0: return 34;   /* d, 32 int8 */
+        case ORACLE_GGML_Q4_K: return 144;  /* d, dmin, 12 scale bytes, 128 nibble bytes */
+        case ORACLE_GGML_Q5_K: return 176;  /* d, dmin, 12 scale bytes, 32 high-bit bytes, 128 nibble bytes */
+        case ORACLE_GGML_Q6_K: return 210;  /* 128 low-nibble bytes, 64 high-pair bytes, 16 int8 scales, d */
+        default: return 0;
+    }
+}
+
+/* Bytes per row of a GGUF tensor (0 for an unsupported type or a row that is
+ * not whole blocks). Restates nbytes_for, rawllm_loader.hpp:367-386. */
+size_t oracle_row_bytes(int type, size_t cols) {
+    size_t be = oracle_block_elems(type);
+    if (be == 0 || cols % be != 0) return 0;
+    return cols / be * block_bytes(type);
+}
+
+/* Y[t*y_stride + r] = W_r . X_t for r < rows, t < seq.
  * Restates proj_all_positions, rawllm_forward.hpp:522-609: Q4_0 weights take
  * the fused path (X quantised to Q8_0 once, then dot_q4_0_q8_0 per row);
- * Q8_0 weights take dequant_q8_0 + dot_f32 against fp32 X.
- * `scratch` must hold seq*cols/32 floats + seq*cols bytes (Q4_0 only) and
- * `rowbuf` cols floats (Q8_0 only). Returns 0, or -1 on a bad argument
- * (cols not a multiple of 32, unsupported type), where the reference throws. */
+ * every other type is dequantised a row at a time (dequantize_row) and dotted
+ * with fp32 X (dot_f32).
+ * `scratch_d`/`scratch_q` must hold seq*cols/32 floats and seq*cols bytes
+ * (Q4_0 only); `rowbuf` is unused (each worker allocates its own row).
+ * Returns 0, or -1 on a bad argument (cols not a multiple of the type's block
+ * size, a type the reference cannot dequantise), where the reference throws. */
 int oracle_proj_all_positions(int type, const uint8_t* W, size_t rows, size_t cols,
                               const float* X, size_t x_stride, float* Y, size_t y_stride,
                               size_t seq, float* scratch_d, int8_t* scratch_q, float* rowbuf) {
-    if (cols % 32 != 0) return -1;
     size_t row_bytes = oracle_row_bytes(type, cols);
     if (row_bytes == 0) return -1;
     size_t nb = cols / 32;
@@ -208,7 +392,7 @@ int oracle_proj_all_positions(int type, const uint8_t* W, size_t rows, size_t co
         float* rb = (float*)malloc(sizeof(float) * cols);
 #pragma omp for schedule(static)
         for (size_t r = 0; r < rows; ++r) {
-            oracle_dequant_q8_0(W + r * row_bytes, cols, rb);
+            oracle_dequantize_row(type, W + r * row_bytes, cols, rb);
             for (size_t t = 0; t < seq; ++t)
                 Y[t * y_stride + r] = oracle_dot_f32(rb, X + t * x_stride, cols);
         }
@@ -416,8 +600,7 @@ int oracle_model_forward(void* p, const int32_t* tokens, size_t seq, float* out_
     for (size_t t = 0; t < seq; ++t) {
         if (tokens[t] < 0 || (size_t)tokens[t] >= te->ne1) return -2;
         const uint8_t* row = te->data + (size_t)tokens[t] * te_row;
-        if (te->type == ORACLE_GGML_Q8_0) oracle_dequant_q8_0(row, n_embd, h + t * n_embd);
-        else oracle_dequant_q4_0(row, n_embd, h + t * n_embd);
+        oracle_dequantize_row(te->type, row, n_embd, h + t * n_embd);
     }
     float* normed = (float*)malloc(sizeof(float) * seq * n_embd);
     float* q = (float*)malloc(sizeof(float) * seq * q_dim);

@@ -63,6 +63,14 @@ def lib():
         L.oracle_proj_all_positions.argtypes = [C.c_int, _u8p, _sz, _sz, _f32p, _sz, _f32p, _sz,
                                                 _sz, _f32p, _i8p, _f32p]
         L.oracle_proj_all_positions.restype = C.c_int
+        L.oracle_bf16_to_fp32.argtypes = [C.c_uint16]
+        L.oracle_bf16_to_fp32.restype = C.c_float
+        L.oracle_dequantize_row.argtypes = [C.c_int, _u8p, _sz, _f32p]
+        L.oracle_dequantize_row.restype = C.c_int
+        L.oracle_row_bytes.argtypes = [C.c_int, _sz]
+        L.oracle_row_bytes.restype = _sz
+        L.oracle_block_elems.argtypes = [C.c_int]
+        L.oracle_block_elems.restype = _sz
         _lib = L
     return _lib
 
@@ -98,6 +106,8 @@ def ref():
         L.ref_proj_all_positions.argtypes = [C.c_void_p, _u8p, C.c_int, _sz, _sz, _f32p, _sz,
                                              _f32p, _sz, _sz]
         L.ref_proj_all_positions.restype = C.c_int
+        L.ref_dequantize_row.argtypes = [C.c_int, _u8p, _sz, _f32p]
+        L.ref_dequantize_row.restype = C.c_int
         L.ref_proj_all_positions_multi.argtypes = [
             C.c_void_p, _sz, C.POINTER(C.c_void_p), C.POINTER(C.c_int), C.POINTER(_sz),
             C.POINTER(_sz), C.POINTER(C.c_void_p), C.POINTER(_sz), _f32p, _sz, _sz]
@@ -119,6 +129,23 @@ def quantize_rows_q8_0(X: np.ndarray, cols: int | None = None):
     q = np.empty((seq, cols), np.int8)
     lib().oracle_quantize_rows_q8_0(X.reshape(-1), stride, cols, seq, d.reshape(-1), q.reshape(-1))
     return d, q
+
+
+def dequantize_row(ggml_type: int, row: np.ndarray, n: int) -> np.ndarray:
+    """Oracle fp32 values of the first n elements of raw GGUF bytes `row`."""
+    out = np.empty(max(1, n), np.float32)
+    if lib().oracle_dequantize_row(ggml_type, np.ascontiguousarray(row, np.uint8).reshape(-1), n, out) != 0:
+        raise RuntimeError(f"oracle_dequantize_row: type {ggml_type} not supported")
+    return out[:n]
+
+
+def ref_dequantize_row(ggml_type: int, row: np.ndarray, n: int) -> np.ndarray:
+    """The reference's own fwd::dequantize_row on the same bytes."""
+    out = np.empty(max(1, n), np.float32)
+    R = ref()
+    if R.ref_dequantize_row(ggml_type, np.ascontiguousarray(row, np.uint8).reshape(-1), n, out) != 0:
+        raise RuntimeError(R.ref_last_error().decode())
+    return out[:n]
 
 
 def proj_all_positions(ggml_type: int, W: np.ndarray, rows: int, cols: int, X: np.ndarray,

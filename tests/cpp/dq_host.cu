@@ -1,0 +1,39 @@
+// Host build of the device block decoders (neon_dequant.cuh's dq_sub is
+// __host__ __device__): the CPU tests decode padded device rows with the very
+// source the kernels run and compare the values with the oracle.
+#include <stdint.h>
+
+#include "neon_dequant.cuh"
+
+namespace {
+template <int TYPE>
+void decode_row(const unsigned char* row, int nu, float* out) {
+    using D = neon::DqShape<TYPE>;
+    for (int u = 0; u < nu; ++u) {
+        float w[32];
+        neon::dq_sub<TYPE>(row + (u / D::SUBS) * D::BB, u % D::SUBS, w);
+        for (int j = 0; j < 32; ++j) out[32 * u + j] = w[j];
+    }
+}
+}  // namespace
+
+// nu 32-value sub-blocks of one padded device row -> out (nu * 32 floats).
+// Returns -1 for a type the dequantising kernel does not take.
+extern "C" int dq_host_decode_row(int type, const unsigned char* row, int nu, float* out) {
+    switch (type) {
+        case NEON_GGML_F32: decode_row<NEON_GGML_F32>(row, nu, out); return 0;
+        case NEON_GGML_F16: decode_row<NEON_GGML_F16>(row, nu, out); return 0;
+        case NEON_GGML_BF16: decode_row<NEON_GGML_BF16>(row, nu, out); return 0;
+        case NEON_GGML_Q4_1: decode_row<NEON_GGML_Q4_1>(row, nu, out); return 0;
+        case NEON_GGML_Q5_0: decode_row<NEON_GGML_Q5_0>(row, nu, out); return 0;
+        case NEON_GGML_Q5_1: decode_row<NEON_GGML_Q5_1>(row, nu, out); return 0;
+        case NEON_GGML_Q4_K: decode_row<NEON_GGML_Q4_K>(row, nu, out); return 0;
+        case NEON_GGML_Q5_K: decode_row<NEON_GGML_Q5_K>(row, nu, out); return 0;
+        case NEON_GGML_Q6_K: decode_row<NEON_GGML_Q6_K>(row, nu, out); return 0;
+        default: return -1;
+    }
+}
+
+// The block geometry the upload and the launcher use (values and bytes per
+// block, blocks per chunk).
+extern "C" void dq_host_geometry(int type, int* be, int* bb, int* cb) { neon::dq_geometry(type, be, bb, cb); }

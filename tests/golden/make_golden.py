@@ -1,6 +1,7 @@
 """Generate the golden vectors in tests/golden/ from the reference itself.
 
     make -C oracle ref && python tests/golden/make_golden.py && python tests/golden/make_golden.py --decode
+    python tests/golden/make_golden.py --types
 
 Every expected output here is produced by the reference's own CPU path --
 rawllm_forward.hpp compiled with the reference's flags into
@@ -15,6 +16,9 @@ Outputs (numpy .npz, a few hundred KB in all):
   matvec.npz         Q4_0 / Q8_0 proj_all_positions cases (W bytes, X, Y)
   multi.npz          a proj_all_positions_multi case shaped like Q/K/V
   decode_tiny.npz    greedy generation of transformer_forward on a small model
+  matvec_types.npz   proj_all_positions of the nine other weight types (F32,
+                     F16, BF16, Q4_1, Q5_0, Q5_1, Q4_K, Q5_K, Q6_K) and a
+                     proj_all_positions_multi case mixing K-quants with Q4_0
 """
 from __future__ import annotations
 
@@ -130,7 +134,7 @@ def main() -> None:
     print("golden vectors written to", HERE)
 
 
-if __name__ == "__main__" and "--decode" not in sys.argv:
+if __name__ == "__main__" and "--decode" not in sys.argv and "--types" not in sys.argv:
     main()
 
 
@@ -158,3 +162,51 @@ TINY_SEED = 3
 
 if __name__ == "__main__" and "--decode" in sys.argv:
     decode_golden()
+
+
+# (type, rows, cols, seq) of the other weight types: ragged row counts, one
+# and several positions, and ragged float rows (block size 1).
+TYPE_CASES = []
+for _t in (S.GGML_Q4_1, S.GGML_Q5_0, S.GGML_Q5_1):
+    TYPE_CASES += [(_t, 37, 512, 1), (_t, 9, 96, 2)]
+for _t in (S.GGML_Q4_K, S.GGML_Q5_K, S.GGML_Q6_K):
+    TYPE_CASES += [(_t, 21, 512, 1), (_t, 6, 256, 3)]
+for _t in (S.GGML_F32, S.GGML_F16, S.GGML_BF16):
+    TYPE_CASES += [(_t, 33, 512, 1), (_t, 13, 45, 2)]
+
+
+def types_golden() -> None:
+    pool = O.RefPool(4)
+    out = {}
+    for i, (typ, rows, cols, seq) in enumerate(TYPE_CASES):
+        W = S.weights(typ, rows, cols, seed=4000 + i)
+        X = S.activations(seq, cols, seed=5000 + i)
+        Y = np.zeros((seq, rows), np.float32)
+        pool.proj_all_positions(typ, W, rows, cols, X, Y)
+        out[f"c{i}_meta"] = np.array([typ, rows, cols, seq], np.int64)
+        out[f"c{i}_W"] = W
+        out[f"c{i}_X"] = X
+        out[f"c{i}_Y"] = Y
+    out["n"] = np.array(len(TYPE_CASES))
+    # a K-quant model's Q/K/V: Q4_K, Q6_K and a Q4_0 target sharing X
+    cols, seq = 512, 2
+    specs = [(S.GGML_Q4_K, 64), (S.GGML_Q6_K, 32), (S.GGML_Q4_0, 32)]
+    X = S.activations(seq, cols, seed=6000)
+    targets = []
+    for j, (typ, rows) in enumerate(specs):
+        W = S.weights(typ, rows, cols, seed=6100 + j)
+        targets.append((typ, W, rows, cols, np.zeros((seq, rows), np.float32)))
+        out[f"m{j}_meta"] = np.array([typ, rows, cols], np.int64)
+        out[f"m{j}_W"] = W
+    pool.proj_all_positions_multi(targets, X)
+    for j, t in enumerate(targets):
+        out[f"m{j}_Y"] = t[4]
+    out["mX"] = X
+    out["m_n"] = np.array(len(specs))
+    pool.close()
+    np.savez_compressed(os.path.join(HERE, "matvec_types.npz"), **out)
+    print("wrote", os.path.join(HERE, "matvec_types.npz"))
+
+
+if __name__ == "__main__" and "--types" in sys.argv:
+    types_golden()

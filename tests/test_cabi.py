@@ -55,7 +55,14 @@ def test_upload_argument_checks_precede_device_use():
     raw = np.zeros(64, np.uint8)
     assert L.neon_cuda_upload(raw.ctypes.data, 2, 1, 31, 0, 0, 1, ctypes.byref(h)) == -1
     assert b"multiple of its quant block size" in L.neon_cuda_last_error()
-    assert L.neon_cuda_upload(raw.ctypes.data, 12, 1, 256, 0, 0, 1, ctypes.byref(h)) == -2
+    # types the reference does not dequantise either (Q8_1, Q2_K, Q3_K, IQ4_NL)
+    for t in (9, 10, 11, 25):
+        assert L.neon_cuda_upload(raw.ctypes.data, t, 1, 256, 0, 0, 1, ctypes.byref(h)) == -2
+    # K-quants: 256-value super-blocks; float types: any input dim passes the check
+    assert L.neon_cuda_upload(raw.ctypes.data, 12, 1, 96, 0, 0, 1, ctypes.byref(h)) == -1
+    assert b"quant block size (256)" in L.neon_cuda_last_error()
+    assert L.neon_cuda_upload(raw.ctypes.data, 14, 4, 256, 1, 3, 2, ctypes.byref(h)) == -1  # bad shard
+    assert L.neon_cuda_upload(raw.ctypes.data, 1, 2, 45, 2, 0, 2, ctypes.byref(h)) == -2  # ragged column split
     assert L.neon_cuda_upload(None, 2, 1, 32, 0, 0, 1, ctypes.byref(h)) == -1
     assert L.neon_cuda_upload(raw.ctypes.data, 2, 4, 32, 1, 3, 2, ctypes.byref(h)) == -1
     assert L.neon_cuda_matvec(None, None, 0, None, 0, 1, None) == -1

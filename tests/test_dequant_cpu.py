@@ -1,0 +1,89 @@
+"""The block decoders of the dequantising kernel (F32, F16, BF16, Q4_1, Q5_0,
+Q5_1, Q4_K, Q5_K, Q6_K), built for the host from the same source the sm_100a
+kernels compile (neon_dequant.cuh: dq_sub is __host__ __device__), decode the
+device layout -- the GGUF rows at a 16-byte pitch, float rows zero-padded to
+32-value blocks -- to exactly the oracle's values (dequantize_row,
+rawllm_forward.hpp:301-321, itself pinned bit-exact to the reference)."""
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+import pytest
+
+import oracle as O
+import synth as S
+from conftest import PKG, ROOT
+
+DQ_TYPES = [t for t in S.ALL_TYPES if t not in (S.GGML_Q4_0, S.GGML_Q8_0)]
+
+
+@pytest.fixture(scope="module")
+def dq(tmp_path_factory):
+    so = str(tmp_path_factory.mktemp("dqhost") / "libdqhost.so")
+    nvcc = os.path.join(os.environ.get("CUDA_HOME", "/usr/local/cuda"), "bin", "nvcc")
+    subprocess.check_call([nvcc if os.path.exists(nvcc) else "nvcc", "-gencode", "arch=compute_100a,code=sm_100a",
+                           "-std=c++17", "-O2", "-shared", "-Xcompiler", "-fPIC", "-Xcompiler", "-ffp-contract=off",
+                           "-I", os.path.join(ROOT, "include"), "-I", os.path.join(PKG, "csrc"),
+                           os.path.join(ROOT, "tests", "cpp", "dq_host.cu"), "-o", so])
+    L = C.CDLL(so)
+    L.dq_host_decode_row.argtypes = [C.c_int, C.c_void_p, C.c_int, C.c_void_p]
+    L.dq_host_geometry.argtypes = [C.c_int, C.POINTER(C.c_int), C.POINTER(C.c_int), C.POINTER(C.c_int)]
+    return L
+
+
+def geometry(L, t):
+    be, bb, cb = C.c_int(), C.c_int(), C.c_int()
+    L.dq_host_geometry(t, C.byref(be), C.byref(bb), C.byref(cb))
+    return be.value, bb.value, cb.value
+
+
+def device_row(L, t, row, cols):
+    """One GGUF row laid out as the upload stores it: zero-padded to whole
+    32-value blocks (float types) and to a 16-byte pitch."""
+    be, bb, _ = geometry(L, t)
+    nu = (cols + 31) // 32
+    pitch = (nu // (be // 32) * bb + 15) & ~15
+    buf = np.zeros(pitch, np.uint8)
+    buf[:row.size] = row
+    return buf, nu
+
+
+def same(a, b):
+    ua, ub = a.view(np.uint32), b.view(np.uint32)
+    return (ua == ub) | (np.isnan(a) & np.isnan(b))
+
+
+@pytest.mark.parametrize("typ", DQ_TYPES, ids=lambda t: S.TYPE_NAMES[t])
+def test_device_decoder_matches_oracle(dq, typ):
+    for cols in (512, 4096):
+        synth = S.weights(typ, 8, cols, seed=11)
+        rand = np.random.default_rng(typ).integers(0, 256, synth.shape, dtype=np.uint8)  # NaN/Inf/subnormal scales
+        for M in (synth, rand):
+            for r in range(M.shape[0]):
+                buf, nu = device_row(dq, typ, M[r], cols)
+                out = np.empty(nu * 32, np.float32)
+                assert dq.dq_host_decode_row(typ, buf.ctypes.data, nu, out.ctypes.data) == 0
+                assert same(out[:cols], O.dequantize_row(typ, M[r], cols)).all(), (S.TYPE_NAMES[typ], cols, r)
+
+
+@pytest.mark.parametrize("typ", [S.GGML_F32, S.GGML_F16, S.GGML_BF16], ids=lambda t: S.TYPE_NAMES[t])
+def test_ragged_float_rows_pad_with_zeros(dq, typ):
+    cols = 45  # block size 1: any input dim is a valid float tensor
+    W = S.weights(typ, 3, cols, seed=2)
+    for r in range(3):
+        buf, nu = device_row(dq, typ, W[r], cols)
+        out = np.empty(nu * 32, np.float32)
+        dq.dq_host_decode_row(typ, buf.ctypes.data, nu, out.ctypes.data)
+        assert same(out[:cols], O.dequantize_row(typ, W[r], cols)).all()
+        assert not out[cols:].any()
+
+
+def test_chunks_stay_16_byte_aligned(dq):
+    # every chunk of CB blocks starts on a 16-byte boundary of a row (the
+    # 128-bit loads), and a chunk is 32 (or 64 for super-blocks) sub-blocks
+    for t in DQ_TYPES:
+        be, bb, cb = geometry(dq, t)
+        assert (cb * bb) % 16 == 0 and cb * (be // 32) in (32, 64), S.TYPE_NAMES[t]
+        assert bb == S.BLOCK_BYTES[t] * (32 if S.BLOCK_ELEMS[t] == 1 else 1)
+    assert geometry(dq, S.GGML_Q4_0) == (0, 0, 0)

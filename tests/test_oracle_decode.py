@@ -150,3 +150,24 @@ def test_kv_cache_shift_matches_reference():
         assert np.array_equal(bits(k1), bits(k2)) and np.array_equal(bits(v1), bits(v2))
     la, lb = a.forward(np.array([5], np.int32)), b.forward(np.array([5], np.int32))
     assert np.array_equal(bits(la), bits(lb))
+
+
+@ref_only
+@pytest.mark.parametrize("wtype,etype,tied", [
+    (S.GGML_Q4_K, S.GGML_Q6_K, False),   # the converter's K-quant output (nanity_convert.py:409-421)
+    (S.GGML_Q5_K, S.GGML_Q5_K, True),
+    (S.GGML_Q6_K, S.GGML_Q4_K, True),
+    (S.GGML_Q4_1, S.GGML_Q5_0, True),
+    (S.GGML_Q5_1, S.GGML_F16, True),
+    (S.GGML_F16, S.GGML_BF16, True),
+    (S.GGML_BF16, S.GGML_F32, False),
+], ids=lambda v: S.TYPE_NAMES.get(v, str(v)) if not isinstance(v, bool) else ("tied" if v else "untied"))
+def test_model_forward_other_types_matches_reference(wtype, etype, tied):
+    """transformer_forward over every other weight type (projections, embedding
+    and lm_head through dequantize_row + dot_f32), bit for bit."""
+    tensors = list(S.model_tensors(TINY, seed=13, wtype=wtype, embd_type=etype, tied=tied))
+    mo, mr = O.Model(TINY, tensors, "port"), O.Model(TINY, tensors, "reference", threads=4)
+    p = S.prompt_tokens(7, TINY.n_vocab, 14)
+    ta, la = mo.generate_greedy(p, 5)
+    tb, lb = mr.generate_greedy(p, 5)
+    assert np.array_equal(ta, tb) and np.array_equal(bits(la), bits(lb))

@@ -54,3 +54,17 @@ def test_bad_cols_rejected():
                                            np.zeros(1, np.float32), 1, 1, np.zeros(1, np.float32),
                                            np.zeros(31, np.int8), np.zeros(31, np.float32))
     assert rc == -1
+
+
+def test_other_types_bitexact():
+    """F32/F16/BF16, Q4_1/Q5_0/Q5_1 and the K-quants: dequantize_row + dot_f32
+    (rawllm_forward.hpp:597-605) against the reference's outputs."""
+    g = load_golden("matvec_types.npz")
+    for i in range(int(g["n"])):
+        typ, rows, cols, seq = (int(v) for v in g[f"c{i}_meta"])
+        Y = O.proj_all_positions(typ, g[f"c{i}_W"], rows, cols, g[f"c{i}_X"])
+        assert np.array_equal(bits(Y), bits(g[f"c{i}_Y"])), f"case {i} type {typ} {rows}x{cols} seq {seq}"
+    for j in range(int(g["m_n"])):
+        typ, rows, cols = (int(v) for v in g[f"m{j}_meta"])
+        Y = O.proj_all_positions(typ, g[f"m{j}_W"], rows, cols, g["mX"])
+        assert np.array_equal(bits(Y), bits(g[f"m{j}_Y"]))
