@@ -208,8 +208,9 @@ typedef struct neon_model* neon_model_t;
  * + KVCache (NEON-3.cpp:535-564). */
 NEON_API int neon_cuda_model_create(const neon_model_config_t* cfg, neon_model_t* out);
 
-/* Upload one tensor (GGUF bytes; ne1 = 0 for a 1-D norm weight). Projection
- * and embedding tensors are Q4_0 or Q8_0, norm weights F32. */
+/* Upload one tensor (GGUF bytes; ne1 = 0 for a 1-D norm weight). Projection,
+ * embedding and lm_head tensors may be any NEON_GGML_* type above (ffn_gate
+ * and ffn_up of one layer share theirs); norm weights are F32. */
 NEON_API int neon_cuda_model_set_tensor(neon_model_t m, int role, int layer, const uint8_t* host_bytes,
                                         size_t nbytes, int ggml_type, size_t ne0, size_t ne1);
 

@@ -441,6 +441,9 @@ int launch_dq(const std::vector<const neon_proj_target_t*>& t, int type, size_t 
             a.s.peer_mode = ext->peer_mode;
             if (ext->peer_mode) a.s.peer = ext->peer;
         }
+        // 128-bit X staging: X, every position's row and the norm weights 16-byte aligned
+        a.s.x_vec = (reinterpret_cast<uintptr_t>(dX) % 16) == 0 && (seq == 1 || x_stride % 4 == 0) &&
+                    (!a.s.norm_w || (reinterpret_cast<uintptr_t>(a.s.norm_w) % 16) == 0);
         a.pitch = (long long)t[start]->W->pitch;
         a.x_stride = (long long)x_stride;
         a.cols = (int)cols;

@@ -19,19 +19,23 @@
 // row per warp. A warp walks its row a chunk at a time: the chunk's bytes are
 // read with coalesced 128-bit loads (the next chunk's loads are in flight
 // while the current one is decoded), parked in the warp's shared-memory
-// buffer, and every lane then decodes whole 32-value sub-blocks from it (one
+// buffer, and every lane then takes whole 32-value sub-blocks from it (one
 // for the 32-value types, two for the K-quants: 8 super-blocks = 64
-// sub-blocks a chunk) and takes their dot products with X, which the CTA
-// staged once in shared memory (fp32, 36-float pitch per 32 values, so the
-// lanes' 128-bit reads of consecutive sub-blocks do not collide). A butterfly
-// shuffle finishes each row; the decode-step epilogues are the one-position
-// kernel's (stream_epilogue).
+// sub-blocks a chunk): their integer codes and affine map (dq_codes), and
+// the dot product a*sum((code - OFF)*x) + b*sum(x) on packed fp32 pairs
+// (dq_code_dot) against X, which the CTA staged once in shared memory (fp32,
+// 36-float pitch per 32 values, so the lanes' 128-bit reads of consecutive
+// sub-blocks do not collide; the spare float holds the sub-block's sum).
+// The float types skip shared memory: each lane multiplies the 16-byte words
+// it loaded. A butterfly shuffle finishes each row; the decode-step
+// epilogues are the one-position kernel's (stream_epilogue).
 //
-// Every decoded value equals the reference's bit for bit: each is one exact
-// product (at most 23 significant bits: fp16 scale x 6-bit sub-scale x 6-bit
-// quant) plus at most one rounded add, so fused or separate multiply-adds
-// give the same float. Only the order of the dot product's additions differs
-// from dot_f32's.
+// Every weight the decoders form equals the reference's bit for bit (dq_sub:
+// one exact product -- at most 23 significant bits, fp16 scale x 6-bit
+// sub-scale x 6-bit quant -- plus at most one rounded add); the kernel's dot
+// product regroups the same sum: per sub-block a*sum((code-OFF)*x) + b*sum(x)
+// instead of sum((a*(code-OFF)+b)*x), and its additions run in another order
+// than dot_f32's.
 #pragma once
 
 #include <string.h>
@@ -120,6 +124,22 @@ __host__ __device__ __forceinline__ float sh_half(const unsigned char* p) {
     return __half2float(__ushort_as_half((unsigned short)sh_u16(p)));
 }
 
+// The value of byte i of u minus OFF, exactly. On the device the word
+// 0x4B0000vv, read as a float, is 2^23 + v, and one exact subtraction leaves
+// v - OFF: no integer-to-float conversion instruction (those issue at a
+// fraction of the FMA rate).
+template <int OFF>
+__host__ __device__ __forceinline__ float byte_val(uint32_t u, int i) {
+#ifdef __CUDA_ARCH__
+    return __int_as_float(__byte_perm(u, 0x4B000000u, 0x7650 + i)) - (8388608.0f + (float)OFF);
+#else
+    return (float)((int)((u >> (8 * i)) & 0xFFu) - OFF);
+#endif
+}
+
+// Bits 0-3 of x to bit 0 of bytes 0-3 (the four shifted copies never overlap).
+__host__ __device__ __forceinline__ uint32_t spread4(uint32_t x) { return (x * 0x00204081u) & 0x01010101u; }
+
 // The (scale, min) pair of sub-block s of a Q4_K / Q5_K super-block from its
 // 12 packed bytes (get_scale_min_k4, rawllm_forward.hpp:224-233): sub-blocks
 // 0-3 use the low six bits of bytes s and s+4; 4-7 take a nibble of byte s+4
@@ -134,16 +154,97 @@ __host__ __device__ __forceinline__ void k4_scale_min(const unsigned char* sc, i
     }
 }
 
-// The 32 values of sub-block s of the block at `blk` (shared or global memory,
-// aligned as a block of the padded-row layout is).
-// Formulas of rawllm_forward.hpp, regrouped by sub-block:
-//   F16 / BF16 / F32  :133-141
+// The 32 integer codes of sub-block s of a block type, four per word in
+// value order (value 4k + i in byte i of v[k]), and the affine map back to
+// weights: value = a * (code - OFF) + b, with a = a0 for values 0-15 and a1
+// for 16-31 (they differ only for Q6_K's 16-value scales). Formulas of
+// rawllm_forward.hpp, regrouped by sub-block:
 //   Q4_1 :164-175  d*q + m             Q5_0 :177-191  d*(q - 16), q = nibble | qh bit << 4
 //   Q5_1 :193-208  d*q + m (q as Q5_0)
 //   Q4_K :235-253  (d*sc)*q - dmin*mn on nibble (s&1) of bytes 32*(s/2)..
 //   Q5_K :255-275  as Q4_K, q += 16 * bit s of qh[l]
 //   Q6_K :277-298  (d*sc)*(q - 32); sub-block s = 4h + k: low bytes 64h + 32(k&1)..,
 //                  high nibble when k >= 2, 2-bit pair k of qh[32h + l], scales 8h + 2k + l/16
+template <int TYPE> struct DqCode {
+    static constexpr int OFF = TYPE == NEON_GGML_Q5_0 ? 16 : TYPE == NEON_GGML_Q6_K ? 32 : 0;
+    static constexpr bool HAS_B = TYPE == NEON_GGML_Q4_1 || TYPE == NEON_GGML_Q5_1 ||
+                                  TYPE == NEON_GGML_Q4_K || TYPE == NEON_GGML_Q5_K;
+    uint32_t v[8];
+    float a0, a1, b;
+};
+
+template <int TYPE>
+__host__ __device__ __forceinline__ void dq_codes(const unsigned char* blk, int s, DqCode<TYPE>& c) {
+    if constexpr (TYPE == NEON_GGML_Q4_1 || TYPE == NEON_GGML_Q5_1) {
+        // 4-byte aligned blocks (20 / 24 bytes)
+        constexpr bool five = TYPE == NEON_GGML_Q5_1;
+        c.a0 = c.a1 = sh_half(blk);
+        c.b = sh_half(blk + 2);
+        const uint32_t qh = five ? sh_u32(blk + 4) : 0u;
+        const unsigned char* qs = blk + (five ? 8 : 4);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint32_t q4 = sh_u32(qs + 4 * k);
+            uint32_t lo = q4 & 0x0F0F0F0Fu, hi = (q4 >> 4) & 0x0F0F0F0Fu;
+            if (five) {
+                lo |= spread4((qh >> (4 * k)) & 0xFu) << 4;
+                hi |= spread4((qh >> (4 * k + 16)) & 0xFu) << 4;
+            }
+            c.v[k] = lo;
+            c.v[k + 4] = hi;
+        }
+    } else if constexpr (TYPE == NEON_GGML_Q5_0) {
+        // 22-byte blocks: only 2-byte alignment
+        c.a0 = c.a1 = sh_half(blk);
+        c.b = 0.f;
+        const uint32_t qh = sh_u16(blk + 2) | (sh_u16(blk + 4) << 16);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint32_t q4 = sh_u16(blk + 6 + 4 * k) | (sh_u16(blk + 8 + 4 * k) << 16);
+            c.v[k] = (q4 & 0x0F0F0F0Fu) | (spread4((qh >> (4 * k)) & 0xFu) << 4);
+            c.v[k + 4] = ((q4 >> 4) & 0x0F0F0F0Fu) | (spread4((qh >> (4 * k + 16)) & 0xFu) << 4);
+        }
+    } else if constexpr (TYPE == NEON_GGML_Q4_K || TYPE == NEON_GGML_Q5_K) {
+        // 16-byte aligned super-blocks (144 / 176 bytes)
+        constexpr bool five = TYPE == NEON_GGML_Q5_K;
+        const float d = sh_half(blk), dmin = sh_half(blk + 2);
+        int sc, mn;
+        k4_scale_min(blk + 4, s, sc, mn);
+        c.a0 = c.a1 = NEON_HD_MUL(d, (float)sc);
+        c.b = -NEON_HD_MUL(dmin, (float)mn);
+        const unsigned char* q = blk + (five ? 48 : 16) + 32 * (s >> 1);
+        const int shift = (s & 1) * 4;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            uint32_t v = (sh_u32(q + 4 * k) >> shift) & 0x0F0F0F0Fu;
+            if (five) v |= ((sh_u32(blk + 16 + 4 * k) >> s) & 0x01010101u) << 4;
+            c.v[k] = v;
+        }
+    } else if constexpr (TYPE == NEON_GGML_Q6_K) {
+        // 210-byte super-blocks: only 2-byte alignment
+        const int h = s >> 2, k = s & 3;
+        const unsigned char* ql = blk + 64 * h + 32 * (k & 1);
+        const unsigned char* qh = blk + 128 + 32 * h;
+        const signed char* scp = reinterpret_cast<const signed char*>(blk + 192 + 8 * h + 2 * k);
+        const float d = sh_half(blk + 208);
+        c.a0 = NEON_HD_MUL(d, (float)scp[0]);
+        c.a1 = NEON_HD_MUL(d, (float)scp[1]);
+        c.b = 0.f;
+        const int lshift = (k >> 1) * 4, hshift = 2 * k;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const uint32_t l4 = sh_u16(ql + 4 * j) | (sh_u16(ql + 4 * j + 2) << 16);
+            const uint32_t h4 = sh_u16(qh + 4 * j) | (sh_u16(qh + 4 * j + 2) << 16);
+            c.v[j] = ((l4 >> lshift) & 0x0F0F0F0Fu) | (((h4 >> hshift) & 0x03030303u) << 4);
+        }
+    }
+}
+
+// The 32 values of sub-block s of the block at `blk` (shared or global memory,
+// aligned as a block of the padded-row layout is): the float types' words, or
+// a * (code - OFF) + b of the block types. Each value is the reference's bit
+// for bit: a * (code - OFF) is exact, so one fused multiply-add rounds once,
+// as the reference's multiply (exact) and add do; types without b multiply.
 template <int TYPE>
 __host__ __device__ __forceinline__ void dq_sub(const unsigned char* blk, int s, float (&w)[32]) {
     if constexpr (TYPE == NEON_GGML_F32) {
@@ -173,108 +274,104 @@ __host__ __device__ __forceinline__ void dq_sub(const unsigned char* blk, int s,
                 }
             }
         }
-    } else if constexpr (TYPE == NEON_GGML_Q4_1 || TYPE == NEON_GGML_Q5_1) {
-        // 4-byte aligned blocks (20 / 24 bytes)
-        constexpr bool five = TYPE == NEON_GGML_Q5_1;
-        const float d = sh_half(blk), m = sh_half(blk + 2);
-        const uint32_t qh = five ? sh_u32(blk + 4) : 0u;
-        const unsigned char* qs = blk + (five ? 8 : 4);
+    } else {
+        DqCode<TYPE> c;
+        dq_codes<TYPE>(blk, s, c);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const uint32_t q4 = sh_u32(qs + 4 * k);
+        for (int k = 0; k < 8; ++k)
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                const int j = 4 * k + i;
-                int lo = (q4 >> (8 * i)) & 0x0F, hi = (q4 >> (8 * i + 4)) & 0x0F;
-                if (five) {
-                    lo |= ((qh >> j) & 1u) << 4;
-                    hi |= ((qh >> (j + 16)) & 1u) << 4;
-                }
-                w[j] = fmaf(d, (float)lo, m);
-                w[j + 16] = fmaf(d, (float)hi, m);
+                const float q = byte_val<DqCode<TYPE>::OFF>(c.v[k], i);
+                // no additive term: a plain product, as the reference's (keeps -0)
+                w[4 * k + i] = DqCode<TYPE>::HAS_B ? fmaf(k < 4 ? c.a0 : c.a1, q, c.b)
+                                                   : NEON_HD_MUL(k < 4 ? c.a0 : c.a1, q);
             }
-        }
-    } else if constexpr (TYPE == NEON_GGML_Q5_0) {
-        // 22-byte blocks: only 2-byte alignment
-        const float d = sh_half(blk);
-        const uint32_t qh = sh_u16(blk + 2) | (sh_u16(blk + 4) << 16);
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            const uint32_t q2 = sh_u16(blk + 6 + 2 * k);
-#pragma unroll
-            for (int i = 0; i < 2; ++i) {
-                const int j = 2 * k + i;
-                const int lo = ((q2 >> (8 * i)) & 0x0F) | (((qh >> j) & 1u) << 4);
-                const int hi = ((q2 >> (8 * i + 4)) & 0x0F) | (((qh >> (j + 16)) & 1u) << 4);
-                w[j] = NEON_HD_MUL(d, (float)(lo - 16));
-                w[j + 16] = NEON_HD_MUL(d, (float)(hi - 16));
-            }
-        }
-    } else if constexpr (TYPE == NEON_GGML_Q4_K || TYPE == NEON_GGML_Q5_K) {
-        // 16-byte aligned super-blocks (144 / 176 bytes)
-        constexpr bool five = TYPE == NEON_GGML_Q5_K;
-        const float d = sh_half(blk), dmin = sh_half(blk + 2);
-        int sc, mn;
-        k4_scale_min(blk + 4, s, sc, mn);
-        const float ds = NEON_HD_MUL(d, (float)sc), ms = NEON_HD_MUL(dmin, (float)mn);
-        const unsigned char* q = blk + (five ? 48 : 16) + 32 * (s >> 1);
-        const int shift = (s & 1) * 4;
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            const uint32_t q4 = sh_u32(q + 4 * k);
-            const uint32_t h4 = five ? sh_u32(blk + 16 + 4 * k) : 0u;
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                int v = (q4 >> (8 * i + shift)) & 0x0F;
-                if (five) v |= ((h4 >> (8 * i + s)) & 1u) << 4;
-                w[4 * k + i] = fmaf(ds, (float)v, -ms);
-            }
-        }
-    } else if constexpr (TYPE == NEON_GGML_Q6_K) {
-        // 210-byte super-blocks: only 2-byte alignment
-        const int h = s >> 2, k = s & 3;
-        const unsigned char* ql = blk + 64 * h + 32 * (k & 1);
-        const unsigned char* qh = blk + 128 + 32 * h;
-        const signed char* scp = reinterpret_cast<const signed char*>(blk + 192 + 8 * h + 2 * k);
-        const float d = sh_half(blk + 208);
-        const float d0 = NEON_HD_MUL(d, (float)scp[0]), d1 = NEON_HD_MUL(d, (float)scp[1]);
-        const int lshift = (k >> 1) * 4, hshift = 2 * k;
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-            const uint32_t l2 = sh_u16(ql + 2 * j), h2 = sh_u16(qh + 2 * j);
-#pragma unroll
-            for (int i = 0; i < 2; ++i) {
-                const int l = 2 * j + i;
-                const int q = (int)((((l2 >> (8 * i + lshift)) & 0x0F) | (((h2 >> (8 * i + hshift)) & 3u) << 4))) - 32;
-                w[l] = NEON_HD_MUL(l < 16 ? d0 : d1, (float)q);
-            }
-        }
     }
 }
 
-// sum_j w[j] * x[j] for one 32-value sub-block (x: 32 floats, 16-byte aligned).
-__device__ __forceinline__ float dq_dot32(const float (&w)[32], const float* x) {
-    const float4* x4 = reinterpret_cast<const float4*>(x);
-    float s0 = 0.f, s1 = 0.f;
+// The dot product of a block-type sub-block with 32 floats of X (shared
+// memory, 16-byte aligned), without forming the weights:
+//     sum_j (a*(code_j - OFF) + b) * x_j = a * sum_j (code_j - OFF) * x_j + b * xsum
+// with xsum = sum_j x_j (staged with X). The inner sum runs on packed fp32
+// pairs (two values per fma.rn.f32x2); codes become floats exactly through
+// the 2^23 bias. The host build runs the same operations one lane at a time,
+// so its results equal the device's bit for bit.
+#ifdef __CUDA_ARCH__
+#define NEON_PAIR unsigned long long
+#define NEON_PAIR_ZERO 0ull
+__device__ __forceinline__ NEON_PAIR pair_bias(uint32_t v, int half, float bias) {
+    // bytes 2*half, 2*half+1 of v as 2^23 + code, minus the bias 2^23 + OFF
+    unsigned long long p;
+    if (half == 0)
+        asm("{ .reg .b32 lo, hi; prmt.b32 lo, %1, 0x4B000000, 0x7650; prmt.b32 hi, %1, 0x4B000000, 0x7651; "
+            "mov.b64 %0, {lo, hi}; }" : "=l"(p) : "r"(v));
+    else
+        asm("{ .reg .b32 lo, hi; prmt.b32 lo, %1, 0x4B000000, 0x7652; prmt.b32 hi, %1, 0x4B000000, 0x7653; "
+            "mov.b64 %0, {lo, hi}; }" : "=l"(p) : "r"(v));
+    const uint32_t nb = __float_as_uint(-bias);
+    return f32x2_add(p, ((unsigned long long)nb << 32) | nb);
+}
+__device__ __forceinline__ NEON_PAIR pair_fma(NEON_PAIR a, NEON_PAIR b, NEON_PAIR c) { return f32x2_fma(a, b, c); }
+__device__ __forceinline__ float pair_sum(NEON_PAIR p) {
+    return __uint_as_float((uint32_t)p) + __uint_as_float((uint32_t)(p >> 32));
+}
+__device__ __forceinline__ void x_pairs(const float* x, int k, NEON_PAIR& p0, NEON_PAIR& p1) {
+    const ulonglong2 t = reinterpret_cast<const ulonglong2*>(x)[k];
+    p0 = t.x;
+    p1 = t.y;
+}
+#else
+struct NeonPair {
+    float lo, hi;
+};
+#define NEON_PAIR NeonPair
+#define NEON_PAIR_ZERO NeonPair{0.f, 0.f}
+inline NeonPair pair_bias(uint32_t v, int half, float bias) {
+    const float b0 = (float)((v >> (16 * half)) & 0xFFu) + 8388608.0f;  // exact
+    const float b1 = (float)((v >> (16 * half + 8)) & 0xFFu) + 8388608.0f;
+    return NeonPair{b0 - bias, b1 - bias};
+}
+inline NeonPair pair_fma(NeonPair a, NeonPair b, NeonPair c) { return NeonPair{fmaf(a.lo, b.lo, c.lo), fmaf(a.hi, b.hi, c.hi)}; }
+inline float pair_sum(NeonPair p) { return p.lo + p.hi; }
+inline void x_pairs(const float* x, int k, NeonPair& p0, NeonPair& p1) {
+    p0 = NeonPair{x[4 * k], x[4 * k + 1]};
+    p1 = NeonPair{x[4 * k + 2], x[4 * k + 3]};
+}
+#endif
+
+template <int TYPE>
+__host__ __device__ __forceinline__ float dq_code_dot(const DqCode<TYPE>& c, const float* x, float xsum) {
+    constexpr float bias = 8388608.0f + (float)DqCode<TYPE>::OFF;
+    NEON_PAIR s0 = NEON_PAIR_ZERO, s1 = NEON_PAIR_ZERO;  // values 0-15, 16-31
 #pragma unroll
-    for (int k = 0; k < 8; k += 2) {
-        const float4 a = x4[k], b = x4[k + 1];
-        s0 = fmaf(w[4 * k], a.x, s0);
-        s1 = fmaf(w[4 * k + 4], b.x, s1);
-        s0 = fmaf(w[4 * k + 1], a.y, s0);
-        s1 = fmaf(w[4 * k + 5], b.y, s1);
-        s0 = fmaf(w[4 * k + 2], a.z, s0);
-        s1 = fmaf(w[4 * k + 6], b.z, s1);
-        s0 = fmaf(w[4 * k + 3], a.w, s0);
-        s1 = fmaf(w[4 * k + 7], b.w, s1);
+    for (int k = 0; k < 8; ++k) {
+        NEON_PAIR x0, x1;
+        x_pairs(x, k, x0, x1);
+        if (k < 4) {
+            s0 = pair_fma(pair_bias(c.v[k], 0, bias), x0, s0);
+            s0 = pair_fma(pair_bias(c.v[k], 1, bias), x1, s0);
+        } else {
+            s1 = pair_fma(pair_bias(c.v[k], 0, bias), x0, s1);
+            s1 = pair_fma(pair_bias(c.v[k], 1, bias), x1, s1);
+        }
     }
-    return s0 + s1;
+    if constexpr (TYPE == NEON_GGML_Q6_K) return fmaf(c.a0, pair_sum(s0), NEON_HD_MUL(c.a1, pair_sum(s1)));
+    const float dot = NEON_HD_MUL(c.a0, pair_sum(s0) + pair_sum(s1));
+    if constexpr (DqCode<TYPE>::HAS_B) return fmaf(c.b, xsum, dot);
+    return dot;
 }
 
 // T positions per CTA (grid.y tiles the positions); one row per warp.
+//
+// Every warp holds two chunks of its row in registers: the loads of chunk
+// i + 2 go out as soon as chunk i has left its registers -- parked in the
+// warp's shared-memory buffer for the block types, consumed in place for the
+// float types, whose lanes take the 16-byte words l, l + 32, ... of a chunk
+// and so read X without bank conflicts.
 template <int TYPE, int T>
 __global__ void __launch_bounds__(kThreads) matvec_dq_kernel(const __grid_constant__ DqArgs a) {
     using D = DqShape<TYPE>;
+    constexpr bool kFloat = TYPE == NEON_GGML_F32 || TYPE == NEON_GGML_F16 || TYPE == NEON_GGML_BF16;
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ float rowv[2][T][kWarps];   // by tile parity: a tile's results never wait on the last epilogue
     __shared__ double dscratch[32];
@@ -297,8 +394,7 @@ __global__ void __launch_bounds__(kThreads) matvec_dq_kernel(const __grid_consta
         chunk = item % nch;
         nblk_c = min(D::CB, a.nblk - chunk * D::CB);
     };
-    uint4 pre[D::WPL];
-    auto load = [&](int item) {
+    auto load = [&](uint4 (&buf)[D::WPL], int item) {
         int span, row0, chunk, nblk_c;
         locate(item, span, row0, chunk, nblk_c);
         const int row = row0 + warp;
@@ -308,12 +404,14 @@ __global__ void __launch_bounds__(kThreads) matvec_dq_kernel(const __grid_consta
 #pragma unroll
         for (int k = 0; k < D::WPL; ++k) {
             const int wi = lane + 32 * k;
-            if (wi < words) pre[k] = ld_weights_u4(src + 16 * wi);
+            if (wi < words) buf[k] = ld_weights_u4(src + 16 * wi);
         }
     };
-    // weights are never written by an earlier kernel of the stream: their
-    // first loads go out before the dependency wait
-    if (n_items > 0) load(0);
+    // weights are never written by an earlier kernel of the stream: the first
+    // two chunks' loads go out before the dependency wait
+    uint4 bufA[D::WPL], bufB[D::WPL];
+    if (n_items > 0) load(bufA, 0);
+    if (n_items > 1) load(bufB, 1);
     pdl_wait();
 
     const unsigned int peer_call =
@@ -322,56 +420,151 @@ __global__ void __launch_bounds__(kThreads) matvec_dq_kernel(const __grid_consta
     if (a.s.rope_cs)
         for (int i = threadIdx.x; i < a.s.rope_half; i += kThreads) rcs[i] = a.s.rope_cs[(long long)pos * a.s.rope_half + i];
 
-    // X of this CTA's positions (rms-normalised first when asked; one position then)
+    // X of this CTA's positions (rms-normalised first when asked; one position
+    // then), zero past `cols`; 128-bit loads, several in flight per thread
     {
         const float nscale = a.s.norm_w ? cta_rms_scale(a.s.x, a.cols, a.s.norm_eps, dscratch) : 1.f;
         for (int t = 0; t < npos; ++t) {
             const float* xp = a.s.x + (long long)(p0 + t) * a.x_stride;
             float* xd = xs + (long long)t * nu * kQ8Pitch;
-            for (int i = threadIdx.x; i < nu * 32; i += kThreads) {
-                float v = 0.f;
-                if (i < a.cols) {
-                    v = __ldg(xp + i);
-                    if (a.s.norm_w) v = __fmul_rn(__fmul_rn(v, nscale), __ldg(a.s.norm_w + i));
+            if (a.s.x_vec) {
+                const int n4 = a.cols >> 2;
+#pragma unroll 4
+                for (int i4 = threadIdx.x; i4 < n4; i4 += kThreads) {
+                    float4 v = __ldg(reinterpret_cast<const float4*>(xp) + i4);
+                    if (a.s.norm_w) {
+                        const float4 g = __ldg(reinterpret_cast<const float4*>(a.s.norm_w) + i4);
+                        v.x = __fmul_rn(__fmul_rn(v.x, nscale), g.x);
+                        v.y = __fmul_rn(__fmul_rn(v.y, nscale), g.y);
+                        v.z = __fmul_rn(__fmul_rn(v.z, nscale), g.z);
+                        v.w = __fmul_rn(__fmul_rn(v.w, nscale), g.w);
+                    }
+                    const int i = 4 * i4;
+                    *reinterpret_cast<float4*>(xd + (i >> 5) * kQ8Pitch + (i & 31)) = v;
                 }
-                xd[(i >> 5) * kQ8Pitch + (i & 31)] = v;
+                for (int i = 4 * n4 + threadIdx.x; i < nu * 32; i += kThreads) {
+                    float v = 0.f;
+                    if (i < a.cols) {
+                        v = __ldg(xp + i);
+                        if (a.s.norm_w) v = __fmul_rn(__fmul_rn(v, nscale), __ldg(a.s.norm_w + i));
+                    }
+                    xd[(i >> 5) * kQ8Pitch + (i & 31)] = v;
+                }
+            } else {
+#pragma unroll 4
+                for (int i = threadIdx.x; i < nu * 32; i += kThreads) {
+                    float v = 0.f;
+                    if (i < a.cols) {
+                        v = __ldg(xp + i);
+                        if (a.s.norm_w) v = __fmul_rn(__fmul_rn(v, nscale), __ldg(a.s.norm_w + i));
+                    }
+                    xd[(i >> 5) * kQ8Pitch + (i & 31)] = v;
+                }
             }
         }
     }
     __syncthreads();
+    if constexpr (!kFloat && DqCode<TYPE>::HAS_B) {
+        // sum of each 32-value sub-block of X, kept in the pitch's spare float
+        for (int idx = threadIdx.x; idx < npos * nu; idx += kThreads) {
+            float* xu = xs + (long long)idx * kQ8Pitch;
+            const float4* x4 = reinterpret_cast<const float4*>(xu);
+            float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+            for (int k = 0; k < 8; k += 2) {
+                const float4 p = x4[k], q = x4[k + 1];
+                s0 += (p.x + p.y) + (p.z + p.w);
+                s1 += (q.x + q.y) + (q.z + q.w);
+            }
+            xu[32] = s0 + s1;
+        }
+        __syncthreads();
+    }
     pdl_launch_dependents();
 
     float acc[T];
 #pragma unroll
     for (int t = 0; t < T; ++t) acc[t] = 0.f;
-    for (int item = 0; item < n_items; ++item) {
+    // the dot products of the item held in `buf`, then `buf` refilled with
+    // item + 2; at a row's last chunk, the row's results and their epilogue
+    auto consume = [&](uint4 (&buf)[D::WPL], int item) {
         int span, row0, chunk, nblk_c;
         locate(item, span, row0, chunk, nblk_c);
         const Span& sp = a.s.span[span];
         const bool valid = row0 + warp < sp.rows;
         const int words = (nblk_c * D::BB + 15) >> 4;
-        // park the chunk in the warp's buffer, then start the next one's loads
-        __syncwarp();
-        if (valid) {
+        if constexpr (kFloat) {
+            if (valid) {
 #pragma unroll
-            for (int k = 0; k < D::WPL; ++k) {
-                const int wi = lane + 32 * k;
-                if (wi < words) reinterpret_cast<uint4*>(wbuf)[wi] = pre[k];
+                for (int k = 0; k < D::WPL; ++k) {
+                    const int wi = lane + 32 * k;
+                    if (wi >= words) continue;
+                    const uint4 v = buf[k];
+                    constexpr int VPW = TYPE == NEON_GGML_F32 ? 4 : 8;  // values per 16-byte word
+                    const int e = chunk * (D::UNITS * 32) + VPW * wi;
+                    float wv[VPW];
+                    if constexpr (TYPE == NEON_GGML_F32) {
+                        wv[0] = __uint_as_float(v.x);
+                        wv[1] = __uint_as_float(v.y);
+                        wv[2] = __uint_as_float(v.z);
+                        wv[3] = __uint_as_float(v.w);
+                    } else {
+                        const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            if constexpr (TYPE == NEON_GGML_F16) {
+                                wv[2 * q] = __half2float(__ushort_as_half((unsigned short)(u[q] & 0xFFFFu)));
+                                wv[2 * q + 1] = __half2float(__ushort_as_half((unsigned short)(u[q] >> 16)));
+                            } else {
+                                wv[2 * q] = __uint_as_float(u[q] << 16);
+                                wv[2 * q + 1] = __uint_as_float(u[q] & 0xFFFF0000u);
+                            }
+                        }
+                    }
+#pragma unroll
+                    for (int t = 0; t < T; ++t) {
+                        if (t >= npos) break;
+                        const float4* x4 = reinterpret_cast<const float4*>(
+                            xs + ((long long)t * nu + (e >> 5)) * kQ8Pitch + (e & 31));
+#pragma unroll
+                        for (int q = 0; q < VPW / 4; ++q) {
+                            const float4 xv = x4[q];
+                            acc[t] = fmaf(wv[4 * q], xv.x, acc[t]);
+                            acc[t] = fmaf(wv[4 * q + 1], xv.y, acc[t]);
+                            acc[t] = fmaf(wv[4 * q + 2], xv.z, acc[t]);
+                            acc[t] = fmaf(wv[4 * q + 3], xv.w, acc[t]);
+                        }
+                    }
+                }
             }
-        }
-        __syncwarp();
-        if (item + 1 < n_items) load(item + 1);
-        if (valid) {
+            if (item + 2 < n_items) load(buf, item + 2);
+        } else {
+            // park the chunk in the warp's buffer, start the loads of item + 2, decode
+            __syncwarp();
+            if (valid) {
 #pragma unroll
-            for (int j = 0; j < D::UPL; ++j) {
-                const int u = lane + 32 * j;
-                if (u < nblk_c * D::SUBS) {
-                    float w[32];
-                    dq_sub<TYPE>(wbuf + (u / D::SUBS) * D::BB, u % D::SUBS, w);
-                    const int unit = chunk * D::UNITS + u;
+                for (int k = 0; k < D::WPL; ++k) {
+                    const int wi = lane + 32 * k;
+                    if (wi < words) reinterpret_cast<uint4*>(wbuf)[wi] = buf[k];
+                }
+            }
+            __syncwarp();
+            if (item + 2 < n_items) load(buf, item + 2);
+            if (valid) {
 #pragma unroll
-                    for (int t = 0; t < T; ++t)
-                        if (t < npos) acc[t] += dq_dot32(w, xs + ((long long)t * nu + unit) * kQ8Pitch);
+                for (int j = 0; j < D::UPL; ++j) {
+                    const int u = lane + 32 * j;
+                    if (u < nblk_c * D::SUBS) {
+                        DqCode<TYPE> c;
+                        dq_codes<TYPE>(wbuf + (u / D::SUBS) * D::BB, u % D::SUBS, c);
+                        const int unit = chunk * D::UNITS + u;
+#pragma unroll
+                        for (int t = 0; t < T; ++t) {
+                            if (t >= npos) break;
+                            const float* xu = xs + ((long long)t * nu + unit) * kQ8Pitch;
+                            acc[t] += dq_code_dot<TYPE>(c, xu, xu[32]);
+                        }
+                    }
                 }
             }
         }
@@ -404,6 +597,10 @@ __global__ void __launch_bounds__(kThreads) matvec_dq_kernel(const __grid_consta
                 }
             }
         }
+    };
+    for (int item = 0; item < n_items; item += 2) {
+        consume(bufA, item);
+        if (item + 1 < n_items) consume(bufB, item + 1);
     }
 }
 

@@ -15,7 +15,33 @@ void decode_row(const unsigned char* row, int nu, float* out) {
         for (int j = 0; j < 32; ++j) out[32 * u + j] = w[j];
     }
 }
+template <int TYPE>
+void dot_row(const unsigned char* row, int nu, const float* x, float* out) {
+    using D = neon::DqShape<TYPE>;
+    for (int u = 0; u < nu; ++u) {
+        neon::DqCode<TYPE> c;
+        neon::dq_codes<TYPE>(row + (u / D::SUBS) * D::BB, u % D::SUBS, c);
+        float xsum = 0.f;
+        for (int j = 0; j < 32; ++j) xsum += x[32 * u + j];
+        out[u] = neon::dq_code_dot<TYPE>(c, x + 32 * u, xsum);
+    }
+}
 }  // namespace
+
+// Per 32-value sub-block of one padded device row, the kernel's dot product
+// with x (nu * 32 floats), computed without forming the weights (the packed
+// code sums, emulated lane by lane). Block types only; -1 otherwise.
+extern "C" int dq_host_code_dots(int type, const unsigned char* row, int nu, const float* x, float* out) {
+    switch (type) {
+        case NEON_GGML_Q4_1: dot_row<NEON_GGML_Q4_1>(row, nu, x, out); return 0;
+        case NEON_GGML_Q5_0: dot_row<NEON_GGML_Q5_0>(row, nu, x, out); return 0;
+        case NEON_GGML_Q5_1: dot_row<NEON_GGML_Q5_1>(row, nu, x, out); return 0;
+        case NEON_GGML_Q4_K: dot_row<NEON_GGML_Q4_K>(row, nu, x, out); return 0;
+        case NEON_GGML_Q5_K: dot_row<NEON_GGML_Q5_K>(row, nu, x, out); return 0;
+        case NEON_GGML_Q6_K: dot_row<NEON_GGML_Q6_K>(row, nu, x, out); return 0;
+        default: return -1;
+    }
+}
 
 // nu 32-value sub-blocks of one padded device row -> out (nu * 32 floats).
 // Returns -1 for a type the dequantising kernel does not take.

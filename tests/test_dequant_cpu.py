@@ -29,6 +29,7 @@ def dq(tmp_path_factory):
     L = C.CDLL(so)
     L.dq_host_decode_row.argtypes = [C.c_int, C.c_void_p, C.c_int, C.c_void_p]
     L.dq_host_geometry.argtypes = [C.c_int, C.POINTER(C.c_int), C.POINTER(C.c_int), C.POINTER(C.c_int)]
+    L.dq_host_code_dots.argtypes = [C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]
     return L
 
 
@@ -87,3 +88,25 @@ def test_chunks_stay_16_byte_aligned(dq):
         assert (cb * bb) % 16 == 0 and cb * (be // 32) in (32, 64), S.TYPE_NAMES[t]
         assert bb == S.BLOCK_BYTES[t] * (32 if S.BLOCK_ELEMS[t] == 1 else 1)
     assert geometry(dq, S.GGML_Q4_0) == (0, 0, 0)
+
+
+BLOCK_TYPES = [t for t in DQ_TYPES if t not in (S.GGML_F32, S.GGML_F16, S.GGML_BF16)]
+
+
+@pytest.mark.parametrize("typ", BLOCK_TYPES, ids=lambda t: S.TYPE_NAMES[t])
+def test_code_dot_products(dq, typ):
+    """The kernel's per-sub-block dot, a*sum((code - OFF)*x) + b*sum(x) on
+    packed pairs, against the exact dot of the oracle's weights with x: the
+    same sum in another order (bound: a few fp32 ulps of sum |w*x|)."""
+    cols = 2048
+    W = S.weights(typ, 16, cols, seed=21)
+    x = S.activations(1, cols, seed=22)[0]
+    for r in range(W.shape[0]):
+        buf, nu = device_row(dq, typ, W[r], cols)
+        got = np.empty(nu, np.float32)
+        assert dq.dq_host_code_dots(typ, buf.ctypes.data, nu, x.ctypes.data, got.ctypes.data) == 0
+        w = O.dequantize_row(typ, W[r], cols).astype(np.float64).reshape(nu, 32)
+        xx = x.astype(np.float64).reshape(nu, 32)
+        exact = (w * xx).sum(axis=1)
+        scale = (np.abs(w) * np.abs(xx)).sum(axis=1) + np.abs(w).max() * np.abs(xx).sum(axis=1)
+        assert np.all(np.abs(got - exact) <= 2e-6 * scale), (S.TYPE_NAMES[typ], r)

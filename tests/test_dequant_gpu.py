@@ -13,7 +13,7 @@ import pytest
 import neon_cuda as N
 import oracle as O
 import synth as S
-from conftest import MATVEC_RTOL, load_golden, max_rel_err
+from conftest import MATVEC_RTOL, load_golden, max_rel_err, rel_l2
 
 pytestmark = pytest.mark.gpu
 torch = pytest.importorskip("torch")
@@ -154,7 +154,11 @@ TINY = S.ModelConfig(1000, 256, 2, 4, 2, 64, 512, ctx_len=64, rope_base=1e4, nam
 ], ids=lambda v: S.TYPE_NAMES.get(v, str(v)) if not isinstance(v, bool) else ("tied" if v else "untied"))
 def test_decoder_of_each_type_matches_oracle(wtype, etype, tied):
     """The fused decode step (norm folded into X staging, RoPE / SwiGLU /
-    residual epilogues, CUDA-graph replay) on the dequantising kernel."""
+    residual epilogues, CUDA-graph replay) on the dequantising kernel: the
+    oracle's greedy tokens, and logits within 1e-3 relative L2 at every step --
+    50x tighter than the whole-model bar of the Q4_0 decoder (conftest.py),
+    since no activation is quantised here, but not the single-matvec
+    per-element bar: fp32 reordering compounds over two layers of attention."""
     tensors = list(S.model_tensors(TINY, seed=17, wtype=wtype, embd_type=etype, tied=tied))
     m = N.Model(TINY, tensors)
     o = O.Model(TINY, tensors, "port")
@@ -164,5 +168,6 @@ def test_decoder_of_each_type_matches_oracle(wtype, etype, tied):
     m.set_length(0)
     got = [m.forward(prompt)] + [m.forward([t]) for t in want_toks[:7]]
     for i, (a, b) in enumerate(zip(got, want_logits)):
-        assert max_rel_err(a, b) <= MATVEC_RTOL, f"step {i}"
+        assert rel_l2(a, b) <= 1e-3, f"step {i}"
+        assert int(np.argmax(a)) == int(np.argmax(b)), f"step {i}"
     m.free()
