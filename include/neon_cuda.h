@@ -110,6 +110,26 @@ NEON_API int neon_cuda_init(int device);
 NEON_API int neon_cuda_upload(const uint8_t* host_bytes, int ggml_type, size_t rows, size_t cols,
                      int shard_mode, int shard_index, int shard_count, neon_tensor_t* out);
 
+/* On-load quantisation. The reference's runtime takes weights as stored; its
+ * exporters quantise them with gguf-py's gguf.quants.quantize
+ * (train_nanity_fixed.py:1162-1169 export_gguf, nanity_convert.py:472-484),
+ * and a .nctr file is F32 only (export_nctr, train_nanity_fixed.py:1259-1433).
+ * These take rows of F32 / F16 / BF16 values (a .nctr tensor, or a float GGUF
+ * tensor) to Q8_0, Q4_0, Q4_1, Q5_0, Q5_1, F16 or BF16 on the device, byte for
+ * byte as gguf-py 0.19.0 writes them (finite inputs; block types need cols a
+ * multiple of 32).
+ *   neon_cuda_quantize_rows: device buffers, rows of bytes_for_type(src, cols)
+ *     in, rows of bytes_for_type(dst, cols) out, on `stream`.
+ *   neon_cuda_quantize_host: the same from host bytes to host bytes, blocking.
+ *   neon_cuda_upload_quantized: neon_cuda_upload of the quantised tensor
+ *     (shard modes as neon_cuda_upload), without a host round trip. */
+NEON_API int neon_cuda_quantize_rows(const void* d_src, int src_type, size_t rows, size_t cols, int dst_type,
+                                     void* d_dst, void* stream);
+NEON_API int neon_cuda_quantize_host(const void* host_src, int src_type, size_t rows, size_t cols, int dst_type,
+                                     void* host_dst);
+NEON_API int neon_cuda_upload_quantized(const void* host_src, int src_type, size_t rows, size_t cols, int dst_type,
+                                        int shard_mode, int shard_index, int shard_count, neon_tensor_t* out);
+
 /* Rows, cols (of the kept shard), type and device bytes of a tensor. */
 NEON_API int neon_cuda_tensor_info(neon_tensor_t W, size_t* rows, size_t* cols, int* ggml_type,
                           size_t* device_bytes);
@@ -213,6 +233,14 @@ NEON_API int neon_cuda_model_create(const neon_model_config_t* cfg, neon_model_t
  * and ffn_up of one layer share theirs); norm weights are F32. */
 NEON_API int neon_cuda_model_set_tensor(neon_model_t m, int role, int layer, const uint8_t* host_bytes,
                                         size_t nbytes, int ggml_type, size_t ne0, size_t ne1);
+
+/* Quantise every later float (F32 / F16 / BF16) projection, embedding or
+ * lm_head tensor given to neon_cuda_model_set_tensor to `ggml_type` (Q8_0,
+ * Q4_0, Q4_1, Q5_0, Q5_1, F16 or BF16) on the device first, byte for byte as
+ * the exporters' gguf-py would have (neon_cuda_quantize_rows): a .nctr model,
+ * F32 only, then runs as the Q8_0 / Q4_0 GGUF its publisher could have
+ * exported. -1 turns it off (the default: tensors run as given). */
+NEON_API int neon_cuda_model_set_quantize(neon_model_t m, int ggml_type);
 
 /* fwd::transformer_forward (rawllm_forward.hpp:987-1236): process `n` new
  * tokens at positions length .. length+n-1, append their K/V to the cache,

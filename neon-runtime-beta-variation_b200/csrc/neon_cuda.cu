@@ -4,6 +4,7 @@
 #include "neon_internal.h"
 #include "neon_kernels.cuh"
 #include "neon_dequant.cuh"
+#include "neon_quant.cuh"
 
 #include <cuda_runtime.h>
 
@@ -721,8 +722,8 @@ namespace {
 // Upload of a dequantising type: the GGUF rows (or the kept shard of them)
 // copied unchanged into rows of a 16-byte pitch, the padding zeroed. One 2-D
 // copy straight from the caller's bytes; no repack kernel.
-int upload_rows(const uint8_t* host_bytes, int type, size_t rows, size_t cols, int shard_mode, int shard_index,
-                int shard_count, neon_tensor_t* out) {
+int upload_rows(const uint8_t* host_bytes, bool on_device, int type, size_t rows, size_t cols, int shard_mode,
+                int shard_index, int shard_count, neon_tensor_t* out) {
     int be, bb, cb;
     dq_geometry(type, &be, &bb, &cb);
     const size_t src_row = row_bytes_of(type, cols);
@@ -775,7 +776,7 @@ int upload_rows(const uint8_t* host_bytes, int type, size_t rows, size_t cols, i
     e = cudaMemsetAsync(t->base, 0, total, st);
     if (e == cudaSuccess)
         e = cudaMemcpy2DAsync(t->base, pitch, host_bytes + r0 * src_row + b0 * (size_t)bb, src_row, width, lrows,
-                              cudaMemcpyHostToDevice, st);
+                              on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, st);
     if (e == cudaSuccess) e = cudaStreamSynchronize(st);
     if (e != cudaSuccess) {
         cudaFree(t->base);
@@ -789,21 +790,28 @@ int upload_rows(const uint8_t* host_bytes, int type, size_t rows, size_t cols, i
 
 extern "C" {
 
-int neon_cuda_upload(const uint8_t* host_bytes, int ggml_type, size_t rows, size_t cols, int shard_mode,
-                     int shard_index, int shard_count, neon_tensor_t* out) {
+}  // extern "C"
+
+namespace {
+// The upload of neon_cuda_upload, from host bytes or (on_device) from GGUF
+// bytes already in this device's memory (the on-load quantiser's output).
+int upload_impl(const uint8_t* host_bytes, bool on_device, int ggml_type, size_t rows, size_t cols, int shard_mode,
+                int shard_index, int shard_count, neon_tensor_t* out) {
     if (!out) return set_err(NEON_ERR_INVALID, "null output handle");
     *out = nullptr;
     if (!host_bytes) return set_err(NEON_ERR_INVALID, "null weight bytes");
     if (!supported_type(ggml_type))
         return set_err(NEON_ERR_UNSUPPORTED, "quant type " + std::to_string(ggml_type) +
-                                                 " is not supported by the CUDA backend (Q4_0 and Q8_0 are)");
+                                                 " is not supported by the CUDA backend (the eleven types "
+                                                 "dequantize_row decodes are)");
     if (rows == 0 || cols == 0) return set_err(NEON_ERR_INVALID, "empty tensor");
     const size_t bs = block_elems_of(ggml_type);
     if (cols % bs != 0)
         return set_err(NEON_ERR_INVALID, "forward(): input dim (" + std::to_string(cols) +
                                              ") isn't a multiple of its quant block size (" + std::to_string(bs) +
                                              ") -- can't dequantize safely.");
-    if (dq_type(ggml_type)) return upload_rows(host_bytes, ggml_type, rows, cols, shard_mode, shard_index, shard_count, out);
+    if (dq_type(ggml_type))
+        return upload_rows(host_bytes, on_device, ggml_type, rows, cols, shard_mode, shard_index, shard_count, out);
     if (rows > (size_t)INT32_MAX / 2 || cols / 32 > (size_t)INT32_MAX / 64)
         return set_err(NEON_ERR_INVALID, "tensor too large");
     size_t nb = cols / 32;
@@ -847,24 +855,31 @@ int neon_cuda_upload(const uint8_t* host_bytes, int ggml_type, size_t rows, size
     t->qs = t->base;
     t->d = reinterpret_cast<uint16_t*>(t->base + d_off);
 
-    // Stage the GGUF rows in chunks of <= 256 MiB and repack them on the device.
-    const size_t chunk_rows = std::max<size_t>(1, (256u << 20) / src_row);
+    // Stage the GGUF rows in chunks of <= 256 MiB and repack them on the device
+    // (device-resident bytes are repacked in place, in one pass).
+    const size_t chunk_rows = on_device ? lrows : std::max<size_t>(1, (256u << 20) / src_row);
     uint8_t* tmp = nullptr;
-    size_t tmp_bytes = std::min(lrows, chunk_rows) * src_row;
-    e = cudaMalloc(&tmp, tmp_bytes);
-    if (e != cudaSuccess) {
-        cudaFree(t->base);
-        delete t;
-        return set_err(NEON_ERR_NOMEM, "cudaMalloc of the upload staging buffer failed");
+    if (!on_device) {
+        size_t tmp_bytes = std::min(lrows, chunk_rows) * src_row;
+        e = cudaMalloc(&tmp, tmp_bytes);
+        if (e != cudaSuccess) {
+            cudaFree(t->base);
+            delete t;
+            return set_err(NEON_ERR_NOMEM, "cudaMalloc of the upload staging buffer failed");
+        }
     }
     cudaStream_t st = g_dev[device].stream;
     for (size_t c = 0; c < lrows; c += chunk_rows) {
         size_t nr = std::min(chunk_rows, lrows - c);
-        e = cudaMemcpyAsync(tmp, host_bytes + (r0 + c) * src_row, nr * src_row, cudaMemcpyHostToDevice, st);
-        if (e != cudaSuccess) break;
+        const uint8_t* src = host_bytes + (r0 + c) * src_row;
+        if (!on_device) {
+            e = cudaMemcpyAsync(tmp, src, nr * src_row, cudaMemcpyHostToDevice, st);
+            if (e != cudaSuccess) break;
+            src = tmp;
+        }
         long long n = (long long)nr * (long long)lnb;
         int grid = (int)std::min<long long>((n + 255) / 256, 65535LL * 8);
-        repack_kernel<<<grid, 256, 0, st>>>(tmp, (long long)src_row, (int)nr, (int)b0, (int)lnb, (int)P,
+        repack_kernel<<<grid, 256, 0, st>>>(src, (long long)src_row, (int)nr, (int)b0, (int)lnb, (int)P,
                                             t->qs + c * lnb * P, t->d + c * lnb);
         g_launches.fetch_add(1, std::memory_order_relaxed);
         e = cudaGetLastError();
@@ -880,6 +895,123 @@ int neon_cuda_upload(const uint8_t* host_bytes, int ggml_type, size_t rows, size
     }
     *out = t;
     return NEON_OK;
+}
+
+// On-load quantisation: `dst` is a type the quantiser produces from float rows.
+bool quantizable(int src, int dst) {
+    const bool float_src = src == NEON_GGML_F32 || src == NEON_GGML_F16 || src == NEON_GGML_BF16;
+    return float_src && (q_block_bytes(dst) != 0 || dst == NEON_GGML_F16 || dst == NEON_GGML_BF16);
+}
+
+int check_quantize_args(int src_type, size_t rows, size_t cols, int dst_type) {
+    if (!quantizable(src_type, dst_type))
+        return set_err(NEON_ERR_UNSUPPORTED, "on-load quantisation takes F32/F16/BF16 rows to Q8_0, Q4_0, Q4_1, "
+                                             "Q5_0, Q5_1, F16 or BF16 (got " + std::to_string(src_type) + " -> " +
+                                                 std::to_string(dst_type) + ")");
+    if (rows == 0 || cols == 0) return set_err(NEON_ERR_INVALID, "empty tensor");
+    if (q_block_bytes(dst_type) && cols % 32 != 0)
+        return set_err(NEON_ERR_INVALID, "input dim (" + std::to_string(cols) +
+                                             ") isn't a multiple of the quantised type's block size (32)");
+    return NEON_OK;
+}
+
+int launch_quantize(const void* d_src, int src_type, size_t rows, size_t cols, int dst_type, void* d_dst,
+                    cudaStream_t st, int sms) {
+    const long long per_row = q_block_bytes(dst_type) ? (long long)cols / 32 : (long long)cols;
+    const long long n = (long long)rows * per_row;
+    const int grid = (int)std::min<long long>((n + 255) / 256, (long long)sms * 16);
+    quantize_rows_kernel<<<grid, 256, 0, st>>>(static_cast<const unsigned char*>(d_src),
+                                               (long long)row_bytes_of(src_type, cols), src_type, (long long)rows,
+                                               (long long)cols, dst_type, static_cast<unsigned char*>(d_dst),
+                                               (long long)row_bytes_of(dst_type, cols));
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return cuda_err(cudaGetLastError(), "quantize_rows_kernel");
+}
+
+// Host float rows -> device GGUF rows of dst_type (caller frees *d_out).
+int quantize_to_device(const void* host_src, int src_type, size_t rows, size_t cols, int dst_type, uint8_t** d_out) {
+    *d_out = nullptr;
+    int device = 0;
+    int rc = current_device(&device);
+    if (rc) return rc;
+    const size_t in_bytes = rows * row_bytes_of(src_type, cols), out_bytes = rows * row_bytes_of(dst_type, cols);
+    void* d_src = nullptr;
+    uint8_t* d_dst = nullptr;
+    if (cudaMalloc(&d_src, in_bytes) != cudaSuccess || cudaMalloc(&d_dst, out_bytes) != cudaSuccess) {
+        cudaFree(d_src);
+        cudaFree(d_dst);
+        return set_err(NEON_ERR_NOMEM, "cudaMalloc of the quantisation buffers failed");
+    }
+    cudaStream_t st = g_dev[device].stream;
+    cudaError_t e = cudaMemcpyAsync(d_src, host_src, in_bytes, cudaMemcpyHostToDevice, st);
+    rc = e == cudaSuccess ? launch_quantize(d_src, src_type, rows, cols, dst_type, d_dst, st, g_dev[device].sms)
+                          : cuda_err(e, "quantisation input copy");
+    if (!rc) rc = cuda_err(cudaStreamSynchronize(st), "quantisation");
+    cudaFree(d_src);
+    if (rc) {
+        cudaFree(d_dst);
+        return rc;
+    }
+    *d_out = d_dst;
+    return NEON_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int neon_cuda_upload(const uint8_t* host_bytes, int ggml_type, size_t rows, size_t cols, int shard_mode,
+                     int shard_index, int shard_count, neon_tensor_t* out) {
+    return upload_impl(host_bytes, false, ggml_type, rows, cols, shard_mode, shard_index, shard_count, out);
+}
+
+int neon_cuda_quantize_rows(const void* d_src, int src_type, size_t rows, size_t cols, int dst_type, void* d_dst,
+                            void* stream) {
+    if (!d_src || !d_dst) return set_err(NEON_ERR_INVALID, "null buffer");
+    int rc = check_quantize_args(src_type, rows, cols, dst_type);
+    if (rc) return rc;
+    int device = 0;
+    rc = current_device(&device);
+    if (rc) return rc;
+    return launch_quantize(d_src, src_type, rows, cols, dst_type, d_dst, (cudaStream_t)stream, g_dev[device].sms);
+}
+
+int neon_cuda_quantize_host(const void* host_src, int src_type, size_t rows, size_t cols, int dst_type,
+                            void* host_dst) {
+    if (!host_src || !host_dst) return set_err(NEON_ERR_INVALID, "null buffer");
+    int rc = check_quantize_args(src_type, rows, cols, dst_type);
+    if (rc) return rc;
+    uint8_t* d = nullptr;
+    rc = quantize_to_device(host_src, src_type, rows, cols, dst_type, &d);
+    if (rc) return rc;
+    cudaError_t e = cudaMemcpy(host_dst, d, rows * row_bytes_of(dst_type, cols), cudaMemcpyDeviceToHost);
+    cudaFree(d);
+    return cuda_err(e, "quantisation output copy");
+}
+
+int neon_cuda_upload_quantized(const void* host_src, int src_type, size_t rows, size_t cols, int dst_type,
+                               int shard_mode, int shard_index, int shard_count, neon_tensor_t* out) {
+    if (!out) return set_err(NEON_ERR_INVALID, "null output handle");
+    *out = nullptr;
+    if (!host_src) return set_err(NEON_ERR_INVALID, "null weight bytes");
+    int rc = check_quantize_args(src_type, rows, cols, dst_type);
+    if (rc) return rc;
+    // a row shard is quantised alone; a column shard is cut from the quantised rows
+    size_t r0 = 0, r1 = rows;
+    if (shard_mode == NEON_SHARD_ROWS) {
+        if (shard_count <= 0 || shard_index < 0 || shard_index >= shard_count)
+            return set_err(NEON_ERR_INVALID, "bad shard index/count");
+        r0 = rows * (size_t)shard_index / (size_t)shard_count;
+        r1 = rows * (size_t)(shard_index + 1) / (size_t)shard_count;
+        if (r1 <= r0) return set_err(NEON_ERR_INVALID, "empty shard");
+    }
+    uint8_t* d = nullptr;
+    rc = quantize_to_device(static_cast<const uint8_t*>(host_src) + r0 * row_bytes_of(src_type, cols), src_type,
+                            r1 - r0, cols, dst_type, &d);
+    if (rc) return rc;
+    rc = upload_impl(d, true, dst_type, r1 - r0, cols, shard_mode == NEON_SHARD_ROWS ? NEON_SHARD_NONE : shard_mode,
+                     shard_index, shard_count, out);
+    cudaFree(d);
+    return rc;
 }
 
 int neon_cuda_tensor_info(neon_tensor_t W, size_t* rows, size_t* cols, int* ggml_type, size_t* device_bytes) {

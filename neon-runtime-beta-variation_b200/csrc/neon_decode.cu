@@ -660,6 +660,7 @@ struct neon_model {
     size_t n_head_l = 0, n_kv_l = 0, ff0 = 0, n_ff_l = 0, vocab0 = 0, vocab_l = 0;
     neon_tensor_t head = nullptr;    // lm_head shard (tensor parallel only)
     bool head_from_output = false;   // `head` was cut from output.weight, not the tied embedding
+    int quantize_to = -1;            // neon_cuda_model_set_quantize: float matrices quantised on load to this type
     float* part = nullptr;           // partial sums of the column-split projections
     float* shift_scratch = nullptr;  // ctx_len x kv_dim, for neon_cuda_model_kv_shift
     float2* shift_cs = nullptr;      // rope_half (cos, sin) of the shift angle
@@ -1204,11 +1205,38 @@ int neon_cuda_model_create_tp(const neon_model_config_t* cfg, neon_comm_t comm, 
     return NEON_OK;
 }
 
+int neon_cuda_model_set_quantize(neon_model_t m, int ggml_type) {
+    if (!m) return error(NEON_ERR_INVALID, "null argument");
+    if (ggml_type >= 0 && ggml_type != NEON_GGML_Q8_0 && ggml_type != NEON_GGML_Q4_0 && ggml_type != NEON_GGML_Q4_1 &&
+        ggml_type != NEON_GGML_Q5_0 && ggml_type != NEON_GGML_Q5_1 && ggml_type != NEON_GGML_F16 &&
+        ggml_type != NEON_GGML_BF16)
+        return error(NEON_ERR_UNSUPPORTED, "on-load quantisation to type " + std::to_string(ggml_type) +
+                                               " is not available (Q8_0, Q4_0, Q4_1, Q5_0, Q5_1, F16, BF16 are)");
+    m->quantize_to = ggml_type < 0 ? -1 : ggml_type;
+    return NEON_OK;
+}
+
 int neon_cuda_model_set_tensor(neon_model_t m, int role, int layer, const uint8_t* host_bytes, size_t nbytes,
                                int ggml_type, size_t ne0, size_t ne1) {
     if (!m || !host_bytes) return error(NEON_ERR_INVALID, "null argument");
     ModelDevice md(m->device);
     const auto& c = m->cfg;
+    const bool matrix = role != NEON_ROLE_OUTPUT_NORM && role != NEON_ROLE_ATTN_NORM && role != NEON_ROLE_FFN_NORM;
+    if (matrix && m->quantize_to >= 0 && m->quantize_to != ggml_type &&
+        (ggml_type == NEON_GGML_F32 || ggml_type == NEON_GGML_F16 || ggml_type == NEON_GGML_BF16) && ne1 > 0) {
+        // a float matrix (a .nctr tensor, an F32/F16 GGUF tensor): quantise it
+        // on the device first, as the exporters' gguf-py would have
+        const size_t in_row = neon_internal::gguf_row_bytes(ggml_type, ne0);
+        const size_t out_row = neon_internal::gguf_row_bytes(m->quantize_to, ne0);
+        if (in_row == 0 || out_row == 0)
+            return error(NEON_ERR_UNSUPPORTED, "on-load quantisation: input dim " + std::to_string(ne0) +
+                                                   " is not a multiple of the block size");
+        if (nbytes < in_row * ne1) return error(NEON_ERR_INVALID, "tensor bytes shorter than its shape");
+        std::vector<uint8_t> q(out_row * ne1);
+        int rc = neon_cuda_quantize_host(host_bytes, ggml_type, ne1, ne0, m->quantize_to, q.data());
+        if (rc) return rc;
+        return neon_cuda_model_set_tensor(m, role, layer, q.data(), q.size(), m->quantize_to, ne0, ne1);
+    }
     if (role == NEON_ROLE_OUTPUT_NORM || role == NEON_ROLE_ATTN_NORM || role == NEON_ROLE_FFN_NORM) {
         if (ggml_type != NEON_GGML_F32 || ne0 != c.n_embd || ne1 > 1 || nbytes != ne0 * 4)
             return error(NEON_ERR_INVALID, "NANITY: norm weight must be F32 [n_embd]");

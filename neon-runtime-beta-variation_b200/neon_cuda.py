@@ -25,6 +25,8 @@ raises.
 from __future__ import annotations
 
 import ctypes as C
+import json
+import struct
 import os
 import threading
 import weakref
@@ -57,6 +59,9 @@ C_ENTRY_POINTS = (
     "neon_cuda_device_count",
     "neon_cuda_init",
     "neon_cuda_upload",
+    "neon_cuda_quantize_rows",
+    "neon_cuda_quantize_host",
+    "neon_cuda_upload_quantized",
     "neon_cuda_tensor_info",
     "neon_cuda_free",
     "neon_cuda_quantize_q8_0",
@@ -69,6 +74,7 @@ C_ENTRY_POINTS = (
     "neon_cuda_matvec_q4_0_noalloc",
     "neon_cuda_model_create",
     "neon_cuda_model_set_tensor",
+    "neon_cuda_model_set_quantize",
     "neon_cuda_model_forward",
     "neon_cuda_model_generate",
     "neon_cuda_model_length",
@@ -135,6 +141,11 @@ def load(path: str | None = None) -> C.CDLL:
         L.neon_cuda_device_count.argtypes = [C.POINTER(C.c_int)]
         L.neon_cuda_init.argtypes = [C.c_int]
         L.neon_cuda_upload.argtypes = [_vp, C.c_int, _sz, _sz, C.c_int, C.c_int, C.c_int, C.POINTER(_vp)]
+        L.neon_cuda_quantize_rows.argtypes = [_vp, C.c_int, _sz, _sz, C.c_int, _vp, _vp]
+        L.neon_cuda_quantize_host.argtypes = [_vp, C.c_int, _sz, _sz, C.c_int, _vp]
+        L.neon_cuda_upload_quantized.argtypes = [_vp, C.c_int, _sz, _sz, C.c_int, C.c_int, C.c_int, C.c_int,
+                                                 C.POINTER(_vp)]
+        L.neon_cuda_model_set_quantize.argtypes = [_vp, C.c_int]
         L.neon_cuda_tensor_info.argtypes = [_vp, C.POINTER(_sz), C.POINTER(_sz), C.POINTER(C.c_int),
                                             C.POINTER(_sz)]
         L.neon_cuda_free.argtypes = [_vp]
@@ -246,6 +257,18 @@ class DeviceTensor:
         self.rows, self.cols, self.type, self.device_bytes = r.value, c.value, t.value, b.value
         self._fin = weakref.finalize(self, L.neon_cuda_free, self.handle)
 
+    @classmethod
+    def _adopt(cls, handle) -> "DeviceTensor":
+        """Wrap a tensor handle the library created."""
+        L = load()
+        self = cls.__new__(cls)
+        self.handle = handle
+        r, c, t, b = _sz(), _sz(), C.c_int(), _sz()
+        _check(L.neon_cuda_tensor_info(self.handle, C.byref(r), C.byref(c), C.byref(t), C.byref(b)))
+        self.rows, self.cols, self.type, self.device_bytes = r.value, c.value, t.value, b.value
+        self._fin = weakref.finalize(self, L.neon_cuda_free, self.handle)
+        return self
+
     def free(self) -> None:
         self._fin()
 
@@ -256,6 +279,37 @@ class DeviceTensor:
         y_stride = self.rows if y_stride is None else y_stride
         _check(load().neon_cuda_matvec(self.handle, _ptr(X), x_stride, _ptr(Y), y_stride, seq,
                                        _vp(_stream(stream))))
+
+
+_ROW_BYTES = {GGML_F32: (1, 4), GGML_F16: (1, 2), GGML_BF16: (1, 2), GGML_Q4_0: (32, 18), GGML_Q4_1: (32, 20),
+              GGML_Q5_0: (32, 22), GGML_Q5_1: (32, 24), GGML_Q8_0: (32, 34), GGML_Q4_K: (256, 144),
+              GGML_Q5_K: (256, 176), GGML_Q6_K: (256, 210)}
+
+
+def row_bytes(ggml_type: int, cols: int) -> int:
+    """Bytes of one GGUF row (GGUFLoader::bytes_for_type, rawllm_loader.hpp:367-386)."""
+    be, bb = _ROW_BYTES[ggml_type]
+    return cols // be * bb
+
+
+def quantize(raw: np.ndarray, src_type: int, rows: int, cols: int, dst_type: int) -> np.ndarray:
+    """Float rows (F32/F16/BF16 bytes) -> GGUF rows of dst_type, quantised on the
+    device as gguf-py's gguf.quants.quantize writes them; shape (rows, row_bytes)."""
+    raw = np.ascontiguousarray(raw)
+    out = np.empty((rows, row_bytes(dst_type, cols)), np.uint8)
+    _check(load().neon_cuda_quantize_host(raw.ctypes.data, int(src_type), rows, cols, int(dst_type),
+                                          out.ctypes.data))
+    return out
+
+
+def upload_quantized(raw: np.ndarray, src_type: int, rows: int, cols: int, dst_type: int,
+                     shard_mode: int = SHARD_NONE, shard_index: int = 0, shard_count: int = 1) -> "DeviceTensor":
+    """A DeviceTensor of float rows quantised to dst_type on the device."""
+    raw = np.ascontiguousarray(raw)
+    h = _vp()
+    _check(load().neon_cuda_upload_quantized(raw.ctypes.data, int(src_type), rows, cols, int(dst_type),
+                                             int(shard_mode), int(shard_index), int(shard_count), C.byref(h)))
+    return DeviceTensor._adopt(h.value)
 
 
 def matvec_multi(targets, X, seq: int = 1, x_stride: int | None = None, stream=None) -> None:
@@ -448,17 +502,92 @@ class Comm:
         self._fin()
 
 
+# ---------------------------------------------------------------------------
+# .nctr models (the reference's F32 export container)
+# ---------------------------------------------------------------------------
+
+# NCTRHeader (rawllm_nctr_loader.hpp:32-62): 116 bytes, little-endian, packed.
+_NCTR_HEADER = struct.Struct("<4s10Iff I f II 6Q")
+_NCTR_SLOT = struct.Struct("<IQQ")  # quant_type, data_offset, nbytes (:70-71)
+NCTR_SPEC_VERSION = 1               # engine::kSpecVersion (rawllm_common.hpp:111)
+NCTR_FLAG_USE_SWIGLU, NCTR_FLAG_HAS_OUTPUT_WEIGHT, NCTR_FLAG_HAS_OPT_STATE = 1, 2, 4
+
+
+class NctrConfig:
+    """engine::Config as NCTRLoader::validate_config fills it
+    (rawllm_nctr_loader.hpp:146-184): the header's fields, ``ctx_len`` the KV
+    capacity (kv_window = min(ctx_len, 4096)) and ``context_length`` the
+    header's value, ``plain_ffn`` = not use_swiglu."""
+
+    def __init__(self, **kw):
+        self.__dict__.update(kw)
+
+
+def load_nctr(path: str):
+    """Open a .nctr file -- the container export_nctr writes
+    (train_nanity_fixed.py:1259-1433), F32 tensors -- as (config, tensors)
+    for :class:`Model`: ``tensors`` are (role, layer, bytes, ggml type, ne0,
+    ne1) views of a read-only memory map, in the positional order of
+    NCTRLoader::build_tensor_table (rawllm_nctr_loader.hpp:217-264).
+    The checks and messages are NCTRLoader::open's (:87-137) and
+    validate_config's."""
+    mm = np.memmap(path, np.uint8, mode="r")
+    size = mm.size
+    if size < _NCTR_HEADER.size:
+        raise RuntimeError("File too small to be NCTR (<header size): " + path)
+    (magic, _fmt, spec, n_vocab, n_embd, n_layer, n_head, n_kv, head_dim, n_ff, ctx_len, rope_base, rope_scale,
+     rope_dim, eps, flags, _align, man_off, man_len, tok_off, tok_len, table_off,
+     data_off) = _NCTR_HEADER.unpack(bytes(mm[:_NCTR_HEADER.size]))
+    if magic != b"NCTR":
+        raise RuntimeError("Not an NCTR file: " + path)
+    if spec != NCTR_SPEC_VERSION:
+        raise RuntimeError(f"NCTR: file declares spec_version {spec}, runtime built against {NCTR_SPEC_VERSION}")
+
+    def in_bounds(off, length):
+        if off > size or length > size - off:
+            raise RuntimeError(f"NCTR: section out of bounds (offset={off} len={length} file_size={size})")
+
+    in_bounds(man_off, man_len)
+    in_bounds(tok_off, tok_len)
+    swiglu, has_output = bool(flags & NCTR_FLAG_USE_SWIGLU), bool(flags & NCTR_FLAG_HAS_OUTPUT_WEIGHT)
+    q_dim, kv_dim = n_head * head_dim, n_kv * head_dim
+    slots = [(0, -1, n_embd, n_vocab), (1, -1, n_embd, 0)] + ([(2, -1, n_embd, n_vocab)] if has_output else [])
+    for i in range(n_layer):
+        slots += [(3, i, n_embd, 0), (4, i, n_embd, q_dim), (5, i, n_embd, kv_dim), (6, i, n_embd, kv_dim),
+                  (7, i, q_dim, n_embd), (8, i, n_embd, 0)]
+        slots += ([(9, i, n_embd, n_ff)] if swiglu else []) + [(10, i, n_embd, n_ff), (11, i, n_ff, n_embd)]
+    in_bounds(table_off, len(slots) * _NCTR_SLOT.size)
+    tensors = []
+    for k, (role, layer, ne0, ne1) in enumerate(slots):
+        o = table_off + k * _NCTR_SLOT.size
+        qtype, off, nbytes = _NCTR_SLOT.unpack(bytes(mm[o:o + _NCTR_SLOT.size]))
+        in_bounds(data_off + off, nbytes)
+        tensors.append((role, layer, mm[data_off + off:data_off + off + nbytes], qtype, ne0, ne1))
+    if n_head == 0 or n_kv == 0 or n_head % n_kv != 0:
+        raise RuntimeError(f"NCTR: n_head must be a nonzero multiple of n_kv_head (got {n_head} / {n_kv})")
+    tok = json.loads(bytes(mm[tok_off:tok_off + tok_len]).decode("utf-8"))
+    cfg = NctrConfig(n_vocab=n_vocab, n_embd=n_embd, n_layer=n_layer, n_head=n_head, n_kv_head=n_kv,
+                     head_dim=head_dim, n_ff=n_ff, ctx_len=min(ctx_len, 4096), context_length=ctx_len,
+                     rope_base=rope_base, rope_scale=rope_scale, rope_dim_count=rope_dim, norm_eps=eps,
+                     plain_ffn=not swiglu, has_optimizer_state=bool(flags & NCTR_FLAG_HAS_OPT_STATE),
+                     bos_id=int(tok.get("bos_id", 1)), eos_id=int(tok.get("eos_id", 2)),
+                     unk_id=int(tok.get("unk_id", 0)), n_tokens=len(tok.get("tokens", [])),
+                     manifest_json=bytes(mm[man_off:man_off + man_len]).decode("utf-8", "replace"))
+    return cfg, tensors
+
+
 class Model:
     """A NANITY decoder on the current device (neon_cuda_model_*).
 
     ``cfg`` has the fields of engine::Config the forward pass reads (n_vocab,
     n_embd, n_layer, n_head, n_kv_head, head_dim, n_ff, ctx_len, rope_base,
     rope_scale, rope_dim_count, norm_eps); ``tensors`` yields (role, layer,
-    GGUF bytes, ggml type, ne0, ne1). With a connected :class:`Comm`, the
+    GGUF bytes, ggml type, ne0, ne1); ``quantize`` (a GGML type) quantises
+    float matrices on load. With a connected :class:`Comm`, the
     model is this rank's tensor-parallel share; every rank passes the WHOLE
     tensors and makes the same calls in the same order."""
 
-    def __init__(self, cfg, tensors=(), comm: Comm | None = None):
+    def __init__(self, cfg, tensors=(), comm: Comm | None = None, quantize: int | None = None):
         L = load()
         self.cfg = cfg
         self.comm = comm
@@ -466,6 +595,9 @@ class Model:
         _check(L.neon_cuda_model_create_tp(C.byref(_config(cfg)), comm.handle if comm else None, C.byref(h)))
         self.handle = h.value
         self._fin = weakref.finalize(self, L.neon_cuda_model_free, self.handle)
+        if quantize is not None:
+            # float matrices (a .nctr model) quantised on load, as gguf-py exports them
+            _check(L.neon_cuda_model_set_quantize(self.handle, int(quantize)))
         for t in tensors:
             self.set_tensor(*t)
 

@@ -272,3 +272,76 @@ void ref_rope_apply(float* vec, size_t n_heads, size_t head_dim, size_t rope_hal
 void ref_axpy_f32(float* out, float w, const float* v, size_t n) { fwd::axpy_f32(out, w, v, n); }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// The reference's .nctr reader, loader::NCTRLoader (rawllm_nctr_loader.hpp),
+// behind a C ABI: open, validate_config, and the positional tensor table, so
+// the tests can check that the package's reader sees the same tensors, the
+// same configuration and the same errors.
+// ---------------------------------------------------------------------------
+#include "rawllm_nctr_loader.hpp"
+
+extern "C" {
+
+// NCTRLoader::open (rawllm_nctr_loader.hpp:87-137); null and ref_last_error() on a throw.
+void* ref_nctr_open(const char* path) {
+    auto* l = new loader::NCTRLoader();
+    try {
+        l->open(path);
+        return l;
+    } catch (const std::exception& e) {
+        delete l;
+        fail(e);
+        return nullptr;
+    }
+}
+
+void ref_nctr_free(void* h) { delete static_cast<loader::NCTRLoader*>(h); }
+
+size_t ref_nctr_count(void* h) { return static_cast<loader::NCTRLoader*>(h)->tensors.size(); }
+
+// Tensor i: its name (into name, cap bytes), GGUF shape (ne0, ne1; ne1 = 0 for
+// 1-D), type, absolute file offset and byte count.
+int ref_nctr_tensor(void* h, size_t i, char* name, size_t cap, uint64_t* ne0, uint64_t* ne1, int* type,
+                    uint64_t* offset, uint64_t* nbytes) {
+    const auto& t = static_cast<loader::NCTRLoader*>(h)->tensors.at(i);
+    std::snprintf(name, cap, "%s", t.name.c_str());
+    *ne0 = t.shape.size() > 0 ? t.shape[0] : 0;
+    *ne1 = t.shape.size() > 1 ? t.shape[1] : 0;
+    *type = static_cast<int>(t.type);
+    *offset = t.file_offset;
+    *nbytes = t.nbytes;
+    return 0;
+}
+
+// NCTRLoader::validate_config (:146-184) into a ref_config_t (ctx_len = the
+// resulting kv_window; plain_ffn = !use_swiglu); -1 on a throw.
+int ref_nctr_config(void* h, ref_config_t* c, uint32_t* header_ctx_len, int* bos, int* eos, size_t* n_tokens) {
+    try {
+        engine::Config cfg;
+        static_cast<loader::NCTRLoader*>(h)->validate_config(cfg);
+        c->n_vocab = cfg.n_vocab;
+        c->n_embd = cfg.n_embd;
+        c->n_layer = cfg.n_layer;
+        c->n_head = cfg.n_head;
+        c->n_kv_head = cfg.n_kv_head;
+        c->head_dim = cfg.head_dim;
+        c->n_ff = cfg.n_ff;
+        c->ctx_len = cfg.kv_window;
+        c->rope_base = cfg.rope_base;
+        c->rope_scale = cfg.rope_scale;
+        c->rope_dim_count = cfg.rope_dim_count;
+        c->norm_eps = cfg.norm_eps;
+        c->plain_ffn = cfg.use_swiglu ? 0 : 1;
+        *header_ctx_len = cfg.ctx_len;
+        const auto& tm = static_cast<loader::NCTRLoader*>(h)->tok_meta;
+        *bos = tm.bos_id;
+        *eos = tm.eos_id;
+        *n_tokens = tm.tokens.size();
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+}  // extern "C"

@@ -2,6 +2,7 @@
 
     make -C oracle ref && python tests/golden/make_golden.py && python tests/golden/make_golden.py --decode
     python tests/golden/make_golden.py --types
+    python tests/golden/make_golden.py --quant      # needs gguf-py (the exporters' quantiser)
 
 Every expected output here is produced by the reference's own CPU path --
 rawllm_forward.hpp compiled with the reference's flags into
@@ -19,6 +20,10 @@ Outputs (numpy .npz, a few hundred KB in all):
   matvec_types.npz   proj_all_positions of the nine other weight types (F32,
                      F16, BF16, Q4_1, Q5_0, Q5_1, Q4_K, Q5_K, Q6_K) and a
                      proj_all_positions_multi case mixing K-quants with Q4_0
+  quant_gguf.npz     float rows and what gguf-py's gguf.quants.quantize writes
+                     for them (Q8_0, Q4_0, Q4_1, Q5_0, Q5_1, F16, BF16): the
+                     quantiser of the reference's exporters
+                     (train_nanity_fixed.py:1162-1169, nanity_convert.py:472-484)
 """
 from __future__ import annotations
 
@@ -134,7 +139,7 @@ def main() -> None:
     print("golden vectors written to", HERE)
 
 
-if __name__ == "__main__" and "--decode" not in sys.argv and "--types" not in sys.argv:
+if __name__ == "__main__" and not {"--decode", "--types", "--quant"} & set(sys.argv):
     main()
 
 
@@ -210,3 +215,40 @@ def types_golden() -> None:
 
 if __name__ == "__main__" and "--types" in sys.argv:
     types_golden()
+
+
+QUANT_TYPES = (S.GGML_Q8_0, S.GGML_Q4_0, S.GGML_Q4_1, S.GGML_Q5_0, S.GGML_Q5_1, S.GGML_F16, S.GGML_BF16)
+
+
+def quant_inputs() -> np.ndarray:
+    """8 x 256 float32: edge blocks (exact .5 ties after scaling, negative and
+    positive extremes, all-zero, constant, tiny and large scales) then random rows."""
+    rng = np.random.default_rng(77)
+    blocks = []
+    b = np.zeros(32, np.float32); b[0] = 127.0; b[1:] = np.arange(-15.5, 15.5, 1.0); blocks.append(b)   # Q8_0 ties
+    b = np.zeros(32, np.float32); b[0] = -8.0; b[1:] = np.arange(-7.75, 7.75, 0.5); blocks.append(b)      # Q4_0 ties
+    b = np.zeros(32, np.float32); b[5] = 16.0; b[6:] = np.arange(-12.5, 13.5, 1.0)[:26]; blocks.append(b)
+    blocks.append(np.zeros(32, np.float32))                                                          # d = 0
+    blocks.append(np.full(32, 0.375, np.float32))                                                    # max == min
+    blocks.append((rng.standard_normal(32) * 1e-6).astype(np.float32))                               # fp16-subnormal d
+    blocks.append((rng.standard_normal(32) * 3e4).astype(np.float32))                                # large
+    b = rng.standard_normal(32).astype(np.float32); b[3] = -4.0; b[9] = 4.0; blocks.append(b)        # |max| tie, sign
+    edge = np.concatenate(blocks).reshape(1, -1)                                                     # 1 x 256
+    rows = (rng.standard_normal((7, 256)) * rng.uniform(0.001, 2, (7, 1))).astype(np.float32)
+    return np.concatenate([edge, rows]).astype(np.float32)
+
+
+def quant_golden() -> None:
+    import gguf
+    from gguf.constants import GGMLQuantizationType as Q
+
+    X = quant_inputs()
+    out = {"x": X, "types": np.array(QUANT_TYPES, np.int64)}
+    for t in QUANT_TYPES:
+        out[f"q{t}"] = np.ascontiguousarray(gguf.quants.quantize(X, Q(t))).view(np.uint8).reshape(X.shape[0], -1)
+    np.savez_compressed(os.path.join(HERE, "quant_gguf.npz"), **out)
+    print("wrote", os.path.join(HERE, "quant_gguf.npz"), "with gguf", __import__("importlib.metadata").metadata.version("gguf"))
+
+
+if __name__ == "__main__" and "--quant" in sys.argv:
+    quant_golden()
