@@ -67,6 +67,8 @@ int set_err(int code, const std::string& msg) {
 int cuda_err(cudaError_t e, const char* what) {
     return set_err(NEON_ERR_CUDA, std::string("CUDA error in ") + what + ": " + cudaGetErrorString(e));
 }
+// NEON_OK for cudaSuccess, else the error as cuda_err reports it.
+int cuda_check(cudaError_t e, const char* what) { return e == cudaSuccess ? NEON_OK : cuda_err(e, what); }
 
 #define NEON_CUDA_TRY(call)                                      \
     do {                                                         \
@@ -925,7 +927,7 @@ int launch_quantize(const void* d_src, int src_type, size_t rows, size_t cols, i
                                                (long long)cols, dst_type, static_cast<unsigned char*>(d_dst),
                                                (long long)row_bytes_of(dst_type, cols));
     g_launches.fetch_add(1, std::memory_order_relaxed);
-    return cuda_err(cudaGetLastError(), "quantize_rows_kernel");
+    return cuda_check(cudaGetLastError(), "quantize_rows_kernel");
 }
 
 // Host float rows -> device GGUF rows of dst_type (caller frees *d_out).
@@ -946,7 +948,7 @@ int quantize_to_device(const void* host_src, int src_type, size_t rows, size_t c
     cudaError_t e = cudaMemcpyAsync(d_src, host_src, in_bytes, cudaMemcpyHostToDevice, st);
     rc = e == cudaSuccess ? launch_quantize(d_src, src_type, rows, cols, dst_type, d_dst, st, g_dev[device].sms)
                           : cuda_err(e, "quantisation input copy");
-    if (!rc) rc = cuda_err(cudaStreamSynchronize(st), "quantisation");
+    if (!rc) rc = cuda_check(cudaStreamSynchronize(st), "quantisation");
     cudaFree(d_src);
     if (rc) {
         cudaFree(d_dst);
@@ -985,7 +987,7 @@ int neon_cuda_quantize_host(const void* host_src, int src_type, size_t rows, siz
     if (rc) return rc;
     cudaError_t e = cudaMemcpy(host_dst, d, rows * row_bytes_of(dst_type, cols), cudaMemcpyDeviceToHost);
     cudaFree(d);
-    return cuda_err(e, "quantisation output copy");
+    return cuda_check(e, "quantisation output copy");
 }
 
 int neon_cuda_upload_quantized(const void* host_src, int src_type, size_t rows, size_t cols, int dst_type,

@@ -47,18 +47,67 @@ namespace neon {
 #define NEON_Q_DIV(a, b) ((a) / (b))
 #endif
 
-__host__ __device__ inline uint16_t q_f16_bits(float v) { return __half_as_ushort(__float2half_rn(v)); }
+// The bits of a float.
+__host__ __device__ inline uint32_t q_bits(float f) {
+#ifdef __CUDA_ARCH__
+    return __float_as_uint(f);
+#else
+    uint32_t x;
+    memcpy(&x, &f, 4);
+    return x;
+#endif
+}
+
+// fp32 -> binary16 bits, round to nearest even (numpy's cast): overflow to
+// infinity from 65520 up, subnormals below 2^-14, zero below 2^-25 (2^-25
+// itself ties to even, to zero); a NaN keeps its top payload bits, quieted.
+// Integer arithmetic only, the same on host and device.
+__host__ __device__ inline uint16_t q_f16_bits(float f) {
+    const uint32_t x = q_bits(f);
+    const uint32_t sign = (x >> 16) & 0x8000u;
+    const uint32_t ax = x & 0x7FFFFFFFu;
+    if (ax >= 0x7F800000u)
+        return (uint16_t)(sign | 0x7C00u | (ax > 0x7F800000u ? 0x200u | ((ax >> 13) & 0x3FFu) : 0u));
+    if (ax >= 0x477FF000u) return (uint16_t)(sign | 0x7C00u);
+    if (ax >= 0x38800000u) {
+        // normal: rebias the exponent (127 -> 15) and round off 13 mantissa bits
+        const uint32_t r = ax - 0x38000000u;
+        return (uint16_t)(sign | ((r + 0x0FFFu + ((r >> 13) & 1u)) >> 13));
+    }
+    if (ax < 0x33000000u) return (uint16_t)sign;
+    // subnormal: the value in units of 2^-24, rounded to nearest even
+    const uint32_t e = ax >> 23, m = (ax & 0x7FFFFFu) | 0x800000u;
+    const uint32_t shift = 126u - e;  // 14..24
+    const uint32_t q = m >> shift, rem = m & ((1u << shift) - 1u), half = 1u << (shift - 1u);
+    return (uint16_t)(sign | (q + ((rem > half || (rem == half && (q & 1u))) ? 1u : 0u)));
+}
+
+// Little-endian stores of 16 / 32 bits at any byte address.
+__host__ __device__ inline void q_put_u16(unsigned char* p, uint32_t v) {
+    p[0] = (unsigned char)(v & 0xFFu);
+    p[1] = (unsigned char)((v >> 8) & 0xFFu);
+}
+__host__ __device__ inline void q_put_u32(unsigned char* p, uint32_t v) {
+    q_put_u16(p, v & 0xFFFFu);
+    q_put_u16(p + 2, v >> 16);
+}
 
 // ggml's fp32 -> bf16: quiet a NaN, else round to nearest even on the bits.
 __host__ __device__ inline uint16_t q_bf16_bits(float v) {
-    uint32_t n;
-    memcpy(&n, &v, 4);
+    const uint32_t n = q_bits(v);
     if ((n & 0x7fffffffu) > 0x7f800000u) return (uint16_t)(((n & 0xffff0000u) | (64u << 16)) >> 16);
     return (uint16_t)(((uint64_t)n + (0x7fffu + ((n >> 16) & 1u))) >> 16);
 }
 
-// Value i of a row of a float type (F32, F16, BF16).
+// Value i of a row of a float type (F32, F16, BF16); rows start on an
+// element boundary (the device buffers are cudaMalloc'd, rows of whole elements).
 __host__ __device__ inline float q_src_value(const unsigned char* row, int src_type, long long i) {
+#ifdef __CUDA_ARCH__
+    if (src_type == NEON_GGML_F32) return reinterpret_cast<const float*>(row)[i];
+    const unsigned short h = reinterpret_cast<const unsigned short*>(row)[i];
+    if (src_type == NEON_GGML_F16) return __half2float(__ushort_as_half(h));
+    return __uint_as_float((uint32_t)h << 16);
+#else
     if (src_type == NEON_GGML_F32) {
         float v;
         memcpy(&v, row + 4 * i, 4);
@@ -71,6 +120,7 @@ __host__ __device__ inline float q_src_value(const unsigned char* row, int src_t
     float v;
     memcpy(&v, &u, 4);
     return v;
+#endif
 }
 
 __host__ __device__ inline int q_trunc_clamp(float v, int hi) {
@@ -78,10 +128,7 @@ __host__ __device__ inline int q_trunc_clamp(float v, int hi) {
     return q < 0 ? 0 : (q > hi ? hi : q);
 }
 
-__host__ __device__ inline void q_put_f16(unsigned char* p, float v) {
-    const uint16_t h = q_f16_bits(v);
-    memcpy(p, &h, 2);
-}
+__host__ __device__ inline void q_put_f16(unsigned char* p, float v) { q_put_u16(p, q_f16_bits(v)); }
 
 // One block of 32 values -> the GGUF block of `dst` (18 / 20 / 22 / 24 / 34
 // bytes). Returns false for a type this quantiser does not produce.
@@ -118,7 +165,7 @@ __host__ __device__ inline bool q_quantize_block(const float* x, int dst, unsign
         for (int j = 0; j < 16; ++j) qs[j] = (unsigned char)((q[j] & 0x0F) | ((q[j + 16] & 0x0F) << 4));
         if (five) {
             for (int j = 0; j < 32; ++j) qh |= (uint32_t)((q[j] >> 4) & 1) << j;
-            memcpy(out + 2, &qh, 4);
+            q_put_u32(out + 2, qh);
         }
         return true;
     }
@@ -141,7 +188,7 @@ __host__ __device__ inline bool q_quantize_block(const float* x, int dst, unsign
         if (five) {
             uint32_t qh = 0;
             for (int j = 0; j < 32; ++j) qh |= (uint32_t)((q[j] >> 4) & 1) << j;
-            memcpy(out + 4, &qh, 4);
+            q_put_u32(out + 4, qh);
         }
         return true;
     }
@@ -178,8 +225,7 @@ __global__ void quantize_rows_kernel(const unsigned char* __restrict__ src, long
             q_quantize_block(x, dst, orow + b * q_block_bytes(dst));
         } else {
             const float v = q_src_value(row, src_type, b);
-            const uint16_t h = dst == NEON_GGML_F16 ? q_f16_bits(v) : q_bf16_bits(v);
-            memcpy(orow + 2 * b, &h, 2);
+            q_put_u16(orow + 2 * b, dst == NEON_GGML_F16 ? q_f16_bits(v) : q_bf16_bits(v));
         }
     }
 }

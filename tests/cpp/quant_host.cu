@@ -26,11 +26,14 @@ extern "C" int q_host_quantize_rows(const unsigned char* src, int src_type, long
         } else {
             for (long long i = 0; i < cols; ++i) {
                 const float v = neon::q_src_value(row, src_type, i);
-                const uint16_t h = dst == NEON_GGML_F16 ? neon::q_f16_bits(v) : neon::q_bf16_bits(v);
-                orow[2 * i] = (unsigned char)(h & 0xFF);
-                orow[2 * i + 1] = (unsigned char)(h >> 8);
+                neon::q_put_u16(orow + 2 * i, dst == NEON_GGML_F16 ? neon::q_f16_bits(v) : neon::q_bf16_bits(v));
             }
         }
     }
     return 0;
+}
+
+// fp32 -> binary16 bits of n values (the quantiser's own conversion).
+extern "C" void q_host_f16_bits(const float* x, long long n, uint16_t* out) {
+    for (long long i = 0; i < n; ++i) out[i] = neon::q_f16_bits(x[i]);
 }

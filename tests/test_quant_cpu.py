@@ -28,6 +28,7 @@ def qh(tmp_path_factory):
                            os.path.join(ROOT, "tests", "cpp", "quant_host.cu"), "-o", so])
     L = C.CDLL(so)
     L.q_host_quantize_rows.argtypes = [C.c_void_p, C.c_int, C.c_longlong, C.c_longlong, C.c_int, C.c_void_p]
+    L.q_host_f16_bits.argtypes = [C.c_void_p, C.c_longlong, C.c_void_p]
     return L
 
 
@@ -74,3 +75,21 @@ def test_roundtrip_through_the_oracle_decoder(qh):
             span = x[r].reshape(-1, 32).max(axis=1, keepdims=True) - x[r].reshape(-1, 32).min(axis=1, keepdims=True)
             step = (span if dst in (S.GGML_Q4_1, S.GGML_Q5_1) else 2 * amax) / steps
             assert np.all(np.abs(y - x[r].reshape(-1, 32)) <= 0.51 * step + 1e-3 * amax), S.TYPE_NAMES[dst]
+
+
+def test_f16_conversion_matches_numpy(qh):
+    """The quantiser's integer fp32 -> fp16 (the scales it stores, and F16
+    output) against numpy's cast: every exponent, ties, subnormals, overflow."""
+    rng = np.random.default_rng(9)
+    bits = rng.integers(0, 2**32, 2_000_000, dtype=np.uint64).astype(np.uint32)
+    x = bits.view(np.float32)
+    x = x[np.isfinite(x)]
+    edges = np.array([0.0, -0.0, 1.0, 65504.0, 65519.996, 65520.0, 2.0**-14, 2.0**-24, 2.0**-25, 3 * 2.0**-26,
+                      2.0**-25 * 1.0000001, 6.1e-5, -5.96e-8, 1.0 + 2.0**-11, 1.0 + 3 * 2.0**-11, np.inf, -np.inf],
+                     np.float32)
+    x = np.concatenate([edges, x, (rng.standard_normal(100000) * 1e-3).astype(np.float32)])
+    got = np.empty(x.size, np.uint16)
+    qh.q_host_f16_bits(x.ctypes.data, x.size, got.ctypes.data)
+    with np.errstate(over="ignore"):
+        want = x.astype(np.float16).view(np.uint16)
+    assert np.array_equal(got, want), np.nonzero(got != want)[0][:10]
