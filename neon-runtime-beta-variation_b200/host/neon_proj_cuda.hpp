@@ -215,11 +215,15 @@ inline bool tensor_role(const std::string& name, int* role, int* layer) {
 // ranks of `comm` (every rank passes the whole loader; each keeps its shard).
 class Decoder {
 public:
+    // `quantize_to` (a NEON_GGML_* type, -1 for none): float weight tensors --
+    // a loader::NCTRLoader's, F32/F16 GGUF tensors -- are quantised on load to
+    // that type, as the exporters' gguf-py would have written them.
     template <class ConfigT, class LoaderT>
-    Decoder(const ConfigT& cfg, const LoaderT& loader, neon_comm_t comm = nullptr) {
+    Decoder(const ConfigT& cfg, const LoaderT& loader, neon_comm_t comm = nullptr, int quantize_to = -1) {
         const neon_model_config_t c = model_config(cfg);
         check(neon_cuda_model_create_tp(&c, comm, &m_));
         try {
+            if (quantize_to >= 0) check(neon_cuda_model_set_quantize(m_, quantize_to));
             for (const auto& t : loader.tensors) {
                 int role = 0, layer = -1;
                 if (!tensor_role(t.name, &role, &layer)) continue;
