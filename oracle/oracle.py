@@ -75,6 +75,18 @@ def lib():
     return _lib
 
 
+def ref_tree() -> str:
+    """The reference source tree oracle/Makefile compiles from (its REF
+    setting, overridable by the REF environment variable), or "" if absent."""
+    path = os.environ.get("REF", "")
+    if not path:
+        with open(os.path.join(HERE, "Makefile")) as f:
+            for line in f:
+                if line.startswith("REF ?="):
+                    path = line.split("=", 1)[1].strip()
+    return path if path and os.path.isdir(path) else ""
+
+
 def ref_available() -> bool:
     return os.path.exists(REF_SO)
 

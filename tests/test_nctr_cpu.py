@@ -4,6 +4,7 @@
 shapes, offsets, configuration, tokenizer ids and error messages; and the
 decode step of the oracle over the file's tensors against the reference's."""
 import ctypes as C
+import os
 
 import numpy as np
 import pytest
@@ -108,3 +109,34 @@ def test_oracle_decode_over_nctr_tensors_matches_reference(tmp_path):
     ta, la = mo.generate_greedy(p, 4)
     tb, lb = mr.generate_greedy(p, 4)
     assert np.array_equal(ta, tb) and np.array_equal(la.view(np.uint32), lb.view(np.uint32))
+
+
+REF_TREE = O.ref_tree()
+
+
+@pytest.mark.skipif(not REF_TREE or not os.path.exists(os.path.join(REF_TREE, "rawllm_nctr_loader.hpp")),
+                    reason="reference tree not present")
+@pytest.mark.parametrize("plain_ffn,has_output", [(False, False), (True, True)])
+def test_cpp_decoder_roles_from_reference_nctr_loader(tmp_path, plain_ffn, has_output):
+    """The C++ adapter compiles with the reference's loader::NCTRLoader and maps
+    every .nctr tensor to the role neon_cuda::Decoder uploads it as (and the
+    header to the model configuration)."""
+    import subprocess
+
+    from conftest import PKG, ROOT
+    exe = str(tmp_path / "nctr_roles")
+    N.load()
+    subprocess.check_call(["g++", "-std=c++17", "-O1", os.path.join(ROOT, "tests", "cpp", "nctr_roles.cpp"),
+                           "-I", os.path.join(ROOT, "include"), "-I", os.path.join(PKG, "host"), "-I", REF_TREE,
+                           "-L", PKG, "-lneon_cuda", f"-Wl,-rpath,{PKG}", "-lpthread", "-o", exe])
+    cfg = TINY.with_(plain_ffn=plain_ffn)
+    path = str(tmp_path / "m.nctr")
+    write_nctr(path, cfg, has_output=has_output)
+    lines = subprocess.run([exe, path], capture_output=True, text=True, check=True).stdout.splitlines()
+    c, tensors = N.load_nctr(path)
+    assert lines[0].split()[1:] == [str(v) for v in (c.n_vocab, c.n_embd, c.n_layer, c.n_head, c.n_kv_head,
+                                                     c.head_dim, c.n_ff, c.ctx_len, int(c.plain_ffn))]
+    assert len(lines) - 1 == len(tensors)
+    for line, (r, l, raw, t, ne0, ne1) in zip(lines[1:], tensors):
+        f = line.split()
+        assert [int(v) for v in f[1:]] == [r, l, ne0, ne1, t, raw.size], line
