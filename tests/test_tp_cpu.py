@@ -114,3 +114,46 @@ def test_tp_decode_gloo_world2_matches_one_rank(tmp_path):
     np.testing.assert_array_equal(r0["tokens"], toks)
     for i in range(n_new):
         assert rel_l2(r0["logits"][i], logits[i]) <= MODEL_L2_RTOL
+
+
+def test_tp_decode_gloo_world2_kquant_model(tmp_path):
+    """The same split of a Q4_K model with a Q6_K embedding: every column cut
+    falls on a 256-value super-block (n_head 8 x head_dim 64 = 256 columns of
+    attn_output per rank; 256 of ffn_down)."""
+    import torch.multiprocessing as mp
+
+    import tp_emulation as E
+
+    cfg = TINY.with_(n_head=8, n_kv_head=2)
+    seed, n_prompt, n_new = 4, 5, 5
+    cfg_args = ((cfg.n_vocab, cfg.n_embd, cfg.n_layer, cfg.n_head, cfg.n_kv_head, cfg.head_dim, cfg.n_ff),
+                dict(ctx_len=cfg.ctx_len, rope_base=cfg.rope_base, norm_eps=cfg.norm_eps, name="tiny-k"))
+    mp.start_processes(E.worker, args=(2, _free_port(), str(tmp_path), cfg_args, seed, n_prompt, n_new,
+                                       S.GGML_Q4_K, S.GGML_Q6_K), nprocs=2, join=True, start_method="spawn")
+    r0 = np.load(tmp_path / "rank0.npz")
+    one = E.RankModel(cfg, S.model_tensors(cfg, seed, wtype=S.GGML_Q4_K, embd_type=S.GGML_Q6_K), 0, 1)
+    toks, logits = one.generate(S.prompt_tokens(n_prompt, cfg.n_vocab, seed + 1), n_new, lambda x: x, lambda x: x)
+    np.testing.assert_array_equal(r0["tokens"], toks)
+    for i in range(n_new):
+        assert rel_l2(r0["logits"][i], logits[i]) <= 1e-4  # no activation quantisation: one fp32 sum reordered
+
+
+# Whether a K-quant model of each benchmark shape can be split: every column
+# cut of attn_output and ffn_down on a 256-value super-block. The head split
+# fixes attn_output's cuts at (heads per rank) x head_dim columns.
+KQ_SPLITTABLE = {
+    ("Qwen3-0.6B-shaped", 2): True, ("Qwen3-0.6B-shaped", 4): True, ("Qwen3-0.6B-shaped", 8): False,
+    ("Phi-4-mini-shaped", 2): True, ("Phi-4-mini-shaped", 4): True, ("Phi-4-mini-shaped", 8): False,
+    ("Llama-3-70B-shaped", 2): True, ("Llama-3-70B-shaped", 4): True, ("Llama-3-70B-shaped", 8): True,
+}
+
+
+@pytest.mark.parametrize("cfg", [S.QWEN3_0_6B, S.PHI4_MINI, S.LLAMA3_70B], ids=lambda c: c.name)
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_kquant_column_cuts_of_the_benchmark_shapes(cfg, world):
+    cuts = set()
+    for role in (S.ROLE_ATTN_OUT, S.ROLE_FFN_DOWN):
+        for r in range(world):
+            _, _, c0, c1 = NC.tp_shard(cfg, role, r, world)
+            cuts |= {c0, c1}
+    assert all(c % 256 == 0 for c in cuts) == KQ_SPLITTABLE[(cfg.name, world)]

@@ -22,21 +22,19 @@ import synth as S
 
 
 def dequant_row(raw: np.ndarray, typ: int, cols: int, row: int) -> np.ndarray:
-    nb, bb = cols // 32, S.BLOCK_BYTES[typ]
-    b = raw.reshape(-1, nb, bb)[row]
-    d = b[:, :2].copy().view(np.float16).astype(np.float32)
-    if typ == S.GGML_Q8_0:
-        q = b[:, 2:].copy().view(np.int8).astype(np.float32)
-    else:
-        qs = b[:, 2:]
-        q = np.concatenate([(qs & 0xF).astype(np.float32) - 8, (qs >> 4).astype(np.float32) - 8], axis=1)
-    return (d * q).reshape(-1).astype(np.float32)
+    """Row `row` of GGUF bytes `raw` (any weight type), decoded by the oracle."""
+    rb = S.row_bytes(typ, cols)
+    return O.dequantize_row(typ, np.ascontiguousarray(raw).reshape(-1)[row * rb:(row + 1) * rb], cols)
 
 
 def shard(raw: np.ndarray, typ: int, ne0: int, ne1: int, rng):
-    """Rows [r0, r1) x columns [c0, c1) of GGUF bytes -> (bytes, rows, cols)."""
+    """Rows [r0, r1) x columns [c0, c1) of GGUF bytes -> (bytes, rows, cols).
+    Columns are cut on the type's blocks (32 values; 256 for the K-quants)."""
     r0, r1, c0, c1 = rng
-    a = raw.reshape(ne1, ne0 // 32, S.BLOCK_BYTES[typ])[r0:r1, c0 // 32:c1 // 32]
+    be, bb = max(32, S.BLOCK_ELEMS[typ]), S.BLOCK_BYTES[typ] * (32 if S.BLOCK_ELEMS[typ] == 1 else 1)
+    if c0 % be or c1 % be:
+        raise ValueError(f"columns [{c0}, {c1}) do not fall on {be}-value blocks")
+    a = np.ascontiguousarray(raw).reshape(ne1, ne0 // be, bb)[r0:r1, c0 // be:c1 // be]
     return np.ascontiguousarray(a).reshape(-1), r1 - r0, c1 - c0
 
 
@@ -137,7 +135,8 @@ class RankModel:
         return np.array(toks, np.int32), np.stack(all_logits)
 
 
-def worker(rank: int, world: int, port: int, out_dir: str, cfg_args, seed: int, n_prompt: int, n_new: int):
+def worker(rank: int, world: int, port: int, out_dir: str, cfg_args, seed: int, n_prompt: int, n_new: int,
+           wtype: int = S.GGML_Q4_0, embd_type: int = S.GGML_Q8_0):
     """torch.multiprocessing entry: one gloo rank of the emulated TP decode."""
     import torch
     import torch.distributed as dist
@@ -157,7 +156,7 @@ def worker(rank: int, world: int, port: int, out_dir: str, cfg_args, seed: int, 
             dist.all_gather_object(parts, np.asarray(x, np.float32))
             return np.concatenate(parts)
 
-        m = RankModel(cfg, S.model_tensors(cfg, seed), rank, world)
+        m = RankModel(cfg, S.model_tensors(cfg, seed, wtype=wtype, embd_type=embd_type), rank, world)
         prompt = S.prompt_tokens(n_prompt, cfg.n_vocab, seed + 1)
         toks, logits = m.generate(prompt, n_new, allreduce, allgather)
         np.savez(os.path.join(out_dir, f"rank{rank}.npz"), tokens=toks, logits=logits)
