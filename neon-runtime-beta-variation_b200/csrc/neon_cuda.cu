@@ -5,6 +5,7 @@
 #include "neon_kernels.cuh"
 #include "neon_dequant.cuh"
 #include "neon_quant.cuh"
+#include "neon_prefill.cuh"
 
 #include <cuda_runtime.h>
 
@@ -33,6 +34,7 @@ constexpr int kStreamCtasPerSm = 4;
 thread_local std::string g_err;
 std::atomic<uint64_t> g_launches{0};
 std::atomic<int> g_pdl{1};
+std::atomic<int> g_prefill_mma{0};  // neon_cuda_set_prefill_mma
 
 struct DeviceState {
     bool ready = false;
@@ -530,6 +532,40 @@ int launch_group(const Group& g, const float* dX, size_t x_stride, size_t seq, c
     const bool q4 = g.type == NEON_GGML_Q4_0;
     if (seq == 1) return launch_stream(g.t, g.type, nb, dX, st, ds, accumulate, base, ext);
     if (ext) return set_err(NEON_ERR_UNSUPPORTED, "fused norm / epilogues need one position");
+    if (q4 && g_prefill_mma.load(std::memory_order_relaxed)) {
+        // tensor-core tiles of 64 rows x 64 positions over the Q8_0 activations
+        size_t start = 0;
+        while (start < g.t.size()) {
+            MatvecArgs a;
+            std::memset(&a, 0, sizeof(a));
+            a.nb = nb;
+            a.seq = (int)seq;
+            a.xq = ds.xq;
+            a.xd = ds.xd;
+            a.xs = ds.xs;
+            a.accumulate = accumulate;
+            int tiles = 0;
+            size_t n = std::min(g.t.size() - start, (size_t)kMaxSpans);
+            for (size_t i = 0; i < n; ++i) {
+                const neon_proj_target_t* tg = g.t[start + i];
+                Span& s = a.span[i];
+                s.qs = tg->W->qs;
+                s.d = tg->W->d;
+                s.y = tg->Y;
+                s.y_stride = (long long)tg->y_stride;
+                s.rows = (int)tg->W->rows;
+                s.tile0 = tiles;
+                tiles += (int)((tg->W->rows + kMmaRows - 1) / kMmaRows);
+            }
+            a.n_spans = (int)n;
+            a.n_tiles = tiles;
+            const dim3 grid(tiles, (unsigned)((seq + kMmaPos - 1) / kMmaPos));
+            int rc = launch_n(matvec_mma_q4_0_kernel, grid, kMmaThreads, 0, st, a);
+            if (rc) return rc;
+            start += n;
+        }
+        return NEON_OK;
+    }
     size_t start = 0;
     while (start < g.t.size()) {
         MatvecArgs a;
@@ -708,6 +744,11 @@ int neon_cuda_init(int device) {
     int rc = init_device(device);
     if (rc) return rc;
     NEON_CUDA_TRY(cudaSetDevice(device));
+    return NEON_OK;
+}
+
+int neon_cuda_set_prefill_mma(int enabled) {
+    g_prefill_mma.store(enabled ? 1 : 0);
     return NEON_OK;
 }
 
