@@ -133,6 +133,8 @@ def parse_args():
     p.add_argument("--layers", type=int, default=None,
                    help="decode workloads: fewer layers (kernel shapes unchanged; for profiling)")
     p.add_argument("--no-decode", action="store_true", help="matvec workloads: skip the decode sub-measurements")
+    p.add_argument("--prefill-mma", action="store_true",
+                   help="prompt passes of Q4_0 models on the tensor-core prefill kernel (neon_cuda_set_prefill_mma)")
     p.add_argument("--type-sweep", action="store_true",
                    help="time the matvec of every weight type (one JSON line each) instead of the headline")
     p.add_argument("--no-large-decode", action="store_true",
@@ -324,6 +326,7 @@ def measure_decode_gpu(name, prompt=None, new_tokens=None, comm=None, barrier=No
     toks = m.generate(prompt_toks, n_new)
     wall = max_over_ranks(time.perf_counter() - t0)
     ms = max_over_ranks(m.decode_ms)
+    prefill_ms = max_over_ranks(m.forward_ms)
     m.free()
     world = comm.world if comm is not None else 1
     return {"workload": decode_desc(cfg, n_prompt, n_new) + (" (weights cut from a seeded block pool)" if big else ""),
@@ -333,6 +336,9 @@ def measure_decode_gpu(name, prompt=None, new_tokens=None, comm=None, barrier=No
             "timing": "CUDA events around the replayed per-token graphs, max over ranks",
             "e2e_tokens_per_s": round(n_new / wall, 2),
             "e2e": "neon_cuda.Model.generate wall clock incl. prompt prefill and token read-back",
+            "prefill_ms": round(prefill_ms, 2), "prefill_tokens_per_s": round(n_prompt * 1e3 / prefill_ms, 1)
+            if prefill_ms > 0 else None,
+            "prefill": "the prompt pass (multi-position kernels), CUDA events, max over ranks",
             "load_s": round(load_s, 2)}, cfg, prompt_toks
 
 
@@ -385,6 +391,8 @@ def run_decode(args):
     import neon_cuda as N
 
     N.init(local)
+    if getattr(args, "prefill_mma", False):
+        N.set_prefill_mma(True)
     N.set_fused_collectives(not args.no_fused_collectives)
     comm = None
     barrier, max_over_ranks = (lambda: None), (lambda v: v)
@@ -533,6 +541,8 @@ def run_neon(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     N.init(local)
+    if getattr(args, "prefill_mma", False):
+        N.set_prefill_mma(True)
     dev = torch.device("cuda", local)
 
     host_w = host_rotation(rank, ROTATION)

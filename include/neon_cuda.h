@@ -272,6 +272,10 @@ NEON_API int neon_cuda_model_kv_shift(neon_model_t m, size_t keep, size_t discar
  * (n x n_kv_head*head_dim floats each). */
 NEON_API int neon_cuda_model_read_kv(neon_model_t m, int layer, size_t n, float* k_host, float* v_host);
 
+/* Device time (CUDA events, ms) of the last neon_cuda_model_forward -- for
+ * neon_cuda_model_generate, its prompt pass. */
+NEON_API int neon_cuda_model_forward_ms(neon_model_t m, float* ms);
+
 /* Time of the last neon_cuda_model_generate's decode steps, device-measured
  * (CUDA events around the replayed graphs), in milliseconds. */
 NEON_API int neon_cuda_model_decode_ms(neon_model_t m, float* ms);

@@ -43,6 +43,7 @@ enum : int { kEpiStore = 0, kEpiRope = 1, kEpiAtPos = 2, kEpiSwiglu = 3, kEpiSil
 #include <vector>
 
 using neon_internal::cuda_error;
+static int cuda_error_if(cudaError_t e, const char* what) { return e == cudaSuccess ? NEON_OK : cuda_error(e, what); }
 using neon_internal::error;
 
 namespace {
@@ -689,6 +690,8 @@ struct neon_model {
     cudaStream_t stream = nullptr;
     cudaGraphExec_t step_graph = nullptr;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    cudaEvent_t evf0 = nullptr, evf1 = nullptr;  // around the last forward pass
+    float forward_ms = 0.f;
     float decode_ms = 0.f;
     std::vector<void*> allocs;
 };
@@ -1139,7 +1142,10 @@ int neon_cuda_model_create_tp(const neon_model_config_t* cfg, neon_comm_t comm, 
     A((void**)&m->d_step, sizeof(int));
     A((void**)&m->d_err, sizeof(unsigned));
     if (!rc) rc = cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) == cudaSuccess ? NEON_OK : error(NEON_ERR_CUDA, "cudaStreamCreate");
-    if (!rc) rc = (cudaEventCreate(&m->ev0) == cudaSuccess && cudaEventCreate(&m->ev1) == cudaSuccess) ? NEON_OK : error(NEON_ERR_CUDA, "cudaEventCreate");
+    if (!rc) rc = (cudaEventCreate(&m->ev0) == cudaSuccess && cudaEventCreate(&m->ev1) == cudaSuccess &&
+                   cudaEventCreate(&m->evf0) == cudaSuccess && cudaEventCreate(&m->evf1) == cudaSuccess)
+                      ? NEON_OK
+                      : error(NEON_ERR_CUDA, "cudaEventCreate");
     if (!rc) {
         // RoPE cos/sin of every position with the host libm, as rope_apply computes
         // them (rawllm_forward.hpp:755-782): theta = ((float)pos / scale) * freq.
@@ -1378,9 +1384,12 @@ int neon_cuda_model_forward(neon_model_t m, const int32_t* tokens, size_t n, flo
     int rc = check_ready(m);
     if (rc) return rc;
     ModelDevice md(m->device);
+    DEC_TRY(cudaEventRecord(m->evf0, m->stream));
     rc = forward_device(m, tokens, n);
+    if (!rc) rc = cuda_error_if(cudaEventRecord(m->evf1, m->stream), "cudaEventRecord");
     if (!rc) rc = sync_and_check(m);
     if (rc) return rc;
+    cudaEventElapsedTime(&m->forward_ms, m->evf0, m->evf1);
     m->length += n;
     if (logits_host)
         DEC_TRY(cudaMemcpy(logits_host, m->world > 1 ? m->logits_full : m->logits, sizeof(float) * m->cfg.n_vocab,
@@ -1513,6 +1522,12 @@ int neon_cuda_model_read_kv(neon_model_t m, int layer, size_t n, float* k_host, 
     return NEON_OK;
 }
 
+int neon_cuda_model_forward_ms(neon_model_t m, float* ms) {
+    if (!m || !ms) return error(NEON_ERR_INVALID, "null argument");
+    *ms = m->forward_ms;
+    return NEON_OK;
+}
+
 int neon_cuda_model_decode_ms(neon_model_t m, float* ms) {
     if (!m || !ms) return error(NEON_ERR_INVALID, "null argument");
     *ms = m->decode_ms;
@@ -1535,6 +1550,8 @@ int neon_cuda_model_free(neon_model_t m) {
     if (m->d_out) cudaFree(m->d_out);
     if (m->ev0) cudaEventDestroy(m->ev0);
     if (m->ev1) cudaEventDestroy(m->ev1);
+    if (m->evf0) cudaEventDestroy(m->evf0);
+    if (m->evf1) cudaEventDestroy(m->evf1);
     if (m->stream) cudaStreamDestroy(m->stream);
     delete m;
     return NEON_OK;

@@ -82,6 +82,7 @@ C_ENTRY_POINTS = (
     "neon_cuda_model_kv_shift",
     "neon_cuda_model_read_kv",
     "neon_cuda_model_decode_ms",
+    "neon_cuda_model_forward_ms",
     "neon_cuda_model_free",
     "neon_cuda_comm_create",
     "neon_cuda_comm_ipc_handle",
@@ -169,6 +170,7 @@ def load(path: str | None = None) -> C.CDLL:
         L.neon_cuda_model_kv_shift.argtypes = [_vp, _sz, _sz]
         L.neon_cuda_model_read_kv.argtypes = [_vp, C.c_int, _sz, _vp, _vp]
         L.neon_cuda_model_decode_ms.argtypes = [_vp, C.POINTER(C.c_float)]
+        L.neon_cuda_model_forward_ms.argtypes = [_vp, C.POINTER(C.c_float)]
         L.neon_cuda_model_free.argtypes = [_vp]
         L.neon_cuda_comm_create.argtypes = [C.c_int, C.c_int, _sz, C.POINTER(_vp)]
         L.neon_cuda_comm_ipc_handle.argtypes = [_vp, _vp, C.POINTER(_sz)]
@@ -656,6 +658,13 @@ class Model:
     def decode_ms(self) -> float:
         ms = C.c_float()
         _check(load().neon_cuda_model_decode_ms(self.handle, C.byref(ms)))
+        return ms.value
+
+    @property
+    def forward_ms(self) -> float:
+        """Device time of the last forward (for generate: the prompt pass), ms."""
+        ms = C.c_float()
+        _check(load().neon_cuda_model_forward_ms(self.handle, C.byref(ms)))
         return ms.value
 
     def free(self) -> None:
