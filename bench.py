@@ -511,7 +511,10 @@ def run_reference(args):
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": 0,
         "steps": K, "warmup": W, "ms_per_step": round(dt / K * 1e3, 4), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "int8/fp32", "data": "synthetic", "config": cfg,
+        "scaling": "weak", "vs_baseline": None,
+        "dtype": ("int8/fp32 (q4_0 x q8_0 integer block dot, fp32 scales)" if TYPE == S.GGML_Q4_0
+                  else f"fp32 ({TYPE_NAME.lower()} rows dequantised, AVX2 fp32 dot)"),
+        "data": "synthetic", "config": cfg,
         "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": cores, "kind": kind,
                          "sample": f"{K} steps x {per_step_calls} calls of the reference's "
                                    f"fwd::proj_all_positions (util::ThreadPool of {cores})"},
