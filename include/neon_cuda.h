@@ -336,10 +336,11 @@ NEON_API int neon_cuda_model_create_tp(const neon_model_config_t* cfg, neon_comm
  * results. Set it before the first generate. */
 NEON_API int neon_cuda_set_fused_collectives(int enabled);
 
-/* Multi-position Q4_0 calls (prefill) on the tensor cores: int8 MMA tiles
- * (mma.sync m16n8k32) of 64 rows x 64 positions, each output bit-exact with
- * the reference's dot_q4_0_q8_0. Off by default (the CUDA-core kernel runs)
- * until a GPU run has validated it; the switch is process-wide. */
+/* Multi-position Q4_0 and Q8_0 calls (prefill) on the tensor cores, tiles of
+ * 64 rows x 64 positions: Q4_0 as int8 MMA (mma.sync m16n8k32), each output
+ * bit-exact with the reference's dot_q4_0_q8_0; Q8_0 as TF32 MMA with X split
+ * into two TF32 terms (fp32 accuracy). Off by default (the CUDA-core kernel
+ * runs) until a GPU run has validated it; the switch is process-wide. */
 NEON_API int neon_cuda_set_prefill_mma(int enabled);
 
 /* Launch option: programmatic dependent launch (PDL) lets a matvec fetch its

@@ -532,17 +532,20 @@ int launch_group(const Group& g, const float* dX, size_t x_stride, size_t seq, c
     const bool q4 = g.type == NEON_GGML_Q4_0;
     if (seq == 1) return launch_stream(g.t, g.type, nb, dX, st, ds, accumulate, base, ext);
     if (ext) return set_err(NEON_ERR_UNSUPPORTED, "fused norm / epilogues need one position");
-    if (q4 && g_prefill_mma.load(std::memory_order_relaxed)) {
-        // tensor-core tiles of 64 rows x 64 positions over the Q8_0 activations
+    if (g_prefill_mma.load(std::memory_order_relaxed)) {
+        // tensor-core tiles of 64 rows x 64 positions: Q4_0 over the Q8_0
+        // activations (int8 MMA), Q8_0 over fp32 X (TF32 MMA)
         size_t start = 0;
         while (start < g.t.size()) {
             MatvecArgs a;
             std::memset(&a, 0, sizeof(a));
             a.nb = nb;
             a.seq = (int)seq;
-            a.xq = ds.xq;
-            a.xd = ds.xd;
-            a.xs = ds.xs;
+            a.x = dX;
+            a.x_stride = (long long)x_stride;
+            a.xq = q4 ? ds.xq : nullptr;
+            a.xd = q4 ? ds.xd : nullptr;
+            a.xs = q4 ? ds.xs : nullptr;
             a.accumulate = accumulate;
             int tiles = 0;
             size_t n = std::min(g.t.size() - start, (size_t)kMaxSpans);
@@ -560,7 +563,7 @@ int launch_group(const Group& g, const float* dX, size_t x_stride, size_t seq, c
             a.n_spans = (int)n;
             a.n_tiles = tiles;
             const dim3 grid(tiles, (unsigned)((seq + kMmaPos - 1) / kMmaPos));
-            int rc = launch_n(matvec_mma_q4_0_kernel, grid, kMmaThreads, 0, st, a);
+            int rc = launch_n(q4 ? matvec_mma_q4_0_kernel : matvec_mma_q8_0_kernel, grid, kMmaThreads, 0, st, a);
             if (rc) return rc;
             start += n;
         }

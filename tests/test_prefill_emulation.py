@@ -1,5 +1,6 @@
-"""The index arithmetic of the tensor-core prefill kernel
-(csrc/neon_prefill.cuh, matvec_mma_q4_0_kernel), emulated on the CPU: the
+"""The index arithmetic of the tensor-core prefill kernels
+(csrc/neon_prefill.cuh: matvec_mma_q4_0_kernel, and below matvec_mma_q8_0_kernel),
+emulated on the CPU: the
 staging of weights and activations into shared memory, every lane's MMA
 fragments (PTX ISA layouts of mma.m16n8k32 .s8: A rows g / g+8 with values
 4t..4t+3 and 16+4t..; B values 4t.. / 16+4t.. of column g; D rows g / g+8,
@@ -116,3 +117,101 @@ def test_prefill_mma_fragments_reach_every_block_once(rows, cols, seq):
     W = S.weights(S.GGML_Q4_0, rows, cols, seed=rows + seq)
     X = S.activations(seq, cols, seed=seq)
     emulate(W, rows, cols, X)
+
+
+KB8, WP8, XP8 = 2, 5, 17  # the Q8_0 kernel: blocks per chunk, staged pitches (uint4 / float4)
+
+
+def emulate_q8(W, rows, cols, X):
+    """matvec_mma_q8_0_kernel's staging and m16n8k8 TF32 fragments (A rows g /
+    g+8, values t and t+4 of each 8-value step; B values t, t+4 of column g; D
+    rows g / g+8, columns 2t, 2t+1): every lane's block step must sum exactly
+    q[row, block, :] . x[pos, block, :] and scale it by d_w[row, block]."""
+    seq, nb = X.shape[0], cols // 32
+    blocks = W.reshape(rows, nb, 34)
+    q = np.ascontiguousarray(blocks[:, :, 2:]).view(np.int8).reshape(rows, nb, 32).astype(np.float64)
+    wscale = blocks[:, :, :2].copy().view(np.float16).astype(np.float32).reshape(rows, nb)
+    xb = X.reshape(seq, nb, 32).astype(np.float64)
+    want = np.einsum("rbk,pbk->rpb", q, xb)
+    seen = np.zeros((rows, seq, nb), bool)
+    lanes = np.arange(32)
+    g, t = lanes // 4, lanes % 4
+    for tile in range((rows + ROWS_T - 1) // ROWS_T):
+        row0 = tile * ROWS_T
+        for p0 in range(0, seq, POS_T):
+            for c in range((nb + KB8 - 1) // KB8):
+                b0 = c * KB8
+                sw = np.zeros((ROWS_T * WP8, 16), np.uint8)
+                swd = np.zeros(ROWS_T * KB8, np.float32)
+                sx = np.zeros((POS_T * XP8, 4), np.float32)
+                for tid in range(128):
+                    for i in range(2):
+                        idx = tid + 128 * i
+                        row, piece = idx // (2 * KB8), idx % (2 * KB8)
+                        gr, gb = row0 + row, b0 + piece // 2
+                        if gr < rows and gb < nb:
+                            sw[row * WP8 + piece] = blocks[gr, gb, 2 + (piece & 1) * 16:2 + (piece & 1) * 16 + 16]
+                    row, kb = tid // KB8, tid % KB8
+                    if row0 + row < rows and b0 + kb < nb:
+                        swd[tid] = wscale[row0 + row, b0 + kb]
+                    for i in range(8):
+                        idx = tid + 128 * i
+                        pos, piece = idx // (8 * KB8), idx % (8 * KB8)
+                        gp, gb = p0 + pos, b0 + piece // 8
+                        if gp < seq and gb < nb:
+                            sx[pos * XP8 + piece] = X[gp, gb * 32 + (piece & 7) * 4:gb * 32 + (piece & 7) * 4 + 4]
+                sq = sw.view(np.int8).reshape(ROWS_T * WP8 * 16)
+                sxf = sx.reshape(-1)
+                for kb in range(min(KB8, nb - b0)):
+                    for w in range(WARPS):
+                        wr = 16 * w
+                        for j in range(8):
+                            D = np.zeros((16, 8))
+                            for ks in range(4):
+                                A = np.zeros((16, 8))
+                                B = np.zeros((8, 8))
+                                for l in range(32):
+                                    qg = ((wr + g[l]) * WP8 + 2 * kb) * 16
+                                    qg8 = ((wr + g[l] + 8) * WP8 + 2 * kb) * 16
+                                    xs = ((8 * j + g[l]) * XP8 + 8 * kb) * 4
+                                    A[g[l], t[l]] = sq[qg + 8 * ks + t[l]]
+                                    A[g[l] + 8, t[l]] = sq[qg8 + 8 * ks + t[l]]
+                                    A[g[l], t[l] + 4] = sq[qg + 8 * ks + t[l] + 4]
+                                    A[g[l] + 8, t[l] + 4] = sq[qg8 + 8 * ks + t[l] + 4]
+                                    B[t[l], g[l]] = sxf[xs + 8 * ks + t[l]]
+                                    B[t[l] + 4, g[l]] = sxf[xs + 8 * ks + t[l] + 4]
+                                D += A @ B
+                            for l in range(32):
+                                dg, dg8 = swd[(wr + g[l]) * KB8 + kb], swd[(wr + g[l] + 8) * KB8 + kb]
+                                for dr, dc, sc in ((0, 0, dg), (0, 1, dg), (8, 0, dg8), (8, 1, dg8)):
+                                    r, p = row0 + wr + g[l] + dr, p0 + 8 * j + 2 * t[l] + dc
+                                    if r < rows and p < seq:
+                                        b = b0 + kb
+                                        assert abs(D[g[l] + dr, 2 * t[l] + dc] - want[r, p, b]) <= 1e-9 * (1 + abs(want[r, p, b]))
+                                        assert sc == wscale[r, b] and not seen[r, p, b]
+                                        seen[r, p, b] = True
+    assert seen.all()
+
+
+@pytest.mark.parametrize("rows,cols,seq", [(70, 160, 9), (64, 64, 66)])
+def test_prefill_mma_q8_0_fragments(rows, cols, seq):
+    W = S.weights(S.GGML_Q8_0, rows, cols, seed=rows + seq)
+    X = S.activations(seq, cols, seed=seq)
+    emulate_q8(W, rows, cols, X)
+
+
+def test_tf32_split_carries_fp32():
+    """x_hi + x_lo, each rounded to TF32 (10 mantissa bits, nearest, ties away
+    as cvt.rna), reproduces x to within 2^-21 relative: the Q8_0 kernel's
+    products q*x_hi + q*x_lo are fp32-accurate."""
+    x = np.random.default_rng(1).standard_normal(200000).astype(np.float32)
+
+    def tf32(v):
+        u = v.view(np.uint32).astype(np.uint64)
+        u = (u + 0x1000) & ~np.uint64(0x1FFF)  # round half away on the 13 dropped bits, clear them
+        return u.astype(np.uint32).view(np.float32)
+
+    hi = tf32(x)
+    lo = tf32((x - hi).astype(np.float32))
+    rel = np.abs((hi.astype(np.float64) + lo) - x) / np.abs(x)
+    assert rel.max() <= 2.0 ** -21

@@ -1,7 +1,8 @@
-"""Multi-position Q4_0 projections (prefill) on the tensor cores
-(neon_cuda_set_prefill_mma, csrc/neon_prefill.cuh) against the oracle, BIT
-FOR BIT: each output is dot_q4_0_q8_0's block sequence with the integer block
-sums from int8 MMA. Also the decoder's prompt pass with the switch on.
+"""Multi-position projections (prefill) on the tensor cores
+(neon_cuda_set_prefill_mma, csrc/neon_prefill.cuh) against the oracle: Q4_0
+BIT FOR BIT (each output is dot_q4_0_q8_0's block sequence with the integer
+block sums from int8 MMA), Q8_0 within the per-row matvec bar (TF32 MMA with X
+split in two TF32 terms). Also the decoder's prompt pass with the switch on.
 Collected after the other GPU suites (the kernel is the newest): with -x, a
 failure here stops nothing else."""
 import numpy as np
@@ -10,7 +11,7 @@ import pytest
 import neon_cuda as N
 import oracle as O
 import synth as S
-from conftest import MODEL_L2_RTOL, rel_l2
+from conftest import MATVEC_RTOL, MODEL_L2_RTOL, max_rel_err, rel_l2
 
 pytestmark = pytest.mark.gpu
 torch = pytest.importorskip("torch")
@@ -42,6 +43,19 @@ def test_bit_exact_with_the_reference_arithmetic(rows, cols, seq):
     Y = dy.cpu().numpy().reshape(seq, rows + 3)
     assert np.array_equal(bits(Y[:, :rows]), bits(O.proj_all_positions(S.GGML_Q4_0, W, rows, cols, X)))
     assert np.all(Y[:, rows:] == -5.0)
+
+
+@pytest.mark.parametrize("rows,cols,seq", [(70, 160, 9), (1000, 4096, 66), (4096, 4096, 64), (33, 32, 3)])
+def test_q8_0_within_the_matvec_bar(rows, cols, seq):
+    W = S.weights(S.GGML_Q8_0, rows, cols, seed=rows + seq)
+    X = S.activations(seq, cols, seed=seq + 2)
+    dt = N.DeviceTensor(W, S.GGML_Q8_0, rows, cols)
+    dx = torch.from_numpy(X.copy()).cuda()
+    dy = torch.zeros(seq * rows, device="cuda")
+    dt.matvec(dx, dy, seq=seq)
+    torch.cuda.synchronize()
+    got = dy.cpu().numpy().reshape(seq, rows)
+    assert max_rel_err(got, O.proj_all_positions(S.GGML_Q8_0, W, rows, cols, X)) <= MATVEC_RTOL
 
 
 def test_multi_targets_bit_exact():
