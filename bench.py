@@ -133,6 +133,9 @@ def parse_args():
     p.add_argument("--layers", type=int, default=None,
                    help="decode workloads: fewer layers (kernel shapes unchanged; for profiling)")
     p.add_argument("--no-decode", action="store_true", help="matvec workloads: skip the decode sub-measurements")
+    p.add_argument("--weights", choices=["q4_0", "q4_k"], default="q4_0",
+                   help="decode workloads: Q4_0 projections + Q8_0 embedding (default), or Q4_K + Q6_K "
+                        "(what nanity_convert.py --quant Q4_K writes)")
     p.add_argument("--prefill-mma", action="store_true",
                    help="prompt passes of Q4_0 models on the tensor-core prefill kernel (neon_cuda_set_prefill_mma)")
     p.add_argument("--type-sweep", action="store_true",
@@ -141,8 +144,10 @@ def parse_args():
                    help="matvec workloads: skip the Llama-3-70B-shaped split decode sub-measurement")
     args = p.parse_args()
     select_workload(args.workload)
-    global LAYERS
+    global LAYERS, WTYPE, EMBD_TYPE
     LAYERS = args.layers
+    if args.weights == "q4_k":
+        WTYPE, EMBD_TYPE = S.GGML_Q4_K, S.GGML_Q6_K
     return args
 
 
@@ -278,6 +283,7 @@ def host_rotation(rank, n):
 
 
 LAYERS = None  # --layers
+WTYPE, EMBD_TYPE = S.GGML_Q4_0, S.GGML_Q8_0  # --weights: decode models' projection / embedding types
 
 
 def decode_config(name, prompt=None, new_tokens=None):
@@ -292,9 +298,9 @@ def decode_config(name, prompt=None, new_tokens=None):
 
 def decode_desc(cfg, n_prompt, n_new):
     return (f"{cfg.name} decoder ({cfg.n_layer} layers, hidden {cfg.n_embd}, {cfg.n_head}/{cfg.n_kv_head} heads, "
-            f"head_dim {cfg.head_dim}, ffn {cfg.n_ff}, vocab {cfg.n_vocab}), random-init Q4_0 projections, "
-            f"Q8_0 tied embedding/lm_head, fp32 norms; greedy decode of {n_new} tokens after a {n_prompt}-token "
-            f"seeded-random prompt")
+            f"head_dim {cfg.head_dim}, ffn {cfg.n_ff}, vocab {cfg.n_vocab}), random-init {S.TYPE_NAMES[WTYPE]} "
+            f"projections, {S.TYPE_NAMES[EMBD_TYPE]} tied embedding/lm_head, fp32 norms; greedy decode of {n_new} "
+            f"tokens after a {n_prompt}-token seeded-random prompt")
 
 
 def is_big(cfg):
@@ -302,9 +308,14 @@ def is_big(cfg):
 
 
 def model_bytes(cfg):
-    """GGUF bytes of the synthetic decoder: Q4_0 projections, Q8_0 embedding."""
-    per_layer = (2 * cfg.q_dim * cfg.n_embd + 2 * cfg.kv_dim * cfg.n_embd + 3 * cfg.n_ff * cfg.n_embd) * 18 // 32
-    return cfg.n_layer * per_layer + cfg.n_vocab * cfg.n_embd * 34 // 32
+    """GGUF bytes of the synthetic decoder's projections and tied embedding."""
+    def rb(rows, cols, t):
+        return rows * S.row_bytes(t, cols)
+
+    per_layer = (rb(cfg.q_dim, cfg.n_embd, WTYPE) + 2 * rb(cfg.kv_dim, cfg.n_embd, WTYPE)
+                 + rb(cfg.n_embd, cfg.q_dim, WTYPE) + (1 if cfg.plain_ffn else 2) * rb(cfg.n_ff, cfg.n_embd, WTYPE)
+                 + rb(cfg.n_embd, cfg.n_ff, WTYPE))
+    return cfg.n_layer * per_layer + rb(cfg.n_vocab, cfg.n_embd, EMBD_TYPE)
 
 
 def measure_decode_gpu(name, prompt=None, new_tokens=None, comm=None, barrier=None, max_over_ranks=None):
@@ -318,7 +329,7 @@ def measure_decode_gpu(name, prompt=None, new_tokens=None, comm=None, barrier=No
     cfg, n_prompt, n_new = decode_config(name, prompt, new_tokens)
     big = is_big(cfg)
     t0 = time.perf_counter()
-    m = N.Model(cfg, S.model_tensors(cfg, seed=5, pooled=big), comm)
+    m = N.Model(cfg, S.model_tensors(cfg, seed=5, pooled=big, wtype=WTYPE, embd_type=EMBD_TYPE), comm)
     load_s = time.perf_counter() - t0
     prompt_toks = S.prompt_tokens(n_prompt, cfg.n_vocab, 6)
     barrier()
@@ -363,7 +374,8 @@ def measure_decode_cpu(cfg, prompt_toks, steps, threads=None):
     import oracle as O
 
     kind = "reference" if O.ref_available() else "port"
-    m = O.Model(cfg, S.model_tensors(cfg, seed=5, pooled=is_big(cfg)), kind, threads=threads)
+    m = O.Model(cfg, S.model_tensors(cfg, seed=5, pooled=is_big(cfg), wtype=WTYPE, embd_type=EMBD_TYPE), kind,
+                threads=threads)
     logits = m.forward(prompt_toks)
     nxt = int(np.argmax(logits))
     t0 = time.perf_counter()

@@ -82,31 +82,34 @@ _pools = {}
 
 
 def pooled_weights(ggml_type: int, rows: int, cols: int, seed: int) -> np.ndarray:
-    """rows x cols GGUF bytes cut from a seeded pool of 8M random blocks (same
-    per-block distributions as q4_0_weights / q8_0_weights) at a seeded
+    """rows x cols GGUF bytes cut from a seeded pool of 8M random 32-value
+    blocks' worth of the type (same per-block distributions as `weights`) at a seeded
     offset: a read-only view when the tensor fits in the pool, else a copy
     that repeats the pool. For benchmark models of tens of GB, where drawing
     every block would take minutes; tensors are not independent of one another."""
+    be = max(BLOCK, BLOCK_ELEMS[ggml_type])  # pool unit: a 32-value block (256 for the K-quants)
+    bb = BLOCK_BYTES[ggml_type] * (BLOCK if BLOCK_ELEMS[ggml_type] == 1 else 1)
+    n_pool = _POOL_BLOCKS * BLOCK // be
     if ggml_type not in _pools:
-        gen = q4_0_weights if ggml_type == GGML_Q4_0 else q8_0_weights
-        pool = gen(_POOL_BLOCKS // 256, 256 * BLOCK, seed=987654321).reshape(-1)
+        pool = weights(ggml_type, n_pool // 256, 256 * be, seed=987654321).reshape(-1)
         pool.flags.writeable = False
         _pools[ggml_type] = pool
     pool = _pools[ggml_type]
-    bb = BLOCK_BYTES[ggml_type]
-    n = rows * (cols // BLOCK)
+    if cols % be:
+        raise ValueError(f"cols={cols} is not a multiple of {be}")
+    n = rows * (cols // be)
     rng = np.random.default_rng(seed)
-    if n <= _POOL_BLOCKS:
-        off = int(rng.integers(0, _POOL_BLOCKS - n + 1)) * bb
-        return pool[off:off + n * bb].reshape(rows, (cols // BLOCK) * bb)
+    if n <= n_pool:
+        off = int(rng.integers(0, n_pool - n + 1)) * bb
+        return pool[off:off + n * bb].reshape(rows, (cols // be) * bb)
     out = np.empty(n * bb, np.uint8)
-    pos, src = 0, int(rng.integers(0, _POOL_BLOCKS)) * bb
+    pos, src = 0, int(rng.integers(0, n_pool)) * bb
     while pos < out.size:
         k = min(out.size - pos, pool.size - src)
         out[pos:pos + k] = pool[src:src + k]
         pos += k
         src = 0
-    return out.reshape(rows, (cols // BLOCK) * bb)
+    return out.reshape(rows, (cols // be) * bb)
 
 
 def _f16_bytes(a) -> np.ndarray:
