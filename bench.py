@@ -138,6 +138,8 @@ def parse_args():
                         "(what nanity_convert.py --quant Q4_K writes)")
     p.add_argument("--prefill-mma", action="store_true",
                    help="prompt passes of Q4_0 models on the tensor-core prefill kernel (neon_cuda_set_prefill_mma)")
+    p.add_argument("--batch", type=int, default=1,
+                   help="matvec workloads: positions per call; > 1 times the prefill path (one JSON line)")
     p.add_argument("--type-sweep", action="store_true",
                    help="time the matvec of every weight type (one JSON line each) instead of the headline")
     p.add_argument("--no-large-decode", action="store_true",
@@ -721,6 +723,72 @@ def run_neon(args):
         dist.destroy_process_group()
 
 
+def run_prefill(args):
+    """Several positions per call (prefill): `--batch` positions of X against
+    the workload's matrix, a CUDA graph of calls over a rotation larger than
+    L2, device-timed. One JSON line: TFLOP/s (2 * batch * rows * cols per call)
+    against the measured dense bf16 tensor peak, and the HBM fraction."""
+    import torch
+
+    import neon_cuda as N
+
+    torch.cuda.set_device(0)
+    N.init(0)
+    if args.prefill_mma:
+        N.set_prefill_mma(True)
+    dev = torch.device("cuda", 0)
+    B = args.batch
+    calls = 64
+    tensors = [N.DeviceTensor(w, TYPE, ROWS, COLS) for w in host_rotation(0, ROTATION)]
+    X = S.activations(B, COLS, seed=7)
+    dx = torch.from_numpy(X).to(dev)
+    ys = torch.zeros((ROTATION, B * ROWS), device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(stream):
+        tensors[0].matvec(dx, ys[0], seq=B, stream=stream)
+    stream.synchronize()
+    launches0 = N.launch_count()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for j in range(calls):
+            tensors[j % ROTATION].matvec(dx, ys[j % ROTATION], seq=B, stream=stream)
+    per_call_launches = (N.launch_count() - launches0) // calls
+    K, W = args.steps, max(3, args.warmup)
+    with torch.cuda.stream(stream):
+        for _ in range(W):
+            graph.replay()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        for _ in range(K):
+            graph.replay()
+        end.record(stream)
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end)
+    per_call_s = ms / 1e3 / (K * calls)
+    flops = 2.0 * B * ROWS * COLS
+    bytes_call = S.algorithmic_bytes(TYPE, ROWS, COLS, seq=B)
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            tc_peak, tc_kind = float(json.load(f)["bf16_tflops"]), "measured dense bf16 (MEASURED_PEAKS.json)"
+    except Exception:
+        tc_peak, tc_kind = 1590.0, "fallback 1.59 PFLOP/s bf16"
+    hbm, _ = measured_peak()
+    tflops = flops / per_call_s / 1e12
+    print(json.dumps({
+        "metric": f"{TYPE_NAME} prefill TFLOP/s (batch {B})", "value": round(tflops, 2), "unit": "TFLOP/s",
+        "n_gpus": 1, "steps": K, "warmup": W, "ms_per_step": round(ms / K, 4), "higher_is_better": True,
+        "kernel": ("tensor cores (int8 / TF32 mma.sync)" if args.prefill_mma else "CUDA cores (multi-position kernel)"),
+        "config": {**workload_config(), "batch": B, "calls_per_step": calls},
+        "us_per_call": round(per_call_s * 1e6, 2), "launches_per_call": per_call_launches,
+        "roofline": {"tensor": {"achieved": round(tflops, 2), "peak": tc_peak, "peak_source": tc_kind,
+                                "frac": round(tflops / tc_peak, 4)},
+                     "hbm": {"achieved": round(bytes_call / per_call_s / 1e9, 1), "peak": hbm,
+                             "frac": round(bytes_call / per_call_s / 1e9 / hbm, 4)}},
+    }), flush=True)
+
+
 def run_type_sweep(args):
     """One JSON line per weight type: device GB/s of a CUDA graph of 1024
     one-position launches over a rotation of tensors larger than L2, timed
@@ -775,6 +843,8 @@ def main():
     args = parse_args()
     if args.type_sweep and args.impl != "reference":
         run_type_sweep(args)
+    elif args.batch > 1 and args.impl != "reference" and args.workload not in DECODE_WORKLOADS:
+        run_prefill(args)
     elif args.impl == "reference":
         run_reference(args)
     elif args.workload in DECODE_WORKLOADS:
