@@ -17,9 +17,9 @@
 //
 // Work decomposition: a CTA (8 warps) owns a tile of 8 consecutive rows, one
 // row per warp. A warp walks its row a chunk at a time: the chunk's bytes are
-// read with coalesced 128-bit loads (the next chunk's loads are in flight
-// while the current one is decoded), parked in the warp's shared-memory
-// buffer, and every lane then takes whole 32-value sub-blocks from it (one
+// read with coalesced 128-bit loads (two chunks in flight per warp, held in
+// registers), parked in the warp's shared-memory buffer, and every lane then
+// takes whole 32-value sub-blocks from it (one
 // for the 32-value types, two for the K-quants: 8 super-blocks = 64
 // sub-blocks a chunk): their integer codes and affine map (dq_codes), and
 // the dot product a*sum((code - OFF)*x) + b*sum(x) on packed fp32 pairs
@@ -70,22 +70,26 @@ template <int TYPE> struct DqShape {
 // Host view of the block geometry of a type: values per block, bytes per
 // block, blocks per chunk (0 if the type is not one of this kernel's).
 __host__ __device__ inline void dq_geometry(int type, int* be, int* bb, int* cb) {
-    int e = 0, b = 0, c = 0;
     switch (type) {
-        case NEON_GGML_F32: e = 32; b = 128; c = 32; break;
-        case NEON_GGML_F16: e = 32; b = 64; c = 32; break;
-        case NEON_GGML_BF16: e = 32; b = 64; c = 32; break;
-        case NEON_GGML_Q4_1: e = 32; b = 20; c = 32; break;
-        case NEON_GGML_Q5_0: e = 32; b = 22; c = 32; break;
-        case NEON_GGML_Q5_1: e = 32; b = 24; c = 32; break;
-        case NEON_GGML_Q4_K: e = 256; b = 144; c = 8; break;
-        case NEON_GGML_Q5_K: e = 256; b = 176; c = 8; break;
-        case NEON_GGML_Q6_K: e = 256; b = 210; c = 8; break;
-        default: break;
+#define NEON_DQ_GEOMETRY(T)    \
+    case T:                    \
+        *be = DqType<T>::BE;   \
+        *bb = DqType<T>::BB;   \
+        *cb = DqType<T>::CB;   \
+        return;
+        NEON_DQ_GEOMETRY(NEON_GGML_F32)
+        NEON_DQ_GEOMETRY(NEON_GGML_F16)
+        NEON_DQ_GEOMETRY(NEON_GGML_BF16)
+        NEON_DQ_GEOMETRY(NEON_GGML_Q4_1)
+        NEON_DQ_GEOMETRY(NEON_GGML_Q5_0)
+        NEON_DQ_GEOMETRY(NEON_GGML_Q5_1)
+        NEON_DQ_GEOMETRY(NEON_GGML_Q4_K)
+        NEON_DQ_GEOMETRY(NEON_GGML_Q5_K)
+        NEON_DQ_GEOMETRY(NEON_GGML_Q6_K)
+#undef NEON_DQ_GEOMETRY
+        default:
+            *be = *bb = *cb = 0;
     }
-    *be = e;
-    *bb = b;
-    *cb = c;
 }
 
 struct DqArgs {
