@@ -7,7 +7,7 @@
 //   shim_driver multi  <cols> <seq> X.bin Y.out <type> <rows> W.bin [<type> <rows> W.bin ...]
 //   shim_driver badshape       (expects the reference's error message)
 //   shim_driver roles <name>...  (GGUF tensor name -> "role layer", or "none")
-//   shim_driver decode <dir> <n_new>
+//   shim_driver decode <dir> <n_new> [quantize_to]
 //       builds neon_cuda::Decoder from <dir>/config.txt (engine::Config fields),
 //       <dir>/manifest.txt ("name type ne0 ne1 file" per tensor) and
 //       <dir>/prompt.bin (int32); writes tokens.bin (greedy generation) and
@@ -97,9 +97,10 @@ int main(int argc, char** argv) {
             }
             return 0;
         }
-        if (mode == "decode" && argc == 4) {
+        if (mode == "decode" && (argc == 4 || argc == 5)) {
             const std::string dir = argv[2];
             const size_t n_new = std::strtoull(argv[3], nullptr, 10);
+            const int quantize_to = argc == 5 ? std::atoi(argv[4]) : -1;
             engine::Config cfg;
             {
                 std::ifstream f(dir + "/config.txt");
@@ -128,7 +129,7 @@ int main(int argc, char** argv) {
             std::vector<int32_t> prompt(pb.size() / 4);
             std::memcpy(prompt.data(), pb.data(), pb.size());
             neon_cuda::check(neon_cuda_init(0));
-            neon_cuda::Decoder d(cfg, g);
+            neon_cuda::Decoder d(cfg, g, nullptr, quantize_to);
             auto toks = d.generate(prompt, n_new, -1);
             {
                 std::ofstream f(dir + "/tokens.bin", std::ios::binary);

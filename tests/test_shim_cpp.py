@@ -93,14 +93,18 @@ def test_shim_multi_matches_oracle(driver, tmp_path):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("plain", [False, True])
-def test_shim_decoder_from_loader_matches_reference(driver, tmp_path, plain):
+@pytest.mark.parametrize("plain,wtype,etype,quantize", [
+    (False, S.GGML_Q4_0, S.GGML_Q8_0, None), (True, S.GGML_Q4_0, S.GGML_Q8_0, None),
+    (False, S.GGML_Q4_K, S.GGML_Q6_K, None),       # a nanity_convert.py --quant Q4_K model
+    (False, S.GGML_F32, S.GGML_F32, S.GGML_Q8_0),  # F32 tensors (a .nctr's) quantised on load
+], ids=["q4_0", "q4_0-plain", "q4_k", "f32-to-q8_0"])
+def test_shim_decoder_from_loader_matches_reference(driver, tmp_path, plain, wtype, etype, quantize):
     """neon_cuda::Decoder built from a loader's GGUF-named tensors and an
     engine::Config gives the reference's greedy tokens."""
     from conftest import MODEL_L2_RTOL, rel_l2
 
     cfg = S.ModelConfig(1000, 256, 2, 4, 2, 64, 512, ctx_len=64, rope_base=1e4, plain_ffn=plain)
-    tensors = list(S.model_tensors(cfg, seed=7))
+    tensors = list(S.model_tensors(cfg, seed=7, wtype=wtype, embd_type=etype))
     lines = []
     for i, (role, layer, raw, typ, ne0, ne1) in enumerate(tensors):
         np.ascontiguousarray(raw).tofile(tmp_path / f"t{i}.bin")
@@ -111,10 +115,15 @@ def test_shim_decoder_from_loader_matches_reference(driver, tmp_path, plain):
         f"{cfg.ctx_len} 0 {cfg.rope_base} {cfg.rope_scale} {cfg.rope_dim_count} {cfg.norm_eps} {0 if plain else 1}\n")
     prompt = S.prompt_tokens(8, cfg.n_vocab, 8)
     prompt.astype(np.int32).tofile(tmp_path / "prompt.bin")
-    out = subprocess.run([driver, "decode", str(tmp_path), "16"], capture_output=True, text=True)
+    out = subprocess.run([driver, "decode", str(tmp_path), "16"] + ([str(quantize)] if quantize is not None else []),
+                         capture_output=True, text=True)
     assert out.returncode == 0, out.stderr
     toks = np.fromfile(tmp_path / "tokens.bin", np.int32)
     logits = np.fromfile(tmp_path / "logits.bin", np.float32)
+    if quantize is not None:  # the reference runs the tensors an exporter would have written
+        N.init(0)
+        tensors = [(r, l, N.quantize(raw, t, ne1, ne0, quantize) if ne1 else raw, quantize if ne1 else t, ne0, ne1)
+                   for r, l, raw, t, ne0, ne1 in tensors]
     kind = "reference" if O.ref_available() else "port"
     ref = O.Model(cfg, tensors, kind)
     ref_toks, ref_logits = ref.generate_greedy(prompt, 16)
