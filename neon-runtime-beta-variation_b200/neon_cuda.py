@@ -513,6 +513,206 @@ class Comm:
 
 
 # ---------------------------------------------------------------------------
+# .gguf models
+# ---------------------------------------------------------------------------
+
+# Bytes of n values of a GGML type (nbytes_for, rawllm_loader.hpp:367-386),
+# as (values per block, bytes per block); 0 bytes: a type the loader cannot size.
+_GGUF_NBYTES = {0: (1, 4), 1: (1, 2), 30: (1, 2), 2: (32, 18), 3: (32, 20), 6: (32, 22), 7: (32, 24), 8: (32, 34),
+                9: (32, 36), 10: (256, 84), 11: (256, 110), 12: (256, 144), 13: (256, 176), 14: (256, 210),
+                25: (32, 18)}
+# GGUF metadata value types (MetaType, rawllm_loader.hpp:66-69): struct code or None for string / array
+_GGUF_SCALARS = {0: "<B", 1: "<b", 2: "<H", 3: "<h", 4: "<I", 5: "<i", 6: "<f", 7: "<B", 10: "<Q", 11: "<q",
+                 12: "<d"}
+_ROLE_NAMES = {"token_embd": 0, "output_norm": 1, "output": 2, "attn_norm": 3, "attn_q": 4, "attn_k": 5,
+               "attn_v": 6, "attn_output": 7, "ffn_norm": 8, "ffn_gate": 9, "ffn_up": 10, "ffn_down": 11}
+
+
+def _gguf_nbytes(t: int, n: int) -> int:
+    be, bb = _GGUF_NBYTES.get(t, (1, 0))
+    return n // be * bb
+
+
+def load_gguf(path: str):
+    """Open a NANITY .gguf file as (config, tensors) for :class:`Model`:
+    restates GGUFLoader::open (rawllm_loader.hpp:84-177: header, metadata,
+    tensor table, general.alignment, bounds) and validate_config (:197-330:
+    the nanity.* keys, every tensor's shape), with their messages. ``tensors``
+    are (role, layer, bytes, ggml type, ne0, ne1) views of a read-only memory
+    map for the names ModelWeights::build looks up (rawllm_forward.hpp:847-866);
+    ``config.ctx_len`` is the KV capacity kv_window = min(context_length, 4096),
+    ``config.bos_id`` / ``eos_id`` / ``unk_id`` the tokenizer's ids."""
+    mm = np.memmap(path, np.uint8, mode="r")
+    size = mm.size
+    if size < 16:
+        raise RuntimeError("File too small to be GGUF (<16 bytes): " + path)
+    pos = 0
+
+    def rd(fmt):
+        nonlocal pos
+        n = struct.calcsize(fmt)
+        if pos + n > size:
+            raise RuntimeError("GGUF: unexpected EOF")
+        v = struct.unpack(fmt, bytes(mm[pos:pos + n]))[0]
+        pos += n
+        return v
+
+    def rd_str():
+        nonlocal pos
+        n = rd("<Q")
+        if pos + n > size:
+            raise RuntimeError("GGUF: string overflow")
+        v = bytes(mm[pos:pos + n]).decode("utf-8", "replace")
+        pos += n
+        return v
+
+    if bytes(mm[:4]) != b"GGUF":
+        raise RuntimeError("Not a GGUF file: " + path)
+    pos = 4
+    ver = rd("<I")
+    if ver < 2 or ver > 3:
+        raise RuntimeError("Unsupported GGUF version")
+    n_tensors, n_kv = rd("<Q"), rd("<Q")
+    meta_num, meta_str, tok = {}, {}, {}
+
+    def value(t, key):
+        nonlocal pos
+        if t in _GGUF_SCALARS:
+            v = rd(_GGUF_SCALARS[t])
+            return float(v != 0) if t == 7 else v
+        if t == 8:
+            return rd_str()
+        if t == 9:
+            et, cnt = rd("<I"), rd("<Q")
+            for _ in range(cnt):  # arrays (the tokenizer's vocabulary and merges) are skipped
+                value(et, key)
+            return None
+        raise RuntimeError("Unknown GGUF meta type")
+
+    for _ in range(n_kv):
+        key = rd_str()
+        t = rd("<I")
+        v = value(t, key)
+        if key.startswith("tokenizer."):
+            if isinstance(v, (int, float)) and t != 8:
+                tok[key] = int(v) & 0xFFFFFFFF
+        elif isinstance(v, str):
+            meta_str[key] = v
+        elif v is not None:
+            meta_num[key] = float(v)
+    infos = []
+    for _ in range(n_tensors):
+        name = rd_str()
+        nd = rd("<I")
+        shape = [rd("<Q") for _ in range(nd)]
+        infos.append((name, shape, rd("<I"), rd("<Q")))
+    alignment = int(meta_num.get("general.alignment", 32)) or 32
+    data_start = (pos + alignment - 1) // alignment * alignment
+    table = {}
+    for name, shape, t, off in infos:
+        n = int(np.prod(shape)) if shape else 1
+        nbytes = _gguf_nbytes(t, n)
+        if data_start + off + nbytes > size:
+            raise RuntimeError(f"Tensor '{name}' OOB")
+        table[name] = (shape, t, mm[data_start + off:data_start + off + nbytes])
+
+    # validate_config
+    def req_str(k):
+        if not meta_str.get(k):
+            raise RuntimeError(f"NANITY: missing required metadata string key '{k}'.")
+        return meta_str[k]
+
+    def req_num(k):
+        if k not in meta_num:
+            raise RuntimeError(f"NANITY: missing required metadata key '{k}'.")
+        return meta_num[k]
+
+    arch = req_str("general.architecture")
+    if arch != "nanity":
+        raise RuntimeError(f'NANITY: general.architecture="{arch}", expected "nanity" -- this file is not a '
+                           "NANITY model.")
+    spec = int(req_num("nanity.spec_version"))
+    if spec != NCTR_SPEC_VERSION:
+        raise RuntimeError(f"NANITY: nanity.spec_version={spec}, this runtime only supports version "
+                           f"{NCTR_SPEC_VERSION}.")
+    u32 = lambda v: int(v) & 0xFFFFFFFF  # noqa: E731
+    n_embd, n_layer = u32(req_num("nanity.embedding_length")), u32(req_num("nanity.block_count"))
+    n_head, n_kv = u32(req_num("nanity.attention.head_count")), u32(req_num("nanity.attention.head_count_kv"))
+    head_dim, n_ff = u32(req_num("nanity.attention.key_length")), u32(req_num("nanity.feed_forward_length"))
+    ctx_len = u32(req_num("nanity.context_length"))
+    f32 = lambda v: float(np.float32(v))  # noqa: E731
+    norm_eps = f32(meta_num.get("nanity.attention.layer_norm_rms_epsilon", 1e-5))
+    rope_base = f32(meta_num.get("nanity.rope.freq_base", 10000.0))
+    rope_scale = f32(meta_num.get("nanity.rope.scale_linear", 1.0))
+    rope_dim = u32(meta_num.get("nanity.rope.dimension_count", 0.0))
+    if 0 in (n_embd, n_layer, n_head, n_kv, head_dim, n_ff):
+        raise RuntimeError("NANITY: one or more required hyperparameters is zero.")
+    if n_head % n_kv:
+        raise RuntimeError(f"NANITY: attention.head_count ({n_head}) must be an exact multiple of "
+                           f"attention.head_count_kv ({n_kv}) -- GQA grouping requires it.")
+    q_dim, kv_dim = n_head * head_dim, n_kv * head_dim
+
+    def shape_str(sh):
+        return "[" + ", ".join(str(v) for v in sh) + "]"
+
+    def find(name):
+        if name not in table:
+            raise RuntimeError(f"NANITY: required tensor '{name}' is missing.")
+        return table[name]
+
+    def check(name, *dims):
+        sh = find(name)[0]
+        if list(sh) != list(dims):
+            raise RuntimeError(f"NANITY: tensor '{name}' has shape {shape_str(sh)}, expected "
+                               f"{shape_str(dims)}.")
+
+    te = find("token_embd.weight")[0]
+    if len(te) != 2 or te[0] != n_embd:
+        raise RuntimeError(f"NANITY: 'token_embd.weight' shape {shape_str(te)} is inconsistent with "
+                           f"nanity.embedding_length={n_embd}.")
+    n_vocab = u32(te[1])
+    if "nanity.vocab_size" in meta_num and u32(meta_num["nanity.vocab_size"]) != n_vocab:
+        raise RuntimeError(f"NANITY: nanity.vocab_size={u32(meta_num['nanity.vocab_size'])} disagrees with "
+                           f"token_embd.weight's vocab dimension ({n_vocab}).")
+    check("output_norm.weight", n_embd)
+    if "output.weight" in table:
+        sh = table["output.weight"][0]
+        if list(sh) != [n_embd, n_vocab]:
+            raise RuntimeError(f"NANITY: 'output.weight' shape {shape_str(sh)} doesn't match "
+                               f"[embedding_length, vocab_size] = [{n_embd}, {n_vocab}].")
+    for i in range(n_layer):
+        p = f"blk.{i}."
+        check(p + "attn_norm.weight", n_embd)
+        check(p + "attn_q.weight", n_embd, q_dim)
+        check(p + "attn_k.weight", n_embd, kv_dim)
+        check(p + "attn_v.weight", n_embd, kv_dim)
+        check(p + "attn_output.weight", q_dim, n_embd)
+        check(p + "ffn_norm.weight", n_embd)
+        check(p + "ffn_gate.weight", n_embd, n_ff)
+        check(p + "ffn_up.weight", n_embd, n_ff)
+        check(p + "ffn_down.weight", n_ff, n_embd)
+
+    tensors = []
+    for name, (shape, t, raw) in table.items():
+        parts = name.split(".")
+        if len(parts) == 2 and parts[1] == "weight" and parts[0] in ("token_embd", "output_norm", "output"):
+            role, layer = _ROLE_NAMES[parts[0]], -1
+        elif (len(parts) == 4 and parts[0] == "blk" and parts[1].isdigit() and parts[3] == "weight"
+              and parts[2] in _ROLE_NAMES and _ROLE_NAMES[parts[2]] >= 3):
+            role, layer = _ROLE_NAMES[parts[2]], int(parts[1])
+        else:
+            continue
+        tensors.append((role, layer, raw, t, int(shape[0]), int(shape[1]) if len(shape) > 1 else 0))
+    cfg = NctrConfig(n_vocab=n_vocab, n_embd=n_embd, n_layer=n_layer, n_head=n_head, n_kv_head=n_kv,
+                     head_dim=head_dim, n_ff=n_ff, ctx_len=min(ctx_len, 4096), context_length=ctx_len,
+                     rope_base=rope_base, rope_scale=rope_scale, rope_dim_count=rope_dim, norm_eps=norm_eps,
+                     plain_ffn=False, bos_id=tok.get("tokenizer.ggml.bos_token_id", 1),
+                     eos_id=tok.get("tokenizer.ggml.eos_token_id", 2),
+                     unk_id=tok.get("tokenizer.ggml.unknown_token_id", 0))
+    return cfg, tensors
+
+
+# ---------------------------------------------------------------------------
 # .nctr models (the reference's F32 export container)
 # ---------------------------------------------------------------------------
 

@@ -345,3 +345,70 @@ int ref_nctr_config(void* h, ref_config_t* c, uint32_t* header_ctx_len, int* bos
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// The reference's GGUF reader, loader::GGUFLoader (rawllm_loader.hpp:84-330),
+// behind the same C ABI as the .nctr one.
+// ---------------------------------------------------------------------------
+extern "C" {
+
+void* ref_gguf_open(const char* path) {
+    auto* l = new loader::GGUFLoader();
+    try {
+        l->open(path);
+        return l;
+    } catch (const std::exception& e) {
+        delete l;
+        fail(e);
+        return nullptr;
+    }
+}
+
+void ref_gguf_free(void* h) { delete static_cast<loader::GGUFLoader*>(h); }
+
+size_t ref_gguf_count(void* h) { return static_cast<loader::GGUFLoader*>(h)->tensors.size(); }
+
+// Tensor i: name, GGUF shape (ne0, ne1), type, the distance of its data from
+// tensor 0's data (bytes), and its byte count.
+int ref_gguf_tensor(void* h, size_t i, char* name, size_t cap, uint64_t* ne0, uint64_t* ne1, int* type,
+                    int64_t* rel_offset, uint64_t* nbytes) {
+    auto* l = static_cast<loader::GGUFLoader*>(h);
+    const auto& t = l->tensors.at(i);
+    std::snprintf(name, cap, "%s", t.name.c_str());
+    *ne0 = t.shape.size() > 0 ? t.shape[0] : 0;
+    *ne1 = t.shape.size() > 1 ? t.shape[1] : 0;
+    *type = static_cast<int>(t.type);
+    *rel_offset = (int64_t)(t.data_ptr - l->tensors.at(0).data_ptr);
+    *nbytes = t.nbytes;
+    return 0;
+}
+
+// validate_config into a ref_config_t (ctx_len = kv_window); -1 on a throw.
+int ref_gguf_config(void* h, ref_config_t* c, uint32_t* header_ctx_len, int* bos, int* eos) {
+    try {
+        engine::Config cfg;
+        auto* l = static_cast<loader::GGUFLoader*>(h);
+        l->validate_config(cfg);
+        c->n_vocab = cfg.n_vocab;
+        c->n_embd = cfg.n_embd;
+        c->n_layer = cfg.n_layer;
+        c->n_head = cfg.n_head;
+        c->n_kv_head = cfg.n_kv_head;
+        c->head_dim = cfg.head_dim;
+        c->n_ff = cfg.n_ff;
+        c->ctx_len = cfg.kv_window;
+        c->rope_base = cfg.rope_base;
+        c->rope_scale = cfg.rope_scale;
+        c->rope_dim_count = cfg.rope_dim_count;
+        c->norm_eps = cfg.norm_eps;
+        c->plain_ffn = cfg.use_swiglu ? 0 : 1;
+        *header_ctx_len = cfg.ctx_len;
+        *bos = l->tok_meta.bos_id;
+        *eos = l->tok_meta.eos_id;
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+}  // extern "C"

@@ -94,3 +94,22 @@ def test_nctr_model_decodes_like_the_oracle(tmp_path, quant):
     for i, (a, b) in enumerate(zip(got, want_logits)):
         assert rel_l2(a, b) <= bar, f"step {i}"
     m.free()
+
+
+def test_gguf_model_decodes_like_the_oracle(tmp_path):
+    """A .gguf file written by gguf-py, read by neon_cuda.load_gguf, decoded on
+    the device: the oracle's greedy tokens on the same tensors."""
+    pytest.importorskip("gguf")
+    from gguf_file import write_gguf
+
+    path = str(tmp_path / "m.gguf")
+    write_gguf(path, TINY, wtype=S.GGML_Q4_K, embd_type=S.GGML_Q6_K, tied=False)
+    c, tensors = N.load_gguf(path)
+    m = N.Model(c, tensors)
+    o = O.Model(TINY.with_(ctx_len=c.ctx_len), tensors, "port")
+    prompt = S.prompt_tokens(9, TINY.n_vocab, 21)
+    want_toks, want_logits = o.generate_greedy(prompt, 6)
+    assert np.array_equal(m.generate(prompt, 6), want_toks)
+    m.set_length(0)
+    assert rel_l2(m.forward(prompt), want_logits[0]) <= 1e-3
+    m.free()
