@@ -1,4 +1,4 @@
-"""On-load quantisation on the device and .nctr models on the GPU.
+"""On-load quantisation on the device, and .nctr / .gguf models on the GPU.
 
 * neon_cuda_quantize_rows / _host: byte for byte what gguf-py's
   gguf.quants.quantize (the reference exporters' quantiser) writes
@@ -8,7 +8,8 @@
 * a .nctr model (F32, as export_nctr writes it) decoded on the device as is
   and quantised on load to Q8_0 / Q4_0: the oracle's greedy tokens on the same
   weights, logits within 1e-3 relative L2 (Q4_0: the whole-model bar, its
-  activations are quantised)."""
+  activations are quantised);
+* a .gguf model written by gguf-py and read by neon_cuda.load_gguf, likewise."""
 import numpy as np
 import pytest
 
