@@ -36,3 +36,27 @@ def test_q8_0_layout_and_dequant():
 def test_seeded():
     assert np.array_equal(S.activations(2, 64, 5), S.activations(2, 64, 5))
     assert not np.array_equal(S.q4_0_weights(2, 64, 5), S.q4_0_weights(2, 64, 6))
+
+
+def test_row_bytes_of_every_type():
+    # nbytes_for (rawllm_loader.hpp:367-386) for a 4096-value row
+    want = {S.GGML_F32: 16384, S.GGML_F16: 8192, S.GGML_BF16: 8192, S.GGML_Q4_0: 2304, S.GGML_Q4_1: 2560,
+            S.GGML_Q5_0: 2816, S.GGML_Q5_1: 3072, S.GGML_Q8_0: 4352, S.GGML_Q4_K: 2304, S.GGML_Q5_K: 2816,
+            S.GGML_Q6_K: 3360}
+    for t, n in want.items():
+        assert S.row_bytes(t, 4096) == n == O.lib().oracle_row_bytes(t, 4096), S.TYPE_NAMES[t]
+
+
+def test_pooled_weights_every_type():
+    """The block pool of the large benchmark models: GGUF rows of the type,
+    seeded, and (past the pool's size) repeated from a seeded offset."""
+    for t in (S.GGML_Q4_K,):  # the 256-value super-block path (Q4_0 / Q8_0 pools serve the bench)
+        a = S.pooled_weights(t, 96, 4096, seed=3)
+        assert a.shape == (96, S.row_bytes(t, 4096))
+        assert np.array_equal(a, S.pooled_weights(t, 96, 4096, seed=3))
+        assert not np.array_equal(a, S.pooled_weights(t, 96, 4096, seed=4))
+    be = 256
+    n_pool = (1 << 23) * 32 // be  # super-blocks in the Q4_K pool
+    rows = n_pool // (8192 // be) + 3  # more blocks than the pool holds
+    big = S.pooled_weights(S.GGML_Q4_K, rows, 8192, seed=5)
+    assert big.shape == (rows, S.row_bytes(S.GGML_Q4_K, 8192))
