@@ -718,6 +718,7 @@ int launched(int n) {
     return NEON_OK;
 }
 bool pdl_enabled() { return g_pdl.load(std::memory_order_relaxed) != 0; }
+bool prefill_mma() { return g_prefill_mma.load(std::memory_order_relaxed) != 0; }
 int device_sms(int device) {
     int rc = init_device(device);
     return rc ? -1 : g_dev[device].sms;

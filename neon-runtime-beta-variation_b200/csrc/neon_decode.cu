@@ -159,6 +159,206 @@ __global__ void embed_kernel(const uint8_t* __restrict__ qs, const uint16_t* __r
     }
 }
 
+// ---------------------------------------------------------------------------
+// Prefill attention on the tensor cores (neon_cuda_set_prefill_mma), the
+// attention loop of transformer_forward (rawllm_forward.hpp:1108-1150) for a
+// tile of 64 positions of one query head: pass 1 takes each position's
+// maximum of the scaled scores s = (q . k) * scale over keys 0..pos; pass 2
+// recomputes the same scores, p = fast_expf(s - max), their sums, and P.V,
+// and the outputs are (P.V) / sum. Both products are TF32 MMAs (mma.sync
+// m16n8k8) with every operand split into two TF32 terms and the three
+// significant partial products kept: fp32 accuracy, in another order of
+// additions than the reference's dot_f32 / axpy. Two passes rather than an
+// online softmax: the reference applies fast_expf, a piecewise-linear
+// exponential, to s minus the maximum over ALL keys, and rescaled partial
+// sums of fast_expf values would not be its numbers. head_dim <= 128.
+// ---------------------------------------------------------------------------
+constexpr int kApRows = 64;   // positions per CTA (4 warps x 16)
+constexpr int kApKeys = 64;   // keys per tile
+constexpr int kApMaxHd = 128;
+
+__device__ __forceinline__ uint32_t ap_tf32(float v) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(v));
+    return r;
+}
+__device__ __forceinline__ void ap_split(float v, uint32_t& hi, uint32_t& lo) {
+    hi = ap_tf32(v);
+    lo = ap_tf32(__fsub_rn(v, __uint_as_float(hi)));
+}
+__device__ __forceinline__ void ap_mma(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                       uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+// c += a * b for a = ah + al, b = bh + bl (the al*bl term dropped), small terms first
+__device__ __forceinline__ void ap_mma3(float (&c)[4], const uint32_t (&ah)[4], const uint32_t (&al)[4],
+                                        uint32_t bh0, uint32_t bh1, uint32_t bl0, uint32_t bl1) {
+    ap_mma(c, ah[0], ah[1], ah[2], ah[3], bl0, bl1);
+    ap_mma(c, al[0], al[1], al[2], al[3], bh0, bh1);
+    ap_mma(c, ah[0], ah[1], ah[2], ah[3], bh0, bh1);
+}
+
+// Dynamic shared memory: Q and K tiles at a pitch of hd+4 floats, V at hd+8,
+// P at 68 (conflict-free fragment reads).
+__host__ __device__ inline int ap_smem_bytes(int hd) {
+    return (int)sizeof(float) * (kApRows * (hd + 4) + kApKeys * (hd + 4) + kApKeys * (hd + 8) + kApRows * (kApKeys + 4));
+}
+
+__global__ void __launch_bounds__(128) attn_prefill_mma_kernel(const float* __restrict__ q, const float* __restrict__ Kc,
+                                                               const float* __restrict__ Vc, float* __restrict__ out,
+                                                               const int* __restrict__ d_pos, int seq, int q_dim,
+                                                               int kv_dim, int hd, int group, float scale) {
+    extern __shared__ float ap_sm[];
+    const int qp = hd + 4, vp = hd + 8, pp = kApKeys + 4;
+    float* Qs = ap_sm;
+    float* Ks = Qs + kApRows * qp;
+    float* Vs = Ks + kApKeys * qp;
+    float* Ps = Vs + kApKeys * vp;
+    const int h = blockIdx.x, t0 = blockIdx.y * kApRows;
+    const int kvh = h / group;
+    const int base = *d_pos;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, tq = lane & 3;
+    const int r0 = warp * 16 + g, r1 = r0 + 8;  // this lane's two rows of the tile
+    const bool ok0 = t0 + r0 < seq, ok1 = t0 + r1 < seq;
+    const int pos0 = base + t0 + r0, pos1 = base + t0 + r1;
+    const int nq = min(kApRows, seq - t0);
+    const int kend = base + t0 + nq;  // keys [0, kend) are seen by some position of the tile
+    const int ntiles = (kend + kApKeys - 1) / kApKeys;
+    const int nd = hd / 8;
+
+    for (int i = tid; i < kApRows * hd; i += blockDim.x) {
+        const int r = i / hd, d = i % hd;
+        Qs[r * qp + d] = t0 + r < seq ? q[(long long)(t0 + r) * q_dim + (long long)h * hd + d] : 0.f;
+    }
+    auto load_tile = [&](int kt, bool with_v) {
+        for (int i = tid; i < kApKeys * hd; i += blockDim.x) {
+            const int r = i / hd, d = i % hd, key = kt * kApKeys + r;
+            const long long src = (long long)key * kv_dim + (long long)kvh * hd + d;
+            Ks[r * qp + d] = key < kend ? Kc[src] : 0.f;
+            if (with_v) Vs[r * vp + d] = key < kend ? Vc[src] : 0.f;
+        }
+    };
+    // the scaled scores of this lane's rows r0, r1 against keys 8j+2tq(+1) of a tile
+    auto scores = [&](float (&sc)[8][4]) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) sc[j][e] = 0.f;
+        for (int ks = 0; ks < nd; ++ks) {
+            uint32_t ah[4], al[4];
+            ap_split(Qs[r0 * qp + 8 * ks + tq], ah[0], al[0]);
+            ap_split(Qs[r1 * qp + 8 * ks + tq], ah[1], al[1]);
+            ap_split(Qs[r0 * qp + 8 * ks + tq + 4], ah[2], al[2]);
+            ap_split(Qs[r1 * qp + 8 * ks + tq + 4], ah[3], al[3]);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                uint32_t bh0, bl0, bh1, bl1;
+                ap_split(Ks[(8 * j + g) * qp + 8 * ks + tq], bh0, bl0);
+                ap_split(Ks[(8 * j + g) * qp + 8 * ks + tq + 4], bh1, bl1);
+                ap_mma3(sc[j], ah, al, bh0, bh1, bl0, bl1);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) sc[j][e] = __fmul_rn(sc[j][e], scale);
+    };
+
+    // pass 1: row maxima over each position's keys 0..pos
+    float m0 = -INFINITY, m1 = -INFINITY;
+    for (int kt = 0; kt < ntiles; ++kt) {
+        __syncthreads();
+        load_tile(kt, false);
+        __syncthreads();
+        float sc[8][4];
+        scores(sc);
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int key = kt * kApKeys + 8 * j + 2 * tq + (e & 1);
+                if (e < 2) {
+                    if (ok0 && key <= pos0) m0 = fmaxf(m0, sc[j][e]);
+                } else if (ok1 && key <= pos1) {
+                    m1 = fmaxf(m1, sc[j][e]);
+                }
+            }
+    }
+#pragma unroll
+    for (int o = 1; o <= 2; o <<= 1) {
+        m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, o));
+        m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, o));
+    }
+
+    // pass 2: p = fast_expf(s - max), sums, P.V
+    float acc[kApMaxHd / 8][4];
+#pragma unroll
+    for (int n = 0; n < kApMaxHd / 8; ++n)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[n][e] = 0.f;
+    float l0 = 0.f, l1 = 0.f;
+    for (int kt = 0; kt < ntiles; ++kt) {
+        __syncthreads();
+        load_tile(kt, true);
+        __syncthreads();
+        float sc[8][4];
+        scores(sc);
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int col = 8 * j + 2 * tq + (e & 1), key = kt * kApKeys + col;
+                const bool on = e < 2 ? (ok0 && key <= pos0) : (ok1 && key <= pos1);
+                const float p = on ? fast_expf_dev(__fsub_rn(sc[j][e], e < 2 ? m0 : m1)) : 0.f;
+                if (e < 2) l0 += p;
+                else l1 += p;
+                Ps[(e < 2 ? r0 : r1) * pp + col] = p;
+            }
+        __syncwarp();  // a warp reads back only its own 16 rows of P
+        for (int ks = 0; ks < kApKeys / 8; ++ks) {
+            uint32_t ah[4], al[4];
+            ap_split(Ps[r0 * pp + 8 * ks + tq], ah[0], al[0]);
+            ap_split(Ps[r1 * pp + 8 * ks + tq], ah[1], al[1]);
+            ap_split(Ps[r0 * pp + 8 * ks + tq + 4], ah[2], al[2]);
+            ap_split(Ps[r1 * pp + 8 * ks + tq + 4], ah[3], al[3]);
+#pragma unroll
+            for (int n = 0; n < kApMaxHd / 8; ++n) {
+                if (n >= nd) break;
+                uint32_t bh0, bl0, bh1, bl1;
+                ap_split(Vs[(8 * ks + tq) * vp + 8 * n + g], bh0, bl0);
+                ap_split(Vs[(8 * ks + tq + 4) * vp + 8 * n + g], bh1, bl1);
+                ap_mma3(acc[n], ah, al, bh0, bh1, bl0, bl1);
+            }
+        }
+        __syncwarp();  // P is rewritten by this warp for the next tile
+    }
+#pragma unroll
+    for (int o = 1; o <= 2; o <<= 1) {
+        l0 += __shfl_xor_sync(0xffffffffu, l0, o);
+        l1 += __shfl_xor_sync(0xffffffffu, l1, o);
+    }
+    const float inv0 = ok0 ? __fdiv_rn(1.0f, l0) : 0.f, inv1 = ok1 ? __fdiv_rn(1.0f, l1) : 0.f;
+#pragma unroll
+    for (int n = 0; n < kApMaxHd / 8; ++n) {
+        if (n >= nd) break;
+        const int d = 8 * n + 2 * tq;
+        if (ok0) {
+            float* o0 = out + (long long)(t0 + r0) * q_dim + (long long)h * hd + d;
+            o0[0] = __fmul_rn(acc[n][0], inv0);
+            o0[1] = __fmul_rn(acc[n][1], inv0);
+        }
+        if (ok1) {
+            float* o1 = out + (long long)(t0 + r1) * q_dim + (long long)h * hd + d;
+            o1[0] = __fmul_rn(acc[n][2], inv1);
+            o1[1] = __fmul_rn(acc[n][3], inv1);
+        }
+    }
+}
+
 // out = x * (1/sqrt(mean(x^2) + eps)) * w per row; one CTA per row
 // (fwd::rms_norm, rawllm_forward.hpp:730-735).
 __global__ void __launch_bounds__(kThreads) rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
@@ -870,7 +1070,13 @@ int run_layers(neon_model* m, const int* toks, int seq) {
                                                             (int)q_dim, (int)kv_dim, Kl, Vl);
             rc = check_launch("rope_kv_kernel");
         }
-        if (!rc) {
+        if (!rc && neon_internal::prefill_mma() && c.head_dim <= (uint32_t)kApMaxHd && c.head_dim % 8 == 0) {
+            // tensor-core tiles of 64 positions per query head
+            attn_prefill_mma_kernel<<<dim3((unsigned)m->n_head_l, (unsigned)((seq + kApRows - 1) / kApRows)), 128,
+                                      ap_smem_bytes((int)c.head_dim), m->stream>>>(
+                m->q, Kl, Vl, m->att, m->d_pos, seq, (int)q_dim, (int)kv_dim, (int)c.head_dim, group, scale);
+            rc = check_launch("attn_prefill_mma_kernel");
+        } else if (!rc) {
             attention_kernel<<<dim3((unsigned)m->n_head_l, seq), kThreads, attn_smem, m->stream>>>(
                 m->q, Kl, Vl, m->att, m->d_pos, (int)q_dim, (int)kv_dim, (int)c.head_dim, group, scale);
             rc = check_launch("attention_kernel");
@@ -1203,6 +1409,10 @@ int neon_cuda_model_create_tp(const neon_model_config_t* cfg, neon_comm_t comm, 
         if (cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(c.ctx_len * sizeof(float))) != cudaSuccess)
             rc = error(NEON_ERR_CUDA, "cudaFuncSetAttribute(attention_kernel)");
     }
+    if (!rc && c.head_dim <= (uint32_t)kApMaxHd &&
+        cudaFuncSetAttribute(attn_prefill_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             ap_smem_bytes((int)c.head_dim)) != cudaSuccess)
+        rc = error(NEON_ERR_CUDA, "cudaFuncSetAttribute(attn_prefill_mma_kernel)");
     if (rc) {
         neon_cuda_model_free(m);
         return rc;

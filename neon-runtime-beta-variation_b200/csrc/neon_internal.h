@@ -119,6 +119,8 @@ PeerSet comm_peer_set(neon_comm_impl* c);
 // + slot_1[i] + ... for i < n, waiting (bounded) for every rank's words.
 int comm_ll_reduce(neon_comm_impl* c, float* h, long long n, cudaStream_t st);
 bool fused_collectives();
+// neon_cuda_set_prefill_mma: prompt passes on the tensor-core kernels.
+bool prefill_mma();
 
 // Decode-step options of a one-position matvec launch (seq == 1 only):
 // RMSNorm of X folded into the X staging, and per-target epilogues (the

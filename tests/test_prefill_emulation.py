@@ -215,3 +215,145 @@ def test_tf32_split_carries_fp32():
     lo = tf32((x - hi).astype(np.float32))
     rel = np.abs((hi.astype(np.float64) + lo) - x) / np.abs(x)
     assert rel.max() <= 2.0 ** -21
+
+
+def fast_expf(x):
+    """engine::fast_expf (rawllm_common.hpp:88-100), as oracle_fast_expf restates it."""
+    L = O.lib()
+    import ctypes as C
+    L.oracle_fast_expf.argtypes = [C.c_float]
+    L.oracle_fast_expf.restype = C.c_float
+    return np.array([L.oracle_fast_expf(float(v)) for v in np.ravel(x)], np.float64).reshape(np.shape(x))
+
+
+def emulate_attention(q, K, V, base, hd, group, scale):
+    """attn_prefill_mma_kernel's lanes (products in float64, no TF32 error):
+    pass 1 row maxima of the masked scaled scores, pass 2 p, sums and P.V, by
+    the kernel's fragment mapping of mma.m16n8k8 (A rows g / g+8, values t and
+    t+4; B values t / t+4 of column g; C rows g / g+8, columns 2t, 2t+1)."""
+    seq, q_dim = q.shape
+    n_head = q_dim // hd
+    out = np.zeros((seq, q_dim))
+    lanes = np.arange(32)
+    g, tq = lanes // 4, lanes % 4
+    for h in range(n_head):
+        kvh = h // group
+        for t0 in range(0, seq, 64):
+            nq = min(64, seq - t0)
+            kend = base + t0 + nq
+            Qs = np.zeros((64, hd))
+            Qs[:nq] = q[t0:t0 + nq, h * hd:(h + 1) * hd]
+            for w in range(4):
+                r0, r1 = w * 16 + g, w * 16 + g + 8
+                ok0, ok1 = t0 + r0 < seq, t0 + r1 < seq
+                pos0, pos1 = base + t0 + r0, base + t0 + r1
+                tiles = []
+                for kt in range((kend + 63) // 64):
+                    Ks = np.zeros((64, hd))
+                    Vs = np.zeros((64, hd))
+                    keys = np.arange(kt * 64, kt * 64 + 64)
+                    valid = keys < kend
+                    Ks[valid] = K[keys[valid], kvh * hd:(kvh + 1) * hd]
+                    Vs[valid] = V[keys[valid], kvh * hd:(kvh + 1) * hd]
+                    # scores: sc[lane][j][e] from the fragments
+                    sc = np.zeros((32, 8, 4))
+                    for ks in range(hd // 8):
+                        A = np.zeros((16, 8))
+                        for l in range(32):
+                            A[g[l], tq[l]] = Qs[r0[l], 8 * ks + tq[l]]
+                            A[g[l] + 8, tq[l]] = Qs[r1[l], 8 * ks + tq[l]]
+                            A[g[l], tq[l] + 4] = Qs[r0[l], 8 * ks + tq[l] + 4]
+                            A[g[l] + 8, tq[l] + 4] = Qs[r1[l], 8 * ks + tq[l] + 4]
+                        for j in range(8):
+                            B = np.zeros((8, 8))
+                            for l in range(32):
+                                B[tq[l], g[l]] = Ks[8 * j + g[l], 8 * ks + tq[l]]
+                                B[tq[l] + 4, g[l]] = Ks[8 * j + g[l], 8 * ks + tq[l] + 4]
+                            C = A @ B
+                            sc[:, j, 0] += C[g, 2 * tq]
+                            sc[:, j, 1] += C[g, 2 * tq + 1]
+                            sc[:, j, 2] += C[g + 8, 2 * tq]
+                            sc[:, j, 3] += C[g + 8, 2 * tq + 1]
+                    tiles.append((kt, sc * scale, Vs))
+                # pass 1
+                m0 = np.full(32, -np.inf)
+                m1 = np.full(32, -np.inf)
+                for kt, sc, _ in tiles:
+                    for j in range(8):
+                        for e in range(4):
+                            key = kt * 64 + 8 * j + 2 * tq + (e & 1)
+                            if e < 2:
+                                on = ok0 & (key <= pos0)
+                                m0 = np.where(on, np.maximum(m0, sc[:, j, e]), m0)
+                            else:
+                                on = ok1 & (key <= pos1)
+                                m1 = np.where(on, np.maximum(m1, sc[:, j, e]), m1)
+                for o in (1, 2):  # the shuffle over the 4 lanes of a row
+                    m0 = np.maximum(m0, m0[lanes ^ o])
+                    m1 = np.maximum(m1, m1[lanes ^ o])
+                # pass 2
+                acc = np.zeros((32, hd // 8, 4))
+                l0 = np.zeros(32)
+                l1 = np.zeros(32)
+                for kt, sc, Vs in tiles:
+                    Ps = np.zeros((64, 64))
+                    for j in range(8):
+                        for e in range(4):
+                            col = 8 * j + 2 * tq + (e & 1)
+                            key = kt * 64 + col
+                            on = (ok0 & (key <= pos0)) if e < 2 else (ok1 & (key <= pos1))
+                            m = m0 if e < 2 else m1
+                            p = np.where(on, fast_expf(np.where(on, sc[:, j, e] - m, 0.0)), 0.0)
+                            if e < 2:
+                                l0 += p
+                            else:
+                                l1 += p
+                            Ps[np.where(e < 2, r0, r1), col] = p
+                    for ks in range(8):
+                        A = np.zeros((16, 8))
+                        for l in range(32):
+                            A[g[l], tq[l]] = Ps[r0[l], 8 * ks + tq[l]]
+                            A[g[l] + 8, tq[l]] = Ps[r1[l], 8 * ks + tq[l]]
+                            A[g[l], tq[l] + 4] = Ps[r0[l], 8 * ks + tq[l] + 4]
+                            A[g[l] + 8, tq[l] + 4] = Ps[r1[l], 8 * ks + tq[l] + 4]
+                        for n in range(hd // 8):
+                            B = np.zeros((8, 8))
+                            for l in range(32):
+                                B[tq[l], g[l]] = Vs[8 * ks + tq[l], 8 * n + g[l]]
+                                B[tq[l] + 4, g[l]] = Vs[8 * ks + tq[l] + 4, 8 * n + g[l]]
+                            C = A @ B
+                            acc[:, n, 0] += C[g, 2 * tq]
+                            acc[:, n, 1] += C[g, 2 * tq + 1]
+                            acc[:, n, 2] += C[g + 8, 2 * tq]
+                            acc[:, n, 3] += C[g + 8, 2 * tq + 1]
+                for o in (1, 2):
+                    l0 = l0 + l0[lanes ^ o]
+                    l1 = l1 + l1[lanes ^ o]
+                for l in range(32):
+                    for n in range(hd // 8):
+                        d = 8 * n + 2 * tq[l]
+                        if ok0[l]:
+                            out[t0 + r0[l], h * hd + d:h * hd + d + 2] = acc[l, n, 0:2] / l0[l]
+                        if ok1[l]:
+                            out[t0 + r1[l], h * hd + d:h * hd + d + 2] = acc[l, n, 2:4] / l1[l]
+    return out
+
+
+def test_prefill_attention_fragments():
+    """The emulated kernel equals a direct causal GQA attention with the
+    reference's softmax (fast_expf of s minus each position's maximum)."""
+    rng = np.random.default_rng(5)
+    seq, base, hd, n_head, n_kv = 70, 5, 16, 2, 1
+    scale = 1.0 / np.sqrt(hd)
+    q = rng.standard_normal((seq, n_head * hd))
+    K = rng.standard_normal((base + seq, n_kv * hd))
+    V = rng.standard_normal((base + seq, n_kv * hd))
+    got = emulate_attention(q, K, V, base, hd, n_head // n_kv, scale)
+    want = np.zeros_like(got)
+    for t in range(seq):
+        for h in range(n_head):
+            kvh = h // (n_head // n_kv)
+            s = K[:base + t + 1, kvh * hd:(kvh + 1) * hd] @ q[t, h * hd:(h + 1) * hd] * scale
+            p = fast_expf(s - s.max())
+            want[t, h * hd:(h + 1) * hd] = (p / p.sum()) @ V[:base + t + 1, kvh * hd:(kvh + 1) * hd]
+    np.testing.assert_allclose(got, want, rtol=1e-9, atol=1e-12)
