@@ -86,3 +86,19 @@ def test_decoder_prompt_pass():
     m.set_length(0)
     assert rel_l2(m.forward(prompt), want_logits[0]) <= MODEL_L2_RTOL
     m.free()
+
+
+def test_prompt_pass_matches_the_cuda_core_kernels():
+    """A Q8_0-weight decoder (no activation quantisation on its path): the
+    prompt pass on the tensor-core projections and attention against the
+    CUDA-core kernels, logits within fp32 noise."""
+    cfg = S.ModelConfig(1000, 256, 2, 4, 2, 64, 512, ctx_len=200, rope_base=1e4)
+    tensors = list(S.model_tensors(cfg, seed=12, wtype=S.GGML_Q8_0))
+    prompt = S.prompt_tokens(150, cfg.n_vocab, 13)
+    m = N.Model(cfg, tensors)
+    on = m.forward(prompt)
+    N.set_prefill_mma(False)
+    m.set_length(0)
+    off = m.forward(prompt)
+    m.free()
+    assert rel_l2(on, off) <= 1e-4 and int(np.argmax(on)) == int(np.argmax(off))
