@@ -195,14 +195,14 @@ NEON_API int neon_cuda_matvec_q4_0_noalloc(neon_tensor_t W, const float* dX, siz
 /* Tensor roles of a NANITY decoder (NANITY_ARCHITECTURE_SPEC.md section 4;
  * fwd::ModelWeights / LayerWeights, rawllm_forward.hpp:823-834). */
 #define NEON_ROLE_TOKEN_EMBD 0 /* token_embd.weight  [n_embd, n_vocab] */
-#define NEON_ROLE_OUTPUT_NORM 1 /* output_norm.weight [n_embd] F32 */
+#define NEON_ROLE_OUTPUT_NORM 1 /* output_norm.weight [n_embd] */
 #define NEON_ROLE_OUTPUT 2     /* output.weight      [n_embd, n_vocab], optional (tied) */
-#define NEON_ROLE_ATTN_NORM 3  /* blk.i.attn_norm.weight [n_embd] F32 */
+#define NEON_ROLE_ATTN_NORM 3  /* blk.i.attn_norm.weight [n_embd] */
 #define NEON_ROLE_ATTN_Q 4     /* blk.i.attn_q.weight    [n_embd, q_dim] */
 #define NEON_ROLE_ATTN_K 5     /* blk.i.attn_k.weight    [n_embd, kv_dim] */
 #define NEON_ROLE_ATTN_V 6     /* blk.i.attn_v.weight    [n_embd, kv_dim] */
 #define NEON_ROLE_ATTN_OUT 7   /* blk.i.attn_output.weight [q_dim, n_embd] */
-#define NEON_ROLE_FFN_NORM 8   /* blk.i.ffn_norm.weight  [n_embd] F32 */
+#define NEON_ROLE_FFN_NORM 8   /* blk.i.ffn_norm.weight  [n_embd] */
 #define NEON_ROLE_FFN_GATE 9   /* blk.i.ffn_gate.weight  [n_embd, n_ff] */
 #define NEON_ROLE_FFN_UP 10    /* blk.i.ffn_up.weight    [n_embd, n_ff] */
 #define NEON_ROLE_FFN_DOWN 11  /* blk.i.ffn_down.weight  [n_ff, n_embd] */
@@ -230,7 +230,10 @@ NEON_API int neon_cuda_model_create(const neon_model_config_t* cfg, neon_model_t
 
 /* Upload one tensor (GGUF bytes; ne1 = 0 for a 1-D norm weight). Projection,
  * embedding and lm_head tensors may be any NEON_GGML_* type above (ffn_gate
- * and ffn_up of one layer share theirs); norm weights are F32. */
+ * and ffn_up of one layer share theirs). A norm weight may be any of them too
+ * whose block divides n_embd: it is decoded to F32 once, here, as the
+ * reference's dequant_full does on every forward (rawllm_forward.hpp:325-328,
+ * at :1077, :1161, :1226). */
 NEON_API int neon_cuda_model_set_tensor(neon_model_t m, int role, int layer, const uint8_t* host_bytes,
                                         size_t nbytes, int ggml_type, size_t ne0, size_t ne1);
 

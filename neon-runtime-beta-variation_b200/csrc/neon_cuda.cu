@@ -712,6 +712,9 @@ int embed_rows(const neon_tensor* E, const int* toks, int seq, int n_embd, int n
                     n_embd, toks, n_vocab, h, err);
 }
 size_t gguf_block_elems(int type) { return block_elems_of(type); }
+bool dequantize_row_host(int type, const uint8_t* p, size_t n, float* out) {
+    return row_bytes_of(type, n) != 0 && dq_row_host(type, p, n, out);
+}
 int cuda_error(cudaError_t e, const char* what) { return cuda_err(e, what); }
 int launched(int n) {
     g_launches.fetch_add((uint64_t)n, std::memory_order_relaxed);

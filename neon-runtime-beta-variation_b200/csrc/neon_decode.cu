@@ -1454,12 +1454,19 @@ int neon_cuda_model_set_tensor(neon_model_t m, int role, int layer, const uint8_
         return neon_cuda_model_set_tensor(m, role, layer, q.data(), q.size(), m->quantize_to, ne0, ne1);
     }
     if (role == NEON_ROLE_OUTPUT_NORM || role == NEON_ROLE_ATTN_NORM || role == NEON_ROLE_FFN_NORM) {
-        if (ggml_type != NEON_GGML_F32 || ne0 != c.n_embd || ne1 > 1 || nbytes != ne0 * 4)
-            return error(NEON_ERR_INVALID, "NANITY: norm weight must be F32 [n_embd]");
+        // any type the reference dequantises (dequant_full, rawllm_forward.hpp:
+        // 325-328, at :1077 / :1161 / :1226), decoded to F32 here, once
+        const size_t rb = neon_internal::gguf_row_bytes(ggml_type, ne0);
+        if (ne0 != c.n_embd || ne1 > 1 || rb == 0 || nbytes != rb)
+            return error(NEON_ERR_INVALID, "NANITY: norm weight must be [n_embd] of a dequantisable type (F32, F16, "
+                                           "BF16 or a block type whose block divides n_embd)");
+        std::vector<float> w(ne0);
+        if (!neon_internal::dequantize_row_host(ggml_type, host_bytes, ne0, w.data()))
+            return error(NEON_ERR_UNSUPPORTED, "norm weight of type " + std::to_string(ggml_type) + " is not supported");
         float* p = nullptr;
-        int rc = dev_alloc(m, (void**)&p, nbytes);
+        int rc = dev_alloc(m, (void**)&p, ne0 * sizeof(float));
         if (rc) return rc;
-        DEC_TRY(cudaMemcpy(p, host_bytes, nbytes, cudaMemcpyHostToDevice));
+        DEC_TRY(cudaMemcpy(p, w.data(), ne0 * sizeof(float), cudaMemcpyHostToDevice));
         if (role == NEON_ROLE_OUTPUT_NORM) m->output_norm = p;
         else {
             if (layer < 0 || (uint32_t)layer >= c.n_layer) return error(NEON_ERR_INVALID, "layer index out of range");

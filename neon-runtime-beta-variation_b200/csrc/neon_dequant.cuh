@@ -636,4 +636,56 @@ __global__ void __launch_bounds__(128) embed_dq_kernel(const unsigned char* __re
     }
 }
 
+// n values of one row of `type` as the host holds it (GGUF layout, any
+// alignment) into out, decoded on the host with the device decoders'
+// arithmetic: the reference's dequantize_row (rawllm_forward.hpp:301-321)
+// bit for bit. For the float types any n; for a block type n whole blocks.
+// Returns false for another type or a ragged block row.
+inline bool dq_row_host(int type, const unsigned char* p, size_t n, float* out) {
+    if (type == NEON_GGML_F32) {
+        memcpy(out, p, n * 4);
+        return true;
+    }
+    if (type == NEON_GGML_F16 || type == NEON_GGML_BF16) {
+        for (size_t i = 0; i < n; ++i) {
+            alignas(4) unsigned char h[2];
+            memcpy(h, p + 2 * i, 2);
+            out[i] = type == NEON_GGML_F16 ? sh_half(h) : NEON_HD_BITS_F32(sh_u16(h) << 16);
+        }
+        return true;
+    }
+    const bool split = type == NEON_GGML_Q8_0 || type == NEON_GGML_Q4_0;
+    int be = 32, bb = type == NEON_GGML_Q8_0 ? 34 : 18, cb;
+    if (!split) dq_geometry(type, &be, &bb, &cb);
+    if (be == 0 || n % (size_t)be != 0) return false;
+    alignas(16) unsigned char blk[256];  // the largest block, Q6_K, is 210 bytes
+    for (size_t b = 0; b < n / be; ++b) {
+        memcpy(blk, p + b * bb, bb);
+        float* o = out + b * be;
+        if (split) {  // dequant_q8_0 / dequant_q4_0 (:143-162): d * q, exact
+            const float d = sh_half(blk);
+            for (int i = 0; i < 32; ++i) {
+                const int q = type == NEON_GGML_Q8_0 ? (int)(int8_t)blk[2 + i]
+                                                     : (int)((blk[2 + (i & 15)] >> (i < 16 ? 0 : 4)) & 15) - 8;
+                o[i] = NEON_HD_MUL(d, (float)q);
+            }
+            continue;
+        }
+        for (int s = 0; s < be / 32; ++s) {
+            float w[32];
+            switch (type) {
+                case NEON_GGML_Q4_1: dq_sub<NEON_GGML_Q4_1>(blk, s, w); break;
+                case NEON_GGML_Q5_0: dq_sub<NEON_GGML_Q5_0>(blk, s, w); break;
+                case NEON_GGML_Q5_1: dq_sub<NEON_GGML_Q5_1>(blk, s, w); break;
+                case NEON_GGML_Q4_K: dq_sub<NEON_GGML_Q4_K>(blk, s, w); break;
+                case NEON_GGML_Q5_K: dq_sub<NEON_GGML_Q5_K>(blk, s, w); break;
+                case NEON_GGML_Q6_K: dq_sub<NEON_GGML_Q6_K>(blk, s, w); break;
+                default: return false;
+            }
+            memcpy(o + 32 * s, w, sizeof w);
+        }
+    }
+    return true;
+}
+
 }  // namespace neon

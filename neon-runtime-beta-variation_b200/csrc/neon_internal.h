@@ -150,6 +150,10 @@ int error(int code, const std::string& msg);
 size_t gguf_row_bytes(int type, size_t cols);
 // Values per block of `type` (block_size_for, rawllm_forward.hpp:289-299); 0 if unsupported.
 size_t gguf_block_elems(int type);
+// n values of a host row of `type`, decoded bit for bit as the reference's
+// dequantize_row does (rawllm_forward.hpp:301-321); false if n or the type
+// does not fit.
+bool dequantize_row_host(int type, const uint8_t* p, size_t n, float* out);
 // h[t] = row toks[t] of a padded-row (non Q4_0/Q8_0) embedding, decoded; a
 // token id out of range sets bit 1 of *err. seq rows of n_embd floats.
 int embed_rows(const neon_tensor* E, const int* toks, int seq, int n_embd, int n_vocab, float* h, unsigned int* err,

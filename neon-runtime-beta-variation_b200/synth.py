@@ -223,20 +223,41 @@ LLAMA3_70B = ModelConfig(128256, 8192, 80, 64, 8, 128, 28672, ctx_len=2432, rope
                          name="Llama-3-70B-shaped")
 
 
+def norm_weights(ggml_type: int, n: int, seed: int) -> np.ndarray:
+    """An RMSNorm weight of n values as raw bytes of `ggml_type`: 1 + 0.1 N(0,1)
+    for the float types (F16 and BF16 rounded to nearest even), random blocks
+    (other_weights / weights) for a block type."""
+    if ggml_type not in (GGML_F32, GGML_F16, GGML_BF16):
+        return weights(ggml_type, 1, n, seed).reshape(-1)
+    v = np.float32(1) + np.random.default_rng(seed).standard_normal(n, dtype=np.float32) * np.float32(0.1)
+    if ggml_type == GGML_F32:
+        return v.view(np.uint8)
+    if ggml_type == GGML_F16:
+        return v.astype(np.float16).view(np.uint8)
+    u = v.view(np.uint32)
+    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16).view(np.uint8)
+
+
 def model_tensors(cfg: ModelConfig, seed: int, wtype: int = GGML_Q4_0, embd_type: int = GGML_Q8_0,
-                  tied: bool = True, pooled: bool = False):
+                  tied: bool = True, pooled: bool = False, norm_type=None):
     """Seeded random-init tensors of a decoder, in GGUF layout:
     yields (role, layer, raw bytes uint8, ggml type, ne0, ne1); ne1 = 0 for 1-D.
     Projections are `wtype` with the benchmark's block distributions, the
-    embedding (also the lm_head when tied) is `embd_type`, norm weights fp32 1.
+    embedding (also the lm_head when tied) is `embd_type`, norm weights fp32 1,
+    or random norm_weights of `norm_type` when one is given.
     `pooled`: tensors cut from one random block pool (pooled_weights)."""
     weights_fn = pooled_weights if pooled else weights
     def sub(role, layer):
         return seed * 1000003 + role * 10007 + layer + 1
 
     ones = np.ones(cfg.n_embd, np.float32).view(np.uint8)
+    def norm(role, layer):
+        if norm_type is None:
+            return ones, GGML_F32
+        return norm_weights(norm_type, cfg.n_embd, sub(role, layer)), norm_type
+
     yield ROLE_TOKEN_EMBD, -1, weights_fn(embd_type, cfg.n_vocab, cfg.n_embd, sub(0, 0)), embd_type, cfg.n_embd, cfg.n_vocab
-    yield ROLE_OUTPUT_NORM, -1, ones, GGML_F32, cfg.n_embd, 0
+    yield (ROLE_OUTPUT_NORM, -1, *norm(ROLE_OUTPUT_NORM, 0), cfg.n_embd, 0)
     if not tied:
         yield ROLE_OUTPUT, -1, weights_fn(wtype, cfg.n_vocab, cfg.n_embd, sub(2, 0)), wtype, cfg.n_embd, cfg.n_vocab
     shapes = {ROLE_ATTN_Q: (cfg.q_dim, cfg.n_embd), ROLE_ATTN_K: (cfg.kv_dim, cfg.n_embd),
@@ -246,8 +267,8 @@ def model_tensors(cfg: ModelConfig, seed: int, wtype: int = GGML_Q4_0, embd_type
     if cfg.plain_ffn:
         del shapes[ROLE_FFN_GATE]
     for li in range(cfg.n_layer):
-        yield ROLE_ATTN_NORM, li, ones, GGML_F32, cfg.n_embd, 0
-        yield ROLE_FFN_NORM, li, ones, GGML_F32, cfg.n_embd, 0
+        yield (ROLE_ATTN_NORM, li, *norm(ROLE_ATTN_NORM, li), cfg.n_embd, 0)
+        yield (ROLE_FFN_NORM, li, *norm(ROLE_FFN_NORM, li), cfg.n_embd, 0)
         for role, (rows, cols) in shapes.items():
             yield role, li, weights_fn(wtype, rows, cols, sub(role, li)), wtype, cols, rows
 

@@ -517,6 +517,21 @@ int oracle_model_set(void* p, int role, int layer, const uint8_t* bytes, size_t 
         t = &m->layers[(size_t)layer * ORACLE_LAYER_ROLES + (role - R_ATTN_NORM)];
     }
     free(t->data);
+    if ((role == R_OUTPUT_NORM || role == R_ATTN_NORM || role == R_FFN_NORM) && type != ORACLE_GGML_F32) {
+        /* norm weights go through dequant_full (rawllm_forward.hpp:325-328,
+         * at :1077, :1161, :1226): any dequantisable type, read as F32 */
+        t->data = (uint8_t*)malloc(ne0 * sizeof(float) + 1);
+        if (oracle_row_bytes(type, ne0) == 0 || oracle_row_bytes(type, ne0) > nbytes ||
+            oracle_dequantize_row(type, bytes, ne0, (float*)t->data) != 0) {
+            free(t->data);
+            t->data = NULL;
+            return -1;
+        }
+        t->type = ORACLE_GGML_F32;
+        t->ne0 = ne0;
+        t->ne1 = ne1;
+        return 0;
+    }
     t->data = (uint8_t*)malloc(nbytes ? nbytes : 1);
     memcpy(t->data, bytes, nbytes);
     t->type = type;

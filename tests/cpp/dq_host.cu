@@ -63,3 +63,9 @@ extern "C" int dq_host_decode_row(int type, const unsigned char* row, int nu, fl
 // The block geometry the upload and the launcher use (values and bytes per
 // block, blocks per chunk).
 extern "C" void dq_host_geometry(int type, int* be, int* bb, int* cb) { neon::dq_geometry(type, be, bb, cb); }
+
+// n values of one host row of `type` (GGUF layout, any alignment) -> out, by
+// neon::dq_row_host, the decoder the engine runs on norm weights at load time.
+extern "C" int dq_host_row(int type, const unsigned char* p, size_t n, float* out) {
+    return neon::dq_row_host(type, p, n, out) ? 0 : -1;
+}

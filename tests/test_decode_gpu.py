@@ -77,6 +77,8 @@ def test_errors_match_reference_messages():
         m.forward([])
     with pytest.raises(RuntimeError, match="has shape"):
         m.set_tensor(S.ROLE_ATTN_Q, 0, S.q4_0_weights(32, 256, 1), S.GGML_Q4_0, 256, 32)
+    with pytest.raises(RuntimeError, match="norm weight must be"):  # a ragged Q4_K row
+        m.set_tensor(S.ROLE_FFN_NORM, 0, np.zeros(144, np.uint8), S.GGML_Q4_K, 256 - 32, 0)
 
 
 @pytest.mark.parametrize("cfg,n_prompt,steps", [
@@ -139,3 +141,20 @@ def test_kv_cache_shift_matches_reference():
     ref.close()
     toks = m.generate(nxt, 12)
     assert np.array_equal(toks, ref_toks)
+
+
+@pytest.mark.parametrize("norm_type", [S.GGML_F16, S.GGML_BF16, S.GGML_Q8_0, S.GGML_Q4_K],
+                         ids=lambda t: S.TYPE_NAMES[t])
+def test_norm_weight_types(norm_type):
+    """RMSNorm weights of F16 / BF16 / block types (dequant_full in the
+    reference, rawllm_forward.hpp:325-328), decoded at load time: the oracle's
+    greedy tokens, and logits within the whole-model bar."""
+    tensors = list(S.model_tensors(TINY, seed=17, norm_type=norm_type))
+    prompt = S.prompt_tokens(11, TINY.n_vocab, 18)
+    o = O.Model(TINY, tensors, "reference" if O.ref_available() else "port")
+    want_toks, want_logits = o.generate_greedy(prompt, 6)
+    m = N.Model(TINY, tensors)
+    assert np.array_equal(m.generate(prompt, 6), want_toks)
+    m.set_length(0)
+    assert rel_l2(m.forward(prompt), want_logits[0]) <= MODEL_L2_RTOL
+    m.free()

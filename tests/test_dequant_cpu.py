@@ -30,6 +30,7 @@ def dq(tmp_path_factory):
     L.dq_host_decode_row.argtypes = [C.c_int, C.c_void_p, C.c_int, C.c_void_p]
     L.dq_host_geometry.argtypes = [C.c_int, C.POINTER(C.c_int), C.POINTER(C.c_int), C.POINTER(C.c_int)]
     L.dq_host_code_dots.argtypes = [C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]
+    L.dq_host_row.argtypes = [C.c_int, C.c_void_p, C.c_size_t, C.c_void_p]
     return L
 
 
@@ -110,3 +111,25 @@ def test_code_dot_products(dq, typ):
         exact = (w * xx).sum(axis=1)
         scale = (np.abs(w) * np.abs(xx)).sum(axis=1) + np.abs(w).max() * np.abs(xx).sum(axis=1)
         assert np.all(np.abs(got - exact) <= 2e-6 * scale), (S.TYPE_NAMES[typ], r)
+
+
+@pytest.mark.parametrize("typ", S.ALL_TYPES, ids=lambda t: S.TYPE_NAMES[t])
+def test_host_row_decoder(dq, typ):
+    """neon::dq_row_host, which decodes non-F32 norm weights at load time,
+    on host rows at every byte offset mod 16 (unaligned blocks): the oracle's
+    values bit for bit, random bytes included; a ragged block row refused."""
+    be = S.BLOCK_ELEMS[typ]
+    n = 512
+    rows = [S.weights(typ, 1, n, seed=31).reshape(-1),
+            np.random.default_rng(typ + 7).integers(0, 256, S.weights(typ, 1, n, seed=31).size, dtype=np.uint8)]
+    for row in rows:
+        want = O.dequantize_row(typ, row, n)
+        for off in range(16):
+            buf = np.zeros(row.size + 16, np.uint8)
+            buf[off:off + row.size] = row
+            out = np.empty(n, np.float32)
+            assert dq.dq_host_row(typ, buf.ctypes.data + off, n, out.ctypes.data) == 0
+            assert same(out, want).all(), (S.TYPE_NAMES[typ], off)
+    if be > 1:
+        out = np.empty(n, np.float32)
+        assert dq.dq_host_row(typ, rows[0].ctypes.data, n - 16, out.ctypes.data) == -1

@@ -171,3 +171,18 @@ def test_model_forward_other_types_matches_reference(wtype, etype, tied):
     ta, la = mo.generate_greedy(p, 5)
     tb, lb = mr.generate_greedy(p, 5)
     assert np.array_equal(ta, tb) and np.array_equal(bits(la), bits(lb))
+
+
+@ref_only
+@pytest.mark.parametrize("norm_type", [S.GGML_F16, S.GGML_BF16, S.GGML_Q8_0, S.GGML_Q4_K],
+                         ids=lambda t: S.TYPE_NAMES[t])
+def test_model_forward_norm_types_matches_reference(norm_type):
+    """RMSNorm weights of another type than F32 (the reference reads them
+    through dequant_full, rawllm_forward.hpp:325-328, at :1077 / :1161 /
+    :1226), random around 1: bit for bit."""
+    tensors = list(S.model_tensors(TINY, seed=15, norm_type=norm_type))
+    mo, mr = O.Model(TINY, tensors, "port"), O.Model(TINY, tensors, "reference", threads=4)
+    p = S.prompt_tokens(7, TINY.n_vocab, 16)
+    ta, la = mo.generate_greedy(p, 4)
+    tb, lb = mr.generate_greedy(p, 4)
+    assert np.array_equal(ta, tb) and np.array_equal(bits(la), bits(lb))
