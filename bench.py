@@ -138,6 +138,9 @@ def parse_args():
                         "(what nanity_convert.py --quant Q4_K writes)")
     p.add_argument("--prefill-mma", action="store_true",
                    help="prompt passes of Q4_0 models on the tensor-core prefill kernel (neon_cuda_set_prefill_mma)")
+    p.add_argument("--dq-ring", action="store_true",
+                   help="one-position calls of the dequantising types on the bulk-copy ring kernel "
+                        "(neon_cuda_set_dq_ring)")
     p.add_argument("--batch", type=int, default=1,
                    help="matvec workloads: positions per call; > 1 times the prefill path (one JSON line)")
     p.add_argument("--type-sweep", action="store_true",
@@ -407,6 +410,8 @@ def run_decode(args):
     N.init(local)
     if getattr(args, "prefill_mma", False):
         N.set_prefill_mma(True)
+    if getattr(args, "dq_ring", False):
+        N.set_dq_ring(True)
     N.set_fused_collectives(not args.no_fused_collectives)
     comm = None
     barrier, max_over_ranks = (lambda: None), (lambda v: v)
@@ -560,6 +565,8 @@ def run_neon(args):
     N.init(local)
     if getattr(args, "prefill_mma", False):
         N.set_prefill_mma(True)
+    if getattr(args, "dq_ring", False):
+        N.set_dq_ring(True)
     dev = torch.device("cuda", local)
 
     host_w = host_rotation(rank, ROTATION)
@@ -705,7 +712,9 @@ def run_neon(args):
                     "d2h_bytes_per_step": CALLS_PER_STEP * ROWS * 4,
                     "api": "neon_cuda.proj_all_positions (host buffers, blocking per call)",
                     "steps": e2e_steps},
-            "roofline": {"bound": "hbm", "kernel": KERNEL, "achieved": round(achieved, 1),
+            "roofline": {"bound": "hbm", "kernel": (KERNEL.replace("matvec_dq_kernel", "matvec_dq_ring_kernel")
+                                                    if args.dq_ring else KERNEL),
+                         "achieved": round(achieved, 1),
                          "peak": peak, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
                          if peak_kind == "measured" else "fallback 6.65 TB/s",
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
@@ -799,6 +808,7 @@ def run_type_sweep(args):
 
     torch.cuda.set_device(0)
     N.init(0)
+    N.set_dq_ring(bool(args.dq_ring))
     dev = torch.device("cuda", 0)
     peak, peak_kind = measured_peak()
     stream = torch.cuda.Stream(device=dev)
@@ -829,7 +839,8 @@ def run_type_sweep(args):
         ms = start.elapsed_time(end)
         bytes_call = S.algorithmic_bytes(TYPE, ROWS, COLS)
         gbs = K * CALLS_PER_STEP * bytes_call / (ms / 1e3) / 1e9
-        print(json.dumps({"workload": name, "type": TYPE_NAME, "kernel": KERNEL, "rows": ROWS, "cols": COLS,
+        kernel = KERNEL.replace("matvec_dq_kernel", "matvec_dq_ring_kernel") if args.dq_ring else KERNEL
+        print(json.dumps({"workload": name, "type": TYPE_NAME, "kernel": kernel, "rows": ROWS, "cols": COLS,
                           "value": round(gbs, 1), "unit": UNIT, "frac": round(gbs / peak, 4),
                           "peak": peak, "peak_source": peak_kind, "us_per_call": round(ms * 1e3 / (K * CALLS_PER_STEP), 3),
                           "bytes_per_call": bytes_call, "rotation_tensors": ROTATION, "steps": K, "warmup": W}),

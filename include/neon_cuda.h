@@ -346,6 +346,14 @@ NEON_API int neon_cuda_set_fused_collectives(int enabled);
  * runs) until a GPU run has validated it; the switch is process-wide. */
 NEON_API int neon_cuda_set_prefill_mma(int enabled);
 
+/* One-position calls of the dequantising types (F32, F16, BF16, Q4_1, Q5_0,
+ * Q5_1, Q4_K, Q5_K, Q6_K) on a bulk-copy ring: a copy warp per CTA streams
+ * row tiles into a ring of shared-memory stages (several tiles in flight per
+ * CTA) and the compute warps decode from it, with the same decoders and
+ * per-sub-block dot products as the register-buffer kernel. Off by default
+ * until a GPU run has validated it; the switch is process-wide. */
+NEON_API int neon_cuda_set_dq_ring(int enabled);
+
 /* Launch option: programmatic dependent launch (PDL) lets a matvec fetch its
  * weights while the previous kernel on the stream finishes; on by default. */
 NEON_API int neon_cuda_set_pdl(int enabled);

@@ -35,6 +35,7 @@ thread_local std::string g_err;
 std::atomic<uint64_t> g_launches{0};
 std::atomic<int> g_pdl{1};
 std::atomic<int> g_prefill_mma{0};  // neon_cuda_set_prefill_mma
+std::atomic<int> g_dq_ring{0};      // neon_cuda_set_dq_ring
 
 struct DeviceState {
     bool ready = false;
@@ -127,6 +128,8 @@ using StreamKernel = void (*)(StreamArgs);
 StreamKernel stream_kernel(int type, int rc);
 using DqKernel = void (*)(DqArgs);
 DqKernel dq_kernel(int type, int T);
+using DqRingKernel = void (*)(DqRingArgs);
+DqRingKernel dq_ring_kernel(int type, int rpw);
 constexpr int kDqTypes[] = {NEON_GGML_F32, NEON_GGML_F16, NEON_GGML_BF16, NEON_GGML_Q4_1, NEON_GGML_Q5_0,
                             NEON_GGML_Q5_1, NEON_GGML_Q4_K, NEON_GGML_Q5_K, NEON_GGML_Q6_K};
 
@@ -161,6 +164,8 @@ int init_device(int device) {
         for (int r : {2, 4, 8, 16, 32}) rc = rc ? rc : ensure_smem(stream_kernel(t, r), kMaxSmem);
     for (int t : kDqTypes)
         for (int T : {1, 2, 4}) rc = rc ? rc : ensure_smem(dq_kernel(t, T), kMaxSmem);
+    for (int t : kDqTypes)
+        for (int rpw : {1, 2}) rc = rc ? rc : ensure_smem(dq_ring_kernel(t, rpw), kMaxSmem);
     if (rc) return rc;
     void* err = nullptr;
     NEON_CUDA_TRY(cudaGetSymbolAddress(&err, g_neon_device_err));
@@ -375,6 +380,134 @@ DqKernel dq_kernel(int type, int T) {
 #undef NEON_DQ_CASE
 }
 
+// The ring kernel instantiation for (type, rows per warp).
+DqRingKernel dq_ring_kernel(int type, int rpw) {
+#define NEON_DQ_RING_CASE(TY) \
+    case TY:                  \
+        return rpw >= 2 ? matvec_dq_ring_kernel<TY, 2> : matvec_dq_ring_kernel<TY, 1>;
+    switch (type) {
+        NEON_DQ_RING_CASE(NEON_GGML_F32)
+        NEON_DQ_RING_CASE(NEON_GGML_F16)
+        NEON_DQ_RING_CASE(NEON_GGML_BF16)
+        NEON_DQ_RING_CASE(NEON_GGML_Q4_1)
+        NEON_DQ_RING_CASE(NEON_GGML_Q5_0)
+        NEON_DQ_RING_CASE(NEON_GGML_Q5_1)
+        NEON_DQ_RING_CASE(NEON_GGML_Q4_K)
+        NEON_DQ_RING_CASE(NEON_GGML_Q5_K)
+        NEON_DQ_RING_CASE(NEON_GGML_Q6_K)
+        default: return nullptr;
+    }
+#undef NEON_DQ_RING_CASE
+}
+
+int dq_ring_occupancy(int type, int rpw, int smem) {
+    static std::mutex mu;
+    static std::vector<std::pair<long long, int>> cache;
+    const long long key = ((long long)type << 40) | ((long long)rpw << 32) | (unsigned)smem;
+    std::lock_guard<std::mutex> lk(mu);
+    for (auto& kv : cache)
+        if (kv.first == key) return kv.second;
+    int occ = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, dq_ring_kernel(type, rpw), kStreamBlock, smem) !=
+        cudaSuccess)
+        occ = 1;
+    occ = std::max(1, occ);
+    cache.emplace_back(key, occ);
+    return occ;
+}
+
+// One launch group of a dequantising type at one position on the ring
+// kernel; returns 1 (nothing launched) when X and one stage do not fit.
+int launch_dq_ring(const std::vector<const neon_proj_target_t*>& t, int type, size_t cols, const float* dX,
+                   cudaStream_t st, DeviceState& ds, int accumulate, const neon_proj_target_t* base,
+                   const neon_internal::MatvecExt* ext) {
+    int be, bb, cb;
+    dq_geometry(type, &be, &bb, &cb);
+    const int nu = (int)((cols + 31) / 32);
+    const int nblk = nu / (be / 32);
+    const long long pitch = (long long)t[0]->W->pitch;
+    size_t total_rows = 0;
+    for (const auto* tg : t) total_rows += tg->W->rows;
+    const DqRingPlan p = plan_dq_ring(type, nblk, pitch, total_rows, ds.sms, kStageTarget);
+    const int rc_rows = kStreamWarps * p.rpw;
+    const int xb = dq_x_bytes(1, nu);
+    if (xb + p.stage_bytes > kMaxSmem) return 1;
+    size_t start = 0;
+    while (start < t.size()) {
+        DqRingArgs r;
+        std::memset(&r, 0, sizeof(r));
+        DqArgs& a = r.d;
+        size_t n = std::min(t.size() - start, (size_t)kMaxSpans);
+        int tiles = 0;
+        for (size_t i = 0; i < n; ++i) {
+            const neon_proj_target_t* tg = t[start + i];
+            Span& sp = a.s.span[i];
+            sp.qs = tg->W->qs;
+            sp.d = nullptr;
+            sp.y = tg->Y;
+            sp.y_stride = (long long)tg->y_stride;
+            sp.rows = (int)tg->W->rows;
+            sp.tile0 = tiles;
+            tiles += (int)((tg->W->rows + rc_rows - 1) / rc_rows);
+            if (ext && ext->epi) {
+                const size_t k = (size_t)(tg - base);
+                sp.epi = ext->epi[k];
+                sp.pos_stride = ext->pos_stride ? ext->pos_stride[k] : 0;
+            }
+            if (ext && ext->peer_mode == 1) sp.epi = kEpiPeer;
+        }
+        a.s.x = dX;
+        a.s.err = ds.err;
+        a.s.n_spans = (int)n;
+        a.s.n_tiles = tiles;
+        a.s.accumulate = accumulate;
+        if (ext) {
+            a.s.norm_w = ext->norm_w;
+            a.s.norm_eps = ext->norm_eps;
+            a.s.d_pos = ext->d_pos;
+            a.s.rope_cs = ext->rope_cs;
+            a.s.rope_half = ext->rope_half;
+            a.s.head_dim = ext->head_dim;
+            a.s.peer_mode = ext->peer_mode;
+            if (ext->peer_mode) a.s.peer = ext->peer;
+        }
+        a.s.x_vec = (reinterpret_cast<uintptr_t>(dX) % 16) == 0 &&
+                    (!a.s.norm_w || (reinterpret_cast<uintptr_t>(a.s.norm_w) % 16) == 0);
+        a.pitch = pitch;
+        a.x_stride = (long long)cols;
+        a.cols = (int)cols;
+        a.nu = nu;
+        a.nblk = nblk;
+        a.nch = p.nch;
+        a.seq = 1;
+        r.kcb = p.kcb;
+        r.row_stride = p.row_stride;
+        r.stage_bytes = p.stage_bytes;
+        // the ring depth that keeps the most weight bytes in flight per SM
+        int best_stages = 1, best_occ = 1;
+        long long best_bytes = -1;
+        for (int st_n = 1; st_n <= kDqRingMaxStages; ++st_n) {
+            const int sm_bytes = xb + st_n * p.stage_bytes;
+            if (sm_bytes > kMaxSmem) break;
+            const int occ = std::min(dq_ring_occupancy(type, p.rpw, sm_bytes), kStreamCtasPerSm);
+            const long long inflight = (long long)occ * st_n * p.stage_bytes;
+            if (inflight >= best_bytes) {
+                best_bytes = inflight;
+                best_stages = st_n;
+                best_occ = occ;
+            }
+        }
+        const int grid = std::min(tiles, ds.sms * best_occ);
+        const int per_cta_items = ((tiles + grid - 1) / grid) * p.nch;
+        r.stages = std::max(1, std::min(best_stages, per_cta_items));
+        const int smem = xb + r.stages * p.stage_bytes;
+        int rc = launch_n(dq_ring_kernel(type, p.rpw), dim3(grid), kStreamBlock, smem, st, r);
+        if (rc) return rc;
+        start += n;
+    }
+    return NEON_OK;
+}
+
 int dq_occupancy(int type, int T, int smem) {
     static std::mutex mu;
     static std::vector<std::pair<long long, int>> cache;
@@ -395,6 +528,10 @@ int dq_occupancy(int type, int T, int smem) {
 int launch_dq(const std::vector<const neon_proj_target_t*>& t, int type, size_t cols, const float* dX,
               size_t x_stride, size_t seq, cudaStream_t st, DeviceState& ds, int accumulate,
               const neon_proj_target_t* base, const neon_internal::MatvecExt* ext) {
+    if (seq == 1 && g_dq_ring.load(std::memory_order_relaxed)) {
+        const int rc = launch_dq_ring(t, type, cols, dX, st, ds, accumulate, base, ext);
+        if (rc != 1) return rc;  // 1: X does not fit beside a stage; the register-buffer kernel below
+    }
     int be, bb, cb;
     dq_geometry(type, &be, &bb, &cb);
     const int nu = (int)((cols + 31) / 32);
@@ -756,6 +893,11 @@ int neon_cuda_init(int device) {
 
 int neon_cuda_set_prefill_mma(int enabled) {
     g_prefill_mma.store(enabled ? 1 : 0);
+    return NEON_OK;
+}
+
+int neon_cuda_set_dq_ring(int enabled) {
+    g_dq_ring.store(enabled ? 1 : 0);
     return NEON_OK;
 }
 

@@ -608,6 +608,276 @@ __global__ void __launch_bounds__(kThreads) matvec_dq_kernel(const __grid_consta
     }
 }
 
+// One position on a bulk-copy ring (the streaming kernel's scheme, for every
+// dequantised type): a copy warp moves the weights of an item -- the RC rows
+// of a tile, one chunk of kcb blocks of each -- into a ring of shared-memory
+// stages with cp.async.bulk, one mbarrier per stage counting its bytes, so a
+// CTA keeps several items in flight where matvec_dq_kernel keeps two chunks
+// per warp in registers, and the compute warps decode straight from the
+// stage. Every warp owns RPW rows of a tile: a read of X serves all of them.
+//
+// Stage layout: row r of the item at r * row_stride; row_stride is the pitch
+// when a whole row is one chunk (the tile is then one contiguous copy), else
+// kcb * BB. Every copy starts and ends on a 16-byte boundary: the pitch and
+// kcb * BB are multiples of 16, and a row's last chunk runs to its pitch.
+constexpr int kDqRingMaxStages = 4;
+
+struct DqRingArgs {
+    DqArgs d;         // spans of RC-row tiles, X, epilogue options; d.nch chunks per row
+    int kcb;          // blocks per chunk
+    int row_stride;   // bytes between a stage's rows
+    int stages;       // ring depth (<= kDqRingMaxStages)
+    int stage_bytes;  // bytes per stage (a multiple of 128)
+};
+
+// Tile plan of a ring launch: RC = 8 * rpw rows per tile (two rows per warp
+// once every SM has 16-row tiles to take); a row is one chunk when the tile's
+// rows fit `stage_target` bytes, else chunks of kcb blocks, kcb a multiple of
+// the smallest block count whose bytes are a multiple of 16 (so every copy
+// starts and ends 16-byte aligned). pitch: bytes per device row.
+struct DqRingPlan {
+    int rpw, kcb, nch, row_stride, stage_bytes;
+};
+inline DqRingPlan plan_dq_ring(int type, int nblk, long long pitch, size_t total_rows, int sms, int stage_target) {
+    int be, bb, cb;
+    dq_geometry(type, &be, &bb, &cb);
+    DqRingPlan p{};
+    p.rpw = total_rows >= (size_t)16 * (size_t)sms ? 2 : 1;
+    const int rc = kStreamWarps * p.rpw;
+    int g = 1;
+    while ((g * bb) % 16) ++g;
+    p.kcb = nblk;
+    p.nch = 1;
+    p.row_stride = (int)pitch;
+    if (rc * pitch > stage_target) {
+        const int k = stage_target / (rc * bb) / g * g;
+        p.kcb = k > g ? k : g;
+        p.nch = (nblk + p.kcb - 1) / p.kcb;
+        if (p.nch == 1) p.kcb = nblk;
+        else p.row_stride = p.kcb * bb;
+    }
+    p.stage_bytes = (rc * p.row_stride + 127) & ~127;
+    return p;
+}
+
+template <int TYPE, int RPW>
+__global__ void __launch_bounds__(kStreamBlock) matvec_dq_ring_kernel(const __grid_constant__ DqRingArgs r) {
+    using D = DqShape<TYPE>;
+    constexpr bool kFloat = TYPE == NEON_GGML_F32 || TYPE == NEON_GGML_F16 || TYPE == NEON_GGML_BF16;
+    constexpr int RC = kStreamWarps * RPW;
+    const DqArgs& a = r.d;
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ float rowv[2][RC];  // by tile parity: a tile's results never wait on the last epilogue
+    __shared__ double dscratch[32];
+    __shared__ float2 rcs[kMaxRopeHalf];
+    __shared__ __align__(8) uint64_t full[kDqRingMaxStages];
+    __shared__ __align__(8) uint64_t empty[kDqRingMaxStages];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nu = a.nu, nch = a.nch, S = r.stages, RS = r.row_stride;
+    float* xs = reinterpret_cast<float*>(smem);
+    unsigned char* ring = smem + dq_x_bytes(1, nu);
+    const int my_tiles =
+        (int)blockIdx.x < a.s.n_tiles ? (a.s.n_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    const int n_items = my_tiles * nch;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kStreamWarps);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    if (warp == kStreamWarps) {
+        // Copy warp. Weights are never written by an earlier kernel of the
+        // stream: no dependency wait; a stage is refilled as soon as every
+        // compute warp has released it.
+        pdl_launch_dependents();
+        for (int item = 0; item < n_items; ++item) {
+            const int stage = item % S;
+            if (item >= S && !mbar_wait(&empty[stage], (uint32_t)(((item / S) - 1) & 1), a.s.err)) break;
+            const int tile = (int)blockIdx.x + (item / nch) * (int)gridDim.x;
+            const int chunk = item % nch;
+            const Span& sp = a.s.span[find_span_of(a.s, tile)];
+            const int row0 = (tile - sp.tile0) * RC;
+            const int nrows = min(RC, sp.rows - row0);
+            unsigned char* dst = ring + stage * r.stage_bytes;
+            if (nch == 1) {
+                const uint32_t bytes = (uint32_t)((long long)nrows * a.pitch);
+                if (lane == 0) {
+                    mbar_arrive_expect_tx(&full[stage], bytes);
+                    bulk_g2s(dst, sp.qs + (long long)row0 * a.pitch, bytes, &full[stage]);
+                }
+                continue;
+            }
+            const long long off = (long long)chunk * RS;
+            const uint32_t cbytes = (uint32_t)min((long long)RS, a.pitch - off);
+            if (lane == 0) mbar_arrive_expect_tx(&full[stage], (uint32_t)nrows * cbytes);
+            __syncwarp();
+            for (int rr = lane; rr < nrows; rr += 32)
+                bulk_g2s(dst + rr * RS, sp.qs + (long long)(row0 + rr) * a.pitch + off, cbytes, &full[stage]);
+        }
+        return;
+    }
+
+    pdl_wait();
+    const unsigned int peer_call =
+        a.s.peer_mode ? *reinterpret_cast<volatile const unsigned int*>(a.s.peer.calls) + 1u : 0u;
+    const int pos = a.s.d_pos ? *a.s.d_pos : 0;
+    if (a.s.rope_cs)
+        for (int i = threadIdx.x; i < a.s.rope_half; i += kStreamThreads)
+            rcs[i] = a.s.rope_cs[(long long)pos * a.s.rope_half + i];
+
+    // X (rms-normalised first when asked), zero past `cols`
+    {
+        const float nscale = a.s.norm_w ? cta_rms_scale(a.s.x, a.cols, a.s.norm_eps, dscratch) : 1.f;
+        const float* xp = a.s.x;
+        if (a.s.x_vec) {
+            const int n4 = a.cols >> 2;
+#pragma unroll 4
+            for (int i4 = threadIdx.x; i4 < n4; i4 += kStreamThreads) {
+                float4 v = __ldg(reinterpret_cast<const float4*>(xp) + i4);
+                if (a.s.norm_w) {
+                    const float4 g = __ldg(reinterpret_cast<const float4*>(a.s.norm_w) + i4);
+                    v.x = __fmul_rn(__fmul_rn(v.x, nscale), g.x);
+                    v.y = __fmul_rn(__fmul_rn(v.y, nscale), g.y);
+                    v.z = __fmul_rn(__fmul_rn(v.z, nscale), g.z);
+                    v.w = __fmul_rn(__fmul_rn(v.w, nscale), g.w);
+                }
+                const int i = 4 * i4;
+                *reinterpret_cast<float4*>(xs + (i >> 5) * kQ8Pitch + (i & 31)) = v;
+            }
+            for (int i = 4 * n4 + threadIdx.x; i < nu * 32; i += kStreamThreads) {
+                float v = 0.f;
+                if (i < a.cols) {
+                    v = __ldg(xp + i);
+                    if (a.s.norm_w) v = __fmul_rn(__fmul_rn(v, nscale), __ldg(a.s.norm_w + i));
+                }
+                xs[(i >> 5) * kQ8Pitch + (i & 31)] = v;
+            }
+        } else {
+#pragma unroll 4
+            for (int i = threadIdx.x; i < nu * 32; i += kStreamThreads) {
+                float v = 0.f;
+                if (i < a.cols) {
+                    v = __ldg(xp + i);
+                    if (a.s.norm_w) v = __fmul_rn(__fmul_rn(v, nscale), __ldg(a.s.norm_w + i));
+                }
+                xs[(i >> 5) * kQ8Pitch + (i & 31)] = v;
+            }
+        }
+    }
+    compute_sync();
+    if constexpr (!kFloat && DqCode<TYPE>::HAS_B) {
+        // sum of each 32-value sub-block of X, kept in the pitch's spare float
+        for (int u = threadIdx.x; u < nu; u += kStreamThreads) {
+            float* xu = xs + (long long)u * kQ8Pitch;
+            const float4* x4 = reinterpret_cast<const float4*>(xu);
+            float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+            for (int k = 0; k < 8; k += 2) {
+                const float4 p = x4[k], q = x4[k + 1];
+                s0 += (p.x + p.y) + (p.z + p.w);
+                s1 += (q.x + q.y) + (q.z + q.w);
+            }
+            xu[32] = s0 + s1;
+        }
+        compute_sync();
+    }
+    pdl_launch_dependents();
+
+    float acc[RPW];
+#pragma unroll
+    for (int i = 0; i < RPW; ++i) acc[i] = 0.f;
+    for (int item = 0; item < n_items; ++item) {
+        const int stage = item % S;
+        const uint32_t parity = (uint32_t)((item / S) & 1);
+        const int tile = (int)blockIdx.x + (item / nch) * (int)gridDim.x;
+        const int chunk = item % nch;
+        const Span& sp = a.s.span[find_span_of(a.s, tile)];
+        const int row0 = (tile - sp.tile0) * RC;
+        const bool ok = mbar_wait(&full[stage], parity, a.s.err);
+        if (compute_sync_or(!ok)) return;
+        const unsigned char* st = ring + stage * r.stage_bytes;
+        const int k0 = chunk * r.kcb;
+        const int nblk_c = min(r.kcb, a.nblk - k0);
+        bool valid[RPW];
+#pragma unroll
+        for (int i = 0; i < RPW; ++i) valid[i] = row0 + warp * RPW + i < sp.rows;
+        if constexpr (kFloat) {
+            // lanes take the 16-byte words l, l + 32, ... of the chunk: X is
+            // then read without bank conflicts
+            constexpr int VPW = TYPE == NEON_GGML_F32 ? 4 : 8;  // values per word
+            const int words = (nblk_c * D::BB) >> 4;
+            for (int wi = lane; wi < words; wi += 32) {
+                const int e = k0 * 32 + VPW * wi;
+                const float4* x4 = reinterpret_cast<const float4*>(xs + (e >> 5) * kQ8Pitch + (e & 31));
+                float xv[VPW];
+#pragma unroll
+                for (int q = 0; q < VPW / 4; ++q) {
+                    const float4 t = x4[q];
+                    xv[4 * q] = t.x;
+                    xv[4 * q + 1] = t.y;
+                    xv[4 * q + 2] = t.z;
+                    xv[4 * q + 3] = t.w;
+                }
+#pragma unroll
+                for (int i = 0; i < RPW; ++i) {
+                    if (!valid[i]) continue;
+                    const uint4 v = *reinterpret_cast<const uint4*>(st + (warp * RPW + i) * RS + 16 * wi);
+                    const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        if constexpr (TYPE == NEON_GGML_F32) {
+                            acc[i] = fmaf(__uint_as_float(u[q]), xv[q], acc[i]);
+                        } else if constexpr (TYPE == NEON_GGML_F16) {
+                            acc[i] = fmaf(__half2float(__ushort_as_half((unsigned short)(u[q] & 0xFFFFu))),
+                                          xv[2 * q], acc[i]);
+                            acc[i] = fmaf(__half2float(__ushort_as_half((unsigned short)(u[q] >> 16))),
+                                          xv[2 * q + 1], acc[i]);
+                        } else {
+                            acc[i] = fmaf(__uint_as_float(u[q] << 16), xv[2 * q], acc[i]);
+                            acc[i] = fmaf(__uint_as_float(u[q] & 0xFFFF0000u), xv[2 * q + 1], acc[i]);
+                        }
+                    }
+                }
+            }
+        } else {
+            for (int u = lane; u < nblk_c * D::SUBS; u += 32) {
+                const float* xu = xs + (long long)(k0 * D::SUBS + u) * kQ8Pitch;
+                const float xsum = DqCode<TYPE>::HAS_B ? xu[32] : 0.f;
+#pragma unroll
+                for (int i = 0; i < RPW; ++i) {
+                    if (!valid[i]) continue;
+                    DqCode<TYPE> c;
+                    dq_codes<TYPE>(st + (warp * RPW + i) * RS + (u / D::SUBS) * D::BB, u % D::SUBS, c);
+                    acc[i] += dq_code_dot<TYPE>(c, xu, xsum);
+                }
+            }
+        }
+        // this warp is done with the stage: release it to the copy warp
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[stage]);
+        if (chunk == nch - 1) {
+            const int tb = (item / nch) & 1;
+#pragma unroll
+            for (int i = 0; i < RPW; ++i) {
+#pragma unroll
+                for (int o = 16; o; o >>= 1) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], o);
+                if (lane == 0) rowv[tb][warp * RPW + i] = acc[i];
+                acc[i] = 0.f;
+            }
+            compute_sync();
+            float yold = 0.f;
+            if (a.s.accumulate && sp.epi == kEpiStore && (int)threadIdx.x < RC && row0 + (int)threadIdx.x < sp.rows)
+                yold = sp.y[row0 + threadIdx.x];
+            stream_epilogue(a.s, sp, row0, RC, rowv[tb], peer_call, pos, rcs, yold);
+        }
+    }
+}
+
 // h[t] = the values of embedding row tokens[t] (transformer_forward's
 // embedding lookup, rawllm_forward.hpp:1023-1033, through dequantize_row).
 // One thread per 32-value sub-block; an out-of-range id sets bit 1 of *err

@@ -98,6 +98,7 @@ C_ENTRY_POINTS = (
     "neon_cuda_set_fused_collectives",
     "neon_cuda_set_pdl",
     "neon_cuda_set_prefill_mma",
+    "neon_cuda_set_dq_ring",
 )
 
 _sz = C.c_size_t
@@ -160,6 +161,7 @@ def load(path: str | None = None) -> C.CDLL:
         L.neon_cuda_launch_count.restype = C.c_uint64
         L.neon_cuda_set_pdl.argtypes = [C.c_int]
         L.neon_cuda_set_prefill_mma.argtypes = [C.c_int]
+        L.neon_cuda_set_dq_ring.argtypes = [C.c_int]
         L.neon_cuda_matvec_q4_0_noalloc.argtypes = [_vp, _vp, _sz, _vp, _sz, _sz, _vp]
         L.neon_cuda_model_create.argtypes = [C.POINTER(_ModelConfig), C.POINTER(_vp)]
         L.neon_cuda_model_set_tensor.argtypes = [_vp, C.c_int, C.c_int, _vp, _sz, C.c_int, _sz, _sz]
@@ -211,6 +213,13 @@ def set_prefill_mma(enabled: bool) -> None:
     """Multi-position Q4_0 calls on the tensor cores (int8 MMA, bit-exact with
     dot_q4_0_q8_0) instead of the CUDA-core kernel; process-wide, off by default."""
     _check(load().neon_cuda_set_prefill_mma(1 if enabled else 0))
+
+
+def set_dq_ring(enabled: bool) -> None:
+    """One-position calls of the dequantising types on the bulk-copy ring
+    kernel (several row tiles in flight per CTA) instead of the register-buffer
+    kernel; process-wide, off by default."""
+    _check(load().neon_cuda_set_dq_ring(1 if enabled else 0))
 
 
 def set_pdl(enabled: bool) -> None:

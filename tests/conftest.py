@@ -20,6 +20,12 @@ for p in (os.path.join(ROOT, "oracle"), PKG, ROOT):
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA GPU (sm_100a, B200)")
+    config.addinivalue_line("markers", "newest: a kernel variant behind an off-by-default switch; run after "
+                                       "every other test, so that with -x its failure stops nothing else")
+
+
+def pytest_collection_modifyitems(config, items):
+    items.sort(key=lambda it: it.get_closest_marker("newest") is not None)  # stable: order kept otherwise
 
 
 def load_golden(name):

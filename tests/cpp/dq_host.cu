@@ -69,3 +69,15 @@ extern "C" void dq_host_geometry(int type, int* be, int* bb, int* cb) { neon::dq
 extern "C" int dq_host_row(int type, const unsigned char* p, size_t n, float* out) {
     return neon::dq_row_host(type, p, n, out) ? 0 : -1;
 }
+
+// The ring kernel's tile plan (neon::plan_dq_ring): out = {rpw, kcb, nch,
+// row_stride, stage_bytes}.
+extern "C" void dq_host_ring_plan(int type, int nblk, long long pitch, size_t total_rows, int sms,
+                                  int stage_target, int* out) {
+    const neon::DqRingPlan p = neon::plan_dq_ring(type, nblk, pitch, total_rows, sms, stage_target);
+    out[0] = p.rpw;
+    out[1] = p.kcb;
+    out[2] = p.nch;
+    out[3] = p.row_stride;
+    out[4] = p.stage_bytes;
+}

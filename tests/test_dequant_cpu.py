@@ -31,6 +31,7 @@ def dq(tmp_path_factory):
     L.dq_host_geometry.argtypes = [C.c_int, C.POINTER(C.c_int), C.POINTER(C.c_int), C.POINTER(C.c_int)]
     L.dq_host_code_dots.argtypes = [C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]
     L.dq_host_row.argtypes = [C.c_int, C.c_void_p, C.c_size_t, C.c_void_p]
+    L.dq_host_ring_plan.argtypes = [C.c_int, C.c_int, C.c_longlong, C.c_size_t, C.c_int, C.c_int, C.c_void_p]
     return L
 
 
@@ -133,3 +134,63 @@ def test_host_row_decoder(dq, typ):
     if be > 1:
         out = np.empty(n, np.float32)
         assert dq.dq_host_row(typ, rows[0].ctypes.data, n - 16, out.ctypes.data) == -1
+
+
+RING_SHAPES = [(4096, 4096), (1000, 2048), (14336, 4096), (4096, 14336), (24, 28672), (77, 1013), (8, 32),
+               (3, 256), (28672, 8192), (8192, 28672), (1024, 3072), (151936, 1024)]
+
+
+@pytest.mark.parametrize("typ", DQ_TYPES, ids=lambda t: S.TYPE_NAMES[t])
+def test_ring_plan_copies(dq, typ):
+    """The bulk-copy ring kernel (matvec_dq_ring_kernel) on its own tile plan
+    (neon::plan_dq_ring), its copy warp and compute warps emulated: every
+    cp.async.bulk starts and ends on a 16-byte boundary on both sides, stays
+    inside the tensor's rows x pitch bytes and its stage, fits one mbarrier
+    phase's byte count; every block of every row is decoded exactly once, from
+    bytes the copy delivered."""
+    be, bb, _ = geometry(dq, typ)
+    subs = be // 32
+    for rows, cols in RING_SHAPES:
+        if S.BLOCK_ELEMS[typ] > 1 and cols % S.BLOCK_ELEMS[typ]:
+            continue
+        nu = (cols + 31) // 32
+        nblk = nu // subs
+        pitch = (nblk * bb + 15) & ~15
+        for sms in (148, 132):
+            out = (C.c_int * 5)()
+            dq.dq_host_ring_plan(typ, nblk, pitch, rows, sms, 40 * 1024, out)
+            rpw, kcb, nch, rs, stage = list(out)
+            RC = 8 * rpw
+            xb = (nu * 36 * 4 + 127) & ~127
+            if xb + stage > 220 * 1024:
+                continue  # the launcher keeps the register-buffer kernel
+            assert rs % 16 == 0 and stage % 128 == 0 and RC * rs <= stage and 1 <= kcb and nch >= 1
+            assert (nch == 1) == (kcb >= nblk) and (nch > 1 or rs == pitch)
+            seen = np.zeros(nblk, np.int64)
+            for row0 in range(0, rows, RC) if rows <= 4096 else (0, ((rows - 1) // RC) * RC):
+                nrows = min(RC, rows - row0)
+                for chunk in range(nch):
+                    if nch == 1:
+                        copies = [(row0 * pitch, 0, nrows * pitch)]
+                        cbytes = pitch
+                    else:
+                        off = chunk * rs
+                        cbytes = min(rs, pitch - off)
+                        assert cbytes > 0
+                        copies = [((row0 + r) * pitch + off, r * rs, cbytes) for r in range(nrows)]
+                    assert sum(c[2] for c in copies) < (1 << 20)
+                    for src, dst, n in copies:
+                        assert src % 16 == 0 and dst % 16 == 0 and n % 16 == 0
+                        assert src + n <= rows * pitch and dst + n <= stage
+                    k0 = chunk * kcb
+                    nblk_c = min(kcb, nblk - k0)
+                    assert nblk_c > 0 and k0 * bb % 16 == 0
+                    # compute warps: blocks [0, nblk_c) of each row of the item
+                    assert nblk_c * bb <= cbytes
+                    if row0 == 0:
+                        seen[k0:k0 + nblk_c] += 1
+                    if typ in (S.GGML_F32, S.GGML_F16, S.GGML_BF16):
+                        words = nblk_c * bb // 16
+                        vpw = 4 if typ == S.GGML_F32 else 8
+                        assert (nblk_c * bb) % 16 == 0 and k0 * 32 + vpw * words <= nu * 32
+            assert np.all(seen == 1), (S.TYPE_NAMES[typ], rows, cols)

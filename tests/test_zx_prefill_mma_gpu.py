@@ -13,7 +13,7 @@ import oracle as O
 import synth as S
 from conftest import MATVEC_RTOL, MODEL_L2_RTOL, max_rel_err, rel_l2
 
-pytestmark = pytest.mark.gpu
+pytestmark = [pytest.mark.gpu, pytest.mark.newest]
 torch = pytest.importorskip("torch")
 
 
