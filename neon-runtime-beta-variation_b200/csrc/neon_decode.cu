@@ -479,10 +479,13 @@ constexpr int kAttnMaxGroup = 8;  // query heads per KV head in the decode atten
 // Decode attention in one launch: a thread-block cluster of cs CTAs (8, or 16
 // for long contexts) per KV head. CTA r of the cluster takes positions
 // [r*chunk, (r+1)*chunk) of the L = *d_pos + 1 cache rows. Its K rows, then its
-// V rows, stream through a two-slot shared-memory ring (cp.async.bulk, one row
+// V rows, stream through a ring of shared-memory slots (cp.async.bulk, one row
 // per copy, rows padded by 64 bytes so the four threads scoring a row read
-// conflict-free quarters) in sub-chunks of kAttnSub rows: the copy of the next
-// sub-chunk is in flight while the current one is used. Scores for the head's
+// conflict-free quarters) in sub-chunks of kAttnSub rows: as many slots as the
+// CTA's sub-chunks need while every cluster of the launch stays resident at
+// once (attn_pick_slots), so at the contexts the configurations use every K
+// and V row of a CTA is in flight together; a slot is refilled as soon as its
+// rows are used. Scores for the head's
 // query group go to shared memory; the CTAs exchange their maxima through
 // distributed shared memory, so every CTA forms p_s = fast_expf(score_s - max
 // over ALL positions) exactly as transformer_forward does (:1123-1137); each
@@ -490,7 +493,9 @@ constexpr int kAttnMaxGroup = 8;  // query heads per KV head in the decode atten
 // order: out = (sum p v) / (sum p).
 // ---------------------------------------------------------------------------
 constexpr int kAttnMaxCluster = 16;
-constexpr int kAttnSub = 64;  // cache rows per ring slot
+constexpr int kAttnSub = 64;            // cache rows per ring slot
+constexpr int kAttnMaxSlots = 8;
+constexpr int kAttnSmemMax = 200 * 1024;  // dynamic shared memory a slot count may take
 
 __device__ __forceinline__ uint32_t smem_addr_d(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -514,10 +519,10 @@ __device__ __forceinline__ bool mbar_wait_d(uint64_t* bar, uint32_t parity, unsi
     }
 }
 
-struct AttnSmem {  // offsets (floats) into the dynamic shared memory
-    int q, sc, ring, co, csum, cmax, bar, total;
+struct AttnSmem {  // offsets (floats) into the dynamic shared memory; slots: ring depth
+    int q, sc, ring, co, csum, cmax, bar, total, slots;
 };
-__host__ __device__ inline AttnSmem attn_smem_layout(int group, int hd, int chunk_max, int cs) {
+__host__ __device__ inline AttnSmem attn_smem_layout(int group, int hd, int chunk_max, int cs, int slots) {
     auto up4 = [](int v) { return (v + 3) & ~3; };  // float4-aligned regions
     auto mx = [](int a, int b) { return a > b ? a : b; };
     const int pitch = hd + 16;
@@ -526,38 +531,40 @@ __host__ __device__ inline AttnSmem attn_smem_layout(int group, int hd, int chun
     l.q = 0;
     l.sc = up4(l.q + group * hd);
     l.ring = up4(l.sc + group * chunk_max);
+    l.slots = slots;
     // once the V rows are used, the ring holds the per-part partial sums, and
     // then (in CTA 0) the cluster's partials
-    const int ring = mx(2 * kAttnSub * pitch, mx(parts * group * hd, cs * group * hd));
+    const int ring = mx(slots * kAttnSub * pitch, mx(parts * group * hd, cs * group * hd));
     l.co = l.ring;
     l.csum = up4(l.ring + ring);
     l.cmax = up4(l.csum + cs * kAttnMaxGroup);
     l.bar = up4(l.cmax + cs * kAttnMaxGroup);
-    l.total = l.bar + 4 * 2;  // two 8-byte mbarriers
+    l.total = l.bar + 2 * slots;  // 8-byte mbarriers
     return l;
 }
 
 __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const float* __restrict__ q, const float* __restrict__ Kc,
                                                                const float* __restrict__ Vc, const int* __restrict__ d_pos,
                                                                int kv_dim, int hd, int group, float scale, int chunk_max,
-                                                               float* __restrict__ out, unsigned int* err) {
+                                                               int slots, float* __restrict__ out, unsigned int* err) {
     namespace cg = cooperative_groups;
     extern __shared__ __align__(16) float sm[];
     cg::cluster_group cl = cg::this_cluster();
     const int rank = (int)cl.block_rank(), cs = (int)cl.num_blocks();
     const int kvh = blockIdx.x / cs;
-    const AttnSmem lay = attn_smem_layout(group, hd, chunk_max, cs);
+    const AttnSmem lay = attn_smem_layout(group, hd, chunk_max, cs, slots);
     float* qs = sm + lay.q;
     float* sc = sm + lay.sc;     // [group][chunk_max]
-    float* ring = sm + lay.ring; // [2][kAttnSub][hd + 4]; later [parts][group][hd]
+    float* ring = sm + lay.ring; // [slots][kAttnSub][hd + 16]; later [parts][group][hd]
     float* co = sm + lay.co;     // [cluster][group][hd]   (CTA 0; overlays the ring)
     float* csum = sm + lay.csum; // [cluster][kAttnMaxGroup] (read in CTA 0)
     float* cmax = sm + lay.cmax; // [cluster][kAttnMaxGroup]
     uint64_t* full = reinterpret_cast<uint64_t*>(sm + lay.bar);
     __shared__ float gm[kAttnMaxGroup];
     const int pitch = hd + 16;
+    const int S = slots;
     if (threadIdx.x == 0) {
-        for (int i = 0; i < 2; ++i)
+        for (int i = 0; i < S; ++i)
             asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr_d(&full[i])) : "memory");
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -572,7 +579,7 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const float* __re
     const int nd4 = hd / 4;
     // item t < n_sub: K rows of sub-chunk t; n_sub <= t < 2 n_sub: V rows of sub-chunk t - n_sub
     auto issue = [&](int t) {
-        const int slot = t & 1;
+        const int slot = t % S;
         const bool is_v = t >= n_sub;
         const int sub = is_v ? t - n_sub : t;
         const int j0 = sub * kAttnSub, rows = min(kAttnSub, len - j0);
@@ -592,14 +599,14 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const float* __re
     };
     const int n_items = 2 * n_sub;
     if (warp == 0)
-        for (int t = 0; t < min(2, n_items); ++t) issue(t);
+        for (int t = 0; t < min(S, n_items); ++t) issue(t);
     for (int i = threadIdx.x; i < group * hd; i += blockDim.x) qs[i] = q[(long long)kvh * group * hd + i];
     __syncthreads();
     bool ok = true;
     // pass 1: scores, a thread per cache row of the slot
     for (int t = 0; t < n_sub; ++t) {
-        ok = ok && mbar_wait_d(&full[t & 1], (uint32_t)((t >> 1) & 1), err);
-        const float* rows_k = ring + (t & 1) * kAttnSub * pitch;
+        ok = ok && mbar_wait_d(&full[t % S], (uint32_t)((t / S) & 1), err);
+        const float* rows_k = ring + (t % S) * kAttnSub * pitch;
         const int j0 = t * kAttnSub, rows = min(kAttnSub, len - j0);
         {
             // four threads per row (lanes 4r'..4r'+3 of a warp), thread q4i takes float4
@@ -636,9 +643,9 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const float* __re
             }
         }
         __syncthreads();  // the slot is free
-        if (warp == 0 && t + 2 < n_items) {
+        if (warp == 0 && t + S < n_items) {
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            issue(t + 2);
+            issue(t + S);
         }
     }
     // this CTA's max per query head (warp gq), published to every CTA of the cluster
@@ -674,8 +681,8 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const float* __re
 #pragma unroll
     for (int gq = 0; gq < kAttnMaxGroup; ++gq) acc[gq] = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int t = n_sub; t < n_items; ++t) {
-        ok = ok && mbar_wait_d(&full[t & 1], (uint32_t)((t >> 1) & 1), err);
-        const float* rows_v = ring + (t & 1) * kAttnSub * pitch;
+        ok = ok && mbar_wait_d(&full[t % S], (uint32_t)((t / S) & 1), err);
+        const float* rows_v = ring + (t % S) * kAttnSub * pitch;
         const int j0 = (t - n_sub) * kAttnSub, rows = min(kAttnSub, len - j0);
         if (part < parts) {
             for (int r = part; r < rows; r += parts) {
@@ -693,9 +700,9 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const float* __re
             }
         }
         __syncthreads();
-        if (warp == 0 && t + 2 < n_items) {
+        if (warp == 0 && t + S < n_items) {
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            issue(t + 2);
+            issue(t + S);
         }
     }
     (void)ok;  // a timed-out copy sets bit 2 of the error word; the results are then not used
@@ -866,6 +873,7 @@ struct neon_model {
     float* shift_scratch = nullptr;  // ctx_len x kv_dim, for neon_cuda_model_kv_shift
     float2* shift_cs = nullptr;      // rope_half (cos, sin) of the shift angle
     int att_cs = 8;                  // CTAs per KV head in the decode attention (a cluster)
+    int att_slots = 2;               // its ring depth (attn_pick_slots)
     float* logits_full = nullptr;    // all-gathered logits (tensor parallel only)
     neon_tensor_t embd = nullptr, output = nullptr;
     float* output_norm = nullptr;
@@ -993,9 +1001,41 @@ int launch_embed(neon_model* m, const int* toks, int seq) {
 
 // Dynamic shared memory of attn_decode_kernel.
 int attn_chunk_max(const neon_model* m) { return (int)((m->cfg.ctx_len + m->att_cs - 1) / m->att_cs); }
-size_t attn_decode_smem(const neon_model* m) {
+size_t attn_decode_smem(const neon_model* m, int slots) {
     const int group = (int)(m->cfg.n_head / m->cfg.n_kv_head);
-    return sizeof(float) * (size_t)attn_smem_layout(group, (int)m->cfg.head_dim, attn_chunk_max(m), m->att_cs).total;
+    return sizeof(float) *
+           (size_t)attn_smem_layout(group, (int)m->cfg.head_dim, attn_chunk_max(m), m->att_cs, slots).total;
+}
+size_t attn_decode_smem(const neon_model* m) { return attn_decode_smem(m, m->att_slots); }
+
+// The ring depth of attn_decode_kernel: a slot per K and V sub-chunk of the
+// longest share (at most kAttnMaxSlots), cut while it would take more than
+// kAttnSmemMax or leave a cluster of the launch waiting for another to finish;
+// never below two (the next sub-chunk in flight while one is used).
+int attn_pick_slots(const neon_model* m) {
+    const int items = 2 * ((attn_chunk_max(m) + kAttnSub - 1) / kAttnSub);
+    for (int slots = std::min(kAttnMaxSlots, items); slots > 2; --slots) {
+        const size_t smem = attn_decode_smem(m, slots);
+        if (smem > (size_t)kAttnSmemMax) continue;
+        cudaLaunchConfig_t q = {};
+        q.gridDim = dim3((unsigned)(m->n_kv_l * m->att_cs));
+        q.blockDim = dim3(kThreads);
+        q.dynamicSmemBytes = smem;
+        cudaLaunchAttribute qa[1];
+        qa[0].id = cudaLaunchAttributeClusterDimension;
+        qa[0].val.clusterDim.x = (unsigned)m->att_cs;
+        qa[0].val.clusterDim.y = 1;
+        qa[0].val.clusterDim.z = 1;
+        q.attrs = qa;
+        q.numAttrs = 1;
+        int clusters = 0;
+        if (cudaOccupancyMaxActiveClusters(&clusters, attn_decode_kernel, &q) != cudaSuccess) {
+            cudaGetLastError();
+            continue;
+        }
+        if (clusters >= (int)m->n_kv_l) return slots;
+    }
+    return 2;
 }
 
 // attn_decode_kernel: one cluster of att_cs CTAs per KV head, PDL when enabled.
@@ -1023,7 +1063,7 @@ int launch_attn_decode(neon_model* m, const float* Kl, const float* Vl) {
     const float scale = 1.0f / std::sqrt((float)c.head_dim);
     cudaError_t e = cudaLaunchKernelEx(&cfg, attn_decode_kernel, (const float*)m->q, Kl, Vl, (const int*)m->d_pos,
                                        (int)m->kv_dim, (int)c.head_dim, (int)(c.n_head / c.n_kv_head), scale,
-                                       attn_chunk_max(m), m->att, m->d_err);
+                                       attn_chunk_max(m), m->att_slots, m->att, m->d_err);
     if (e != cudaSuccess) return cuda_error(e, "attn_decode_kernel");
     return neon_internal::launched(1);
 }
@@ -1390,7 +1430,7 @@ int neon_cuda_model_create_tp(const neon_model_config_t* cfg, neon_comm_t comm, 
             q.numAttrs = 1;
             int clusters = 0;
             if (q.dynamicSmemBytes > 48 * 1024)
-                cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)q.dynamicSmemBytes);
+                cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
             if (attn_decode_smem(m) > 220 * 1024 ||
                 cudaOccupancyMaxActiveClusters(&clusters, attn_decode_kernel, &q) != cudaSuccess || clusters < 1) {
                 cudaGetLastError();
@@ -1398,12 +1438,15 @@ int neon_cuda_model_create_tp(const neon_model_config_t* cfg, neon_comm_t comm, 
             }
         }
     }
-    if (!rc && attn_decode_smem(m) > 48 * 1024) {
-        if (attn_decode_smem(m) > 220 * 1024)
-            rc = error(NEON_ERR_UNSUPPORTED, "decode attention: ctx_len too large for one cluster per KV head");
-        else if (cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)attn_decode_smem(m)) != cudaSuccess)
+    if (!rc && attn_decode_smem(m) > 220 * 1024)
+        rc = error(NEON_ERR_UNSUPPORTED, "decode attention: ctx_len too large for one cluster per KV head");
+    if (!rc) {
+        // the process-wide limit at its largest, so that no later model lowers it under an earlier one's
+        if (cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024) !=
+            cudaSuccess)
             rc = error(NEON_ERR_CUDA, "cudaFuncSetAttribute(attn_decode_kernel)");
+        else
+            m->att_slots = attn_pick_slots(m);
     }
     if (!rc && c.ctx_len * sizeof(float) > 48 * 1024) {
         if (cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(c.ctx_len * sizeof(float))) != cudaSuccess)
