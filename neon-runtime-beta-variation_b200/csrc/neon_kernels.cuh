@@ -86,6 +86,10 @@ __device__ __forceinline__ uint4 ld_weights_u4(const void* p) {
     return v;
 }
 
+// Fetch the line holding p into L1 (no register is written): a load of it
+// later in the kernel then hits L1 instead of paying an L2 round trip.
+__device__ __forceinline__ void prefetch_l1(const void* p) { asm volatile("prefetch.global.L1 [%0];" ::"l"(p)); }
+
 __device__ __forceinline__ uint16_t ld_weights_u16(const void* p) {
     uint16_t v;
     asm("ld.global.nc.L1::no_allocate.u16 %0, [%1];" : "=h"(v) : "l"(p));
@@ -558,6 +562,8 @@ __device__ __forceinline__ void stage_x_q8_norm(const float* __restrict__ x, int
     const long long e0 = (long long)b * 32 + part * EPT;
     float xv[EPT];
     load_x_part<TPB>(x, x_vec, act, b, part, xv);
+    // the norm weights never change: fetched into L1 with X's loads, not after the reduction
+    if (act) prefetch_l1(norm_w + e0);
     double ss = 0.0;
 #pragma unroll
     for (int j = 0; j < EPT; ++j) ss = fma((double)xv[j], (double)xv[j], ss);
@@ -786,11 +792,14 @@ __global__ void __launch_bounds__(kStreamBlock) matvec_stream_kernel(const __gri
     const unsigned int peer_call =
         a.peer_mode ? *reinterpret_cast<volatile const unsigned int*>(a.peer.calls) + 1u : 0u;
 
-    // the token's position and its RoPE row, read once per launch
+    // the token's position and its RoPE row, read once per launch; the row
+    // (rope_half <= kMaxRopeHalf <= kStreamThreads entries, one per thread) is
+    // fetched into L1 alongside X's loads and copied to shared memory after
+    // the X staging
     __shared__ float2 rcs[kMaxRopeHalf];
+    static_assert(kMaxRopeHalf <= kStreamThreads, "one RoPE entry per thread");
     const int pos = a.d_pos ? *a.d_pos : 0;
-    if (a.rope_cs)
-        for (int i = threadIdx.x; i < a.rope_half; i += kStreamThreads) rcs[i] = a.rope_cs[(long long)pos * a.rope_half + i];
+    if (a.rope_cs && (int)threadIdx.x < a.rope_half) prefetch_l1(a.rope_cs + (long long)pos * a.rope_half + threadIdx.x);
 
     // Stage X once per CTA (normalised first when asked), then let the next
     // launch start.
@@ -814,6 +823,7 @@ __global__ void __launch_bounds__(kStreamBlock) matvec_stream_kernel(const __gri
             xs[(i >> 5) * kQ8Pitch + (i & 31)] = v;
         }
     }
+    if (a.rope_cs && (int)threadIdx.x < a.rope_half) rcs[threadIdx.x] = a.rope_cs[(long long)pos * a.rope_half + threadIdx.x];
     compute_sync();
     pdl_launch_dependents();
 
