@@ -21,11 +21,16 @@ for p in (os.path.join(ROOT, "oracle"), PKG, ROOT):
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA GPU (sm_100a, B200)")
     config.addinivalue_line("markers", "newest: a kernel variant behind an off-by-default switch; run after "
-                                       "every other test, so that with -x its failure stops nothing else")
+                                       "the other tests, so that with -x its failure stops none of them")
+    config.addinivalue_line("markers", "last: run after every other test, the newest included")
 
 
 def pytest_collection_modifyitems(config, items):
-    items.sort(key=lambda it: it.get_closest_marker("newest") is not None)  # stable: order kept otherwise
+    def rank(it):
+        if it.get_closest_marker("last") is not None:
+            return 2
+        return 1 if it.get_closest_marker("newest") is not None else 0
+    items.sort(key=rank)  # stable: the order is kept otherwise
 
 
 def load_golden(name):

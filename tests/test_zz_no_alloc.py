@@ -21,7 +21,7 @@ import neon_cuda as N
 import synth as S
 from conftest import MATVEC_RTOL, max_rel_err
 
-pytestmark = pytest.mark.gpu
+pytestmark = [pytest.mark.gpu, pytest.mark.last]
 
 torch = pytest.importorskip("torch")
 
