@@ -141,6 +141,9 @@ def parse_args():
     p.add_argument("--dq-ring", action="store_true",
                    help="one-position calls of the dequantising types on the bulk-copy ring kernel "
                         "(neon_cuda_set_dq_ring)")
+    p.add_argument("--launch-overlap", action="store_true",
+                   help="one-position Q4_0 / Q8_0 launches sized to leave room for the next launch's CTAs "
+                        "(neon_cuda_set_launch_overlap)")
     p.add_argument("--batch", type=int, default=1,
                    help="matvec workloads: positions per call; > 1 times the prefill path (one JSON line)")
     p.add_argument("--type-sweep", action="store_true",
@@ -412,6 +415,8 @@ def run_decode(args):
         N.set_prefill_mma(True)
     if getattr(args, "dq_ring", False):
         N.set_dq_ring(True)
+    if getattr(args, "launch_overlap", False):
+        N.set_launch_overlap(True)
     N.set_fused_collectives(not args.no_fused_collectives)
     comm = None
     barrier, max_over_ranks = (lambda: None), (lambda v: v)
@@ -567,6 +572,8 @@ def run_neon(args):
         N.set_prefill_mma(True)
     if getattr(args, "dq_ring", False):
         N.set_dq_ring(True)
+    if getattr(args, "launch_overlap", False):
+        N.set_launch_overlap(True)
     dev = torch.device("cuda", local)
 
     host_w = host_rotation(rank, ROTATION)
@@ -706,6 +713,8 @@ def run_neon(args):
             "dtype": compute_dtype(TYPE),
             "data": "synthetic",
             "config": {**workload_config(), "parallelism": f"dp{world} (independent rotations)",
+                       "variants": [v for v, on in (("launch_overlap", args.launch_overlap), ("dq_ring", args.dq_ring),
+                                                    ("prefill_mma", args.prefill_mma)) if on],
                        "launch": "CUDA graph of 1024 PDL launches per step"},
             "e2e": {"value": round(e2e_value, 2), "unit": UNIT,
                     "h2d_bytes_per_step": CALLS_PER_STEP * COLS * 4,

@@ -354,6 +354,13 @@ NEON_API int neon_cuda_set_prefill_mma(int enabled);
  * until a GPU run has validated it; the switch is process-wide. */
 NEON_API int neon_cuda_set_dq_ring(int enabled);
 
+/* Size one-position Q4_0 / Q8_0 launches to half the CTAs an SM holds, so the
+ * next launch on the stream finds room on every SM and streams its weights
+ * (before its dependency wait) while this one runs, instead of after this
+ * one's CTAs leave. Results are unchanged (only the grid and ring depth
+ * change). Off by default until a GPU run has measured it; process-wide. */
+NEON_API int neon_cuda_set_launch_overlap(int enabled);
+
 /* Launch option: programmatic dependent launch (PDL) lets a matvec fetch its
  * weights while the previous kernel on the stream finishes; on by default. */
 NEON_API int neon_cuda_set_pdl(int enabled);

@@ -99,6 +99,7 @@ C_ENTRY_POINTS = (
     "neon_cuda_set_pdl",
     "neon_cuda_set_prefill_mma",
     "neon_cuda_set_dq_ring",
+    "neon_cuda_set_launch_overlap",
 )
 
 _sz = C.c_size_t
@@ -162,6 +163,7 @@ def load(path: str | None = None) -> C.CDLL:
         L.neon_cuda_set_pdl.argtypes = [C.c_int]
         L.neon_cuda_set_prefill_mma.argtypes = [C.c_int]
         L.neon_cuda_set_dq_ring.argtypes = [C.c_int]
+        L.neon_cuda_set_launch_overlap.argtypes = [C.c_int]
         L.neon_cuda_matvec_q4_0_noalloc.argtypes = [_vp, _vp, _sz, _vp, _sz, _sz, _vp]
         L.neon_cuda_model_create.argtypes = [C.POINTER(_ModelConfig), C.POINTER(_vp)]
         L.neon_cuda_model_set_tensor.argtypes = [_vp, C.c_int, C.c_int, _vp, _sz, C.c_int, _sz, _sz]
@@ -220,6 +222,13 @@ def set_dq_ring(enabled: bool) -> None:
     kernel (several row tiles in flight per CTA) instead of the register-buffer
     kernel; process-wide, off by default."""
     _check(load().neon_cuda_set_dq_ring(1 if enabled else 0))
+
+
+def set_launch_overlap(enabled: bool) -> None:
+    """One-position Q4_0 / Q8_0 launches sized to half the CTAs an SM holds, so
+    the next launch's CTAs stream their weights while this one runs;
+    process-wide, off by default."""
+    _check(load().neon_cuda_set_launch_overlap(1 if enabled else 0))
 
 
 def set_pdl(enabled: bool) -> None:
