@@ -144,6 +144,9 @@ def parse_args():
     p.add_argument("--launch-overlap", action="store_true",
                    help="one-position Q4_0 / Q8_0 launches sized to leave room for the next launch's CTAs "
                         "(neon_cuda_set_launch_overlap)")
+    p.add_argument("--decode-chain", action="store_true",
+                   help="decode steps with the projections between attention launches as one launch "
+                        "(neon_cuda_set_decode_chain)")
     p.add_argument("--batch", type=int, default=1,
                    help="matvec workloads: positions per call; > 1 times the prefill path (one JSON line)")
     p.add_argument("--type-sweep", action="store_true",
@@ -417,6 +420,8 @@ def run_decode(args):
         N.set_dq_ring(True)
     if getattr(args, "launch_overlap", False):
         N.set_launch_overlap(True)
+    if getattr(args, "decode_chain", False):
+        N.set_decode_chain(True)
     N.set_fused_collectives(not args.no_fused_collectives)
     comm = None
     barrier, max_over_ranks = (lambda: None), (lambda v: v)
@@ -447,7 +452,10 @@ def run_decode(args):
         line = {"metric": DECODE_METRIC, "value": res["tokens_per_s"], "unit": "tokens/s", "n_gpus": world,
                 "steps": res["generated"], "warmup": 0, "ms_per_step": res["ms_per_token"], "higher_is_better": True,
                 "scaling": "strong", "vs_baseline": None, "dtype": "int8/fp32 (q4_0 x q8_0 dp4a, fp32 scales)",
-                "data": "synthetic", "config": {"workload": res["workload"], "parallelism": res["parallelism"]},
+                "data": "synthetic", "config": {"workload": res["workload"], "parallelism": res["parallelism"],
+                                                "variants": [v for v, on in (("launch_overlap", args.launch_overlap),
+                                                                             ("decode_chain", args.decode_chain),
+                                                                             ("prefill_mma", args.prefill_mma)) if on]},
                 "e2e": {"value": res["e2e_tokens_per_s"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 4, "api": res["e2e"]},
                 "load_s": res["load_s"], "roofline": decode_roofline(dict(res), cfg, world)["hbm"],
@@ -574,6 +582,8 @@ def run_neon(args):
         N.set_dq_ring(True)
     if getattr(args, "launch_overlap", False):
         N.set_launch_overlap(True)
+    if getattr(args, "decode_chain", False):
+        N.set_decode_chain(True)
     dev = torch.device("cuda", local)
 
     host_w = host_rotation(rank, ROTATION)
@@ -714,7 +724,8 @@ def run_neon(args):
             "data": "synthetic",
             "config": {**workload_config(), "parallelism": f"dp{world} (independent rotations)",
                        "variants": [v for v, on in (("launch_overlap", args.launch_overlap), ("dq_ring", args.dq_ring),
-                                                    ("prefill_mma", args.prefill_mma)) if on],
+                                                    ("prefill_mma", args.prefill_mma),
+                                                    ("decode_chain", args.decode_chain)) if on],
                        "launch": "CUDA graph of 1024 PDL launches per step"},
             "e2e": {"value": round(e2e_value, 2), "unit": UNIT,
                     "h2d_bytes_per_step": CALLS_PER_STEP * COLS * 4,

@@ -6,6 +6,7 @@
 #include "neon_dequant.cuh"
 #include "neon_quant.cuh"
 #include "neon_prefill.cuh"
+#include "neon_chain.cuh"
 
 #include <cuda_runtime.h>
 
@@ -37,6 +38,7 @@ std::atomic<int> g_pdl{1};
 std::atomic<int> g_prefill_mma{0};  // neon_cuda_set_prefill_mma
 std::atomic<int> g_dq_ring{0};      // neon_cuda_set_dq_ring
 std::atomic<int> g_launch_overlap{0};  // neon_cuda_set_launch_overlap
+std::atomic<int> g_decode_chain{0};    // neon_cuda_set_decode_chain
 
 struct DeviceState {
     bool ready = false;
@@ -167,6 +169,7 @@ int init_device(int device) {
         for (int T : {1, 2, 4}) rc = rc ? rc : ensure_smem(dq_kernel(t, T), kMaxSmem);
     for (int t : kDqTypes)
         for (int rpw : {1, 2}) rc = rc ? rc : ensure_smem(dq_ring_kernel(t, rpw), kMaxSmem);
+    if (!rc) rc = ensure_smem(matvec_chain_kernel, kMaxSmem);
     if (rc) return rc;
     void* err = nullptr;
     NEON_CUDA_TRY(cudaGetSymbolAddress(&err, g_neon_device_err));
@@ -867,6 +870,104 @@ int launched(int n) {
 }
 bool pdl_enabled() { return g_pdl.load(std::memory_order_relaxed) != 0; }
 bool prefill_mma() { return g_prefill_mma.load(std::memory_order_relaxed) != 0; }
+bool decode_chain() { return g_decode_chain.load(std::memory_order_relaxed) != 0; }
+
+// Resident matvec_chain_kernel CTAs per SM at `smem` bytes (0: none fit).
+int chain_occupancy(int smem) {
+    static std::mutex mu;
+    static std::vector<std::pair<int, int>> cache;
+    std::lock_guard<std::mutex> lk(mu);
+    for (auto& kv : cache)
+        if (kv.first == smem) return kv.second;
+    int occ = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, matvec_chain_kernel, kStreamBlock, smem) != cudaSuccess) {
+        cudaGetLastError();
+        occ = 0;
+    }
+    cache.emplace_back(smem, occ);
+    return occ;
+}
+
+int matvec_chain(const ChainPhaseDesc* ph, int n, const int* d_pos, unsigned int* sync, cudaStream_t st) {
+    if (n < 1 || n > kChainMaxPhases || !sync) return set_err(NEON_ERR_UNSUPPORTED, "projection chain: 1-4 phases");
+    int device = 0;
+    int rc = current_device(&device);
+    if (rc) return rc;
+    DeviceState& ds = g_dev[device];
+    ChainArgs c;
+    std::memset(&c, 0, sizeof(c));
+    int slot = 0, xb = 0;
+    for (int p = 0; p < n; ++p) {
+        const ChainPhaseDesc& d = ph[p];
+        if (d.n < 1 || d.n > kChainMaxSpans || !d.t || !d.x)
+            return set_err(NEON_ERR_UNSUPPORTED, "projection chain: 1-3 targets per phase");
+        const size_t cols = d.t[0].W ? d.t[0].W->cols : 0;
+        size_t total_rows = 0;
+        for (int i = 0; i < d.n; ++i) {
+            const neon_tensor* W = d.t[i].W;
+            if (!W || W->type != NEON_GGML_Q4_0 || W->cols != cols || W->device != device || !d.t[i].Y)
+                return set_err(NEON_ERR_UNSUPPORTED, "projection chain: Q4_0 targets of one input dim on this device");
+            total_rows += W->rows;
+        }
+        const int nb = (int)(cols / 32);
+        const StreamPlan pl = plan_stream(NEON_GGML_Q4_0, nb, total_rows, ds.sms);
+        ChainPhase& P = c.ph[p];
+        int tiles = 0;
+        for (int i = 0; i < d.n; ++i) {
+            const neon_proj_target_t& tg = d.t[i];
+            Span& sp = P.span[i];
+            sp.qs = tg.W->qs;
+            sp.d = tg.W->d;
+            sp.y = tg.Y;
+            sp.y_stride = (long long)tg.y_stride;
+            sp.rows = (int)tg.W->rows;
+            sp.tile0 = tiles;
+            tiles += (int)((tg.W->rows + pl.rc - 1) / pl.rc);
+            sp.epi = d.ext.epi ? d.ext.epi[i] : kEpiStore;
+            sp.pos_stride = d.ext.pos_stride ? d.ext.pos_stride[i] : 0;
+        }
+        P.n_spans = d.n;
+        P.n_tiles = tiles;
+        P.x = d.x;
+        P.x_vec = (reinterpret_cast<uintptr_t>(d.x) % 16) == 0;
+        P.norm_w = d.ext.norm_w;
+        P.norm_eps = d.ext.norm_eps;
+        P.rope_cs = d.ext.rope_cs;
+        P.rope_half = d.ext.rope_half;
+        P.head_dim = d.ext.head_dim;
+        P.accumulate = d.accumulate;
+        P.nb = nb;
+        P.kc = pl.kc;
+        P.nch = pl.nch;
+        P.rc = pl.rc;
+        slot = std::max(slot, pl.stage_bytes);
+        xb = std::max(xb, stream_x_bytes(NEON_GGML_Q4_0, nb));
+    }
+    // the ring depth that keeps the most weight bytes in flight per SM; the
+    // grid is what the SMs hold at once (the barriers need every CTA resident)
+    int best_stages = 0, best_occ = 0;
+    long long best_bytes = -1;
+    for (int st_n = 1; st_n <= kChainMaxStages && xb + st_n * slot <= kMaxSmem; ++st_n) {
+        int occ = chain_occupancy(xb + st_n * slot);
+        if (occ < 1) continue;
+        occ = std::min(occ, kStreamCtasPerSm);
+        const long long inflight = (long long)occ * st_n * slot;
+        if (inflight >= best_bytes) {
+            best_bytes = inflight;
+            best_stages = st_n;
+            best_occ = occ;
+        }
+    }
+    if (best_stages < 1) return set_err(NEON_ERR_UNSUPPORTED, "projection chain: X and one ring slot exceed shared memory");
+    c.n_phases = n;
+    c.stages = best_stages;
+    c.slot_bytes = slot;
+    c.x_bytes = xb;
+    c.d_pos = d_pos;
+    c.err = ds.err;
+    c.sync = sync;
+    return launch_n(matvec_chain_kernel, dim3(ds.sms * best_occ), kStreamBlock, xb + best_stages * slot, st, c);
+}
 int device_sms(int device) {
     int rc = init_device(device);
     return rc ? -1 : g_dev[device].sms;
@@ -911,6 +1012,11 @@ int neon_cuda_set_dq_ring(int enabled) {
 
 int neon_cuda_set_launch_overlap(int enabled) {
     g_launch_overlap.store(enabled ? 1 : 0);
+    return NEON_OK;
+}
+
+int neon_cuda_set_decode_chain(int enabled) {
+    g_decode_chain.store(enabled ? 1 : 0);
     return NEON_OK;
 }
 

@@ -891,6 +891,7 @@ struct neon_model {
     float *gu = nullptr, *act = nullptr, *logits = nullptr;
     int *d_tokens = nullptr, *d_tok = nullptr, *d_pos = nullptr, *d_step = nullptr, *d_out = nullptr;
     unsigned* d_err = nullptr;
+    unsigned int* chain_sync = nullptr;    // the projection chain's barrier words (zero between launches)
     unsigned long long* am_key = nullptr;  // argmax scratch
     unsigned int* am_count = nullptr;
     size_t out_cap = 0;
@@ -1151,12 +1152,102 @@ int run_head(neon_model* m, const float* x) {
     return neon_internal::matvec(&t, 1, x, m->cfg.n_embd, 1, m->stream, 0, &ext);
 }
 
+// The projection chain (neon_cuda_set_decode_chain) takes a model whose
+// projections are all Q4_0, on one device.
+bool chain_applies(const neon_model* m) {
+    for (const auto& L : m->layers) {
+        for (auto* w : L.w)
+            if (!w || w->type != NEON_GGML_Q4_0) return false;
+        if (!L.gateup || L.gateup->type != NEON_GGML_Q4_0) return false;
+    }
+    return true;
+}
+
+// The decode step with the projection chain: layer 0's Q/K/V as its own
+// launch, then per layer the attention launch and ONE matvec_chain_kernel
+// launch for attn_output (+= h), gate/up (rms_norm folded, SwiGLU / SiLU),
+// ffn_down (+= h) and the next layer's Q/K/V (rms_norm folded, RoPE, cache
+// rows): the same arithmetic as run_step's launches, bit for bit.
+int run_step_chain(neon_model* m) {
+    const auto& c = m->cfg;
+    const size_t n_embd = c.n_embd, q_dim = m->q_dim, kv_dim = m->kv_dim, n_ff = m->n_ff_l;
+    float* hc = m->h;
+    const int qkv_epi[3] = {neon::kEpiRope, neon::kEpiRope, neon::kEpiAtPos};
+    const long long qkv_stride[3] = {0, (long long)kv_dim, (long long)kv_dim};
+    const int ffn_epi = c.plain_ffn ? neon::kEpiSilu : neon::kEpiSwiglu;
+    const long long zero_stride = 0;
+    auto qkv_ext = [&](uint32_t li) {
+        neon_internal::MatvecExt ext;
+        ext.norm_w = m->layers[li].attn_norm;
+        ext.norm_eps = c.norm_eps;
+        ext.d_pos = m->d_pos;
+        ext.rope_cs = m->rope_cs;
+        ext.rope_half = (int)m->rope_half;
+        ext.head_dim = (int)c.head_dim;
+        ext.epi = qkv_epi;
+        ext.pos_stride = qkv_stride;
+        return ext;
+    };
+    auto qkv_targets = [&](uint32_t li, neon_proj_target_t (&t)[3]) {
+        const auto& L = m->layers[li];
+        float* Kl = m->K + (size_t)li * c.ctx_len * kv_dim;
+        float* Vl = m->V + (size_t)li * c.ctx_len * kv_dim;
+        t[0] = {L.w[0], m->q, q_dim};
+        t[1] = {L.w[1], Kl, kv_dim};
+        t[2] = {L.w[2], Vl, kv_dim};
+    };
+    int rc = launch_embed(m, m->d_tok, 1);
+    if (!rc) {
+        neon_proj_target_t t[3];
+        qkv_targets(0, t);
+        const neon_internal::MatvecExt ext = qkv_ext(0);
+        rc = neon_internal::matvec(t, 3, hc, n_embd, 1, m->stream, 0, &ext);
+    }
+    for (uint32_t li = 0; li < c.n_layer && !rc; ++li) {
+        const auto& L = m->layers[li];
+        const float* Kl = m->K + (size_t)li * c.ctx_len * kv_dim;
+        const float* Vl = m->V + (size_t)li * c.ctx_len * kv_dim;
+        rc = launch_attn_decode(m, Kl, Vl);
+        if (rc) break;
+        const neon_proj_target_t t_out{L.w[3], hc, n_embd}, t_gu{L.gateup, m->act, n_ff}, t_down{L.w[4], hc, n_embd};
+        neon_proj_target_t t_qkv[3];
+        neon_internal::ChainPhaseDesc ph[4];
+        ph[0].t = &t_out;
+        ph[0].n = 1;
+        ph[0].x = m->att;
+        ph[0].accumulate = 1;
+        ph[1].t = &t_gu;
+        ph[1].n = 1;
+        ph[1].x = hc;
+        ph[1].ext.norm_w = L.ffn_norm;
+        ph[1].ext.norm_eps = c.norm_eps;
+        ph[1].ext.epi = &ffn_epi;
+        ph[1].ext.pos_stride = &zero_stride;
+        ph[2].t = &t_down;
+        ph[2].n = 1;
+        ph[2].x = m->act;
+        ph[2].accumulate = 1;
+        int n = 3;
+        if (li + 1 < c.n_layer) {
+            qkv_targets(li + 1, t_qkv);
+            ph[3].t = t_qkv;
+            ph[3].n = 3;
+            ph[3].x = hc;
+            ph[3].ext = qkv_ext(li + 1);
+            n = 4;
+        }
+        rc = neon_internal::matvec_chain(ph, n, m->d_pos, m->chain_sync, m->stream);
+    }
+    return rc;
+}
+
 // One decode position (token in *d_tok, position *d_pos): the fused step.
 //
 // Tensor parallel with fused collectives: attn_output and ffn_down store their
 // partial rows as LL words straight into every rank's slot, and a small
 // reduce launch adds the ranks' rows into the residual.
 int run_step(neon_model* m) {
+    if (m->world == 1 && neon_internal::decode_chain() && chain_applies(m)) return run_step_chain(m);
     const auto& c = m->cfg;
     int rc = launch_embed(m, m->d_tok, 1);
     const size_t n_embd = c.n_embd, q_dim = m->q_dim, kv_dim = m->kv_dim, n_ff = m->n_ff_l;
@@ -1258,7 +1349,10 @@ int sync_and_check(neon_model* m) {
         const int rc = neon_cuda_comm_check(static_cast<neon_comm*>(m->comm));
         if (rc) return rc;
     }
-    return neon_internal::check_device_error(m->device);
+    const int rc = neon_internal::check_device_error(m->device);
+    // a launch that gave up waiting leaves the chain's barrier words set
+    if (rc && m->chain_sync) cudaMemset(m->chain_sync, 0, 4 * sizeof(unsigned int));
+    return rc;
 }
 
 // Tokens [0, n) of `tokens_dev` at positions length..; logits of the last.
@@ -1387,6 +1481,7 @@ int neon_cuda_model_create_tp(const neon_model_config_t* cfg, neon_comm_t comm, 
     A((void**)&m->d_pos, sizeof(int));
     A((void**)&m->d_step, sizeof(int));
     A((void**)&m->d_err, sizeof(unsigned));
+    A((void**)&m->chain_sync, 4 * sizeof(unsigned int));
     if (!rc) rc = cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) == cudaSuccess ? NEON_OK : error(NEON_ERR_CUDA, "cudaStreamCreate");
     if (!rc) rc = (cudaEventCreate(&m->ev0) == cudaSuccess && cudaEventCreate(&m->ev1) == cudaSuccess &&
                    cudaEventCreate(&m->evf0) == cudaSuccess && cudaEventCreate(&m->evf1) == cudaSuccess)
@@ -1409,6 +1504,7 @@ int neon_cuda_model_create_tp(const neon_model_config_t* cfg, neon_comm_t comm, 
             cudaMemset(m->d_err, 0, sizeof(unsigned)) != cudaSuccess || cudaMemset(m->K, 0, kv_bytes) != cudaSuccess ||
             cudaMemset(m->am_key, 0, sizeof(unsigned long long)) != cudaSuccess ||
             cudaMemset(m->am_count, 0, sizeof(unsigned int)) != cudaSuccess ||
+            cudaMemset(m->chain_sync, 0, 4 * sizeof(unsigned int)) != cudaSuccess ||
             cudaMemset(m->V, 0, kv_bytes) != cudaSuccess)
             rc = error(NEON_ERR_CUDA, "model initialisation copies failed");
     }

@@ -144,6 +144,24 @@ struct MatvecExt {
 // neon_cuda_matvec_multi on `st`, with y += result when `accumulate`.
 int matvec(const neon_proj_target_t* targets, size_t n, const float* dX, size_t x_stride, size_t seq,
            cudaStream_t st, int accumulate, const MatvecExt* ext = nullptr);
+
+// One phase of a decode projection chain (matvec_chain): one position of Q4_0
+// targets sharing their input dim, X, the accumulate flag and the epilogue
+// options of `ext` (its d_pos and peer fields are not used).
+struct ChainPhaseDesc {
+    const neon_proj_target_t* t = nullptr;
+    int n = 0;
+    const float* x = nullptr;
+    int accumulate = 0;
+    MatvecExt ext{};
+};
+// The phases as one launch of matvec_chain_kernel (grid barriers between
+// them; `sync`: three zeroed device words the launch leaves zeroed).
+// NEON_ERR_UNSUPPORTED, with nothing launched, when a phase does not fit it
+// (a type other than Q4_0, more than 3 targets, more than 4 phases, X too
+// large for shared memory).
+int matvec_chain(const ChainPhaseDesc* phases, int n, const int* d_pos, unsigned int* sync, cudaStream_t st);
+bool decode_chain();  // neon_cuda_set_decode_chain
 int error(int code, const std::string& msg);
 // Bytes of one GGUF row of `type` with `cols` values (0: unsupported type, or
 // cols not a multiple of the type's block size). rawllm_loader.hpp:367-386.

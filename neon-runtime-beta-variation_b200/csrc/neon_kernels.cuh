@@ -437,13 +437,28 @@ __host__ __device__ constexpr int stream_x_bytes(int type, int nb) {
     return ((type == 2 ? nb * kQ4Rec : nb * kQ8Pitch * 4) + 127) & ~127;
 }
 
+// X loads of the staging functions: read-only through the non-coherent path
+// (X was written by an earlier kernel), or with CG through L2 only, for X
+// written earlier in the same launch by other CTAs (matvec_chain_kernel).
+template <bool CG>
+__device__ __forceinline__ float ld_x(const float* p) {
+    if constexpr (CG) return __ldcg(p);
+    else return __ldg(p);
+}
+template <bool CG>
+__device__ __forceinline__ float4 ld_x4(const float4* p) {
+    if constexpr (CG) return __ldcg(p);
+    else return __ldg(p);
+}
+
 // rms_norm's scale 1/sqrt(mean(x^2) + eps) of n floats (fwd::rms_norm,
 // rawllm_forward.hpp:730-735): a double sum of squares over the whole CTA,
 // so every CTA of the launch derives the same scale.
+template <bool CG = false>
 __device__ __forceinline__ float cta_rms_scale(const float* __restrict__ x, int n, float eps, double* scratch) {
     double ss = 0.0;
     for (int i = threadIdx.x; i < n; i += kStreamThreads) {
-        const double v = (double)__ldg(x + i);
+        const double v = (double)ld_x<CG>(x + i);
         ss = fma(v, v, ss);
     }
 #pragma unroll
@@ -502,7 +517,7 @@ __device__ __forceinline__ void quantize_store_q8(float (&xv)[32 / TPB], bool ac
 }
 
 // The EPT elements of X thread `part` of block b holds.
-template <int TPB>
+template <int TPB, bool CG = false>
 __device__ __forceinline__ void load_x_part(const float* __restrict__ x, bool x_vec, bool act, int b, int part,
                                             float (&xv)[32 / TPB]) {
     constexpr int EPT = 32 / TPB;
@@ -510,12 +525,12 @@ __device__ __forceinline__ void load_x_part(const float* __restrict__ x, bool x_
     if (act && x_vec) {
 #pragma unroll
         for (int k = 0; k < EPT / 4; ++k) {
-            const float4 v = __ldg(reinterpret_cast<const float4*>(x + e0) + k);
+            const float4 v = ld_x4<CG>(reinterpret_cast<const float4*>(x + e0) + k);
             xv[4 * k] = v.x; xv[4 * k + 1] = v.y; xv[4 * k + 2] = v.z; xv[4 * k + 3] = v.w;
         }
     } else if (act) {
 #pragma unroll
-        for (int j = 0; j < EPT; ++j) xv[j] = __ldg(x + e0 + j);
+        for (int j = 0; j < EPT; ++j) xv[j] = ld_x<CG>(x + e0 + j);
     } else {
 #pragma unroll
         for (int j = 0; j < EPT; ++j) xv[j] = 0.f;
@@ -527,7 +542,7 @@ __device__ __forceinline__ void load_x_part(const float* __restrict__ x, bool x_
 // threads of one block are always all active or all idle.
 // With norm_w, each element is first replaced by (x * scale) * w, rms_norm's
 // output (the reference multiplies in that order).
-template <int TPB>
+template <int TPB, bool CG = false>
 __device__ __forceinline__ void stage_x_q8(const float* __restrict__ x, int nb, bool x_vec, unsigned char* rec,
                                            const float* __restrict__ norm_w, float scale) {
     constexpr int EPT = 32 / TPB;
@@ -538,7 +553,7 @@ __device__ __forceinline__ void stage_x_q8(const float* __restrict__ x, int nb, 
         const bool act = i < n;
         const int b = act ? i / TPB : 0, part = i % TPB;
         float xv[EPT];
-        load_x_part<TPB>(x, x_vec, act, b, part, xv);
+        load_x_part<TPB, CG>(x, x_vec, act, b, part, xv);
         if (norm_w && act) {
             const float* wb = norm_w + (long long)b * 32 + part * EPT;
 #pragma unroll
@@ -552,7 +567,7 @@ __device__ __forceinline__ void stage_x_q8(const float* __restrict__ x, int nb, 
 // cover X once (nb * TPB <= kStreamThreads): every thread loads its elements,
 // the CTA reduces the double sum of squares, and the same registers are
 // scaled, multiplied by the norm weight and quantised.
-template <int TPB>
+template <int TPB, bool CG = false>
 __device__ __forceinline__ void stage_x_q8_norm(const float* __restrict__ x, int nb, bool x_vec, unsigned char* rec,
                                                 const float* __restrict__ norm_w, float eps, double* scratch) {
     constexpr int EPT = 32 / TPB;
@@ -561,7 +576,7 @@ __device__ __forceinline__ void stage_x_q8_norm(const float* __restrict__ x, int
     const int b = act ? i / TPB : 0, part = i % TPB;
     const long long e0 = (long long)b * 32 + part * EPT;
     float xv[EPT];
-    load_x_part<TPB>(x, x_vec, act, b, part, xv);
+    load_x_part<TPB, CG>(x, x_vec, act, b, part, xv);
     // the norm weights never change: fetched into L1 with X's loads, not after the reduction
     if (act) prefetch_l1(norm_w + e0);
     double ss = 0.0;

@@ -100,6 +100,7 @@ C_ENTRY_POINTS = (
     "neon_cuda_set_prefill_mma",
     "neon_cuda_set_dq_ring",
     "neon_cuda_set_launch_overlap",
+    "neon_cuda_set_decode_chain",
 )
 
 _sz = C.c_size_t
@@ -164,6 +165,7 @@ def load(path: str | None = None) -> C.CDLL:
         L.neon_cuda_set_prefill_mma.argtypes = [C.c_int]
         L.neon_cuda_set_dq_ring.argtypes = [C.c_int]
         L.neon_cuda_set_launch_overlap.argtypes = [C.c_int]
+        L.neon_cuda_set_decode_chain.argtypes = [C.c_int]
         L.neon_cuda_matvec_q4_0_noalloc.argtypes = [_vp, _vp, _sz, _vp, _sz, _sz, _vp]
         L.neon_cuda_model_create.argtypes = [C.POINTER(_ModelConfig), C.POINTER(_vp)]
         L.neon_cuda_model_set_tensor.argtypes = [_vp, C.c_int, C.c_int, _vp, _sz, C.c_int, _sz, _sz]
@@ -229,6 +231,13 @@ def set_launch_overlap(enabled: bool) -> None:
     the next launch's CTAs stream their weights while this one runs;
     process-wide, off by default."""
     _check(load().neon_cuda_set_launch_overlap(1 if enabled else 0))
+
+
+def set_decode_chain(enabled: bool) -> None:
+    """Decode steps of one-device Q4_0 models with the projections between two
+    attention launches as one launch (grid barriers between them); read when a
+    model captures its step; process-wide, off by default."""
+    _check(load().neon_cuda_set_decode_chain(1 if enabled else 0))
 
 
 def set_pdl(enabled: bool) -> None:
