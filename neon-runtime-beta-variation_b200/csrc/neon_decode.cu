@@ -1237,6 +1237,16 @@ int run_step_chain(neon_model* m) {
             n = 4;
         }
         rc = neon_internal::matvec_chain(ph, n, m->d_pos, m->chain_sync, m->stream);
+        if (rc == NEON_ERR_UNSUPPORTED) {
+            // a shape the chain does not take (nothing was launched): the phases one launch each
+            rc = NEON_OK;
+            for (int p = 0; p < n && !rc; ++p) {
+                neon_internal::MatvecExt ext = ph[p].ext;
+                ext.d_pos = m->d_pos;
+                const size_t cols = ph[p].t[0].W->cols;
+                rc = neon_internal::matvec(ph[p].t, (size_t)ph[p].n, ph[p].x, cols, 1, m->stream, ph[p].accumulate, &ext);
+            }
+        }
     }
     return rc;
 }
