@@ -147,6 +147,9 @@ def parse_args():
     p.add_argument("--decode-chain", action="store_true",
                    help="decode steps with the projections between attention launches as one launch "
                         "(neon_cuda_set_decode_chain)")
+    p.add_argument("--tiles", default=None, metavar="RC:KC",
+                   help="one-position Q4_0 / Q8_0 tile shape: RC rows per tile, KC blocks per row chunk "
+                        "(0 = whole rows); neon_cuda_set_stream_tiles")
     p.add_argument("--batch", type=int, default=1,
                    help="matvec workloads: positions per call; > 1 times the prefill path (one JSON line)")
     p.add_argument("--type-sweep", action="store_true",
@@ -422,6 +425,8 @@ def run_decode(args):
         N.set_launch_overlap(True)
     if getattr(args, "decode_chain", False):
         N.set_decode_chain(True)
+    if getattr(args, "tiles", None):
+        N.set_stream_tiles(*(int(v) for v in args.tiles.split(":")))
     N.set_fused_collectives(not args.no_fused_collectives)
     comm = None
     barrier, max_over_ranks = (lambda: None), (lambda v: v)
@@ -584,6 +589,8 @@ def run_neon(args):
         N.set_launch_overlap(True)
     if getattr(args, "decode_chain", False):
         N.set_decode_chain(True)
+    if getattr(args, "tiles", None):
+        N.set_stream_tiles(*(int(v) for v in args.tiles.split(":")))
     dev = torch.device("cuda", local)
 
     host_w = host_rotation(rank, ROTATION)
@@ -725,7 +732,8 @@ def run_neon(args):
             "config": {**workload_config(), "parallelism": f"dp{world} (independent rotations)",
                        "variants": [v for v, on in (("launch_overlap", args.launch_overlap), ("dq_ring", args.dq_ring),
                                                     ("prefill_mma", args.prefill_mma),
-                                                    ("decode_chain", args.decode_chain)) if on],
+                                                    ("decode_chain", args.decode_chain)) if on]
+                       + ([f"tiles {args.tiles}"] if args.tiles else []),
                        "launch": "CUDA graph of 1024 PDL launches per step"},
             "e2e": {"value": round(e2e_value, 2), "unit": UNIT,
                     "h2d_bytes_per_step": CALLS_PER_STEP * COLS * 4,
@@ -829,6 +837,8 @@ def run_type_sweep(args):
     torch.cuda.set_device(0)
     N.init(0)
     N.set_dq_ring(bool(args.dq_ring))
+    if args.tiles:
+        N.set_stream_tiles(*(int(v) for v in args.tiles.split(":")))
     dev = torch.device("cuda", 0)
     peak, peak_kind = measured_peak()
     stream = torch.cuda.Stream(device=dev)

@@ -370,6 +370,13 @@ NEON_API int neon_cuda_set_launch_overlap(int enabled);
  * run has validated it; process-wide. */
 NEON_API int neon_cuda_set_decode_chain(int enabled);
 
+/* Tile shape of later one-position Q4_0 / Q8_0 launches, for tuning sweeps:
+ * rows_per_tile (2, 4, 8, 16 or 32) rows per tile, each row in chunks of
+ * blocks_per_chunk 32-value blocks (0: whole rows). (0, 0) returns to the
+ * built-in planner, the default. A shape whose stage does not fit shared
+ * memory makes the call fail with NEON_ERR_UNSUPPORTED. Process-wide. */
+NEON_API int neon_cuda_set_stream_tiles(int rows_per_tile, int blocks_per_chunk);
+
 /* Launch option: programmatic dependent launch (PDL) lets a matvec fetch its
  * weights while the previous kernel on the stream finishes; on by default. */
 NEON_API int neon_cuda_set_pdl(int enabled);

@@ -39,6 +39,7 @@ std::atomic<int> g_prefill_mma{0};  // neon_cuda_set_prefill_mma
 std::atomic<int> g_dq_ring{0};      // neon_cuda_set_dq_ring
 std::atomic<int> g_launch_overlap{0};  // neon_cuda_set_launch_overlap
 std::atomic<int> g_decode_chain{0};    // neon_cuda_set_decode_chain
+std::atomic<int> g_tile_rc{0}, g_tile_kc{0};  // neon_cuda_set_stream_tiles (0: the planner's choice)
 
 struct DeviceState {
     bool ready = false;
@@ -221,7 +222,14 @@ StreamPlan plan_stream(int type, int nb, size_t total_rows, int sms) {
     const int P = type == NEON_GGML_Q4_0 ? 16 : 32;
     const long long row_bytes = (long long)nb * (P + 2);
     StreamPlan p{};
-    if (row_bytes * 2 <= kStageTarget) {
+    const int forced_rc = g_tile_rc.load(std::memory_order_relaxed);
+    if (forced_rc) {
+        // neon_cuda_set_stream_tiles: RC rows per tile, chunks of kc blocks (0 or >= nb: whole rows)
+        const int kc = g_tile_kc.load(std::memory_order_relaxed);
+        p.rc = forced_rc;
+        p.kc = kc <= 0 || kc >= nb ? nb : kc;
+        p.nch = (nb + p.kc - 1) / p.kc;
+    } else if (row_bytes * 2 <= kStageTarget) {
         p.kc = nb;
         p.nch = 1;
         p.rc = 32;
@@ -1017,6 +1025,16 @@ int neon_cuda_set_launch_overlap(int enabled) {
 
 int neon_cuda_set_decode_chain(int enabled) {
     g_decode_chain.store(enabled ? 1 : 0);
+    return NEON_OK;
+}
+
+int neon_cuda_set_stream_tiles(int rows_per_tile, int blocks_per_chunk) {
+    if (rows_per_tile != 0 && rows_per_tile != 2 && rows_per_tile != 4 && rows_per_tile != 8 && rows_per_tile != 16 &&
+        rows_per_tile != 32)
+        return set_err(NEON_ERR_INVALID, "rows per tile must be 0 (the planner's choice), 2, 4, 8, 16 or 32");
+    if (blocks_per_chunk < 0) return set_err(NEON_ERR_INVALID, "blocks per chunk must be >= 0");
+    g_tile_kc.store(blocks_per_chunk);
+    g_tile_rc.store(rows_per_tile);
     return NEON_OK;
 }
 

@@ -101,6 +101,7 @@ C_ENTRY_POINTS = (
     "neon_cuda_set_dq_ring",
     "neon_cuda_set_launch_overlap",
     "neon_cuda_set_decode_chain",
+    "neon_cuda_set_stream_tiles",
 )
 
 _sz = C.c_size_t
@@ -166,6 +167,7 @@ def load(path: str | None = None) -> C.CDLL:
         L.neon_cuda_set_dq_ring.argtypes = [C.c_int]
         L.neon_cuda_set_launch_overlap.argtypes = [C.c_int]
         L.neon_cuda_set_decode_chain.argtypes = [C.c_int]
+        L.neon_cuda_set_stream_tiles.argtypes = [C.c_int, C.c_int]
         L.neon_cuda_matvec_q4_0_noalloc.argtypes = [_vp, _vp, _sz, _vp, _sz, _sz, _vp]
         L.neon_cuda_model_create.argtypes = [C.POINTER(_ModelConfig), C.POINTER(_vp)]
         L.neon_cuda_model_set_tensor.argtypes = [_vp, C.c_int, C.c_int, _vp, _sz, C.c_int, _sz, _sz]
@@ -238,6 +240,13 @@ def set_decode_chain(enabled: bool) -> None:
     attention launches as one launch (grid barriers between them); read when a
     model captures its step; process-wide, off by default."""
     _check(load().neon_cuda_set_decode_chain(1 if enabled else 0))
+
+
+def set_stream_tiles(rows_per_tile: int = 0, blocks_per_chunk: int = 0) -> None:
+    """Tile shape of later one-position Q4_0 / Q8_0 launches (rows per tile,
+    blocks per row chunk; 0 = whole rows); (0, 0) is the built-in planner.
+    For tuning sweeps; process-wide."""
+    _check(load().neon_cuda_set_stream_tiles(int(rows_per_tile), int(blocks_per_chunk)))
 
 
 def set_pdl(enabled: bool) -> None:
