@@ -152,6 +152,9 @@ def parse_args():
                         "(0 = whole rows); neon_cuda_set_stream_tiles")
     p.add_argument("--batch", type=int, default=1,
                    help="matvec workloads: positions per call; > 1 times the prefill path (one JSON line)")
+    p.add_argument("--tile-sweep", action="store_true",
+                   help="time the one-position Q4_0 / Q8_0 workloads under every tile shape of the sweep "
+                        "(one JSON line each) instead of the headline")
     p.add_argument("--type-sweep", action="store_true",
                    help="time the matvec of every weight type (one JSON line each) instead of the headline")
     p.add_argument("--no-large-decode", action="store_true",
@@ -826,6 +829,40 @@ def run_prefill(args):
     }), flush=True)
 
 
+def time_matvec_graph(N, torch, stream, tensors, K, W):
+    """Device GB/s of the selected workload: a CUDA graph of CALLS_PER_STEP
+    one-position launches over `tensors` (a rotation larger than L2), K
+    replays timed with CUDA events after W warm-up replays (the headline's
+    method). Returns (GB/s, microseconds per call)."""
+    dev = torch.device("cuda", 0)
+    dx = torch.from_numpy(S.activations(1, COLS, seed=7)).to(dev)
+    ys = torch.zeros((len(tensors), ROWS), device=dev)
+    n = len(tensors)
+    with torch.cuda.stream(stream):
+        tensors[0].matvec(dx, ys[0], stream=stream)
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for j in range(CALLS_PER_STEP):
+            tensors[j % n].matvec(dx, ys[j % n], stream=stream)
+    with torch.cuda.stream(stream):
+        for _ in range(W):
+            graph.replay()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        for _ in range(K):
+            graph.replay()
+        end.record(stream)
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end)
+    del graph
+    torch.cuda.synchronize()
+    bytes_call = S.algorithmic_bytes(TYPE, ROWS, COLS)
+    return K * CALLS_PER_STEP * bytes_call / (ms / 1e3) / 1e9, ms * 1e3 / (K * CALLS_PER_STEP)
+
+
 def run_type_sweep(args):
     """One JSON line per weight type: device GB/s of a CUDA graph of 1024
     one-position launches over a rotation of tensors larger than L2, timed
@@ -839,50 +876,75 @@ def run_type_sweep(args):
     N.set_dq_ring(bool(args.dq_ring))
     if args.tiles:
         N.set_stream_tiles(*(int(v) for v in args.tiles.split(":")))
-    dev = torch.device("cuda", 0)
     peak, peak_kind = measured_peak()
-    stream = torch.cuda.Stream(device=dev)
+    stream = torch.cuda.Stream(device=torch.device("cuda", 0))
     K, W = args.steps, max(3, args.warmup)
     for name in TYPE_SWEEP:
         select_workload(name)
         tensors = [N.DeviceTensor(w, TYPE, ROWS, COLS) for w in host_rotation(0, ROTATION)]
-        dx = torch.from_numpy(S.activations(1, COLS, seed=7)).to(dev)
-        ys = torch.zeros((ROTATION, ROWS), device=dev)
-        with torch.cuda.stream(stream):
-            tensors[0].matvec(dx, ys[0], stream=stream)
-        stream.synchronize()
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=stream):
-            for j in range(CALLS_PER_STEP):
-                tensors[j % ROTATION].matvec(dx, ys[j % ROTATION], stream=stream)
-        with torch.cuda.stream(stream):
-            for _ in range(W):
-                graph.replay()
-        torch.cuda.synchronize()
-        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with torch.cuda.stream(stream):
-            start.record(stream)
-            for _ in range(K):
-                graph.replay()
-            end.record(stream)
-        torch.cuda.synchronize()
-        ms = start.elapsed_time(end)
-        bytes_call = S.algorithmic_bytes(TYPE, ROWS, COLS)
-        gbs = K * CALLS_PER_STEP * bytes_call / (ms / 1e3) / 1e9
+        gbs, us = time_matvec_graph(N, torch, stream, tensors, K, W)
+        del tensors
+        torch.cuda.empty_cache()
         kernel = KERNEL.replace("matvec_dq_kernel", "matvec_dq_ring_kernel") if args.dq_ring else KERNEL
         print(json.dumps({"workload": name, "type": TYPE_NAME, "kernel": kernel, "rows": ROWS, "cols": COLS,
                           "value": round(gbs, 1), "unit": UNIT, "frac": round(gbs / peak, 4),
-                          "peak": peak, "peak_source": peak_kind, "us_per_call": round(ms * 1e3 / (K * CALLS_PER_STEP), 3),
-                          "bytes_per_call": bytes_call, "rotation_tensors": ROTATION, "steps": K, "warmup": W}),
+                          "peak": peak, "peak_source": peak_kind, "us_per_call": round(us, 3),
+                          "bytes_per_call": S.algorithmic_bytes(TYPE, ROWS, COLS), "rotation_tensors": ROTATION,
+                          "steps": K, "warmup": W}),
               flush=True)
-        del graph, tensors
+
+
+# (rows per tile, chunks per row; 0 = whole rows) of the tile sweep, after the planner's own choice
+TILE_SWEEP_SHAPES = [(2, 0), (4, 0), (8, 0), (16, 0), (32, 0), (4, 2), (8, 2), (8, 4), (16, 4), (16, 8), (32, 8)]
+TILE_SWEEP_WORKLOADS = ["q4_0_4096x4096", "q4_0_28672x8192", "q4_0_8192x28672", "q8_0_4096x4096",
+                        "q8_0_14336x4096", "q8_0_4096x14336"]
+
+
+def run_tile_sweep(args):
+    """One JSON line per (workload, tile shape) of the one-position Q4_0 / Q8_0
+    kernel, timed as the type sweep times a workload: the planner's choice
+    (with and without launch overlap), then every forced shape of
+    TILE_SWEEP_SHAPES that fits shared memory (neon_cuda_set_stream_tiles)."""
+    import torch
+
+    import neon_cuda as N
+
+    torch.cuda.set_device(0)
+    N.init(0)
+    peak, peak_kind = measured_peak()
+    stream = torch.cuda.Stream(device=torch.device("cuda", 0))
+    K, W = args.steps, max(3, args.warmup)
+    for name in TILE_SWEEP_WORKLOADS:
+        select_workload(name)
+        nb = COLS // 32
+        tensors = [N.DeviceTensor(w, TYPE, ROWS, COLS) for w in host_rotation(0, ROTATION)]
+        runs = [("planner", 0, 0, False), ("planner + launch overlap", 0, 0, True)]
+        for rc, nch in TILE_SWEEP_SHAPES:
+            kc = 0 if nch == 0 else ((nb + nch - 1) // nch + 7) // 8 * 8
+            runs.append((f"rc {rc}, kc {kc or nb}", rc, kc, False))
+        for label, rc, kc, overlap in runs:
+            N.set_stream_tiles(rc, kc)
+            N.set_launch_overlap(overlap)
+            line = {"workload": name, "tiles": label, "rows": ROWS, "cols": COLS, "unit": UNIT, "steps": K,
+                    "warmup": W, "peak": peak, "peak_source": peak_kind}
+            try:
+                gbs, us = time_matvec_graph(N, torch, stream, tensors, K, W)
+                line.update({"value": round(gbs, 1), "frac": round(gbs / peak, 4), "us_per_call": round(us, 3)})
+            except RuntimeError as e:  # a stage that does not fit shared memory is refused before any launch
+                line["skipped"] = str(e).splitlines()[0][:160]
+            print(json.dumps(line), flush=True)
+        del tensors
         torch.cuda.synchronize()
         torch.cuda.empty_cache()
+    N.set_stream_tiles(0, 0)
+    N.set_launch_overlap(False)
 
 
 def main():
     args = parse_args()
-    if args.type_sweep and args.impl != "reference":
+    if args.tile_sweep and args.impl != "reference":
+        run_tile_sweep(args)
+    elif args.type_sweep and args.impl != "reference":
         run_type_sweep(args)
     elif args.batch > 1 and args.impl != "reference" and args.workload not in DECODE_WORKLOADS:
         run_prefill(args)
