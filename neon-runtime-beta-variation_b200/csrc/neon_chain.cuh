@@ -16,15 +16,24 @@
 //    are read through L2 (ld.global.cg), never the non-coherent path.
 // Every CTA of the grid must be resident at once for the barriers: the host
 // sizes the grid to the CTAs the SMs hold (one wave), and a barrier that
-// waits longer than ~2 s records bit 4 of the error word, raises the abort
-// word and returns, so every other CTA leaves too.
+// waits longer than its bound records bit 4 of the error word, raises the
+// abort word and returns, so every other CTA leaves too.
+//
+// Tensor parallel (fused collectives): attn_output and ffn_down store their
+// partial rows as LL words into every rank's slot (the streaming kernel's
+// kEpiPeer epilogue), and an LL-reduce phase -- comm_ll_reduce_kernel's work,
+// each CTA a slice of the vector -- adds the ranks' words into the residual
+// before the next projection reads it; a layer is then 6 phases in one launch
+// instead of 7 launches. The launch reads the communicator's count of
+// completed LL collectives once, numbers its own (count + 1, + 2), and the
+// last CTA to leave records the new count.
 #pragma once
 
 #include "neon_kernels.cuh"
 
 namespace neon {
 
-constexpr int kChainMaxPhases = 4;
+constexpr int kChainMaxPhases = 6;
 constexpr int kChainMaxSpans = 3;   // Q, K, V
 constexpr int kChainMaxStages = 8;
 
@@ -39,6 +48,10 @@ struct ChainPhase {
     int x_vec;               // x is 16-byte aligned
     int accumulate;          // kEpiStore spans: y += result
     int rope_half, head_dim;
+    int ll_reduce;           // 1: an LL-reduce phase (h[i] += the ranks' words, i < n); no projection
+    float* h;                //   its residual
+    int n;                   //   and length
+    int peer_k;              // LL collective of a kEpiPeer or LL-reduce phase: count + 1 + peer_k
 };
 
 struct ChainArgs {
@@ -47,6 +60,10 @@ struct ChainArgs {
     unsigned int* err;       // device error word: bit 0 a ring wait, bit 4 a grid barrier timed out
     unsigned int* sync;      // [0] barrier arrivals, [1] departures, [2] abort; zero between launches
     int n_phases;
+    int has_peer;            // tensor parallel: `peer` is the communicator's LL set
+    int n_peer;              // LL collectives of the launch
+    PeerSet peer;
+    unsigned long long barrier_ns;  // bound of a grid-barrier wait
     int stages;              // ring depth
     int slot_bytes;          // bytes per ring slot: the largest phase's stream_stage_bytes
     int x_bytes;             // X region: the largest phase's stream_x_bytes
@@ -83,7 +100,7 @@ __device__ __forceinline__ bool chain_barrier(const ChainArgs& c, int k) {
                 ok = false;
                 break;
             }
-            if (globaltimer_ns() - t0 > 2000000000ull) {
+            if (globaltimer_ns() - t0 > c.barrier_ns) {
                 atomicOr(c.err, 16u);
                 atomicExch(&c.sync[2], 1u);
                 ok = false;
@@ -95,9 +112,11 @@ __device__ __forceinline__ bool chain_barrier(const ChainArgs& c, int k) {
     return !compute_sync_or(!ok);
 }
 
-// matvec_stream_kernel's epilogues for the chain's phases (no fused collective).
-__device__ __forceinline__ void chain_epilogue(const ChainPhase& P, const Span& sp, int row0, int RC,
-                                               const float* rowv, int pos, const float2* rcs, float yold) {
+// matvec_stream_kernel's epilogues for the chain's phases; kEpiPeer stores LL
+// collective `call`.
+__device__ __forceinline__ void chain_epilogue(const ChainArgs& c, const ChainPhase& P, const Span& sp, int row0,
+                                               int RC, const float* rowv, int pos, const float2* rcs, float yold,
+                                               unsigned int call) {
     const int t = threadIdx.x;
     if (t >= RC) return;
     const int row = row0 + t;
@@ -131,8 +150,66 @@ __device__ __forceinline__ void chain_epilogue(const ChainPhase& P, const Span& 
         case kEpiSilu:
             sp.y[row] = silu_dev(v);
             break;
+        case kEpiPeer: {
+            // this rank's partial row sum, as an LL word, into its slot on every rank (NVLink stores)
+            const long long off = ll_slot_off(c.peer.world, (int)(call & 1u), c.peer.rank) / 8 + row;
+            const unsigned long long w = ll_pack(v, call);
+            for (int p = 0; p < c.peer.world; ++p)
+                st_relaxed_sys_u64(reinterpret_cast<unsigned long long*>(c.peer.base[p]) + off, w);
+            break;
+        }
         default:
             break;
+    }
+}
+
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64_chain(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// An LL-reduce phase (comm_ll_reduce_kernel's arithmetic): h[i] = h[i] +
+// (slot_0[i] + slot_1[i] + ...) in rank order for this CTA's elements, every
+// word polled until it carries `call`, each poll bounded by the
+// communicator's timeout (bit 0 of its error word, then no more waits).
+__device__ __forceinline__ void chain_ll_reduce(const ChainArgs& c, const ChainPhase& P, unsigned int call,
+                                                volatile int* skip) {
+    const PeerSet& p = c.peer;
+    const unsigned long long* slots =
+        reinterpret_cast<const unsigned long long*>(p.base[p.rank] + ll_slot_off(p.world, (int)(call & 1u), 0));
+    for (int i = blockIdx.x * kStreamThreads + threadIdx.x; i < P.n; i += gridDim.x * kStreamThreads) {
+        float s = 0.f;
+        // four ranks' words in flight at a time (registers: the kernel shares
+        // them with the projections' phases)
+        for (int r0 = 0; r0 < p.world; r0 += 4) {
+            unsigned long long w[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                if (r0 + k < p.world) w[k] = ld_relaxed_sys_u64_chain(slots + (long long)(r0 + k) * kCommFusedFloats + i);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int r = r0 + k;
+                if (r >= p.world) break;
+                const unsigned long long* a = slots + (long long)r * kCommFusedFloats + i;
+                if ((unsigned int)(w[k] >> 32) != call && !*skip) {
+                    const unsigned long long t0 = globaltimer_ns();
+                    for (;;) {
+                        w[k] = ld_relaxed_sys_u64_chain(a);
+                        if ((unsigned int)(w[k] >> 32) == call || *skip) break;
+                        if (globaltimer_ns() - t0 > p.timeout_ns) {
+                            atomicOr(p.err, 1u);
+                            *skip = 1;
+                            break;
+                        }
+                        __nanosleep(32);
+                    }
+                }
+                const float v = __uint_as_float((unsigned int)w[k]);
+                s = r ? s + v : v;
+            }
+        }
+        P.h[i] = __ldcg(P.h + i) + s;
     }
 }
 
@@ -143,7 +220,7 @@ template <int RC, int R>
 __device__ __forceinline__ bool chain_consume(const ChainArgs& c, const ChainPhase& P, int n_items, int& g,
                                               const unsigned char* xsm, const unsigned char* ring, uint64_t* full,
                                               uint64_t* empty, float (*red)[128], float (*rowv)[32], int pos,
-                                              const float2* rcs) {
+                                              const float2* rcs, unsigned int call) {
     constexpr int P16 = 16;
     constexpr int G = RC / R;
     constexpr int TPG = kStreamThreads / G;
@@ -230,7 +307,7 @@ __device__ __forceinline__ bool chain_consume(const ChainArgs& c, const ChainPha
                 rowv[tb][threadIdx.x] = v;
             }
             if (WPG > 1) compute_sync();
-            chain_epilogue(P, sp, row0, RC, rowv[tb], pos, rcs, yold);
+            chain_epilogue(c, P, sp, row0, RC, rowv[tb], pos, rcs, yold, call);
 #pragma unroll
             for (int rr = 0; rr < R; ++rr) acc[rr] = 0.f;
         }
@@ -253,6 +330,7 @@ __global__ void __launch_bounds__(kStreamBlock) matvec_chain_kernel(const __grid
     unsigned char* ring = smem + c.x_bytes;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     auto items_of = [&](const ChainPhase& P) {
+        if (P.ll_reduce) return 0;
         const int my_tiles =
             (int)blockIdx.x < P.n_tiles ? (P.n_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
         return my_tiles * P.nch;
@@ -323,12 +401,24 @@ __global__ void __launch_bounds__(kStreamBlock) matvec_chain_kernel(const __grid
     }
 
     // compute warps
+    __shared__ int s_skip;
     pdl_wait();
     const int pos = c.d_pos ? *c.d_pos : 0;
+    // the communicator's count of completed LL collectives, before any CTA of
+    // this launch can have recorded a new one (that happens after the last
+    // barrier)
+    const unsigned int call0 = c.has_peer ? *reinterpret_cast<volatile const unsigned int*>(c.peer.calls) : 0u;
+    if (threadIdx.x == 0) s_skip = c.has_peer && *reinterpret_cast<volatile unsigned int*>(c.peer.err) != 0u;
+    compute_sync();
     int g = 0;
     for (int p = 0; p < c.n_phases; ++p) {
         const ChainPhase& P = c.ph[p];
         if (p > 0 && !chain_barrier(c, p)) return;
+        const unsigned int call = call0 + 1u + (unsigned int)P.peer_k;
+        if (P.ll_reduce) {
+            chain_ll_reduce(c, P, call, &s_skip);
+            continue;
+        }
         if (P.rope_cs && (int)threadIdx.x < P.rope_half) prefetch_l1(P.rope_cs + (long long)pos * P.rope_half + threadIdx.x);
         const int nb = P.nb;
         const int tpb = kStreamThreads / nb;
@@ -349,11 +439,11 @@ __global__ void __launch_bounds__(kStreamBlock) matvec_chain_kernel(const __grid
         const int n_items = items_of(P);
         bool ok = true;
         switch (P.rc) {  // R per RC: matvec_stream_kernel's Q4_0 instantiations
-            case 2: ok = chain_consume<2, 2>(c, P, n_items, g, xsm, ring, full, empty, red, rowv, pos, rcs); break;
-            case 4: ok = chain_consume<4, 2>(c, P, n_items, g, xsm, ring, full, empty, red, rowv, pos, rcs); break;
-            case 8: ok = chain_consume<8, 2>(c, P, n_items, g, xsm, ring, full, empty, red, rowv, pos, rcs); break;
-            case 16: ok = chain_consume<16, 4>(c, P, n_items, g, xsm, ring, full, empty, red, rowv, pos, rcs); break;
-            default: ok = chain_consume<32, 4>(c, P, n_items, g, xsm, ring, full, empty, red, rowv, pos, rcs); break;
+            case 2: ok = chain_consume<2, 2>(c, P, n_items, g, xsm, ring, full, empty, red, rowv, pos, rcs, call); break;
+            case 4: ok = chain_consume<4, 2>(c, P, n_items, g, xsm, ring, full, empty, red, rowv, pos, rcs, call); break;
+            case 8: ok = chain_consume<8, 2>(c, P, n_items, g, xsm, ring, full, empty, red, rowv, pos, rcs, call); break;
+            case 16: ok = chain_consume<16, 4>(c, P, n_items, g, xsm, ring, full, empty, red, rowv, pos, rcs, call); break;
+            default: ok = chain_consume<32, 4>(c, P, n_items, g, xsm, ring, full, empty, red, rowv, pos, rcs, call); break;
         }
         if (!ok) {
             if (threadIdx.x == 0) atomicExch(&c.sync[2], 1u);
@@ -361,7 +451,8 @@ __global__ void __launch_bounds__(kStreamBlock) matvec_chain_kernel(const __grid
         }
     }
     // Every CTA has passed its last barrier once all have departed: the last
-    // to depart zeroes the counters for the next launch.
+    // to depart zeroes the counters for the next launch and records the LL
+    // collectives of this one as completed.
     if (c.n_phases > 1) {
         compute_sync();
         if (threadIdx.x == 0) {
@@ -369,6 +460,7 @@ __global__ void __launch_bounds__(kStreamBlock) matvec_chain_kernel(const __grid
             if (atomicAdd(&c.sync[1], 1u) == gridDim.x - 1) {
                 atomicExch(&c.sync[0], 0u);
                 atomicExch(&c.sync[1], 0u);
+                if (c.has_peer) *c.peer.calls = call0 + (unsigned int)c.n_peer;
             }
         }
     }

@@ -896,17 +896,29 @@ int chain_occupancy(int smem) {
     return occ;
 }
 
-int matvec_chain(const ChainPhaseDesc* ph, int n, const int* d_pos, unsigned int* sync, cudaStream_t st) {
-    if (n < 1 || n > kChainMaxPhases || !sync) return set_err(NEON_ERR_UNSUPPORTED, "projection chain: 1-4 phases");
+int matvec_chain(const ChainPhaseDesc* ph, int n, const int* d_pos, unsigned int* sync, const PeerSet* peer,
+                 cudaStream_t st) {
+    if (n < 1 || n > kChainMaxPhases || !sync) return set_err(NEON_ERR_UNSUPPORTED, "projection chain: 1-6 phases");
     int device = 0;
     int rc = current_device(&device);
     if (rc) return rc;
     DeviceState& ds = g_dev[device];
     ChainArgs c;
     std::memset(&c, 0, sizeof(c));
-    int slot = 0, xb = 0;
+    int slot = 0, xb = 0, n_peer = 0;
     for (int p = 0; p < n; ++p) {
         const ChainPhaseDesc& d = ph[p];
+        if (d.ll_h) {
+            // LL reduce of the collective the last kEpiPeer phase produced
+            if (!peer || n_peer == 0 || d.ll_len <= 0 || d.ll_len > kCommFusedFloats)
+                return set_err(NEON_ERR_UNSUPPORTED, "projection chain: an LL reduce needs a kEpiPeer phase before it");
+            ChainPhase& P = c.ph[p];
+            P.ll_reduce = 1;
+            P.h = d.ll_h;
+            P.n = d.ll_len;
+            P.peer_k = n_peer - 1;
+            continue;
+        }
         if (d.n < 1 || d.n > kChainMaxSpans || !d.t || !d.x)
             return set_err(NEON_ERR_UNSUPPORTED, "projection chain: 1-3 targets per phase");
         const size_t cols = d.t[0].W ? d.t[0].W->cols : 0;
@@ -933,6 +945,11 @@ int matvec_chain(const ChainPhaseDesc* ph, int n, const int* d_pos, unsigned int
             tiles += (int)((tg.W->rows + pl.rc - 1) / pl.rc);
             sp.epi = d.ext.epi ? d.ext.epi[i] : kEpiStore;
             sp.pos_stride = d.ext.pos_stride ? d.ext.pos_stride[i] : 0;
+            if (d.ext.peer_mode == 1) sp.epi = kEpiPeer;
+        }
+        if (d.ext.peer_mode == 1) {
+            if (!peer || d.n != 1) return set_err(NEON_ERR_UNSUPPORTED, "projection chain: a kEpiPeer phase needs the LL set");
+            c.ph[p].peer_k = n_peer++;
         }
         P.n_spans = d.n;
         P.n_tiles = tiles;
@@ -968,6 +985,14 @@ int matvec_chain(const ChainPhaseDesc* ph, int n, const int* d_pos, unsigned int
     }
     if (best_stages < 1) return set_err(NEON_ERR_UNSUPPORTED, "projection chain: X and one ring slot exceed shared memory");
     c.n_phases = n;
+    c.n_peer = n_peer;
+    c.barrier_ns = 2000000000ull;
+    if (peer) {
+        c.has_peer = 1;
+        c.peer = *peer;
+        // a CTA in an LL reduce may wait up to the communicator's bound for a peer
+        c.barrier_ns = std::max<unsigned long long>(c.barrier_ns, peer->timeout_ns + 1000000000ull);
+    }
     c.stages = best_stages;
     c.slot_bytes = slot;
     c.x_bytes = xb;

@@ -1153,7 +1153,8 @@ int run_head(neon_model* m, const float* x) {
 }
 
 // The projection chain (neon_cuda_set_decode_chain) takes a model whose
-// projections are all Q4_0, on one device.
+// projections are all Q4_0 (one device, or tensor parallel with fused
+// collectives).
 bool chain_applies(const neon_model* m) {
     for (const auto& L : m->layers) {
         for (auto* w : L.w)
@@ -1167,11 +1168,14 @@ bool chain_applies(const neon_model* m) {
 // launch, then per layer the attention launch and ONE matvec_chain_kernel
 // launch for attn_output (+= h), gate/up (rms_norm folded, SwiGLU / SiLU),
 // ffn_down (+= h) and the next layer's Q/K/V (rms_norm folded, RoPE, cache
-// rows): the same arithmetic as run_step's launches, bit for bit.
+// rows) -- tensor parallel, each residual projection followed by its LL
+// reduce: the same arithmetic as run_step's launches, bit for bit.
 int run_step_chain(neon_model* m) {
     const auto& c = m->cfg;
     const size_t n_embd = c.n_embd, q_dim = m->q_dim, kv_dim = m->kv_dim, n_ff = m->n_ff_l;
     float* hc = m->h;
+    const bool tp = m->world > 1;
+    const PeerSet peer = tp ? neon_internal::comm_peer_set(m->comm) : PeerSet{};
     const int qkv_epi[3] = {neon::kEpiRope, neon::kEpiRope, neon::kEpiAtPos};
     const long long qkv_stride[3] = {0, (long long)kv_dim, (long long)kv_dim};
     const int ffn_epi = c.plain_ffn ? neon::kEpiSilu : neon::kEpiSwiglu;
@@ -1209,38 +1213,57 @@ int run_step_chain(neon_model* m) {
         const float* Vl = m->V + (size_t)li * c.ctx_len * kv_dim;
         rc = launch_attn_decode(m, Kl, Vl);
         if (rc) break;
-        const neon_proj_target_t t_out{L.w[3], hc, n_embd}, t_gu{L.gateup, m->act, n_ff}, t_down{L.w[4], hc, n_embd};
+        // one device: attn_output and ffn_down accumulate into h; tensor
+        // parallel: they store their partial rows as LL words into every
+        // rank's slot and an LL-reduce phase adds the ranks' rows into h
+        float* res_y = tp ? m->part : hc;
+        const neon_proj_target_t t_out{L.w[3], res_y, n_embd}, t_gu{L.gateup, m->act, n_ff},
+            t_down{L.w[4], res_y, n_embd};
         neon_proj_target_t t_qkv[3];
-        neon_internal::ChainPhaseDesc ph[4];
-        ph[0].t = &t_out;
-        ph[0].n = 1;
-        ph[0].x = m->att;
-        ph[0].accumulate = 1;
-        ph[1].t = &t_gu;
-        ph[1].n = 1;
-        ph[1].x = hc;
-        ph[1].ext.norm_w = L.ffn_norm;
-        ph[1].ext.norm_eps = c.norm_eps;
-        ph[1].ext.epi = &ffn_epi;
-        ph[1].ext.pos_stride = &zero_stride;
-        ph[2].t = &t_down;
-        ph[2].n = 1;
-        ph[2].x = m->act;
-        ph[2].accumulate = 1;
-        int n = 3;
+        neon_internal::ChainPhaseDesc ph[6];  // the chain takes up to six phases
+        int n = 0;
+        auto residual = [&](const neon_proj_target_t* t, const float* x) {
+            ph[n].t = t;
+            ph[n].n = 1;
+            ph[n].x = x;
+            if (tp) {
+                ph[n].ext.peer_mode = 1;
+                ph[n].ext.peer = peer;
+                ++n;
+                ph[n].ll_h = hc;
+                ph[n].ll_len = (int)n_embd;
+            } else {
+                ph[n].accumulate = 1;
+            }
+            ++n;
+        };
+        residual(&t_out, m->att);
+        ph[n].t = &t_gu;
+        ph[n].n = 1;
+        ph[n].x = hc;
+        ph[n].ext.norm_w = L.ffn_norm;
+        ph[n].ext.norm_eps = c.norm_eps;
+        ph[n].ext.epi = &ffn_epi;
+        ph[n].ext.pos_stride = &zero_stride;
+        ++n;
+        residual(&t_down, m->act);
         if (li + 1 < c.n_layer) {
             qkv_targets(li + 1, t_qkv);
-            ph[3].t = t_qkv;
-            ph[3].n = 3;
-            ph[3].x = hc;
-            ph[3].ext = qkv_ext(li + 1);
-            n = 4;
+            ph[n].t = t_qkv;
+            ph[n].n = 3;
+            ph[n].x = hc;
+            ph[n].ext = qkv_ext(li + 1);
+            ++n;
         }
-        rc = neon_internal::matvec_chain(ph, n, m->d_pos, m->chain_sync, m->stream);
+        rc = neon_internal::matvec_chain(ph, n, m->d_pos, m->chain_sync, tp ? &peer : nullptr, m->stream);
         if (rc == NEON_ERR_UNSUPPORTED) {
             // a shape the chain does not take (nothing was launched): the phases one launch each
             rc = NEON_OK;
             for (int p = 0; p < n && !rc; ++p) {
+                if (ph[p].ll_h) {
+                    rc = neon_internal::comm_ll_reduce(m->comm, hc, (long long)n_embd, m->stream);
+                    continue;
+                }
                 neon_internal::MatvecExt ext = ph[p].ext;
                 ext.d_pos = m->d_pos;
                 const size_t cols = ph[p].t[0].W->cols;
@@ -1257,7 +1280,8 @@ int run_step_chain(neon_model* m) {
 // partial rows as LL words straight into every rank's slot, and a small
 // reduce launch adds the ranks' rows into the residual.
 int run_step(neon_model* m) {
-    if (m->world == 1 && neon_internal::decode_chain() && chain_applies(m)) return run_step_chain(m);
+    if (neon_internal::decode_chain() && chain_applies(m) && (m->world == 1 || neon_internal::fused_collectives()))
+        return run_step_chain(m);
     const auto& c = m->cfg;
     int rc = launch_embed(m, m->d_tok, 1);
     const size_t n_embd = c.n_embd, q_dim = m->q_dim, kv_dim = m->kv_dim, n_ff = m->n_ff_l;

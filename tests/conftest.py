@@ -20,16 +20,20 @@ for p in (os.path.join(ROOT, "oracle"), PKG, ROOT):
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA GPU (sm_100a, B200)")
-    config.addinivalue_line("markers", "newest: a kernel variant behind an off-by-default switch; run after "
-                                       "the other tests, so that with -x its failure stops none of them")
+    config.addinivalue_line("markers", "newest(order=0): a kernel variant behind an off-by-default switch; run "
+                                       "after the other tests (by order), so that with -x its failure stops "
+                                       "none of them")
     config.addinivalue_line("markers", "last: run after every other test, the newest included")
 
 
 def pytest_collection_modifyitems(config, items):
     def rank(it):
         if it.get_closest_marker("last") is not None:
-            return 2
-        return 1 if it.get_closest_marker("newest") is not None else 0
+            return (2, 0)
+        m = it.get_closest_marker("newest")
+        if m is None:
+            return (0, 0)
+        return (1, m.args[0] if m.args else 0)
     items.sort(key=rank)  # stable: the order is kept otherwise
 
 

@@ -16,7 +16,7 @@ import oracle as O
 import synth as S
 from conftest import MODEL_L2_RTOL, rel_l2
 
-pytestmark = [pytest.mark.gpu, pytest.mark.newest]
+pytestmark = [pytest.mark.gpu, pytest.mark.newest(1)]
 torch = pytest.importorskip("torch")
 
 TINY = S.ModelConfig(1000, 256, 2, 4, 2, 64, 512, ctx_len=64, rope_base=1e4, name="tiny")
