@@ -19,9 +19,10 @@ def tensor_name(role, layer):
 
 
 def write_gguf(path, cfg, seed=5, wtype=S.GGML_Q4_0, embd_type=S.GGML_Q8_0, tied=True, arch="nanity",
-               spec_version=1, drop_key=None, bad_shape=None, vocab_size=None, alignment=None):
+               spec_version=1, drop_key=None, bad_shape=None, vocab_size=None, alignment=None, norm_type=None):
     """A NANITY .gguf of `cfg`; returns the tensor list (role, layer, bytes,
-    type, ne0, ne1) as synth.model_tensors made it."""
+    type, ne0, ne1) as synth.model_tensors made it (norm weights of
+    `norm_type` when given: 1-D tensors of that type)."""
     import gguf
     from gguf.constants import GGMLQuantizationType as Q
 
@@ -42,7 +43,7 @@ def write_gguf(path, cfg, seed=5, wtype=S.GGML_Q4_0, embd_type=S.GGML_Q8_0, tied
     w.add_token_list([f"t{i}" for i in range(cfg.n_vocab)])
     w.add_bos_token_id(1)
     w.add_eos_token_id(2)
-    tensors = list(S.model_tensors(cfg, seed=seed, wtype=wtype, embd_type=embd_type, tied=tied))
+    tensors = list(S.model_tensors(cfg, seed=seed, wtype=wtype, embd_type=embd_type, tied=tied, norm_type=norm_type))
     for role, layer, raw, typ, ne0, ne1 in tensors:
         name = tensor_name(role, layer)
         a = np.ascontiguousarray(raw).view(np.uint8)
@@ -52,6 +53,9 @@ def write_gguf(path, cfg, seed=5, wtype=S.GGML_Q4_0, embd_type=S.GGML_Q8_0, tied
         if typ == S.GGML_F32:
             arr = a.view(np.float32).reshape((ne1, ne0) if ne1 else (ne0,))
             w.add_tensor(name, arr)
+        elif ne1 == 0:  # a 1-D tensor of another type: its bytes, shape from the type's block size
+            w.add_tensor(name, a.view(np.float16) if typ == S.GGML_F16 else a, raw_dtype=None if typ == S.GGML_F16
+                         else Q(typ))
         else:
             w.add_tensor(name, a.reshape(ne1, -1), raw_dtype=Q(typ))
     w.write_header_to_file()

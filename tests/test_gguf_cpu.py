@@ -34,14 +34,16 @@ def ref_lib():
     return R
 
 
-MODELS = [(S.GGML_Q4_0, S.GGML_Q8_0, True), (S.GGML_Q4_K, S.GGML_Q6_K, False), (S.GGML_F16, S.GGML_F16, True)]
-ids = ["q4_0", "q4_k", "f16"]
+MODELS = [(S.GGML_Q4_0, S.GGML_Q8_0, True, None), (S.GGML_Q4_K, S.GGML_Q6_K, False, None),
+          (S.GGML_F16, S.GGML_F16, True, None), (S.GGML_Q4_0, S.GGML_Q8_0, True, S.GGML_F16),
+          (S.GGML_Q4_K, S.GGML_Q6_K, False, S.GGML_BF16)]
+ids = ["q4_0", "q4_k", "f16", "q4_0-f16-norms", "q4_k-bf16-norms"]
 
 
-@pytest.mark.parametrize("wtype,etype,tied", MODELS, ids=ids)
-def test_reader_returns_the_written_tensors(tmp_path, wtype, etype, tied):
+@pytest.mark.parametrize("wtype,etype,tied,ntype", MODELS, ids=ids)
+def test_reader_returns_the_written_tensors(tmp_path, wtype, etype, tied, ntype):
     path = str(tmp_path / "m.gguf")
-    written = write_gguf(path, TINY, wtype=wtype, embd_type=etype, tied=tied, alignment=64)
+    written = write_gguf(path, TINY, wtype=wtype, embd_type=etype, tied=tied, alignment=64, norm_type=ntype)
     c, tensors = N.load_gguf(path)
     got = {(r, l): (raw, t, ne0, ne1) for r, l, raw, t, ne0, ne1 in tensors}
     assert len(got) == len(written)
@@ -56,11 +58,11 @@ def test_reader_returns_the_written_tensors(tmp_path, wtype, etype, tied):
 
 
 @ref_only
-@pytest.mark.parametrize("wtype,etype,tied", MODELS, ids=ids)
-def test_reader_matches_reference_loader(tmp_path, wtype, etype, tied):
+@pytest.mark.parametrize("wtype,etype,tied,ntype", MODELS, ids=ids)
+def test_reader_matches_reference_loader(tmp_path, wtype, etype, tied, ntype):
     R = ref_lib()
     path = str(tmp_path / "m.gguf")
-    write_gguf(path, TINY, wtype=wtype, embd_type=etype, tied=tied)
+    write_gguf(path, TINY, wtype=wtype, embd_type=etype, tied=tied, norm_type=ntype)
     c, tensors = N.load_gguf(path)
     h = R.ref_gguf_open(path.encode())
     assert h, R.ref_last_error()
@@ -125,9 +127,10 @@ def test_errors_match_reference_loader(tmp_path, kw, post):
 
 
 @ref_only
-def test_oracle_decode_over_gguf_tensors_matches_reference(tmp_path):
+@pytest.mark.parametrize("ntype", [None, S.GGML_F16], ids=["f32-norms", "f16-norms"])
+def test_oracle_decode_over_gguf_tensors_matches_reference(tmp_path, ntype):
     path = str(tmp_path / "m.gguf")
-    write_gguf(path, TINY, wtype=S.GGML_Q4_K, embd_type=S.GGML_Q6_K, tied=False)
+    write_gguf(path, TINY, wtype=S.GGML_Q4_K, embd_type=S.GGML_Q6_K, tied=False, norm_type=ntype)
     c, tensors = N.load_gguf(path)
     cfg = TINY.with_(ctx_len=c.ctx_len)
     mo, mr = O.Model(cfg, tensors, "port"), O.Model(cfg, tensors, "reference", threads=2)

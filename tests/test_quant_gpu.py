@@ -97,14 +97,16 @@ def test_nctr_model_decodes_like_the_oracle(tmp_path, quant):
     m.free()
 
 
-def test_gguf_model_decodes_like_the_oracle(tmp_path):
+@pytest.mark.parametrize("ntype", [None, S.GGML_F16], ids=["f32-norms", "f16-norms"])
+def test_gguf_model_decodes_like_the_oracle(tmp_path, ntype):
     """A .gguf file written by gguf-py, read by neon_cuda.load_gguf, decoded on
-    the device: the oracle's greedy tokens on the same tensors."""
+    the device: the oracle's greedy tokens on the same tensors (norm weights
+    F32, or F16 as some converters write them)."""
     pytest.importorskip("gguf")
     from gguf_file import write_gguf
 
     path = str(tmp_path / "m.gguf")
-    write_gguf(path, TINY, wtype=S.GGML_Q4_K, embd_type=S.GGML_Q6_K, tied=False)
+    write_gguf(path, TINY, wtype=S.GGML_Q4_K, embd_type=S.GGML_Q6_K, tied=False, norm_type=ntype)
     c, tensors = N.load_gguf(path)
     m = N.Model(c, tensors)
     o = O.Model(TINY.with_(ctx_len=c.ctx_len), tensors, "port")
