@@ -273,6 +273,19 @@ def model_tensors(cfg: ModelConfig, seed: int, wtype: int = GGML_Q4_0, embd_type
             yield role, li, weights_fn(wtype, rows, cols, sub(role, li)), wtype, cols, rows
 
 
+def mixed_k_quant_tensors(cfg: ModelConfig, seed: int):
+    """A decoder with the type mix of a Q4_K_M conversion: Q4_K projections and
+    embedding, Q6_K attn_v, ffn_down and lm_head (untied), fp32 norms -- so
+    one layer's Q/K/V and its residual projections span two types. Same tuple
+    layout as model_tensors."""
+    q6 = {ROLE_ATTN_V, ROLE_FFN_DOWN, ROLE_OUTPUT}
+    for role, layer, raw, typ, ne0, ne1 in model_tensors(cfg, seed, wtype=GGML_Q4_K, embd_type=GGML_Q4_K, tied=False):
+        if role in q6:
+            raw = weights(GGML_Q6_K, ne1, ne0, seed * 7919 + role * 131 + layer + 3)
+            typ = GGML_Q6_K
+        yield role, layer, raw, typ, ne0, ne1
+
+
 def prompt_tokens(n: int, n_vocab: int, seed: int) -> np.ndarray:
     """Seeded random prompt token ids."""
     return np.random.default_rng(seed).integers(0, n_vocab, size=n, dtype=np.int32)

@@ -171,3 +171,19 @@ def test_decoder_of_each_type_matches_oracle(wtype, etype, tied):
         assert rel_l2(a, b) <= 1e-3, f"step {i}"
         assert int(np.argmax(a)) == int(np.argmax(b)), f"step {i}"
     m.free()
+
+
+def test_decoder_of_a_mixed_k_quant_model():
+    """Q4_K projections with Q6_K attn_v, ffn_down and lm_head (a Q4_K_M
+    conversion's mix): Q/K/V and each residual projection span two types, so
+    the fused step splits them by type. The oracle's greedy tokens, logits
+    within the same bar as the single-type decoders."""
+    tensors = list(S.mixed_k_quant_tensors(TINY, seed=19))
+    m = N.Model(TINY, tensors)
+    o = O.Model(TINY, tensors, "port")
+    prompt = S.prompt_tokens(9, TINY.n_vocab, 20)
+    want_toks, want_logits = o.generate_greedy(prompt, 8)
+    assert np.array_equal(m.generate(prompt, 8), want_toks)
+    m.set_length(0)
+    assert rel_l2(m.forward(prompt), want_logits[0]) <= 1e-3
+    m.free()

@@ -186,3 +186,16 @@ def test_model_forward_norm_types_matches_reference(norm_type):
     ta, la = mo.generate_greedy(p, 4)
     tb, lb = mr.generate_greedy(p, 4)
     assert np.array_equal(ta, tb) and np.array_equal(bits(la), bits(lb))
+
+
+@ref_only
+def test_mixed_k_quant_model_matches_reference():
+    """The type mix of a Q4_K_M conversion (Q4_K projections, Q6_K attn_v,
+    ffn_down and lm_head): transformer_forward bit for bit."""
+    tensors = list(S.mixed_k_quant_tensors(TINY, seed=19))
+    assert {t[3] for t in tensors if t[5]} == {S.GGML_Q4_K, S.GGML_Q6_K}
+    mo, mr = O.Model(TINY, tensors, "port"), O.Model(TINY, tensors, "reference", threads=4)
+    p = S.prompt_tokens(7, TINY.n_vocab, 20)
+    ta, la = mo.generate_greedy(p, 4)
+    tb, lb = mr.generate_greedy(p, 4)
+    assert np.array_equal(ta, tb) and np.array_equal(bits(la), bits(lb))
