@@ -36,6 +36,17 @@ def test_exports_every_declared_symbol():
     assert exported == declared, "exported C symbols differ from the header"
 
 
+def test_python_binding_types_every_argument():
+    """ctypes passes an untyped argument as a C int: a pointer or size_t would
+    be cut to 32 bits. Every entry point that takes arguments has argtypes."""
+    text = re.sub(r"/\*.*?\*/", "", open(os.path.join(ROOT, "include", "neon_cuda.h")).read(), flags=re.S)
+    L = N.load()
+    for name, params in re.findall(r"\b(neon_cuda_\w+)\s*\(([^)]*)\)", text):
+        if params.strip() in ("", "void"):
+            continue
+        assert getattr(L, name).argtypes is not None, f"{name}: no argtypes in neon_cuda.py"
+
+
 def test_no_gpu_host_calls_fail_cleanly():
     import torch
     if torch.cuda.is_available():
