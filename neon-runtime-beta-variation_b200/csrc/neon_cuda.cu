@@ -210,46 +210,11 @@ int launch(void (*kern)(KArgs...), dim3 grid, size_t smem, cudaStream_t st, Args
     return launch_n(kern, grid, kThreads, smem, st, std::forward<Args>(args)...);
 }
 
-// Tile plan of a streaming (one-position) launch.
-struct StreamPlan {
-    int rc, kc, nch, stages, stage_bytes, smem;
-};
-
-// Rows per tile: the largest of 32, 16, 8, 4, 2 whose tile fits one stage and
-// still gives every SM a tile; rows that do not fit a stage even 2 at a time
-// are cut into chunks.
+// Tile plan of a streaming (one-position) launch: plan_stream_tiles with
+// this library's stage target, shared-memory budget and tile override.
 StreamPlan plan_stream(int type, int nb, size_t total_rows, int sms) {
-    const int P = type == NEON_GGML_Q4_0 ? 16 : 32;
-    const long long row_bytes = (long long)nb * (P + 2);
-    StreamPlan p{};
-    const int forced_rc = g_tile_rc.load(std::memory_order_relaxed);
-    if (forced_rc) {
-        // neon_cuda_set_stream_tiles: RC rows per tile, chunks of kc blocks (0 or >= nb: whole rows)
-        const int kc = g_tile_kc.load(std::memory_order_relaxed);
-        p.rc = forced_rc;
-        p.kc = kc <= 0 || kc >= nb ? nb : kc;
-        p.nch = (nb + p.kc - 1) / p.kc;
-    } else if (row_bytes * 2 <= kStageTarget) {
-        p.kc = nb;
-        p.nch = 1;
-        p.rc = 32;
-        while (p.rc > 2 && ((long long)p.rc * row_bytes > kStageTarget ||
-                            (long long)((total_rows + p.rc - 1) / p.rc) < sms))
-            p.rc /= 2;
-    } else {
-        p.rc = 2;
-        int nch = (int)((row_bytes * 2 + kStageTarget - 1) / kStageTarget);
-        p.kc = ((nb + nch - 1) / nch + 7) & ~7;
-        p.nch = (nb + p.kc - 1) / p.kc;
-    }
-    p.stage_bytes = stream_stage_bytes(type, p.rc, p.kc);
-    p.stages = kMaxStages;
-    p.smem = stream_smem_bytes(type, nb, p.stages, p.stage_bytes);
-    while (p.stages > 1 && p.smem > kMaxSmem) {
-        --p.stages;
-        p.smem = stream_smem_bytes(type, nb, p.stages, p.stage_bytes);
-    }
-    return p;
+    return plan_stream_tiles(type, nb, total_rows, sms, kStageTarget, kMaxSmem,
+                             g_tile_rc.load(std::memory_order_relaxed), g_tile_kc.load(std::memory_order_relaxed));
 }
 
 // The streaming kernel instantiation for (type, rows per tile).

@@ -954,6 +954,48 @@ __host__ __device__ constexpr int stream_stage_bytes(int type, int rc, int kc) {
     return ((rc * kc * (type == 2 ? 16 : 32) + rc * stream_scale_pitch(kc) * 2 + 16) + 127) & ~127;
 }
 
+// Tile plan of a streaming (one-position) launch. Rows per tile: the largest
+// of 32, 16, 8, 4, 2 whose tile fits one stage of `stage_target` bytes and
+// still gives every SM a tile; rows that do not fit a stage even 2 at a time
+// are cut into chunks. forced_rc (2..32, 0: none) imposes a shape instead:
+// forced_rc rows, chunks of forced_kc blocks (0 or >= nb: whole rows). The
+// ring takes as many stages (<= kMaxStages) as fit `max_smem` with X; smem
+// above max_smem means the shape does not fit at all.
+struct StreamPlan {
+    int rc, kc, nch, stages, stage_bytes, smem;
+};
+inline StreamPlan plan_stream_tiles(int type, int nb, size_t total_rows, int sms, int stage_target, int max_smem,
+                                    int forced_rc, int forced_kc) {
+    const int P = type == 2 ? 16 : 32;
+    const long long row_bytes = (long long)nb * (P + 2);
+    StreamPlan p{};
+    if (forced_rc) {
+        p.rc = forced_rc;
+        p.kc = forced_kc <= 0 || forced_kc >= nb ? nb : forced_kc;
+        p.nch = (nb + p.kc - 1) / p.kc;
+    } else if (row_bytes * 2 <= stage_target) {
+        p.kc = nb;
+        p.nch = 1;
+        p.rc = 32;
+        while (p.rc > 2 && ((long long)p.rc * row_bytes > stage_target ||
+                            (long long)((total_rows + p.rc - 1) / p.rc) < sms))
+            p.rc /= 2;
+    } else {
+        p.rc = 2;
+        const int nch = (int)((row_bytes * 2 + stage_target - 1) / stage_target);
+        p.kc = ((nb + nch - 1) / nch + 7) & ~7;
+        p.nch = (nb + p.kc - 1) / p.kc;
+    }
+    p.stage_bytes = stream_stage_bytes(type, p.rc, p.kc);
+    p.stages = kMaxStages;
+    p.smem = stream_smem_bytes(type, nb, p.stages, p.stage_bytes);
+    while (p.stages > 1 && p.smem > max_smem) {
+        --p.stages;
+        p.smem = stream_smem_bytes(type, nb, p.stages, p.stage_bytes);
+    }
+    return p;
+}
+
 // ---------------------------------------------------------------------------
 // Any number of positions (prefill), CUDA-core path. grid.y tiles the
 // positions by T; X comes from global memory (fp32 for Q8_0 weights, the
