@@ -26,6 +26,7 @@
 // differ from the reference's sequential order by fp32 rounding only.
 #include "neon_cuda.h"
 #include "neon_internal.h"
+#include "neon_attn_layout.h"
 
 namespace neon {
 // epilogue kinds of the one-position matvec kernel (see neon_kernels.cuh)
@@ -473,7 +474,6 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const float* __rest
     }
 }
 
-constexpr int kAttnMaxGroup = 8;  // query heads per KV head in the decode attention
 
 // ---------------------------------------------------------------------------
 // Decode attention in one launch: a thread-block cluster of cs CTAs (8, or 16
@@ -492,10 +492,6 @@ constexpr int kAttnMaxGroup = 8;  // query heads per KV head in the decode atten
 // CTA sums p and p * v over its positions, and CTA 0 adds the partials in rank
 // order: out = (sum p v) / (sum p).
 // ---------------------------------------------------------------------------
-constexpr int kAttnMaxCluster = 16;
-constexpr int kAttnSub = 64;            // cache rows per ring slot
-constexpr int kAttnMaxSlots = 8;
-constexpr int kAttnSmemMax = 200 * 1024;  // dynamic shared memory a slot count may take
 
 __device__ __forceinline__ uint32_t smem_addr_d(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -519,29 +515,7 @@ __device__ __forceinline__ bool mbar_wait_d(uint64_t* bar, uint32_t parity, unsi
     }
 }
 
-struct AttnSmem {  // offsets (floats) into the dynamic shared memory; slots: ring depth
-    int q, sc, ring, co, csum, cmax, bar, total, slots;
-};
-__host__ __device__ inline AttnSmem attn_smem_layout(int group, int hd, int chunk_max, int cs, int slots) {
-    auto up4 = [](int v) { return (v + 3) & ~3; };  // float4-aligned regions
-    auto mx = [](int a, int b) { return a > b ? a : b; };
-    const int pitch = hd + 16;
-    const int parts = kThreads / (hd / 4);
-    AttnSmem l;
-    l.q = 0;
-    l.sc = up4(l.q + group * hd);
-    l.ring = up4(l.sc + group * chunk_max);
-    l.slots = slots;
-    // once the V rows are used, the ring holds the per-part partial sums, and
-    // then (in CTA 0) the cluster's partials
-    const int ring = mx(slots * kAttnSub * pitch, mx(parts * group * hd, cs * group * hd));
-    l.co = l.ring;
-    l.csum = up4(l.ring + ring);
-    l.cmax = up4(l.csum + cs * kAttnMaxGroup);
-    l.bar = up4(l.cmax + cs * kAttnMaxGroup);
-    l.total = l.bar + 2 * slots;  // 8-byte mbarriers
-    return l;
-}
+static_assert(kThreads == kAttnThreads, "the attention layout assumes kThreads threads");
 
 __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const float* __restrict__ q, const float* __restrict__ Kc,
                                                                const float* __restrict__ Vc, const int* __restrict__ d_pos,
