@@ -1,12 +1,8 @@
 // Shared-memory layout of the decode attention kernel (attn_decode_kernel in
 // neon_decode.cu), host and device: the host sizes the launch with it, the
-// kernel places its regions with it, and the CPU tests check it.
+// kernel places its regions with it, and the CPU tests check it (nvcc
+// builds every file that includes it).
 #pragma once
-
-#ifndef __CUDACC__
-#define __host__
-#define __device__
-#endif
 
 constexpr int kAttnThreads = 256;          // threads per CTA
 constexpr int kAttnMaxGroup = 8;           // query heads per KV head
