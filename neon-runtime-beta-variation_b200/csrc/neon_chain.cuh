@@ -69,6 +69,26 @@ struct ChainArgs {
     int x_bytes;             // X region: the largest phase's stream_x_bytes
 };
 
+// Ring of a chain launch: a slot holds the largest phase's stage, the X
+// region the largest phase's X; `max_stages` is how many slots fit beside X in
+// max_smem (0: the chain does not fit). nb[i], rows[i]: phase i's blocks per
+// row and rows (all targets); projection phases only.
+struct ChainRing {
+    int slot_bytes, x_bytes, max_stages;
+};
+inline ChainRing plan_chain_ring(const int* nb, const size_t* rows, int n, int sms, int stage_target, int max_smem,
+                                 int forced_rc, int forced_kc) {
+    ChainRing r{0, 0, 0};
+    for (int i = 0; i < n; ++i) {
+        const StreamPlan p = plan_stream_tiles(2, nb[i], rows[i], sms, stage_target, max_smem, forced_rc, forced_kc);
+        if (p.stage_bytes > r.slot_bytes) r.slot_bytes = p.stage_bytes;
+        const int xb = stream_x_bytes(2, nb[i]);
+        if (xb > r.x_bytes) r.x_bytes = xb;
+    }
+    while (r.max_stages < kChainMaxStages && r.x_bytes + (r.max_stages + 1) * r.slot_bytes <= max_smem) ++r.max_stages;
+    return r;
+}
+
 __device__ __forceinline__ int chain_span_of(const ChainPhase& p, int tile) {
     int s = 0;
 #pragma unroll

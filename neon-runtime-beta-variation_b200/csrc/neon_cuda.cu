@@ -870,7 +870,9 @@ int matvec_chain(const ChainPhaseDesc* ph, int n, const int* d_pos, unsigned int
     DeviceState& ds = g_dev[device];
     ChainArgs c;
     std::memset(&c, 0, sizeof(c));
-    int slot = 0, xb = 0, n_peer = 0;
+    int n_peer = 0, n_proj = 0;
+    int proj_nb[kChainMaxPhases];
+    size_t proj_rows[kChainMaxPhases];
     for (int p = 0; p < n; ++p) {
         const ChainPhaseDesc& d = ph[p];
         if (d.ll_h) {
@@ -930,14 +932,18 @@ int matvec_chain(const ChainPhaseDesc* ph, int n, const int* d_pos, unsigned int
         P.kc = pl.kc;
         P.nch = pl.nch;
         P.rc = pl.rc;
-        slot = std::max(slot, pl.stage_bytes);
-        xb = std::max(xb, stream_x_bytes(NEON_GGML_Q4_0, nb));
+        proj_nb[n_proj] = nb;
+        proj_rows[n_proj++] = total_rows;
     }
+    const ChainRing ring = plan_chain_ring(proj_nb, proj_rows, n_proj, ds.sms, kStageTarget, kMaxSmem,
+                                           g_tile_rc.load(std::memory_order_relaxed),
+                                           g_tile_kc.load(std::memory_order_relaxed));
+    const int slot = ring.slot_bytes, xb = ring.x_bytes;
     // the ring depth that keeps the most weight bytes in flight per SM; the
     // grid is what the SMs hold at once (the barriers need every CTA resident)
     int best_stages = 0, best_occ = 0;
     long long best_bytes = -1;
-    for (int st_n = 1; st_n <= kChainMaxStages && xb + st_n * slot <= kMaxSmem; ++st_n) {
+    for (int st_n = 1; st_n <= ring.max_stages; ++st_n) {
         int occ = chain_occupancy(xb + st_n * slot);
         if (occ < 1) continue;
         occ = std::min(occ, kStreamCtasPerSm);
