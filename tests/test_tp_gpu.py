@@ -4,53 +4,26 @@ sums, and the split decoder against the reference's greedy tokens -- the small
 model's golden generation and, for the Qwen3-0.6B-shaped decoder, the same
 tokens as one GPU and as the reference's own transformer_forward. Skipped on
 a host with fewer than two GPUs."""
-import os
-import signal
-import socket
-import subprocess
-import sys
-
 import numpy as np
 import pytest
 
 import oracle as O
 import synth as S
 from conftest import MODEL_L2_RTOL, load_golden, rel_l2
+from tp_launch import run_tp_worker
 
 pytestmark = pytest.mark.gpu
 torch = pytest.importorskip("torch")
 
-HERE = os.path.dirname(os.path.abspath(__file__))
 QWEN_PROMPT, QWEN_STEPS = 128, 32
-
-
-def _free_port():
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
 
 
 @pytest.fixture(scope="module")
 def tp2(tmp_path_factory):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
-    out = tmp_path_factory.mktemp("tp2") / "rank0.npz"
-    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes", "1", "--nproc-per-node", "2",
-           "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
-           os.path.join(HERE, "tp_gpu_worker.py"), "--out", str(out),
-           "--qwen-prompt", str(QWEN_PROMPT), "--qwen-steps", str(QWEN_STEPS)]
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0", OMP_NUM_THREADS="4")
-    p = subprocess.Popen(cmd, env=env, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, start_new_session=True)
-    try:
-        log, _ = p.communicate(timeout=900)
-    except subprocess.TimeoutExpired:
-        os.killpg(p.pid, signal.SIGTERM)
-        log, _ = p.communicate()
-        pytest.fail("tensor-parallel worker timed out:\n" + log.decode(errors="replace")[-4000:])
-    text = log.decode(errors="replace")
-    assert p.returncode == 0, text[-4000:]
-    print(text[-2000:])
-    return dict(np.load(out))
+    return run_tp_worker(tmp_path_factory.mktemp("tp2") / "rank0.npz", "--qwen-prompt", str(QWEN_PROMPT),
+                         "--qwen-steps", str(QWEN_STEPS))
 
 
 def test_allreduce_bit_exact(tp2):

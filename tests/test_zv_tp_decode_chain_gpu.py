@@ -4,15 +4,11 @@ and the chain's LL-reduce phases add them into the residual inside the same
 launch. Tokens and logits must equal the launch-per-projection split decoder's
 bit for bit. Run after the one-GPU chain test; skipped with fewer than two
 GPUs."""
-import os
-import signal
-import subprocess
-import sys
-
 import numpy as np
 import pytest
 
-from test_tp_gpu import HERE, QWEN_PROMPT, QWEN_STEPS, _free_port
+from test_tp_gpu import QWEN_PROMPT, QWEN_STEPS
+from tp_launch import run_tp_worker
 
 pytestmark = [pytest.mark.gpu, pytest.mark.newest(2)]
 torch = pytest.importorskip("torch")
@@ -22,22 +18,8 @@ torch = pytest.importorskip("torch")
 def chain2(tmp_path_factory):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
-    out = tmp_path_factory.mktemp("tpchain") / "rank0.npz"
-    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes", "1", "--nproc-per-node", "2",
-           "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
-           os.path.join(HERE, "tp_gpu_worker.py"), "--out", str(out), "--chain",
-           "--qwen-prompt", str(QWEN_PROMPT), "--qwen-steps", str(QWEN_STEPS)]
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0", OMP_NUM_THREADS="4")
-    p = subprocess.Popen(cmd, env=env, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, start_new_session=True)
-    try:
-        log, _ = p.communicate(timeout=900)
-    except subprocess.TimeoutExpired:
-        os.killpg(p.pid, signal.SIGTERM)
-        log, _ = p.communicate()
-        pytest.fail("tensor-parallel worker timed out:\n" + log.decode(errors="replace")[-4000:])
-    text = log.decode(errors="replace")
-    assert p.returncode == 0, text[-4000:]
-    return dict(np.load(out))
+    return run_tp_worker(tmp_path_factory.mktemp("tpchain") / "rank0.npz", "--chain", "--qwen-prompt",
+                         str(QWEN_PROMPT), "--qwen-steps", str(QWEN_STEPS))
 
 
 @pytest.mark.parametrize("name", ["tiny", "qwen"])
