@@ -178,8 +178,10 @@ NEON_API uint64_t neon_cuda_launch_count(void);
 /* Allocation-free Q4_0 matvec, for callers that cannot let a library allocate
  * device memory (a server that has reserved all of HBM for its own pools, a
  * framework allocator that holds the free memory, a loop that cannot take
- * cudaMalloc's device-wide synchronisation). Same arguments and results as
- * neon_cuda_matvec on a Q4_0 tensor, but the Q8_0 activations live in a fixed
+ * cudaMalloc's device-wide synchronisation). Same arguments as
+ * neon_cuda_matvec on a Q4_0 tensor; results are bit-identical to its default
+ * multi-position path (seq > 1) and within the matvec tolerance of its
+ * one-position streaming kernel (seq == 1). The Q8_0 activations live in a fixed
  * 1.25 MiB array compiled into the library (held by every GPU that loads it)
  * instead of allocated scratch: seq*cols may not exceed 1,048,576. The first
  * call on a device looks up that array's address; make it before any stream

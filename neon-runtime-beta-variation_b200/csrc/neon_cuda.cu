@@ -784,7 +784,10 @@ int matvec_targets(const neon_proj_target_t* targets, size_t n_targets, const fl
                     ds.xd, ds.xs);
         if (rc) return rc;
     }
-    if (ext && groups.size() > 1) return set_err(NEON_ERR_UNSUPPORTED, "fused epilogues need one launch group");
+    // Targets of different (type, cols) groups -- a Q4_K_M-style model's Q4_K
+    // Q/K with a Q6_K V -- take one launch per group; every launch folds the
+    // same norm into its own X staging and applies each target's own epilogue
+    // (ext->epi / pos_stride are indexed by the target's place in `targets`).
     if (ext && ext->rope_cs && (ext->rope_half < 0 || ext->rope_half > kMaxRopeHalf))
         return set_err(NEON_ERR_UNSUPPORTED, "RoPE epilogue: rope dimension above 256");
     if (ext && ext->peer_mode) {
@@ -1501,9 +1504,12 @@ int noalloc_scratch(int device, unsigned char** base) {
 
 extern "C" int neon_cuda_matvec_q4_0_noalloc(neon_tensor_t W, const float* dX, size_t x_stride, float* dY,
                                              size_t y_stride, size_t seq, void* stream) {
-    if (!W) return set_err(NEON_ERR_INVALID, "null tensor handle");
+    int vrc = validate_tensor(W);
+    if (vrc) return vrc;
     if (W->type != NEON_GGML_Q4_0)
         return set_err(NEON_ERR_UNSUPPORTED, "neon_cuda_matvec_q4_0_noalloc runs Q4_0 tensors only");
+    if (W->device < 0 || W->device >= kMaxDevices) return set_err(NEON_ERR_INVALID, "device index out of range");
+    if (W->cols == 0 || W->rows == 0) return set_err(NEON_ERR_INVALID, "empty tensor");
     if (seq == 0) return NEON_OK;
     if (!dX || !dY) return set_err(NEON_ERR_INVALID, "null X or Y");
     if (seq > 1 && y_stride < W->rows) return set_err(NEON_ERR_INVALID, "y_stride smaller than the tensor's rows");

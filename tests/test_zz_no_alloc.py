@@ -18,6 +18,7 @@ import numpy as np
 import pytest
 
 import neon_cuda as N
+import oracle as O
 import synth as S
 from conftest import MATVEC_RTOL, max_rel_err
 
@@ -36,8 +37,13 @@ def lib():
 
 
 def test_noalloc_matches_allocating_entry_point_on_two_calls(lib):
+    """Two calls in a row through the shared array: each bit-identical to the
+    allocating entry point's default multi-position path (the same quantiser
+    and matvec kernels), and within the per-row bar of the oracle."""
     rows, cols = 1024, 4096
-    dt = N.DeviceTensor(S.q4_0_weights(rows, cols, seed=61), S.GGML_Q4_0, rows, cols)
+    W = S.q4_0_weights(rows, cols, seed=61)
+    dt = N.DeviceTensor(W, S.GGML_Q4_0, rows, cols)
+    N.set_prefill_mma(False)  # the default multi-position path: the CUDA-core kernel
     for call, seq in enumerate((16, 5)):
         X = S.activations(seq, cols, seed=62 + call)
         dx = torch.from_numpy(X).cuda()
@@ -48,8 +54,11 @@ def test_noalloc_matches_allocating_entry_point_on_two_calls(lib):
         assert rc == 0, lib.neon_cuda_last_error()
         dt.matvec(dx, y_alloc, seq=seq)
         torch.cuda.synchronize()
-        err = max_rel_err(y_noalloc.cpu().numpy(), y_alloc.cpu().numpy())
-        assert err <= MATVEC_RTOL, f"call {call + 1}: max rel err {err}"
+        got = y_noalloc.cpu().numpy()
+        assert np.array_equal(got.view(np.uint32), y_alloc.cpu().numpy().view(np.uint32)), f"call {call + 1}"
+        ref = O.proj_all_positions(S.GGML_Q4_0, W, rows, cols, X).reshape(-1)
+        err = max_rel_err(got, ref)
+        assert err <= MATVEC_RTOL, f"call {call + 1}: max rel err {err} against the oracle"
 
 
 def test_noalloc_one_position_and_limits(lib):
@@ -62,7 +71,12 @@ def test_noalloc_one_position_and_limits(lib):
     assert lib.neon_cuda_matvec_q4_0_noalloc(dt.handle, dx.data_ptr(), cols, y0.data_ptr(), rows, 1, None) == 0
     dt.matvec(dx, y1)
     torch.cuda.synchronize()
+    # one position: the allocating entry point streams (a different kernel), so
+    # the two agree within the per-row bar, and both with the oracle
     assert max_rel_err(y0.cpu().numpy(), y1.cpu().numpy()) <= MATVEC_RTOL
+    W = S.q4_0_weights(rows, cols, seed=71)
+    ref = O.proj_all_positions(S.GGML_Q4_0, W, rows, cols, X).reshape(-1)
+    assert max_rel_err(y0.cpu().numpy(), ref) <= MATVEC_RTOL
     # beyond the fixed array: a clear error, nothing launched
     seq = LIMIT // cols + 1
     before = N.launch_count()
