@@ -150,6 +150,9 @@ def parse_args():
     p.add_argument("--tiles", default=None, metavar="RC:KC",
                    help="one-position Q4_0 / Q8_0 tile shape: RC rows per tile, KC blocks per row chunk "
                         "(0 = whole rows); neon_cuda_set_stream_tiles")
+    p.add_argument("--resident", type=int, default=None, metavar="K",
+                   help="one-position Q4_0 / Q8_0 launches that fit shared memory on the resident kernel with K "
+                        "CTAs per SM (0: streaming kernel only); neon_cuda_set_resident (default: the library's)")
     p.add_argument("--batch", type=int, default=1,
                    help="matvec workloads: positions per call; > 1 times the prefill path (one JSON line)")
     p.add_argument("--tile-sweep", action="store_true",
@@ -430,6 +433,8 @@ def run_decode(args):
         N.set_decode_chain(True)
     if getattr(args, "tiles", None):
         N.set_stream_tiles(*(int(v) for v in args.tiles.split(":")))
+    if args.resident is not None:
+        N.set_resident(args.resident)
     N.set_fused_collectives(not args.no_fused_collectives)
     comm = None
     barrier, max_over_ranks = (lambda: None), (lambda v: v)
@@ -594,6 +599,8 @@ def run_neon(args):
         N.set_decode_chain(True)
     if getattr(args, "tiles", None):
         N.set_stream_tiles(*(int(v) for v in args.tiles.split(":")))
+    if getattr(args, "resident", None) is not None:
+        N.set_resident(args.resident)
     dev = torch.device("cuda", local)
 
     host_w = host_rotation(rank, ROTATION)

@@ -381,6 +381,17 @@ NEON_API int neon_cuda_set_decode_chain(int enabled);
  * memory makes the call fail with NEON_ERR_UNSUPPORTED. Process-wide. */
 NEON_API int neon_cuda_set_stream_tiles(int rows_per_tile, int blocks_per_chunk);
 
+/* One-position Q4_0 / Q8_0 launches whose weights fit shared memory (up to a
+ * few MB per SM, decode-sized projections) run on the resident kernel: each
+ * CTA copies its whole contiguous row range into shared memory at start,
+ * before the dependency wait, and lets the next launch start at once, so the
+ * weight streams of consecutive launches overlap. ctas_per_sm sets how many
+ * of one launch's CTAs share an SM (default 2); 0 sends every one-position
+ * launch to the streaming kernel. Results agree with the streaming kernel
+ * within the matvec tolerance (the same block dots, summed in another
+ * order). Process-wide. */
+NEON_API int neon_cuda_set_resident(int ctas_per_sm);
+
 /* Launch option: programmatic dependent launch (PDL) lets a matvec fetch its
  * weights while the previous kernel on the stream finishes; on by default. */
 NEON_API int neon_cuda_set_pdl(int enabled);

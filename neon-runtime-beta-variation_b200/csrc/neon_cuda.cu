@@ -7,6 +7,7 @@
 #include "neon_quant.cuh"
 #include "neon_prefill.cuh"
 #include "neon_chain.cuh"
+#include "neon_resident.cuh"
 
 #include <cuda_runtime.h>
 
@@ -40,10 +41,12 @@ std::atomic<int> g_dq_ring{0};      // neon_cuda_set_dq_ring
 std::atomic<int> g_launch_overlap{0};  // neon_cuda_set_launch_overlap
 std::atomic<int> g_decode_chain{0};    // neon_cuda_set_decode_chain
 std::atomic<int> g_tile_rc{0}, g_tile_kc{0};  // neon_cuda_set_stream_tiles (0: the planner's choice)
+std::atomic<int> g_resident{2};  // neon_cuda_set_resident: CTAs per SM of a resident launch (0: off)
 
 struct DeviceState {
     bool ready = false;
     int sms = 0;
+    int smem_per_sm = 0;  // shared memory of one SM (bytes)
     unsigned int* err = nullptr;  // device error word (g_neon_device_err on this device)
     std::mutex mu;
     // scratch of multi-position Q4_0 calls (activation quants)
@@ -134,6 +137,8 @@ using DqKernel = void (*)(DqArgs);
 DqKernel dq_kernel(int type, int T);
 using DqRingKernel = void (*)(DqRingArgs);
 DqRingKernel dq_ring_kernel(int type, int rpw);
+StreamKernel resident_kernel(int type, int tpg);
+constexpr int kResTpgs[] = {16, 32, 64, 128, 256};
 constexpr int kDqTypes[] = {NEON_GGML_F32, NEON_GGML_F16, NEON_GGML_BF16, NEON_GGML_Q4_1, NEON_GGML_Q5_0,
                             NEON_GGML_Q5_1, NEON_GGML_Q4_K, NEON_GGML_Q5_K, NEON_GGML_Q6_K};
 
@@ -162,10 +167,13 @@ int init_device(int device) {
         return set_err(NEON_ERR_UNSUPPORTED, std::string("device ") + p.name +
                                                  " is not sm_100-class; this library is built for sm_100a only");
     st.sms = p.multiProcessorCount;
+    st.smem_per_sm = (int)p.sharedMemPerMultiprocessor;
     NEON_CUDA_TRY(cudaStreamCreateWithFlags(&st.stream, cudaStreamNonBlocking));
     int rc = NEON_OK;
     for (int t : {NEON_GGML_Q4_0, NEON_GGML_Q8_0})
         for (int r : {2, 4, 8, 16, 32}) rc = rc ? rc : ensure_smem(stream_kernel(t, r), kMaxSmem);
+    for (int t : {NEON_GGML_Q4_0, NEON_GGML_Q8_0})
+        for (int tpg : kResTpgs) rc = rc ? rc : ensure_smem(resident_kernel(t, tpg), kMaxSmem);
     for (int t : kDqTypes)
         for (int T : {1, 2, 4}) rc = rc ? rc : ensure_smem(dq_kernel(t, T), kMaxSmem);
     for (int t : kDqTypes)
@@ -257,9 +265,87 @@ int stream_occupancy(int type, int rc, int smem) {
     return occ;
 }
 
+// The resident kernel instantiation for (type, threads per row group).
+StreamKernel resident_kernel(int type, int tpg) {
+    if (type == NEON_GGML_Q4_0) {
+        switch (tpg) {
+            case 16: return matvec_resident_kernel<NEON_GGML_Q4_0, 16>;
+            case 32: return matvec_resident_kernel<NEON_GGML_Q4_0, 32>;
+            case 64: return matvec_resident_kernel<NEON_GGML_Q4_0, 64>;
+            case 128: return matvec_resident_kernel<NEON_GGML_Q4_0, 128>;
+            default: return matvec_resident_kernel<NEON_GGML_Q4_0, 256>;
+        }
+    }
+    switch (tpg) {
+        case 16: return matvec_resident_kernel<NEON_GGML_Q8_0, 16>;
+        case 32: return matvec_resident_kernel<NEON_GGML_Q8_0, 32>;
+        case 64: return matvec_resident_kernel<NEON_GGML_Q8_0, 64>;
+        case 128: return matvec_resident_kernel<NEON_GGML_Q8_0, 128>;
+        default: return matvec_resident_kernel<NEON_GGML_Q8_0, 256>;
+    }
+}
+
+// One-position targets whose weights fit the resident kernel (all targets in
+// one launch): launched, NEON_OK; 1 when the plan does not apply (nothing
+// launched); an error code otherwise.
+int launch_resident(const std::vector<const neon_proj_target_t*>& t, int type, int nb, const float* dX,
+                    cudaStream_t st, DeviceState& ds, int accumulate, const neon_proj_target_t* base,
+                    const neon_internal::MatvecExt* ext) {
+    const int k = g_resident.load(std::memory_order_relaxed);
+    if (k <= 0 || t.empty() || t.size() > (size_t)kMaxSpans || g_tile_rc.load(std::memory_order_relaxed)) return 1;
+    StreamArgs a;
+    std::memset(&a, 0, sizeof(a));
+    long long rows[kMaxSpans];
+    int tile0[kMaxSpans];
+    for (size_t i = 0; i < t.size(); ++i) rows[i] = (long long)t[i]->W->rows;
+    const long long vrows = res_span_starts(rows, (int)t.size(), tile0);
+    if (vrows > (1LL << 30)) return 1;
+    ResPlan p;
+    if (!matvec_resident_plan(type, nb, (int)vrows, ds.sms, k, ds.smem_per_sm, &p)) return 1;
+    for (size_t i = 0; i < t.size(); ++i) {
+        const neon_proj_target_t* tg = t[i];
+        Span& s = a.span[i];
+        s.qs = tg->W->qs;
+        s.d = tg->W->d;
+        s.y = tg->Y;
+        s.y_stride = (long long)tg->y_stride;
+        s.rows = (int)tg->W->rows;
+        s.tile0 = tile0[i];
+        if (ext && ext->epi) {
+            const size_t j = (size_t)(tg - base);
+            s.epi = ext->epi[j];
+            s.pos_stride = ext->pos_stride ? ext->pos_stride[j] : 0;
+        }
+        if (ext && ext->peer_mode == 1) s.epi = kEpiPeer;
+    }
+    a.x = dX;
+    a.err = ds.err;
+    if (ext) {
+        a.norm_w = ext->norm_w;
+        a.norm_eps = ext->norm_eps;
+        a.d_pos = ext->d_pos;
+        a.rope_cs = ext->rope_cs;
+        a.rope_half = ext->rope_half;
+        a.head_dim = ext->head_dim;
+        a.peer_mode = ext->peer_mode;
+        if (ext->peer_mode) a.peer = ext->peer;
+    }
+    a.x_vec = (reinterpret_cast<uintptr_t>(dX) % 16) == 0;
+    a.accumulate = accumulate;
+    a.n_spans = (int)t.size();
+    a.nb = nb;
+    a.rpc = p.rpc;
+    a.n_vrows = (int)vrows;
+    return launch_n(resident_kernel(type, p.tpg), dim3(p.grid), kStreamThreads, p.smem, st, a);
+}
+
 int launch_stream(const std::vector<const neon_proj_target_t*>& t, int type, int nb, const float* dX,
                   cudaStream_t st, DeviceState& ds, int accumulate, const neon_proj_target_t* base,
                   const neon_internal::MatvecExt* ext) {
+    {
+        const int rrc = launch_resident(t, type, nb, dX, st, ds, accumulate, base, ext);
+        if (rrc != 1) return rrc;
+    }
     size_t total_rows = 0;
     for (auto* tg : t) total_rows += tg->W->rows;
     const StreamPlan p = plan_stream(type, nb, total_rows, ds.sms);
@@ -1034,6 +1120,12 @@ int neon_cuda_set_stream_tiles(int rows_per_tile, int blocks_per_chunk) {
     if (blocks_per_chunk < 0) return set_err(NEON_ERR_INVALID, "blocks per chunk must be >= 0");
     g_tile_kc.store(blocks_per_chunk);
     g_tile_rc.store(rows_per_tile);
+    return NEON_OK;
+}
+
+int neon_cuda_set_resident(int ctas_per_sm) {
+    if (ctas_per_sm < 0 || ctas_per_sm > 8) return set_err(NEON_ERR_INVALID, "CTAs per SM must be 0 (off) .. 8");
+    g_resident.store(ctas_per_sm);
     return NEON_OK;
 }
 

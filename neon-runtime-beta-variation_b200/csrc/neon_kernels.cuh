@@ -338,6 +338,10 @@ struct StreamArgs {
     int head_dim;
     int peer_mode;          // 1: fused collective producer (neon_internal::MatvecExt)
     PeerSet peer;
+    // matvec_resident_kernel only: rows per CTA (even) and the rows of all
+    // spans (each span starting at an even row, span[i].tile0)
+    int rpc;
+    int n_vrows;
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -655,10 +659,11 @@ __device__ __forceinline__ float silu_dev(float x) {
 // span's epilogue; threads t < RC own row row0 + t. `pos` is the token's
 // position, `rcs` its RoPE (cos, sin) row staged in shared memory, `yold` the
 // row's previous output (read ahead of the dot products when accumulating).
+// `t` is the row's place in the tile (by default the calling thread's index).
 __device__ __forceinline__ void stream_epilogue(const StreamArgs& a, const Span& sp, int row0, int RC,
                                                 const float* rowv, unsigned int peer_call, int pos,
-                                                const float2* rcs, float yold) {
-    const int t = threadIdx.x;
+                                                const float2* rcs, float yold, int t = -1) {
+    if (t < 0) t = threadIdx.x;
     if (t >= RC) return;
     const int row = row0 + t;
     if (row >= sp.rows) return;

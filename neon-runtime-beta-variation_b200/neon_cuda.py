@@ -102,6 +102,7 @@ C_ENTRY_POINTS = (
     "neon_cuda_set_launch_overlap",
     "neon_cuda_set_decode_chain",
     "neon_cuda_set_stream_tiles",
+    "neon_cuda_set_resident",
 )
 
 _sz = C.c_size_t
@@ -168,6 +169,7 @@ def load(path: str | None = None) -> C.CDLL:
         L.neon_cuda_set_launch_overlap.argtypes = [C.c_int]
         L.neon_cuda_set_decode_chain.argtypes = [C.c_int]
         L.neon_cuda_set_stream_tiles.argtypes = [C.c_int, C.c_int]
+        L.neon_cuda_set_resident.argtypes = [C.c_int]
         L.neon_cuda_matvec_q4_0_noalloc.argtypes = [_vp, _vp, _sz, _vp, _sz, _sz, _vp]
         L.neon_cuda_model_create.argtypes = [C.POINTER(_ModelConfig), C.POINTER(_vp)]
         L.neon_cuda_model_set_tensor.argtypes = [_vp, C.c_int, C.c_int, _vp, _sz, C.c_int, _sz, _sz]
@@ -247,6 +249,13 @@ def set_stream_tiles(rows_per_tile: int = 0, blocks_per_chunk: int = 0) -> None:
     blocks per row chunk; 0 = whole rows); (0, 0) is the built-in planner.
     For tuning sweeps; process-wide."""
     _check(load().neon_cuda_set_stream_tiles(int(rows_per_tile), int(blocks_per_chunk)))
+
+
+def set_resident(ctas_per_sm: int = 2) -> None:
+    """One-position Q4_0 / Q8_0 launches that fit shared memory run on the
+    resident kernel with this many CTAs per SM (default 2); 0 sends them all
+    to the streaming kernel. Process-wide."""
+    _check(load().neon_cuda_set_resident(int(ctas_per_sm)))
 
 
 def set_pdl(enabled: bool) -> None:
