@@ -141,9 +141,6 @@ def parse_args():
     p.add_argument("--dq-ring", action="store_true",
                    help="one-position calls of the dequantising types on the bulk-copy ring kernel "
                         "(neon_cuda_set_dq_ring)")
-    p.add_argument("--launch-overlap", action="store_true",
-                   help="one-position Q4_0 / Q8_0 launches sized to leave room for the next launch's CTAs "
-                        "(neon_cuda_set_launch_overlap)")
     p.add_argument("--decode-chain", action="store_true",
                    help="decode steps with the projections between attention launches as one launch "
                         "(neon_cuda_set_decode_chain)")
@@ -427,8 +424,6 @@ def run_decode(args):
         N.set_prefill_mma(True)
     if getattr(args, "dq_ring", False):
         N.set_dq_ring(True)
-    if getattr(args, "launch_overlap", False):
-        N.set_launch_overlap(True)
     if getattr(args, "decode_chain", False):
         N.set_decode_chain(True)
     if getattr(args, "tiles", None):
@@ -466,9 +461,10 @@ def run_decode(args):
                 "steps": res["generated"], "warmup": 0, "ms_per_step": res["ms_per_token"], "higher_is_better": True,
                 "scaling": "strong", "vs_baseline": None, "dtype": "int8/fp32 (q4_0 x q8_0 dp4a, fp32 scales)",
                 "data": "synthetic", "config": {"workload": res["workload"], "parallelism": res["parallelism"],
-                                                "variants": [v for v, on in (("launch_overlap", args.launch_overlap),
-                                                                             ("decode_chain", args.decode_chain),
-                                                                             ("prefill_mma", args.prefill_mma)) if on]},
+                                                "variants": [v for v, on in (("decode_chain", args.decode_chain),
+                                                                             ("prefill_mma", args.prefill_mma)) if on]
+                                                + ([f"resident {args.resident}"] if args.resident is not None
+                                                   else [])},
                 "e2e": {"value": res["e2e_tokens_per_s"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 4, "api": res["e2e"]},
                 "load_s": res["load_s"], "roofline": decode_roofline(dict(res), cfg, world)["hbm"],
@@ -593,8 +589,6 @@ def run_neon(args):
         N.set_prefill_mma(True)
     if getattr(args, "dq_ring", False):
         N.set_dq_ring(True)
-    if getattr(args, "launch_overlap", False):
-        N.set_launch_overlap(True)
     if getattr(args, "decode_chain", False):
         N.set_decode_chain(True)
     if getattr(args, "tiles", None):
@@ -740,10 +734,10 @@ def run_neon(args):
             "dtype": compute_dtype(TYPE),
             "data": "synthetic",
             "config": {**workload_config(), "parallelism": f"dp{world} (independent rotations)",
-                       "variants": [v for v, on in (("launch_overlap", args.launch_overlap), ("dq_ring", args.dq_ring),
-                                                    ("prefill_mma", args.prefill_mma),
+                       "variants": [v for v, on in (("dq_ring", args.dq_ring), ("prefill_mma", args.prefill_mma),
                                                     ("decode_chain", args.decode_chain)) if on]
-                       + ([f"tiles {args.tiles}"] if args.tiles else []),
+                       + ([f"tiles {args.tiles}"] if args.tiles else [])
+                       + ([f"resident {args.resident}"] if args.resident is not None else []),
                        "launch": "CUDA graph of 1024 PDL launches per step"},
             "e2e": {"value": round(e2e_value, 2), "unit": UNIT,
                     "h2d_bytes_per_step": CALLS_PER_STEP * COLS * 4,
@@ -910,8 +904,9 @@ TILE_SWEEP_WORKLOADS = ["q4_0_4096x4096", "q4_0_28672x8192", "q4_0_8192x28672", 
 def run_tile_sweep(args):
     """One JSON line per (workload, tile shape) of the one-position Q4_0 / Q8_0
     kernel, timed as the type sweep times a workload: the planner's choice
-    (with and without launch overlap), then every forced shape of
-    TILE_SWEEP_SHAPES that fits shared memory (neon_cuda_set_stream_tiles)."""
+    (resident kernel where it applies, and the streaming kernel alone), then
+    every forced shape of TILE_SWEEP_SHAPES that fits shared memory
+    (neon_cuda_set_stream_tiles; the streaming kernel)."""
     import torch
 
     import neon_cuda as N
@@ -925,13 +920,13 @@ def run_tile_sweep(args):
         select_workload(name)
         nb = COLS // 32
         tensors = [N.DeviceTensor(w, TYPE, ROWS, COLS) for w in host_rotation(0, ROTATION)]
-        runs = [("planner", 0, 0, False), ("planner + launch overlap", 0, 0, True)]
+        runs = [("planner", 0, 0, 2), ("planner, streaming kernel only", 0, 0, 0)]
         for rc, nch in TILE_SWEEP_SHAPES:
             kc = 0 if nch == 0 else ((nb + nch - 1) // nch + 7) // 8 * 8
-            runs.append((f"rc {rc}, kc {kc or nb}", rc, kc, False))
-        for label, rc, kc, overlap in runs:
+            runs.append((f"rc {rc}, kc {kc or nb}", rc, kc, 0))
+        for label, rc, kc, resident in runs:
             N.set_stream_tiles(rc, kc)
-            N.set_launch_overlap(overlap)
+            N.set_resident(resident)
             line = {"workload": name, "tiles": label, "rows": ROWS, "cols": COLS, "unit": UNIT, "steps": K,
                     "warmup": W, "peak": peak, "peak_source": peak_kind}
             try:
@@ -944,7 +939,7 @@ def run_tile_sweep(args):
         torch.cuda.synchronize()
         torch.cuda.empty_cache()
     N.set_stream_tiles(0, 0)
-    N.set_launch_overlap(False)
+    N.set_resident(2)
 
 
 def main():

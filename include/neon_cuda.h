@@ -356,13 +356,6 @@ NEON_API int neon_cuda_set_prefill_mma(int enabled);
  * until a GPU run has validated it; the switch is process-wide. */
 NEON_API int neon_cuda_set_dq_ring(int enabled);
 
-/* Size one-position Q4_0 / Q8_0 launches to half the CTAs an SM holds, so the
- * next launch on the stream finds room on every SM and streams its weights
- * (before its dependency wait) while this one runs, instead of after this
- * one's CTAs leave. Results are unchanged (only the grid and ring depth
- * change). Off by default until a GPU run has measured it; process-wide. */
-NEON_API int neon_cuda_set_launch_overlap(int enabled);
-
 /* Decode step (neon_cuda_model_*, all projections Q4_0): the four projections
  * between two attention launches -- attn_output, ffn gate/up, ffn_down and the
  * next layer's Q/K/V -- as the phases of one launch separated by grid

@@ -38,7 +38,6 @@ std::atomic<uint64_t> g_launches{0};
 std::atomic<int> g_pdl{1};
 std::atomic<int> g_prefill_mma{0};  // neon_cuda_set_prefill_mma
 std::atomic<int> g_dq_ring{0};      // neon_cuda_set_dq_ring
-std::atomic<int> g_launch_overlap{0};  // neon_cuda_set_launch_overlap
 std::atomic<int> g_decode_chain{0};    // neon_cuda_set_decode_chain
 std::atomic<int> g_tile_rc{0}, g_tile_kc{0};  // neon_cuda_set_stream_tiles (0: the planner's choice)
 std::atomic<int> g_resident{2};  // neon_cuda_set_resident: CTAs per SM of a resident launch (0: off)
@@ -398,24 +397,17 @@ int launch_stream(const std::vector<const neon_proj_target_t*>& t, int type, int
         a.accumulate = accumulate;
         // Pick the ring depth that keeps the most weight bytes in flight per
         // SM (resident CTAs x stages x stage bytes), then size the grid to what
-        // is resident: a CTA that starts late repays the X staging. With launch
-        // overlap, the grid takes half the CTAs an SM holds, so the next
-        // launch's CTAs are resident (and stream their weights) while this one
-        // runs; when no depth leaves room for two, the usual choice.
+        // is resident: a CTA that starts late repays the X staging.
         int best_stages = 1, best_occ = 1;
         long long best_bytes = -1;
-        for (int pass = g_launch_overlap.load(std::memory_order_relaxed) ? 0 : 1; pass < 2 && best_bytes < 0; ++pass) {
-            for (int st_n = 1; st_n <= p.stages; ++st_n) {
-                const int sm_bytes = stream_smem_bytes(type, nb, st_n, p.stage_bytes);
-                int occ = std::min(stream_occupancy(type, p.rc, sm_bytes), kStreamCtasPerSm);
-                if (pass == 0) occ /= 2;
-                if (occ < 1) continue;
-                const long long inflight = (long long)occ * st_n * p.stage_bytes;
-                if (inflight >= best_bytes) {
-                    best_bytes = inflight;
-                    best_stages = st_n;
-                    best_occ = occ;
-                }
+        for (int st_n = 1; st_n <= p.stages; ++st_n) {
+            const int sm_bytes = stream_smem_bytes(type, nb, st_n, p.stage_bytes);
+            const int occ = std::min(stream_occupancy(type, p.rc, sm_bytes), kStreamCtasPerSm);
+            const long long inflight = (long long)occ * st_n * p.stage_bytes;
+            if (inflight >= best_bytes) {
+                best_bytes = inflight;
+                best_stages = st_n;
+                best_occ = occ;
             }
         }
         const int grid = std::min(tiles, ds.sms * best_occ);
@@ -1100,11 +1092,6 @@ int neon_cuda_set_prefill_mma(int enabled) {
 
 int neon_cuda_set_dq_ring(int enabled) {
     g_dq_ring.store(enabled ? 1 : 0);
-    return NEON_OK;
-}
-
-int neon_cuda_set_launch_overlap(int enabled) {
-    g_launch_overlap.store(enabled ? 1 : 0);
     return NEON_OK;
 }
 

@@ -99,7 +99,6 @@ C_ENTRY_POINTS = (
     "neon_cuda_set_pdl",
     "neon_cuda_set_prefill_mma",
     "neon_cuda_set_dq_ring",
-    "neon_cuda_set_launch_overlap",
     "neon_cuda_set_decode_chain",
     "neon_cuda_set_stream_tiles",
     "neon_cuda_set_resident",
@@ -166,7 +165,6 @@ def load(path: str | None = None) -> C.CDLL:
         L.neon_cuda_set_pdl.argtypes = [C.c_int]
         L.neon_cuda_set_prefill_mma.argtypes = [C.c_int]
         L.neon_cuda_set_dq_ring.argtypes = [C.c_int]
-        L.neon_cuda_set_launch_overlap.argtypes = [C.c_int]
         L.neon_cuda_set_decode_chain.argtypes = [C.c_int]
         L.neon_cuda_set_stream_tiles.argtypes = [C.c_int, C.c_int]
         L.neon_cuda_set_resident.argtypes = [C.c_int]
@@ -228,13 +226,6 @@ def set_dq_ring(enabled: bool) -> None:
     kernel (several row tiles in flight per CTA) instead of the register-buffer
     kernel; process-wide, off by default."""
     _check(load().neon_cuda_set_dq_ring(1 if enabled else 0))
-
-
-def set_launch_overlap(enabled: bool) -> None:
-    """One-position Q4_0 / Q8_0 launches sized to half the CTAs an SM holds, so
-    the next launch's CTAs stream their weights while this one runs;
-    process-wide, off by default."""
-    _check(load().neon_cuda_set_launch_overlap(1 if enabled else 0))
 
 
 def set_decode_chain(enabled: bool) -> None:
