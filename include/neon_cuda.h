@@ -379,7 +379,7 @@ NEON_API int neon_cuda_set_stream_tiles(int rows_per_tile, int blocks_per_chunk)
  * CTA copies its whole contiguous row range into shared memory at start,
  * before the dependency wait, and lets the next launch start at once, so the
  * weight streams of consecutive launches overlap. ctas_per_sm sets how many
- * of one launch's CTAs share an SM (default 2); 0 sends every one-position
+ * of one launch's CTAs share an SM (default 1); 0 sends every one-position
  * launch to the streaming kernel. Results agree with the streaming kernel
  * within the matvec tolerance (the same block dots, summed in another
  * order). Process-wide. */

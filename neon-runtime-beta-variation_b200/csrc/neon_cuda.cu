@@ -40,13 +40,14 @@ std::atomic<int> g_prefill_mma{0};  // neon_cuda_set_prefill_mma
 std::atomic<int> g_dq_ring{0};      // neon_cuda_set_dq_ring
 std::atomic<int> g_decode_chain{0};    // neon_cuda_set_decode_chain
 std::atomic<int> g_tile_rc{0}, g_tile_kc{0};  // neon_cuda_set_stream_tiles (0: the planner's choice)
-std::atomic<int> g_resident{2};  // neon_cuda_set_resident: CTAs per SM of a resident launch (0: off)
+std::atomic<int> g_resident{1};  // neon_cuda_set_resident: CTAs per SM of a resident launch (0: off)
 
 struct DeviceState {
     bool ready = false;
     int sms = 0;
     int smem_per_sm = 0;  // shared memory of one SM (bytes)
     unsigned int* err = nullptr;  // device error word (g_neon_device_err on this device)
+    unsigned int* err_host = nullptr;  // pinned copy of the error word, read back by the host-buffer calls
     std::mutex mu;
     // scratch of multi-position Q4_0 calls (activation quants)
     int8_t* xq = nullptr;
@@ -182,6 +183,10 @@ int init_device(int device) {
     void* err = nullptr;
     NEON_CUDA_TRY(cudaGetSymbolAddress(&err, g_neon_device_err));
     st.err = static_cast<unsigned int*>(err);
+    void* eh = nullptr;
+    NEON_CUDA_TRY(cudaHostAlloc(&eh, sizeof(unsigned int), cudaHostAllocPortable));
+    st.err_host = static_cast<unsigned int*>(eh);
+    *st.err_host = 0;
     st.ready = true;
     return NEON_OK;
 }
@@ -1509,8 +1514,14 @@ int neon_cuda_proj_all_positions_multi(const neon_proj_target_t* targets, size_t
     if (rc) return rc;
     for (size_t i = 0; i < n_targets; ++i)
         NEON_CUDA_TRY(cudaMemcpyAsync(targets[i].Y, dt[i].Y, y_len[i] * 4, cudaMemcpyDeviceToHost, st));
+    // the device error word comes back with Y: one synchronisation for both
+    NEON_CUDA_TRY(cudaMemcpyAsync(ds.err_host, ds.err, sizeof(unsigned int), cudaMemcpyDeviceToHost, st));
     NEON_CUDA_TRY(cudaStreamSynchronize(st));
-    return check_device_err(device);
+    if (*ds.err_host) {
+        *ds.err_host = 0;
+        return check_device_err(device);  // clears the device word and reports the timeout
+    }
+    return NEON_OK;
 }
 
 int neon_cuda_proj_all_positions(neon_tensor_t W, const float* hX, size_t x_stride, float* hY, size_t y_stride,

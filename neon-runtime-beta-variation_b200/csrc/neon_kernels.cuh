@@ -140,7 +140,7 @@ __device__ __forceinline__ void quantize_block_thread(const float* x, uint32_t q
 #pragma unroll
     for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(x[j]));
     d = __fdiv_rn(amax, 127.0f);
-    const float id = d > 0.f ? __fdiv_rn(1.0f, d) : 0.f;
+    const float id = d > 0.f ? __frcp_rn(d) : 0.f;  // 1/d correctly rounded, as 1.0f / d
     int s = 0;
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
@@ -174,7 +174,7 @@ __global__ void __launch_bounds__(kThreads) quantize_q8_0_kernel(
 #pragma unroll
         for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
         const float d = __fdiv_rn(amax, 127.0f);
-        const float id = d > 0.f ? __fdiv_rn(1.0f, d) : 0.f;
+        const float id = d > 0.f ? __frcp_rn(d) : 0.f;  // 1/d correctly rounded, as 1.0f / d
         const int v = q8_round_clamp(__fmul_rn(xv, id));
         q_out[(long long)t * nb * 32 + (long long)b * 32 + lane] = (int8_t)v;
         if (sums) {
@@ -236,17 +236,45 @@ __device__ __forceinline__ float warp_sum(float v) {
 // -> j+16) against 32 int8 quants whose sum is qsum. Nibbles are dotted
 // unsigned and 8*qsum is subtracted, giving sum((nib-8)*q) exactly
 // (block_isum_scalar, rawllm_forward.hpp:384-392).
+// Two independent accumulators (low and high nibbles) halve the dependent
+// dp4a chain; integer sums are exact, so the order does not matter.
 __device__ __forceinline__ int q4_block_isum(const uint4 w, const uint4 x0, const uint4 x1, int qsum) {
-    int acc = 0;
-    acc = __dp4a((int)(w.x & 0x0F0F0F0Fu), (int)x0.x, acc);
-    acc = __dp4a((int)(w.y & 0x0F0F0F0Fu), (int)x0.y, acc);
-    acc = __dp4a((int)(w.z & 0x0F0F0F0Fu), (int)x0.z, acc);
-    acc = __dp4a((int)(w.w & 0x0F0F0F0Fu), (int)x0.w, acc);
-    acc = __dp4a((int)((w.x >> 4) & 0x0F0F0F0Fu), (int)x1.x, acc);
-    acc = __dp4a((int)((w.y >> 4) & 0x0F0F0F0Fu), (int)x1.y, acc);
-    acc = __dp4a((int)((w.z >> 4) & 0x0F0F0F0Fu), (int)x1.z, acc);
-    acc = __dp4a((int)((w.w >> 4) & 0x0F0F0F0Fu), (int)x1.w, acc);
-    return acc - 8 * qsum;
+    int lo = 0, hi = 0;
+    lo = __dp4a((int)(w.x & 0x0F0F0F0Fu), (int)x0.x, lo);
+    hi = __dp4a((int)((w.x >> 4) & 0x0F0F0F0Fu), (int)x1.x, hi);
+    lo = __dp4a((int)(w.y & 0x0F0F0F0Fu), (int)x0.y, lo);
+    hi = __dp4a((int)((w.y >> 4) & 0x0F0F0F0Fu), (int)x1.y, hi);
+    lo = __dp4a((int)(w.z & 0x0F0F0F0Fu), (int)x0.z, lo);
+    hi = __dp4a((int)((w.z >> 4) & 0x0F0F0F0Fu), (int)x1.z, hi);
+    lo = __dp4a((int)(w.w & 0x0F0F0F0Fu), (int)x0.w, lo);
+    hi = __dp4a((int)((w.w >> 4) & 0x0F0F0F0Fu), (int)x1.w, hi);
+    return (lo + hi) - 8 * qsum;
+}
+
+// dp4a of four unsigned bytes of a with four signed bytes of b, plus c.
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// The same exact block sum as q4_block_isum, as a float, with fewer integer
+// operations: the high nibbles are dotted in place (16 x their value), so
+// 16 * isum = 16 * lo + hi16 - 128 * qsum, and `bias` = 0x4B400000 - 128 * qsum
+// folds the qsum term and the float conversion's 1.5 * 2^23 bias into one
+// add. |16 * isum| < 2^22, so the conversion is exact, and so is the scaling
+// by 1/16: the result equals (float)q4_block_isum(w, x0, x1, qsum).
+__device__ __forceinline__ float q4_block_dot16(const uint4 w, const uint4 x0, const uint4 x1, int bias) {
+    int lo = 0, hi = 0;
+    lo = dp4a_us(w.x & 0x0F0F0F0Fu, x0.x, lo);
+    hi = dp4a_us(w.x & 0xF0F0F0F0u, x1.x, hi);
+    lo = dp4a_us(w.y & 0x0F0F0F0Fu, x0.y, lo);
+    hi = dp4a_us(w.y & 0xF0F0F0F0u, x1.y, hi);
+    lo = dp4a_us(w.z & 0x0F0F0F0Fu, x0.z, lo);
+    hi = dp4a_us(w.z & 0xF0F0F0F0u, x1.z, hi);
+    lo = dp4a_us(w.w & 0x0F0F0F0Fu, x0.w, lo);
+    hi = dp4a_us(w.w & 0xF0F0F0F0u, x1.w, hi);
+    return __fmul_rn(__int_as_float(lo * 16 + hi + bias) - 12582912.0f, 0.0625f);
 }
 
 // Exact int -> float for |v| < 2^22 without the conversion pipe: the bits of
@@ -495,7 +523,7 @@ __device__ __forceinline__ void quantize_store_q8(float (&xv)[32 / TPB], bool ac
 #pragma unroll
     for (int o = 1; o < TPB; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
     const float d = __fdiv_rn(amax, 127.0f);
-    const float id = d > 0.f ? __fdiv_rn(1.0f, d) : 0.f;
+    const float id = d > 0.f ? __frcp_rn(d) : 0.f;  // 1/d correctly rounded, as 1.0f / d
     uint32_t q[EPT / 4];
     int s = 0;
 #pragma unroll

@@ -17,14 +17,15 @@
 // of the following launches:
 //   1. at CTA start, one thread issues ONE bulk copy per span piece for the
 //      payload and one for the scales (weights are never written by earlier
-//      kernels, so this happens before the dependency wait), and the CTA lets
-//      the next launch start at once;
-//   2. the next launch's CTAs become resident beside this one and start their
+//      kernels, so this happens before the dependency wait);
+//   2. after the wait the CTA stages X (Q4_0: bit-exact Q8_0 records, RMSNorm
+//      folded as in the streaming kernel; Q8_0: fp32) and lets the next
+//      launch start: its CTAs become resident beside this one and start their
 //      own copies, so the weight stream of launch N+1 runs while launch N
-//      waits, stages X and computes;
-//   3. after the wait the CTA stages X (Q4_0: bit-exact Q8_0 records, RMSNorm
-//      folded as in the streaming kernel; Q8_0: fp32), waits for its weights
-//      (already there in steady state), computes and runs the epilogues.
+//      computes and N+1 waits (triggering before the X loads made them queue
+//      behind the next launch's weight traffic);
+//   3. the CTA waits for its weights (already there in steady state),
+//      computes and runs the epilogues.
 // The host sizes the CTAs (matvec_resident_plan) so that two launches fit on
 // an SM at once; larger matrices take the streaming kernel.
 //
@@ -32,9 +33,8 @@
 // (g, s) owns the CTA's local rows g, g + G, g + 2G, ... (at most
 // kResRowsPerThread) and the blocks s, s + TPG, ... of each: one
 // shared-memory read of an X block serves all its rows. A row's partial sums
-// meet by shuffles (and, for TPG > 32, through shared memory). A row's sum is
-// formed the same way whatever CTA owns it, so the grid size does not change
-// results.
+// meet by shuffles (and, for TPG > 32, through shared memory). For a given
+// TPG a row's sum is formed the same way whatever CTA owns it.
 //
 // Shared memory: X (the streaming kernel's layout), then the payload of the
 // CTA's rows (local row lr at lr * nb * P), then the scale windows (a
@@ -151,9 +151,11 @@ __global__ void __launch_bounds__(kStreamThreads, 4) matvec_resident_kernel(cons
     constexpr int LPG = TPG >= 32 ? 32 : TPG;
     constexpr int MAXR = kResRowsPerThread;
     constexpr int MAXROWS = G * MAXR;
+    static_assert(MAXR == 8 && LPG >= 8, "the row butterfly takes 8 rows per thread and 8 or more lanes per group");
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ float rowres[MAXROWS];
     __shared__ float red[WPG > 1 ? MAXROWS * WPG : 1];
+    __shared__ int rowsb[MAXROWS];  // scale index of (local row, block 0); 0 for span padding
     __shared__ ResSeg seg[kResMaxSegs];
     __shared__ int n_seg;
     __shared__ float2 rcs[kMaxRopeHalf];
@@ -165,7 +167,7 @@ __global__ void __launch_bounds__(kStreamThreads, 4) matvec_resident_kernel(cons
     unsigned char* pay = smem + L.pay;
     uint16_t* sc = reinterpret_cast<uint16_t*>(smem + L.sc);
     uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L.bar);
-    const int tid = threadIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31;
     const int v0 = (int)blockIdx.x * a.rpc;
     const int nloc = min(a.rpc, a.n_vrows - v0);
 
@@ -186,26 +188,33 @@ __global__ void __launch_bounds__(kStreamThreads, 4) matvec_resident_kernel(cons
             bulk_g2s(sc + c.sc_dst_half, sp.d + c.sc_src_half, c.sc_bytes, bar);
         }
     }
-    // the weights are on their way: let the next launch's CTAs in (they start
-    // their own copies), then wait for the kernel before this one
-    pdl_launch_dependents();
+    // Everything that depends on the launch's parameters only, before the
+    // wait: each local row's scale index, and this thread's epilogue piece
+    // (thread tid runs the epilogue of local row tid).
+    int eseg = -1;
+    if (tid < MAXROWS) {
+        int sbv = 0;
+        for (int k = 0; k < n_seg; ++k)
+            if (tid >= seg[k].lr0 && tid < seg[k].lr0 + seg[k].n) {
+                sbv = seg[k].sb + tid * nb;
+                eseg = k;
+            }
+        rowsb[tid] = sbv;
+    }
+    const float* yold_p = nullptr;  // the accumulate epilogue's y[row]
+    if (eseg >= 0) {
+        const Span& sp = a.span[seg[eseg].span];
+        if (a.accumulate && sp.epi == kEpiStore) yold_p = sp.y + seg[eseg].row0 + tid - seg[eseg].lr0;
+    }
+    const bool rope_row = a.rope_cs && tid < a.rope_half;
     pdl_wait();
 
+    // what the kernel before may have written: the position, the collective's
+    // call count and y[row]; loaded now, used after the X staging
     const unsigned int peer_call =
         a.peer_mode ? *reinterpret_cast<volatile const unsigned int*>(a.peer.calls) + 1u : 0u;
     const int pos = a.d_pos ? *a.d_pos : 0;
-    if (a.rope_cs && tid < a.rope_half) prefetch_l1(a.rope_cs + (long long)pos * a.rope_half + tid);
-    // this thread's epilogue row (local row tid) and, when accumulating, its old value
-    int eseg = -1;
-    float yold = 0.f;
-    if (tid < nloc) {
-        for (int k = 0; k < n_seg; ++k)
-            if (tid >= seg[k].lr0 && tid < seg[k].lr0 + seg[k].n) eseg = k;
-        if (eseg >= 0) {
-            const Span& sp = a.span[seg[eseg].span];
-            if (a.accumulate && sp.epi == kEpiStore) yold = sp.y[seg[eseg].row0 + tid - seg[eseg].lr0];
-        }
-    }
+    const float yold = yold_p ? *yold_p : 0.f;
 
     // X, staged once per CTA (normalised first when asked)
     const int tpb = TYPE == 2 ? kStreamThreads / nb : 0;
@@ -227,19 +236,25 @@ __global__ void __launch_bounds__(kStreamThreads, 4) matvec_resident_kernel(cons
             xs[(i >> 5) * kQ8Pitch + (i & 31)] = v;
         }
     }
-    if (a.rope_cs && tid < a.rope_half) rcs[tid] = a.rope_cs[(long long)pos * a.rope_half + tid];
+    // X is read: the next launch's CTAs may take their places now and start
+    // their copies (earlier, their weight traffic would delay these X loads)
+    pdl_launch_dependents();
     const bool ok = mbar_wait(bar, 0, a.err);
-    if (__syncthreads_or(!ok)) return;  // also: X and the RoPE row are staged
+    if (__syncthreads_or(!ok)) return;  // also: X, the RoPE row and rowsb are in place
 
-    // dot products
+    // Dot products, all MAXR rows of the thread without branches (a row past
+    // nloc repeats the last row; its sum is not stored), so the compiler
+    // interleaves the rows' independent chains.
+    // the position's RoPE row: loaded here, in shared memory before the epilogue
+    float2 rope_v = make_float2(0.f, 0.f);
+    if (rope_row) rope_v = a.rope_cs[(long long)pos * a.rope_half + tid];
     const int g = tid / TPG, s = tid % TPG;
-    int sb[MAXR];
+    int wofs[MAXR], sofs[MAXR];
 #pragma unroll
     for (int i = 0; i < MAXR; ++i) {
-        const int lr = g + i * G;
-        sb[i] = 0;  // a row of no span (span padding): in-bounds reads, result unused
-        for (int k = 0; k < n_seg; ++k)
-            if (lr >= seg[k].lr0 && lr < seg[k].lr0 + seg[k].n) sb[i] = seg[k].sb + lr * nb;
+        const int lr = min(g + i * G, nloc - 1);
+        wofs[i] = lr * nb;
+        sofs[i] = rowsb[lr];
     }
     float part[MAXR];
 #pragma unroll
@@ -250,14 +265,12 @@ __global__ void __launch_bounds__(kStreamThreads, 4) matvec_resident_kernel(cons
             const uint4 x0 = r4[0], x1 = r4[1];
             const uint2 xm = *reinterpret_cast<const uint2*>(r4 + 2);
             const float xd = __uint_as_float(xm.x);
+            const int bias = 0x4B400000 - 128 * (int)xm.y;
 #pragma unroll
             for (int i = 0; i < MAXR; ++i) {
-                const int lr = g + i * G;
-                if (lr < nloc) {
-                    const float wd = fp16_bits_to_f32(sc[sb[i] + b]);
-                    const uint4 w = *reinterpret_cast<const uint4*>(pay + ((size_t)lr * nb + b) * P);
-                    part[i] = fmaf(wd * xd, small_int_to_f32(q4_block_isum(w, x0, x1, (int)xm.y)), part[i]);
-                }
+                const float wd = fp16_bits_to_f32(sc[sofs[i] + b]);
+                const uint4 w = *reinterpret_cast<const uint4*>(pay + (size_t)(wofs[i] + b) * P);
+                part[i] = fmaf(wd * xd, q4_block_dot16(w, x0, x1, bias), part[i]);
             }
         } else {
             const ulonglong2* xv2 =
@@ -271,32 +284,45 @@ __global__ void __launch_bounds__(kStreamThreads, 4) matvec_resident_kernel(cons
             }
 #pragma unroll
             for (int i = 0; i < MAXR; ++i) {
-                const int lr = g + i * G;
-                if (lr < nloc) {
-                    const float wd = fp16_bits_to_f32(sc[sb[i] + b]);
-                    const uint4* w4 = reinterpret_cast<const uint4*>(pay + ((size_t)lr * nb + b) * P);
-                    part[i] = fmaf(wd, q8_block_dot_x2(w4[0], w4[1], xv), part[i]);
-                }
+                const float wd = fp16_bits_to_f32(sc[sofs[i] + b]);
+                const uint4* w4 = reinterpret_cast<const uint4*>(pay + (size_t)(wofs[i] + b) * P);
+                part[i] = fmaf(wd, q8_block_dot_x2(w4[0], w4[1], xv), part[i]);
             }
         }
     }
-    // row sums: shuffles over the group's lanes (warp-uniform condition: the
-    // warp's first group decides; a lane past nloc adds zeros)
-    const int gw0 = TPG >= 32 ? g : (tid & ~31) / TPG;
+    // Row sums over the group's LPG lanes by a transposing butterfly: three
+    // exchange steps each hand half of the remaining rows to the partner lane
+    // (8 -> 4 -> 2 -> 1 rows per lane), then plain steps finish the one row a
+    // lane keeps -- 9 shuffles for 8 rows instead of 40. Every row's sum is the
+    // same tree over the same lanes, whatever its place in the CTA.
+    float v4[4], v2[2];
+    const bool h4 = lane & (LPG / 2), h2 = lane & (LPG / 4), h1 = lane & (LPG / 8);
 #pragma unroll
-    for (int i = 0; i < MAXR; ++i) {
-        if (gw0 + i * G < nloc) {
-            float v = part[i];
+    for (int j = 0; j < 4; ++j) {
+        const float r = __shfl_xor_sync(0xffffffffu, h4 ? part[j] : part[j + 4], LPG / 2);
+        v4[j] = (h4 ? part[j + 4] : part[j]) + r;
+    }
 #pragma unroll
-            for (int o = LPG / 2; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-            const int lr = g + i * G;
-            if (WPG == 1) {
-                if (s == 0 && lr < nloc) rowres[lr] = v;
-            } else if ((tid & 31) == 0) {
-                red[lr * WPG + (s >> 5)] = v;
-            }
+    for (int j = 0; j < 2; ++j) {
+        const float r = __shfl_xor_sync(0xffffffffu, h2 ? v4[j] : v4[j + 2], LPG / 4);
+        v2[j] = (h2 ? v4[j + 2] : v4[j]) + r;
+    }
+    float v1;
+    {
+        const float r = __shfl_xor_sync(0xffffffffu, h1 ? v2[0] : v2[1], LPG / 8);
+        v1 = (h1 ? v2[1] : v2[0]) + r;
+    }
+#pragma unroll
+    for (int o = LPG / 16; o; o >>= 1) v1 += __shfl_xor_sync(0xffffffffu, v1, o);
+    {
+        const int ri = (h4 ? 4 : 0) + (h2 ? 2 : 0) + (h1 ? 1 : 0);
+        const int lr = g + ri * G;
+        if ((lane & (LPG / 8 - 1)) == 0 && lr < nloc) {
+            if (WPG == 1) rowres[lr] = v1;
+            else red[lr * WPG + (s >> 5)] = v1;
         }
     }
+    if (rope_row) rcs[tid] = rope_v;
     __syncthreads();
     if (WPG > 1 && tid < nloc) {
         float v = 0.f;
@@ -319,12 +345,13 @@ struct ResPlan {
 inline bool matvec_resident_plan(int type, int nb, int n_vrows, int sms, int ctas_per_sm, int smem_per_sm,
                                  ResPlan* p) {
     if (n_vrows <= 0 || nb <= 0 || ctas_per_sm <= 0 || sms <= 0) return false;
-    const int tpg = res_tpg(nb);
-    const int maxr = res_max_rows(tpg);
     for (int k = ctas_per_sm; k <= 8 * ctas_per_sm; k *= 2) {
         int rpc = (n_vrows + k * sms - 1) / (k * sms);
         rpc = (rpc + 1) & ~1;
-        if (rpc > maxr) continue;
+        // fewer threads per row group hold more rows per CTA
+        int tpg = res_tpg(nb);
+        while (rpc > res_max_rows(tpg) && tpg > 16) tpg /= 2;
+        if (rpc > res_max_rows(tpg)) continue;
         const ResLayout L = res_layout(type, nb, rpc);
         const int grid = (n_vrows + rpc - 1) / rpc;
         const int per_sm = (grid + sms - 1) / sms;  // this launch's CTAs on the busiest SM

@@ -242,9 +242,9 @@ def set_stream_tiles(rows_per_tile: int = 0, blocks_per_chunk: int = 0) -> None:
     _check(load().neon_cuda_set_stream_tiles(int(rows_per_tile), int(blocks_per_chunk)))
 
 
-def set_resident(ctas_per_sm: int = 2) -> None:
+def set_resident(ctas_per_sm: int = 1) -> None:
     """One-position Q4_0 / Q8_0 launches that fit shared memory run on the
-    resident kernel with this many CTAs per SM (default 2); 0 sends them all
+    resident kernel with this many CTAs per SM (default 1); 0 sends them all
     to the streaming kernel. Process-wide."""
     _check(load().neon_cuda_set_resident(int(ctas_per_sm)))
 

@@ -3,8 +3,7 @@ decode-sized Q4_0 / Q8_0 projections) against the oracle, through the C ABI.
 
   * several targets in one launch whose rows are odd (span pieces inside one
     CTA, scale windows at every 16-byte offset), against the oracle;
-  * CTAs per SM 1, 2, 4: the rows land in other CTAs, but every row's sum is
-    formed the same way -- bitwise identical;
+  * CTAs per SM 1, 2, 4: against the oracle, and bitwise repeatable;
   * the streaming kernel (resident kernel switched off) still matches the
     oracle on the same shapes, so both one-position paths stay covered;
   * the decode step's epilogues (norm folded, RoPE, cache rows, SwiGLU,
@@ -28,7 +27,7 @@ def device():
     assert torch.cuda.is_available(), "GPU tests need a CUDA device"
     N.init(0)
     yield
-    N.set_resident(2)
+    N.set_resident(1)
 
 
 def bits(a):
@@ -46,7 +45,7 @@ def multi(typ, shapes, cols, X, resident):
         torch.cuda.synchronize()
         return Ws, [y.cpu().numpy() for y in ys]
     finally:
-        N.set_resident(2)
+        N.set_resident(1)
 
 
 @pytest.mark.parametrize("typ", [S.GGML_Q4_0, S.GGML_Q8_0])
@@ -65,10 +64,15 @@ def test_spans_with_odd_rows(typ, shapes, cols):
 
 @pytest.mark.parametrize("typ", [S.GGML_Q4_0, S.GGML_Q8_0])
 @pytest.mark.parametrize("rows,cols", [(4096, 4096), (1000, 3072), (6144, 1024), (301, 800)])
-def test_ctas_per_sm_bitwise(typ, rows, cols):
+def test_ctas_per_sm(typ, rows, cols):
+    """Every CTAs-per-SM setting against the oracle (the setting may change
+    the row-group width, so the fp32 sum order), and bitwise repeatable."""
     X = S.activations(1, cols, seed=rows)
-    outs = [multi(typ, (rows,), cols, X, k)[1][0] for k in (1, 2, 4)]
-    assert np.array_equal(bits(outs[0]), bits(outs[1])) and np.array_equal(bits(outs[0]), bits(outs[2]))
+    for k in (1, 2, 4):
+        Ws, (y,) = multi(typ, (rows,), cols, X, k)
+        assert max_rel_err(y, O.proj_all_positions(typ, Ws[0], rows, cols, X)) <= MATVEC_RTOL, f"k={k}"
+        _, (y2,) = multi(typ, (rows,), cols, X, k)
+        assert np.array_equal(bits(y), bits(y2)), f"k={k} not repeatable"
 
 
 @pytest.mark.parametrize("typ", [S.GGML_Q4_0, S.GGML_Q8_0])
@@ -79,7 +83,7 @@ def test_streaming_kernel_ragged(typ, rows, cols):
     assert max_rel_err(got[0], O.proj_all_positions(typ, Ws[0], rows, cols, X)) <= MATVEC_RTOL
 
 
-@pytest.mark.parametrize("resident", [2, 0])
+@pytest.mark.parametrize("resident", [1, 2, 0])
 def test_decode_epilogues(resident):
     """A small decoder (norms folded into X staging, RoPE and cache-row
     epilogues on Q/K/V, SwiGLU on gate/up, accumulate on attn_output and
@@ -95,7 +99,7 @@ def test_decode_epilogues(resident):
         logits = m.forward(prompt)
         m.free()
     finally:
-        N.set_resident(2)
+        N.set_resident(1)
     o = O.Model(cfg, tensors, "port")
     want, want_logits = o.generate_greedy(prompt, 12)
     o.close()

@@ -155,7 +155,7 @@ def test_benchmark_shapes(lib, typ, k):
         check_launch(lib, typ, list(rows), cols, k)
     # the headline matvec takes the resident kernel at the default setting
     if typ == Q4_0:
-        assert check_launch(lib, typ, [4096], 4096, 2)["ok"]
+        assert check_launch(lib, typ, [4096], 4096, 1)["ok"]
 
 
 @pytest.mark.parametrize("world", [1, 2, 4, 8])
@@ -168,7 +168,7 @@ def test_decode_shapes(lib, model, world):
     # the small model's projections are all resident
     if model == "qwen3_0_6b" and world == 1:
         for rows, cols in model_shapes(n_embd, q_dim, kv_dim, n_ff, world):
-            assert check_launch(lib, Q4_0, list(rows), cols, 2)["ok"], (rows, cols)
+            assert check_launch(lib, Q4_0, list(rows), cols, 1)["ok"], (rows, cols)
 
 
 @pytest.mark.parametrize("typ", [Q4_0, Q8_0])
