@@ -478,45 +478,48 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const float* __rest
 // ---------------------------------------------------------------------------
 // Decode attention in one launch: a thread-block cluster of cs CTAs (8, or 16
 // for long contexts) per KV head. CTA r of the cluster takes positions
-// [r*chunk, (r+1)*chunk) of the L = *d_pos + 1 cache rows. Its K rows, then its
-// V rows, stream through a ring of shared-memory slots (cp.async.bulk, one row
-// per copy, rows padded by 64 bytes so the four threads scoring a row read
-// conflict-free quarters) in sub-chunks of kAttnSub rows: as many slots as the
-// CTA's sub-chunks need while every cluster of the launch stays resident at
-// once (attn_pick_slots), so at the contexts the configurations use every K
-// and V row of a CTA is in flight together; a slot is refilled as soon as its
-// rows are used. Scores for the head's
-// query group go to shared memory; the CTAs exchange their maxima through
-// distributed shared memory, so every CTA forms p_s = fast_expf(score_s - max
-// over ALL positions) exactly as transformer_forward does (:1123-1137); each
-// CTA sums p and p * v over its positions, and CTA 0 adds the partials in rank
-// order: out = (sum p v) / (sum p).
+// [r*chunk, (r+1)*chunk) of the L = *d_pos + 1 cache rows, in tiles of
+// kAttnSub rows. Its V tiles go into a ring of shared-memory slots with
+// 16-byte cp.async copies from all threads (rows padded by 64 bytes, so the
+// threads of the V pass read conflict-free), the first ring's worth issued
+// before the K pass starts; K rows are read straight into registers (four
+// threads per row, two tiles' loads in flight). One copy instruction per
+// 16 bytes from every thread keeps far more bytes in flight than one bulk
+// copy per 512-byte row from one warp. Scores for the head's query group go
+// to shared memory; the CTAs exchange their maxima through distributed shared
+// memory, so every CTA forms p_s = fast_expf(score_s - max over ALL
+// positions) exactly as transformer_forward does (:1123-1137); each CTA sums p
+// and p * v over its positions, and CTA 0 adds the partials in rank order:
+// out = (sum p v) / (sum p).
 // ---------------------------------------------------------------------------
 
-__device__ __forceinline__ uint32_t smem_addr_d(const void* p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                     static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst))),
+                 "l"(gsrc)
+                 : "memory");
 }
-__device__ __forceinline__ bool mbar_wait_d(uint64_t* bar, uint32_t parity, unsigned int* err) {
-    uint32_t done = 0;
-    unsigned long long t0 = 0;
-    for (int it = 0;; ++it) {
-        asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
-                     : "=r"(done)
-                     : "r"(smem_addr_d(bar)), "r"(parity)
-                     : "memory");
-        if (done) return true;
-        unsigned long long t;
-        asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-        if (it == 0) t0 = t;
-        else if (t - t0 > 2000000000ull) {
-            atomicOr(err, 4u);
-            return false;
-        }
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// Wait until at most n (0..kAttnMaxSlots-1) of this thread's copy groups are pending.
+__device__ __forceinline__ void cp_async_wait_pending(int n) {
+    switch (n) {
+        case 0: asm volatile("cp.async.wait_group 0;" ::: "memory"); break;
+        case 1: asm volatile("cp.async.wait_group 1;" ::: "memory"); break;
+        case 2: asm volatile("cp.async.wait_group 2;" ::: "memory"); break;
+        case 3: asm volatile("cp.async.wait_group 3;" ::: "memory"); break;
+        case 4: asm volatile("cp.async.wait_group 4;" ::: "memory"); break;
+        case 5: asm volatile("cp.async.wait_group 5;" ::: "memory"); break;
+        case 6: asm volatile("cp.async.wait_group 6;" ::: "memory"); break;
+        default: asm volatile("cp.async.wait_group 7;" ::: "memory"); break;
     }
 }
 
 static_assert(kThreads == kAttnThreads, "the attention layout assumes kThreads threads");
+static_assert(kAttnMaxSlots <= 8, "cp_async_wait_pending covers 8 pending groups");
 
+// C4: float4 columns of a K row per scoring thread (head_dim / 16, rounded up
+// to 2, 4, 8 or 16).
+template <int C4>
 __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const float* __restrict__ q, const float* __restrict__ Kc,
                                                                const float* __restrict__ Vc, const int* __restrict__ d_pos,
                                                                int kv_dim, int hd, int group, float scale, int chunk_max,
@@ -529,78 +532,73 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const float* __re
     const AttnSmem lay = attn_smem_layout(group, hd, chunk_max, cs, slots);
     float* qs = sm + lay.q;
     float* sc = sm + lay.sc;     // [group][chunk_max]
-    float* ring = sm + lay.ring; // [slots][kAttnSub][hd + 16]; later [parts][group][hd]
+    float* ring = sm + lay.ring; // [slots][kAttnSub][hd + 16]: V tiles; later [parts][group][hd]
     float* co = sm + lay.co;     // [cluster][group][hd]   (CTA 0; overlays the ring)
     float* csum = sm + lay.csum; // [cluster][kAttnMaxGroup] (read in CTA 0)
     float* cmax = sm + lay.cmax; // [cluster][kAttnMaxGroup]
-    uint64_t* full = reinterpret_cast<uint64_t*>(sm + lay.bar);
     __shared__ float gm[kAttnMaxGroup];
+    (void)err;
     const int pitch = hd + 16;
     const int S = slots;
-    if (threadIdx.x == 0) {
-        for (int i = 0; i < S; ++i)
-            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr_d(&full[i])) : "memory");
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    }
     pdl_wait_d();
     pdl_trigger_d();
-    __syncthreads();
     const int L = *d_pos + 1;
     const int chunk = (L + cs - 1) / cs;
     const int s0 = min(L, rank * chunk), len = min(L, s0 + chunk) - s0;
     const int n_sub = (len + kAttnSub - 1) / kAttnSub;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nd4 = hd / 4;
-    // item t < n_sub: K rows of sub-chunk t; n_sub <= t < 2 n_sub: V rows of sub-chunk t - n_sub
-    auto issue = [&](int t) {
-        const int slot = t % S;
-        const bool is_v = t >= n_sub;
-        const int sub = is_v ? t - n_sub : t;
-        const int j0 = sub * kAttnSub, rows = min(kAttnSub, len - j0);
-        const float* base = (is_v ? Vc : Kc) + (long long)kvh * hd;
-        float* dst = ring + slot * kAttnSub * pitch;
-        if (lane == 0)
-            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr_d(&full[slot])),
-                         "r"((uint32_t)(rows * hd * 4))
-                         : "memory");
-        __syncwarp();
-        for (int r = lane; r < rows; r += 32)
-            asm volatile(
-                "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                    smem_addr_d(dst + r * pitch)),
-                "l"(base + (long long)(s0 + j0 + r) * kv_dim), "r"((uint32_t)(hd * 4)), "r"(smem_addr_d(&full[slot]))
-                : "memory");
+    // V tile t into ring slot t % S: rows j0 .. j0 + rows, hd floats each, as
+    // 16-byte copies spread over all threads; one commit group per tile
+    auto issue_v = [&](int t) {
+        const int j0 = t * kAttnSub, rows = min(kAttnSub, len - j0);
+        const float* base = Vc + (long long)kvh * hd;
+        float* dst = ring + (t % S) * kAttnSub * pitch;
+        for (int i = threadIdx.x; i < rows * nd4; i += kThreads) {
+            const int r = i / nd4, c = i - r * nd4;
+            cp_async16(dst + r * pitch + 4 * c, base + (long long)(s0 + j0 + r) * kv_dim + 4 * c);
+        }
+        cp_async_commit();
     };
-    const int n_items = 2 * n_sub;
-    if (warp == 0)
-        for (int t = 0; t < min(S, n_items); ++t) issue(t);
+    const int pre = min(S, n_sub);
+    for (int t = 0; t < pre; ++t) issue_v(t);
     for (int i = threadIdx.x; i < group * hd; i += blockDim.x) qs[i] = q[(long long)kvh * group * hd + i];
     __syncthreads();
-    bool ok = true;
-    // pass 1: scores, a thread per cache row of the slot
-    for (int t = 0; t < n_sub; ++t) {
-        ok = ok && mbar_wait_d(&full[t % S], (uint32_t)((t / S) & 1), err);
-        const float* rows_k = ring + (t % S) * kAttnSub * pitch;
-        const int j0 = t * kAttnSub, rows = min(kAttnSub, len - j0);
-        {
-            // four threads per row (lanes 4r'..4r'+3 of a warp), thread q4i takes float4
-            // columns q4i, q4i+4, ..; the four partial dots meet by two shuffles
-            const int r = threadIdx.x >> 2, q4i = threadIdx.x & 3;
-            const float4* kr = reinterpret_cast<const float4*>(rows_k + r * pitch);
+    // pass 1: scores, four threads per cache row (lanes 4r'..4r'+3 of a warp);
+    // thread q4i takes float4 columns q4i, q4i + 4, .. of the row, read from
+    // global memory into registers (two tiles in flight); the four partial
+    // dots meet by two shuffles
+    {
+        const int r = threadIdx.x >> 2, q4i = threadIdx.x & 3;
+        auto load_k = [&](int t, float4 (&k)[C4]) {
+            const int row = t * kAttnSub + r;
+            const float4* kr = reinterpret_cast<const float4*>(Kc + (long long)(s0 + row) * kv_dim + (long long)kvh * hd);
+#pragma unroll
+            for (int u = 0; u < C4; ++u) {
+                const int c = q4i + 4 * u;
+                k[u] = (row < len && c < nd4) ? __ldg(kr + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        };
+        auto score = [&](int t, const float4 (&k)[C4]) {
+            const int j0 = t * kAttnSub, rows = min(kAttnSub, len - j0);
             float acc[kAttnMaxGroup];
 #pragma unroll
             for (int gq = 0; gq < kAttnMaxGroup; ++gq) acc[gq] = 0.f;
             if (r < rows) {
-                for (int c = q4i; c < nd4; c += 4) {
-                    const float4 k4 = kr[c];
 #pragma unroll
-                    for (int gq = 0; gq < kAttnMaxGroup; ++gq) {
-                        if (gq < group) {
-                            const float4 q4 = reinterpret_cast<const float4*>(qs + gq * hd)[c];
-                            acc[gq] = __fmaf_rn(q4.x, k4.x, acc[gq]);
-                            acc[gq] = __fmaf_rn(q4.y, k4.y, acc[gq]);
-                            acc[gq] = __fmaf_rn(q4.z, k4.z, acc[gq]);
-                            acc[gq] = __fmaf_rn(q4.w, k4.w, acc[gq]);
+                for (int u = 0; u < C4; ++u) {
+                    const int c = q4i + 4 * u;
+                    if (c < nd4) {
+                        const float4 k4 = k[u];
+#pragma unroll
+                        for (int gq = 0; gq < kAttnMaxGroup; ++gq) {
+                            if (gq < group) {
+                                const float4 q4 = reinterpret_cast<const float4*>(qs + gq * hd)[c];
+                                acc[gq] = __fmaf_rn(q4.x, k4.x, acc[gq]);
+                                acc[gq] = __fmaf_rn(q4.y, k4.y, acc[gq]);
+                                acc[gq] = __fmaf_rn(q4.z, k4.z, acc[gq]);
+                                acc[gq] = __fmaf_rn(q4.w, k4.w, acc[gq]);
+                            }
                         }
                     }
                 }
@@ -615,13 +613,16 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const float* __re
                 for (int gq = 0; gq < kAttnMaxGroup; ++gq)
                     if (gq < group) sc[gq * chunk_max + j0 + r] = __fmul_rn(acc[gq], scale);
             }
-        }
-        __syncthreads();  // the slot is free
-        if (warp == 0 && t + S < n_items) {
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            issue(t + S);
+        };
+        for (int t = 0; t < n_sub; t += 2) {
+            float4 ka[C4], kb[C4];
+            load_k(t, ka);
+            if (t + 1 < n_sub) load_k(t + 1, kb);
+            score(t, ka);
+            if (t + 1 < n_sub) score(t + 1, kb);
         }
     }
+    __syncthreads();
     // this CTA's max per query head (warp gq), published to every CTA of the cluster
     if (warp < group) {
         float m = -INFINITY;
@@ -654,10 +655,12 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const float* __re
     float4 acc[kAttnMaxGroup];
 #pragma unroll
     for (int gq = 0; gq < kAttnMaxGroup; ++gq) acc[gq] = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int t = n_sub; t < n_items; ++t) {
-        ok = ok && mbar_wait_d(&full[t % S], (uint32_t)((t / S) & 1), err);
+    for (int t = 0; t < n_sub; ++t) {
+        // groups issued so far: tiles 0 .. min(n_sub, S + t) - 1; tile t must be complete
+        cp_async_wait_pending(min(n_sub, S + t) - t - 1);
+        __syncthreads();
         const float* rows_v = ring + (t % S) * kAttnSub * pitch;
-        const int j0 = (t - n_sub) * kAttnSub, rows = min(kAttnSub, len - j0);
+        const int j0 = t * kAttnSub, rows = min(kAttnSub, len - j0);
         if (part < parts) {
             for (int r = part; r < rows; r += parts) {
                 const float4 v4 = reinterpret_cast<const float4*>(rows_v + r * pitch)[c4];
@@ -673,13 +676,9 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const float* __re
                 }
             }
         }
-        __syncthreads();
-        if (warp == 0 && t + S < n_items) {
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            issue(t + S);
-        }
+        __syncthreads();  // the slot is free
+        if (t + S < n_sub) issue_v(t + S);
     }
-    (void)ok;  // a timed-out copy sets bit 2 of the error word; the results are then not used
     // per-part partials -> the ring (its copies are all consumed), then the CTA's partial to CTA 0
     float* red = ring;
     if (part < parts) {
@@ -974,6 +973,18 @@ int launch_embed(neon_model* m, const int* toks, int seq) {
                     nb, toks, (int)c.n_vocab, m->h, m->d_err);
 }
 
+// The attn_decode_kernel instantiation for a head dim: float4 columns per
+// scoring thread, head_dim / 16 rounded up to 2, 4, 8 or 16.
+using AttnKernel = void (*)(const float*, const float*, const float*, const int*, int, int, int, float, int, int,
+                            float*, unsigned int*);
+AttnKernel attn_kernel_for(int hd) {
+    const int c4 = (hd / 4 + 3) / 4;
+    if (c4 <= 2) return attn_decode_kernel<2>;
+    if (c4 <= 4) return attn_decode_kernel<4>;
+    if (c4 <= 8) return attn_decode_kernel<8>;
+    return attn_decode_kernel<16>;
+}
+
 // Dynamic shared memory of attn_decode_kernel.
 int attn_chunk_max(const neon_model* m) { return (int)((m->cfg.ctx_len + m->att_cs - 1) / m->att_cs); }
 size_t attn_decode_smem(const neon_model* m, int slots) {
@@ -983,12 +994,12 @@ size_t attn_decode_smem(const neon_model* m, int slots) {
 }
 size_t attn_decode_smem(const neon_model* m) { return attn_decode_smem(m, m->att_slots); }
 
-// The ring depth of attn_decode_kernel: a slot per K and V sub-chunk of the
-// longest share (at most kAttnMaxSlots), cut while it would take more than
+// The ring depth of attn_decode_kernel: a slot per V tile of the longest
+// share (at most kAttnMaxSlots), cut while it would take more than
 // kAttnSmemMax or leave a cluster of the launch waiting for another to finish;
-// never below two (the next sub-chunk in flight while one is used).
+// never below two (the next tile in flight while one is used).
 int attn_pick_slots(const neon_model* m) {
-    const int items = 2 * ((attn_chunk_max(m) + kAttnSub - 1) / kAttnSub);
+    const int items = (attn_chunk_max(m) + kAttnSub - 1) / kAttnSub;
     for (int slots = std::min(kAttnMaxSlots, items); slots > 2; --slots) {
         const size_t smem = attn_decode_smem(m, slots);
         if (smem > (size_t)kAttnSmemMax) continue;
@@ -1004,7 +1015,7 @@ int attn_pick_slots(const neon_model* m) {
         q.attrs = qa;
         q.numAttrs = 1;
         int clusters = 0;
-        if (cudaOccupancyMaxActiveClusters(&clusters, attn_decode_kernel, &q) != cudaSuccess) {
+        if (cudaOccupancyMaxActiveClusters(&clusters, attn_kernel_for((int)m->cfg.head_dim), &q) != cudaSuccess) {
             cudaGetLastError();
             continue;
         }
@@ -1036,7 +1047,7 @@ int launch_attn_decode(neon_model* m, const float* Kl, const float* Vl) {
     cfg.attrs = attr;
     cfg.numAttrs = n;
     const float scale = 1.0f / std::sqrt((float)c.head_dim);
-    cudaError_t e = cudaLaunchKernelEx(&cfg, attn_decode_kernel, (const float*)m->q, Kl, Vl, (const int*)m->d_pos,
+    cudaError_t e = cudaLaunchKernelEx(&cfg, attn_kernel_for((int)c.head_dim), (const float*)m->q, Kl, Vl, (const int*)m->d_pos,
                                        (int)m->kv_dim, (int)c.head_dim, (int)(c.n_head / c.n_kv_head), scale,
                                        attn_chunk_max(m), m->att_slots, m->att, m->d_err);
     if (e != cudaSuccess) return cuda_error(e, "attn_decode_kernel");
@@ -1519,7 +1530,8 @@ int neon_cuda_model_create_tp(const neon_model_config_t* cfg, neon_comm_t comm, 
     if (!rc) {
         // long contexts: 16 CTAs per KV head when the device schedules clusters that large
         if (c.ctx_len > 1024 &&
-            cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess) {
+            cudaFuncSetAttribute(attn_kernel_for((int)c.head_dim), cudaFuncAttributeNonPortableClusterSizeAllowed, 1) ==
+                cudaSuccess) {
             m->att_cs = kAttnMaxCluster;
             cudaLaunchConfig_t q = {};
             q.gridDim = dim3((unsigned)(m->n_kv_l * m->att_cs));
@@ -1534,9 +1546,11 @@ int neon_cuda_model_create_tp(const neon_model_config_t* cfg, neon_comm_t comm, 
             q.numAttrs = 1;
             int clusters = 0;
             if (q.dynamicSmemBytes > 48 * 1024)
-                cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+                cudaFuncSetAttribute(attn_kernel_for((int)c.head_dim), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     220 * 1024);
             if (attn_decode_smem(m) > 220 * 1024 ||
-                cudaOccupancyMaxActiveClusters(&clusters, attn_decode_kernel, &q) != cudaSuccess || clusters < 1) {
+                cudaOccupancyMaxActiveClusters(&clusters, attn_kernel_for((int)c.head_dim), &q) != cudaSuccess ||
+                clusters < 1) {
                 cudaGetLastError();
                 m->att_cs = 8;
             }
@@ -1546,8 +1560,8 @@ int neon_cuda_model_create_tp(const neon_model_config_t* cfg, neon_comm_t comm, 
         rc = error(NEON_ERR_UNSUPPORTED, "decode attention: ctx_len too large for one cluster per KV head");
     if (!rc) {
         // the process-wide limit at its largest, so that no later model lowers it under an earlier one's
-        if (cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024) !=
-            cudaSuccess)
+        if (cudaFuncSetAttribute(attn_kernel_for((int)c.head_dim), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 220 * 1024) != cudaSuccess)
             rc = error(NEON_ERR_CUDA, "cudaFuncSetAttribute(attn_decode_kernel)");
         else
             m->att_slots = attn_pick_slots(m);
