@@ -137,7 +137,9 @@ def parse_args():
                    help="decode workloads: Q4_0 projections + Q8_0 embedding (default), or Q4_K + Q6_K "
                         "(what nanity_convert.py --quant Q4_K writes)")
     p.add_argument("--prefill-mma", action="store_true",
-                   help="prompt passes of Q4_0 models on the tensor-core prefill kernel (neon_cuda_set_prefill_mma)")
+                   help="multi-position calls on the tensor-core prefill kernels (the default; neon_cuda_set_prefill_mma)")
+    p.add_argument("--cuda-core-prefill", action="store_true",
+                   help="multi-position calls on the CUDA-core kernel instead (neon_cuda_set_prefill_mma(0))")
     p.add_argument("--dq-ring", action="store_true",
                    help="one-position calls of the dequantising types on the bulk-copy ring kernel "
                         "(neon_cuda_set_dq_ring)")
@@ -420,8 +422,7 @@ def run_decode(args):
     import neon_cuda as N
 
     N.init(local)
-    if getattr(args, "prefill_mma", False):
-        N.set_prefill_mma(True)
+    N.set_prefill_mma(not getattr(args, "cuda_core_prefill", False))
     if getattr(args, "dq_ring", False):
         N.set_dq_ring(True)
     if getattr(args, "decode_chain", False):
@@ -462,7 +463,7 @@ def run_decode(args):
                 "scaling": "strong", "vs_baseline": None, "dtype": "int8/fp32 (q4_0 x q8_0 dp4a, fp32 scales)",
                 "data": "synthetic", "config": {"workload": res["workload"], "parallelism": res["parallelism"],
                                                 "variants": [v for v, on in (("decode_chain", args.decode_chain),
-                                                                             ("prefill_mma", args.prefill_mma)) if on]
+                                                                             ("cuda_core_prefill", args.cuda_core_prefill)) if on]
                                                 + ([f"resident {args.resident}"] if args.resident is not None
                                                    else [])},
                 "e2e": {"value": res["e2e_tokens_per_s"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
@@ -585,8 +586,7 @@ def run_neon(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     N.init(local)
-    if getattr(args, "prefill_mma", False):
-        N.set_prefill_mma(True)
+    N.set_prefill_mma(not getattr(args, "cuda_core_prefill", False))
     if getattr(args, "dq_ring", False):
         N.set_dq_ring(True)
     if getattr(args, "decode_chain", False):
@@ -734,7 +734,8 @@ def run_neon(args):
             "dtype": compute_dtype(TYPE),
             "data": "synthetic",
             "config": {**workload_config(), "parallelism": f"dp{world} (independent rotations)",
-                       "variants": [v for v, on in (("dq_ring", args.dq_ring), ("prefill_mma", args.prefill_mma),
+                       "variants": [v for v, on in (("dq_ring", args.dq_ring),
+                                                    ("cuda_core_prefill", args.cuda_core_prefill),
                                                     ("decode_chain", args.decode_chain)) if on]
                        + ([f"tiles {args.tiles}"] if args.tiles else [])
                        + ([f"resident {args.resident}"] if args.resident is not None else []),
@@ -775,8 +776,7 @@ def run_prefill(args):
 
     torch.cuda.set_device(0)
     N.init(0)
-    if args.prefill_mma:
-        N.set_prefill_mma(True)
+    N.set_prefill_mma(not args.cuda_core_prefill)
     dev = torch.device("cuda", 0)
     B = args.batch
     calls = 64
@@ -820,7 +820,7 @@ def run_prefill(args):
     print(json.dumps({
         "metric": f"{TYPE_NAME} prefill TFLOP/s (batch {B})", "value": round(tflops, 2), "unit": "TFLOP/s",
         "n_gpus": 1, "steps": K, "warmup": W, "ms_per_step": round(ms / K, 4), "higher_is_better": True,
-        "kernel": ("tensor cores (int8 / TF32 mma.sync)" if args.prefill_mma else "CUDA cores (multi-position kernel)"),
+        "kernel": ("CUDA cores (multi-position kernel)" if args.cuda_core_prefill else "tensor cores (int8 / TF32 mma.sync)"),
         "config": {**workload_config(), "batch": B, "calls_per_step": calls},
         "us_per_call": round(per_call_s * 1e6, 2), "launches_per_call": per_call_launches,
         "roofline": {"tensor": {"achieved": round(tflops, 2), "peak": tc_peak, "peak_source": tc_kind,

@@ -30,13 +30,17 @@ constexpr int kMpR = 2, kMpT = 4;
 // stage (weights of one item).
 constexpr int kMaxSmem = 220 * 1024;
 constexpr int kStageTarget = 40 * 1024;
+// Stage target of the streaming (one-position Q4_0 / Q8_0) kernel's tiles:
+// a tile sweep on B200 put the best tile at 64-80 KB on every large shape
+// (e.g. Q4_0 28672x8192: 16-row tiles; Q8_0 4096x14336: 4-row tiles).
+constexpr int kStreamStageTarget = 80 * 1024;
 // Resident streaming CTAs per SM the grid is sized for.
 constexpr int kStreamCtasPerSm = 4;
 
 thread_local std::string g_err;
 std::atomic<uint64_t> g_launches{0};
 std::atomic<int> g_pdl{1};
-std::atomic<int> g_prefill_mma{0};  // neon_cuda_set_prefill_mma
+std::atomic<int> g_prefill_mma{1};  // neon_cuda_set_prefill_mma
 std::atomic<int> g_dq_ring{0};      // neon_cuda_set_dq_ring
 std::atomic<int> g_decode_chain{0};    // neon_cuda_set_decode_chain
 std::atomic<int> g_tile_rc{0}, g_tile_kc{0};  // neon_cuda_set_stream_tiles (0: the planner's choice)
@@ -224,8 +228,8 @@ int launch(void (*kern)(KArgs...), dim3 grid, size_t smem, cudaStream_t st, Args
 
 // Tile plan of a streaming (one-position) launch: plan_stream_tiles with
 // this library's stage target, shared-memory budget and tile override.
-StreamPlan plan_stream(int type, int nb, size_t total_rows, int sms) {
-    return plan_stream_tiles(type, nb, total_rows, sms, kStageTarget, kMaxSmem,
+StreamPlan plan_stream(int type, int nb, size_t total_rows, int sms, int stage_target = kStreamStageTarget) {
+    return plan_stream_tiles(type, nb, total_rows, sms, stage_target, kMaxSmem,
                              g_tile_rc.load(std::memory_order_relaxed), g_tile_kc.load(std::memory_order_relaxed));
 }
 
@@ -983,7 +987,8 @@ int matvec_chain(const ChainPhaseDesc* ph, int n, const int* d_pos, unsigned int
             total_rows += W->rows;
         }
         const int nb = (int)(cols / 32);
-        const StreamPlan pl = plan_stream(NEON_GGML_Q4_0, nb, total_rows, ds.sms);
+        // the chain's phases use the stage target its ring slots are sized for
+        const StreamPlan pl = plan_stream(NEON_GGML_Q4_0, nb, total_rows, ds.sms, kStageTarget);
         ChainPhase& P = c.ph[p];
         int tiles = 0;
         for (int i = 0; i < d.n; ++i) {

@@ -560,67 +560,71 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const float* __re
         }
         cp_async_commit();
     };
-    const int pre = min(S, n_sub);
-    for (int t = 0; t < pre; ++t) issue_v(t);
-    for (int i = threadIdx.x; i < group * hd; i += blockDim.x) qs[i] = q[(long long)kvh * group * hd + i];
-    __syncthreads();
     // pass 1: scores, four threads per cache row (lanes 4r'..4r'+3 of a warp);
     // thread q4i takes float4 columns q4i, q4i + 4, .. of the row, read from
-    // global memory into registers (two tiles in flight); the four partial
-    // dots meet by two shuffles
-    {
-        const int r = threadIdx.x >> 2, q4i = threadIdx.x & 3;
-        auto load_k = [&](int t, float4 (&k)[C4]) {
-            const int row = t * kAttnSub + r;
-            const float4* kr = reinterpret_cast<const float4*>(Kc + (long long)(s0 + row) * kv_dim + (long long)kvh * hd);
+    // global memory into registers; the four partial dots meet by two
+    // shuffles. The first two K tiles are requested before anything else, then
+    // the V tiles of the ring, then the query rows: the K loads do not queue
+    // behind the other traffic.
+    const int r = threadIdx.x >> 2, q4i = threadIdx.x & 3;
+    auto load_k = [&](int t, float4 (&k)[C4]) {
+        const int row = t * kAttnSub + r;
+        const float4* kr = reinterpret_cast<const float4*>(Kc + (long long)(s0 + row) * kv_dim + (long long)kvh * hd);
+#pragma unroll
+        for (int u = 0; u < C4; ++u) {
+            const int c = q4i + 4 * u;
+            k[u] = (t < n_sub && row < len && c < nd4) ? __ldg(kr + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    };
+    auto score = [&](int t, const float4 (&k)[C4]) {
+        const int j0 = t * kAttnSub, rows = min(kAttnSub, len - j0);
+        float acc[kAttnMaxGroup];
+#pragma unroll
+        for (int gq = 0; gq < kAttnMaxGroup; ++gq) acc[gq] = 0.f;
+        if (r < rows) {
 #pragma unroll
             for (int u = 0; u < C4; ++u) {
                 const int c = q4i + 4 * u;
-                k[u] = (row < len && c < nd4) ? __ldg(kr + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-            }
-        };
-        auto score = [&](int t, const float4 (&k)[C4]) {
-            const int j0 = t * kAttnSub, rows = min(kAttnSub, len - j0);
-            float acc[kAttnMaxGroup];
+                if (c < nd4) {
+                    const float4 k4 = k[u];
 #pragma unroll
-            for (int gq = 0; gq < kAttnMaxGroup; ++gq) acc[gq] = 0.f;
-            if (r < rows) {
-#pragma unroll
-                for (int u = 0; u < C4; ++u) {
-                    const int c = q4i + 4 * u;
-                    if (c < nd4) {
-                        const float4 k4 = k[u];
-#pragma unroll
-                        for (int gq = 0; gq < kAttnMaxGroup; ++gq) {
-                            if (gq < group) {
-                                const float4 q4 = reinterpret_cast<const float4*>(qs + gq * hd)[c];
-                                acc[gq] = __fmaf_rn(q4.x, k4.x, acc[gq]);
-                                acc[gq] = __fmaf_rn(q4.y, k4.y, acc[gq]);
-                                acc[gq] = __fmaf_rn(q4.z, k4.z, acc[gq]);
-                                acc[gq] = __fmaf_rn(q4.w, k4.w, acc[gq]);
-                            }
+                    for (int gq = 0; gq < kAttnMaxGroup; ++gq) {
+                        if (gq < group) {
+                            const float4 q4 = reinterpret_cast<const float4*>(qs + gq * hd)[c];
+                            acc[gq] = __fmaf_rn(q4.x, k4.x, acc[gq]);
+                            acc[gq] = __fmaf_rn(q4.y, k4.y, acc[gq]);
+                            acc[gq] = __fmaf_rn(q4.z, k4.z, acc[gq]);
+                            acc[gq] = __fmaf_rn(q4.w, k4.w, acc[gq]);
                         }
                     }
                 }
             }
-#pragma unroll
-            for (int gq = 0; gq < kAttnMaxGroup; ++gq) {
-                acc[gq] += __shfl_xor_sync(0xffffffffu, acc[gq], 1);
-                acc[gq] += __shfl_xor_sync(0xffffffffu, acc[gq], 2);
-            }
-            if (r < rows && q4i == 0) {
-#pragma unroll
-                for (int gq = 0; gq < kAttnMaxGroup; ++gq)
-                    if (gq < group) sc[gq * chunk_max + j0 + r] = __fmul_rn(acc[gq], scale);
-            }
-        };
-        for (int t = 0; t < n_sub; t += 2) {
-            float4 ka[C4], kb[C4];
-            load_k(t, ka);
-            if (t + 1 < n_sub) load_k(t + 1, kb);
-            score(t, ka);
-            if (t + 1 < n_sub) score(t + 1, kb);
         }
+#pragma unroll
+        for (int gq = 0; gq < kAttnMaxGroup; ++gq) {
+            acc[gq] += __shfl_xor_sync(0xffffffffu, acc[gq], 1);
+            acc[gq] += __shfl_xor_sync(0xffffffffu, acc[gq], 2);
+        }
+        if (r < rows && q4i == 0) {
+#pragma unroll
+            for (int gq = 0; gq < kAttnMaxGroup; ++gq)
+                if (gq < group) sc[gq * chunk_max + j0 + r] = __fmul_rn(acc[gq], scale);
+        }
+    };
+    float4 ka[C4], kb[C4];
+    load_k(0, ka);
+    load_k(1, kb);
+    const int pre = min(S, n_sub);
+    for (int t = 0; t < pre; ++t) issue_v(t);
+    for (int i = threadIdx.x; i < group * hd; i += blockDim.x) qs[i] = q[(long long)kvh * group * hd + i];
+    __syncthreads();
+    for (int t = 0; t < n_sub; t += 2) {
+        if (t > 0) {
+            load_k(t, ka);
+            load_k(t + 1, kb);
+        }
+        score(t, ka);
+        if (t + 1 < n_sub) score(t + 1, kb);
     }
     __syncthreads();
     // this CTA's max per query head (warp gq), published to every CTA of the cluster

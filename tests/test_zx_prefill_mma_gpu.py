@@ -23,7 +23,7 @@ def mma_on():
     N.init(0)
     N.set_prefill_mma(True)
     yield
-    N.set_prefill_mma(False)
+    N.set_prefill_mma(True)  # the default
 
 
 def bits(a):

@@ -43,7 +43,14 @@ def test_noalloc_matches_allocating_entry_point_on_two_calls(lib):
     rows, cols = 1024, 4096
     W = S.q4_0_weights(rows, cols, seed=61)
     dt = N.DeviceTensor(W, S.GGML_Q4_0, rows, cols)
-    N.set_prefill_mma(False)  # the default multi-position path: the CUDA-core kernel
+    N.set_prefill_mma(False)  # the allocating entry point's CUDA-core multi-position kernel, the same as this one's
+    try:
+        _two_calls(lib, dt, W, rows, cols)
+    finally:
+        N.set_prefill_mma(True)  # the default
+
+
+def _two_calls(lib, dt, W, rows, cols):
     for call, seq in enumerate((16, 5)):
         X = S.activations(seq, cols, seed=62 + call)
         dx = torch.from_numpy(X).cuda()
