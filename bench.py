@@ -143,9 +143,6 @@ def parse_args():
     p.add_argument("--dq-ring", action="store_true",
                    help="one-position calls of the dequantising types on the bulk-copy ring kernel "
                         "(neon_cuda_set_dq_ring)")
-    p.add_argument("--decode-chain", action="store_true",
-                   help="decode steps with the projections between attention launches as one launch "
-                        "(neon_cuda_set_decode_chain)")
     p.add_argument("--tiles", default=None, metavar="RC:KC",
                    help="one-position Q4_0 / Q8_0 tile shape: RC rows per tile, KC blocks per row chunk "
                         "(0 = whole rows); neon_cuda_set_stream_tiles")
@@ -425,8 +422,6 @@ def run_decode(args):
     N.set_prefill_mma(not getattr(args, "cuda_core_prefill", False))
     if getattr(args, "dq_ring", False):
         N.set_dq_ring(True)
-    if getattr(args, "decode_chain", False):
-        N.set_decode_chain(True)
     if getattr(args, "tiles", None):
         N.set_stream_tiles(*(int(v) for v in args.tiles.split(":")))
     if args.resident is not None:
@@ -462,8 +457,8 @@ def run_decode(args):
                 "steps": res["generated"], "warmup": 0, "ms_per_step": res["ms_per_token"], "higher_is_better": True,
                 "scaling": "strong", "vs_baseline": None, "dtype": "int8/fp32 (q4_0 x q8_0 dp4a, fp32 scales)",
                 "data": "synthetic", "config": {"workload": res["workload"], "parallelism": res["parallelism"],
-                                                "variants": [v for v, on in (("decode_chain", args.decode_chain),
-                                                                             ("cuda_core_prefill", args.cuda_core_prefill)) if on]
+                                                "variants": [v for v, on in (("cuda_core_prefill", args.cuda_core_prefill),)
+                                                             if on]
                                                 + ([f"resident {args.resident}"] if args.resident is not None
                                                    else [])},
                 "e2e": {"value": res["e2e_tokens_per_s"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
@@ -589,8 +584,6 @@ def run_neon(args):
     N.set_prefill_mma(not getattr(args, "cuda_core_prefill", False))
     if getattr(args, "dq_ring", False):
         N.set_dq_ring(True)
-    if getattr(args, "decode_chain", False):
-        N.set_decode_chain(True)
     if getattr(args, "tiles", None):
         N.set_stream_tiles(*(int(v) for v in args.tiles.split(":")))
     if getattr(args, "resident", None) is not None:
@@ -735,8 +728,7 @@ def run_neon(args):
             "data": "synthetic",
             "config": {**workload_config(), "parallelism": f"dp{world} (independent rotations)",
                        "variants": [v for v, on in (("dq_ring", args.dq_ring),
-                                                    ("cuda_core_prefill", args.cuda_core_prefill),
-                                                    ("decode_chain", args.decode_chain)) if on]
+                                                    ("cuda_core_prefill", args.cuda_core_prefill)) if on]
                        + ([f"tiles {args.tiles}"] if args.tiles else [])
                        + ([f"resident {args.resident}"] if args.resident is not None else []),
                        "launch": "CUDA graph of 1024 PDL launches per step"},

@@ -357,17 +357,6 @@ NEON_API int neon_cuda_set_prefill_mma(int enabled);
  * until a GPU run has validated it; the switch is process-wide. */
 NEON_API int neon_cuda_set_dq_ring(int enabled);
 
-/* Decode step (neon_cuda_model_*, all projections Q4_0): the four projections
- * between two attention launches -- attn_output, ffn gate/up, ffn_down and the
- * next layer's Q/K/V -- as the phases of one launch separated by grid
- * barriers, the next phase's weights streaming while the current one
- * finishes, instead of four launches; tensor parallel with fused collectives,
- * the two LL reduces become phases of the same launch (seven launches a layer
- * become two). Same arithmetic, bit for bit. Read when a model captures its
- * decode step; off by default until a GPU run has validated it;
- * process-wide. */
-NEON_API int neon_cuda_set_decode_chain(int enabled);
-
 /* Tile shape of later one-position Q4_0 / Q8_0 launches, for tuning sweeps:
  * rows_per_tile (2, 4, 8, 16 or 32) rows per tile, each row in chunks of
  * blocks_per_chunk 32-value blocks (0: whole rows). (0, 0) returns to the

@@ -6,7 +6,6 @@
 #include "neon_dequant.cuh"
 #include "neon_quant.cuh"
 #include "neon_prefill.cuh"
-#include "neon_chain.cuh"
 #include "neon_resident.cuh"
 
 #include <cuda_runtime.h>
@@ -42,7 +41,6 @@ std::atomic<uint64_t> g_launches{0};
 std::atomic<int> g_pdl{1};
 std::atomic<int> g_prefill_mma{1};  // neon_cuda_set_prefill_mma
 std::atomic<int> g_dq_ring{0};      // neon_cuda_set_dq_ring
-std::atomic<int> g_decode_chain{0};    // neon_cuda_set_decode_chain
 std::atomic<int> g_tile_rc{0}, g_tile_kc{0};  // neon_cuda_set_stream_tiles (0: the planner's choice)
 std::atomic<int> g_resident{1};  // neon_cuda_set_resident: CTAs per SM of a resident launch (0: off)
 
@@ -182,7 +180,6 @@ int init_device(int device) {
         for (int T : {1, 2, 4}) rc = rc ? rc : ensure_smem(dq_kernel(t, T), kMaxSmem);
     for (int t : kDqTypes)
         for (int rpw : {1, 2}) rc = rc ? rc : ensure_smem(dq_ring_kernel(t, rpw), kMaxSmem);
-    if (!rc) rc = ensure_smem(matvec_chain_kernel, kMaxSmem);
     if (rc) return rc;
     void* err = nullptr;
     NEON_CUDA_TRY(cudaGetSymbolAddress(&err, g_neon_device_err));
@@ -228,8 +225,8 @@ int launch(void (*kern)(KArgs...), dim3 grid, size_t smem, cudaStream_t st, Args
 
 // Tile plan of a streaming (one-position) launch: plan_stream_tiles with
 // this library's stage target, shared-memory budget and tile override.
-StreamPlan plan_stream(int type, int nb, size_t total_rows, int sms, int stage_target = kStreamStageTarget) {
-    return plan_stream_tiles(type, nb, total_rows, sms, stage_target, kMaxSmem,
+StreamPlan plan_stream(int type, int nb, size_t total_rows, int sms) {
+    return plan_stream_tiles(type, nb, total_rows, sms, kStreamStageTarget, kMaxSmem,
                              g_tile_rc.load(std::memory_order_relaxed), g_tile_kc.load(std::memory_order_relaxed));
 }
 
@@ -933,136 +930,7 @@ int launched(int n) {
 }
 bool pdl_enabled() { return g_pdl.load(std::memory_order_relaxed) != 0; }
 bool prefill_mma() { return g_prefill_mma.load(std::memory_order_relaxed) != 0; }
-bool decode_chain() { return g_decode_chain.load(std::memory_order_relaxed) != 0; }
 
-// Resident matvec_chain_kernel CTAs per SM at `smem` bytes (0: none fit).
-int chain_occupancy(int smem) {
-    static std::mutex mu;
-    static std::vector<std::pair<int, int>> cache;
-    std::lock_guard<std::mutex> lk(mu);
-    for (auto& kv : cache)
-        if (kv.first == smem) return kv.second;
-    int occ = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, matvec_chain_kernel, kStreamBlock, smem) != cudaSuccess) {
-        cudaGetLastError();
-        occ = 0;
-    }
-    cache.emplace_back(smem, occ);
-    return occ;
-}
-
-int matvec_chain(const ChainPhaseDesc* ph, int n, const int* d_pos, unsigned int* sync, const PeerSet* peer,
-                 cudaStream_t st) {
-    if (n < 1 || n > kChainMaxPhases || !sync) return set_err(NEON_ERR_UNSUPPORTED, "projection chain: 1-6 phases");
-    int device = 0;
-    int rc = current_device(&device);
-    if (rc) return rc;
-    DeviceState& ds = g_dev[device];
-    ChainArgs c;
-    std::memset(&c, 0, sizeof(c));
-    int n_peer = 0, n_proj = 0;
-    int proj_nb[kChainMaxPhases];
-    size_t proj_rows[kChainMaxPhases];
-    for (int p = 0; p < n; ++p) {
-        const ChainPhaseDesc& d = ph[p];
-        if (d.ll_h) {
-            // LL reduce of the collective the last kEpiPeer phase produced
-            if (!peer || n_peer == 0 || d.ll_len <= 0 || d.ll_len > kCommFusedFloats)
-                return set_err(NEON_ERR_UNSUPPORTED, "projection chain: an LL reduce needs a kEpiPeer phase before it");
-            ChainPhase& P = c.ph[p];
-            P.ll_reduce = 1;
-            P.h = d.ll_h;
-            P.n = d.ll_len;
-            P.peer_k = n_peer - 1;
-            continue;
-        }
-        if (d.n < 1 || d.n > kChainMaxSpans || !d.t || !d.x)
-            return set_err(NEON_ERR_UNSUPPORTED, "projection chain: 1-3 targets per phase");
-        const size_t cols = d.t[0].W ? d.t[0].W->cols : 0;
-        size_t total_rows = 0;
-        for (int i = 0; i < d.n; ++i) {
-            const neon_tensor* W = d.t[i].W;
-            if (!W || W->type != NEON_GGML_Q4_0 || W->cols != cols || W->device != device || !d.t[i].Y)
-                return set_err(NEON_ERR_UNSUPPORTED, "projection chain: Q4_0 targets of one input dim on this device");
-            total_rows += W->rows;
-        }
-        const int nb = (int)(cols / 32);
-        // the chain's phases use the stage target its ring slots are sized for
-        const StreamPlan pl = plan_stream(NEON_GGML_Q4_0, nb, total_rows, ds.sms, kStageTarget);
-        ChainPhase& P = c.ph[p];
-        int tiles = 0;
-        for (int i = 0; i < d.n; ++i) {
-            const neon_proj_target_t& tg = d.t[i];
-            Span& sp = P.span[i];
-            sp.qs = tg.W->qs;
-            sp.d = tg.W->d;
-            sp.y = tg.Y;
-            sp.y_stride = (long long)tg.y_stride;
-            sp.rows = (int)tg.W->rows;
-            sp.tile0 = tiles;
-            tiles += (int)((tg.W->rows + pl.rc - 1) / pl.rc);
-            sp.epi = d.ext.epi ? d.ext.epi[i] : kEpiStore;
-            sp.pos_stride = d.ext.pos_stride ? d.ext.pos_stride[i] : 0;
-            if (d.ext.peer_mode == 1) sp.epi = kEpiPeer;
-        }
-        if (d.ext.peer_mode == 1) {
-            if (!peer || d.n != 1) return set_err(NEON_ERR_UNSUPPORTED, "projection chain: a kEpiPeer phase needs the LL set");
-            c.ph[p].peer_k = n_peer++;
-        }
-        P.n_spans = d.n;
-        P.n_tiles = tiles;
-        P.x = d.x;
-        P.x_vec = (reinterpret_cast<uintptr_t>(d.x) % 16) == 0;
-        P.norm_w = d.ext.norm_w;
-        P.norm_eps = d.ext.norm_eps;
-        P.rope_cs = d.ext.rope_cs;
-        P.rope_half = d.ext.rope_half;
-        P.head_dim = d.ext.head_dim;
-        P.accumulate = d.accumulate;
-        P.nb = nb;
-        P.kc = pl.kc;
-        P.nch = pl.nch;
-        P.rc = pl.rc;
-        proj_nb[n_proj] = nb;
-        proj_rows[n_proj++] = total_rows;
-    }
-    const ChainRing ring = plan_chain_ring(proj_nb, proj_rows, n_proj, ds.sms, kStageTarget, kMaxSmem,
-                                           g_tile_rc.load(std::memory_order_relaxed),
-                                           g_tile_kc.load(std::memory_order_relaxed));
-    const int slot = ring.slot_bytes, xb = ring.x_bytes;
-    // the ring depth that keeps the most weight bytes in flight per SM; the
-    // grid is what the SMs hold at once (the barriers need every CTA resident)
-    int best_stages = 0, best_occ = 0;
-    long long best_bytes = -1;
-    for (int st_n = 1; st_n <= ring.max_stages; ++st_n) {
-        int occ = chain_occupancy(xb + st_n * slot);
-        if (occ < 1) continue;
-        occ = std::min(occ, kStreamCtasPerSm);
-        const long long inflight = (long long)occ * st_n * slot;
-        if (inflight >= best_bytes) {
-            best_bytes = inflight;
-            best_stages = st_n;
-            best_occ = occ;
-        }
-    }
-    if (best_stages < 1) return set_err(NEON_ERR_UNSUPPORTED, "projection chain: X and one ring slot exceed shared memory");
-    c.n_phases = n;
-    c.n_peer = n_peer;
-    c.barrier_ns = 2000000000ull;
-    if (peer) {
-        c.has_peer = 1;
-        c.peer = *peer;
-        // a CTA in an LL reduce may wait up to the communicator's bound for a peer
-        c.barrier_ns = std::max<unsigned long long>(c.barrier_ns, peer->timeout_ns + 1000000000ull);
-    }
-    c.stages = best_stages;
-    c.slot_bytes = slot;
-    c.x_bytes = xb;
-    c.d_pos = d_pos;
-    c.err = ds.err;
-    c.sync = sync;
-    return launch_n(matvec_chain_kernel, dim3(ds.sms * best_occ), kStreamBlock, xb + best_stages * slot, st, c);
-}
 int device_sms(int device) {
     int rc = init_device(device);
     return rc ? -1 : g_dev[device].sms;
@@ -1102,11 +970,6 @@ int neon_cuda_set_prefill_mma(int enabled) {
 
 int neon_cuda_set_dq_ring(int enabled) {
     g_dq_ring.store(enabled ? 1 : 0);
-    return NEON_OK;
-}
-
-int neon_cuda_set_decode_chain(int enabled) {
-    g_decode_chain.store(enabled ? 1 : 0);
     return NEON_OK;
 }
 

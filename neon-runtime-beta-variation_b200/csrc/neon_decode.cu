@@ -868,7 +868,6 @@ struct neon_model {
     float *gu = nullptr, *act = nullptr, *logits = nullptr;
     int *d_tokens = nullptr, *d_tok = nullptr, *d_pos = nullptr, *d_step = nullptr, *d_out = nullptr;
     unsigned* d_err = nullptr;
-    unsigned int* chain_sync = nullptr;    // the projection chain's barrier words (zero between launches)
     unsigned long long* am_key = nullptr;  // argmax scratch
     unsigned int* am_count = nullptr;
     size_t out_cap = 0;
@@ -1141,136 +1140,12 @@ int run_head(neon_model* m, const float* x) {
     return neon_internal::matvec(&t, 1, x, m->cfg.n_embd, 1, m->stream, 0, &ext);
 }
 
-// The projection chain (neon_cuda_set_decode_chain) takes a model whose
-// projections are all Q4_0 (one device, or tensor parallel with fused
-// collectives).
-bool chain_applies(const neon_model* m) {
-    for (const auto& L : m->layers) {
-        for (auto* w : L.w)
-            if (!w || w->type != NEON_GGML_Q4_0) return false;
-        if (!L.gateup || L.gateup->type != NEON_GGML_Q4_0) return false;
-    }
-    return true;
-}
-
-// The decode step with the projection chain: layer 0's Q/K/V as its own
-// launch, then per layer the attention launch and ONE matvec_chain_kernel
-// launch for attn_output (+= h), gate/up (rms_norm folded, SwiGLU / SiLU),
-// ffn_down (+= h) and the next layer's Q/K/V (rms_norm folded, RoPE, cache
-// rows) -- tensor parallel, each residual projection followed by its LL
-// reduce: the same arithmetic as run_step's launches, bit for bit.
-int run_step_chain(neon_model* m) {
-    const auto& c = m->cfg;
-    const size_t n_embd = c.n_embd, q_dim = m->q_dim, kv_dim = m->kv_dim, n_ff = m->n_ff_l;
-    float* hc = m->h;
-    const bool tp = m->world > 1;
-    const PeerSet peer = tp ? neon_internal::comm_peer_set(m->comm) : PeerSet{};
-    const int qkv_epi[3] = {neon::kEpiRope, neon::kEpiRope, neon::kEpiAtPos};
-    const long long qkv_stride[3] = {0, (long long)kv_dim, (long long)kv_dim};
-    const int ffn_epi = c.plain_ffn ? neon::kEpiSilu : neon::kEpiSwiglu;
-    const long long zero_stride = 0;
-    auto qkv_ext = [&](uint32_t li) {
-        neon_internal::MatvecExt ext;
-        ext.norm_w = m->layers[li].attn_norm;
-        ext.norm_eps = c.norm_eps;
-        ext.d_pos = m->d_pos;
-        ext.rope_cs = m->rope_cs;
-        ext.rope_half = (int)m->rope_half;
-        ext.head_dim = (int)c.head_dim;
-        ext.epi = qkv_epi;
-        ext.pos_stride = qkv_stride;
-        return ext;
-    };
-    auto qkv_targets = [&](uint32_t li, neon_proj_target_t (&t)[3]) {
-        const auto& L = m->layers[li];
-        float* Kl = m->K + (size_t)li * c.ctx_len * kv_dim;
-        float* Vl = m->V + (size_t)li * c.ctx_len * kv_dim;
-        t[0] = {L.w[0], m->q, q_dim};
-        t[1] = {L.w[1], Kl, kv_dim};
-        t[2] = {L.w[2], Vl, kv_dim};
-    };
-    int rc = launch_embed(m, m->d_tok, 1);
-    if (!rc) {
-        neon_proj_target_t t[3];
-        qkv_targets(0, t);
-        const neon_internal::MatvecExt ext = qkv_ext(0);
-        rc = neon_internal::matvec(t, 3, hc, n_embd, 1, m->stream, 0, &ext);
-    }
-    for (uint32_t li = 0; li < c.n_layer && !rc; ++li) {
-        const auto& L = m->layers[li];
-        const float* Kl = m->K + (size_t)li * c.ctx_len * kv_dim;
-        const float* Vl = m->V + (size_t)li * c.ctx_len * kv_dim;
-        rc = launch_attn_decode(m, Kl, Vl);
-        if (rc) break;
-        // one device: attn_output and ffn_down accumulate into h; tensor
-        // parallel: they store their partial rows as LL words into every
-        // rank's slot and an LL-reduce phase adds the ranks' rows into h
-        float* res_y = tp ? m->part : hc;
-        const neon_proj_target_t t_out{L.w[3], res_y, n_embd}, t_gu{L.gateup, m->act, n_ff},
-            t_down{L.w[4], res_y, n_embd};
-        neon_proj_target_t t_qkv[3];
-        neon_internal::ChainPhaseDesc ph[6];  // the chain takes up to six phases
-        int n = 0;
-        auto residual = [&](const neon_proj_target_t* t, const float* x) {
-            ph[n].t = t;
-            ph[n].n = 1;
-            ph[n].x = x;
-            if (tp) {
-                ph[n].ext.peer_mode = 1;
-                ph[n].ext.peer = peer;
-                ++n;
-                ph[n].ll_h = hc;
-                ph[n].ll_len = (int)n_embd;
-            } else {
-                ph[n].accumulate = 1;
-            }
-            ++n;
-        };
-        residual(&t_out, m->att);
-        ph[n].t = &t_gu;
-        ph[n].n = 1;
-        ph[n].x = hc;
-        ph[n].ext.norm_w = L.ffn_norm;
-        ph[n].ext.norm_eps = c.norm_eps;
-        ph[n].ext.epi = &ffn_epi;
-        ph[n].ext.pos_stride = &zero_stride;
-        ++n;
-        residual(&t_down, m->act);
-        if (li + 1 < c.n_layer) {
-            qkv_targets(li + 1, t_qkv);
-            ph[n].t = t_qkv;
-            ph[n].n = 3;
-            ph[n].x = hc;
-            ph[n].ext = qkv_ext(li + 1);
-            ++n;
-        }
-        rc = neon_internal::matvec_chain(ph, n, m->d_pos, m->chain_sync, tp ? &peer : nullptr, m->stream);
-        if (rc == NEON_ERR_UNSUPPORTED) {
-            // a shape the chain does not take (nothing was launched): the phases one launch each
-            rc = NEON_OK;
-            for (int p = 0; p < n && !rc; ++p) {
-                if (ph[p].ll_h) {
-                    rc = neon_internal::comm_ll_reduce(m->comm, hc, (long long)n_embd, m->stream);
-                    continue;
-                }
-                neon_internal::MatvecExt ext = ph[p].ext;
-                ext.d_pos = m->d_pos;
-                const size_t cols = ph[p].t[0].W->cols;
-                rc = neon_internal::matvec(ph[p].t, (size_t)ph[p].n, ph[p].x, cols, 1, m->stream, ph[p].accumulate, &ext);
-            }
-        }
-    }
-    return rc;
-}
-
 // One decode position (token in *d_tok, position *d_pos): the fused step.
 //
 // Tensor parallel with fused collectives: attn_output and ffn_down store their
 // partial rows as LL words straight into every rank's slot, and a small
 // reduce launch adds the ranks' rows into the residual.
 int run_step(neon_model* m) {
-    if (neon_internal::decode_chain() && chain_applies(m) && (m->world == 1 || neon_internal::fused_collectives()))
-        return run_step_chain(m);
     const auto& c = m->cfg;
     int rc = launch_embed(m, m->d_tok, 1);
     const size_t n_embd = c.n_embd, q_dim = m->q_dim, kv_dim = m->kv_dim, n_ff = m->n_ff_l;
@@ -1372,10 +1247,7 @@ int sync_and_check(neon_model* m) {
         const int rc = neon_cuda_comm_check(static_cast<neon_comm*>(m->comm));
         if (rc) return rc;
     }
-    const int rc = neon_internal::check_device_error(m->device);
-    // a launch that gave up waiting leaves the chain's barrier words set
-    if (rc && m->chain_sync) cudaMemset(m->chain_sync, 0, 4 * sizeof(unsigned int));
-    return rc;
+    return neon_internal::check_device_error(m->device);
 }
 
 // Tokens [0, n) of `tokens_dev` at positions length..; logits of the last.
@@ -1504,7 +1376,6 @@ int neon_cuda_model_create_tp(const neon_model_config_t* cfg, neon_comm_t comm, 
     A((void**)&m->d_pos, sizeof(int));
     A((void**)&m->d_step, sizeof(int));
     A((void**)&m->d_err, sizeof(unsigned));
-    A((void**)&m->chain_sync, 4 * sizeof(unsigned int));
     if (!rc) rc = cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) == cudaSuccess ? NEON_OK : error(NEON_ERR_CUDA, "cudaStreamCreate");
     if (!rc) rc = (cudaEventCreate(&m->ev0) == cudaSuccess && cudaEventCreate(&m->ev1) == cudaSuccess &&
                    cudaEventCreate(&m->evf0) == cudaSuccess && cudaEventCreate(&m->evf1) == cudaSuccess)
@@ -1527,7 +1398,6 @@ int neon_cuda_model_create_tp(const neon_model_config_t* cfg, neon_comm_t comm, 
             cudaMemset(m->d_err, 0, sizeof(unsigned)) != cudaSuccess || cudaMemset(m->K, 0, kv_bytes) != cudaSuccess ||
             cudaMemset(m->am_key, 0, sizeof(unsigned long long)) != cudaSuccess ||
             cudaMemset(m->am_count, 0, sizeof(unsigned int)) != cudaSuccess ||
-            cudaMemset(m->chain_sync, 0, 4 * sizeof(unsigned int)) != cudaSuccess ||
             cudaMemset(m->V, 0, kv_bytes) != cudaSuccess)
             rc = error(NEON_ERR_CUDA, "model initialisation copies failed");
     }

@@ -145,29 +145,6 @@ struct MatvecExt {
 int matvec(const neon_proj_target_t* targets, size_t n, const float* dX, size_t x_stride, size_t seq,
            cudaStream_t st, int accumulate, const MatvecExt* ext = nullptr);
 
-// One phase of a decode projection chain (matvec_chain): one position of Q4_0
-// targets sharing their input dim, X, the accumulate flag and the epilogue
-// options of `ext` (its d_pos and peer fields are not used).
-struct ChainPhaseDesc {
-    const neon_proj_target_t* t = nullptr;
-    int n = 0;
-    const float* x = nullptr;
-    int accumulate = 0;
-    MatvecExt ext{};       // peer_mode 1: the targets' rows go as LL words to every rank (one target)
-    // an LL-reduce phase instead (tensor parallel): h[i] += the ranks' words of
-    // the last kEpiPeer phase before it, i < len; no targets
-    float* ll_h = nullptr;
-    int ll_len = 0;
-};
-// The phases as one launch of matvec_chain_kernel (grid barriers between
-// them; `sync`: three zeroed device words the launch leaves zeroed; `peer`:
-// the communicator's LL set when a phase is kEpiPeer or LL-reduce, else
-// null). NEON_ERR_UNSUPPORTED, with nothing launched, when a phase does not
-// fit it (a type other than Q4_0, more than 3 targets, more than 6 phases,
-// X too large for shared memory).
-int matvec_chain(const ChainPhaseDesc* phases, int n, const int* d_pos, unsigned int* sync, const PeerSet* peer,
-                 cudaStream_t st);
-bool decode_chain();  // neon_cuda_set_decode_chain
 int error(int code, const std::string& msg);
 // Bytes of one GGUF row of `type` with `cols` values (0: unsupported type, or
 // cols not a multiple of the type's block size). rawllm_loader.hpp:367-386.

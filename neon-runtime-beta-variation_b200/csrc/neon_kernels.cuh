@@ -471,7 +471,7 @@ __host__ __device__ constexpr int stream_x_bytes(int type, int nb) {
 
 // X loads of the staging functions: read-only through the non-coherent path
 // (X was written by an earlier kernel), or with CG through L2 only, for X
-// written earlier in the same launch by other CTAs (matvec_chain_kernel).
+// written earlier in the same launch by other CTAs.
 template <bool CG>
 __device__ __forceinline__ float ld_x(const float* p) {
     if constexpr (CG) return __ldcg(p);

@@ -99,7 +99,6 @@ C_ENTRY_POINTS = (
     "neon_cuda_set_pdl",
     "neon_cuda_set_prefill_mma",
     "neon_cuda_set_dq_ring",
-    "neon_cuda_set_decode_chain",
     "neon_cuda_set_stream_tiles",
     "neon_cuda_set_resident",
 )
@@ -165,7 +164,6 @@ def load(path: str | None = None) -> C.CDLL:
         L.neon_cuda_set_pdl.argtypes = [C.c_int]
         L.neon_cuda_set_prefill_mma.argtypes = [C.c_int]
         L.neon_cuda_set_dq_ring.argtypes = [C.c_int]
-        L.neon_cuda_set_decode_chain.argtypes = [C.c_int]
         L.neon_cuda_set_stream_tiles.argtypes = [C.c_int, C.c_int]
         L.neon_cuda_set_resident.argtypes = [C.c_int]
         L.neon_cuda_matvec_q4_0_noalloc.argtypes = [_vp, _vp, _sz, _vp, _sz, _sz, _vp]
@@ -226,13 +224,6 @@ def set_dq_ring(enabled: bool) -> None:
     kernel (several row tiles in flight per CTA) instead of the register-buffer
     kernel; process-wide, off by default."""
     _check(load().neon_cuda_set_dq_ring(1 if enabled else 0))
-
-
-def set_decode_chain(enabled: bool) -> None:
-    """Decode steps of one-device Q4_0 models with the projections between two
-    attention launches as one launch (grid barriers between them); read when a
-    model captures its step; process-wide, off by default."""
-    _check(load().neon_cuda_set_decode_chain(1 if enabled else 0))
 
 
 def set_stream_tiles(rows_per_tile: int = 0, blocks_per_chunk: int = 0) -> None:

@@ -18,14 +18,3 @@ extern "C" void stream_host_plan(int type, int nb, size_t total_rows, int sms, i
     out[6] = neon::stream_scale_pitch(p.kc);
     out[7] = neon::stream_x_bytes(type, nb);
 }
-
-#include "neon_chain.cuh"
-
-// The projection chain's ring (neon::plan_chain_ring): out = {slot bytes, X bytes, stages that fit}.
-extern "C" void stream_host_chain_ring(const int* nb, const size_t* rows, int n, int sms, int stage_target,
-                                       int max_smem, int* out) {
-    const neon::ChainRing r = neon::plan_chain_ring(nb, rows, n, sms, stage_target, max_smem, 0, 0);
-    out[0] = r.slot_bytes;
-    out[1] = r.x_bytes;
-    out[2] = r.max_stages;
-}

@@ -33,14 +33,35 @@ def test_tiny_golden_generation():
     assert m.length == len(g["prompt"]) + 16
 
 
-def test_tiny_forward_logits_and_kv():
+def close(a, b, strict):
+    """Per-element bar on the CUDA-core prompt path (the same arithmetic as the
+    golden up to fp32 summation order); on the tensor-core path (the default),
+    whose prompt attention sums in another order, the whole-model bar: a
+    1e-7 difference can flip a Q8_0 activation at a rounding tie downstream
+    (conftest.py)."""
+    return max_rel_err(a, b) <= MATVEC_RTOL if strict else rel_l2(a, b) <= MODEL_L2_RTOL
+
+
+PREFILL = [pytest.param(False, id="cuda_core_prefill"), pytest.param(True, id="tensor_core_prefill")]
+
+
+@pytest.fixture
+def prefill(request):
+    N.set_prefill_mma(request.param)
+    yield request.param
+    N.set_prefill_mma(True)  # the default
+
+
+@pytest.mark.parametrize("prefill", PREFILL, indirect=True)
+def test_tiny_forward_logits_and_kv(prefill):
+    strict = not prefill
     g = load_golden("decode_tiny.npz")
     m = N.Model(TINY, S.model_tensors(TINY, seed=3))
     logits = m.forward(g["prompt"])
-    assert max_rel_err(logits, g["logits"][0]) <= MATVEC_RTOL
+    assert close(logits, g["logits"][0], strict)
     for i, t in enumerate(g["tokens"][:6]):
         logits = m.forward([t])
-        assert max_rel_err(logits, g["logits"][i + 1]) <= MATVEC_RTOL, f"step {i}"
+        assert close(logits, g["logits"][i + 1], strict), f"step {i}"
     o = O.Model(TINY, list(S.model_tensors(TINY, seed=3)), "port")
     o.forward(g["prompt"])
     for t in g["tokens"][:6]:
@@ -49,16 +70,17 @@ def test_tiny_forward_logits_and_kv():
     for layer in range(TINY.n_layer):
         k1, v1 = m.read_kv(layer, n)
         k2, v2 = o.kv(layer, n)
-        assert max_rel_err(k1, k2) <= MATVEC_RTOL and max_rel_err(v1, v2) <= MATVEC_RTOL
+        assert close(k1, k2, strict) and close(v1, v2, strict)
 
 
-def test_rewind_and_eos():
+@pytest.mark.parametrize("prefill", PREFILL, indirect=True)
+def test_rewind_and_eos(prefill):
     g = load_golden("decode_tiny.npz")
     m = N.Model(TINY, S.model_tensors(TINY, seed=3))
     m.forward(g["prompt"])
     m.set_length(3)  # keep the first 3 prompt positions, re-feed the rest
     logits = m.forward(g["prompt"][3:])
-    assert max_rel_err(logits, g["logits"][0]) <= MATVEC_RTOL
+    assert close(logits, g["logits"][0], not prefill)
     # stopping before the eos token, as run_generation does
     m2 = N.Model(TINY, S.model_tensors(TINY, seed=3))
     eos = int(g["tokens"][5])

@@ -18,7 +18,6 @@ from conftest import PKG, ROOT
 
 Q4_0, Q8_0 = 2, 8
 STAGE_TARGET, MAX_SMEM, MAX_STAGES = 80 * 1024, 220 * 1024, 3  # the streaming kernel's stage target
-CHAIN_STAGE_TARGET = 40 * 1024  # the projection chain's
 
 
 @pytest.fixture(scope="module")
@@ -32,13 +31,12 @@ def lib(tmp_path_factory):
     L = C.CDLL(so)
     L.stream_host_plan.argtypes = [C.c_int, C.c_int, C.c_size_t, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
                                    C.c_void_p]
-    L.stream_host_chain_ring.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p]
     return L
 
 
-def plan(L, typ, nb, rows, rc=0, kc=0, sms=148, stage_target=STAGE_TARGET):
+def plan(L, typ, nb, rows, rc=0, kc=0, sms=148):
     out = (C.c_int * 8)()
-    L.stream_host_plan(typ, nb, rows, sms, stage_target, MAX_SMEM, rc, kc, out)
+    L.stream_host_plan(typ, nb, rows, sms, STAGE_TARGET, MAX_SMEM, rc, kc, out)
     return dict(zip(("rc", "kc", "nch", "stages", "stage_bytes", "smem", "sph", "x_bytes"), out))
 
 
@@ -112,31 +110,3 @@ def test_every_forced_shape(lib, typ, rows, cols):
             if p["smem"] > MAX_SMEM:
                 continue  # refused by the launcher before any launch
             emulate(p, typ, rows, nb)
-
-
-# (name, n_embd, n_head, n_kv_head, head_dim, n_ff): the decode benchmark models
-MODELS = [("qwen3", 1024, 16, 8, 128, 3072), ("phi4", 3072, 24, 8, 128, 8192), ("llama70b", 8192, 64, 8, 128, 28672)]
-
-
-@pytest.mark.parametrize("name,n_embd,n_head,n_kv,hd,n_ff", MODELS, ids=[m[0] for m in MODELS])
-@pytest.mark.parametrize("world", [1, 2, 4, 8])
-def test_projection_chain_fits(lib, name, n_embd, n_head, n_kv, hd, n_ff, world):
-    """The projection chain's phases at the benchmark models and tensor-parallel
-    widths (attn_output, gate/up, down, the next layer's Q/K/V, each rank's
-    shard): X and at least two ring slots fit shared memory, so the chain takes
-    these layers; each phase's items use its own plan, checked above, inside a
-    slot at least its stage's size."""
-    q_dim, kv_dim = n_head * hd, n_kv * hd
-    if n_kv % world:
-        pytest.skip("KV heads do not split over this many ranks")
-    phases = [(q_dim // world // 32, n_embd), (n_embd // 32, 2 * n_ff // world), (n_ff // world // 32, n_embd),
-              (n_embd // 32, (q_dim + 2 * kv_dim) // world)]
-    nb = (C.c_int * 4)(*[p[0] for p in phases])
-    rows = (C.c_size_t * 4)(*[p[1] for p in phases])
-    out = (C.c_int * 3)()
-    lib.stream_host_chain_ring(nb, rows, 4, 148, CHAIN_STAGE_TARGET, MAX_SMEM, out)
-    slot, xb, stages = list(out)
-    assert stages >= 2 and xb + stages * slot <= MAX_SMEM
-    for b, r in phases:
-        p = plan(lib, Q4_0, b, r, stage_target=CHAIN_STAGE_TARGET)
-        assert p["stage_bytes"] <= slot and p["x_bytes"] <= xb

@@ -53,37 +53,11 @@ def allreduce_cases(comm, rank, world, dev):
     return out
 
 
-def chain_cases(comm, qwen, a, res):
-    """Tokens and logits of the small and the Qwen3-shaped decoders split over
-    the ranks, with the projection chain off and on (fused collectives)."""
-    NC.set_fused_collectives(True)
-    for name, cfg, tensors, prompt, steps in (
-            ("tiny", TINY, list(S.model_tensors(TINY, seed=3)), S.prompt_tokens(9, TINY.n_vocab, 4), 12),
-            ("qwen", qwen, list(S.model_tensors(qwen, seed=21)), S.prompt_tokens(a.qwen_prompt, qwen.n_vocab, 22),
-             a.qwen_steps)):
-        for chain in (False, True):
-            NC.set_decode_chain(chain)
-            m = NC.Model(cfg, tensors, comm)
-            dist.barrier()
-            toks = m.generate(prompt, steps)
-            m.set_length(0)
-            dist.barrier()
-            logits = [m.forward(prompt)] + [m.forward([t]) for t in toks[:4]]
-            tag = f"{name}_{'chain' if chain else 'plain'}"
-            res[tag + "_tokens"], res[tag + "_logits"] = toks, np.stack(logits)
-            res[tag + "_ms"] = np.array(m.decode_ms)
-            m.free()
-    NC.set_decode_chain(False)
-    comm.check()
-
-
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--out", required=True)
     ap.add_argument("--qwen-prompt", type=int, default=128)
     ap.add_argument("--qwen-steps", type=int, default=32)
-    ap.add_argument("--chain", action="store_true",
-                    help="only the projection chain: each model decoded with it off and on (fused collectives)")
     a = ap.parse_args()
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
@@ -97,12 +71,6 @@ def main():
     comm = NC.Comm.from_process_group(floats)
     comm.set_timeout(20.0)
     try:
-        if a.chain:
-            chain_cases(comm, qwen, a, res)
-            if rank == 0:
-                np.savez(a.out, **res)
-            dist.barrier()
-            return
         for name, err in allreduce_cases(comm, rank, world, dev):
             res[f"allreduce_{name}"] = np.array(err)
 
