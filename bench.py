@@ -21,8 +21,13 @@ y) per second, whole job.
             the reference's own CPU path (oracle/_ref, rawllm_forward.hpp
             compiled with its flags) on this host's cores, bounded sample.
 
-With --gpus N under torchrun every rank runs its own rotation (weak scaling,
-no data-path collective); value = all ranks' bytes / max-over-ranks time.
+With --gpus N under torchrun the same matrices are split by rows over the N
+ranks (strong scaling): each call is the row-sharded matvec with the output
+all-gathered on every rank (neon_cuda_matvec_allgather, the fused NVLink
+all-gather); value = the whole matrices' bytes / max-over-ranks time. The
+`decode` list carries batch-1 decode tokens/s (Qwen3-0.6B-shaped at 1 GPU,
+Phi-4-mini-shaped at 1 and 2, Llama-3-70B-shaped tensor parallel over all N)
+and, at 1 GPU, `sweep` the other Q4_0 / Q8_0 matvec shapes.
 --impl reference times the reference's CPU path alone (rank 0 only).
 """
 from __future__ import annotations
@@ -48,7 +53,7 @@ UNIT = "GB/s"
 CALLS_PER_STEP = 1024
 ROTATION_BYTES = 3 * 126e6  # weights rotated per step: 3x the L2
 FALLBACK_HBM_GBS = 6650.0
-KERNEL = "matvec_stream_kernel"
+KERNEL = "matvec_resident_kernel"
 
 # name -> (ggml type, rows, cols); the first is the headline workload.
 WORKLOADS = {
@@ -88,13 +93,25 @@ def select_workload(name):
         return
     TYPE, ROWS, COLS = WORKLOADS[name]
     TYPE_NAME = S.TYPE_NAMES[TYPE]
-    KERNEL = "matvec_stream_kernel" if TYPE in (S.GGML_Q4_0, S.GGML_Q8_0) else "matvec_dq_kernel"
+    KERNEL = one_position_kernel(TYPE, ROWS, COLS)
     METRIC = f"{TYPE_NAME} matvec HBM GB/s vs peak"
     ROTATION = max(2, int(-(-ROTATION_BYTES // (ROWS * S.row_bytes(TYPE, COLS)))))
 
 
+def one_position_kernel(t, rows, cols):
+    """The kernel the library runs for one position of this workload on one
+    GPU: Q4_0 / Q8_0 matrices of up to ~10 MB take the resident kernel (their
+    per-CTA share fits shared memory beside the next launch's; the plan is
+    csrc/neon_resident.cuh, checked at these shapes by
+    tests/test_resident_plan_cpu.py), larger ones the streaming kernel, the
+    other types the dequantising kernel."""
+    if t not in (S.GGML_Q4_0, S.GGML_Q8_0):
+        return "matvec_dq_kernel"
+    return "matvec_resident_kernel" if rows * S.row_bytes(t, cols) <= 10_000_000 else "matvec_stream_kernel"
+
+
 def profile_summary_path():
-    kind = "stream" if KERNEL == "matvec_stream_kernel" else "dq"
+    kind = {"matvec_stream_kernel": "stream", "matvec_resident_kernel": "resident"}.get(KERNEL, "dq")
     return os.path.join(ROOT, "profiles", f"matvec_{kind}_{TYPE_NAME.lower()}_{ROWS}x{COLS}.txt")
 
 
@@ -133,6 +150,8 @@ def parse_args():
     p.add_argument("--layers", type=int, default=None,
                    help="decode workloads: fewer layers (kernel shapes unchanged; for profiling)")
     p.add_argument("--no-decode", action="store_true", help="matvec workloads: skip the decode sub-measurements")
+    p.add_argument("--no-sweep", action="store_true",
+                   help="matvec workloads: skip the sweep of the other Q4_0 / Q8_0 benchmark shapes")
     p.add_argument("--weights", choices=["q4_0", "q4_k"], default="q4_0",
                    help="decode workloads: Q4_0 projections + Q8_0 embedding (default), or Q4_K + Q6_K "
                         "(what nanity_convert.py --quant Q4_K writes)")
@@ -564,6 +583,37 @@ def run_reference(args):
 # GPU arm
 # ---------------------------------------------------------------------------
 
+SWEEP_WORKLOADS = ["q8_0_4096x4096", "q8_0_14336x4096", "q8_0_4096x14336", "q4_0_28672x8192", "q4_0_8192x28672"]
+
+
+def measure_sweep(N, torch, stream, steps=20, warmup=3):
+    """The other one-position Q4_0 / Q8_0 benchmark shapes (the Q8_0 sweep of
+    the matvec configurations and the Llama-3-70B FFN shapes), each timed as
+    the headline is (a CUDA graph of 1024 calls over a rotation larger than
+    L2), with its own roofline fraction. Restores the headline workload."""
+    head = (TYPE, ROWS, COLS, ROTATION, METRIC, TYPE_NAME, KERNEL)
+    peak, peak_kind = measured_peak()
+    out = []
+    try:
+        for name in SWEEP_WORKLOADS:
+            select_workload(name)
+            tensors = [N.DeviceTensor(w, TYPE, ROWS, COLS) for w in host_rotation(0, ROTATION)]
+            gbs, us = time_matvec_graph(N, torch, stream, tensors, steps, warmup)
+            out.append({"workload": name, "rows": ROWS, "cols": COLS, "type": TYPE_NAME, "kernel": KERNEL,
+                        "value": round(gbs, 1), "unit": UNIT, "us_per_call": round(us, 3),
+                        "frac": round(gbs / peak, 4), "peak": peak, "peak_source": peak_kind,
+                        "bytes_per_call": S.algorithmic_bytes(TYPE, ROWS, COLS), "rotation_tensors": ROTATION,
+                        "steps": steps, "warmup": warmup})
+            del tensors
+            torch.cuda.synchronize()
+            torch.cuda.empty_cache()
+    finally:
+        g = globals()
+        for k, v in zip(("TYPE", "ROWS", "COLS", "ROTATION", "METRIC", "TYPE_NAME", "KERNEL"), head):
+            g[k] = v
+    return out
+
+
 def run_neon(args):
     import torch
     import torch.distributed as dist
@@ -590,24 +640,47 @@ def run_neon(args):
         N.set_resident(args.resident)
     dev = torch.device("cuda", local)
 
-    host_w = host_rotation(rank, ROTATION)
-    tensors = [N.DeviceTensor(w, TYPE, ROWS, COLS) for w in host_w]
+    # One GPU: a rotation of whole matrices. N > 1 (strong scaling): every rank
+    # keeps its row shard of the SAME matrices (N times as many, so that each
+    # rank's shards still exceed L2) and each call is the row-sharded matvec
+    # with its output all-gathered on every rank (neon_cuda_matvec_allgather).
+    tp = world > 1
+    comm_mv = None
+    row0 = ROWS * rank // world
+    if tp:
+        comm_mv = N.Comm.from_process_group(4096)
+        comm_mv.set_timeout(30.0)
+        rot = ROTATION * world
+        host_w = None
+        tensors = [N.DeviceTensor(S.weights(TYPE, ROWS, COLS, seed=i), TYPE, ROWS, COLS, N.SHARD_ROWS, rank, world)
+                   for i in range(rot)]
+    else:
+        rot = ROTATION
+        host_w = host_rotation(rank, ROTATION)
+        tensors = [N.DeviceTensor(w, TYPE, ROWS, COLS) for w in host_w]
     x_host = S.activations(1, COLS, seed=7)
     dx = torch.from_numpy(x_host).to(dev)
     assert x_host.shape == (1, COLS)
-    ys = torch.zeros((ROTATION, ROWS), device=dev)
+    ys = torch.zeros((rot, ROWS), device=dev)
     stream = torch.cuda.Stream(device=dev)
+
+    def call(j, s, x=dx, y=None):
+        t = tensors[j % rot]
+        y = ys[j % rot] if y is None else y
+        if tp:
+            comm_mv.matvec_allgather(t, x, y, ROWS, row0, stream=s)
+        else:
+            t.matvec(x, y, stream=s)
 
     def launch_step(s):
         for j in range(CALLS_PER_STEP):
-            t = tensors[j % ROTATION]
-            t.matvec(dx, ys[j % ROTATION], stream=s)
+            call(j, s)
 
     with torch.cuda.stream(stream):
-        tensors[0].matvec(dx, ys[0], stream=stream)
+        call(0, stream)
     stream.synchronize()
 
-    # capture one step (1024 launches) in a CUDA graph
+    # capture one step (1024 calls) in a CUDA graph
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
         launch_step(stream)
@@ -646,32 +719,55 @@ def run_neon(args):
     if sampler:
         sampler.stop()
     assert N.launch_count() == launches_before, "graph replay should not go through the launch API"
-    gpu_launches = K * CALLS_PER_STEP
-    bytes_call = S.algorithmic_bytes(TYPE, ROWS, COLS)
-    total_bytes = world * K * CALLS_PER_STEP * bytes_call
+    gpu_launches = K * CALLS_PER_STEP * (2 if tp else 1)
+    bytes_call = S.algorithmic_bytes(TYPE, ROWS, COLS)  # the whole matrix, x and y of one call
+    total_bytes = (1 if tp else world) * K * CALLS_PER_STEP * bytes_call
     value = total_bytes / (ms / 1e3) / 1e9
-    per_launch_s = ms / 1e3 / (K * CALLS_PER_STEP)
-    achieved = bytes_call / per_launch_s / 1e9
+    per_call_s = ms / 1e3 / (K * CALLS_PER_STEP)
+    achieved = bytes_call / world / per_call_s / 1e9  # one GPU's share of the bytes over the call's time
 
-    # end to end through the public host-buffer API
+    # end to end: host buffers in and out every call (pinned), blocking
     x_pin = torch.from_numpy(x_host.copy()).pin_memory()
     y_pin = torch.zeros(ROWS, dtype=torch.float32).pin_memory()
-    x_np, y_np = x_pin.numpy(), y_pin.numpy()
-    infos = [N.TensorInfo(f"rot{i}", [COLS, ROWS], TYPE, host_w[i]) for i in range(ROTATION)]
-    for i in range(ROTATION):  # upload happens once, at "load" time, outside the timed region
-        N.proj_all_positions(infos[i], x_np, COLS, y_np, ROWS, 1)
     e2e_steps = max(1, min(args.e2e_steps, K))
+    if tp:
+        dx_e = torch.empty(COLS, device=dev)
+        dy_e = torch.empty(ROWS, device=dev)
+
+        def e2e_call(j):
+            with torch.cuda.stream(stream):
+                dx_e.copy_(x_pin[0], non_blocking=True)
+                call(j, stream, dx_e, dy_e)
+                y_pin.copy_(dy_e, non_blocking=True)
+            stream.synchronize()
+        api = "neon_cuda_matvec_allgather per call: pinned host x in, host y out, blocking"
+    else:
+        x_np, y_np = x_pin.numpy(), y_pin.numpy()
+        infos = [N.TensorInfo(f"rot{i}", [COLS, ROWS], TYPE, host_w[i]) for i in range(rot)]
+        for i in range(rot):  # upload happens once, at "load" time, outside the timed region
+            N.proj_all_positions(infos[i], x_np, COLS, y_np, ROWS, 1)
+
+        def e2e_call(j):
+            N.proj_all_positions(infos[j % rot], x_np, COLS, y_np, ROWS, 1)
+        api = "neon_cuda.proj_all_positions (host buffers, blocking per call)"
+    e2e_call(0)
     barrier()
     t0 = time.perf_counter()
     for _ in range(e2e_steps):
         for j in range(CALLS_PER_STEP):
-            N.proj_all_positions(infos[j % ROTATION], x_np, COLS, y_np, ROWS, 1)
+            e2e_call(j)
     e2e_s = time.perf_counter() - t0
     if world > 1:
         t = torch.tensor([e2e_s], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
-    e2e_value = world * e2e_steps * CALLS_PER_STEP * bytes_call / e2e_s / 1e9
+    e2e_value = (1 if tp else world) * e2e_steps * CALLS_PER_STEP * bytes_call / e2e_s / 1e9
+    if tp:
+        comm_mv.check()
+
+    sweep = None
+    if world == 1 and not args.no_sweep:
+        sweep = measure_sweep(N, torch, stream)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -685,6 +781,13 @@ def run_neon(args):
         torch.cuda.synchronize()
         torch.cuda.empty_cache()
         decode = []
+        def max_over(v):
+            if world == 1:
+                return v
+            t = torch.tensor([float(v)], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            return float(t.item())
+
         if world == 1:
             d, dcfg, dprompt = measure_decode_gpu("decode_qwen3")
             if not args.no_cpu_baseline:
@@ -695,19 +798,26 @@ def run_neon(args):
             d["parity"] = ("greedy tokens identical to the reference's transformer_forward over 64 steps "
                            "(tests/test_decode_gpu.py)")
             decode.append(decode_roofline(d, dcfg, 1))
+        if world <= 2:
+            # the Phi-4-mini-shaped decoder, at 1 and 2 GPUs
+            pcomm = None
+            if world > 1:
+                pcfg0, _, _ = decode_config("decode_phi4")
+                pcomm = N.Comm.from_process_group(N.model_comm_floats(pcfg0, world))
+                pcomm.set_timeout(30.0)
+            d, dcfg, _ = measure_decode_gpu("decode_phi4", comm=pcomm, barrier=barrier, max_over_ranks=max_over)
+            d["parity"] = ("greedy tokens identical to the reference's transformer_forward (Phi-4-mini-shaped, "
+                           "tests/test_decode_gpu.py)")
+            decode.append(decode_roofline(d, dcfg, world))
+            if pcomm is not None:
+                barrier()
+                pcomm.free()
         if not args.no_large_decode:
             comm = None
             if world > 1:
                 cfg0, _, _ = decode_config("decode_llama70b")
                 comm = N.Comm.from_process_group(N.model_comm_floats(cfg0, world))
                 comm.set_timeout(30.0)
-
-            def max_over(v):
-                if world == 1:
-                    return v
-                t = torch.tensor([float(v)], device=dev, dtype=torch.float64)
-                dist.all_reduce(t, op=dist.ReduceOp.MAX)
-                return float(t.item())
             d, dcfg, _ = measure_decode_gpu("decode_llama70b", comm=comm, barrier=barrier, max_over_ranks=max_over)
             d["parity"] = ("split decode: greedy tokens identical to one GPU and to the reference on the "
                            "Qwen3-shaped decoder at 2 GPUs (tests/test_tp_gpu.py)")
@@ -722,29 +832,35 @@ def run_neon(args):
         clocks = sampler.summary(t_wall0, t_wall1) if sampler else {}
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": K,
-            "warmup": W, "ms_per_step": round(ms / K, 5), "higher_is_better": True, "scaling": "weak",
+            "warmup": W, "ms_per_step": round(ms / K, 5), "higher_is_better": True,
+            "scaling": "strong" if tp else "weak",
             "vs_baseline": None,
             "dtype": compute_dtype(TYPE),
             "data": "synthetic",
-            "config": {**workload_config(), "parallelism": f"dp{world} (independent rotations)",
+            "config": {**workload_config(), "rotation_tensors": rot,
+                       "parallelism": (f"tp{world}: row shards, output all-gathered on every rank every call "
+                                       "(neon_cuda_matvec_allgather)") if tp else "one GPU",
                        "variants": [v for v, on in (("dq_ring", args.dq_ring),
                                                     ("cuda_core_prefill", args.cuda_core_prefill)) if on]
                        + ([f"tiles {args.tiles}"] if args.tiles else [])
                        + ([f"resident {args.resident}"] if args.resident is not None else []),
-                       "launch": "CUDA graph of 1024 PDL launches per step"},
+                       "launch": f"CUDA graph of 1024 calls per step ({2 if tp else 1} PDL launches per call)"},
             "e2e": {"value": round(e2e_value, 2), "unit": UNIT,
                     "h2d_bytes_per_step": CALLS_PER_STEP * COLS * 4,
                     "d2h_bytes_per_step": CALLS_PER_STEP * ROWS * 4,
-                    "api": "neon_cuda.proj_all_positions (host buffers, blocking per call)",
-                    "steps": e2e_steps},
+                    "api": api, "steps": e2e_steps},
             "roofline": {"bound": "hbm", "kernel": (KERNEL.replace("matvec_dq_kernel", "matvec_dq_ring_kernel")
                                                     if args.dq_ring else KERNEL),
                          "achieved": round(achieved, 1),
                          "peak": peak, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
                          if peak_kind == "measured" else "fallback 6.65 TB/s",
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
-                         "traffic": traffic, "algorithmic_bytes_per_launch": bytes_call},
+                         "traffic": traffic if not tp else None,
+                         "algorithmic_bytes_per_launch": bytes_call // world,
+                         "note": ("one GPU's shard bytes over the time of a whole call (its matvec and the "
+                                  "all-gather launch)") if tp else "bytes of one launch over its time in the graph"},
             "cpu_baseline": cpu,
+            "sweep": sweep,
             "decode": decode,
             "gpu_launches": gpu_launches,
             "clocks": clocks,
@@ -752,6 +868,9 @@ def run_neon(args):
         print(json.dumps(line), flush=True)
     if args.no_decode:
         del graph
+    if comm_mv is not None:
+        barrier()
+        comm_mv.free()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -308,6 +308,23 @@ NEON_API int neon_cuda_model_free(neon_model_t m);
  * the communicator must be recreated. Never run two ranks on one GPU. */
 typedef struct neon_comm* neon_comm_t;
 
+/* Row-sharded tensor-parallel matvec with the output all-gathered, one
+ * position: every rank passes its row shard W of an n_total-row matrix (rows
+ * [row0, row0 + W's rows) of it, e.g. a NEON_SHARD_ROWS upload) and the same
+ * X; afterwards dY[0 .. n_total) holds the whole product on every rank. The
+ * shard's matvec stores each row straight into every rank's communicator
+ * buffer over NVLink (an 8-byte word carrying the value and the call number),
+ * and a second launch copies the n_total words of this rank's buffer into dY
+ * once they all carry this call (bounded waits; a peer that never writes
+ * leaves the communicator's error set, see neon_cuda_comm_check). The ranks'
+ * shards must tile [0, n_total) exactly, n_total <= 65536, and every rank
+ * must make the same sequence of collective calls. No counterpart in the
+ * reference (its HIP backend's only collective is all_reduce_sum,
+ * rawllm_rocm.hpp:531-562); the all-gather at the row-shard boundary of the
+ * tensor-parallel matvec. */
+NEON_API int neon_cuda_matvec_allgather(neon_comm_t c, neon_tensor_t W, const float* dX, float* dY, size_t n_total,
+                                        size_t row0, void* stream);
+
 NEON_API int neon_cuda_comm_create(int rank, int world, size_t max_floats, neon_comm_t* out);
 /* CUDA IPC handle of this rank's buffer; handle_out NULL: only the size. */
 NEON_API int neon_cuda_comm_ipc_handle(neon_comm_t c, void* handle_out, size_t* handle_bytes);

@@ -322,6 +322,44 @@ __global__ void __launch_bounds__(256) comm_ll_reduce_kernel(PeerSet p, float* _
     }
 }
 
+// Second half of a fused all-gather (each rank's row-shard matvec stored its
+// rows as LL words at their places in the gather slot of every rank): y[i] =
+// the value of word i of this rank's gather slot, for i < n, waiting
+// (bounded) until the word carries this call; all of a thread's loads are
+// issued before any wait. The last CTA records the call as completed.
+__global__ void __launch_bounds__(256) comm_ll_gather_kernel(PeerSet p, float* __restrict__ y, int n) {
+    __shared__ int s_skip;
+    pdl_wait_c();
+    pdl_trigger_c();
+    if (threadIdx.x == 0) s_skip = *reinterpret_cast<volatile unsigned int*>(p.err) != 0u;
+    __syncthreads();
+    const unsigned int call = *reinterpret_cast<volatile const unsigned int*>(p.calls) + 1u;
+    const unsigned long long* slot =
+        reinterpret_cast<const unsigned long long*>(p.base[p.rank] + ll_slot_off(p.world, (int)(call & 1u), 0));
+    constexpr int kPer = 4;
+    for (int i0 = blockIdx.x * blockDim.x * kPer + threadIdx.x; i0 < n; i0 += gridDim.x * blockDim.x * kPer) {
+        unsigned long long w[kPer];
+#pragma unroll
+        for (int k = 0; k < kPer; ++k) {
+            const int i = i0 + k * blockDim.x;
+            if (i < n) w[k] = ld_relaxed_sys_u64c(slot + i);
+        }
+#pragma unroll
+        for (int k = 0; k < kPer; ++k) {
+            const int i = i0 + k * blockDim.x;
+            if (i < n) {
+                if ((unsigned int)(w[k] >> 32) != call) w[k] = ll_wait_word(slot + i, call, p.err, p.timeout_ns, &s_skip);
+                y[i] = __uint_as_float((unsigned int)w[k]);
+            }
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && atomicAdd(p.counter, 1u) == gridDim.x - 1) {
+        *p.counter = 0u;
+        *p.calls = call;
+    }
+}
+
 template <typename... KArgs, typename... Args>
 int launch_comm(void (*kern)(KArgs...), int grid, int threads, cudaStream_t st, Args... args) {
     cudaLaunchConfig_t cfg = {};
@@ -382,6 +420,13 @@ int comm_ll_reduce(neon_comm_impl* c, float* h, long long n, cudaStream_t st) {
     if (n <= 0 || n > kCommFusedFloats) return error(NEON_ERR_INVALID, "fused all-reduce: bad length");
     const int grid = (int)std::min<long long>((n + 255) / 256, 148);
     return launch_comm(comm_ll_reduce_kernel, grid, 256, st, comm_peer_set(c), h, (int)n);
+}
+
+int comm_ll_gather(neon_comm_impl* c, float* y, long long n, cudaStream_t st) {
+    if (!c || !c->connected) return error(NEON_ERR_INVALID, "communicator not connected");
+    if (n <= 0 || n > kCommFusedFloats) return error(NEON_ERR_INVALID, "fused all-gather: bad length");
+    const int grid = (int)std::min<long long>((n + 1023) / 1024, 148);
+    return launch_comm(comm_ll_gather_kernel, grid, 256, st, comm_peer_set(c), y, (int)n);
 }
 
 int comm_argmax(neon_comm_impl* c, unsigned long long* key, int* d_tok, int* out, int* d_step, int* d_pos, int advance,
@@ -507,6 +552,25 @@ int neon_cuda_set_fused_collectives(int enabled) {
 int neon_cuda_comm_allreduce(neon_comm_t c, const float* dIn, float* dOut, size_t n, int add, void* stream) {
     if (!c || !dIn || !dOut) return error(NEON_ERR_INVALID, "null argument");
     return neon_internal::comm_allreduce(c, dIn, dOut, (long long)n, add, (cudaStream_t)stream);
+}
+
+int neon_cuda_matvec_allgather(neon_comm_t c, neon_tensor_t W, const float* dX, float* dY, size_t n_total,
+                               size_t row0, void* stream) {
+    if (!c || !W || !dX || !dY) return error(NEON_ERR_INVALID, "null argument");
+    if (!c->connected) return error(NEON_ERR_INVALID, "communicator not connected");
+    if (W->device != c->device) return error(NEON_ERR_INVALID, "the shard and the communicator live on different devices");
+    if (n_total == 0 || n_total > (size_t)kCommFusedFloats || row0 + W->rows > n_total)
+        return error(NEON_ERR_INVALID, "all-gather matvec: rows [row0, row0 + shard rows) must lie in [0, n_total), "
+                                       "n_total <= " + std::to_string(kCommFusedFloats));
+    const neon_proj_target_t t{W, dY, W->rows};
+    neon_internal::MatvecExt ext;
+    ext.peer_mode = 2;
+    ext.gather_row0 = (long long)row0;
+    ext.peer = neon_internal::comm_peer_set(c);
+    const cudaStream_t st = (cudaStream_t)stream;
+    int rc = neon_internal::matvec(&t, 1, dX, W->cols, 1, st, 0, &ext);
+    if (!rc) rc = neon_internal::comm_ll_gather(c, dY, (long long)n_total, st);
+    return rc;
 }
 
 int neon_cuda_comm_check(neon_comm_t c) {

@@ -322,6 +322,10 @@ int launch_resident(const std::vector<const neon_proj_target_t*>& t, int type, i
             s.pos_stride = ext->pos_stride ? ext->pos_stride[j] : 0;
         }
         if (ext && ext->peer_mode == 1) s.epi = kEpiPeer;
+        if (ext && ext->peer_mode == 2) {
+            s.epi = kEpiGather;
+            s.pos_stride = ext->gather_row0;
+        }
     }
     a.x = dX;
     a.err = ds.err;
@@ -380,6 +384,10 @@ int launch_stream(const std::vector<const neon_proj_target_t*>& t, int type, int
                 s.pos_stride = ext->pos_stride ? ext->pos_stride[k] : 0;
             }
             if (ext && ext->peer_mode == 1) s.epi = kEpiPeer;
+        if (ext && ext->peer_mode == 2) {
+            s.epi = kEpiGather;
+            s.pos_stride = ext->gather_row0;
+        }
         }
         a.x = dX;
         a.err = ds.err;
@@ -523,6 +531,10 @@ int launch_dq_ring(const std::vector<const neon_proj_target_t*>& t, int type, si
                 sp.pos_stride = ext->pos_stride ? ext->pos_stride[k] : 0;
             }
             if (ext && ext->peer_mode == 1) sp.epi = kEpiPeer;
+            if (ext && ext->peer_mode == 2) {
+                sp.epi = kEpiGather;
+                sp.pos_stride = ext->gather_row0;
+            }
         }
         a.s.x = dX;
         a.s.err = ds.err;
@@ -635,6 +647,10 @@ int launch_dq(const std::vector<const neon_proj_target_t*>& t, int type, size_t 
                 sp.pos_stride = ext->pos_stride ? ext->pos_stride[k] : 0;
             }
             if (ext && ext->peer_mode == 1) sp.epi = kEpiPeer;
+            if (ext && ext->peer_mode == 2) {
+                sp.epi = kEpiGather;
+                sp.pos_stride = ext->gather_row0;
+            }
         }
         a.s.x = dX;
         a.s.err = ds.err;
@@ -875,10 +891,10 @@ int matvec_targets(const neon_proj_target_t* targets, size_t n_targets, const fl
     if (ext && ext->rope_cs && (ext->rope_half < 0 || ext->rope_half > kMaxRopeHalf))
         return set_err(NEON_ERR_UNSUPPORTED, "RoPE epilogue: rope dimension above 256");
     if (ext && ext->peer_mode) {
-        if (seq != 1 || ext->peer_mode != 1 || n_targets != 1 || ext->peer.world < 1 ||
-            ext->peer.world > kCommMaxRanks)
+        if (seq != 1 || (ext->peer_mode != 1 && ext->peer_mode != 2) || n_targets != 1 || ext->peer.world < 1 ||
+            ext->peer.world > kCommMaxRanks || ext->gather_row0 < 0)
             return set_err(NEON_ERR_INVALID, "fused collective: bad launch options");
-        if (targets[0].W->rows > (size_t)kCommFusedFloats)
+        if ((size_t)ext->gather_row0 + targets[0].W->rows > (size_t)kCommFusedFloats)
             return set_err(NEON_ERR_UNSUPPORTED, "fused collective: vector longer than its slot");
     }
     for (const Group& g : groups) {

@@ -118,6 +118,9 @@ PeerSet comm_peer_set(neon_comm_impl* c);
 // Completes a fused all-reduce a producing matvec started: h[i] += slot_0[i]
 // + slot_1[i] + ... for i < n, waiting (bounded) for every rank's words.
 int comm_ll_reduce(neon_comm_impl* c, float* h, long long n, cudaStream_t st);
+// Completes a fused all-gather the producing row-shard matvecs started:
+// y[i] = the gather slot's word i for i < n, waiting (bounded) for each.
+int comm_ll_gather(neon_comm_impl* c, float* y, long long n, cudaStream_t st);
 bool fused_collectives();
 // neon_cuda_set_prefill_mma: prompt passes on the tensor-core kernels.
 bool prefill_mma();
@@ -135,9 +138,12 @@ struct MatvecExt {
     int head_dim = 0;
     const int* epi = nullptr;               // per target; null: plain store
     const long long* pos_stride = nullptr;  // per target
-    // 1: produce a fused collective (one target, one position): the rows go
-    // as LL words to every rank's slot instead of to Y
+    // produce a fused collective (one target, one position) instead of
+    // storing Y: 1 (all-reduce) the rows go as LL words to this rank's slot on
+    // every rank; 2 (all-gather) each row r goes as an LL word to position
+    // gather_row0 + r of the gather slot on every rank
     int peer_mode = 0;
+    long long gather_row0 = 0;
     PeerSet peer{};
 };
 

@@ -46,6 +46,8 @@ enum : int {
     kEpiSwiglu = 3,  // rows interleave gate/up: y[i] = silu(v_2i) * v_2i+1
     kEpiPeer = 4,    // fused collective: row r into slot [parity][rank] of every rank
     kEpiSilu = 5,    // y[r] = silu(v): the plain SiLU-FFN variant's activation
+    kEpiGather = 6,  // fused all-gather: row r (of a row shard starting at row pos_stride of the
+                     // whole output) into the gather slot [parity] of every rank, at pos_stride + r
 };
 
 struct Span {
@@ -364,7 +366,7 @@ struct StreamArgs {
     const float2* rope_cs;  // [position][rope_half] (cos, sin)
     int rope_half;
     int head_dim;
-    int peer_mode;          // 1: fused collective producer (neon_internal::MatvecExt)
+    int peer_mode;          // 1: fused all-reduce producer, 2: fused all-gather producer (neon_internal::MatvecExt)
     PeerSet peer;
     // matvec_resident_kernel only: rows per CTA (even) and the rows of all
     // spans (each span starting at an even row, span[i].tile0)
@@ -732,6 +734,14 @@ __device__ __forceinline__ void stream_epilogue(const StreamArgs& a, const Span&
         case kEpiPeer: {
             // this rank's partial row sum, as an LL word, into its slot on every rank (NVLink stores)
             const long long off = ll_slot_off(a.peer.world, (int)(peer_call & 1u), a.peer.rank) / 8 + row;
+            const unsigned long long w = ll_pack(v, peer_call);
+            for (int p = 0; p < a.peer.world; ++p)
+                st_relaxed_sys_u64(reinterpret_cast<unsigned long long*>(a.peer.base[p]) + off, w);
+            break;
+        }
+        case kEpiGather: {
+            // this rank's row, as an LL word, at its place in the whole output, into every rank's gather slot
+            const long long off = ll_slot_off(a.peer.world, (int)(peer_call & 1u), 0) / 8 + sp.pos_stride + row;
             const unsigned long long w = ll_pack(v, peer_call);
             for (int p = 0; p < a.peer.world; ++p)
                 st_relaxed_sys_u64(reinterpret_cast<unsigned long long*>(a.peer.base[p]) + off, w);

@@ -90,6 +90,7 @@ C_ENTRY_POINTS = (
     "neon_cuda_comm_connect_local",
     "neon_cuda_comm_set_timeout",
     "neon_cuda_comm_allreduce",
+    "neon_cuda_matvec_allgather",
     "neon_cuda_comm_check",
     "neon_cuda_comm_free",
     "neon_cuda_model_comm_floats",
@@ -184,6 +185,7 @@ def load(path: str | None = None) -> C.CDLL:
         L.neon_cuda_comm_connect_local.argtypes = [C.POINTER(_vp), C.c_int]
         L.neon_cuda_comm_set_timeout.argtypes = [_vp, C.c_double]
         L.neon_cuda_comm_allreduce.argtypes = [_vp, _vp, _vp, _sz, C.c_int, _vp]
+        L.neon_cuda_matvec_allgather.argtypes = [_vp, _vp, _vp, _vp, _sz, _sz, _vp]
         L.neon_cuda_comm_check.argtypes = [_vp]
         L.neon_cuda_comm_free.argtypes = [_vp]
         L.neon_cuda_model_comm_floats.argtypes = [C.POINTER(_ModelConfig), C.c_int, C.POINTER(_sz)]
@@ -531,6 +533,13 @@ class Comm:
             n = x.numel()
         _check(load().neon_cuda_comm_allreduce(self.handle, _ptr(x), _ptr(out), int(n), 1 if add else 0,
                                                _stream(stream)))
+
+    def matvec_allgather(self, w: "DeviceTensor", x, y, n_total: int, row0: int, stream=None) -> None:
+        """y[0 .. n_total) = the whole matvec on every rank, from this rank's row
+        shard w (rows row0 .. row0 + w.rows of the matrix) and x (device
+        buffers); the ranks' shards must tile [0, n_total)."""
+        _check(load().neon_cuda_matvec_allgather(self.handle, w.handle, _ptr(x), _ptr(y), int(n_total), int(row0),
+                                                 _stream(stream)))
 
     def check(self) -> None:
         _check(load().neon_cuda_comm_check(self.handle))

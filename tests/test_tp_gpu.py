@@ -1,6 +1,7 @@
 """Tensor-parallel decode on two GPUs (one process per GPU, launched with
 torch.distributed.run): the peer-memory all-reduce bit-exact against host
-sums, and the split decoder against the reference's greedy tokens -- the small
+sums, the row-sharded matvec with its output all-gathered against the oracle
+on every rank, and the split decoder against the reference's greedy tokens -- the small
 model's golden generation and, for the Qwen3-0.6B-shaped decoder, the same
 tokens as one GPU and as the reference's own transformer_forward. Skipped on
 a host with fewer than two GPUs."""
@@ -9,7 +10,7 @@ import pytest
 
 import oracle as O
 import synth as S
-from conftest import MODEL_L2_RTOL, load_golden, rel_l2
+from conftest import MATVEC_RTOL, MODEL_L2_RTOL, load_golden, max_rel_err, rel_l2
 from tp_launch import run_tp_worker
 
 pytestmark = pytest.mark.gpu
@@ -30,6 +31,22 @@ def test_allreduce_bit_exact(tp2):
     for k, v in tp2.items():
         if k.startswith("allreduce_"):
             assert float(v) == 0.0, k
+
+
+def test_allgather_matvec_matches_oracle_on_every_rank(tp2):
+    """neon_cuda_matvec_allgather: each rank's row shard, gathered, equals the
+    whole matvec (oracle, per-row bar) on every rank and every call, and all
+    ranks hold the same bits."""
+    from tp_gpu_worker import ALLGATHER_CASES
+
+    for name, typ, rows, cols in ALLGATHER_CASES:
+        got = tp2[f"allgather_{name}"]  # [rank][call][rows]
+        W = S.weights(typ, rows, cols, seed=rows + cols)
+        ref = O.proj_all_positions(typ, W, rows, cols, S.activations(1, cols, seed=cols))[0]
+        for r in range(got.shape[0]):
+            for call in range(got.shape[1]):
+                assert max_rel_err(got[r, call], ref) <= MATVEC_RTOL, f"{name} rank {r} call {call}"
+                assert np.array_equal(got[r, call].view(np.uint32), got[0, 0].view(np.uint32)), f"{name} {r} {call}"
 
 
 def test_tiny_golden_tokens_and_logits(tp2):

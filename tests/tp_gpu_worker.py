@@ -3,7 +3,8 @@ torch.distributed.run, one process per GPU; gloo carries only the IPC handles
 and the host-side checks).
 
 Writes rank 0's observations to --out (npz): the all-reduce results against
-their exact host sums, the small model's greedy tokens and per-step logits,
+their exact host sums, every rank's output of the all-gathered row-sharded
+matvecs, the small model's greedy tokens and per-step logits,
 and the Qwen3-0.6B-shaped decoder's tokens split over the ranks and on one GPU.
 """
 from __future__ import annotations
@@ -53,6 +54,37 @@ def allreduce_cases(comm, rank, world, dev):
     return out
 
 
+ALLGATHER_CASES = (("q4_0_4096", S.GGML_Q4_0, 4096, 4096), ("q8_0_ragged", S.GGML_Q8_0, 1001, 1024),
+                   ("q4_k", S.GGML_Q4_K, 512, 2048), ("tiny", S.GGML_Q4_0, 3, 64))
+
+
+def allgather_cases(comm, rank, world, dev, res):
+    """Row-sharded matvecs with the output all-gathered: every rank's y for
+    three calls in a row (the first two on the same X, the third after an
+    all-reduce on the same communicator); rank 0 keeps its own and rank 1's."""
+    for name, typ, rows, cols in ALLGATHER_CASES:
+        W = S.weights(typ, rows, cols, seed=rows + cols)
+        dt = NC.DeviceTensor(W, typ, rows, cols, NC.SHARD_ROWS, rank, world)
+        row0 = rows * rank // world
+        X = S.activations(1, cols, seed=cols)
+        x = torch.from_numpy(X[0]).to(dev)
+        ys = []
+        for call in range(3):
+            if call == 2:
+                t = torch.ones(8, device=dev)
+                comm.allreduce(t, t, stream=torch.cuda.current_stream(dev))
+            y = torch.full((rows,), float("nan"), device=dev)
+            dist.barrier()
+            comm.matvec_allgather(dt, x, y, rows, row0, stream=torch.cuda.current_stream(dev))
+            torch.cuda.synchronize(dev)
+            ys.append(y.cpu().numpy())
+        comm.check()
+        parts = [None] * world
+        dist.all_gather_object(parts, np.stack(ys))
+        res[f"allgather_{name}"] = np.stack(parts)  # [rank][call][rows]
+        dt.free()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--out", required=True)
@@ -73,6 +105,7 @@ def main():
     try:
         for name, err in allreduce_cases(comm, rank, world, dev):
             res[f"allreduce_{name}"] = np.array(err)
+        allgather_cases(comm, rank, world, dev, res)
 
         # small model: greedy tokens, then logits step by step
         from conftest import load_golden  # noqa: E402
