@@ -34,6 +34,8 @@ enum : int { kEpiStore = 0, kEpiRope = 1, kEpiAtPos = 2, kEpiSwiglu = 3, kEpiSil
 }  // namespace neon
 
 #include <cooperative_groups.h>
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -478,115 +480,129 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const float* __rest
 // ---------------------------------------------------------------------------
 // Decode attention in one launch: a thread-block cluster of cs CTAs (8, or 16
 // for long contexts) per KV head. CTA r of the cluster takes positions
-// [r*chunk, (r+1)*chunk) of the L = *d_pos + 1 cache rows, in tiles of
-// kAttnSub rows. Its V tiles go into a ring of shared-memory slots with
-// 16-byte cp.async copies from all threads (rows padded by 64 bytes, so the
-// threads of the V pass read conflict-free), the first ring's worth issued
-// before the K pass starts; K rows are read straight into registers (four
-// threads per row, two tiles' loads in flight). One copy instruction per
-// 16 bytes from every thread keeps far more bytes in flight than one bulk
-// copy per 512-byte row from one warp. Scores for the head's query group go
-// to shared memory; the CTAs exchange their maxima through distributed shared
-// memory, so every CTA forms p_s = fast_expf(score_s - max over ALL
-// positions) exactly as transformer_forward does (:1123-1137); each CTA sums p
-// and p * v over its positions, and CTA 0 adds the partials in rank order:
-// out = (sum p v) / (sum p).
+// [r*chunk, (r+1)*chunk) of the L = *d_pos + 1 cache rows. Its K rows, then its
+// V rows, stream through a ring of shared-memory slots of kAttnSub rows: one
+// thread fills a slot with TMA tensor copies of 16-row boxes (the layer's K or
+// V cache as a 2D tensor, rows x kv_dim, one CUtensorMap each, built when the
+// model is created), as many slots as the CTA's tiles need while every
+// cluster of the launch stays resident (attn_pick_slots), so at the
+// configurations' contexts all of a CTA's rows are requested at once by a
+// handful of copy instructions; a slot is refilled as soon as its rows are
+// used. Scores for the head's query group go to shared memory; the CTAs
+// exchange their maxima through distributed shared memory, so every CTA forms
+// p_s = fast_expf(score_s - max over ALL positions) exactly as
+// transformer_forward does (:1123-1137); each CTA sums p and p * v over its
+// positions, and CTA 0 adds the partials in rank order: out = (sum p v) /
+// (sum p).
 // ---------------------------------------------------------------------------
 
-__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
-                     static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst))),
-                 "l"(gsrc)
-                 : "memory");
+__device__ __forceinline__ uint32_t smem_addr_d(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-// Wait until at most n (0..kAttnMaxSlots-1) of this thread's copy groups are pending.
-__device__ __forceinline__ void cp_async_wait_pending(int n) {
-    switch (n) {
-        case 0: asm volatile("cp.async.wait_group 0;" ::: "memory"); break;
-        case 1: asm volatile("cp.async.wait_group 1;" ::: "memory"); break;
-        case 2: asm volatile("cp.async.wait_group 2;" ::: "memory"); break;
-        case 3: asm volatile("cp.async.wait_group 3;" ::: "memory"); break;
-        case 4: asm volatile("cp.async.wait_group 4;" ::: "memory"); break;
-        case 5: asm volatile("cp.async.wait_group 5;" ::: "memory"); break;
-        case 6: asm volatile("cp.async.wait_group 6;" ::: "memory"); break;
-        default: asm volatile("cp.async.wait_group 7;" ::: "memory"); break;
+__device__ __forceinline__ bool mbar_wait_d(uint64_t* bar, uint32_t parity, unsigned int* err) {
+    uint32_t done = 0;
+    unsigned long long t0 = 0;
+    for (int it = 0;; ++it) {
+        asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+                     : "=r"(done)
+                     : "r"(smem_addr_d(bar)), "r"(parity)
+                     : "memory");
+        if (done) return true;
+        unsigned long long t;
+        asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+        if (it == 0) t0 = t;
+        else if (t - t0 > 2000000000ull) {
+            atomicOr(err, 4u);
+            return false;
+        }
     }
 }
 
 static_assert(kThreads == kAttnThreads, "the attention layout assumes kThreads threads");
-static_assert(kAttnMaxSlots <= 8, "cp_async_wait_pending covers 8 pending groups");
 
-// C4: float4 columns of a K row per scoring thread (head_dim / 16, rounded up
-// to 2, 4, 8 or 16).
-template <int C4>
-__global__ void __launch_bounds__(kThreads) attn_decode_kernel(const float* __restrict__ q, const float* __restrict__ Kc,
-                                                               const float* __restrict__ Vc, const int* __restrict__ d_pos,
-                                                               int kv_dim, int hd, int group, float scale, int chunk_max,
-                                                               int slots, float* __restrict__ out, unsigned int* err) {
+// A 16-row box of a head's K or V rows: 2D tensor copy (columns x .. x + hd,
+// rows y .. y + kAttnBox of the layer's cache) into shared memory, completion
+// counted in bytes on `bar`. Rows past the cache's end arrive as zeros.
+__device__ __forceinline__ void tma_box(float* dst, const CUtensorMap* tm, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_addr_d(dst)),
+        "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(smem_addr_d(bar))
+        : "memory");
+}
+
+__global__ void __launch_bounds__(kThreads) attn_decode_kernel(const float* __restrict__ q,
+                                                               const __grid_constant__ CUtensorMap tmk,
+                                                               const __grid_constant__ CUtensorMap tmv,
+                                                               const int* __restrict__ d_pos, int hd, int group,
+                                                               float scale, int chunk_max, int slots,
+                                                               float* __restrict__ out, unsigned int* err) {
     namespace cg = cooperative_groups;
-    extern __shared__ __align__(16) float sm[];
+    extern __shared__ __align__(1024) float sm[];
     cg::cluster_group cl = cg::this_cluster();
     const int rank = (int)cl.block_rank(), cs = (int)cl.num_blocks();
     const int kvh = blockIdx.x / cs;
     const AttnSmem lay = attn_smem_layout(group, hd, chunk_max, cs, slots);
     float* qs = sm + lay.q;
     float* sc = sm + lay.sc;     // [group][chunk_max]
-    float* ring = sm + lay.ring; // [slots][kAttnSub][hd + 16]: V tiles; later [parts][group][hd]
+    float* ring = sm + lay.ring; // [slots][kAttnSub][hd] (128-byte aligned); later [parts][group][hd]
     float* co = sm + lay.co;     // [cluster][group][hd]   (CTA 0; overlays the ring)
     float* csum = sm + lay.csum; // [cluster][kAttnMaxGroup] (read in CTA 0)
     float* cmax = sm + lay.cmax; // [cluster][kAttnMaxGroup]
+    uint64_t* full = reinterpret_cast<uint64_t*>(sm + lay.bar);
     __shared__ float gm[kAttnMaxGroup];
-    (void)err;
-    const int pitch = hd + 16;
+    const int pitch = hd;
     const int S = slots;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < S; ++i)
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr_d(&full[i])) : "memory");
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
     pdl_wait_d();
     pdl_trigger_d();
+    __syncthreads();
     const int L = *d_pos + 1;
     const int chunk = (L + cs - 1) / cs;
     const int s0 = min(L, rank * chunk), len = min(L, s0 + chunk) - s0;
     const int n_sub = (len + kAttnSub - 1) / kAttnSub;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nd4 = hd / 4;
-    // V tile t into ring slot t % S: rows j0 .. j0 + rows, hd floats each, as
-    // 16-byte copies spread over all threads; one commit group per tile
-    auto issue_v = [&](int t) {
-        const int j0 = t * kAttnSub, rows = min(kAttnSub, len - j0);
-        const float* base = Vc + (long long)kvh * hd;
-        float* dst = ring + (t % S) * kAttnSub * pitch;
-        for (int i = threadIdx.x; i < rows * nd4; i += kThreads) {
-            const int r = i / nd4, c = i - r * nd4;
-            cp_async16(dst + r * pitch + 4 * c, base + (long long)(s0 + j0 + r) * kv_dim + 4 * c);
-        }
-        cp_async_commit();
+    // item t < n_sub: K rows of sub-chunk t; n_sub <= t < 2 n_sub: V rows of sub-chunk t - n_sub
+    auto issue = [&](int t) {
+        const int slot = t % S;
+        const bool is_v = t >= n_sub;
+        const int sub = is_v ? t - n_sub : t;
+        const int j0 = sub * kAttnSub, rows = min(kAttnSub, len - j0);
+        const int boxes = (rows + kAttnBox - 1) / kAttnBox;
+        float* dst = ring + slot * kAttnSub * pitch;
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr_d(&full[slot])),
+                     "r"((uint32_t)(boxes * kAttnBox * hd * 4))
+                     : "memory");
+        for (int bx = 0; bx < boxes; ++bx)
+            tma_box(dst + bx * kAttnBox * pitch, is_v ? &tmv : &tmk, kvh * hd, s0 + j0 + bx * kAttnBox, &full[slot]);
     };
-    // pass 1: scores, four threads per cache row (lanes 4r'..4r'+3 of a warp);
-    // thread q4i takes float4 columns q4i, q4i + 4, .. of the row, read from
-    // global memory into registers; the four partial dots meet by two
-    // shuffles. The first two K tiles are requested before anything else, then
-    // the V tiles of the ring, then the query rows: the K loads do not queue
-    // behind the other traffic.
-    const int r = threadIdx.x >> 2, q4i = threadIdx.x & 3;
-    auto load_k = [&](int t, float4 (&k)[C4]) {
-        const int row = t * kAttnSub + r;
-        const float4* kr = reinterpret_cast<const float4*>(Kc + (long long)(s0 + row) * kv_dim + (long long)kvh * hd);
-#pragma unroll
-        for (int u = 0; u < C4; ++u) {
-            const int c = q4i + 4 * u;
-            k[u] = (t < n_sub && row < len && c < nd4) ? __ldg(kr + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-    };
-    auto score = [&](int t, const float4 (&k)[C4]) {
+    const int n_items = 2 * n_sub;
+    if (threadIdx.x == 0)
+        for (int t = 0; t < min(S, n_items); ++t) issue(t);
+    for (int i = threadIdx.x; i < group * hd; i += blockDim.x) qs[i] = q[(long long)kvh * group * hd + i];
+    __syncthreads();
+    bool ok = true;
+    // pass 1: scores, a thread per cache row of the slot
+    for (int t = 0; t < n_sub; ++t) {
+        ok = ok && mbar_wait_d(&full[t % S], (uint32_t)((t / S) & 1), err);
+        const float* rows_k = ring + (t % S) * kAttnSub * pitch;
         const int j0 = t * kAttnSub, rows = min(kAttnSub, len - j0);
-        float acc[kAttnMaxGroup];
+        {
+            // four threads per row (lanes 4r'..4r'+3 of a warp), thread q4i takes float4
+            // columns q4i, q4i+4, ..; the four partial dots meet by two shuffles
+            const int r = threadIdx.x >> 2, q4i = threadIdx.x & 3;
+            const float4* kr = reinterpret_cast<const float4*>(rows_k + r * pitch);
+            float acc[kAttnMaxGroup];
 #pragma unroll
-        for (int gq = 0; gq < kAttnMaxGroup; ++gq) acc[gq] = 0.f;
-        if (r < rows) {
-#pragma unroll
-            for (int u = 0; u < C4; ++u) {
-                const int c = q4i + 4 * u;
-                if (c < nd4) {
-                    const float4 k4 = k[u];
+            for (int gq = 0; gq < kAttnMaxGroup; ++gq) acc[gq] = 0.f;
+            if (r < rows) {
+                for (int c = q4i; c < nd4; c += 4) {
+                    const float4 k4 = kr[c];
 #pragma unroll
                     for (int gq = 0; gq < kAttnMaxGroup; ++gq) {
                         if (gq < group) {
@@ -599,34 +615,23 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const float* __re
                     }
                 }
             }
-        }
 #pragma unroll
-        for (int gq = 0; gq < kAttnMaxGroup; ++gq) {
-            acc[gq] += __shfl_xor_sync(0xffffffffu, acc[gq], 1);
-            acc[gq] += __shfl_xor_sync(0xffffffffu, acc[gq], 2);
-        }
-        if (r < rows && q4i == 0) {
+            for (int gq = 0; gq < kAttnMaxGroup; ++gq) {
+                acc[gq] += __shfl_xor_sync(0xffffffffu, acc[gq], 1);
+                acc[gq] += __shfl_xor_sync(0xffffffffu, acc[gq], 2);
+            }
+            if (r < rows && q4i == 0) {
 #pragma unroll
-            for (int gq = 0; gq < kAttnMaxGroup; ++gq)
-                if (gq < group) sc[gq * chunk_max + j0 + r] = __fmul_rn(acc[gq], scale);
+                for (int gq = 0; gq < kAttnMaxGroup; ++gq)
+                    if (gq < group) sc[gq * chunk_max + j0 + r] = __fmul_rn(acc[gq], scale);
+            }
         }
-    };
-    float4 ka[C4], kb[C4];
-    load_k(0, ka);
-    load_k(1, kb);
-    const int pre = min(S, n_sub);
-    for (int t = 0; t < pre; ++t) issue_v(t);
-    for (int i = threadIdx.x; i < group * hd; i += blockDim.x) qs[i] = q[(long long)kvh * group * hd + i];
-    __syncthreads();
-    for (int t = 0; t < n_sub; t += 2) {
-        if (t > 0) {
-            load_k(t, ka);
-            load_k(t + 1, kb);
+        __syncthreads();  // the slot is free
+        if (threadIdx.x == 0 && t + S < n_items) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            issue(t + S);
         }
-        score(t, ka);
-        if (t + 1 < n_sub) score(t + 1, kb);
     }
-    __syncthreads();
     // this CTA's max per query head (warp gq), published to every CTA of the cluster
     if (warp < group) {
         float m = -INFINITY;
@@ -659,12 +664,10 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const float* __re
     float4 acc[kAttnMaxGroup];
 #pragma unroll
     for (int gq = 0; gq < kAttnMaxGroup; ++gq) acc[gq] = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int t = 0; t < n_sub; ++t) {
-        // groups issued so far: tiles 0 .. min(n_sub, S + t) - 1; tile t must be complete
-        cp_async_wait_pending(min(n_sub, S + t) - t - 1);
-        __syncthreads();
+    for (int t = n_sub; t < n_items; ++t) {
+        ok = ok && mbar_wait_d(&full[t % S], (uint32_t)((t / S) & 1), err);
         const float* rows_v = ring + (t % S) * kAttnSub * pitch;
-        const int j0 = t * kAttnSub, rows = min(kAttnSub, len - j0);
+        const int j0 = (t - n_sub) * kAttnSub, rows = min(kAttnSub, len - j0);
         if (part < parts) {
             for (int r = part; r < rows; r += parts) {
                 const float4 v4 = reinterpret_cast<const float4*>(rows_v + r * pitch)[c4];
@@ -680,9 +683,13 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const float* __re
                 }
             }
         }
-        __syncthreads();  // the slot is free
-        if (t + S < n_sub) issue_v(t + S);
+        __syncthreads();
+        if (threadIdx.x == 0 && t + S < n_items) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            issue(t + S);
+        }
     }
+    (void)ok;  // a timed-out copy sets bit 2 of the error word; the results are then not used
     // per-part partials -> the ring (its copies are all consumed), then the CTA's partial to CTA 0
     float* red = ring;
     if (part < parts) {
@@ -879,6 +886,7 @@ struct neon_model {
     float forward_ms = 0.f;
     float decode_ms = 0.f;
     std::vector<void*> allocs;
+    std::vector<CUtensorMap> tm_k, tm_v;  // per layer: the K and V caches as 2D tensors (attn_decode_kernel)
 };
 
 namespace {
@@ -976,19 +984,52 @@ int launch_embed(neon_model* m, const int* toks, int seq) {
                     nb, toks, (int)c.n_vocab, m->h, m->d_err);
 }
 
-// The attn_decode_kernel instantiation for a head dim: float4 columns per
-// scoring thread, head_dim / 16 rounded up to 2, 4, 8 or 16.
-using AttnKernel = void (*)(const float*, const float*, const float*, const int*, int, int, int, float, int, int,
-                            float*, unsigned int*);
-AttnKernel attn_kernel_for(int hd) {
-    const int c4 = (hd / 4 + 3) / 4;
-    if (c4 <= 2) return attn_decode_kernel<2>;
-    if (c4 <= 4) return attn_decode_kernel<4>;
-    if (c4 <= 8) return attn_decode_kernel<8>;
-    return attn_decode_kernel<16>;
-}
+// The decode attention kernel (one for every head dim).
+using AttnKernel = void (*)(const float*, CUtensorMap, CUtensorMap, const int*, int, int, float, int, int, float*,
+                            unsigned int*);
+AttnKernel attn_kernel_for(int) { return attn_decode_kernel; }
 
 // Dynamic shared memory of attn_decode_kernel.
+// The layers' K and V caches as 2D tensors for the decode attention's TMA
+// copies: ctx_len rows of kv_dim floats each, boxes of kAttnBox rows x
+// head_dim columns (a box's first column, kvh * head_dim, is 16-byte aligned:
+// head_dim is a multiple of 4). cuTensorMapEncodeTiled comes from the driver
+// through the runtime's entry-point query, so the library does not link
+// libcuda.
+int build_kv_maps(neon_model* m) {
+    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+    if (!encode) {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess || !fn)
+            return error(NEON_ERR_CUDA, "decode attention: cuTensorMapEncodeTiled is not available");
+        encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+    const auto& c = m->cfg;
+    if (c.head_dim == 0 || c.head_dim > 256 || c.head_dim % 4)
+        return error(NEON_ERR_UNSUPPORTED, "decode attention: head_dim must be a multiple of 4, at most 256");
+    m->tm_k.assign(c.n_layer, CUtensorMap{});
+    m->tm_v.assign(c.n_layer, CUtensorMap{});
+    for (uint32_t li = 0; li < c.n_layer; ++li) {
+        for (int which = 0; which < 2; ++which) {
+            float* base = (which ? m->V : m->K) + (size_t)li * c.ctx_len * m->kv_dim;
+            const cuuint64_t dims[2] = {(cuuint64_t)m->kv_dim, (cuuint64_t)c.ctx_len};
+            const cuuint64_t strides[1] = {(cuuint64_t)m->kv_dim * sizeof(float)};
+            const cuuint32_t box[2] = {(cuuint32_t)c.head_dim, (cuuint32_t)kAttnBox};
+            const cuuint32_t estr[2] = {1, 1};
+            const CUresult r = encode(which ? &m->tm_v[li] : &m->tm_k[li], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base,
+                                      dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                      CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+            if (r != CUDA_SUCCESS)
+                return error(NEON_ERR_CUDA, "decode attention: cuTensorMapEncodeTiled failed (" +
+                                                std::to_string((int)r) + ")");
+        }
+    }
+    return NEON_OK;
+}
+
 int attn_chunk_max(const neon_model* m) { return (int)((m->cfg.ctx_len + m->att_cs - 1) / m->att_cs); }
 size_t attn_decode_smem(const neon_model* m, int slots) {
     const int group = (int)(m->cfg.n_head / m->cfg.n_kv_head);
@@ -997,12 +1038,12 @@ size_t attn_decode_smem(const neon_model* m, int slots) {
 }
 size_t attn_decode_smem(const neon_model* m) { return attn_decode_smem(m, m->att_slots); }
 
-// The ring depth of attn_decode_kernel: a slot per V tile of the longest
-// share (at most kAttnMaxSlots), cut while it would take more than
+// The ring depth of attn_decode_kernel: a slot per K and V tile of the
+// longest share (at most kAttnMaxSlots), cut while it would take more than
 // kAttnSmemMax or leave a cluster of the launch waiting for another to finish;
 // never below two (the next tile in flight while one is used).
 int attn_pick_slots(const neon_model* m) {
-    const int items = (attn_chunk_max(m) + kAttnSub - 1) / kAttnSub;
+    const int items = 2 * ((attn_chunk_max(m) + kAttnSub - 1) / kAttnSub);
     for (int slots = std::min(kAttnMaxSlots, items); slots > 2; --slots) {
         const size_t smem = attn_decode_smem(m, slots);
         if (smem > (size_t)kAttnSmemMax) continue;
@@ -1028,7 +1069,7 @@ int attn_pick_slots(const neon_model* m) {
 }
 
 // attn_decode_kernel: one cluster of att_cs CTAs per KV head, PDL when enabled.
-int launch_attn_decode(neon_model* m, const float* Kl, const float* Vl) {
+int launch_attn_decode(neon_model* m, uint32_t li) {
     const auto& c = m->cfg;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(m->n_kv_l * m->att_cs));
@@ -1050,8 +1091,8 @@ int launch_attn_decode(neon_model* m, const float* Kl, const float* Vl) {
     cfg.attrs = attr;
     cfg.numAttrs = n;
     const float scale = 1.0f / std::sqrt((float)c.head_dim);
-    cudaError_t e = cudaLaunchKernelEx(&cfg, attn_kernel_for((int)c.head_dim), (const float*)m->q, Kl, Vl, (const int*)m->d_pos,
-                                       (int)m->kv_dim, (int)c.head_dim, (int)(c.n_head / c.n_kv_head), scale,
+    cudaError_t e = cudaLaunchKernelEx(&cfg, attn_decode_kernel, (const float*)m->q, m->tm_k[li], m->tm_v[li],
+                                       (const int*)m->d_pos, (int)c.head_dim, (int)(c.n_head / c.n_kv_head), scale,
                                        attn_chunk_max(m), m->att_slots, m->att, m->d_err);
     if (e != cudaSuccess) return cuda_error(e, "attn_decode_kernel");
     return neon_internal::launched(1);
@@ -1187,7 +1228,7 @@ int run_step(neon_model* m) {
             ext.pos_stride = stride;
             rc = neon_internal::matvec(t, 3, hc, n_embd, 1, m->stream, 0, &ext);
         }
-        if (!rc) rc = launch_attn_decode(m, Kl, Vl);
+        if (!rc) rc = launch_attn_decode(m, li);
         if (!rc) rc = residual(L.w[3], m->att, q_dim);
         if (!rc) {
             // act = silu(gate) * up, (gate, up) = W x with x = rms_norm(h); or silu(up)
@@ -1401,6 +1442,7 @@ int neon_cuda_model_create_tp(const neon_model_config_t* cfg, neon_comm_t comm, 
             cudaMemset(m->V, 0, kv_bytes) != cudaSuccess)
             rc = error(NEON_ERR_CUDA, "model initialisation copies failed");
     }
+    if (!rc) rc = build_kv_maps(m);
     if (!rc) {
         // long contexts: 16 CTAs per KV head when the device schedules clusters that large
         if (c.ctx_len > 1024 &&

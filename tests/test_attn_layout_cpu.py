@@ -1,11 +1,11 @@
 """The decode attention's shared-memory layout (csrc/neon_attn_layout.h, built
 for the host) at every ring depth the host may pick, with the kernel's copies
 and writes emulated: at the configurations' shapes (and a 16K context) the
-regions do not overlap, the ring holds its V tiles and, after the V pass, the
-per-part and per-cluster partials that overlay it; every 16-byte copy of a V
-row lands 16-byte aligned inside its slot and reads a cache row below the
-capacity, as does every float4 read of a K row; the total fits the launch's
-shared memory."""
+regions do not overlap, the ring holds its K and V tiles and, after the V
+pass, the per-part and per-cluster partials that overlay it; every TMA box
+lands 128-byte aligned inside its slot and starts at a cache row below the
+capacity and a 16-byte-aligned column; the mbarriers are 8-byte aligned; the
+total fits the launch's shared memory."""
 import ctypes as C
 import os
 import subprocess
@@ -14,7 +14,7 @@ import pytest
 
 from conftest import PKG, ROOT
 
-SUB, MAX_SLOTS, SMEM_MAX, THREADS = 64, 8, 200 * 1024, 256
+SUB, BOX, MAX_SLOTS, SMEM_MAX, THREADS = 64, 16, 8, 200 * 1024, 256
 
 
 @pytest.fixture(scope="module")
@@ -40,10 +40,9 @@ def test_layout_and_copies(lib, name, n_head, n_kv, hd, ctx):
     kv_dim = n_kv * hd
     cs = 16 if ctx > 1024 else 8
     chunk_max = -(-ctx // cs)
-    items = -(-chunk_max // SUB)  # V tiles of the longest share: the ring's items
-    pitch = hd + 16
-    nd4 = hd // 4
-    parts = THREADS // nd4
+    items = 2 * (-(-chunk_max // SUB))  # K then V tiles of the longest share: the ring's items
+    pitch = hd
+    parts = THREADS // (hd // 4)
     for slots in range(2, max(2, min(MAX_SLOTS, items)) + 1):
         out = (C.c_int * 8)()
         lib.attn_host_layout(group, hd, chunk_max, cs, slots, out)
@@ -54,26 +53,29 @@ def test_layout_and_copies(lib, name, n_head, n_kv, hd, ctx):
         assert q == 0 and sc >= q + group * hd and ring >= sc + group * chunk_max
         assert csum - ring >= max(slots * SUB * pitch, parts * group * hd, cs * group * hd) and co == ring
         assert cmax >= csum + cs * 8 and bar >= cmax + cs * 8 and total == bar + 2 * slots
-        assert all(v % 4 == 0 for v in (sc, ring, csum, cmax, bar)) and (bar * 4) % 8 == 0
-        # the kernel's accesses at the longest share: V tile t -> slot t % slots as 16-byte
-        # copies (row r, float4 column c at ring + slot*SUB*pitch + r*pitch + 4c); K rows read
-        # straight from the cache in float4 columns
+        assert all(v % 4 == 0 for v in (sc, csum, cmax, bar)) and (bar * 4) % 8 == 0 and (ring * 4) % 128 == 0
+        # the kernel's TMA copies at the longest share: item t (K tiles, then V tiles) -> slot
+        # t % slots, box b of BOX rows at ring + slot*SUB*hd + b*BOX*hd, from cache row
+        # s0 + j0 + b*BOX, column kvh*hd; rows past the cache's end arrive as zeros
         L = ctx
         chunk = -(-L // cs)
         for rank in (0, cs - 1):
             s0 = min(L, rank * chunk)
             n = min(L, s0 + chunk) - s0
             n_sub = -(-n // SUB)
-            for t in range(n_sub):
-                rows = min(SUB, n - t * SUB)
-                for r in (0, rows - 1):
-                    pos = s0 + t * SUB + r
-                    assert pos < ctx
-                    for c in (0, nd4 - 1):
-                        dst = ring + (t % slots) * SUB * pitch + r * pitch + 4 * c
-                        assert (dst * 4) % 16 == 0 and dst + 4 <= ring + slots * SUB * pitch <= csum
-                        for kvh in (0, n_kv - 1):
-                            src = pos * kv_dim + kvh * hd + 4 * c
-                            assert (src * 4) % 16 == 0 and src + 4 <= ctx * kv_dim
-                    # its score goes to sc[gq * chunk_max + j0 + r], below the next region
-                    assert t * SUB + r < chunk_max
+            for t in range(2 * n_sub):
+                sub = t - n_sub if t >= n_sub else t
+                rows = min(SUB, n - sub * SUB)
+                boxes = -(-rows // BOX)
+                assert boxes * BOX * hd * 4 < (1 << 20)  # one mbarrier phase's byte count
+                for b in range(boxes):
+                    dst = ring + (t % slots) * SUB * pitch + b * BOX * pitch
+                    assert (dst * 4) % 128 == 0 and dst + BOX * pitch <= ring + slots * SUB * pitch <= csum
+                    y = s0 + sub * SUB + b * BOX
+                    assert 0 <= y < ctx
+                    for kvh in (0, n_kv - 1):
+                        x = kvh * hd
+                        assert (x * 4) % 16 == 0 and x + hd <= kv_dim
+                # its scores go to sc[gq * chunk_max + j0 + r], r < rows, below the next region
+                if t < n_sub:
+                    assert sub * SUB + rows <= chunk_max
