@@ -168,6 +168,9 @@ def parse_args():
     p.add_argument("--resident", type=int, default=None, metavar="K",
                    help="one-position Q4_0 / Q8_0 launches that fit shared memory on the resident kernel with K "
                         "CTAs per SM (0: streaming kernel only); neon_cuda_set_resident (default: the library's)")
+    p.add_argument("--attn-rows", default=None, metavar="MIN:SHARE",
+                   help="decode attention: at least MIN cache rows per CTA, the cluster sized for SHARE rows of "
+                        "ctx_len per CTA (multiples of 32); neon_cuda_set_attn_rows (default: the library's)")
     p.add_argument("--batch", type=int, default=1,
                    help="matvec workloads: positions per call; > 1 times the prefill path (one JSON line)")
     p.add_argument("--tile-sweep", action="store_true",
@@ -445,6 +448,8 @@ def run_decode(args):
         N.set_stream_tiles(*(int(v) for v in args.tiles.split(":")))
     if args.resident is not None:
         N.set_resident(args.resident)
+    if args.attn_rows:
+        N.set_attn_rows(*(int(v) for v in args.attn_rows.split(":")))
     N.set_fused_collectives(not args.no_fused_collectives)
     comm = None
     barrier, max_over_ranks = (lambda: None), (lambda v: v)
@@ -479,7 +484,8 @@ def run_decode(args):
                                                 "variants": [v for v, on in (("cuda_core_prefill", args.cuda_core_prefill),)
                                                              if on]
                                                 + ([f"resident {args.resident}"] if args.resident is not None
-                                                   else [])},
+                                                   else [])
+                                                + ([f"attn rows {args.attn_rows}"] if args.attn_rows else [])},
                 "e2e": {"value": res["e2e_tokens_per_s"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 4, "api": res["e2e"]},
                 "load_s": res["load_s"], "roofline": decode_roofline(dict(res), cfg, world)["hbm"],
@@ -638,6 +644,8 @@ def run_neon(args):
         N.set_stream_tiles(*(int(v) for v in args.tiles.split(":")))
     if getattr(args, "resident", None) is not None:
         N.set_resident(args.resident)
+    if getattr(args, "attn_rows", None):
+        N.set_attn_rows(*(int(v) for v in args.attn_rows.split(":")))
     dev = torch.device("cuda", local)
 
     # One GPU: a rotation of whole matrices. N > 1 (strong scaling): every rank

@@ -392,6 +392,14 @@ NEON_API int neon_cuda_set_stream_tiles(int rows_per_tile, int blocks_per_chunk)
  * order). Process-wide. */
 NEON_API int neon_cuda_set_resident(int ctas_per_sm);
 
+/* Decode attention work split: a model's cluster of CTAs per KV head is the
+ * smallest (up to 16) whose share of ctx_len is at most share_rows rows (read
+ * when a model is created; default 128); at a step the cluster's CTAs take
+ * the context in shares of at least min_rows (read when a step is launched
+ * or captured; default 32). Multiples of 32 from 32 to 16384. Tuning and
+ * tests only; no counterpart in the reference. Process-wide. */
+NEON_API int neon_cuda_set_attn_rows(int min_rows, int share_rows);
+
 /* Launch option: programmatic dependent launch (PDL) lets a matvec fetch its
  * weights while the previous kernel on the stream finishes; on by default. */
 NEON_API int neon_cuda_set_pdl(int enabled);

@@ -33,13 +33,13 @@ namespace neon {
 enum : int { kEpiStore = 0, kEpiRope = 1, kEpiAtPos = 2, kEpiSwiglu = 3, kEpiSilu = 5 };
 }  // namespace neon
 
-#include <cooperative_groups.h>
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstring>
 #include <string>
@@ -54,6 +54,11 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kMaxChunk = 256;      // positions per forward chunk (prefill)
 constexpr int kMaxCtx = 16384;      // attention scores live in shared memory
+
+// neon_cuda_set_attn_rows: the decode attention's cache rows per CTA at
+// least (read when a step is launched), and the share of ctx_len per CTA the
+// cluster size is chosen for (read when a model is created); multiples of 32.
+std::atomic<int> g_attn_min_rows{32}, g_attn_share_rows{128};
 
 #define DEC_TRY(call)                                              \
     do {                                                           \
@@ -478,35 +483,62 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const float* __rest
 
 
 // ---------------------------------------------------------------------------
-// Decode attention in one launch: a thread-block cluster of cs CTAs (8, or 16
-// for long contexts) per KV head. CTA r of the cluster takes positions
-// [r*chunk, (r+1)*chunk) of the L = *d_pos + 1 cache rows. Its K rows, then its
-// V rows, stream through a ring of shared-memory slots of kAttnSub rows: one
-// thread fills a slot with TMA tensor copies of 16-row boxes (the layer's K or
-// V cache as a 2D tensor, rows x kv_dim, one CUtensorMap each, built when the
-// model is created), as many slots as the CTA's tiles need while every
-// cluster of the launch stays resident (attn_pick_slots), so at the
-// configurations' contexts all of a CTA's rows are requested at once by a
-// handful of copy instructions; a slot is refilled as soon as its rows are
-// used. Scores for the head's query group go to shared memory; the CTAs
-// exchange their maxima through distributed shared memory, so every CTA forms
-// p_s = fast_expf(score_s - max over ALL positions) exactly as
-// transformer_forward does (:1123-1137); each CTA sums p and p * v over its
-// positions, and CTA 0 adds the partials in rank order: out = (sum p v) /
-// (sum p).
+// Decode attention (transformer_forward's attention at one position,
+// rawllm_forward.hpp:1115-1151): a thread-block cluster of cs CTAs per KV
+// head. At context length L = *d_pos + 1, CTA r of the cluster takes cache
+// rows [r * rows, (r + 1) * rows) (attn_rows_per_cta); the first n_act CTAs
+// have rows, the others leave after the cluster's opening barrier.
+//
+// K and V rows land in shared memory by TMA tensor copies of 32-row x
+// bw-float boxes with the matching swizzle, so that a lane per cache row
+// reads its row's 16-byte chunks without bank conflicts. A CTA's rows come in
+// rounds of round_rows through two slots: its K rounds, then its V rounds,
+// item t in slot t % 2, each slot refilled as soon as its item is consumed,
+// so that the V rows arrive while the K rows are scored (the slots stay
+// small enough for two CTAs per SM, which keeps every KV head's cluster
+// resident at once). The rows before *d_pos were written by earlier decode
+// steps, whose kernels have all finished before any kernel of this step
+// starts (each step opens with the embedding kernel, which waits for the
+// step before); the first two items' copies of them are issued before the
+// dependency wait and overlap the kernel before. Only the box that holds the
+// new row, written by the kernel before, waits.
+//
+// Pass 1 (per round): warp tasks (32-row box, dim block), a lane per row, the
+// group's query rows read as broadcasts: the partial dot per (row, head, dim
+// block); the score is the blocks' partials added in order, times the scale.
+// Each CTA sends its per-head maxima to every active CTA of the cluster
+// (st.async into the peer's shared memory, counted on the peer's mbarrier),
+// so that all form p = fast_expf(score - max over ALL positions) exactly as
+// transformer_forward does (:1123-1137): fast_expf is an approximation, and
+// rescaling by per-CTA maxima would not reproduce its values. Pass 2: a warp
+// per row stride, a lane per float4 column: o = sum p * v, l = sum p. Each
+// CTA keeps (o, l) in its shared memory and signals CTA 0, which reads them
+// through distributed shared memory and adds them in rank order:
+// out = (sum o) * (1 / sum l).
 // ---------------------------------------------------------------------------
 
 __device__ __forceinline__ uint32_t smem_addr_d(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
-__device__ __forceinline__ bool mbar_wait_d(uint64_t* bar, uint32_t parity, unsigned int* err) {
+
+// Bounded wait on an mbarrier phase (2 s of %globaltimer, then bit 2 of the
+// error word); `cluster`: acquire at cluster scope (data from other CTAs).
+__device__ __forceinline__ bool mbar_wait_d(uint64_t* bar, uint32_t parity, unsigned int* err, bool cluster = false) {
     uint32_t done = 0;
     unsigned long long t0 = 0;
     for (int it = 0;; ++it) {
-        asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
-                     : "=r"(done)
-                     : "r"(smem_addr_d(bar)), "r"(parity)
-                     : "memory");
+        if (cluster)
+            asm volatile(
+                "{ .reg .pred p; mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, "
+                "0, p; }"
+                : "=r"(done)
+                : "r"(smem_addr_d(bar)), "r"(parity)
+                : "memory");
+        else
+            asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+                         : "=r"(done)
+                         : "r"(smem_addr_d(bar)), "r"(parity)
+                         : "memory");
         if (done) return true;
         unsigned long long t;
         asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
@@ -520,9 +552,9 @@ __device__ __forceinline__ bool mbar_wait_d(uint64_t* bar, uint32_t parity, unsi
 
 static_assert(kThreads == kAttnThreads, "the attention layout assumes kThreads threads");
 
-// A 16-row box of a head's K or V rows: 2D tensor copy (columns x .. x + hd,
-// rows y .. y + kAttnBox of the layer's cache) into shared memory, completion
-// counted in bytes on `bar`. Rows past the cache's end arrive as zeros.
+// A box of the layer's K or V cache (a 2D tensor, rows x kv_dim): columns x ..
+// x + bw, rows y .. y + 32, into shared memory, completion counted in bytes on
+// `bar`. Rows past the cache's end arrive as zeros.
 __device__ __forceinline__ void tma_box(float* dst, const CUtensorMap* tm, int x, int y, uint64_t* bar) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
@@ -531,202 +563,294 @@ __device__ __forceinline__ void tma_box(float* dst, const CUtensorMap* tm, int x
         : "memory");
 }
 
-__global__ void __launch_bounds__(kThreads) attn_decode_kernel(const float* __restrict__ q,
-                                                               const __grid_constant__ CUtensorMap tmk,
-                                                               const __grid_constant__ CUtensorMap tmv,
-                                                               const int* __restrict__ d_pos, int hd, int group,
-                                                               float scale, int chunk_max, int slots,
-                                                               float* __restrict__ out, unsigned int* err) {
-    namespace cg = cooperative_groups;
+// Offset (floats) of 16-byte chunk c of row r in a dim block of BW-float rows
+// as a TMA box with the BW*4-byte swizzle leaves it: the chunk index XOR bits
+// 7.. of the row's byte offset (the block starts 1024-byte aligned).
+template <int BW>
+__device__ __forceinline__ int attn_swz(int r, int c) {
+    constexpr int kW = BW * 4, kM = kW / 16 - 1;
+    return r * BW + ((c ^ ((r * kW >> 7) & kM)) << 2);
+}
+
+template <int GP, int BW>
+__global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(
+    const float* __restrict__ q, const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
+    const int* __restrict__ d_pos, int hd, int group, float scale, int min_rows, int round_rows, int score_rows,
+    float* __restrict__ out, unsigned int* err) {
     extern __shared__ __align__(1024) float sm[];
-    cg::cluster_group cl = cg::this_cluster();
-    const int rank = (int)cl.block_rank(), cs = (int)cl.num_blocks();
+    uint32_t rank, cs;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
+    asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(cs));
     const int kvh = blockIdx.x / cs;
-    const AttnSmem lay = attn_smem_layout(group, hd, chunk_max, cs, slots);
-    float* qs = sm + lay.q;
-    float* sc = sm + lay.sc;     // [group][chunk_max]
-    float* ring = sm + lay.ring; // [slots][kAttnSub][hd] (128-byte aligned); later [parts][group][hd]
-    float* co = sm + lay.co;     // [cluster][group][hd]   (CTA 0; overlays the ring)
-    float* csum = sm + lay.csum; // [cluster][kAttnMaxGroup] (read in CTA 0)
-    float* cmax = sm + lay.cmax; // [cluster][kAttnMaxGroup]
-    uint64_t* full = reinterpret_cast<uint64_t*>(sm + lay.bar);
-    __shared__ float gm[kAttnMaxGroup];
-    const int pitch = hd;
-    const int S = slots;
+    const int pos = __ldcg(d_pos), L = pos + 1;
+    const int rows = attn_rows_per_cta(L, (int)cs, min_rows);
+    const int n_act = (L + rows - 1) / rows;
+    const int s0 = (int)rank * rows;
+    const int len = s0 < L ? min(rows, L - s0) : 0;
+    const int nbk = hd / BW;
+    const AttnSmem lay = attn_smem_layout(hd, GP, BW, round_rows, score_rows, (int)cs);
+    float* const slot0 = sm + lay.k;  // the two slots of K or V rows
+    float* const slot1 = sm + lay.v;
+    auto slot = [&](int t) { return (t & 1) ? slot1 : slot0; };
+    float* ps = sm + lay.ps;  // [nbk][round_rows][GP]
+    float* sc = sm + lay.sc;  // [score_rows][GP]
+    float* qs = sm + lay.q;   // [GP][hd]
+    float* wm = sm + lay.wm;  // [warps][GP]
+    float* wl = sm + lay.wl;
+    float* cmax = sm + lay.cmax;  // [cs][GP]
+    // slot 0, slot 1, the cluster's maxima, (CTA 0) the peers' partials, (peers) CTA 0 has read them
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sm + lay.bar);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const bool aligned = (smem_addr_d(sm) & 1023u) == 0;  // the swizzled boxes need it
     if (threadIdx.x == 0) {
-        for (int i = 0; i < S; ++i)
-            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr_d(&full[i])) : "memory");
+        if (!aligned) atomicOr(err, 8u);
+        for (int i = 0; i < 5; ++i)
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr_d(&bars[i])),
+                         "r"(i == 3 ? (uint32_t)max(1, n_act - 1) : 1u)
+                         : "memory");
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        if (len > 0 && n_act > 1)
+            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr_d(&bars[2])),
+                         "r"((uint32_t)(n_act * GP * 4))
+                         : "memory");
+    }
+    __syncthreads();
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+    if (len == 0 || !aligned) {
+        asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+        return;
+    }
+    const int nr = (len + round_rows - 1) / round_rows, n_items = 2 * nr;
+    constexpr uint32_t kBoxBytes = BW * kAttnBoxRows * 4;
+    // item t (K round t, then V round t - nr) into slot t % 2 by warp 0;
+    // mode 0: every box, 1: the boxes without row pos (before the dependency
+    // wait), 2: the box with it
+    auto issue = [&](int t, int mode) {
+        const bool is_v = t >= nr;
+        const int r0 = (is_v ? t - nr : t) * round_rows;
+        const int nrb = (min(round_rows, len - r0) + kAttnBoxRows - 1) / kAttnBoxRows;
+        uint64_t* bar = &bars[t & 1];
+        if (mode != 2 && lane == 0)
+            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr_d(bar)),
+                         "r"((uint32_t)(nrb * nbk) * kBoxBytes)
+                         : "memory");
+        __syncwarp();
+        for (int i = lane; i < nrb * nbk; i += 32) {
+            const int rb = i / nbk, nb = i - rb * nbk, y = s0 + r0 + rb * kAttnBoxRows;
+            const bool has_pos = pos < y + kAttnBoxRows;
+            if ((mode == 1 && has_pos) || (mode == 2 && !has_pos)) continue;
+            tma_box(slot(t) + (nb * round_rows + rb * kAttnBoxRows) * BW, is_v ? &tmv : &tmk, kvh * hd + nb * BW,
+                    y, bar);
+        }
+    };
+    // slot t % 2 is read: refill it with item t + 2 (after the barrier that closes the reads)
+    auto refill = [&](int t) {
+        if (warp == 0 && t + 2 < n_items) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            issue(t + 2, 0);
+        }
+    };
+    if (warp == 0) {
+#pragma unroll 1
+        for (int t = 0; t < 2; ++t) issue(t, 1);
     }
     pdl_wait_d();
     pdl_trigger_d();
+    if (warp == 0) {
+#pragma unroll 1
+        for (int t = 0; t < 2; ++t) issue(t, 2);
+    }
+    for (int i = threadIdx.x; i < GP * hd; i += kAttnThreads)
+        qs[i] = i < group * hd ? q[(long long)kvh * group * hd + i] : 0.f;
     __syncthreads();
-    const int L = *d_pos + 1;
-    const int chunk = (L + cs - 1) / cs;
-    const int s0 = min(L, rank * chunk), len = min(L, s0 + chunk) - s0;
-    const int n_sub = (len + kAttnSub - 1) / kAttnSub;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nd4 = hd / 4;
-    // item t < n_sub: K rows of sub-chunk t; n_sub <= t < 2 n_sub: V rows of sub-chunk t - n_sub
-    auto issue = [&](int t) {
-        const int slot = t % S;
-        const bool is_v = t >= n_sub;
-        const int sub = is_v ? t - n_sub : t;
-        const int j0 = sub * kAttnSub, rows = min(kAttnSub, len - j0);
-        const int boxes = (rows + kAttnBox - 1) / kAttnBox;
-        float* dst = ring + slot * kAttnSub * pitch;
-        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr_d(&full[slot])),
-                     "r"((uint32_t)(boxes * kAttnBox * hd * 4))
-                     : "memory");
-        for (int bx = 0; bx < boxes; ++bx)
-            tma_box(dst + bx * kAttnBox * pitch, is_v ? &tmv : &tmk, kvh * hd, s0 + j0 + bx * kAttnBox, &full[slot]);
-    };
-    const int n_items = 2 * n_sub;
-    if (threadIdx.x == 0)
-        for (int t = 0; t < min(S, n_items); ++t) issue(t);
-    for (int i = threadIdx.x; i < group * hd; i += blockDim.x) qs[i] = q[(long long)kvh * group * hd + i];
-    __syncthreads();
+
+    // pass 1, per round: partial dots per (row, head, dim block), then the scores
+    const int gq = threadIdx.x % GP;  // the head of this thread's (row, head) pairs
+    float run_max = -INFINITY;
     bool ok = true;
-    // pass 1: scores, a thread per cache row of the slot
-    for (int t = 0; t < n_sub; ++t) {
-        ok = ok && mbar_wait_d(&full[t % S], (uint32_t)((t / S) & 1), err);
-        const float* rows_k = ring + (t % S) * kAttnSub * pitch;
-        const int j0 = t * kAttnSub, rows = min(kAttnSub, len - j0);
-        {
-            // four threads per row (lanes 4r'..4r'+3 of a warp), thread q4i takes float4
-            // columns q4i, q4i+4, ..; the four partial dots meet by two shuffles
-            const int r = threadIdx.x >> 2, q4i = threadIdx.x & 3;
-            const float4* kr = reinterpret_cast<const float4*>(rows_k + r * pitch);
-            float acc[kAttnMaxGroup];
+    for (int j = 0; j < nr; ++j) {
+        const int r0 = j * round_rows, rl = min(round_rows, len - r0);
+        const int nrb = (rl + kAttnBoxRows - 1) / kAttnBoxRows;
+        ok = mbar_wait_d(&bars[j & 1], (uint32_t)((j >> 1) & 1), err) && ok;
+        const float* Ks = slot(j);
+        for (int t = warp; t < nrb * nbk; t += kAttnWarps) {
+            const int rb = t / nbk, nb = t - rb * nbk, r = rb * kAttnBoxRows + lane;
+            if (r < rl) {
+                const float* kb = Ks + nb * round_rows * BW;
+                const float* qb = qs + nb * BW;
+                float acc[GP];
 #pragma unroll
-            for (int gq = 0; gq < kAttnMaxGroup; ++gq) acc[gq] = 0.f;
-            if (r < rows) {
-                for (int c = q4i; c < nd4; c += 4) {
-                    const float4 k4 = kr[c];
+                for (int g = 0; g < GP; ++g) acc[g] = 0.f;
+#pragma unroll 2
+                for (int c = 0; c < BW / 4; ++c) {
+                    const float4 k4 = *reinterpret_cast<const float4*>(kb + attn_swz<BW>(r, c));
 #pragma unroll
-                    for (int gq = 0; gq < kAttnMaxGroup; ++gq) {
-                        if (gq < group) {
-                            const float4 q4 = reinterpret_cast<const float4*>(qs + gq * hd)[c];
-                            acc[gq] = __fmaf_rn(q4.x, k4.x, acc[gq]);
-                            acc[gq] = __fmaf_rn(q4.y, k4.y, acc[gq]);
-                            acc[gq] = __fmaf_rn(q4.z, k4.z, acc[gq]);
-                            acc[gq] = __fmaf_rn(q4.w, k4.w, acc[gq]);
-                        }
+                    for (int g = 0; g < GP; ++g) {
+                        const float4 q4 = *reinterpret_cast<const float4*>(qb + g * hd + c * 4);
+                        acc[g] = __fmaf_rn(q4.x, k4.x, acc[g]);
+                        acc[g] = __fmaf_rn(q4.y, k4.y, acc[g]);
+                        acc[g] = __fmaf_rn(q4.z, k4.z, acc[g]);
+                        acc[g] = __fmaf_rn(q4.w, k4.w, acc[g]);
                     }
                 }
-            }
+                float* dst = ps + (nb * round_rows + r) * GP;
+                if constexpr (GP >= 4) {
 #pragma unroll
-            for (int gq = 0; gq < kAttnMaxGroup; ++gq) {
-                acc[gq] += __shfl_xor_sync(0xffffffffu, acc[gq], 1);
-                acc[gq] += __shfl_xor_sync(0xffffffffu, acc[gq], 2);
-            }
-            if (r < rows && q4i == 0) {
+                    for (int g = 0; g < GP; g += 4)
+                        *reinterpret_cast<float4*>(dst + g) = make_float4(acc[g], acc[g + 1], acc[g + 2], acc[g + 3]);
+                } else {
 #pragma unroll
-                for (int gq = 0; gq < kAttnMaxGroup; ++gq)
-                    if (gq < group) sc[gq * chunk_max + j0 + r] = __fmul_rn(acc[gq], scale);
-            }
-        }
-        __syncthreads();  // the slot is free
-        if (threadIdx.x == 0 && t + S < n_items) {
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            issue(t + S);
-        }
-    }
-    // this CTA's max per query head (warp gq), published to every CTA of the cluster
-    if (warp < group) {
-        float m = -INFINITY;
-        for (int j = lane; j < len; j += 32) m = fmaxf(m, sc[warp * chunk_max + j]);
-        m = warp_max_f(m);
-        if (lane < cs) *cl.map_shared_rank(&cmax[rank * kAttnMaxGroup + warp], lane) = m;
-    }
-    cl.sync();
-    if ((int)threadIdx.x < group) {
-        float m = -INFINITY;
-        for (int r = 0; r < cs; ++r) m = fmaxf(m, cmax[r * kAttnMaxGroup + threadIdx.x]);
-        gm[threadIdx.x] = m;
-    }
-    __syncthreads();
-    // p = fast_expf(score - max), in place; the CTA's sum of p per head to CTA 0
-    for (int idx = threadIdx.x; idx < group * len; idx += blockDim.x) {
-        const int gq = idx / len, j = idx - gq * len;
-        sc[gq * chunk_max + j] = fast_expf_dev(__fsub_rn(sc[gq * chunk_max + j], gm[gq]));
-    }
-    __syncthreads();
-    if (warp < group) {
-        float sp = 0.f;
-        for (int j = lane; j < len; j += 32) sp += sc[warp * chunk_max + j];
-        sp = warp_sum_f(sp);
-        if (lane == 0) *cl.map_shared_rank(&csum[rank * kAttnMaxGroup + warp], 0) = sp;
-    }
-    // pass 2: sum over positions of p * v; thread (column of 4 dims, part)
-    const int parts = blockDim.x / nd4;
-    const int c4 = threadIdx.x % nd4, part = threadIdx.x / nd4;
-    float4 acc[kAttnMaxGroup];
-#pragma unroll
-    for (int gq = 0; gq < kAttnMaxGroup; ++gq) acc[gq] = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int t = n_sub; t < n_items; ++t) {
-        ok = ok && mbar_wait_d(&full[t % S], (uint32_t)((t / S) & 1), err);
-        const float* rows_v = ring + (t % S) * kAttnSub * pitch;
-        const int j0 = (t - n_sub) * kAttnSub, rows = min(kAttnSub, len - j0);
-        if (part < parts) {
-            for (int r = part; r < rows; r += parts) {
-                const float4 v4 = reinterpret_cast<const float4*>(rows_v + r * pitch)[c4];
-#pragma unroll
-                for (int gq = 0; gq < kAttnMaxGroup; ++gq) {
-                    if (gq < group) {
-                        const float p = sc[gq * chunk_max + j0 + r];
-                        acc[gq].x = __fmaf_rn(p, v4.x, acc[gq].x);
-                        acc[gq].y = __fmaf_rn(p, v4.y, acc[gq].y);
-                        acc[gq].z = __fmaf_rn(p, v4.z, acc[gq].z);
-                        acc[gq].w = __fmaf_rn(p, v4.w, acc[gq].w);
-                    }
+                    for (int g = 0; g < GP; ++g) dst[g] = acc[g];
                 }
             }
         }
         __syncthreads();
-        if (threadIdx.x == 0 && t + S < n_items) {
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            issue(t + S);
+        refill(j);
+        for (int r = threadIdx.x / GP; r < rl; r += kAttnThreads / GP) {
+            float d = ps[r * GP + gq];
+            for (int nb = 1; nb < nbk; ++nb) d += ps[(nb * round_rows + r) * GP + gq];
+            const float s = __fmul_rn(d, scale);
+            sc[(r0 + r) * GP + gq] = s;
+            run_max = fmaxf(run_max, s);
+        }
+        __syncthreads();  // ps is free for the next round
+    }
+    // this CTA's maximum per head, then the cluster's
+#pragma unroll
+    for (int o = 16; o >= GP; o >>= 1) run_max = fmaxf(run_max, __shfl_xor_sync(0xffffffffu, run_max, o));
+    if (lane < GP) wm[warp * GP + lane] = run_max;
+    __syncthreads();
+    float m = wm[gq];
+#pragma unroll
+    for (int w = 1; w < kAttnWarps; ++w) m = fmaxf(m, wm[w * GP + gq]);
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");  // every CTA's barriers are set up
+    if (n_act > 1) {
+        if ((int)threadIdx.x < n_act * GP) {  // head gq's maximum to CTA threadIdx.x / GP
+            const uint32_t peer = threadIdx.x / GP;
+            uint32_t dst, bar;
+            asm volatile("mapa.shared::cluster.u32 %0, %1, %2;"
+                         : "=r"(dst)
+                         : "r"(smem_addr_d(&cmax[rank * GP + gq])), "r"(peer));
+            asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(bar) : "r"(smem_addr_d(&bars[2])), "r"(peer));
+            asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(dst),
+                         "r"(__float_as_uint(m)), "r"(bar)
+                         : "memory");
+        }
+        ok = mbar_wait_d(&bars[2], 0, err, true) && ok;
+        m = cmax[gq];
+        for (int r = 1; r < n_act; ++r) m = fmaxf(m, cmax[r * GP + gq]);
+    }
+    // p = fast_expf(score - max) in place, l = sum p
+    float lsum = 0.f;
+    for (int r = threadIdx.x / GP; r < len; r += kAttnThreads / GP) {
+        const float p = fast_expf_dev(__fsub_rn(sc[r * GP + gq], m));
+        sc[r * GP + gq] = p;
+        lsum += p;
+    }
+#pragma unroll
+    for (int o = 16; o >= GP; o >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
+    if (lane < GP) wl[warp * GP + lane] = lsum;
+    __syncthreads();
+
+    // pass 2, per round: o = sum over rows of p * v, a lane per float4 column
+    const int nc = hd / 4;
+    constexpr int kCB = BW / 4;  // 16-byte chunks per block row
+    float4 acc[2][GP];
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int g = 0; g < GP; ++g) acc[i][g] = make_float4(0.f, 0.f, 0.f, 0.f);
+    const int c0 = lane, c1 = lane + 32;
+    const int vo0 = (c0 / kCB) * round_rows * BW, vo1 = (c1 / kCB) * round_rows * BW;
+    auto pv = [&](float4(&a)[GP], const float* Vs, int vo, int c, int r, const float* p) {
+        const float4 v4 = *reinterpret_cast<const float4*>(Vs + vo + attn_swz<BW>(r, c % kCB));
+#pragma unroll
+        for (int g = 0; g < GP; ++g) {
+            a[g].x = __fmaf_rn(p[g], v4.x, a[g].x);
+            a[g].y = __fmaf_rn(p[g], v4.y, a[g].y);
+            a[g].z = __fmaf_rn(p[g], v4.z, a[g].z);
+            a[g].w = __fmaf_rn(p[g], v4.w, a[g].w);
+        }
+    };
+    for (int j = 0; j < nr; ++j) {
+        const int t = nr + j, r0 = j * round_rows, rl = min(round_rows, len - r0);
+        ok = mbar_wait_d(&bars[t & 1], (uint32_t)((t >> 1) & 1), err) && ok;
+        const float* Vs = slot(t);
+        for (int r = warp; r < rl; r += kAttnWarps) {
+            float p[GP];
+            const float* pr = sc + (r0 + r) * GP;
+            if constexpr (GP >= 4) {
+#pragma unroll
+                for (int g = 0; g < GP; g += 4) {
+                    const float4 p4 = *reinterpret_cast<const float4*>(pr + g);
+                    p[g] = p4.x, p[g + 1] = p4.y, p[g + 2] = p4.z, p[g + 3] = p4.w;
+                }
+            } else {
+#pragma unroll
+                for (int g = 0; g < GP; ++g) p[g] = pr[g];
+            }
+            if (c0 < nc) pv(acc[0], Vs, vo0, c0, r, p);
+            if (c1 < nc) pv(acc[1], Vs, vo1, c1, r, p);
+        }
+        if (j + 1 < nr) {
+            __syncthreads();  // the slot is read
+            refill(t);
         }
     }
-    (void)ok;  // a timed-out copy sets bit 2 of the error word; the results are then not used
-    // per-part partials -> the ring (its copies are all consumed), then the CTA's partial to CTA 0
-    float* red = ring;
-    if (part < parts) {
+    (void)ok;  // a copy or exchange that timed out set bit 2 of the error word; the results are then not used
+    // the warps' sums -> red (slot 0: the last item is in slot 1, and the
+    // barrier after the one before it closed slot 0's reads), then this CTA's
+    // o and l into ps and lsum, where CTA 0 reads them
+    float* red = sm + lay.red;
 #pragma unroll
-        for (int gq = 0; gq < kAttnMaxGroup; ++gq)
-            if (gq < group) reinterpret_cast<float4*>(red + ((long long)part * group + gq) * hd)[c4] = acc[gq];
+    for (int g = 0; g < GP; ++g) {
+        if (c0 < nc) *reinterpret_cast<float4*>(red + (warp * GP + g) * hd + c0 * 4) = acc[0][g];
+        if (c1 < nc) *reinterpret_cast<float4*>(red + (warp * GP + g) * hd + c1 * 4) = acc[1][g];
     }
     __syncthreads();
-    // this CTA's partial of every (head, dim), held while the cluster finishes
-    // with its rings (CTA 0's ring then takes the partials)
-    constexpr int kMaxPer = kAttnMaxGroup * 256 / kThreads;
-    float mine[kMaxPer];
-#pragma unroll
-    for (int u = 0; u < kMaxPer; ++u) {
-        const int idx = threadIdx.x + u * kThreads;
-        float r = 0.f;
-        if (idx < group * hd)
-            for (int k = 0; k < parts; ++k) r += red[(long long)k * group * hd + idx];
-        mine[u] = r;
+    const int ne = GP * hd;
+    float* mine = ps;               // [GP][hd]
+    float* mine_l = sm + lay.lsum;  // [GP]
+    if ((int)threadIdx.x < GP) {
+        float v = 0.f;
+        for (int w = 0; w < kAttnWarps; ++w) v += wl[w * GP + threadIdx.x];
+        mine_l[threadIdx.x] = v;
     }
-    cl.sync();
-    float* co0 = cl.map_shared_rank(co, 0);
+#pragma unroll 1
+    for (int e = threadIdx.x; e < ne; e += kAttnThreads) {
+        float v = 0.f;
 #pragma unroll
-    for (int u = 0; u < kMaxPer; ++u) {
-        const int idx = threadIdx.x + u * kThreads;
-        if (idx < group * hd) co0[rank * group * hd + idx] = mine[u];
+        for (int w = 0; w < kAttnWarps; ++w) v += red[w * ne + e];
+        mine[e] = v;
     }
-    cl.sync();
-    if (rank == 0) {
-        for (int idx = threadIdx.x; idx < group * hd; idx += blockDim.x) {
-            const int gq = idx / hd;
-            float num = 0.f, den = 0.f;
-            for (int r = 0; r < cs; ++r) {
-                num += co[r * group * hd + idx];
-                den += csum[r * kAttnMaxGroup + gq];
-            }
-            out[(long long)kvh * group * hd + idx] = __fmul_rn(num, __fdiv_rn(1.0f, den));
+    __syncthreads();
+    if (rank != 0) {
+        if (threadIdx.x == 0) {
+            uint32_t ready;
+            asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(ready) : "r"(smem_addr_d(&bars[3])));
+            asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(ready) : "memory");
+            mbar_wait_d(&bars[4], 0, err);  // CTA 0 has read this CTA's partial
+        }
+        return;
+    }
+    // CTA 0: out = (sum o) * (1 / sum l) over the active CTAs in rank order
+    if (n_act > 1) mbar_wait_d(&bars[3], 0, err, true);  // every active CTA's partial is in place
+#pragma unroll 1
+    for (int e = threadIdx.x; e < group * hd; e += kAttnThreads) {
+        const int g = e / hd;
+        float num = mine[e], den = mine_l[g];
+        for (int r = 1; r < n_act; ++r) {
+            num += *static_cast<const float*>(__cluster_map_shared_rank(&mine[e], r));
+            den += *static_cast<const float*>(__cluster_map_shared_rank(&mine_l[g], r));
+        }
+        out[(long long)kvh * group * hd + e] = __fmul_rn(num, __fdiv_rn(1.0f, den));
+    }
+    if (n_act > 1) {
+        __syncthreads();  // the peers' partials are read: release them
+        if ((int)threadIdx.x >= 1 && (int)threadIdx.x < n_act) {
+            uint32_t done;
+            asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(done) : "r"(smem_addr_d(&bars[4])), "r"(threadIdx.x));
+            asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(done) : "memory");
         }
     }
 }
@@ -856,8 +980,9 @@ struct neon_model {
     float* part = nullptr;           // partial sums of the column-split projections
     float* shift_scratch = nullptr;  // ctx_len x kv_dim, for neon_cuda_model_kv_shift
     float2* shift_cs = nullptr;      // rope_half (cos, sin) of the shift angle
-    int att_cs = 8;                  // CTAs per KV head in the decode attention (a cluster)
-    int att_slots = 2;               // its ring depth (attn_pick_slots)
+    // decode attention (attn_decode_kernel, attn_plan): a cluster of att_cs CTAs per KV head, K and
+    // V rows in rounds of att_round, scores for att_score_rows rows
+    int att_gp = 1, att_cs = 1, att_round = kAttnBoxRows, att_score_rows = kAttnMinScores, att_smem = 0;
     float* logits_full = nullptr;    // all-gathered logits (tensor parallel only)
     neon_tensor_t embd = nullptr, output = nullptr;
     float* output_norm = nullptr;
@@ -984,18 +1109,25 @@ int launch_embed(neon_model* m, const int* toks, int seq) {
                     nb, toks, (int)c.n_vocab, m->h, m->d_err);
 }
 
-// The decode attention kernel (one for every head dim).
-using AttnKernel = void (*)(const float*, CUtensorMap, CUtensorMap, const int*, int, int, float, int, int, float*,
+// The decode attention kernel for a padded group (head dims are multiples of
+// 32: 128-byte swizzled boxes).
+using AttnKernel = void (*)(const float*, CUtensorMap, CUtensorMap, const int*, int, int, float, int, int, int, float*,
                             unsigned int*);
-AttnKernel attn_kernel_for(int) { return attn_decode_kernel; }
+AttnKernel attn_kernel_for(int gp) {
+    switch (gp) {
+        case 1: return attn_decode_kernel<1, 32>;
+        case 2: return attn_decode_kernel<2, 32>;
+        case 4: return attn_decode_kernel<4, 32>;
+        default: return attn_decode_kernel<8, 32>;
+    }
+}
 
-// Dynamic shared memory of attn_decode_kernel.
 // The layers' K and V caches as 2D tensors for the decode attention's TMA
-// copies: ctx_len rows of kv_dim floats each, boxes of kAttnBox rows x
-// head_dim columns (a box's first column, kvh * head_dim, is 16-byte aligned:
-// head_dim is a multiple of 4). cuTensorMapEncodeTiled comes from the driver
-// through the runtime's entry-point query, so the library does not link
-// libcuda.
+// copies: ctx_len rows of kv_dim floats each, boxes of kAttnBoxRows rows x
+// 32 columns (128 bytes, the 128-byte swizzle; a box's first column,
+// kvh * head_dim + 32 * block, is 128-byte aligned). cuTensorMapEncodeTiled
+// comes from the driver through the runtime's entry-point query, so the
+// library does not link libcuda.
 int build_kv_maps(neon_model* m) {
     static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
     if (!encode) {
@@ -1007,8 +1139,8 @@ int build_kv_maps(neon_model* m) {
         encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
     }
     const auto& c = m->cfg;
-    if (c.head_dim == 0 || c.head_dim > 256 || c.head_dim % 4)
-        return error(NEON_ERR_UNSUPPORTED, "decode attention: head_dim must be a multiple of 4, at most 256");
+    if (attn_block_width((int)c.head_dim) != 32)
+        return error(NEON_ERR_UNSUPPORTED, "decode attention: head_dim must be a multiple of 32");
     m->tm_k.assign(c.n_layer, CUtensorMap{});
     m->tm_v.assign(c.n_layer, CUtensorMap{});
     for (uint32_t li = 0; li < c.n_layer; ++li) {
@@ -1016,11 +1148,11 @@ int build_kv_maps(neon_model* m) {
             float* base = (which ? m->V : m->K) + (size_t)li * c.ctx_len * m->kv_dim;
             const cuuint64_t dims[2] = {(cuuint64_t)m->kv_dim, (cuuint64_t)c.ctx_len};
             const cuuint64_t strides[1] = {(cuuint64_t)m->kv_dim * sizeof(float)};
-            const cuuint32_t box[2] = {(cuuint32_t)c.head_dim, (cuuint32_t)kAttnBox};
+            const cuuint32_t box[2] = {32u, (cuuint32_t)kAttnBoxRows};
             const cuuint32_t estr[2] = {1, 1};
             const CUresult r = encode(which ? &m->tm_v[li] : &m->tm_k[li], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base,
                                       dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                                      CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
             if (r != CUDA_SUCCESS)
                 return error(NEON_ERR_CUDA, "decode attention: cuTensorMapEncodeTiled failed (" +
@@ -1030,51 +1162,59 @@ int build_kv_maps(neon_model* m) {
     return NEON_OK;
 }
 
-int attn_chunk_max(const neon_model* m) { return (int)((m->cfg.ctx_len + m->att_cs - 1) / m->att_cs); }
-size_t attn_decode_smem(const neon_model* m, int slots) {
-    const int group = (int)(m->cfg.n_head / m->cfg.n_kv_head);
-    return sizeof(float) *
-           (size_t)attn_smem_layout(group, (int)m->cfg.head_dim, attn_chunk_max(m), m->att_cs, slots).total;
-}
-size_t attn_decode_smem(const neon_model* m) { return attn_decode_smem(m, m->att_slots); }
-
-// The ring depth of attn_decode_kernel: a slot per K and V tile of the
-// longest share (at most kAttnMaxSlots), cut while it would take more than
-// kAttnSmemMax or leave a cluster of the launch waiting for another to finish;
-// never below two (the next tile in flight while one is used).
-int attn_pick_slots(const neon_model* m) {
-    const int items = 2 * ((attn_chunk_max(m) + kAttnSub - 1) / kAttnSub);
-    for (int slots = std::min(kAttnMaxSlots, items); slots > 2; --slots) {
-        const size_t smem = attn_decode_smem(m, slots);
-        if (smem > (size_t)kAttnSmemMax) continue;
-        cudaLaunchConfig_t q = {};
-        q.gridDim = dim3((unsigned)(m->n_kv_l * m->att_cs));
-        q.blockDim = dim3(kThreads);
-        q.dynamicSmemBytes = smem;
-        cudaLaunchAttribute qa[1];
-        qa[0].id = cudaLaunchAttributeClusterDimension;
-        qa[0].val.clusterDim.x = (unsigned)m->att_cs;
-        qa[0].val.clusterDim.y = 1;
-        qa[0].val.clusterDim.z = 1;
-        q.attrs = qa;
-        q.numAttrs = 1;
-        int clusters = 0;
-        if (cudaOccupancyMaxActiveClusters(&clusters, attn_kernel_for((int)m->cfg.head_dim), &q) != cudaSuccess) {
-            cudaGetLastError();
-            continue;
-        }
-        if (clusters >= (int)m->n_kv_l) return slots;
+// Clusters of cs CTAs of the decode attention with `smem` bytes each fit the
+// device (cs > 8 needs the non-portable cluster size).
+bool attn_cluster_fits(AttnKernel k, int cs, int smem) {
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmemMax) != cudaSuccess ||
+        (cs > 8 && cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)) {
+        cudaGetLastError();
+        return false;
     }
-    return 2;
+    cudaLaunchConfig_t q = {};
+    q.gridDim = dim3((unsigned)cs);
+    q.blockDim = dim3(kAttnThreads);
+    q.dynamicSmemBytes = (size_t)smem;
+    cudaLaunchAttribute qa[1];
+    qa[0].id = cudaLaunchAttributeClusterDimension;
+    qa[0].val.clusterDim.x = (unsigned)cs;
+    qa[0].val.clusterDim.y = 1;
+    qa[0].val.clusterDim.z = 1;
+    q.attrs = qa;
+    q.numAttrs = 1;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, k, &q) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return clusters >= 1;
 }
 
-// attn_decode_kernel: one cluster of att_cs CTAs per KV head, PDL when enabled.
+// The decode attention's split (attn_plan), with the largest cluster the
+// device schedules (16, else 8, ...).
+int plan_attention(neon_model* m) {
+    const auto& c = m->cfg;
+    const int group = (int)(c.n_head / c.n_kv_head);
+    for (int cs_max = kAttnMaxCluster; cs_max >= 1; cs_max /= 2) {
+        AttnPlan p;
+        if (!attn_plan((int)c.ctx_len, group, (int)c.head_dim, cs_max, g_attn_share_rows.load(), &p)) break;
+        if (!attn_cluster_fits(attn_kernel_for(p.gp), p.cs, p.smem_bytes)) continue;
+        m->att_gp = p.gp;
+        m->att_cs = p.cs;
+        m->att_round = p.round_rows;
+        m->att_score_rows = p.score_rows;
+        m->att_smem = p.smem_bytes;
+        return NEON_OK;
+    }
+    return error(NEON_ERR_UNSUPPORTED, "decode attention: no cluster split of ctx_len fits the device");
+}
+
+// attn_decode_kernel: a cluster of att_cs CTAs per KV head, PDL when enabled.
 int launch_attn_decode(neon_model* m, uint32_t li) {
     const auto& c = m->cfg;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(m->n_kv_l * m->att_cs));
-    cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = attn_decode_smem(m);
+    cfg.blockDim = dim3(kAttnThreads);
+    cfg.dynamicSmemBytes = (size_t)m->att_smem;
     cfg.stream = m->stream;
     cudaLaunchAttribute attr[2];
     int n = 0;
@@ -1091,9 +1231,10 @@ int launch_attn_decode(neon_model* m, uint32_t li) {
     cfg.attrs = attr;
     cfg.numAttrs = n;
     const float scale = 1.0f / std::sqrt((float)c.head_dim);
-    cudaError_t e = cudaLaunchKernelEx(&cfg, attn_decode_kernel, (const float*)m->q, m->tm_k[li], m->tm_v[li],
+    const int min_rows = std::min(g_attn_min_rows.load(), m->att_score_rows);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, attn_kernel_for(m->att_gp), (const float*)m->q, m->tm_k[li], m->tm_v[li],
                                        (const int*)m->d_pos, (int)c.head_dim, (int)(c.n_head / c.n_kv_head), scale,
-                                       attn_chunk_max(m), m->att_slots, m->att, m->d_err);
+                                       min_rows, m->att_round, m->att_score_rows, m->att, m->d_err);
     if (e != cudaSuccess) return cuda_error(e, "attn_decode_kernel");
     return neon_internal::launched(1);
 }
@@ -1284,6 +1425,10 @@ int sync_and_check(neon_model* m) {
         DEC_TRY(cudaMemset(m->d_err, 0, sizeof(unsigned)));
         return error(NEON_ERR_CUDA, "decode attention: a shared-memory copy of the KV cache never completed");
     }
+    if (e & 8u) {
+        DEC_TRY(cudaMemset(m->d_err, 0, sizeof(unsigned)));
+        return error(NEON_ERR_CUDA, "decode attention: dynamic shared memory not 1024-byte aligned");
+    }
     if (m->world > 1) {
         const int rc = neon_cuda_comm_check(static_cast<neon_comm*>(m->comm));
         if (rc) return rc;
@@ -1417,6 +1562,7 @@ int neon_cuda_model_create_tp(const neon_model_config_t* cfg, neon_comm_t comm, 
     A((void**)&m->d_pos, sizeof(int));
     A((void**)&m->d_step, sizeof(int));
     A((void**)&m->d_err, sizeof(unsigned));
+    if (!rc) rc = plan_attention(m);
     if (!rc) rc = cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) == cudaSuccess ? NEON_OK : error(NEON_ERR_CUDA, "cudaStreamCreate");
     if (!rc) rc = (cudaEventCreate(&m->ev0) == cudaSuccess && cudaEventCreate(&m->ev1) == cudaSuccess &&
                    cudaEventCreate(&m->evf0) == cudaSuccess && cudaEventCreate(&m->evf1) == cudaSuccess)
@@ -1443,45 +1589,6 @@ int neon_cuda_model_create_tp(const neon_model_config_t* cfg, neon_comm_t comm, 
             rc = error(NEON_ERR_CUDA, "model initialisation copies failed");
     }
     if (!rc) rc = build_kv_maps(m);
-    if (!rc) {
-        // long contexts: 16 CTAs per KV head when the device schedules clusters that large
-        if (c.ctx_len > 1024 &&
-            cudaFuncSetAttribute(attn_kernel_for((int)c.head_dim), cudaFuncAttributeNonPortableClusterSizeAllowed, 1) ==
-                cudaSuccess) {
-            m->att_cs = kAttnMaxCluster;
-            cudaLaunchConfig_t q = {};
-            q.gridDim = dim3((unsigned)(m->n_kv_l * m->att_cs));
-            q.blockDim = dim3(kThreads);
-            q.dynamicSmemBytes = attn_decode_smem(m);
-            cudaLaunchAttribute qa[1];
-            qa[0].id = cudaLaunchAttributeClusterDimension;
-            qa[0].val.clusterDim.x = (unsigned)m->att_cs;
-            qa[0].val.clusterDim.y = 1;
-            qa[0].val.clusterDim.z = 1;
-            q.attrs = qa;
-            q.numAttrs = 1;
-            int clusters = 0;
-            if (q.dynamicSmemBytes > 48 * 1024)
-                cudaFuncSetAttribute(attn_kernel_for((int)c.head_dim), cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     220 * 1024);
-            if (attn_decode_smem(m) > 220 * 1024 ||
-                cudaOccupancyMaxActiveClusters(&clusters, attn_kernel_for((int)c.head_dim), &q) != cudaSuccess ||
-                clusters < 1) {
-                cudaGetLastError();
-                m->att_cs = 8;
-            }
-        }
-    }
-    if (!rc && attn_decode_smem(m) > 220 * 1024)
-        rc = error(NEON_ERR_UNSUPPORTED, "decode attention: ctx_len too large for one cluster per KV head");
-    if (!rc) {
-        // the process-wide limit at its largest, so that no later model lowers it under an earlier one's
-        if (cudaFuncSetAttribute(attn_kernel_for((int)c.head_dim), cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 220 * 1024) != cudaSuccess)
-            rc = error(NEON_ERR_CUDA, "cudaFuncSetAttribute(attn_decode_kernel)");
-        else
-            m->att_slots = attn_pick_slots(m);
-    }
     if (!rc && c.ctx_len * sizeof(float) > 48 * 1024) {
         if (cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(c.ctx_len * sizeof(float))) != cudaSuccess)
             rc = error(NEON_ERR_CUDA, "cudaFuncSetAttribute(attention_kernel)");
@@ -1495,6 +1602,15 @@ int neon_cuda_model_create_tp(const neon_model_config_t* cfg, neon_comm_t comm, 
         return rc;
     }
     *out = m;
+    return NEON_OK;
+}
+
+int neon_cuda_set_attn_rows(int min_rows, int share_rows) {
+    if (min_rows < kAttnBoxRows || share_rows < kAttnBoxRows || min_rows > kMaxCtx || share_rows > kMaxCtx ||
+        min_rows % kAttnBoxRows || share_rows % kAttnBoxRows)
+        return error(NEON_ERR_INVALID, "attention rows: multiples of 32 from 32 to 16384");
+    g_attn_min_rows.store(min_rows);
+    g_attn_share_rows.store(share_rows);
     return NEON_OK;
 }
 

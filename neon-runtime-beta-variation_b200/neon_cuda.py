@@ -102,6 +102,7 @@ C_ENTRY_POINTS = (
     "neon_cuda_set_dq_ring",
     "neon_cuda_set_stream_tiles",
     "neon_cuda_set_resident",
+    "neon_cuda_set_attn_rows",
 )
 
 _sz = C.c_size_t
@@ -167,6 +168,7 @@ def load(path: str | None = None) -> C.CDLL:
         L.neon_cuda_set_dq_ring.argtypes = [C.c_int]
         L.neon_cuda_set_stream_tiles.argtypes = [C.c_int, C.c_int]
         L.neon_cuda_set_resident.argtypes = [C.c_int]
+        L.neon_cuda_set_attn_rows.argtypes = [C.c_int, C.c_int]
         L.neon_cuda_matvec_q4_0_noalloc.argtypes = [_vp, _vp, _sz, _vp, _sz, _sz, _vp]
         L.neon_cuda_model_create.argtypes = [C.POINTER(_ModelConfig), C.POINTER(_vp)]
         L.neon_cuda_model_set_tensor.argtypes = [_vp, C.c_int, C.c_int, _vp, _sz, C.c_int, _sz, _sz]
@@ -240,6 +242,14 @@ def set_resident(ctas_per_sm: int = 1) -> None:
     resident kernel with this many CTAs per SM (default 1); 0 sends them all
     to the streaming kernel. Process-wide."""
     _check(load().neon_cuda_set_resident(int(ctas_per_sm)))
+
+
+def set_attn_rows(min_rows: int = 32, share_rows: int = 128) -> None:
+    """Decode attention: models created afterwards take the smallest cluster
+    (up to 16 CTAs per KV head) whose share of ctx_len is at most share_rows
+    rows; steps launched afterwards give each CTA at least min_rows rows.
+    Multiples of 32. Process-wide."""
+    _check(load().neon_cuda_set_attn_rows(int(min_rows), int(share_rows)))
 
 
 def set_pdl(enabled: bool) -> None:

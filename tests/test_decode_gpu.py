@@ -106,7 +106,7 @@ def test_errors_match_reference_messages():
 @pytest.mark.parametrize("cfg,n_prompt,steps", [
     (TINY.with_(n_vocab=777, n_embd=384, n_ff=1024, n_head=6, n_kv_head=2, ctx_len=300), 200, 24),
     (TINY.with_(plain_ffn=True, n_ff=768, ctx_len=120), 40, 24),                 # SiLU-FFN without a gate
-    (TINY.with_(n_head=8, n_kv_head=1, ctx_len=1100), 1060, 16),                 # long context: 16-CTA clusters, group 8
+    (TINY.with_(n_head=8, n_kv_head=1, ctx_len=1100), 1060, 16),                 # long context: 17 CTAs merged, group 8
     (S.QWEN3_0_6B.with_(ctx_len=128 + 64 + 1), 128, 64),
 ])
 def test_greedy_matches_reference(cfg, n_prompt, steps):
@@ -131,6 +131,40 @@ def test_greedy_matches_reference(cfg, n_prompt, steps):
         errs.append(rel_l2(m2.forward([t]), ref_logits[i + 1]))
     print(f"{cfg.name}: min top-2 margin {margin:.3g}, logits rel-L2 max {max(errs):.2e}")
     assert max(errs) <= MODEL_L2_RTOL
+
+
+def test_attention_splits_agree():
+    """The decode attention at three work splits of one cluster of 16 CTAs per
+    KV head (sized for 32-row shares; K and V in 32-row shared-memory rounds):
+    32-row shares over up to 8 CTAs, 96-row shares over 3 CTAs in 3 rounds
+    each, and one CTA for the whole context in up to 8 rounds (no exchange).
+    F32 projections and embedding keep activations unquantised, so the model
+    is continuous and the comparison sees the attention's rounding alone:
+    every decode step's logits within MATVEC_RTOL per element of the oracle's,
+    and the three splits within 1e-5 relative L2 of each other."""
+    cfg = TINY.with_(n_head=8, n_kv_head=2, ctx_len=256 + 1)
+    tensors = list(S.model_tensors(cfg, seed=31, wtype=S.GGML_F32, embd_type=S.GGML_F32))
+    prompt = S.prompt_tokens(230, cfg.n_vocab, 32)
+    toks = S.prompt_tokens(10, cfg.n_vocab, 33)
+    o = O.Model(cfg, tensors, "port")
+    o.forward(prompt)
+    ref = [o.forward([t]) for t in toks]
+    runs, errs = [], {}
+    try:
+        for lo, hi in ((32, 32), (96, 32), (256, 32)):
+            N.set_attn_rows(lo, hi)
+            m = N.Model(cfg, tensors)
+            m.forward(prompt)
+            runs.append([m.forward([t]) for t in toks])
+            m.free()
+            errs[f"{lo}-{hi}"] = [max_rel_err(lg, want) for lg, want in zip(runs[-1], ref)]
+    finally:
+        N.set_attn_rows()
+    print({k: f"{max(v):.2e}" for k, v in errs.items()})
+    assert all(max(v) <= MATVEC_RTOL for v in errs.values()), errs
+    for other in runs[1:]:
+        for a, b in zip(runs[0], other):
+            assert rel_l2(a, b) <= 1e-5
 
 
 def test_kv_cache_shift_matches_reference():
