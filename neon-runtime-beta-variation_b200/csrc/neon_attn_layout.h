@@ -10,6 +10,7 @@ constexpr int kAttnMaxGroup = 8;          // query heads per KV head
 constexpr int kAttnMaxCluster = 16;       // CTAs per KV head at most (a cluster)
 constexpr int kAttnBoxRows = 32;          // cache rows per TMA tensor copy
 constexpr int kAttnMinScores = 256;       // score rows a CTA holds at least
+constexpr int kAttnMaxRound = 256;        // rows of one round (a TMA box dimension is at most 256)
 constexpr int kAttnSmemTwo = 112 * 1024;  // dynamic shared memory of two CTAs per SM
 constexpr int kAttnSmemMax = 200 * 1024;  // dynamic shared memory a CTA may take
 
@@ -82,7 +83,8 @@ struct AttnPlan {
 // a cluster of cs CTAs per KV head, the smallest power of two (at most
 // cs_max) whose share of ctx is at most share_rows rows; a CTA's scores for
 // up to score_rows rows (its largest share, at least kAttnMinScores); its K
-// and V rows in rounds of round_rows: its largest share, lowered until the
+// and V rows in rounds of round_rows: its largest share (at most
+// kAttnMaxRound), lowered until the
 // CTA fits kAttnSmemTwo (two CTAs per SM, so that the device holds the
 // clusters of every KV head at once), else kAttnSmemMax. False when no
 // split fits.
@@ -100,7 +102,7 @@ inline bool attn_plan(int ctx, int group, int hd, int cs_max, int share_rows, At
     };
     if (attn_block_width(hd) == 0) return false;
     for (int limit : {kAttnSmemTwo, kAttnSmemMax})
-        for (int r = share; r >= kAttnBoxRows; r -= kAttnBoxRows)
+        for (int r = share < kAttnMaxRound ? share : kAttnMaxRound; r >= kAttnBoxRows; r -= kAttnBoxRows)
             if (fit(r, limit)) return true;
     return false;
 }

@@ -575,8 +575,9 @@ __device__ __forceinline__ int attn_swz(int r, int c) {
 template <int GP, int BW>
 __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(
     const float* __restrict__ q, const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
-    const int* __restrict__ d_pos, int hd, int group, float scale, int min_rows, int round_rows, int score_rows,
-    float* __restrict__ out, unsigned int* err) {
+    const __grid_constant__ CUtensorMap tmk_r, const __grid_constant__ CUtensorMap tmv_r, const int* __restrict__ d_pos,
+    int hd, int group, float scale, int min_rows, int round_rows, int score_rows, float* __restrict__ out,
+    unsigned int* err) {
     extern __shared__ __align__(1024) float sm[];
     uint32_t rank, cs;
     asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
@@ -621,26 +622,34 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(
         return;
     }
     const int nr = (len + round_rows - 1) / round_rows, n_items = 2 * nr;
-    constexpr uint32_t kBoxBytes = BW * kAttnBoxRows * 4;
     // item t (K round t, then V round t - nr) into slot t % 2 by warp 0;
     // mode 0: every box, 1: the boxes without row pos (before the dependency
     // wait), 2: the box with it
+    // item t: an item without row pos as one round-sized box per dim block (the
+    // round maps), the item with it as 32-row boxes, of which only the one
+    // holding row pos waits for the dependency
     auto issue = [&](int t, int mode) {
         const bool is_v = t >= nr;
         const int r0 = (is_v ? t - nr : t) * round_rows;
         const int nrb = (min(round_rows, len - r0) + kAttnBoxRows - 1) / kAttnBoxRows;
+        const bool pos_item = pos < s0 + r0 + nrb * kAttnBoxRows;  // rows < len <= pos + 1 - s0
         uint64_t* bar = &bars[t & 1];
+        float* base = slot(t);
         if (mode != 2 && lane == 0)
             asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr_d(bar)),
-                         "r"((uint32_t)(nrb * nbk) * kBoxBytes)
+                         "r"((uint32_t)(nbk * (pos_item ? nrb * kAttnBoxRows : round_rows) * BW * 4))
                          : "memory");
         __syncwarp();
+        if (!pos_item) {
+            if (mode != 2 && lane < nbk)
+                tma_box(base + lane * round_rows * BW, is_v ? &tmv_r : &tmk_r, kvh * hd + lane * BW, s0 + r0, bar);
+            return;
+        }
         for (int i = lane; i < nrb * nbk; i += 32) {
             const int rb = i / nbk, nb = i - rb * nbk, y = s0 + r0 + rb * kAttnBoxRows;
             const bool has_pos = pos < y + kAttnBoxRows;
             if ((mode == 1 && has_pos) || (mode == 2 && !has_pos)) continue;
-            tma_box(slot(t) + (nb * round_rows + rb * kAttnBoxRows) * BW, is_v ? &tmv : &tmk, kvh * hd + nb * BW,
-                    y, bar);
+            tma_box(base + (nb * round_rows + rb * kAttnBoxRows) * BW, is_v ? &tmv : &tmk, kvh * hd + nb * BW, y, bar);
         }
     };
     // slot t % 2 is read: refill it with item t + 2 (after the barrier that closes the reads)
@@ -833,17 +842,22 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(
         }
         return;
     }
-    // CTA 0: out = (sum o) * (1 / sum l) over the active CTAs in rank order
+    // CTA 0: out = (sum o) * (1 / sum l) over the active CTAs in rank order,
+    // four elements of one head per thread
     if (n_act > 1) mbar_wait_d(&bars[3], 0, err, true);  // every active CTA's partial is in place
 #pragma unroll 1
-    for (int e = threadIdx.x; e < group * hd; e += kAttnThreads) {
-        const int g = e / hd;
-        float num = mine[e], den = mine_l[g];
+    for (int e = 4 * threadIdx.x; e < group * hd; e += 4 * kAttnThreads) {
+        const int g = e / hd;  // hd % 4 == 0: the four share a head
+        float4 num = *reinterpret_cast<const float4*>(&mine[e]);
+        float den = mine_l[g];
         for (int r = 1; r < n_act; ++r) {
-            num += *static_cast<const float*>(__cluster_map_shared_rank(&mine[e], r));
+            const float4 v = *static_cast<const float4*>(__cluster_map_shared_rank(&mine[e], r));
+            num.x += v.x, num.y += v.y, num.z += v.z, num.w += v.w;
             den += *static_cast<const float*>(__cluster_map_shared_rank(&mine_l[g], r));
         }
-        out[(long long)kvh * group * hd + e] = __fmul_rn(num, __fdiv_rn(1.0f, den));
+        const float inv = __fdiv_rn(1.0f, den);
+        *reinterpret_cast<float4*>(&out[(long long)kvh * group * hd + e]) =
+            make_float4(__fmul_rn(num.x, inv), __fmul_rn(num.y, inv), __fmul_rn(num.z, inv), __fmul_rn(num.w, inv));
     }
     if (n_act > 1) {
         __syncthreads();  // the peers' partials are read: release them
@@ -1011,7 +1025,9 @@ struct neon_model {
     float forward_ms = 0.f;
     float decode_ms = 0.f;
     std::vector<void*> allocs;
-    std::vector<CUtensorMap> tm_k, tm_v;  // per layer: the K and V caches as 2D tensors (attn_decode_kernel)
+    // per layer: the K and V caches as 2D tensors for attn_decode_kernel, in boxes of 32 rows (tm_k,
+    // tm_v) and of one round (tm_kr, tm_vr)
+    std::vector<CUtensorMap> tm_k, tm_v, tm_kr, tm_vr;
 };
 
 namespace {
@@ -1111,8 +1127,8 @@ int launch_embed(neon_model* m, const int* toks, int seq) {
 
 // The decode attention kernel for a padded group (head dims are multiples of
 // 32: 128-byte swizzled boxes).
-using AttnKernel = void (*)(const float*, CUtensorMap, CUtensorMap, const int*, int, int, float, int, int, int, float*,
-                            unsigned int*);
+using AttnKernel = void (*)(const float*, CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, const int*, int, int,
+                            float, int, int, int, float*, unsigned int*);
 AttnKernel attn_kernel_for(int gp) {
     switch (gp) {
         case 1: return attn_decode_kernel<1, 32>;
@@ -1123,9 +1139,10 @@ AttnKernel attn_kernel_for(int gp) {
 }
 
 // The layers' K and V caches as 2D tensors for the decode attention's TMA
-// copies: ctx_len rows of kv_dim floats each, boxes of kAttnBoxRows rows x
-// 32 columns (128 bytes, the 128-byte swizzle; a box's first column,
-// kvh * head_dim + 32 * block, is 128-byte aligned). cuTensorMapEncodeTiled
+// copies: ctx_len rows of kv_dim floats each, boxes of 32 columns (128 bytes,
+// the 128-byte swizzle; a box's first column, kvh * head_dim + 32 * block, is
+// 128-byte aligned) by kAttnBoxRows rows, and by att_round rows (a whole
+// round in one copy per dim block). cuTensorMapEncodeTiled
 // comes from the driver through the runtime's entry-point query, so the
 // library does not link libcuda.
 int build_kv_maps(neon_model* m) {
@@ -1143,17 +1160,19 @@ int build_kv_maps(neon_model* m) {
         return error(NEON_ERR_UNSUPPORTED, "decode attention: head_dim must be a multiple of 32");
     m->tm_k.assign(c.n_layer, CUtensorMap{});
     m->tm_v.assign(c.n_layer, CUtensorMap{});
+    m->tm_kr.assign(c.n_layer, CUtensorMap{});
+    m->tm_vr.assign(c.n_layer, CUtensorMap{});
     for (uint32_t li = 0; li < c.n_layer; ++li) {
-        for (int which = 0; which < 2; ++which) {
-            float* base = (which ? m->V : m->K) + (size_t)li * c.ctx_len * m->kv_dim;
+        for (int which = 0; which < 4; ++which) {
+            float* base = (which & 1 ? m->V : m->K) + (size_t)li * c.ctx_len * m->kv_dim;
+            CUtensorMap* tm = which == 0 ? &m->tm_k[li] : which == 1 ? &m->tm_v[li] : which == 2 ? &m->tm_kr[li] : &m->tm_vr[li];
             const cuuint64_t dims[2] = {(cuuint64_t)m->kv_dim, (cuuint64_t)c.ctx_len};
             const cuuint64_t strides[1] = {(cuuint64_t)m->kv_dim * sizeof(float)};
-            const cuuint32_t box[2] = {32u, (cuuint32_t)kAttnBoxRows};
+            const cuuint32_t box[2] = {32u, (cuuint32_t)(which < 2 ? kAttnBoxRows : m->att_round)};
             const cuuint32_t estr[2] = {1, 1};
-            const CUresult r = encode(which ? &m->tm_v[li] : &m->tm_k[li], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base,
-                                      dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+            const CUresult r = encode(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box, estr,
+                                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
             if (r != CUDA_SUCCESS)
                 return error(NEON_ERR_CUDA, "decode attention: cuTensorMapEncodeTiled failed (" +
                                                 std::to_string((int)r) + ")");
@@ -1233,7 +1252,7 @@ int launch_attn_decode(neon_model* m, uint32_t li) {
     const float scale = 1.0f / std::sqrt((float)c.head_dim);
     const int min_rows = std::min(g_attn_min_rows.load(), m->att_score_rows);
     cudaError_t e = cudaLaunchKernelEx(&cfg, attn_kernel_for(m->att_gp), (const float*)m->q, m->tm_k[li], m->tm_v[li],
-                                       (const int*)m->d_pos, (int)c.head_dim, (int)(c.n_head / c.n_kv_head), scale,
+                                       m->tm_kr[li], m->tm_vr[li], (const int*)m->d_pos, (int)c.head_dim, (int)(c.n_head / c.n_kv_head), scale,
                                        min_rows, m->att_round, m->att_score_rows, m->att, m->d_err);
     if (e != cudaSuccess) return cuda_error(e, "attn_decode_kernel");
     return neon_internal::launched(1);

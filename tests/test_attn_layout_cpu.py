@@ -3,7 +3,8 @@
 rounds and exchanges emulated at every context length the benchmark models
 and a 16K context reach, for cluster caps of 16 and 8 and several row
 settings: the CTAs' shares cover [0, L) once with at most cs CTAs; every TMA
-box (K rounds, then V rounds, item t in slot t % 2) starts at a cache row
+box (K rounds, then V rounds, item t in slot t % 2; one round-sized box per
+dim block, or 32-row boxes for the item with the new row) starts at a cache row
 below ctx_len, a 128-byte-aligned column and a 1024-byte-aligned offset
 inside its slot; the K box with the new row is issued once, by the last
 active CTA, after the dependency wait; the scores fit their region;
@@ -105,16 +106,23 @@ def test_split_layout_and_copies(lib, name, n_head, n_kv, hd, ctx, min_rows, sha
                     for t in range(2 * nr):  # items: K rounds, then V rounds; item t in slot t % 2
                         r0 = (t % nr) * rr
                         nrb = -(-min(rr, n - r0) // BOX)
+                        base = v if t % 2 else k
+                        if pos >= s0 + r0 + nrb * BOX:  # no new row: one round-sized box per dim block
+                            assert rr <= 256 and nbk * rr * bw * 4 < (1 << 20)
+                            assert 0 <= s0 + r0 < ctx and s0 + r0 + rr - 1 >= s0 + min(rr, n - r0) - 1
+                            for nb in range(nbk):
+                                dst = base + nb * rr * bw
+                                assert (dst * 4) % 1024 == 0 and dst + rr * bw <= base + rr * hd
+                            continue
+                        assert rank == n_act - 1 and t % nr == nr - 1  # the last CTA's last round
                         assert nrb * nbk * bw * BOX * 4 < (1 << 20)  # one mbarrier phase's byte count
                         for rb in range(nrb):
                             y = s0 + r0 + rb * BOX
                             assert 0 <= y <= pos < ctx
                             if pos < y + BOX and t < nr:  # the K box with the new row: after the wait
-                                assert rank == n_act - 1
                                 post += 1
                             for nb in range(nbk):
-                                dst = (v if t % 2 else k) + (nb * rr + rb * BOX) * bw
-                                base = v if t % 2 else k
+                                dst = base + (nb * rr + rb * BOX) * bw
                                 assert (dst * 4) % 1024 == 0 and dst + BOX * bw <= base + rr * hd
                                 for kvh in (0, kv_dim // hd - 1):
                                     x = kvh * hd + nb * bw
