@@ -687,9 +687,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(
             if (r < rl) {
                 const float* kb = Ks + nb * round_rows * BW;
                 const float* qb = qs + nb * BW;
-                float acc[GP];
+                // two chains per head (the x, z and the y, w products), added at the end
+                float acc[GP], acc2[GP];
 #pragma unroll
-                for (int g = 0; g < GP; ++g) acc[g] = 0.f;
+                for (int g = 0; g < GP; ++g) acc[g] = acc2[g] = 0.f;
 #pragma unroll 2
                 for (int c = 0; c < BW / 4; ++c) {
                     const float4 k4 = *reinterpret_cast<const float4*>(kb + attn_swz<BW>(r, c));
@@ -697,11 +698,13 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(
                     for (int g = 0; g < GP; ++g) {
                         const float4 q4 = *reinterpret_cast<const float4*>(qb + g * hd + c * 4);
                         acc[g] = __fmaf_rn(q4.x, k4.x, acc[g]);
-                        acc[g] = __fmaf_rn(q4.y, k4.y, acc[g]);
+                        acc2[g] = __fmaf_rn(q4.y, k4.y, acc2[g]);
                         acc[g] = __fmaf_rn(q4.z, k4.z, acc[g]);
-                        acc[g] = __fmaf_rn(q4.w, k4.w, acc[g]);
+                        acc2[g] = __fmaf_rn(q4.w, k4.w, acc2[g]);
                     }
                 }
+#pragma unroll
+                for (int g = 0; g < GP; ++g) acc[g] += acc2[g];
                 float* dst = ps + (nb * round_rows + r) * GP;
                 if constexpr (GP >= 4) {
 #pragma unroll
@@ -785,6 +788,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(
         const int t = nr + j, r0 = j * round_rows, rl = min(round_rows, len - r0);
         ok = mbar_wait_d(&bars[t & 1], (uint32_t)((t >> 1) & 1), err) && ok;
         const float* Vs = slot(t);
+#pragma unroll 2
         for (int r = warp; r < rl; r += kAttnWarps) {
             float p[GP];
             const float* pr = sc + (r0 + r) * GP;
