@@ -160,8 +160,10 @@ def parse_args():
     p.add_argument("--cuda-core-prefill", action="store_true",
                    help="multi-position calls on the CUDA-core kernel instead (neon_cuda_set_prefill_mma(0))")
     p.add_argument("--dq-ring", action="store_true",
-                   help="one-position calls of the dequantising types on the bulk-copy ring kernel "
-                        "(neon_cuda_set_dq_ring)")
+                   help="one-position calls of every dequantising type on the bulk-copy ring kernel "
+                        "(neon_cuda_set_dq_ring; default: the types it is faster for)")
+    p.add_argument("--no-dq-ring", action="store_true",
+                   help="one-position calls of every dequantising type on the register-buffer kernel")
     p.add_argument("--tiles", default=None, metavar="RC:KC",
                    help="one-position Q4_0 / Q8_0 tile shape: RC rows per tile, KC blocks per row chunk "
                         "(0 = whole rows); neon_cuda_set_stream_tiles")
@@ -993,7 +995,7 @@ def run_type_sweep(args):
 
     torch.cuda.set_device(0)
     N.init(0)
-    N.set_dq_ring(bool(args.dq_ring))
+    N.set_dq_ring(True if args.dq_ring else (False if args.no_dq_ring else None))
     if args.tiles:
         N.set_stream_tiles(*(int(v) for v in args.tiles.split(":")))
     peak, peak_kind = measured_peak()

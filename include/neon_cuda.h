@@ -370,8 +370,9 @@ NEON_API int neon_cuda_set_prefill_mma(int enabled);
  * Q5_1, Q4_K, Q5_K, Q6_K) on a bulk-copy ring: a copy warp per CTA streams
  * row tiles into a ring of shared-memory stages (several tiles in flight per
  * CTA) and the compute warps decode from it, with the same decoders and
- * per-sub-block dot products as the register-buffer kernel. Off by default
- * until a GPU run has validated it; the switch is process-wide. */
+ * per-sub-block dot products as the register-buffer kernel. enabled = 1 for
+ * every such type, 0 for none, -1 (the default) for the types it measured
+ * faster for on B200 (Q4_1, F16, BF16). Process-wide. */
 NEON_API int neon_cuda_set_dq_ring(int enabled);
 
 /* Tile shape of later one-position Q4_0 / Q8_0 launches, for tuning sweeps:

@@ -40,7 +40,7 @@ thread_local std::string g_err;
 std::atomic<uint64_t> g_launches{0};
 std::atomic<int> g_pdl{1};
 std::atomic<int> g_prefill_mma{1};  // neon_cuda_set_prefill_mma
-std::atomic<int> g_dq_ring{0};      // neon_cuda_set_dq_ring
+std::atomic<int> g_dq_ring{-1};     // neon_cuda_set_dq_ring: 1 on, 0 off, -1 the types it is faster for
 std::atomic<int> g_tile_rc{0}, g_tile_kc{0};  // neon_cuda_set_stream_tiles (0: the planner's choice)
 std::atomic<int> g_resident{1};  // neon_cuda_set_resident: CTAs per SM of a resident launch (0: off)
 
@@ -608,7 +608,12 @@ int dq_occupancy(int type, int T, int smem) {
 int launch_dq(const std::vector<const neon_proj_target_t*>& t, int type, size_t cols, const float* dX,
               size_t x_stride, size_t seq, cudaStream_t st, DeviceState& ds, int accumulate,
               const neon_proj_target_t* base, const neon_internal::MatvecExt* ext) {
-    if (seq == 1 && g_dq_ring.load(std::memory_order_relaxed)) {
+    // the ring by default only where it measured faster on B200 (4096x4096,
+    // one position: Q4_1 1402 vs 1221 GB/s, F16 3252 vs 2714, BF16 3291 vs
+    // 2831); the K-quants, Q5_0/Q5_1 and F32 ran slower on it
+    const int ring = g_dq_ring.load(std::memory_order_relaxed);
+    const bool ring_type = type == NEON_GGML_Q4_1 || type == NEON_GGML_F16 || type == NEON_GGML_BF16;
+    if (seq == 1 && (ring == 1 || (ring < 0 && ring_type))) {
         const int rc = launch_dq_ring(t, type, cols, dX, st, ds, accumulate, base, ext);
         if (rc != 1) return rc;  // 1: X does not fit beside a stage; the register-buffer kernel below
     }
@@ -985,7 +990,7 @@ int neon_cuda_set_prefill_mma(int enabled) {
 }
 
 int neon_cuda_set_dq_ring(int enabled) {
-    g_dq_ring.store(enabled ? 1 : 0);
+    g_dq_ring.store(enabled < 0 ? -1 : enabled ? 1 : 0);
     return NEON_OK;
 }
 

@@ -223,11 +223,12 @@ def set_prefill_mma(enabled: bool) -> None:
     _check(load().neon_cuda_set_prefill_mma(1 if enabled else 0))
 
 
-def set_dq_ring(enabled: bool) -> None:
+def set_dq_ring(enabled) -> None:
     """One-position calls of the dequantising types on the bulk-copy ring
     kernel (several row tiles in flight per CTA) instead of the register-buffer
-    kernel; process-wide, off by default."""
-    _check(load().neon_cuda_set_dq_ring(1 if enabled else 0))
+    kernel: True for every such type, False for none, None (the default) for
+    the types it measured faster for (Q4_1, F16, BF16). Process-wide."""
+    _check(load().neon_cuda_set_dq_ring(-1 if enabled is None else 1 if enabled else 0))
 
 
 def set_stream_tiles(rows_per_tile: int = 0, blocks_per_chunk: int = 0) -> None:
