@@ -173,6 +173,9 @@ def parse_args():
     p.add_argument("--attn-rows", default=None, metavar="MIN:SHARE",
                    help="decode attention: at least MIN cache rows per CTA, the cluster sized for SHARE rows of "
                         "ctx_len per CTA (multiples of 32); neon_cuda_set_attn_rows (default: the library's)")
+    p.add_argument("--attn-head-split", type=int, default=None, metavar="H",
+                   help="decode attention: each KV head's query heads over at most H clusters when SMs are idle "
+                        "(neon_cuda_set_attn_head_split; default: the library's)")
     p.add_argument("--batch", type=int, default=1,
                    help="matvec workloads: positions per call; > 1 times the prefill path (one JSON line)")
     p.add_argument("--tile-sweep", action="store_true",
@@ -452,6 +455,8 @@ def run_decode(args):
         N.set_resident(args.resident)
     if args.attn_rows:
         N.set_attn_rows(*(int(v) for v in args.attn_rows.split(":")))
+    if args.attn_head_split:
+        N.set_attn_head_split(args.attn_head_split)
     N.set_fused_collectives(not args.no_fused_collectives)
     comm = None
     barrier, max_over_ranks = (lambda: None), (lambda v: v)
@@ -487,7 +492,9 @@ def run_decode(args):
                                                              if on]
                                                 + ([f"resident {args.resident}"] if args.resident is not None
                                                    else [])
-                                                + ([f"attn rows {args.attn_rows}"] if args.attn_rows else [])},
+                                                + ([f"attn rows {args.attn_rows}"] if args.attn_rows else [])
+                                                + ([f"attn head split {args.attn_head_split}"]
+                                                   if args.attn_head_split else [])},
                 "e2e": {"value": res["e2e_tokens_per_s"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 4, "api": res["e2e"]},
                 "load_s": res["load_s"], "roofline": decode_roofline(dict(res), cfg, world)["hbm"],
@@ -648,6 +655,8 @@ def run_neon(args):
         N.set_resident(args.resident)
     if getattr(args, "attn_rows", None):
         N.set_attn_rows(*(int(v) for v in args.attn_rows.split(":")))
+    if getattr(args, "attn_head_split", None):
+        N.set_attn_head_split(args.attn_head_split)
     dev = torch.device("cuda", local)
 
     # One GPU: a rotation of whole matrices. N > 1 (strong scaling): every rank

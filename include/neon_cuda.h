@@ -401,6 +401,14 @@ NEON_API int neon_cuda_set_resident(int ctas_per_sm);
  * tests only; no counterpart in the reference. Process-wide. */
 NEON_API int neon_cuda_set_attn_rows(int min_rows, int share_rows);
 
+/* Decode attention: when a model's clusters (one per KV head) leave SMs idle
+ * -- few KV heads per rank under tensor parallelism -- each KV head's query
+ * heads are spread over up to max_split clusters (a power of two from 1 to
+ * 8; default 8; 1: one cluster per KV head), each reading the same K and V
+ * rows for its share of the heads. Read when a model is created. Tuning and
+ * tests only; no counterpart in the reference. Process-wide. */
+NEON_API int neon_cuda_set_attn_head_split(int max_split);
+
 /* Launch option: programmatic dependent launch (PDL) lets a matvec fetch its
  * weights while the previous kernel on the stream finishes; on by default. */
 NEON_API int neon_cuda_set_pdl(int enabled);

@@ -59,6 +59,9 @@ constexpr int kMaxCtx = 16384;      // attention scores live in shared memory
 // least (read when a step is launched), and the share of ctx_len per CTA the
 // cluster size is chosen for (read when a model is created); multiples of 32.
 std::atomic<int> g_attn_min_rows{32}, g_attn_share_rows{128};
+// neon_cuda_set_attn_head_split: clusters per KV head at most (read when a
+// model is created)
+std::atomic<int> g_attn_head_split{8};
 
 #define DEC_TRY(call)                                              \
     do {                                                           \
@@ -576,13 +579,18 @@ template <int GP, int BW>
 __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(
     const float* __restrict__ q, const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
     const __grid_constant__ CUtensorMap tmk_r, const __grid_constant__ CUtensorMap tmv_r, const int* __restrict__ d_pos,
-    int hd, int group, float scale, int min_rows, int round_rows, int score_rows, float* __restrict__ out,
+    int hd, int group, int hsplit, float scale, int min_rows, int round_rows, int score_rows, float* __restrict__ out,
     unsigned int* err) {
     extern __shared__ __align__(1024) float sm[];
     uint32_t rank, cs;
     asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
     asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(cs));
-    const int kvh = blockIdx.x / cs;
+    // cluster c = blockIdx.x / cs: KV head c / hsplit, its query heads
+    // [h0, h0 + GP) (those below group are real; the rest are zero rows)
+    const int kvh = blockIdx.x / (cs * hsplit);
+    const int h0 = (int)((blockIdx.x / cs) % hsplit) * GP;
+    const int nh = min(GP, group - h0);  // real query heads of this cluster
+    const long long qrow0 = ((long long)kvh * group + h0) * hd;  // its first query / output element
     const int pos = __ldcg(d_pos), L = pos + 1;
     const int rows = attn_rows_per_cta(L, (int)cs, min_rows);
     const int n_act = (L + rows - 1) / rows;
@@ -670,7 +678,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(
         for (int t = 0; t < 2; ++t) issue(t, 2);
     }
     for (int i = threadIdx.x; i < GP * hd; i += kAttnThreads)
-        qs[i] = i < group * hd ? q[(long long)kvh * group * hd + i] : 0.f;
+        qs[i] = i < nh * hd ? q[qrow0 + i] : 0.f;
     __syncthreads();
 
     // pass 1, per round: partial dots per (row, head, dim block), then the scores
@@ -850,7 +858,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(
     // four elements of one head per thread
     if (n_act > 1) mbar_wait_d(&bars[3], 0, err, true);  // every active CTA's partial is in place
 #pragma unroll 1
-    for (int e = 4 * threadIdx.x; e < group * hd; e += 4 * kAttnThreads) {
+    for (int e = 4 * threadIdx.x; e < nh * hd; e += 4 * kAttnThreads) {
         const int g = e / hd;  // hd % 4 == 0: the four share a head
         float4 num = *reinterpret_cast<const float4*>(&mine[e]);
         float den = mine_l[g];
@@ -860,7 +868,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(
             den += *static_cast<const float*>(__cluster_map_shared_rank(&mine_l[g], r));
         }
         const float inv = __fdiv_rn(1.0f, den);
-        *reinterpret_cast<float4*>(&out[(long long)kvh * group * hd + e]) =
+        *reinterpret_cast<float4*>(&out[qrow0 + e]) =
             make_float4(__fmul_rn(num.x, inv), __fmul_rn(num.y, inv), __fmul_rn(num.z, inv), __fmul_rn(num.w, inv));
     }
     if (n_act > 1) {
@@ -1000,7 +1008,9 @@ struct neon_model {
     float2* shift_cs = nullptr;      // rope_half (cos, sin) of the shift angle
     // decode attention (attn_decode_kernel, attn_plan): a cluster of att_cs CTAs per KV head, K and
     // V rows in rounds of att_round, scores for att_score_rows rows
+    // (att_gp: query heads per cluster, padded; att_hsplit: clusters per KV head)
     int att_gp = 1, att_cs = 1, att_round = kAttnBoxRows, att_score_rows = kAttnMinScores, att_smem = 0;
+    int att_hsplit = 1;
     float* logits_full = nullptr;    // all-gathered logits (tensor parallel only)
     neon_tensor_t embd = nullptr, output = nullptr;
     float* output_norm = nullptr;
@@ -1131,7 +1141,7 @@ int launch_embed(neon_model* m, const int* toks, int seq) {
 
 // The decode attention kernel for a padded group (head dims are multiples of
 // 32: 128-byte swizzled boxes).
-using AttnKernel = void (*)(const float*, CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, const int*, int, int,
+using AttnKernel = void (*)(const float*, CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, const int*, int, int, int,
                             float, int, int, int, float*, unsigned int*);
 AttnKernel attn_kernel_for(int gp) {
     switch (gp) {
@@ -1185,13 +1195,14 @@ int build_kv_maps(neon_model* m) {
     return NEON_OK;
 }
 
-// Clusters of cs CTAs of the decode attention with `smem` bytes each fit the
-// device (cs > 8 needs the non-portable cluster size).
-bool attn_cluster_fits(AttnKernel k, int cs, int smem) {
+// How many clusters of cs CTAs of the decode attention with `smem` bytes
+// each the device holds at once (0: none; cs > 8 needs the non-portable
+// cluster size).
+int attn_max_clusters(AttnKernel k, int cs, int smem) {
     if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmemMax) != cudaSuccess ||
         (cs > 8 && cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)) {
         cudaGetLastError();
-        return false;
+        return 0;
     }
     cudaLaunchConfig_t q = {};
     q.gridDim = dim3((unsigned)cs);
@@ -1207,21 +1218,38 @@ bool attn_cluster_fits(AttnKernel k, int cs, int smem) {
     int clusters = 0;
     if (cudaOccupancyMaxActiveClusters(&clusters, k, &q) != cudaSuccess) {
         cudaGetLastError();
-        return false;
+        return 0;
     }
-    return clusters >= 1;
+    return clusters;
 }
 
 // The decode attention's split (attn_plan), with the largest cluster the
-// device schedules (16, else 8, ...).
+// device schedules (16, else 8, ...); then, while the grid leaves SMs idle,
+// each KV head's query heads over 2, 4, ... clusters (the same K and V rows,
+// a fraction of the score and p*v arithmetic per CTA), as long as every
+// cluster of the launch stays resident at once.
 int plan_attention(neon_model* m) {
     const auto& c = m->cfg;
-    const int group = (int)(c.n_head / c.n_kv_head);
+    const int group = (int)(c.n_head / c.n_kv_head), gp = attn_group_pad(group);
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, m->device);
     for (int cs_max = kAttnMaxCluster; cs_max >= 1; cs_max /= 2) {
         AttnPlan p;
         if (!attn_plan((int)c.ctx_len, group, (int)c.head_dim, cs_max, g_attn_share_rows.load(), &p)) break;
-        if (!attn_cluster_fits(attn_kernel_for(p.gp), p.cs, p.smem_bytes)) continue;
+        if (attn_max_clusters(attn_kernel_for(p.gp), p.cs, p.smem_bytes) < 1) continue;
+        int hsplit = 1;
+        for (int h = 2; h <= gp && h <= g_attn_head_split.load(); h *= 2) {
+            AttnPlan ph;
+            if ((h - 1) * (gp / h) >= group ||  // a cluster without a real query head
+                (int)m->n_kv_l * h * p.cs > sms ||
+                !attn_plan((int)c.ctx_len, gp / h, (int)c.head_dim, cs_max, g_attn_share_rows.load(), &ph) ||
+                ph.cs != p.cs || attn_max_clusters(attn_kernel_for(ph.gp), ph.cs, ph.smem_bytes) < (int)m->n_kv_l * h)
+                break;
+            hsplit = h;
+            p = ph;
+        }
         m->att_gp = p.gp;
+        m->att_hsplit = hsplit;
         m->att_cs = p.cs;
         m->att_round = p.round_rows;
         m->att_score_rows = p.score_rows;
@@ -1235,7 +1263,7 @@ int plan_attention(neon_model* m) {
 int launch_attn_decode(neon_model* m, uint32_t li) {
     const auto& c = m->cfg;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)(m->n_kv_l * m->att_cs));
+    cfg.gridDim = dim3((unsigned)(m->n_kv_l * m->att_hsplit * m->att_cs));
     cfg.blockDim = dim3(kAttnThreads);
     cfg.dynamicSmemBytes = (size_t)m->att_smem;
     cfg.stream = m->stream;
@@ -1256,7 +1284,8 @@ int launch_attn_decode(neon_model* m, uint32_t li) {
     const float scale = 1.0f / std::sqrt((float)c.head_dim);
     const int min_rows = std::min(g_attn_min_rows.load(), m->att_score_rows);
     cudaError_t e = cudaLaunchKernelEx(&cfg, attn_kernel_for(m->att_gp), (const float*)m->q, m->tm_k[li], m->tm_v[li],
-                                       m->tm_kr[li], m->tm_vr[li], (const int*)m->d_pos, (int)c.head_dim, (int)(c.n_head / c.n_kv_head), scale,
+                                       m->tm_kr[li], m->tm_vr[li], (const int*)m->d_pos, (int)c.head_dim, (int)(c.n_head / c.n_kv_head),
+                                       m->att_hsplit, scale,
                                        min_rows, m->att_round, m->att_score_rows, m->att, m->d_err);
     if (e != cudaSuccess) return cuda_error(e, "attn_decode_kernel");
     return neon_internal::launched(1);
@@ -1625,6 +1654,13 @@ int neon_cuda_model_create_tp(const neon_model_config_t* cfg, neon_comm_t comm, 
         return rc;
     }
     *out = m;
+    return NEON_OK;
+}
+
+int neon_cuda_set_attn_head_split(int max_split) {
+    if (max_split < 1 || max_split > kAttnMaxGroup || (max_split & (max_split - 1)))
+        return error(NEON_ERR_INVALID, "attention head split: a power of two from 1 to 8");
+    g_attn_head_split.store(max_split);
     return NEON_OK;
 }
 

@@ -103,6 +103,7 @@ C_ENTRY_POINTS = (
     "neon_cuda_set_stream_tiles",
     "neon_cuda_set_resident",
     "neon_cuda_set_attn_rows",
+    "neon_cuda_set_attn_head_split",
 )
 
 _sz = C.c_size_t
@@ -169,6 +170,7 @@ def load(path: str | None = None) -> C.CDLL:
         L.neon_cuda_set_stream_tiles.argtypes = [C.c_int, C.c_int]
         L.neon_cuda_set_resident.argtypes = [C.c_int]
         L.neon_cuda_set_attn_rows.argtypes = [C.c_int, C.c_int]
+        L.neon_cuda_set_attn_head_split.argtypes = [C.c_int]
         L.neon_cuda_matvec_q4_0_noalloc.argtypes = [_vp, _vp, _sz, _vp, _sz, _sz, _vp]
         L.neon_cuda_model_create.argtypes = [C.POINTER(_ModelConfig), C.POINTER(_vp)]
         L.neon_cuda_model_set_tensor.argtypes = [_vp, C.c_int, C.c_int, _vp, _sz, C.c_int, _sz, _sz]
@@ -251,6 +253,13 @@ def set_attn_rows(min_rows: int = 32, share_rows: int = 128) -> None:
     rows; steps launched afterwards give each CTA at least min_rows rows.
     Multiples of 32. Process-wide."""
     _check(load().neon_cuda_set_attn_rows(int(min_rows), int(share_rows)))
+
+
+def set_attn_head_split(max_split: int = 8) -> None:
+    """Decode attention: spread each KV head's query heads over up to
+    max_split clusters when one cluster per KV head leaves SMs idle (models
+    created afterwards); 1 keeps one cluster per KV head. Process-wide."""
+    _check(load().neon_cuda_set_attn_head_split(int(max_split)))
 
 
 def set_pdl(enabled: bool) -> None:

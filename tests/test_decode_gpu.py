@@ -134,14 +134,16 @@ def test_greedy_matches_reference(cfg, n_prompt, steps):
 
 
 def test_attention_splits_agree():
-    """The decode attention at three work splits of one cluster of 16 CTAs per
-    KV head (sized for 32-row shares; K and V in 32-row shared-memory rounds):
-    32-row shares over up to 8 CTAs, 96-row shares over 3 CTAs in 3 rounds
-    each, and one CTA for the whole context in up to 8 rounds (no exchange).
-    F32 projections and embedding keep activations unquantised, so the model
-    is continuous and the comparison sees the attention's rounding alone:
-    every decode step's logits within MATVEC_RTOL per element of the oracle's,
-    and the three splits within 1e-5 relative L2 of each other."""
+    """The decode attention at four work splits of a cluster of 16 CTAs per
+    KV head (sized for 32-row shares; K and V in 32-row shared-memory
+    rounds): 32-row shares over up to 8 CTAs, with each KV head's 4 query
+    heads in one cluster and spread over 4 clusters; 96-row shares over 3
+    CTAs in 3 rounds each; one CTA for the whole context in up to 8 rounds
+    (no exchange). F32 projections and embedding keep activations
+    unquantised, so the model is continuous and the comparison sees the
+    attention's rounding alone: every decode step's logits within MATVEC_RTOL
+    per element of the oracle's, and the splits within 1e-5 relative L2 of
+    each other."""
     cfg = TINY.with_(n_head=8, n_kv_head=2, ctx_len=256 + 1)
     tensors = list(S.model_tensors(cfg, seed=31, wtype=S.GGML_F32, embd_type=S.GGML_F32))
     prompt = S.prompt_tokens(230, cfg.n_vocab, 32)
@@ -151,15 +153,17 @@ def test_attention_splits_agree():
     ref = [o.forward([t]) for t in toks]
     runs, errs = [], {}
     try:
-        for lo, hi in ((32, 32), (96, 32), (256, 32)):
+        for lo, hi, split in ((32, 32, 1), (32, 32, 8), (96, 32, 1), (256, 32, 1)):
             N.set_attn_rows(lo, hi)
+            N.set_attn_head_split(split)
             m = N.Model(cfg, tensors)
             m.forward(prompt)
             runs.append([m.forward([t]) for t in toks])
             m.free()
-            errs[f"{lo}-{hi}"] = [max_rel_err(lg, want) for lg, want in zip(runs[-1], ref)]
+            errs[f"{lo}-{hi}/{split}"] = [max_rel_err(lg, want) for lg, want in zip(runs[-1], ref)]
     finally:
         N.set_attn_rows()
+        N.set_attn_head_split()
     print({k: f"{max(v):.2e}" for k, v in errs.items()})
     assert all(max(v) <= MATVEC_RTOL for v in errs.values()), errs
     for other in runs[1:]:
