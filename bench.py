@@ -497,7 +497,9 @@ def run_decode(args):
                                                    if args.attn_head_split else [])},
                 "e2e": {"value": res["e2e_tokens_per_s"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 4, "api": res["e2e"]},
-                "load_s": res["load_s"], "roofline": decode_roofline(dict(res), cfg, world)["hbm"],
+                "load_s": res["load_s"], "prefill_ms": res.get("prefill_ms"),
+                "prefill_tokens_per_s": res.get("prefill_tokens_per_s"),
+                "roofline": decode_roofline(dict(res), cfg, world)["hbm"],
                 "cpu_baseline": cpu, "clocks": sampler.summary(t0, t1)}
         print(json.dumps(line), flush=True)
     if comm is not None:

@@ -44,15 +44,21 @@ struct MmaStage {
     float xd[kMmaPos * kMmaKb];      // [pos][kb]: their fp32 scale
 };
 
-// D = A (16x32 s8, row-major) x B (32x8 s8, column-major), int32.
+// D = A (16x32 s8, row-major) x B (32x8 s8, column-major) + 0x4B400000, int32:
+// |A x B| < 2^22 for a Q4_0 x Q8_0 block (32 * 8 * 127), so each D read as a
+// float is exactly 1.5 * 2^23 + isum, and isum as a float is one FADD away
+// (no int-to-float conversion, which runs at an eighth of the FMA rate).
+constexpr int kMmaFloatBias = 0x4B400000;
 __device__ __forceinline__ void mma_s8_m16n8k32(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                                 uint32_t b0, uint32_t b1) {
     asm volatile(
         "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%10,%11,%12,%13};"
         : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0), "r"(0), "r"(0), "r"(0));
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(kMmaFloatBias), "r"(kMmaFloatBias),
+          "r"(kMmaFloatBias), "r"(kMmaFloatBias));
 }
+__device__ __forceinline__ float mma_isum_f32(int d) { return __int_as_float(d) - 12582912.0f; }
 
 // Rows of a 64-row tile and positions of a 64-position tile (grid.y).
 // MatvecArgs as the CUDA-core multi-position kernel takes it, with the span
@@ -150,10 +156,10 @@ __global__ void __launch_bounds__(kMmaThreads) matvec_mma_q4_0_kernel(const __gr
                 // block step total = fma(d_w * d_x, (float)isum, total)
                 const float xd0 = s.xd[(8 * j + 2 * t) * kMmaKb + kb];
                 const float xd1 = s.xd[(8 * j + 2 * t + 1) * kMmaKb + kb];
-                acc[j][0] = fmaf(__fmul_rn(wdg, xd0), (float)d[0], acc[j][0]);
-                acc[j][1] = fmaf(__fmul_rn(wdg, xd1), (float)d[1], acc[j][1]);
-                acc[j][2] = fmaf(__fmul_rn(wdg8, xd0), (float)d[2], acc[j][2]);
-                acc[j][3] = fmaf(__fmul_rn(wdg8, xd1), (float)d[3], acc[j][3]);
+                acc[j][0] = fmaf(__fmul_rn(wdg, xd0), mma_isum_f32(d[0]), acc[j][0]);
+                acc[j][1] = fmaf(__fmul_rn(wdg, xd1), mma_isum_f32(d[1]), acc[j][1]);
+                acc[j][2] = fmaf(__fmul_rn(wdg8, xd0), mma_isum_f32(d[2]), acc[j][2]);
+                acc[j][3] = fmaf(__fmul_rn(wdg8, xd1), mma_isum_f32(d[3]), acc[j][3]);
             }
         }
         if (c + 1 < nchunks) store(st[(c + 1) & 1]);

@@ -200,6 +200,18 @@ def test_prefill_mma_q8_0_fragments(rows, cols, seq):
     emulate_q8(W, rows, cols, X)
 
 
+def test_mma_float_bias_is_exact():
+    """The Q4_0 prefill kernel seeds its int32 MMA accumulator with 0x4B400000
+    and reads D as a float: 1.5 * 2^23 + isum exactly, so D - 12582912.0f is
+    (float)isum for every block sum a Q4_0 x Q8_0 block can give
+    (|isum| <= 32 * 8 * 127 < 2^22) -- checked over the whole range."""
+    isum = np.arange(-32 * 8 * 127, 32 * 8 * 127 + 1, dtype=np.int64)
+    d = (isum + 0x4B400000).astype(np.int32)
+    f = d.view(np.float32) - np.float32(12582912.0)
+    assert np.array_equal(f, isum.astype(np.float32))
+    assert 32 * 8 * 127 < 2 ** 22
+
+
 def test_tf32_split_carries_fp32():
     """x_hi + x_lo, each rounded to TF32 (10 mantissa bits, nearest, ties away
     as cvt.rna), reproduces x to within 2^-21 relative: the Q8_0 kernel's
