@@ -370,6 +370,177 @@ __global__ void __launch_bounds__(128) attn_prefill_mma_kernel(const float* __re
     }
 }
 
+// Causal GQA attention of a multi-position forward (transformer_forward
+// :1115-1151) on the CUDA cores, register-tiled like an fp32 GEMM: a CTA of
+// 256 threads takes query head blockIdx.x at 64 positions (blockIdx.y) and
+// walks the key tiles of 64 cached rows; thread (ty, tx) of a 16 x 16 grid
+// owns rows 4ty..4ty+3 and, for the scores, keys 4tx..4tx+3 of a tile, for
+// the output dims (HD/16)tx.. of the head. Q and the K tile sit transposed in
+// shared memory (a score is one fmaf chain over the head dim, in order), V in
+// its own layout, p transposed for the p*v loop. The reference's two passes:
+// the row maxima over each position's keys 0..pos first, then
+// p = fast_expf(score - max), l = sum p and o = sum p * v; out = o * (1 / l).
+// 112 KB of shared memory: two CTAs per SM.
+constexpr int kPfRows = 64, kPfKeys = 64, kPfThreads = 256;
+template <int HD>
+constexpr int pf_smem_bytes() {
+    return (int)sizeof(float) * (HD * kPfRows + HD * kPfKeys + kPfKeys * HD + kPfKeys * kPfRows);
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kPfThreads, 2) attn_prefill_f32_kernel(const float* __restrict__ q,
+                                                                         const float* __restrict__ Kc,
+                                                                         const float* __restrict__ Vc,
+                                                                         float* __restrict__ out,
+                                                                         const int* __restrict__ d_pos, int seq,
+                                                                         int q_dim, int kv_dim, int group,
+                                                                         float scale) {
+    constexpr int DPT = HD / 16;  // output dims per thread
+    extern __shared__ __align__(16) float pf_sm[];
+    float* qt = pf_sm;                 // [HD][64]: Q of the tile's positions, transposed
+    float* kt = qt + HD * kPfRows;     // [HD][64]: the key tile, transposed
+    float* vs = kt + HD * kPfKeys;     // [64][HD]
+    float* pt = vs + kPfKeys * HD;     // [64 keys][64 rows]: p, transposed
+    const int h = blockIdx.x, t0 = blockIdx.y * kPfRows, kvh = h / group;
+    const int base = *d_pos;
+    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+    const int nq = min(kPfRows, seq - t0);
+    const int kend = base + t0 + nq;  // keys [0, kend) are seen by some position of the tile
+    const int ntiles = (kend + kPfKeys - 1) / kPfKeys;
+
+    // Q: float4 along the head dim from each position's row, stored transposed
+    for (int i = tid; i < kPfRows * (HD / 4); i += kPfThreads) {
+        const int r = i % kPfRows, d4 = i / kPfRows;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (r < nq) v = *reinterpret_cast<const float4*>(q + (long long)(t0 + r) * q_dim + (long long)h * HD + 4 * d4);
+        qt[(4 * d4 + 0) * kPfRows + r] = v.x;
+        qt[(4 * d4 + 1) * kPfRows + r] = v.y;
+        qt[(4 * d4 + 2) * kPfRows + r] = v.z;
+        qt[(4 * d4 + 3) * kPfRows + r] = v.w;
+    }
+    auto load_k = [&](int t) {
+        for (int i = tid; i < kPfKeys * (HD / 4); i += kPfThreads) {
+            const int r = i % kPfKeys, d4 = i / kPfKeys, key = t * kPfKeys + r;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (key < kend) v = *reinterpret_cast<const float4*>(Kc + (long long)key * kv_dim + (long long)kvh * HD + 4 * d4);
+            kt[(4 * d4 + 0) * kPfKeys + r] = v.x;
+            kt[(4 * d4 + 1) * kPfKeys + r] = v.y;
+            kt[(4 * d4 + 2) * kPfKeys + r] = v.z;
+            kt[(4 * d4 + 3) * kPfKeys + r] = v.w;
+        }
+    };
+    auto load_v = [&](int t) {
+        for (int i = tid; i < kPfKeys * (HD / 4); i += kPfThreads) {
+            const int r = i / (HD / 4), d4 = i % (HD / 4), key = t * kPfKeys + r;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (key < kend) v = *reinterpret_cast<const float4*>(Vc + (long long)key * kv_dim + (long long)kvh * HD + 4 * d4);
+            *reinterpret_cast<float4*>(vs + r * HD + 4 * d4) = v;
+        }
+    };
+    // the scaled scores of rows 4ty.. against keys 4tx.. of the tile in kt
+    auto scores = [&](float (&s)[4][4]) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) s[i][j] = 0.f;
+#pragma unroll 4
+        for (int d = 0; d < HD; ++d) {
+            const float4 qa = *reinterpret_cast<const float4*>(qt + d * kPfRows + 4 * ty);
+            const float4 kb = *reinterpret_cast<const float4*>(kt + d * kPfKeys + 4 * tx);
+            const float qv[4] = {qa.x, qa.y, qa.z, qa.w}, kv[4] = {kb.x, kb.y, kb.z, kb.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) s[i][j] = __fmaf_rn(qv[i], kv[j], s[i][j]);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) s[i][j] = __fmul_rn(s[i][j], scale);
+    };
+    int pos[4];
+    bool live[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        live[i] = 4 * ty + i < nq;
+        pos[i] = base + t0 + 4 * ty + i;
+    }
+
+    // pass 1: row maxima
+    float m[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+    for (int t = 0; t < ntiles; ++t) {
+        __syncthreads();
+        load_k(t);
+        __syncthreads();
+        float s[4][4];
+        scores(s);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                if (live[i] && t * kPfKeys + 4 * tx + j <= pos[i]) m[i] = fmaxf(m[i], s[i][j]);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int o = 8; o; o >>= 1) m[i] = fmaxf(m[i], __shfl_xor_sync(0xffffffffu, m[i], o));
+
+    // pass 2: p, l and o = sum p * v
+    float acc[4][DPT], l[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int c = 0; c < DPT; ++c) acc[i][c] = 0.f;
+    for (int t = 0; t < ntiles; ++t) {
+        __syncthreads();
+        load_k(t);
+        load_v(t);
+        __syncthreads();
+        float s[4][4];
+        scores(s);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            float p4[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const bool on = live[i] && t * kPfKeys + 4 * tx + j <= pos[i];
+                p4[i] = on ? fast_expf_dev(__fsub_rn(s[i][j], m[i])) : 0.f;
+                l[i] += p4[i];
+            }
+            *reinterpret_cast<float4*>(pt + (4 * tx + j) * kPfRows + 4 * ty) = make_float4(p4[0], p4[1], p4[2], p4[3]);
+        }
+        __syncthreads();
+#pragma unroll 4
+        for (int k = 0; k < kPfKeys; ++k) {
+            const float4 pa = *reinterpret_cast<const float4*>(pt + k * kPfRows + 4 * ty);
+            const float pv[4] = {pa.x, pa.y, pa.z, pa.w};
+            float vv[DPT];
+#pragma unroll
+            for (int c = 0; c < DPT; c += 4) {
+                const float4 v4 = *reinterpret_cast<const float4*>(vs + k * HD + DPT * tx + c);
+                vv[c] = v4.x, vv[c + 1] = v4.y, vv[c + 2] = v4.z, vv[c + 3] = v4.w;
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int c = 0; c < DPT; ++c) acc[i][c] = __fmaf_rn(pv[i], vv[c], acc[i][c]);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+#pragma unroll
+        for (int o = 8; o; o >>= 1) l[i] += __shfl_xor_sync(0xffffffffu, l[i], o);
+        if (!live[i]) continue;
+        const float inv = __fdiv_rn(1.0f, l[i]);
+        float* o = out + (long long)(t0 + 4 * ty + i) * q_dim + (long long)h * HD + DPT * tx;
+#pragma unroll
+        for (int c = 0; c < DPT; c += 4)
+            *reinterpret_cast<float4*>(o + c) = make_float4(__fmul_rn(acc[i][c], inv), __fmul_rn(acc[i][c + 1], inv),
+                                                            __fmul_rn(acc[i][c + 2], inv), __fmul_rn(acc[i][c + 3], inv));
+    }
+}
+
+
 // out = x * (1/sqrt(mean(x^2) + eps)) * w per row; one CTA per row
 // (fwd::rms_norm, rawllm_forward.hpp:730-735).
 __global__ void __launch_bounds__(kThreads) rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
@@ -1333,7 +1504,17 @@ int run_layers(neon_model* m, const int* toks, int seq) {
                                                             (int)q_dim, (int)kv_dim, Kl, Vl);
             rc = check_launch("rope_kv_kernel");
         }
-        if (!rc && neon_internal::prefill_mma() && c.head_dim <= (uint32_t)kApMaxHd && c.head_dim % 8 == 0) {
+        if (!rc && (c.head_dim == 64 || c.head_dim == 128)) {
+            // register-tiled fp32 tiles of 64 positions per query head
+            const dim3 grid((unsigned)m->n_head_l, (unsigned)((seq + kPfRows - 1) / kPfRows));
+            if (c.head_dim == 128)
+                attn_prefill_f32_kernel<128><<<grid, kPfThreads, pf_smem_bytes<128>(), m->stream>>>(
+                    m->q, Kl, Vl, m->att, m->d_pos, seq, (int)q_dim, (int)kv_dim, group, scale);
+            else
+                attn_prefill_f32_kernel<64><<<grid, kPfThreads, pf_smem_bytes<64>(), m->stream>>>(
+                    m->q, Kl, Vl, m->att, m->d_pos, seq, (int)q_dim, (int)kv_dim, group, scale);
+            rc = check_launch("attn_prefill_f32_kernel");
+        } else if (!rc && neon_internal::prefill_mma() && c.head_dim <= (uint32_t)kApMaxHd && c.head_dim % 8 == 0) {
             // tensor-core tiles of 64 positions per query head
             attn_prefill_mma_kernel<<<dim3((unsigned)m->n_head_l, (unsigned)((seq + kApRows - 1) / kApRows)), 128,
                                       ap_smem_bytes((int)c.head_dim), m->stream>>>(
@@ -1649,6 +1830,11 @@ int neon_cuda_model_create_tp(const neon_model_config_t* cfg, neon_comm_t comm, 
         cudaFuncSetAttribute(attn_prefill_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              ap_smem_bytes((int)c.head_dim)) != cudaSuccess)
         rc = error(NEON_ERR_CUDA, "cudaFuncSetAttribute(attn_prefill_mma_kernel)");
+    if (!rc && (cudaFuncSetAttribute(attn_prefill_f32_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     pf_smem_bytes<128>()) != cudaSuccess ||
+                cudaFuncSetAttribute(attn_prefill_f32_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     pf_smem_bytes<64>()) != cudaSuccess))
+        rc = error(NEON_ERR_CUDA, "cudaFuncSetAttribute(attn_prefill_f32_kernel)");
     if (rc) {
         neon_cuda_model_free(m);
         return rc;
