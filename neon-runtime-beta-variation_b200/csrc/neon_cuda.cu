@@ -788,7 +788,9 @@ int launch_group(const Group& g, const float* dX, size_t x_stride, size_t seq, c
             }
             a.n_spans = (int)n;
             a.n_tiles = tiles;
-            const dim3 grid(tiles, (unsigned)((seq + kMmaPos - 1) / kMmaPos));
+            if (tiles > 65535) return set_err(NEON_ERR_UNSUPPORTED, "more than 65535 row tiles in one prefill launch");
+            // position tiles along x, so that the CTAs of one row tile run together and read its weights once
+            const dim3 grid((unsigned)((seq + kMmaPos - 1) / kMmaPos), tiles);
             int rc = launch_n(q4 ? matvec_mma_q4_0_kernel : matvec_mma_q8_0_kernel, grid, kMmaThreads, 0, st, a);
             if (rc) return rc;
             start += n;

@@ -60,7 +60,7 @@ __device__ __forceinline__ void mma_s8_m16n8k32(int (&c)[4], uint32_t a0, uint32
 }
 __device__ __forceinline__ float mma_isum_f32(int d) { return __int_as_float(d) - 12582912.0f; }
 
-// Rows of a 64-row tile and positions of a 64-position tile (grid.y).
+// Positions of a 64-position tile (grid.x) and rows of a 64-row tile (grid.y).
 // MatvecArgs as the CUDA-core multi-position kernel takes it, with the span
 // tiles counted in 64-row units and xq / xd the call's Q8_0 activations.
 __global__ void __launch_bounds__(kMmaThreads) matvec_mma_q4_0_kernel(const __grid_constant__ MatvecArgs a) {
@@ -68,10 +68,10 @@ __global__ void __launch_bounds__(kMmaThreads) matvec_mma_q4_0_kernel(const __gr
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, t = lane & 3;  // the MMA fragment coordinates of this lane
     const int nb = a.nb, cols = nb * 32;
-    const int tile = blockIdx.x;
+    const int tile = blockIdx.y;  // position tiles vary fastest: a row tile's weights stay in L2 for all of them
     const Span& sp = a.span[find_span(a, tile)];
     const int row0 = (tile - sp.tile0) * kMmaRows;
-    const int p0 = blockIdx.y * kMmaPos;
+    const int p0 = blockIdx.x * kMmaPos;
     const int nchunks = (nb + kMmaKb - 1) / kMmaKb;
 
     pdl_launch_dependents();
@@ -227,10 +227,10 @@ __global__ void __launch_bounds__(kMmaThreads) matvec_mma_q8_0_kernel(const __gr
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, t = lane & 3;
     const int nb = a.nb;
-    const int tile = blockIdx.x;
+    const int tile = blockIdx.y;  // position tiles vary fastest: a row tile's weights stay in L2 for all of them
     const Span& sp = a.span[find_span(a, tile)];
     const int row0 = (tile - sp.tile0) * kMmaRows;
-    const int p0 = blockIdx.y * kMmaPos;
+    const int p0 = blockIdx.x * kMmaPos;
     const int nchunks = (nb + kMma8Kb - 1) / kMma8Kb;
 
     pdl_launch_dependents();
