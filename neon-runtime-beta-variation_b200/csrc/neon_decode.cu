@@ -801,12 +801,11 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(
         return;
     }
     const int nr = (len + round_rows - 1) / round_rows, n_items = 2 * nr;
-    // item t (K round t, then V round t - nr) into slot t % 2 by warp 0;
-    // mode 0: every box, 1: the boxes without row pos (before the dependency
-    // wait), 2: the box with it
-    // item t: an item without row pos as one round-sized box per dim block (the
-    // round maps), the item with it as 32-row boxes, of which only the one
-    // holding row pos waits for the dependency
+    // item t (K round t, then V round t - nr) into slot t % 2, issued by warp 0:
+    // an item without row pos as one round-sized box per dim block (the round
+    // maps; rows past the CTA's share land in slot rows nothing reads), the
+    // item with it as 32-row boxes. mode 0: every box, 1: the boxes without
+    // row pos (before the dependency wait), 2: the box with it
     auto issue = [&](int t, int mode) {
         const bool is_v = t >= nr;
         const int r0 = (is_v ? t - nr : t) * round_rows;
