@@ -86,3 +86,25 @@ def test_reference_error_messages():
     W = N.TensorInfo("blk.0.ffn_up.weight", [100, 2], N.GGML_Q4_0, np.zeros(36, np.uint8))
     with pytest.raises(RuntimeError, match=r"input dim \(100\) isn't a multiple of its quant block size \(32\)"):
         N.proj_all_positions(W, np.zeros(100, np.float32), 100, np.zeros(2, np.float32), 2, 1)
+
+
+def test_switch_arguments_are_checked():
+    """The process-wide switches refuse out-of-range arguments with
+    NEON_ERR_INVALID and a message, on the host, and keep their value: the
+    decode attention's rows (multiples of 32 from 32 to 16384) and head split
+    (a power of two from 1 to 8), the resident kernel's CTAs per SM (0..8)."""
+    L = N.load()
+    for lo, share in ((16, 128), (32, 0), (48, 128), (32, 100), (32, 16416)):
+        assert L.neon_cuda_set_attn_rows(lo, share) == -1, (lo, share)
+        assert b"attention rows" in L.neon_cuda_last_error()
+    for split in (0, 3, 16, -1):
+        assert L.neon_cuda_set_attn_head_split(split) == -1, split
+        assert b"head split" in L.neon_cuda_last_error()
+    for k in (-1, 9):
+        assert L.neon_cuda_set_resident(k) != 0, k
+    # accepted values, then the defaults back
+    assert L.neon_cuda_set_attn_rows(64, 256) == 0 and L.neon_cuda_set_attn_head_split(2) == 0
+    assert L.neon_cuda_set_resident(2) == 0
+    N.set_attn_rows()
+    N.set_attn_head_split()
+    N.set_resident()
