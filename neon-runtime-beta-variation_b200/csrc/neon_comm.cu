@@ -289,9 +289,17 @@ __device__ __noinline__ unsigned long long ll_wait_word(const unsigned long long
 // slot_1[i] + ... in rank order, one thread per element; all of a thread's
 // loads are issued before any wait. The last CTA records the call as
 // completed (every CTA read the count before it counted itself in).
-__global__ void __launch_bounds__(256) comm_ll_reduce_kernel(PeerSet p, float* __restrict__ h, int n) {
+// wait_producer 0 skips the dependency wait, so that the polls overlap a long
+// producer's tail: the words carry their call number, so polling them is the
+// synchronisation; h and the call count were written by kernels that
+// completed before the producer's own dependency wait returned, and a
+// producer stages its input before it stores a word, so when every word has
+// arrived nothing of the producer's reads is left for later writers. The
+// kernel after this one waits for it as usual.
+__global__ void __launch_bounds__(256) comm_ll_reduce_kernel(PeerSet p, float* __restrict__ h, int n,
+                                                             int wait_producer) {
     __shared__ int s_skip;
-    pdl_wait_c();
+    if (wait_producer) pdl_wait_c();
     pdl_trigger_c();
     if (threadIdx.x == 0) s_skip = *reinterpret_cast<volatile unsigned int*>(p.err) != 0u;
     __syncthreads();
@@ -415,11 +423,11 @@ PeerSet comm_peer_set(neon_comm_impl* c) {
 
 bool fused_collectives() { return g_fused.load(std::memory_order_relaxed) != 0; }
 
-int comm_ll_reduce(neon_comm_impl* c, float* h, long long n, cudaStream_t st) {
+int comm_ll_reduce(neon_comm_impl* c, float* h, long long n, cudaStream_t st, bool wait_producer) {
     if (!c || !c->connected) return error(NEON_ERR_INVALID, "communicator not connected");
     if (n <= 0 || n > kCommFusedFloats) return error(NEON_ERR_INVALID, "fused all-reduce: bad length");
     const int grid = (int)std::min<long long>((n + 255) / 256, 148);
-    return launch_comm(comm_ll_reduce_kernel, grid, 256, st, comm_peer_set(c), h, (int)n);
+    return launch_comm(comm_ll_reduce_kernel, grid, 256, st, comm_peer_set(c), h, (int)n, wait_producer ? 1 : 0);
 }
 
 int comm_ll_gather(neon_comm_impl* c, float* y, long long n, cudaStream_t st) {

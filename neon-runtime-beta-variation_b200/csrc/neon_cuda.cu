@@ -430,6 +430,7 @@ int launch_stream(const std::vector<const neon_proj_target_t*>& t, int type, int
         const int smem = stream_smem_bytes(type, nb, a.stages, p.stage_bytes);
         int rc = launch_n(stream_kernel(type, p.rc), dim3(grid), kStreamBlock, smem, st, a);
         if (rc) return rc;
+        if (ext && ext->launched_stream) *ext->launched_stream = true;
         start += n;
     }
     return NEON_OK;

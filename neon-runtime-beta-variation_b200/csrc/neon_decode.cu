@@ -1577,8 +1577,10 @@ int run_step(neon_model* m) {
         neon_internal::MatvecExt ext;
         ext.peer_mode = 1;
         ext.peer = neon_internal::comm_peer_set(m->comm);
+        bool streamed = false;  // a long producer: the reduce polls its words while its tail runs
+        ext.launched_stream = &streamed;
         int r = neon_internal::matvec(&t, 1, x, x_stride, 1, m->stream, 0, &ext);
-        if (!r) r = neon_internal::comm_ll_reduce(m->comm, hc, (long long)n_embd, m->stream);
+        if (!r) r = neon_internal::comm_ll_reduce(m->comm, hc, (long long)n_embd, m->stream, !streamed);
         return r;
     };
     for (uint32_t li = 0; li < c.n_layer && !rc; ++li) {

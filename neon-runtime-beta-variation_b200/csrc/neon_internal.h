@@ -117,7 +117,9 @@ int comm_argmax(neon_comm_impl* c, unsigned long long* key, int* d_tok, int* out
 PeerSet comm_peer_set(neon_comm_impl* c);
 // Completes a fused all-reduce a producing matvec started: h[i] += slot_0[i]
 // + slot_1[i] + ... for i < n, waiting (bounded) for every rank's words.
-int comm_ll_reduce(neon_comm_impl* c, float* h, long long n, cudaStream_t st);
+// wait_producer false: no dependency wait (the LL words are the
+// synchronisation; worth it when the producer is a long launch)
+int comm_ll_reduce(neon_comm_impl* c, float* h, long long n, cudaStream_t st, bool wait_producer = true);
 // Completes a fused all-gather the producing row-shard matvecs started:
 // y[i] = the gather slot's word i for i < n, waiting (bounded) for each.
 int comm_ll_gather(neon_comm_impl* c, float* y, long long n, cudaStream_t st);
@@ -145,6 +147,9 @@ struct MatvecExt {
     int peer_mode = 0;
     long long gather_row0 = 0;
     PeerSet peer{};
+    // set to true when the call ran on the streaming kernel (a long launch,
+    // whose tail a following LL reduce may overlap); left alone otherwise
+    bool* launched_stream = nullptr;
 };
 
 // neon_cuda_matvec_multi on `st`, with y += result when `accumulate`.
