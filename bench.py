@@ -29,6 +29,9 @@ all-gather); value = the whole matrices' bytes / max-over-ranks time. The
 Phi-4-mini-shaped at 1 and 2, Llama-3-70B-shaped tensor parallel over all N)
 and, at 1 GPU, `sweep` the other Q4_0 / Q8_0 matvec shapes.
 --impl reference times the reference's CPU path alone (rank 0 only).
+The tuning switches (--resident, --tiles, --dq-ring / --no-dq-ring,
+--attn-rows, --attn-head-split, --cuda-core-prefill; see --help) time the
+library's variants on any workload and name themselves in config.variants.
 """
 from __future__ import annotations
 
