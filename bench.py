@@ -31,7 +31,9 @@ and, at 1 GPU, `sweep` the other Q4_0 / Q8_0 matvec shapes.
 --impl reference times the reference's CPU path alone (rank 0 only).
 The tuning switches (--resident, --tiles, --dq-ring / --no-dq-ring,
 --attn-rows, --attn-head-split, --cuda-core-prefill; see --help) time the
-library's variants on any workload and name themselves in config.variants.
+library's variants; the matvec line names --resident, --tiles, --dq-ring and
+--cuda-core-prefill in config.variants, a decode workload's line also the
+attention switches.
 """
 from __future__ import annotations
 
